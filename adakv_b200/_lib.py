@@ -1,0 +1,172 @@
+"""ctypes binding of ``libadakv_b200.so`` (the C ABI in ``include/adakv_b200.h``).
+
+The library is built in-tree by :mod:`adakv_b200.build`.  Loading fails loudly
+when it is missing: there is no CPU or eager-torch fallback for any operator.
+Torch is used only to hand device pointers and the current CUDA stream to the
+library; no torch type crosses the C ABI.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+import torch
+
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libadakv_b200.so")
+
+DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2
+POLICY_FIXED, POLICY_ADAPTIVE = 0, 1
+OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_CUDA = 0, 1, 2, 3
+ST_WAIT_TIMEOUT, ST_BAD_BLOCK_ID, ST_BAD_SEL_LEN, ST_BAD_SEQ_LEN = 1, 2, 4, 8
+
+TORCH_DTYPES = {torch.float32: DTYPE_F32, torch.float16: DTYPE_F16, torch.bfloat16: DTYPE_BF16}
+POLICIES = {"fixed": POLICY_FIXED, "adaptive": POLICY_ADAPTIVE}
+
+
+class Geometry(ctypes.Structure):
+    _fields_ = [("batch", ctypes.c_int32), ("n_q_heads", ctypes.c_int32),
+                ("n_kv_heads", ctypes.c_int32), ("head_dim", ctypes.c_int32),
+                ("block_size", ctypes.c_int32), ("max_seq_len", ctypes.c_int32),
+                ("nb_cap", ctypes.c_int32), ("dtype", ctypes.c_int32)]
+
+
+class View(ctypes.Structure):
+    _fields_ = [("data", ctypes.c_void_p), ("stride_b", ctypes.c_int64),
+                ("stride_h", ctypes.c_int64), ("stride_s", ctypes.c_int64)]
+
+
+class SelectParams(ctypes.Structure):
+    _fields_ = [("avg_budget", ctypes.c_double), ("temperature", ctypes.c_double),
+                ("k_min", ctypes.c_int32), ("k_max", ctypes.c_int32),
+                ("n_sink_blocks", ctypes.c_int32), ("n_local_blocks", ctypes.c_int32),
+                ("c_min", ctypes.c_int32), ("policy", ctypes.c_int32)]
+
+
+_P = ctypes.POINTER
+_vp = ctypes.c_void_p
+_SIGNATURES = {
+    "adakv_abi_version": (ctypes.c_int, []),
+    "adakv_last_error": (ctypes.c_char_p, []),
+    "adakv_plan_table_width": (ctypes.c_int32, [_P(Geometry), _P(SelectParams)]),
+    "adakv_plan_workspace_bytes": (ctypes.c_size_t, [_P(Geometry), _P(SelectParams)]),
+    "adakv_attend_workspace_bytes": (ctypes.c_size_t, [_P(Geometry), ctypes.c_int32]),
+    "adakv_centroid_build": (ctypes.c_int, [_P(Geometry), _P(View), _vp, _vp, _vp]),
+    "adakv_kv_append": (ctypes.c_int, [_P(Geometry), _P(View), _P(View), _P(View), _P(View),
+                                       ctypes.c_int32, _vp, _vp, _vp]),
+    "adakv_centroid_refresh": (ctypes.c_int, [_P(Geometry), _P(View), ctypes.c_int32, _vp, _vp,
+                                              _vp]),
+    "adakv_plan": (ctypes.c_int, [_P(Geometry), _P(SelectParams), _P(View), _vp, _vp, _vp,
+                                  ctypes.c_int32, _vp, _vp, _vp, ctypes.c_size_t, _vp]),
+    "adakv_attend": (ctypes.c_int, [_P(Geometry), _P(View), _P(View), _P(View), _vp,
+                                    ctypes.c_int32, _vp, _vp, ctypes.c_float, _P(View), _vp,
+                                    ctypes.c_size_t, _vp]),
+    "adakv_decode_step": (ctypes.c_int, [_P(Geometry), _P(SelectParams), _P(View), _P(View),
+                                         _P(View), _vp, _vp, ctypes.c_float, _vp, ctypes.c_int32,
+                                         _vp, _P(View), _vp, ctypes.c_size_t, _vp]),
+    "adakv_read_status": (ctypes.c_int, [_vp, _P(ctypes.c_uint32), _vp]),
+}
+
+_lib = None
+_lock = threading.Lock()
+
+
+def lib():
+    """Load (once) and return the C library; raises if it was not built."""
+    global _lib
+    if _lib is None:
+        with _lock:
+            if _lib is None:
+                if not os.path.exists(LIB_PATH):
+                    raise RuntimeError(
+                        f"{LIB_PATH} is missing: build it with `python -m adakv_b200.build` "
+                        "(there is no CPU fallback for the AdaKV CUDA path)")
+                handle = ctypes.CDLL(LIB_PATH)
+                for name, (res, args) in _SIGNATURES.items():
+                    fn = getattr(handle, name)
+                    fn.restype = res
+                    fn.argtypes = args
+                _lib = handle
+    return _lib
+
+
+def check(rc: int) -> None:
+    """Raise the reference's exception type for a non-zero return code."""
+    if rc == OK:
+        return
+    msg = lib().adakv_last_error().decode(errors="replace")
+    if rc == ERR_INVALID:
+        raise ValueError(msg)
+    if rc == ERR_UNSUPPORTED:
+        raise NotImplementedError(msg)
+    raise RuntimeError(msg)
+
+
+def require_cuda(*tensors) -> None:
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("adakv_b200 runs on CUDA tensors only (no CPU fallback); "
+                               "use the oracle package for CPU reference checks")
+
+
+def dtype_code(t: torch.Tensor) -> int:
+    try:
+        return TORCH_DTYPES[t.dtype]
+    except KeyError:
+        raise ValueError(f"unsupported dtype {t.dtype}; expected float32, float16 or bfloat16")
+
+
+def view4(t: torch.Tensor) -> View:
+    """[B, H, S, D] (or [B, H, D] for q / out) view with a contiguous last dim."""
+    if t.stride(-1) != 1:
+        raise ValueError("the head_dim axis must be contiguous")
+    if t.dim() == 4:
+        return View(t.data_ptr(), t.stride(0), t.stride(1), t.stride(2))
+    if t.dim() == 3:
+        return View(t.data_ptr(), t.stride(0), t.stride(1), 0)
+    raise ValueError(f"expected a 3-D or 4-D tensor, got {tuple(t.shape)}")
+
+
+def stream_ptr(device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def select_params(avg_budget, k_min=2, k_max=64, n_sink_blocks=1, n_local_blocks=4, c_min=1,
+                  temperature=1.0, budget_policy="adaptive") -> SelectParams:
+    if budget_policy not in POLICIES:
+        if budget_policy == "adaptive_nucleus":
+            raise NotImplementedError("budget_policy='adaptive_nucleus' is not built yet")
+        raise ValueError(f"unknown budget_policy: {budget_policy!r}")
+    return SelectParams(float(avg_budget), float(temperature), int(k_min), int(k_max),
+                        int(n_sink_blocks), int(n_local_blocks), int(c_min),
+                        POLICIES[budget_policy])
+
+
+def geometry(batch, n_q_heads, n_kv_heads, head_dim, block_size, max_seq_len, nb_cap,
+             dtype) -> Geometry:
+    return Geometry(int(batch), int(n_q_heads), int(n_kv_heads), int(head_dim), int(block_size),
+                    int(max_seq_len), int(nb_cap), int(dtype))
+
+
+# ---------------------------------------------------------------------------
+# workspace: one zero-initialised device buffer per (device, stream), grown on
+# demand.  The kernels leave its counters at zero after every call.
+# ---------------------------------------------------------------------------
+_workspaces: dict = {}
+
+
+def workspace(nbytes: int, device) -> torch.Tensor:
+    device = torch.device(device)
+    key = (device.index, stream_ptr(device))
+    ws = _workspaces.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.zeros(max(int(nbytes), 256), dtype=torch.uint8, device=device)
+        _workspaces[key] = ws
+    return ws
+
+
+def read_status(ws: torch.Tensor) -> int:
+    """Synchronise and return (and clear) the device status bits of a workspace."""
+    out = ctypes.c_uint32(0)
+    check(lib().adakv_read_status(ws.data_ptr(), ctypes.byref(out), stream_ptr(ws.device)))
+    return int(out.value)

@@ -1,0 +1,131 @@
+"""Batched, preallocated decode state over the C ABI.
+
+:class:`BatchedDecoder` owns everything one attention layer needs for ragged
+batched decode: the K/V cache ``[B, Hkv, capacity, D]``, the float32 centroid
+table ``[B, Hkv, nb_cap, D]``, per-sequence lengths on the device, the plan
+outputs and one workspace.  Every method only enqueues kernels on the current
+stream (no allocation, no host synchronisation), so a decode step can be
+captured in a CUDA graph after one warm-up call.
+
+The reference runs batch 1 only (``adakv/runtime.py:97``, ``adakv/patch.py:96``);
+this is the batched form of the same step used for ragged-batch decode.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import _lib
+
+
+class BatchedDecoder:
+    def __init__(self, batch, n_q_heads, n_kv_heads, head_dim, block_size, capacity, dtype,
+                 device="cuda", avg_budget=64, k_min=2, k_max=64, n_sink_blocks=1,
+                 n_local_blocks=4, c_min=1, temperature=1.0, budget_policy="adaptive"):
+        self.device = torch.device(device)
+        if self.device.type != "cuda":
+            raise RuntimeError("BatchedDecoder needs a CUDA device (no CPU fallback)")
+        self.B, self.Hq, self.Hkv, self.D = batch, n_q_heads, n_kv_heads, head_dim
+        self.bs, self.capacity, self.dtype = block_size, capacity, dtype
+        self.nb_cap = (capacity + block_size - 1) // block_size
+        self.params = _lib.select_params(avg_budget, k_min, k_max, n_sink_blocks, n_local_blocks,
+                                         c_min, temperature, budget_policy)
+        self.k = torch.zeros((batch, n_kv_heads, capacity, head_dim), dtype=dtype, device=device)
+        self.v = torch.zeros_like(self.k)
+        self.centroid = torch.zeros((batch, n_kv_heads, self.nb_cap, head_dim), dtype=torch.float32,
+                                    device=device)
+        self.seq_lens = torch.zeros((batch,), dtype=torch.int32, device=device)
+        self.host_seq_lens = [0] * batch
+        geo = self.geometry()
+        L = _lib.lib()
+        self.table_width = L.adakv_plan_table_width(geo, self.params)
+        if self.table_width < 1:
+            _lib.check(_lib.ERR_INVALID)
+        self.block_table = torch.zeros((batch * n_q_heads, self.table_width), dtype=torch.int32,
+                                       device=device)
+        self.sel_lens = torch.zeros((batch * n_q_heads,), dtype=torch.int32, device=device)
+        self.ws_bytes = L.adakv_plan_workspace_bytes(geo, self.params)
+        self.workspace = torch.zeros((self.ws_bytes,), dtype=torch.uint8, device=device)
+        self.out = torch.zeros((batch, n_q_heads, head_dim), dtype=dtype, device=device)
+
+    def geometry(self, max_seq_len=None):
+        return _lib.geometry(self.B, self.Hq, self.Hkv, self.D, self.bs,
+                             max_seq_len if max_seq_len is not None else self.capacity,
+                             self.nb_cap, _lib.TORCH_DTYPES[self.dtype])
+
+    def _stream(self):
+        return _lib.stream_ptr(self.device)
+
+    # -- prefill ------------------------------------------------------------------
+    def load(self, K, V, seq_lens):
+        """Copy prefilled K/V ``[B, Hkv, S, D]`` into the cache and build the centroids."""
+        seq_lens = [int(s) for s in seq_lens]
+        S = K.shape[2]
+        if S > self.capacity or max(seq_lens) > S:
+            raise ValueError("prefill longer than the cache capacity")
+        self.k[:, :, :S].copy_(K, non_blocking=True)
+        self.v[:, :, :S].copy_(V, non_blocking=True)
+        self.host_seq_lens = seq_lens
+        self.seq_lens.copy_(torch.tensor(seq_lens, dtype=torch.int32), non_blocking=True)
+        with torch.cuda.device(self.device):
+            _lib.check(_lib.lib().adakv_centroid_build(
+                self.geometry(), _lib.view4(self.k), self.seq_lens.data_ptr(),
+                self.centroid.data_ptr(), self._stream()))
+
+    # -- decode -------------------------------------------------------------------
+    def append(self, k_new, v_new, advance=True):
+        """Append ``[B, Hkv, n, D]`` tokens to every sequence and refresh the touched
+        centroids.  With ``advance=False`` the lengths stay put and the last ``n``
+        tokens are overwritten (fixed-context benchmarking)."""
+        n = k_new.shape[2]
+        if advance:
+            if max(self.host_seq_lens) + n > self.capacity:
+                raise ValueError("cache capacity exceeded")
+            self.host_seq_lens = [s + n for s in self.host_seq_lens]
+            self.seq_lens.add_(n)
+        with torch.cuda.device(self.device):
+            _lib.check(_lib.lib().adakv_kv_append(
+                self.geometry(), _lib.view4(self.k), _lib.view4(self.v), _lib.view4(k_new),
+                _lib.view4(v_new), n, self.seq_lens.data_ptr(), self.centroid.data_ptr(),
+                self._stream()))
+
+    def plan(self, q, scores_out=None):
+        """Block selection for ``q`` ``[B, Hq, D]``; fills ``block_table`` / ``sel_lens``."""
+        with torch.cuda.device(self.device):
+            _lib.check(_lib.lib().adakv_plan(
+                self.geometry(), self.params, _lib.view4(q), self.centroid.data_ptr(),
+                self.seq_lens.data_ptr(), self.block_table.data_ptr(), self.table_width,
+                self.sel_lens.data_ptr(),
+                scores_out.data_ptr() if scores_out is not None else None,
+                self.workspace.data_ptr(), self.ws_bytes, self._stream()))
+        return self.block_table, self.sel_lens
+
+    def step(self, q, sm_scale=None, out=None):
+        """Selection + attention for ``q`` ``[B, Hq, D]``; returns ``[B, Hq, D]``."""
+        out = self.out if out is None else out
+        scale = 1.0 / math.sqrt(self.D) if sm_scale is None else float(sm_scale)
+        with torch.cuda.device(self.device):
+            _lib.check(_lib.lib().adakv_decode_step(
+                self.geometry(), self.params, _lib.view4(q), _lib.view4(self.k),
+                _lib.view4(self.v), self.centroid.data_ptr(), self.seq_lens.data_ptr(), scale,
+                self.block_table.data_ptr(), self.table_width, self.sel_lens.data_ptr(),
+                _lib.view4(out), self.workspace.data_ptr(), self.ws_bytes, self._stream()))
+        return out
+
+    def attend(self, q, block_table, sel_lens, sm_scale=None, out=None):
+        """Attention over a caller-given table (``adakv_attend``)."""
+        from .kernels.block_sparse_decode import block_sparse_decode_batched
+        return block_sparse_decode_batched(q, self.k, self.v, block_table, sel_lens, self.bs,
+                                           sm_scale, seq_lens=self.seq_lens,
+                                           max_seq_len=self.capacity, out=out)
+
+    def status(self) -> int:
+        """Synchronise; return and clear the device status bits (ADAKV_ST_*)."""
+        return _lib.read_status(self.workspace)
+
+    def selected_sets(self):
+        """Host copy of the selection: list over rows (b*Hq + h) of block-id arrays."""
+        bt = self.block_table.cpu().numpy()
+        sl = self.sel_lens.cpu().numpy()
+        return [bt[r, : sl[r]] for r in range(bt.shape[0])]

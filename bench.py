@@ -1,0 +1,400 @@
+#!/usr/bin/env python
+"""Benchmark of the AdaKV decode attention step on B200.
+
+Metric: microseconds per decode attention step, with achieved
+HBM GB/s against the measured copy bandwidth.  Workload = configuration 1:
+Llama-3.1-8B attention layer (32 q / 8 KV heads, head_dim 128), bf16, batch 1,
+block 16, avg_budget 64 (k_max 512 so the mean budget is not capped), seeded
+synthetic K/V/q with planted retrieval blocks (even KV heads) and recency-biased
+local heads (odd KV heads).  The headline is the 131072-token context; 32768 and
+65536 are reported beside it.
+
+One step = append one token (in-place K/V write + trailing-centroid refresh),
+centroid estimator, entropy budget, top-k selection, ragged split-KV attention:
+5 kernels, captured once in a CUDA graph and replayed.  Each step gets a fresh
+query (a pool of perturbed queries) and L2 is flushed (256 MB write) between
+steps, outside the timed events.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Under torchrun each rank runs its own batch-1 replica (no collective on the
+data path); the reported value is the max over ranks.  ``--impl reference``
+times the NumPy oracle port of the reference's algorithm on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = ("µs per decode attention step at 32K/128K/1M ctx; achieved HBM GB/s vs ~8 TB/s "
+          "roofline")
+CFG = dict(Hq=32, Hkv=8, D=128, bs=16, avg=64, k_min=2, k_max=512, sink=1, local=4, c_min=1)
+HEADLINE_S = 131072
+L2_FLUSH_BYTES = 256 << 20
+
+
+def workload_name(S):
+    return (f"cfg1 Llama-3.1-8B attention decode: batch 1, 32 q / 8 KV heads, head_dim 128, "
+            f"ctx {S}, block 16, avg_budget 64, k_max 512, entropy budget, bf16")
+
+
+# ---------------------------------------------------------------------------
+# clocks sampled during the timed region (NVML, in-process)
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+               0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
+
+    def __init__(self, index, period=0.005):
+        self.samples, self.reasons, self.ok = [], 0, False
+        self.period, self._stop = period, threading.Event()
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception as e:  # noqa: BLE001
+            self.err = str(e)
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+                self.reasons |= self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+            except Exception:  # noqa: BLE001
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self.ok:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        if self.ok:
+            self._stop.set()
+            self._t.join()
+
+    def summary(self):
+        if not self.ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "error": self.err}
+        names = [n for bit, n in self.REASONS.items() if self.reasons & bit and n != "gpu_idle"]
+        return {"sm_mhz": float(statistics.median(self.samples)) if self.samples else None,
+                "sm_max_mhz": float(self.max_mhz), "reasons": names, "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------------------
+# inputs
+# ---------------------------------------------------------------------------
+def make_inputs(S, seed, pool):
+    from adakv_b200.synth import make_decode_case, round_to_dtype
+    case = make_decode_case(seed, 1, CFG["Hq"], CFG["Hkv"], CFG["D"], S, CFG["bs"], "bf16")
+    rng = np.random.default_rng(seed + 7)
+    # fresh queries per step: perturbations of the planted-structure query
+    qs = round_to_dtype(case.q[None] + 0.5 * rng.standard_normal((pool,) + case.q.shape,
+                                                                 dtype=np.float32), "bf16")
+    kts = round_to_dtype(rng.standard_normal((pool, 1, CFG["Hkv"], 1, CFG["D"]), dtype=np.float32),
+                         "bf16")
+    vts = round_to_dtype(rng.standard_normal((pool, 1, CFG["Hkv"], 1, CFG["D"]), dtype=np.float32),
+                         "bf16")
+    return case, qs, kts, vts
+
+
+def algorithmic_bytes(sets, S):
+    """Bytes a step must move: fp32 centroid table + the union of the selected K/V
+    blocks per KV head (bf16) + the append (one block read, one centroid row and
+    one K/V token written) + q and out."""
+    Hq, Hkv, D, bs = CFG["Hq"], CFG["Hkv"], CFG["D"], CFG["bs"]
+    g = Hq // Hkv
+    nb = (S + bs - 1) // bs
+    cent = Hkv * nb * D * 4
+    union = sum(len(set().union(*[set(sets[h].tolist()) for h in range(k * g, (k + 1) * g)]))
+                for k in range(Hkv))
+    kv = union * bs * D * 2 * 2
+    append = Hkv * (bs * D * 2 + D * 4 + 2 * D * 2)
+    qo = 2 * Hq * D * 2
+    per_head = sum(len(s) for s in sets) * bs * D * 2 * 2
+    return cent + kv + append + qo, dict(centroid=cent, kv_union=kv, kv_per_q_head=per_head,
+                                        union_blocks=union,
+                                        mean_blocks_per_head=float(np.mean([len(s) for s in sets])))
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def run_ours(S, steps, warmup, seed, device, pool=16, e2e_steps=None):
+    import torch
+    from adakv_b200.batch import BatchedDecoder
+    case, qs, kts, vts = make_inputs(S, seed, pool)
+    dt = torch.bfloat16
+    dec = BatchedDecoder(1, CFG["Hq"], CFG["Hkv"], CFG["D"], CFG["bs"], S, dt, device,
+                         avg_budget=CFG["avg"], k_min=CFG["k_min"], k_max=CFG["k_max"],
+                         n_sink_blocks=CFG["sink"], n_local_blocks=CFG["local"], c_min=CFG["c_min"])
+    dec.load(torch.from_numpy(case.K).to(device, dt), torch.from_numpy(case.V).to(device, dt),
+             case.seq_lens)
+    q_pool = torch.from_numpy(qs).to(device, dt)
+    kt_pool = torch.from_numpy(kts).to(device, dt)
+    vt_pool = torch.from_numpy(vts).to(device, dt)
+    q_buf, kt_buf, vt_buf = q_pool[0].clone(), kt_pool[0].clone(), vt_pool[0].clone()
+
+    def step():
+        dec.append(kt_buf, vt_buf, advance=False)
+        dec.step(q_buf)
+
+    # algorithmic bytes per step, averaged over the query pool (outside timing)
+    nbytes = []
+    for i in range(pool):
+        q_buf.copy_(q_pool[i])
+        step()
+        nbytes.append(algorithmic_bytes(dec.selected_sets(), S))
+    if dec.status() != 0:
+        raise RuntimeError("device status flags set during warm-up")
+    bytes_per_step = float(np.mean([b for b, _ in nbytes]))
+    detail = {k: float(np.mean([d[k] for _, d in nbytes])) for k in nbytes[0][1]}
+
+    stream = torch.cuda.current_stream(device)
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize(device)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+
+    def timed(n, fn, record):
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(n)]
+        for i in range(n):
+            j = i % pool
+            q_buf.copy_(q_pool[j])
+            kt_buf.copy_(kt_pool[j])
+            vt_buf.copy_(vt_pool[j])
+            flush.zero_()
+            ev[i][0].record(stream)
+            fn(j)
+            ev[i][1].record(stream)
+        torch.cuda.synchronize(device)
+        if record:
+            return [s.elapsed_time(e) * 1000.0 for s, e in ev]
+        return None
+
+    timed(max(warmup, 3), lambda j: graph.replay(), False)
+    with ClockSampler(device.index if device.index is not None else 0) as clk:
+        us = timed(steps, lambda j: graph.replay(), True)
+    clocks = clk.summary()
+
+    # end to end through the public API, host buffers in pinned memory
+    q_h = torch.from_numpy(qs).to(dt).pin_memory()
+    kt_h = torch.from_numpy(kts).to(dt).pin_memory()
+    vt_h = torch.from_numpy(vts).to(dt).pin_memory()
+    out_h = torch.empty((1, CFG["Hq"], CFG["D"]), dtype=dt).pin_memory()
+    qd, ktd, vtd = q_buf, kt_buf, vt_buf
+
+    def e2e_step(j):
+        qd.copy_(q_h[j], non_blocking=True)
+        ktd.copy_(kt_h[j], non_blocking=True)
+        vtd.copy_(vt_h[j], non_blocking=True)
+        dec.append(ktd, vtd, advance=False)
+        out = dec.step(qd)
+        out_h.copy_(out, non_blocking=True)
+
+    n_e2e = e2e_steps or min(steps, 1000)
+    timed(3, e2e_step, False)
+    us_e2e = timed(n_e2e, e2e_step, True)
+    h2d = (q_h[0].numel() + kt_h[0].numel() + vt_h[0].numel()) * 2
+    d2h = out_h.numel() * 2
+    return dict(us=us, us_e2e=us_e2e, bytes=bytes_per_step, detail=detail, clocks=clocks,
+                h2d=h2d, d2h=d2h, steps=steps, e2e_steps=n_e2e)
+
+
+# ---------------------------------------------------------------------------
+# CPU: the NumPy oracle port of the reference algorithm
+# ---------------------------------------------------------------------------
+def oracle_step(q, K, V, cent, kt, vt, S, pool_exec=None):
+    """One decode step of the oracle on the host: refresh the trailing centroid,
+    score, budget, select, attend over the selected tokens."""
+    from oracle import adakv_oracle as O
+    bs, Hq, Hkv = CFG["bs"], CFG["Hq"], CFG["Hkv"]
+    g = Hq // Hkv
+    K[:, S - 1] = kt[:, 0]
+    V[:, S - 1] = vt[:, 0]
+    j = (S - 1) // bs
+    cent[:, j] = O.build_centroids(K[:, j * bs:S], bs)[:, 0]
+
+    def scores_of(k):
+        return O.block_scores(q[k * g:(k + 1) * g], cent[k:k + 1])
+
+    if pool_exec is None:
+        scores = O.block_scores(q, cent)
+    else:
+        scores = np.concatenate(list(pool_exec.map(scores_of, range(Hkv))), axis=0)
+    k = O.allocate_budget(scores, CFG["avg"], CFG["k_min"], CFG["k_max"], CFG["sink"], CFG["local"],
+                          CFG["c_min"])
+
+    def sel_attend(kv):
+        sl = slice(kv * g, (kv + 1) * g)
+        mask, _ = O.select_blocks(scores[sl], k[sl], CFG["sink"], CFG["local"], CFG["c_min"])
+        return O.attend_mask(q[sl], K[kv:kv + 1], V[kv:kv + 1], mask, bs)
+
+    if pool_exec is None:
+        return np.concatenate([sel_attend(kv) for kv in range(Hkv)], axis=0)
+    return np.concatenate(list(pool_exec.map(sel_attend, range(Hkv))), axis=0)
+
+
+def run_cpu(S, seed, max_steps, budget_s, threads):
+    from concurrent.futures import ThreadPoolExecutor
+    from threadpoolctl import threadpool_limits
+    from oracle import adakv_oracle as O
+    case, qs, kts, vts = make_inputs(S, seed, 16)
+    K, V = case.K[0].copy(), case.V[0].copy()
+    cent = O.build_centroids(K, CFG["bs"])
+    ex = ThreadPoolExecutor(threads) if threads > 1 else None
+    times = []
+    with threadpool_limits(1):
+        t_end = time.perf_counter() + budget_s
+        i = 0
+        while i < max_steps and (i < 2 or time.perf_counter() < t_end):
+            j = i % len(qs)
+            t0 = time.perf_counter()
+            oracle_step(qs[j][0], K, V, cent, kts[j][0], vts[j][0], S, ex)
+            times.append((time.perf_counter() - t0) * 1e6)
+            i += 1
+    if ex:
+        ex.shutdown()
+    return times
+
+
+# ---------------------------------------------------------------------------
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--contexts", type=int, nargs="+", default=[32768, 65536, HEADLINE_S])
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    headline = HEADLINE_S if HEADLINE_S in args.contexts else max(args.contexts)
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        threads = os.cpu_count() or 1
+        times = run_cpu(headline, args.seed, max(args.steps, 1), 60.0, threads)
+        v = float(np.mean(times))
+        line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "us", "n_gpus": args.gpus,
+                "steps": len(times), "warmup": 0, "ms_per_step": v / 1000.0,
+                "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic", "config": {"workload": workload_name(headline)},
+                "cpu_baseline": {"value": v, "unit": "us", "cores": threads, "kind": "port",
+                                 "sample": f"{len(times)} full decode steps at ctx {headline} "
+                                           f"(NumPy oracle port, {threads} threads over KV heads)"},
+                "e2e": {"value": v, "unit": "us", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
+
+    import torch
+    import torch.distributed as dist
+    if world > 1:
+        from datetime import timedelta
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    from adakv_b200 import _lib
+    _lib.lib()
+
+    results = {}
+    for S in args.contexts:
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(device)
+        r = run_ours(S, args.steps, args.warmup, args.seed + rank, device)
+        mean_us = float(np.mean(r["us"]))
+        if world > 1:
+            t = torch.tensor([mean_us, float(np.mean(r["us_e2e"]))], device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            mean_us, e2e_us = t.tolist()
+        else:
+            e2e_us = float(np.mean(r["us_e2e"]))
+        r["mean_us"], r["e2e_us"] = mean_us, e2e_us
+        results[S] = r
+        torch.cuda.empty_cache()
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        times = run_cpu(headline, args.seed, 10_000, args.cpu_seconds, 1)
+        cpu = {"value": float(np.mean(times)), "unit": "us", "cores": 1, "kind": "port",
+               "sample": f"{len(times)} full decode steps at ctx {headline} (NumPy oracle port of "
+                         f"the reference algorithm, incremental centroids, 1 thread)"}
+
+    if rank == 0:
+        peaks = {}
+        try:
+            with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+                peaks = json.load(f)
+        except OSError:
+            pass
+        peak = float(peaks.get("hbm_gbs", 6650.0))
+        r = results[headline]
+        v = r["mean_us"]
+        achieved = r["bytes"] / (v * 1e-6) / 1e9
+        ctx = {}
+        for S, rr in results.items():
+            a = rr["bytes"] / (rr["mean_us"] * 1e-6) / 1e9
+            ctx[str(S)] = {"us": rr["mean_us"], "us_median": float(np.median(rr["us"])),
+                           "us_p90": float(np.percentile(rr["us"], 90)), "e2e_us": rr["e2e_us"],
+                           "bytes_per_step": rr["bytes"], "achieved_gbs": a, "frac": a / peak,
+                           **{k: v2 for k, v2 in rr["detail"].items()}}
+        line = {
+            "metric": METRIC, "value": v, "unit": "us", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": v / 1000.0, "higher_is_better": False,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded Gaussian K/V/q, planted retrieval blocks, recency heads)",
+            "config": {"workload": workload_name(headline),
+                       "parallelism": f"replicas x{world} (batch-1 per GPU, no collective)",
+                       "l2": "flushed between steps (256 MB write, outside the timed events)",
+                       "timing": "CUDA events per step around one CUDA-graph replay of the 5 kernels"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": None,
+                         "scope": "whole decode step (all 5 kernels); bytes = fp32 centroid "
+                                  "table + union of selected K/V blocks per KV head + append",
+                         "peak_source": "MEASURED_PEAKS.json hbm_gbs" if peaks else "fallback"},
+            "cpu_baseline": cpu,
+            "e2e": {"value": r["e2e_us"], "unit": "us", "h2d_bytes_per_step": r["h2d"],
+                    "d2h_bytes_per_step": r["d2h"],
+                    "path": "BatchedDecoder.append + .step (C ABI) with pinned host q/k/v in, out back"},
+            "gpu_launches": 5 * args.steps,
+            "clocks": r["clocks"],
+            "contexts": ctx,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,185 @@
+/*
+ * adakv_b200.h -- C ABI of the B200 (sm_100a) AdaKV decode hot path.
+ *
+ * One decode step of AdaKV (query-aware, per-head-adaptive block-sparse
+ * attention) runs as hand-written CUDA kernels behind these entry points:
+ *
+ *   adakv_centroid_build   per-block key centroids after prefill        (a)
+ *   adakv_kv_append        in-place KV append + trailing-centroid refresh (a)
+ *   adakv_centroid_refresh trailing-centroid refresh of a caller-grown cache (a)
+ *   adakv_plan             q.centroid estimator, entropy budget, top-k  (b)(c)
+ *   adakv_attend           ragged block-sparse split-KV flash decode    (d)
+ *   adakv_decode_step      adakv_plan followed by adakv_attend          (b)-(d)
+ *
+ * Conventions
+ *   - Every function returns ADAKV_OK (0) or an error code; the message of
+ *     the last error on the calling thread is returned by adakv_last_error().
+ *     Arguments are validated on the host before anything is launched.
+ *   - Pointers are device pointers unless stated otherwise.  Nothing here
+ *     allocates device memory: scratch lives in a caller-provided workspace
+ *     (size from adakv_*_workspace_bytes, zero-filled once before first use;
+ *     the kernels leave its counters at zero again after every call).
+ *   - All work is enqueued on `stream` (a cudaStream_t passed as void*); no
+ *     function synchronises the host except adakv_read_status.
+ *   - Tensors are [batch, heads, tokens, head_dim] views described by
+ *     adakv_view; head_dim must be contiguous and each row 16-byte aligned.
+ *   - q/K/V/out share one element type (adakv_geometry.dtype); centroids and
+ *     scores are float32.
+ *
+ * Reference interfaces replaced (paths inside the adakv project):
+ *   adakv/attention.py:119-139  AdaKVCache.append_prefill   -> adakv_centroid_build
+ *   adakv/runtime.py:43-60      update_cache_decode         -> adakv_kv_append
+ *   adakv/attention.py:141-146  AdaKVCache.append_decode    -> adakv_kv_append
+ *   adakv/attention.py:149-247  plan_selection              -> adakv_plan
+ *   adakv/kernels/block_sparse_decode.py:103-135 block_sparse_decode -> adakv_attend
+ *   adakv/attention.py:250-268  adakv_decode_attention      -> adakv_decode_step
+ *   adakv/runtime.py:85-112     adakv_decode_step           -> adakv_decode_step
+ */
+#ifndef ADAKV_B200_H_
+#define ADAKV_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ADAKV_B200_ABI_VERSION 1
+
+/* element types of q / K / V / out */
+#define ADAKV_DTYPE_F32 0
+#define ADAKV_DTYPE_F16 1
+#define ADAKV_DTYPE_BF16 2
+
+/* budget policies (adakv/budget.py:45-86) */
+#define ADAKV_POLICY_FIXED 0    /* every head gets round(target) blocks           */
+#define ADAKV_POLICY_ADAPTIVE 1 /* surplus split by normalised score entropy       */
+
+/* return codes */
+#define ADAKV_OK 0
+#define ADAKV_ERR_INVALID 1     /* bad argument (reference: ValueError / assert)   */
+#define ADAKV_ERR_UNSUPPORTED 2 /* valid but not built (e.g. head_dim 96)          */
+#define ADAKV_ERR_CUDA 3        /* a CUDA runtime call failed                      */
+
+/* device status bits (adakv_read_status) */
+#define ADAKV_ST_WAIT_TIMEOUT 1u /* a bounded device wait gave up                   */
+#define ADAKV_ST_BAD_BLOCK_ID 2u /* a block table entry was outside [0, nb)        */
+#define ADAKV_ST_BAD_SEL_LEN 4u  /* sel_lens[h] exceeded the table width          */
+#define ADAKV_ST_BAD_SEQ_LEN 8u  /* seq_lens[b] outside [1, max_seq_len]           */
+
+/* Problem geometry.  One decode query token per sequence. */
+typedef struct adakv_geometry {
+  int32_t batch;       /* B sequences                                        */
+  int32_t n_q_heads;   /* Hq                                                 */
+  int32_t n_kv_heads;  /* Hkv; Hq % Hkv == 0, Hq / Hkv <= 16                 */
+  int32_t head_dim;    /* D: 64 or 128                                       */
+  int32_t block_size;  /* tokens per block: 16 or 32                         */
+  int32_t max_seq_len; /* host-side bound of every seq_lens[b]               */
+  int32_t nb_cap;      /* block capacity of the centroid table, >= ceil(max_seq_len / block_size) */
+  int32_t dtype;       /* ADAKV_DTYPE_*                                      */
+} adakv_geometry;
+
+/* A [B, H, S, D] tensor view (element strides; the D stride is 1). */
+typedef struct adakv_view {
+  void* data;
+  int64_t stride_b;
+  int64_t stride_h;
+  int64_t stride_s; /* ignored for q and out */
+} adakv_view;
+
+/* Selection knobs, named and defaulted as plan_selection
+ * (adakv/attention.py:149-162): avg_budget, k_min=2, k_max=64,
+ * n_sink_blocks=1, n_local_blocks=4, c_min=1, temperature=1.0,
+ * policy=ADAKV_POLICY_ADAPTIVE. */
+typedef struct adakv_select_params {
+  double avg_budget;
+  double temperature;
+  int32_t k_min;
+  int32_t k_max;
+  int32_t n_sink_blocks;
+  int32_t n_local_blocks;
+  int32_t c_min;
+  int32_t policy;
+} adakv_select_params;
+
+/* ABI version of the loaded library (ADAKV_B200_ABI_VERSION). */
+int adakv_abi_version(void);
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* adakv_last_error(void);
+
+/* Width of the block table adakv_plan writes: the largest per-head count
+ * this geometry and these knobs can produce (plan_selection's max_sel without
+ * the host sync of adakv/attention.py:242). */
+int32_t adakv_plan_table_width(const adakv_geometry* geo, const adakv_select_params* sp);
+
+/* Workspace bytes for adakv_plan / adakv_decode_step. */
+size_t adakv_plan_workspace_bytes(const adakv_geometry* geo, const adakv_select_params* sp);
+
+/* Workspace bytes for a stand-alone adakv_attend over a table of `table_width`. */
+size_t adakv_attend_workspace_bytes(const adakv_geometry* geo, int32_t table_width);
+
+/* Centroid table from a prefilled cache (adakv/attention.py:119-139,
+ * oracle adakv/estimator.py:27-48): centroid[b, h, j, :] = mean of the keys of
+ * block j over its real tokens, float32, summed in token order.
+ * k: [B, Hkv, S, D]; centroid: [B, Hkv, nb_cap, D] float32 contiguous;
+ * seq_lens: [B] int32 device array or NULL (every sequence max_seq_len). */
+int adakv_centroid_build(const adakv_geometry* geo, const adakv_view* k, const int32_t* seq_lens,
+                         float* centroid, void* stream);
+
+/* Append n_new tokens per sequence in place and refresh the centroids of every
+ * block they touch (adakv/runtime.py:43-60, without the full-cache torch.cat).
+ * seq_lens[b] is the length AFTER the append; the new tokens land at
+ * [seq_lens[b] - n_new, seq_lens[b]).  k_new/v_new: [B, Hkv, n_new, D]. */
+int adakv_kv_append(const adakv_geometry* geo, const adakv_view* k_cache, const adakv_view* v_cache,
+                    const adakv_view* k_new, const adakv_view* v_new, int32_t n_new,
+                    const int32_t* seq_lens, float* centroid, void* stream);
+
+/* Recompute the centroids of every block touched by the last n_new tokens of
+ * each sequence, reading the cache only (the tokens were already written by
+ * the caller, e.g. a HuggingFace DynamicCache).  Same numerics as
+ * adakv_centroid_build on those blocks. */
+int adakv_centroid_refresh(const adakv_geometry* geo, const adakv_view* k, int32_t n_new,
+                           const int32_t* seq_lens, float* centroid, void* stream);
+
+/* Block selection for one decode query per sequence (adakv/attention.py:149-247):
+ * scores = q . centroid (GQA folded, unscaled), per-head budget from the
+ * normalised entropy of softmax(scores / T) with the mean pinned to
+ * avg_budget, sink/local blocks forced, top-k of the rest (ties -> lowest
+ * block index).  Writes block_table[(b*Hq + h) * table_width + i] for
+ * i < sel_lens[b*Hq + h] in ascending block order.  scores_out (nullable):
+ * [B, Hq, nb_cap] float32 copy of the block scores. */
+int adakv_plan(const adakv_geometry* geo, const adakv_select_params* sp, const adakv_view* q,
+               const float* centroid, const int32_t* seq_lens, int32_t* block_table,
+               int32_t table_width, int32_t* sel_lens, float* scores_out, void* workspace,
+               size_t workspace_bytes, void* stream);
+
+/* Ragged block-sparse decode attention over a given table
+ * (adakv/kernels/block_sparse_decode.py:103-135): out[b, h] = softmax over the
+ * tokens of the listed blocks of (q . k) * sm_scale, times V; tokens at or past
+ * seq_lens[b] are masked.  Rows with sel_lens 0 produce zeros. */
+int adakv_attend(const adakv_geometry* geo, const adakv_view* q, const adakv_view* k,
+                 const adakv_view* v, const int32_t* block_table, int32_t table_width,
+                 const int32_t* sel_lens, const int32_t* seq_lens, float sm_scale,
+                 const adakv_view* out, void* workspace, size_t workspace_bytes, void* stream);
+
+/* adakv_plan + attention over its selection, with no host synchronisation
+ * in between (adakv/attention.py:250-268, adakv/runtime.py:85-112).
+ * The workspace is sized by adakv_plan_workspace_bytes. */
+int adakv_decode_step(const adakv_geometry* geo, const adakv_select_params* sp,
+                      const adakv_view* q, const adakv_view* k, const adakv_view* v,
+                      const float* centroid, const int32_t* seq_lens, float sm_scale,
+                      int32_t* block_table, int32_t table_width, int32_t* sel_lens,
+                      const adakv_view* out, void* workspace, size_t workspace_bytes,
+                      void* stream);
+
+/* Synchronise `stream`, copy the workspace's device status word (ADAKV_ST_*
+ * bits) to *status and clear it. */
+int adakv_read_status(void* workspace, uint32_t* status, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ADAKV_B200_H_ */

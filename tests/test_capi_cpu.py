@@ -1,0 +1,158 @@
+"""C-ABI checks that need no GPU: the library loads, exports every function
+``include/adakv_b200.h`` declares, and rejects bad arguments on the host
+(before any CUDA call) with the documented codes and messages."""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+
+from adakv_b200 import _lib
+from adakv_b200.build import LIB, build
+
+HEADER = os.path.join(os.path.dirname(__file__), "..", "include", "adakv_b200.h")
+
+
+@pytest.fixture(scope="module")
+def lib():
+    build()
+    return _lib.lib()
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?\w+\**\s+\**(adakv_\w+)\s*\(", text, flags=re.M)))
+
+
+def test_header_declares_the_entry_points():
+    names = declared_functions()
+    for n in ["adakv_abi_version", "adakv_last_error", "adakv_plan_table_width",
+              "adakv_plan_workspace_bytes", "adakv_attend_workspace_bytes", "adakv_centroid_build",
+              "adakv_kv_append", "adakv_centroid_refresh", "adakv_plan", "adakv_attend",
+              "adakv_decode_step", "adakv_read_status"]:
+        assert n in names, n
+
+
+def test_library_exports_every_declared_symbol(lib):
+    out = subprocess.run(["nm", "-D", "--defined-only", LIB], capture_output=True, text=True,
+                         check=True).stdout
+    exported = set(re.findall(r"\sT\s+(\w+)$", out, flags=re.M))
+    missing = [n for n in declared_functions() if n not in exported]
+    assert not missing, f"declared but not exported: {missing}"
+    for n in declared_functions():
+        assert hasattr(lib, n)
+
+
+def test_no_torch_in_the_abi():
+    code = re.sub(r"/\*.*?\*/", "", open(HEADER).read(), flags=re.S)
+    assert "torch" not in code.lower()
+    out = subprocess.run(["ldd", LIB], capture_output=True, text=True).stdout
+    assert "libtorch" not in out and "libc10" not in out
+
+
+def test_abi_version(lib):
+    assert lib.adakv_abi_version() == 1
+
+
+def geo(**kw):
+    d = dict(batch=1, n_q_heads=32, n_kv_heads=8, head_dim=128, block_size=16, max_seq_len=4096,
+             nb_cap=256, dtype=_lib.DTYPE_BF16)
+    d.update(kw)
+    return _lib.Geometry(*[d[f] for f, _ in _lib.Geometry._fields_])
+
+
+def params(**kw):
+    d = dict(avg_budget=64.0, temperature=1.0, k_min=2, k_max=512, n_sink_blocks=1,
+             n_local_blocks=4, c_min=1, policy=_lib.POLICY_ADAPTIVE)
+    d.update(kw)
+    return _lib.SelectParams(*[d[f] for f, _ in _lib.SelectParams._fields_])
+
+
+def test_table_width_and_workspace_sizes(lib):
+    g, p = geo(), params()
+    assert lib.adakv_plan_table_width(g, p) == 256          # min(k_max, nb_cap)
+    assert lib.adakv_plan_table_width(g, params(k_max=64)) == 64
+    assert lib.adakv_plan_table_width(g, params(k_max=2, n_sink_blocks=3, n_local_blocks=4)) == 8
+    ws = lib.adakv_plan_workspace_bytes(g, p)
+    assert ws > 0 and ws % 256 == 0
+    assert lib.adakv_attend_workspace_bytes(g, 64) > 0
+    assert lib.adakv_attend_workspace_bytes(g, 0) == 0
+
+
+@pytest.mark.parametrize("bad,code,text", [
+    (dict(n_q_heads=30), _lib.ERR_INVALID, "multiple"),
+    (dict(head_dim=96), _lib.ERR_UNSUPPORTED, "head_dim"),
+    (dict(block_size=8), _lib.ERR_UNSUPPORTED, "block_size"),
+    (dict(nb_cap=10), _lib.ERR_INVALID, "nb_cap"),
+    (dict(dtype=7), _lib.ERR_INVALID, "dtype"),
+    (dict(batch=0), _lib.ERR_INVALID, "batch"),
+    (dict(n_q_heads=64, n_kv_heads=2), _lib.ERR_UNSUPPORTED, "group"),
+])
+def test_geometry_validation(lib, bad, code, text):
+    q = _lib.View(0x1000, 0, 128, 0)
+    rc = lib.adakv_plan(geo(**bad), params(), q, 0x1000, None, 0x1000, 256, 0x1000, None, 0x1000,
+                        1 << 30, None)
+    assert rc == code
+    assert text in lib.adakv_last_error().decode()
+
+
+@pytest.mark.parametrize("bad,text", [
+    (dict(policy=5), "budget_policy"),
+    (dict(k_max=0), "k_max"),
+    (dict(avg_budget=float("nan")), "avg_budget"),
+    (dict(c_min=-1), "c_min"),
+])
+def test_param_validation(lib, bad, text):
+    q = _lib.View(0x1000, 4096, 128, 0)
+    rc = lib.adakv_plan(geo(), params(**bad), q, 0x1000, None, 0x1000, 512, 0x1000, None, 0x1000,
+                        1 << 30, None)
+    assert rc == _lib.ERR_INVALID
+    assert text in lib.adakv_last_error().decode()
+
+
+def test_pointer_and_workspace_validation(lib):
+    g, p = geo(), params()
+    good_q = _lib.View(0x1000, 4096, 128, 0)
+    # misaligned q
+    rc = lib.adakv_plan(g, p, _lib.View(0x1002, 4096, 128, 0), 0x1000, None, 0x1000, 512, 0x1000,
+                        None, 0x1000, 1 << 30, None)
+    assert rc == _lib.ERR_INVALID and "aligned" in lib.adakv_last_error().decode()
+    # table too narrow
+    rc = lib.adakv_plan(g, p, good_q, 0x1000, None, 0x1000, 8, 0x1000, None, 0x1000, 1 << 30, None)
+    assert rc == _lib.ERR_INVALID and "table_width" in lib.adakv_last_error().decode()
+    # workspace too small
+    rc = lib.adakv_plan(g, p, good_q, 0x1000, None, 0x1000, 512, 0x1000, None, 0x1000, 64, None)
+    assert rc == _lib.ERR_INVALID and "workspace" in lib.adakv_last_error().decode()
+    # strides not multiples of 16 bytes
+    kv = _lib.View(0x1000, 4096 * 128, 4096 * 128, 3)
+    rc = lib.adakv_centroid_build(g, kv, None, 0x1000, None)
+    assert rc == _lib.ERR_INVALID and "strides" in lib.adakv_last_error().decode()
+    rc = lib.adakv_kv_append(g, kv, kv, kv, kv, 0, None, 0x1000, None)
+    assert rc == _lib.ERR_INVALID
+
+
+def test_python_wrappers_refuse_cpu_tensors():
+    import torch
+    from adakv_b200.attention import AdaKVCache
+    from adakv_b200.kernels.block_sparse_decode import block_sparse_decode
+    k = torch.zeros(2, 64, 64)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        AdaKVCache(16).append_prefill(k, k)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        block_sparse_decode(torch.zeros(4, 64), k, k, torch.zeros(4, 2, dtype=torch.int32),
+                            torch.ones(4, dtype=torch.int32), 16)
+    with pytest.raises(NotImplementedError):
+        AdaKVCache(16, estimator="minmax").append_prefill(k, k)
+    with pytest.raises(ValueError):
+        AdaKVCache(16, estimator="bogus")
+
+
+def test_missing_library_fails_loudly(monkeypatch, tmp_path):
+    monkeypatch.setattr(_lib, "LIB_PATH", str(tmp_path / "nope.so"))
+    monkeypatch.setattr(_lib, "_lib", None)
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        _lib.lib()
