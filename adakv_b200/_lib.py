@@ -62,8 +62,9 @@ _SIGNATURES = {
                                     ctypes.c_int32, _vp, _vp, ctypes.c_float, _P(View), _vp,
                                     ctypes.c_size_t, _vp]),
     "adakv_decode_step": (ctypes.c_int, [_P(Geometry), _P(SelectParams), _P(View), _P(View),
-                                         _P(View), _vp, _vp, ctypes.c_float, _vp, ctypes.c_int32,
-                                         _vp, _P(View), _vp, ctypes.c_size_t, _vp]),
+                                         _P(View), _P(View), _P(View), ctypes.c_int32, _vp, _vp,
+                                         ctypes.c_float, _vp, ctypes.c_int32, _vp, _P(View), _vp,
+                                         ctypes.c_size_t, _vp]),
     "adakv_read_status": (ctypes.c_int, [_vp, _P(ctypes.c_uint32), _vp]),
 }
 
@@ -149,15 +150,15 @@ def geometry(batch, n_q_heads, n_kv_heads, head_dim, block_size, max_seq_len, nb
 
 
 # ---------------------------------------------------------------------------
-# workspace: one zero-initialised device buffer per (device, stream), grown on
-# demand.  The kernels leave its counters at zero after every call.
+# workspace: one zero-initialised device buffer per (device, stream, kind),
+# grown on demand.  Calls that share one are ordered by their stream.
 # ---------------------------------------------------------------------------
 _workspaces: dict = {}
 
 
-def workspace(nbytes: int, device) -> torch.Tensor:
+def workspace(nbytes: int, device, kind: str = "plan") -> torch.Tensor:
     device = torch.device(device)
-    key = (device.index, stream_ptr(device))
+    key = (device.index, stream_ptr(device), kind)
     ws = _workspaces.get(key)
     if ws is None or ws.numel() < nbytes:
         ws = torch.zeros(max(int(nbytes), 256), dtype=torch.uint8, device=device)

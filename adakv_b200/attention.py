@@ -291,7 +291,8 @@ def _decode(q, cache, avg_budget, k_min, k_max, n_sink_blocks, n_local_blocks, t
     with torch.cuda.device(q.device):
         _lib.check(L.adakv_decode_step(
             geo, sp, _lib.view4(q.unsqueeze(0)), _lib.view4(cache.k.unsqueeze(0)),
-            _lib.view4(cache.v.unsqueeze(0)), cache._cbuf.data_ptr(), None, float(sm_scale),
+            _lib.view4(cache.v.unsqueeze(0)), None, None, 0, cache._cbuf.data_ptr(), None,
+            float(sm_scale),
             block_table.data_ptr(), width, sel_lens.data_ptr(), _lib.view4(out.unsqueeze(0)),
             ws.data_ptr(), ws.numel(), _lib.stream_ptr(q.device)))
     if tracing_enabled():

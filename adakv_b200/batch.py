@@ -101,16 +101,32 @@ class BatchedDecoder:
                 self.workspace.data_ptr(), self.ws_bytes, self._stream()))
         return self.block_table, self.sel_lens
 
-    def step(self, q, sm_scale=None, out=None):
-        """Selection + attention for ``q`` ``[B, Hq, D]``; returns ``[B, Hq, D]``."""
+    def step(self, q, sm_scale=None, out=None, k_new=None, v_new=None, advance=True):
+        """Selection + attention for ``q`` ``[B, Hq, D]``; returns ``[B, Hq, D]``.
+
+        With ``k_new`` / ``v_new`` (``[B, Hkv, n, D]``) the step first appends those
+        tokens (fused into the estimator kernel: in-place cache write + centroid
+        refresh).  ``advance=False`` overwrites the last ``n`` tokens instead of
+        growing the sequences (fixed-context benchmarking)."""
         out = self.out if out is None else out
         scale = 1.0 / math.sqrt(self.D) if sm_scale is None else float(sm_scale)
+        n_new = 0
+        kn = vn = None
+        if k_new is not None:
+            n_new = k_new.shape[2]
+            if advance:
+                if max(self.host_seq_lens) + n_new > self.capacity:
+                    raise ValueError("cache capacity exceeded")
+                self.host_seq_lens = [s + n_new for s in self.host_seq_lens]
+                self.seq_lens.add_(n_new)
+            kn, vn = _lib.view4(k_new), _lib.view4(v_new)
         with torch.cuda.device(self.device):
             _lib.check(_lib.lib().adakv_decode_step(
                 self.geometry(), self.params, _lib.view4(q), _lib.view4(self.k),
-                _lib.view4(self.v), self.centroid.data_ptr(), self.seq_lens.data_ptr(), scale,
-                self.block_table.data_ptr(), self.table_width, self.sel_lens.data_ptr(),
-                _lib.view4(out), self.workspace.data_ptr(), self.ws_bytes, self._stream()))
+                _lib.view4(self.v), kn, vn, n_new, self.centroid.data_ptr(),
+                self.seq_lens.data_ptr(), scale, self.block_table.data_ptr(), self.table_width,
+                self.sel_lens.data_ptr(), _lib.view4(out), self.workspace.data_ptr(),
+                self.ws_bytes, self._stream()))
         return out
 
     def attend(self, q, block_table, sel_lens, sm_scale=None, out=None):

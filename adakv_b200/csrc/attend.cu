@@ -1,120 +1,183 @@
-// (d) Fused ragged block-sparse split-KV flash decode.
+// (d) Fused ragged block-sparse split-KV flash decode over the GQA union.
 //
 // out[b, h] = softmax_t((q[b, h] . K[b, h/g, t]) * sm_scale) . V[b, h/g, t] over the
-// tokens t of the selected blocks of query head h (tokens >= seq_len masked), the
-// semantics of the reference kernel (adakv/kernels/block_sparse_decode.py:51-100)
-// and of the oracle (adakv/reference.py:76-80).
+// tokens t of head h's selected blocks (tokens >= seq_len masked): the semantics
+// of the reference kernel (adakv/kernels/block_sparse_decode.py:51-100) and of
+// the oracle (adakv/reference.py:76-80).
 //
-// Work decomposition: head h's selected list is cut into work items of up to C
-// blocks (C = item_blocks); item i carries {b, h, first item of the head, count}
-// plus its C block ids, so a CTA reaches its K/V with one dependent load.  The
-// grid is persistent (grid-stride over items).  Per item, 128 threads issue
-// cp.async 16-byte copies of all C blocks' K and V rows into shared memory
-// (zero-fill past seq_len), then each of the 4 warps runs an online softmax over
-// one block at a time: a token row is spread over D*sizeof(T)/16 lanes (16 for
-// bf16 D=128), dot products finish with xor shuffles, and the lane keeps its
-// 16-byte slice of the output accumulator.  Warps merge in shared memory into
-// the item's (m, l, o); a head with one item writes its output directly,
-// otherwise the item's partial goes to the workspace and the last item of the
-// head to finish (atomic ticket) merges all partials in item order and writes
-// the output -- no second kernel, no spinning.
+// One thread-block cluster per (sequence, KV head).  The g query heads of the
+// group select overlapping block sets; the cluster reads their selection
+// bitmaps, forms the union, and splits the union evenly over its CTAs, so every
+// selected K/V block is read from HBM exactly once for the whole group (the
+// split-KV axis).  Each CTA gathers its blocks with 16-byte cp.async copies
+// (zero-fill past seq_len) into a double-buffered shared-memory ring, and warp
+// h of the CTA runs the online softmax of query head h over the blocks whose
+// head bit is set: a token row is spread over D*sizeof(T)/16 lanes, dot products
+// finish with xor shuffles, the lane keeps its 16-byte slice of the output.
+// The per-CTA partials (m, l, o) are merged across the cluster through
+// distributed shared memory -- no global scratch, no atomics, no second kernel.
 //
-// HBM traffic: the selected K/V blocks (bs * D * sizeof(T) * 2 bytes each), q,
-// out; partials stay in L2.
+// HBM traffic: the union of the group's selected K/V blocks
+// (bs * D * sizeof(T) * 2 bytes per block) plus the selection bitmaps, q and out.
+#include <cooperative_groups.h>
+
 #include "kernels.h"
 
 namespace adakv {
 
+namespace cg = cooperative_groups;
+
+constexpr int kAttendMaxThreads = 512;  // g <= 16 warps
+
+__device__ __forceinline__ void cp_async_wait_one() {
+  asm volatile("cp.async.wait_group 1;" ::: "memory");
+}
+
+// shared-memory carve-up of one attend CTA (host and device agree on it)
+struct AttendSmem {
+  size_t kv, hw, list, mask, part, total;
+};
+
+__host__ __device__ inline AttendSmem attend_smem_layout(int elt, int D, int BS, int nbt, int g,
+                                                         int nw_max, int slice_cap) {
+  auto al = [](size_t x) { return (x + 15) / 16 * 16; };
+  AttendSmem s;
+  s.kv = 0;
+  s.hw = s.kv + al((size_t)2 * 2 * nbt * BS * D * elt);
+  s.list = s.hw + al((size_t)g * nw_max * 4);
+  s.mask = s.list + al((size_t)slice_cap * 4);
+  s.part = s.mask + al((size_t)slice_cap * 4);
+  s.total = s.part + al((size_t)(32 + g * D) * 4);
+  return s;
+}
+
 template <typename T, int D, int BS>
-__global__ void __launch_bounds__(kAttendThreads) attend_kernel(AttendParams p) {
+__global__ void __launch_bounds__(kAttendMaxThreads) attend_kernel(AttendParams p) {
   constexpr int VEC = 16 / sizeof(T);       // elements per 16-byte chunk
   constexpr int LPT = D / VEC;              // lanes per token row
   constexpr int TPP = 32 / LPT;             // token rows per warp pass
   constexpr int PASSES = BS / TPP;
   constexpr int ROWC = D / VEC;             // 16-byte chunks per token row
-  constexpr int NW = kAttendThreads / 32;
+  constexpr int BLK = BS * D;               // elements of one K (or V) block
   static_assert(LPT <= 32 && BS % TPP == 0, "unsupported tile shape");
-  extern __shared__ __align__(16) unsigned char smem_raw[];
-  T* Ks = reinterpret_cast<T*>(smem_raw);
-  T* Vs = Ks + (size_t)p.item_blocks * BS * D;
-  __shared__ int s_blk[kMaxItemBlocks];
-  __shared__ float s_m[NW], s_l[NW];
-  __shared__ float s_o[NW][D];
-  __shared__ int s_last;
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ int scan_scratch[33];
 
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int C = p.item_blocks;
-  const int d0 = (lane % LPT) * VEC;
-  const int tl = lane / LPT;
+  cg::cluster_group cl = cg::this_cluster();
+  const int rank = (int)cl.block_rank();
+  const int CL = (int)cl.num_blocks();
+  const int kvh = blockIdx.y, b = blockIdx.z;
+  const int nthr = blockDim.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = p.g, NBT = p.nbt;
+  const AttendSmem L = attend_smem_layout(sizeof(T), D, BS, NBT, g, p.nw_max, p.slice_cap);
+  T* kbuf = reinterpret_cast<T*>(smem + L.kv);                 // [2][NBT][BS][D]
+  T* vbuf = kbuf + (size_t)2 * NBT * BLK;
+  uint32_t* hw = reinterpret_cast<uint32_t*>(smem + L.hw);     // [g][nw_max] head words
+  int* list = reinterpret_cast<int*>(smem + L.list);           // [slice_cap] block ids
+  uint32_t* lmask = reinterpret_cast<uint32_t*>(smem + L.mask);  // [slice_cap] head bits
+  float* pm = reinterpret_cast<float*>(smem + L.part);         // [16] running max per head
+  float* pl = pm + 16;                                         // [16] denominators
+  float* po = pl + 16;                                         // [g][D] numerators
+
   pdl_wait();
+  int S = seq_len_of(p.seq_lens, b, p.max_seq_len);
+  if (S < 0 || S > p.max_seq_len) S = 0;
+  const int nb = ceil_div(S, BS);
+  const int nw = ceil_div(nb, 32);
+  const int row0 = b * p.Hq + kvh * g;
 
-  // heads with an empty selection produce zeros
-  for (int r = blockIdx.x; r < p.B * p.Hq; r += gridDim.x) {
-    if (p.sel_lens[r] <= 0 && tid < D) {
-      const int b = r / p.Hq, h = r % p.Hq;
-      static_cast<T*>(const_cast<void*>(p.out.data))[b * p.out.sb + h * p.out.sh + tid] = from_f32<T>(0.f);
+  // ---- the group's selection bitmaps and their union ----
+  for (int idx = tid; idx < g * nw; idx += nthr) {
+    const int hh = idx / nw, w = idx - hh * nw;
+    hw[hh * p.nw_max + w] = p.bitmap[(int64_t)(row0 + hh) * p.bm_words + w];
+  }
+  __syncthreads();
+  auto uni = [&](int w) -> uint32_t {
+    uint32_t u = 0;
+    for (int hh = 0; hh < g; ++hh) u |= hw[hh * p.nw_max + w];
+    return u;
+  };
+  const int wpt = ceil_div(nw, nthr);
+  const int w0 = imin(tid * wpt, nw), w1 = imin(w0 + wpt, nw);
+  int cnt = 0;
+  for (int w = w0; w < w1; ++w) cnt += __popc(uni(w));
+  const int before = block_exclusive_scan(cnt, scan_scratch);
+  const int U = scan_scratch[32];
+  const int lo = (int)((int64_t)U * rank / CL), hi = (int)((int64_t)U * (rank + 1) / CL);
+  int rk = before;
+  for (int w = w0; w < w1 && rk < hi; ++w) {
+    uint32_t u = uni(w);
+    while (u && rk < hi) {
+      const int bit = __ffs(u) - 1;
+      u &= u - 1u;
+      if (rk >= lo) {
+        uint32_t m = 0;
+        for (int hh = 0; hh < g; ++hh) m |= ((hw[hh * p.nw_max + w] >> bit) & 1u) << hh;
+        list[rk - lo] = w * 32 + bit;
+        lmask[rk - lo] = m;
+      }
+      ++rk;
     }
   }
+  __syncthreads();
+  const int n = hi - lo;
 
-  const int total = *p.total_items;
-  for (int item = blockIdx.x; item < total; item += gridDim.x) {
-    const int4 hdr = p.work_hdr[item];
-    const int b = hdr.x, h = hdr.y, base = hdr.z, K = hdr.w;
-    const int first = (item - base) * C;
-    const int cnt = imin(C, K - first);
-    const int kvh = h / p.g;
-    int S = seq_len_of(p.seq_lens, b, p.max_seq_len);
-    if (S < 0 || S > p.max_seq_len) S = 0;
-    const int nb = ceil_div(S, BS);
-    if (tid < cnt) {
-      int blk = p.work_blk[(int64_t)item * C + tid];
-      if (blk < 0 || blk >= nb) {
-        report(p.status, ADAKV_ST_BAD_BLOCK_ID);
-        blk = -1;
+  // ---- gather: double-buffered batches of NBT blocks ----
+  const T* kbase = static_cast<const T*>(p.k.data) + b * p.k.sb + kvh * p.k.sh;
+  const T* vbase = static_cast<const T*>(p.v.data) + b * p.v.sb + kvh * p.v.sh;
+  auto issue = [&](int batch) {
+    const int first = batch * NBT;
+    const int cntb = imin(NBT, n - first);
+    if (cntb > 0) {
+      T* kd = kbuf + (size_t)(batch & 1) * NBT * BLK;
+      T* vd = vbuf + (size_t)(batch & 1) * NBT * BLK;
+      const int chunks = cntb * BS * ROWC;
+      for (int c = tid; c < chunks; c += nthr) {
+        const int slot = c / (BS * ROWC);
+        const int rem = c - slot * (BS * ROWC);
+        const int tok = rem / ROWC, col = rem - tok * ROWC;
+        const int pos = list[first + slot] * BS + tok;
+        const bool valid = pos < S;
+        const int64_t srow = valid ? (int64_t)pos : 0;
+        const size_t off = (size_t)slot * BLK + tok * D + col * VEC;
+        cp_async16(kd + off, kbase + srow * p.k.ss + col * VEC, valid);
+        cp_async16(vd + off, vbase + srow * p.v.ss + col * VEC, valid);
       }
-      s_blk[tid] = blk;
-    }
-    __syncthreads();
-
-    const T* kbase = static_cast<const T*>(p.k.data) + b * p.k.sb + kvh * p.k.sh;
-    const T* vbase = static_cast<const T*>(p.v.data) + b * p.v.sb + kvh * p.v.sh;
-    const int nchunks = cnt * BS * ROWC;
-    for (int c = tid; c < nchunks; c += kAttendThreads) {
-      const int slot = c / (BS * ROWC);
-      const int rem = c - slot * (BS * ROWC);
-      const int tok = rem / ROWC, col = rem - tok * ROWC;
-      const int blk = s_blk[slot];
-      const int pos = blk * BS + tok;
-      const bool valid = blk >= 0 && pos < S;
-      const int64_t srow = valid ? (int64_t)pos : 0;
-      const size_t soff = ((size_t)slot * BS + tok) * D + col * VEC;
-      cp_async16(Ks + soff, kbase + srow * p.k.ss + col * VEC, valid);
-      cp_async16(Vs + soff, vbase + srow * p.v.ss + col * VEC, valid);
     }
     cp_async_commit();
+  };
+  issue(0);
+  issue(1);
 
-    float qf[VEC];
-    {
-      const uint4 u = *reinterpret_cast<const uint4*>(static_cast<const T*>(p.q.data) + b * p.q.sb +
-                                                      h * p.q.sh + d0);
-      Unpack16<T>::run(u, qf);
-    }
-    cp_async_wait_all();
-    __syncthreads();
-
-    float m_run = -INFINITY, l_run = 0.f;
-    float o[VEC];
+  const int d0 = (lane % LPT) * VEC;
+  const int tl = lane / LPT;
+  float qf[VEC];
+  {
+    const uint4 u = *reinterpret_cast<const uint4*>(static_cast<const T*>(p.q.data) + b * p.q.sb +
+                                                    (int64_t)(kvh * g + warp) * p.q.sh + d0);
+    Unpack16<T>::run(u, qf);
+  }
+  float m_run = -INFINITY, l_run = 0.f;
+  float o[VEC];
 #pragma unroll
-    for (int e = 0; e < VEC; ++e) o[e] = 0.f;
+  for (int e = 0; e < VEC; ++e) o[e] = 0.f;
 
-    for (int slot = warp; slot < cnt; slot += NW) {
-      const int blk = s_blk[slot];
-      if (blk < 0) continue;
+  const int nbatches = ceil_div(n, NBT);
+  for (int bi = 0; bi < nbatches; ++bi) {
+    cp_async_wait_one();
+    __syncthreads();
+    const T* kt = kbuf + (size_t)(bi & 1) * NBT * BLK;
+    const T* vt = vbuf + (size_t)(bi & 1) * NBT * BLK;
+    const int first = bi * NBT;
+    const int cntb = imin(NBT, n - first);
+    for (int slot = 0; slot < cntb; ++slot) {
+      if (!((lmask[first + slot] >> warp) & 1u)) continue;  // warp-uniform
+      const int blk = list[first + slot];
       float sc[PASSES];
 #pragma unroll
       for (int pp = 0; pp < PASSES; ++pp) {
         const int tok = pp * TPP + tl;
-        const uint4 u = *reinterpret_cast<const uint4*>(Ks + ((size_t)slot * BS + tok) * D + d0);
+        const uint4 u = *reinterpret_cast<const uint4*>(kt + (size_t)slot * BLK + tok * D + d0);
         float kf[VEC];
         Unpack16<T>::run(u, kf);
         float part = 0.f;
@@ -130,8 +193,8 @@ __global__ void __launch_bounds__(kAttendThreads) attend_kernel(AttendParams p) 
 #pragma unroll
       for (int off = LPT; off < 32; off <<= 1) mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, off));
       const float m_new = fmaxf(m_run, mb);
-      if (m_new == -INFINITY) continue;  // every token so far is masked (warp-uniform)
-      const float alpha = expf(m_run - m_new);  // m_run = -inf -> 0
+      if (m_new == -INFINITY) continue;
+      const float alpha = expf(m_run - m_new);
       float l_part = 0.f;
 #pragma unroll
       for (int e = 0; e < VEC; ++e) o[e] *= alpha;
@@ -140,7 +203,7 @@ __global__ void __launch_bounds__(kAttendThreads) attend_kernel(AttendParams p) 
         const int tok = pp * TPP + tl;
         const float pt = expf(sc[pp] - m_new);
         l_part += pt;
-        const uint4 u = *reinterpret_cast<const uint4*>(Vs + ((size_t)slot * BS + tok) * D + d0);
+        const uint4 u = *reinterpret_cast<const uint4*>(vt + (size_t)slot * BLK + tok * D + d0);
         float vf[VEC];
         Unpack16<T>::run(u, vf);
 #pragma unroll
@@ -149,111 +212,83 @@ __global__ void __launch_bounds__(kAttendThreads) attend_kernel(AttendParams p) 
       l_run = l_run * alpha + l_part;
       m_run = m_new;
     }
-    // merge the token groups of the warp (lanes that share dims d0..)
-#pragma unroll
-    for (int off = LPT; off < 32; off <<= 1) {
-      l_run += __shfl_xor_sync(0xffffffffu, l_run, off);
-#pragma unroll
-      for (int e = 0; e < VEC; ++e) o[e] += __shfl_xor_sync(0xffffffffu, o[e], off);
-    }
-    if (lane < LPT) {
-#pragma unroll
-      for (int e = 0; e < VEC; ++e) s_o[warp][d0 + e] = o[e];
-    }
-    if (lane == 0) {
-      s_m[warp] = m_run;
-      s_l[warp] = l_run;
-    }
-    __syncthreads();
+    __syncthreads();  // the buffer is refilled next
+    issue(bi + 2);
+  }
+  cp_async_wait_all();
 
-    float M = s_m[0];
+  // ---- per-CTA partial of each head ----
 #pragma unroll
-    for (int w = 1; w < NW; ++w) M = fmaxf(M, s_m[w]);
-    float L = 0.f, O = 0.f;
-    if (M != -INFINITY) {
+  for (int off = LPT; off < 32; off <<= 1) {
+    l_run += __shfl_xor_sync(0xffffffffu, l_run, off);
 #pragma unroll
-      for (int w = 0; w < NW; ++w) {
-        const float f = (s_m[w] == -INFINITY) ? 0.f : expf(s_m[w] - M);
-        L += s_l[w] * f;
-        if (tid < D) O += s_o[w][tid] * f;
-      }
-    }
-    const int n_items = ceil_div(K, C);
-    T* orow = static_cast<T*>(const_cast<void*>(p.out.data)) + b * p.out.sb + h * p.out.sh;
-    if (n_items == 1) {
-      if (tid < D) orow[tid] = from_f32<T>(L > 0.f ? O / L : 0.f);
-    } else {
-      if (tid < D) p.part_o[(int64_t)item * D + tid] = O;
-      if (tid == 0) p.part_ml[item] = make_float2(M, L);
-      __threadfence();
-      __syncthreads();
-      if (tid == 0) s_last = (atomicAdd(&p.head_counter[b * p.Hq + h], 1) == n_items - 1);
-      __syncthreads();
-      if (s_last) {
-        __threadfence();
-        float M2 = -INFINITY;
-        for (int it = 0; it < n_items; ++it) M2 = fmaxf(M2, __ldcg(&p.part_ml[base + it]).x);
-        float L2 = 0.f, O2 = 0.f;
-        if (M2 != -INFINITY) {
-          for (int it = 0; it < n_items; ++it) {
-            const float2 ml = __ldcg(&p.part_ml[base + it]);
-            const float f = (ml.x == -INFINITY) ? 0.f : expf(ml.x - M2);
-            L2 += ml.y * f;
-            if (tid < D) O2 += __ldcg(&p.part_o[(int64_t)(base + it) * D + tid]) * f;
-          }
+    for (int e = 0; e < VEC; ++e) o[e] += __shfl_xor_sync(0xffffffffu, o[e], off);
+  }
+  if (lane < LPT) {
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) po[warp * D + d0 + e] = o[e];
+  }
+  if (lane == 0) {
+    pm[warp] = m_run;
+    pl[warp] = l_run;
+  }
+  cl.sync();
+
+  // ---- cluster merge: CTA `rank` finalises heads rank, rank + CL, ... ----
+  for (int hh = rank; hh < g; hh += CL) {
+    float M = -INFINITY;
+    for (int c = 0; c < CL; ++c) M = fmaxf(M, *cl.map_shared_rank(&pm[hh], c));
+    T* orow = static_cast<T*>(const_cast<void*>(p.out.data)) + b * p.out.sb +
+              (int64_t)(kvh * g + hh) * p.out.sh;
+    for (int d = tid; d < D; d += nthr) {
+      float Lsum = 0.f, O = 0.f;
+      if (M != -INFINITY) {
+        for (int c = 0; c < CL; ++c) {
+          const float mc = *cl.map_shared_rank(&pm[hh], c);
+          const float f = (mc == -INFINITY) ? 0.f : expf(mc - M);
+          Lsum += *cl.map_shared_rank(&pl[hh], c) * f;
+          O += *cl.map_shared_rank(&po[hh * D + d], c) * f;
         }
-        if (tid < D) orow[tid] = from_f32<T>(L2 > 0.f ? O2 / L2 : 0.f);
-        if (tid == 0) p.head_counter[b * p.Hq + h] = 0;
       }
+      orow[d] = from_f32<T>(Lsum > 0.f ? O / Lsum : 0.f);
     }
-    __syncthreads();  // shared tiles are reused by the next item
   }
+  cl.sync();  // keep this CTA's shared memory alive until every reader is done
+  pdl_launch_dependents();
 }
 
-// Stand-alone attend: build work items from a caller-given (block_table, sel_lens).
-// Pass 1 (one CTA): clamp counts, exclusive scan of per-head item counts.
-__global__ void __launch_bounds__(1024) items_scan_kernel(AttendParams p) {
-  __shared__ int scan_scratch[33];
-  const int rows = p.B * p.Hq;
-  int carry = 0;
-  for (int base = 0; base < rows; base += blockDim.x) {
-    const int r = base + threadIdx.x;
-    int items = 0;
-    if (r < rows) {
-      int k = p.sel_lens[r];
-      if (k > p.table_width || k < 0) {
-        report(p.status, ADAKV_ST_BAD_SEL_LEN);
-        k = k < 0 ? 0 : p.table_width;
-      }
-      items = ceil_div(k, p.item_blocks);
+// Stand-alone attend: caller-given (block_table, sel_lens) -> per-head bitmaps.
+// Duplicate ids collapse to one bit; ids outside [0, nb) are flagged and skipped.
+__global__ void __launch_bounds__(256) table_bitmap_kernel(TableParams p) {
+  extern __shared__ uint32_t sbits[];
+  const int h = blockIdx.x, b = blockIdx.y, row = b * p.Hq + h;
+  pdl_wait();
+  int S = seq_len_of(p.seq_lens, b, p.max_seq_len);
+  if (S < 0 || S > p.max_seq_len) {
+    if (threadIdx.x == 0 && h == 0) report(p.status, ADAKV_ST_BAD_SEQ_LEN);
+    S = 0;
+  }
+  const int nb = ceil_div(S, p.bs);
+  const int nw = ceil_div(nb, 32);
+  for (int w = threadIdx.x; w < nw; w += blockDim.x) sbits[w] = 0u;
+  __syncthreads();
+  int k = p.sel_lens[row];
+  if (k < 0 || k > p.table_width) {
+    if (threadIdx.x == 0) report(p.status, ADAKV_ST_BAD_SEL_LEN);
+    k = k < 0 ? 0 : p.table_width;
+  }
+  const int* trow = p.block_table + (int64_t)row * p.table_width;
+  for (int i = threadIdx.x; i < k; i += blockDim.x) {
+    const int blk = trow[i];
+    if (blk < 0 || blk >= nb) {
+      report(p.status, ADAKV_ST_BAD_BLOCK_ID);
+    } else {
+      atomicOr(&sbits[blk >> 5], 1u << (blk & 31));
     }
-    const int off = block_exclusive_scan(items, scan_scratch);
-    if (r < rows) p.head_item_base[r] = carry + off;
-    carry += scan_scratch[32];
-    __syncthreads();
   }
-  if (threadIdx.x == 0) *p.total_items_w = carry;
-}
-
-// Pass 2 (one CTA per head): copy the head's block ids into its items.
-__global__ void __launch_bounds__(256) items_fill_kernel(AttendParams p) {
-  const int h = blockIdx.x, b = blockIdx.y, r = b * p.Hq + h;
-  int k = p.sel_lens[r];
-  k = k < 0 ? 0 : (k > p.table_width ? p.table_width : k);
-  const int C = p.item_blocks;
-  const int base = p.head_item_base[r];
-  const int* trow = p.block_table + (int64_t)r * p.table_width;
-  for (int i = threadIdx.x; i < k; i += blockDim.x)
-    p.work_blk_w[(int64_t)(base + i / C) * C + i % C] = trow[i];
-  for (int j = threadIdx.x; j < ceil_div(k, C); j += blockDim.x)
-    p.work_hdr_w[base + j] = make_int4(b, h, base, k);
-}
-
-template <typename T, int D, int BS>
-static cudaError_t launch_attend_t(const AttendParams& p, int grid, cudaStream_t stream) {
-  const size_t smem = (size_t)p.item_blocks * BS * D * sizeof(T) * 2;
-  attend_kernel<T, D, BS><<<grid, kAttendThreads, smem, stream>>>(p);
-  return cudaGetLastError();
+  __syncthreads();
+  for (int w = threadIdx.x; w < nw; w += blockDim.x) p.bitmap[(int64_t)row * p.bm_words + w] = sbits[w];
+  pdl_launch_dependents();
 }
 
 template <typename F>
@@ -274,52 +309,63 @@ static cudaError_t for_each_attend(int dtype, int D, int bs, F&& f) {
   return cudaErrorInvalidValue;
 }
 
+size_t attend_smem_bytes(int dtype, int D, int bs, int nbt, int g, int nw_max, int slice_cap) {
+  return attend_smem_layout(dtype == ADAKV_DTYPE_F32 ? 4 : 2, D, bs, nbt, g, nw_max, slice_cap).total;
+}
+
 cudaError_t attend_kernels_init() {
   for (int dt = 0; dt < 3; ++dt)
     for (int D : {64, 128})
       for (int bs : {16, 32}) {
         cudaError_t e = for_each_attend(dt, D, bs, [](auto kern, int) {
-          return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      (int)kAttendSmemMax);
+          cudaError_t r = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               (int)kAttendSmemMax);
+          if (r != cudaSuccess) return r;
+          return cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
         });
         if (e != cudaSuccess) return e;
       }
-  return cudaSuccess;
+  return cudaFuncSetAttribute(table_bitmap_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              64 * 1024);
 }
 
-int attend_ctas_per_sm(int dtype, int D, int bs, int item_blocks) {
-  int n = 0;
-  for_each_attend(dtype, D, bs, [&](auto kern, int elt) {
-    const size_t smem = (size_t)item_blocks * bs * D * elt * 2;
-    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kAttendThreads, smem);
+int attend_max_cluster(int dtype, int D, int bs, int g, size_t smem) {
+  int best = 1;
+  for_each_attend(dtype, D, bs, [&](auto kern, int) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(16, 1, 1);
+    cfg.blockDim = dim3(32 * g, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 16;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    cudaError_t e = cudaOccupancyMaxPotentialClusterSize(&n, kern, &cfg);
+    if (e == cudaSuccess && n > 0) best = n;
+    return e;
   });
-  return n > 0 ? n : 1;
+  int c = 1;
+  while (c * 2 <= best && c * 2 <= 16) c *= 2;
+  return c;
 }
 
-cudaError_t launch_attend(const AttendParams& p, int dtype, int D, int bs, int grid,
-                          cudaStream_t stream) {
-#define ADAKV_ATT_CASE(TT, DD, BB) \
-  if (D == DD && bs == BB) return launch_attend_t<TT, DD, BB>(p, grid, stream);
-#define ADAKV_ATT_T(TT) \
-  ADAKV_ATT_CASE(TT, 64, 16) ADAKV_ATT_CASE(TT, 64, 32) ADAKV_ATT_CASE(TT, 128, 16) ADAKV_ATT_CASE(TT, 128, 32)
-  if (dtype == ADAKV_DTYPE_F32) {
-    ADAKV_ATT_T(float)
-  } else if (dtype == ADAKV_DTYPE_F16) {
-    ADAKV_ATT_T(__half)
-  } else if (dtype == ADAKV_DTYPE_BF16) {
-    ADAKV_ATT_T(__nv_bfloat16)
-  }
-#undef ADAKV_ATT_T
-#undef ADAKV_ATT_CASE
-  return cudaErrorInvalidValue;
+cudaError_t launch_attend(const AttendParams& p, int dtype, int D, int bs, int cluster,
+                          cudaStream_t st, const LaunchOpts& o) {
+  const size_t smem = attend_smem_bytes(dtype, D, bs, p.nbt, p.g, p.nw_max, p.slice_cap);
+  LaunchOpts oc = o;
+  oc.cluster_x = (unsigned)cluster;
+  return for_each_attend(dtype, D, bs, [&](auto kern, int) {
+    return launch_ex(kern, dim3(cluster, p.Hkv, p.B), dim3(32 * p.g), smem, st, oc, p);
+  });
 }
 
-cudaError_t launch_items(const AttendParams& p, cudaStream_t stream) {
-  items_scan_kernel<<<1, 1024, 0, stream>>>(p);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return e;
-  items_fill_kernel<<<dim3(p.Hq, p.B), 256, 0, stream>>>(p);
-  return cudaGetLastError();
+cudaError_t launch_table_bitmap(const TableParams& p, cudaStream_t st, const LaunchOpts& o) {
+  const int nw_max = ceil_div(ceil_div(p.max_seq_len, p.bs), 32);
+  return launch_ex(table_bitmap_kernel, dim3(p.Hq, p.B), dim3(256), (size_t)nw_max * 4, st, o, p);
 }
 
 }  // namespace adakv

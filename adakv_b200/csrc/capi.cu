@@ -5,11 +5,15 @@
 // adakv/attention.py:192,200,226, adakv/runtime.py:97), derive the workspace
 // layout, size grids from host-known bounds (no device->host synchronisation
 // anywhere on the decode path), and enqueue the kernels on the caller's stream.
+#include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <map>
 #include <mutex>
+#include <tuple>
 #include <string>
 
 #include "kernels.h"
@@ -44,10 +48,21 @@ int fail(int code, const char* fmt, ...) {
 struct DeviceState {
   bool ready = false;
   int num_sms = 0;
+  bool coop_pdl_ok = true;  // cooperative + programmatic launch accepted together
+  std::map<int, int> plan_ctas;                    // nb_max -> plan CTAs per SM
+  std::map<std::tuple<int, int, int, int, size_t>, int> clusters;  // attend shape -> cluster
 };
 constexpr int kMaxDevices = 64;
 DeviceState g_dev[kMaxDevices];
 std::mutex g_dev_mu;
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("ADAKV_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
 
 int device_state(DeviceState** out) {
   int dev = 0;
@@ -57,7 +72,8 @@ int device_state(DeviceState** out) {
   DeviceState& s = g_dev[dev];
   if (!s.ready) {
     CUDA_TRY(cudaDeviceGetAttribute(&s.num_sms, cudaDevAttrMultiProcessorCount, dev));
-    CUDA_TRY(select_kernels_init());
+    CUDA_TRY(estimate_kernels_init());
+    CUDA_TRY(plan_kernels_init());
     CUDA_TRY(attend_kernels_init());
     s.ready = true;
   }
@@ -91,6 +107,10 @@ int check_geometry(const adakv_geometry* g) {
   const int nb = ceil_div(g->max_seq_len, g->block_size);
   if (g->nb_cap < nb)
     return fail(ADAKV_ERR_INVALID, "nb_cap %d < ceil(max_seq_len / block_size) = %d", g->nb_cap, nb);
+  if (nb > kPlanMaxBlocks)
+    return fail(ADAKV_ERR_UNSUPPORTED, "max_seq_len / block_size = %d blocks > %d", nb, kPlanMaxBlocks);
+  if (g->batch > kEstMaxBatch)
+    return fail(ADAKV_ERR_UNSUPPORTED, "batch %d > %d", g->batch, kEstMaxBatch);
   if ((int64_t)g->batch * g->n_q_heads > (1 << 24))
     return fail(ADAKV_ERR_UNSUPPORTED, "batch * n_q_heads too large");
   return ADAKV_OK;
@@ -145,52 +165,33 @@ View to_view(const adakv_view* v) {
   return r;
 }
 
-// Blocks per attend work item: 4 keeps ~500 items per 128K-token batch-1 step
-// (several per SM); bounded by the shared-memory budget of one CTA.
-int item_blocks_for(const adakv_geometry* g) {
-  const size_t per_block = (size_t)g->block_size * g->head_dim * elt_size(g->dtype) * 2;
-  int c = 4;
-  while (c > 1 && (size_t)c * per_block > kAttendSmemMax) --c;
-  return c;
-}
+// Workspace layout (byte offsets into the caller's buffer; every region is
+// 256-byte aligned).  Counters never need resetting: the plan barrier compares
+// per-head slot tags with a per-call epoch that the estimator increments.
+struct WsLayout {
+  size_t status, epoch, slots, scores, bitmap, bytes;
+  int score_stride, bm_words;
+};
 
-WsLayout plan_layout(const adakv_geometry* g, int table_width) {
-  return make_layout(g->batch, g->n_q_heads, g->head_dim, g->nb_cap, table_width,
-                     item_blocks_for(g), true);
-}
-
-WsLayout attend_layout(const adakv_geometry* g, int table_width) {
-  return make_layout(g->batch, g->n_q_heads, g->head_dim, g->nb_cap, table_width,
-                     item_blocks_for(g), false);
+WsLayout make_ws(const adakv_geometry* g, bool with_plan) {
+  WsLayout L{};
+  const int rows = g->batch * g->n_q_heads;
+  L.score_stride = (int)align_up((size_t)g->nb_cap, 4);
+  L.bm_words = ceil_div(g->nb_cap, 32);
+  size_t o = 0;
+  auto take = [&](size_t bytes) { size_t at = o; o = align_up(o + bytes, 256); return at; };
+  L.status = take(16);
+  L.epoch = take(16);
+  L.slots = with_plan ? take(sizeof(PlanSlot) * rows) : 0;
+  L.scores = with_plan ? take(sizeof(float) * (size_t)rows * L.score_stride) : 0;
+  L.bitmap = take(sizeof(uint32_t) * (size_t)rows * L.bm_words);
+  L.bytes = o;
+  return L;
 }
 
 template <typename T>
 T* ws_at(void* ws, size_t off) {
   return reinterpret_cast<T*>(static_cast<char*>(ws) + off);
-}
-
-// Grid of the persistent attend kernel: enough CTAs for every work item the
-// selection can produce (a tight bound for the plan path, where the per-head
-// counts of a sequence sum to at most Hq * target + Hq / 2 + 1), capped at the
-// number of co-resident CTAs.
-int attend_grid(const DeviceState* ds, const adakv_geometry* g, const WsLayout& L,
-                const adakv_select_params* sp) {
-  int64_t items = L.items_cap;
-  if (sp && sp->policy == ADAKV_POLICY_ADAPTIVE) {
-    const SeqBudget sb = seq_budget(g->nb_cap, to_cfg(sp));
-    if (sb.hi >= sb.lo) {
-      const double per_seq = g->n_q_heads * sb.target + g->n_q_heads / 2.0 + 1.0;
-      const int64_t tight =
-          (int64_t)g->batch * ((int64_t)std::ceil(per_seq / L.item_blocks) + g->n_q_heads);
-      if (tight < items) items = tight;
-    }
-  }
-  const int64_t resident =
-      (int64_t)ds->num_sms *
-      attend_ctas_per_sm(g->dtype, g->head_dim, g->block_size, L.item_blocks);
-  int64_t grid = items < resident ? items : resident;
-  if (grid < 1) grid = 1;
-  return (int)grid;
 }
 
 int check_workspace(void* ws, size_t bytes, size_t need) {
@@ -202,14 +203,16 @@ int check_workspace(void* ws, size_t bytes, size_t need) {
   return ADAKV_OK;
 }
 
-// plan = estimator + budget + select (shared by adakv_plan and adakv_decode_step)
-int enqueue_plan(const adakv_geometry* g, const adakv_select_params* sp, const adakv_view* q,
-                 const float* centroid, const int32_t* seq_lens, int32_t* block_table,
-                 int32_t table_width, int32_t* sel_lens, void* ws, const WsLayout& L,
-                 cudaStream_t st) {
+// estimator (+ fused append) and the plan kernel; shared by adakv_plan and
+// adakv_decode_step
+int enqueue_plan(const DeviceState* ds, const adakv_geometry* g, const adakv_select_params* sp,
+                 const adakv_view* q, float* centroid, const int32_t* seq_lens,
+                 const adakv_view* k, const adakv_view* v, const adakv_view* k_new,
+                 const adakv_view* v_new, int n_new, int32_t* block_table, int32_t table_width,
+                 int32_t* sel_lens, void* ws, const WsLayout& L, cudaStream_t st) {
   const int nb_max = ceil_div(g->max_seq_len, g->block_size);
   uint32_t* status = ws_at<uint32_t>(ws, L.status);
-  const SelectCfg cfg = to_cfg(sp);
+  const bool pdl = pdl_enabled();
 
   EstParams ep{};
   ep.q = to_view(q);
@@ -224,60 +227,77 @@ int enqueue_plan(const adakv_geometry* g, const adakv_select_params* sp, const a
   ep.bs = g->block_size;
   ep.scores = ws_at<float>(ws, L.scores);
   ep.score_stride = L.score_stride;
-  ep.chunkmax = ws_at<float>(ws, L.chunkmax);
-  ep.chunks_cap = L.chunks_cap;
+  ep.epoch = ws_at<uint32_t>(ws, L.epoch);
+  ep.slots = ws_at<PlanSlot>(ws, L.slots);
+  if (n_new > 0) {
+    ep.k = to_view(k);
+    ep.v = to_view(v);
+    ep.k_new = to_view(k_new);
+    ep.v_new = to_view(v_new);
+    ep.n_new = n_new;
+  }
   ep.status = status;
-  CUDA_TRY(launch_estimate(ep, g->dtype, g->head_dim, nb_max, st));
+  const int64_t chunks = (int64_t)g->batch * g->n_kv_heads * ceil_div(nb_max, kEstRows);
+  const int est_grid = (int)std::max<int64_t>(1, std::min<int64_t>(ds->num_sms, chunks));
+  LaunchOpts oe;
+  oe.pdl = pdl;
+  CUDA_TRY(launch_estimate(ep, g->dtype, g->head_dim, nb_max, est_grid, st, oe));
 
-  BudgetParams bp{};
-  bp.seq_lens = seq_lens;
-  bp.max_seq_len = g->max_seq_len;
-  bp.B = g->batch;
-  bp.Hq = g->n_q_heads;
-  bp.bs = g->block_size;
-  bp.cfg = cfg;
-  bp.scores = ep.scores;
-  bp.score_stride = L.score_stride;
-  bp.chunkmax = ep.chunkmax;
-  bp.chunks_cap = L.chunks_cap;
-  bp.weights = ws_at<double>(ws, L.weights);
-  bp.seq_counter = ws_at<int>(ws, L.seq_counter);
-  bp.glob_counter = ws_at<int>(ws, L.glob_counter);
-  bp.sel_lens = sel_lens;
-  bp.head_item_off = ws_at<int>(ws, L.head_item_off);
-  bp.seq_items = ws_at<int>(ws, L.seq_items);
-  bp.head_item_base = ws_at<int>(ws, L.head_item_base);
-  bp.total_items = ws_at<int>(ws, L.total_items);
-  bp.item_blocks = L.item_blocks;
-  bp.status = status;
-  CUDA_TRY(launch_budget(bp, st));
-
-  SelectParams sp2{};
-  sp2.seq_lens = seq_lens;
-  sp2.max_seq_len = g->max_seq_len;
-  sp2.B = g->batch;
-  sp2.Hq = g->n_q_heads;
-  sp2.bs = g->block_size;
-  sp2.n_sink = sp->n_sink_blocks;
-  sp2.n_local = sp->n_local_blocks;
-  sp2.scores = ep.scores;
-  sp2.score_stride = L.score_stride;
-  sp2.sel_lens = sel_lens;
-  sp2.block_table = block_table;
-  sp2.table_width = table_width;
-  sp2.head_item_base = bp.head_item_base;
-  sp2.work_hdr = ws_at<int4>(ws, L.work_hdr);
-  sp2.work_blk = ws_at<int>(ws, L.work_blk);
-  sp2.item_blocks = L.item_blocks;
-  sp2.status = status;
-  CUDA_TRY(launch_select(sp2, nb_max, st));
+  PlanParams pp{};
+  pp.seq_lens = seq_lens;
+  pp.max_seq_len = g->max_seq_len;
+  pp.B = g->batch;
+  pp.Hq = g->n_q_heads;
+  pp.bs = g->block_size;
+  pp.cfg = to_cfg(sp);
+  pp.scores = ep.scores;
+  pp.score_stride = L.score_stride;
+  pp.epoch = ep.epoch;
+  pp.slots = ws_at<PlanSlot>(ws, L.slots);
+  pp.sel_lens = sel_lens;
+  pp.block_table = block_table;
+  pp.table_width = table_width;
+  pp.bitmap = ws_at<uint32_t>(ws, L.bitmap);
+  pp.bm_words = L.bm_words;
+  pp.nw_max = ceil_div(nb_max, 32);
+  pp.status = status;
+  int per_sm;
+  {
+    std::lock_guard<std::mutex> lock(g_dev_mu);
+    auto it = ds->plan_ctas.find(nb_max);
+    if (it == ds->plan_ctas.end())
+      it = const_cast<DeviceState*>(ds)->plan_ctas.emplace(nb_max, plan_ctas_per_sm(nb_max)).first;
+    per_sm = it->second;
+  }
+  const int capacity = ds->num_sms * per_sm;
+  if (capacity < g->n_q_heads)
+    return fail(ADAKV_ERR_UNSUPPORTED, "n_q_heads %d exceeds the co-resident plan CTAs (%d)",
+                g->n_q_heads, capacity);
+  pp.seqs_per_round = std::min(g->batch, capacity / g->n_q_heads);
+  const int plan_grid = pp.seqs_per_round * g->n_q_heads;
+  LaunchOpts op;
+  op.coop = true;
+  op.pdl = pdl && ds->coop_pdl_ok;
+  cudaError_t e = launch_plan(pp, nb_max, plan_grid, st, op);
+  if (e != cudaSuccess && op.pdl) {
+    // some drivers refuse cooperative + programmatic together: drop the overlap
+    (void)cudaGetLastError();
+    const_cast<DeviceState*>(ds)->coop_pdl_ok = false;
+    op.pdl = false;
+    e = launch_plan(pp, nb_max, plan_grid, st, op);
+  }
+  CUDA_TRY(e);
   return ADAKV_OK;
 }
 
-AttendParams attend_params(const adakv_geometry* g, const adakv_view* q, const adakv_view* k,
-                           const adakv_view* v, const adakv_view* out, const int32_t* seq_lens,
-                           float sm_scale, const int32_t* block_table, int32_t table_width,
-                           const int32_t* sel_lens, void* ws, const WsLayout& L) {
+// attend over the bitmaps in the workspace
+int enqueue_attend(const DeviceState* ds, const adakv_geometry* g, const adakv_view* q,
+                   const adakv_view* k, const adakv_view* v, const adakv_view* out,
+                   const int32_t* seq_lens, float sm_scale, void* ws, const WsLayout& L,
+                   cudaStream_t st) {
+  (void)ds;
+  const int nb_max = ceil_div(g->max_seq_len, g->block_size);
+  const int gq = g->n_q_heads / g->n_kv_heads;
   AttendParams ap{};
   ap.q = to_view(q);
   ap.k = to_view(k);
@@ -287,24 +307,47 @@ AttendParams attend_params(const adakv_geometry* g, const adakv_view* q, const a
   ap.max_seq_len = g->max_seq_len;
   ap.B = g->batch;
   ap.Hq = g->n_q_heads;
-  ap.g = g->n_q_heads / g->n_kv_heads;
+  ap.Hkv = g->n_kv_heads;
+  ap.g = gq;
   ap.sm_scale = sm_scale;
-  ap.block_table = block_table;
-  ap.table_width = table_width;
-  ap.sel_lens = sel_lens;
-  ap.work_hdr = ws_at<int4>(ws, L.work_hdr);
-  ap.work_blk = ws_at<int>(ws, L.work_blk);
-  ap.total_items = ws_at<int>(ws, L.total_items);
-  ap.item_blocks = L.item_blocks;
-  ap.head_item_base = ws_at<int>(ws, L.head_item_base);
-  ap.work_hdr_w = ws_at<int4>(ws, L.work_hdr);
-  ap.work_blk_w = ws_at<int>(ws, L.work_blk);
-  ap.total_items_w = ws_at<int>(ws, L.total_items);
-  ap.head_counter = ws_at<int>(ws, L.head_counter);
-  ap.part_ml = ws_at<float2>(ws, L.part_ml);
-  ap.part_o = ws_at<float>(ws, L.part_o);
+  ap.bitmap = ws_at<uint32_t>(ws, L.bitmap);
+  ap.bm_words = L.bm_words;
+  ap.nw_max = ceil_div(nb_max, 32);
   ap.status = ws_at<uint32_t>(ws, L.status);
-  return ap;
+  // blocks per gather batch: two buffers of K+V tiles within ~96 KB
+  const size_t per_block = (size_t)g->block_size * g->head_dim * elt_size(g->dtype) * 2;
+  ap.nbt = (int)std::max<size_t>(1, std::min<size_t>(8, (96 * 1024) / (2 * per_block)));
+  int cluster = 16;
+  size_t smem = 0;
+  for (;;) {
+    ap.slice_cap = ceil_div(nb_max, cluster) + 1;
+    smem = attend_smem_bytes(g->dtype, g->head_dim, g->block_size, ap.nbt, gq, ap.nw_max,
+                             ap.slice_cap);
+    while (smem > kAttendSmemMax && ap.nbt > 1) {
+      --ap.nbt;
+      smem = attend_smem_bytes(g->dtype, g->head_dim, g->block_size, ap.nbt, gq, ap.nw_max,
+                               ap.slice_cap);
+    }
+    if (smem > kAttendSmemMax)
+      return fail(ADAKV_ERR_UNSUPPORTED, "sequence too long for the attend kernel's shared memory");
+    int best;
+    {
+      std::lock_guard<std::mutex> lock(g_dev_mu);
+      const auto key = std::make_tuple(g->dtype, g->head_dim, g->block_size, gq, smem);
+      auto it = ds->clusters.find(key);
+      if (it == ds->clusters.end())
+        it = const_cast<DeviceState*>(ds)
+                 ->clusters.emplace(key, attend_max_cluster(g->dtype, g->head_dim, g->block_size, gq, smem))
+                 .first;
+      best = it->second;
+    }
+    if (best >= cluster || cluster == 1) break;
+    cluster = best;
+  }
+  LaunchOpts oa;
+  oa.pdl = pdl_enabled();
+  CUDA_TRY(launch_attend(ap, g->dtype, g->head_dim, g->block_size, cluster, st, oa));
+  return ADAKV_OK;
 }
 
 int check_attend_views(const adakv_geometry* g, const adakv_view* q, const adakv_view* k,
@@ -332,7 +375,7 @@ int32_t adakv_plan_table_width(const adakv_geometry* geo, const adakv_select_par
 
 size_t adakv_plan_workspace_bytes(const adakv_geometry* geo, const adakv_select_params* sp) {
   if (check_geometry(geo) || check_params(sp)) return 0;
-  return plan_layout(geo, table_width_for(geo->nb_cap, to_cfg(sp))).bytes;
+  return make_ws(geo, true).bytes;
 }
 
 size_t adakv_attend_workspace_bytes(const adakv_geometry* geo, int32_t table_width) {
@@ -341,7 +384,7 @@ size_t adakv_attend_workspace_bytes(const adakv_geometry* geo, int32_t table_wid
     fail(ADAKV_ERR_INVALID, "table_width must be >= 1");
     return 0;
   }
-  return attend_layout(geo, table_width).bytes;
+  return make_ws(geo, false).bytes;
 }
 
 int adakv_centroid_build(const adakv_geometry* geo, const adakv_view* k, const int32_t* seq_lens,
@@ -438,13 +481,13 @@ int adakv_plan(const adakv_geometry* geo, const adakv_select_params* sp, const a
   const int need_w = table_width_for(geo->nb_cap, to_cfg(sp));
   if (table_width < need_w)
     return fail(ADAKV_ERR_INVALID, "table_width %d < required %d", table_width, need_w);
-  const WsLayout L = plan_layout(geo, table_width);
+  const WsLayout L = make_ws(geo, true);
   if ((rc = check_workspace(workspace, workspace_bytes, L.bytes))) return rc;
   DeviceState* ds = nullptr;
   if ((rc = device_state(&ds))) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if ((rc = enqueue_plan(geo, sp, q, centroid, seq_lens, block_table, table_width, sel_lens,
-                         workspace, L, st)))
+  if ((rc = enqueue_plan(ds, geo, sp, q, const_cast<float*>(centroid), seq_lens, nullptr, nullptr,
+                         nullptr, nullptr, 0, block_table, table_width, sel_lens, workspace, L, st)))
     return rc;
   if (scores_out) {
     CUDA_TRY(cudaMemcpy2DAsync(scores_out, sizeof(float) * geo->nb_cap,
@@ -465,22 +508,33 @@ int adakv_attend(const adakv_geometry* geo, const adakv_view* q, const adakv_vie
   if (!block_table || !sel_lens) return fail(ADAKV_ERR_INVALID, "block_table / sel_lens are NULL");
   if (table_width < 1) return fail(ADAKV_ERR_INVALID, "table_width must be >= 1");
   if (!std::isfinite(sm_scale)) return fail(ADAKV_ERR_INVALID, "sm_scale must be finite");
-  const WsLayout L = attend_layout(geo, table_width);
+  const WsLayout L = make_ws(geo, false);
   if ((rc = check_workspace(workspace, workspace_bytes, L.bytes))) return rc;
   DeviceState* ds = nullptr;
   if ((rc = device_state(&ds))) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  AttendParams ap = attend_params(geo, q, k, v, out, seq_lens, sm_scale, block_table, table_width,
-                                  sel_lens, workspace, L);
-  CUDA_TRY(launch_items(ap, st));
-  CUDA_TRY(launch_attend(ap, geo->dtype, geo->head_dim, geo->block_size,
-                         attend_grid(ds, geo, L, nullptr), st));
-  return ADAKV_OK;
+  TableParams tp{};
+  tp.block_table = block_table;
+  tp.table_width = table_width;
+  tp.sel_lens = sel_lens;
+  tp.seq_lens = seq_lens;
+  tp.max_seq_len = geo->max_seq_len;
+  tp.B = geo->batch;
+  tp.Hq = geo->n_q_heads;
+  tp.bs = geo->block_size;
+  tp.bitmap = ws_at<uint32_t>(workspace, L.bitmap);
+  tp.bm_words = L.bm_words;
+  tp.status = ws_at<uint32_t>(workspace, L.status);
+  LaunchOpts ot;
+  ot.pdl = pdl_enabled();
+  CUDA_TRY(launch_table_bitmap(tp, st, ot));
+  return enqueue_attend(ds, geo, q, k, v, out, seq_lens, sm_scale, workspace, L, st);
 }
 
 int adakv_decode_step(const adakv_geometry* geo, const adakv_select_params* sp,
                       const adakv_view* q, const adakv_view* k, const adakv_view* v,
-                      const float* centroid, const int32_t* seq_lens, float sm_scale,
+                      const adakv_view* k_new, const adakv_view* v_new, int32_t n_new,
+                      float* centroid, const int32_t* seq_lens, float sm_scale,
                       int32_t* block_table, int32_t table_width, int32_t* sel_lens,
                       const adakv_view* out, void* workspace, size_t workspace_bytes,
                       void* stream) {
@@ -488,6 +542,12 @@ int adakv_decode_step(const adakv_geometry* geo, const adakv_select_params* sp,
   if ((rc = check_geometry(geo))) return rc;
   if ((rc = check_params(sp))) return rc;
   if ((rc = check_attend_views(geo, q, k, v, out))) return rc;
+  if (n_new < 0 || n_new > geo->max_seq_len)
+    return fail(ADAKV_ERR_INVALID, "n_new must be in [0, max_seq_len] (got %d)", n_new);
+  if (n_new > 0) {
+    if ((rc = check_view(k_new, "k_new", geo->dtype, true))) return rc;
+    if ((rc = check_view(v_new, "v_new", geo->dtype, true))) return rc;
+  }
   if (!centroid || reinterpret_cast<uintptr_t>(centroid) % 16)
     return fail(ADAKV_ERR_INVALID, "centroid must be a 16-byte aligned device pointer");
   if (!block_table || !sel_lens) return fail(ADAKV_ERR_INVALID, "block_table / sel_lens are NULL");
@@ -495,19 +555,15 @@ int adakv_decode_step(const adakv_geometry* geo, const adakv_select_params* sp,
   const int need_w = table_width_for(geo->nb_cap, to_cfg(sp));
   if (table_width < need_w)
     return fail(ADAKV_ERR_INVALID, "table_width %d < required %d", table_width, need_w);
-  const WsLayout L = plan_layout(geo, table_width);
+  const WsLayout L = make_ws(geo, true);
   if ((rc = check_workspace(workspace, workspace_bytes, L.bytes))) return rc;
   DeviceState* ds = nullptr;
   if ((rc = device_state(&ds))) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if ((rc = enqueue_plan(geo, sp, q, centroid, seq_lens, block_table, table_width, sel_lens,
-                         workspace, L, st)))
+  if ((rc = enqueue_plan(ds, geo, sp, q, centroid, seq_lens, k, v, k_new, v_new, n_new,
+                         block_table, table_width, sel_lens, workspace, L, st)))
     return rc;
-  AttendParams ap = attend_params(geo, q, k, v, out, seq_lens, sm_scale, block_table, table_width,
-                                  sel_lens, workspace, L);
-  CUDA_TRY(launch_attend(ap, geo->dtype, geo->head_dim, geo->block_size,
-                         attend_grid(ds, geo, L, sp), st));
-  return ADAKV_OK;
+  return enqueue_attend(ds, geo, q, k, v, out, seq_lens, sm_scale, workspace, L, st);
 }
 
 int adakv_read_status(void* workspace, uint32_t* status, void* stream) {

@@ -81,25 +81,39 @@ __global__ void __launch_bounds__(256) centroid_kernel(CentroidParams p) {
   const T* vn = from_input ? static_cast<const T*>(p.v_new.data) + b * p.v_new.sb + h * p.v_new.sh + d
                            : nullptr;
 
+  // issue the token loads of up to 16 tokens together (independent loads in
+  // flight at once), then add them in token order
+  constexpr int kGroup = 16;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 8
-  for (int t = t0; t < t1; ++t) {
-    float4 x;
-    if (from_input && t >= S_old) {  // a new token: read it from the input, store it in the cache
-      const T* src = kn + (int64_t)(t - S_old) * p.k_new.ss;
-      x = load4<T>(src);
-      copy4<T>(kw + (int64_t)t * p.k.ss, src);
-      copy4<T>(vw + (int64_t)t * p.v.ss, vn + (int64_t)(t - S_old) * p.v_new.ss);
-    } else {
-      x = load4<T>(kc + (int64_t)t * p.k.ss);
+  for (int base = t0; base < t1; base += kGroup) {
+    float4 x[kGroup];
+#pragma unroll
+    for (int u = 0; u < kGroup; ++u) {
+      const int t = base + u;
+      if (t < t1) {
+        if (from_input && t >= S_old) {  // a new token: read it from the input, store it in the cache
+          const T* src = kn + (int64_t)(t - S_old) * p.k_new.ss;
+          x[u] = load4<T>(src);
+          copy4<T>(kw + (int64_t)t * p.k.ss, src);
+          copy4<T>(vw + (int64_t)t * p.v.ss, vn + (int64_t)(t - S_old) * p.v_new.ss);
+        } else {
+          x[u] = load4<T>(kc + (int64_t)t * p.k.ss);
+        }
+      }
     }
-    if (t == t0) {
-      acc = x;
-    } else {
-      acc.x = __fadd_rn(acc.x, x.x);
-      acc.y = __fadd_rn(acc.y, x.y);
-      acc.z = __fadd_rn(acc.z, x.z);
-      acc.w = __fadd_rn(acc.w, x.w);
+#pragma unroll
+    for (int u = 0; u < kGroup; ++u) {
+      const int t = base + u;
+      if (t < t1) {
+        if (t == t0) {
+          acc = x[u];
+        } else {
+          acc.x = __fadd_rn(acc.x, x[u].x);
+          acc.y = __fadd_rn(acc.y, x[u].y);
+          acc.z = __fadd_rn(acc.z, x[u].z);
+          acc.w = __fadd_rn(acc.w, x[u].w);
+        }
+      }
     }
   }
   const float n = (float)(t1 - t0);

@@ -17,12 +17,7 @@ namespace adakv {
 // ---------------------------------------------------------------------------
 // constants
 // ---------------------------------------------------------------------------
-constexpr int kEstRows = 64;          // centroid rows (blocks) per estimator CTA
-constexpr int kEstThreads = 256;      // 8 warps x 8 rows
-constexpr int kBudgetThreads = 256;
-constexpr int kSelectThreads = 1024;
-constexpr int kAttendThreads = 128;   // 4 warps, one selected block per warp at a time
-constexpr int kMaxItemBlocks = 16;    // max selected blocks handled by one attend work item
+constexpr int kEstRows = 64;          // centroid rows (blocks) per estimator chunk
 constexpr uint64_t kWaitLimitNs = 200ull * 1000ull * 1000ull;  // bounded spin: 200 ms
 
 // ---------------------------------------------------------------------------
@@ -37,15 +32,6 @@ struct SelectCfg {
   double avg_budget;
   double temperature;
   int k_min, k_max, n_sink, n_local, c_min, policy;
-};
-
-// Workspace layout: byte offsets into one caller-provided device buffer.
-struct WsLayout {
-  size_t status, seq_counter, glob_counter, head_counter, total_items;
-  size_t weights, head_item_base, head_item_off, seq_items, chunkmax, scores;
-  size_t work_hdr, work_blk, part_ml, part_o;
-  size_t bytes;
-  int items_cap, item_blocks, score_stride, chunks_cap;
 };
 
 __host__ __device__ inline int ceil_div(int a, int b) { return (a + b - 1) / b; }
@@ -111,34 +97,6 @@ inline int table_width_for(int nb_cap, const SelectCfg& c) {
 }
 
 inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
-
-inline WsLayout make_layout(int B, int Hq, int D, int nb_cap, int table_width, int item_blocks,
-                            bool with_scores) {
-  WsLayout L{};
-  L.item_blocks = item_blocks;
-  L.items_cap = B * Hq * ceil_div(imax(table_width, 1), item_blocks);
-  L.score_stride = (int)align_up((size_t)imax(nb_cap, 1), 4);
-  L.chunks_cap = ceil_div(imax(nb_cap, 1), kEstRows);
-  size_t o = 0;
-  auto take = [&](size_t bytes) { size_t at = o; o = align_up(o + bytes, 256); return at; };
-  L.status = take(16);
-  L.seq_counter = take(sizeof(int) * B);
-  L.glob_counter = take(16);
-  L.head_counter = take(sizeof(int) * B * Hq);
-  L.total_items = take(16);
-  L.weights = take(sizeof(double) * B * Hq);
-  L.head_item_base = take(sizeof(int) * B * Hq);
-  L.head_item_off = take(sizeof(int) * B * Hq);
-  L.seq_items = take(sizeof(int) * (B + 1));
-  L.chunkmax = with_scores ? take(sizeof(float) * (size_t)B * Hq * L.chunks_cap) : 0;
-  L.scores = with_scores ? take(sizeof(float) * (size_t)B * Hq * L.score_stride) : 0;
-  L.work_hdr = take(sizeof(int4) * (size_t)L.items_cap);
-  L.work_blk = take(sizeof(int) * (size_t)L.items_cap * item_blocks);
-  L.part_ml = take(sizeof(float2) * (size_t)L.items_cap);
-  L.part_o = take(sizeof(float) * (size_t)L.items_cap * D);
-  L.bytes = o;
-  return L;
-}
 
 // ---------------------------------------------------------------------------
 // device helpers

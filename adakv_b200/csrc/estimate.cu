@@ -1,20 +1,30 @@
-// (b) Centroid block estimator: scores[b, h, j] = q[b, h] . centroid[b, h / g, j]
-// (unscaled, float32), the reference's einsum("hd,hbd->hb") over GQA-expanded
-// centroids (adakv/estimator.py:73-74, adakv/attention.py:187-189) with the
-// expansion folded away: each centroid row is read from HBM once and scored
-// against all g query heads of its KV head.
+// (b) Centroid block estimator, with (a) the step's KV append fused in.
 //
-// One CTA streams kEstRows contiguous centroid rows of one (b, kv head) into
-// shared memory with a single bulk copy (the TMA engine, completion on an
-// mbarrier), then 8 warps score 8 rows each.  Lane l owns dims
-// [l*D/32, (l+1)*D/32) of every row and keeps the g queries' matching slices in
-// registers; 32 (row, head) partial dot products are finished with one
-// 31-shuffle butterfly reduce-scatter, after which lane l holds the full score of
-// slot l.  The CTA also emits the per-(b, h) maximum over its rows, which the
-// budget kernel combines into the softmax maximum.
+// scores[b, h, j] = q[b, h] . centroid[b, h / g, j] (unscaled, float32): the
+// reference's einsum("hd,hbd->hb") over GQA-expanded centroids
+// (adakv/estimator.py:73-74, adakv/attention.py:187-189) with the expansion
+// folded away -- every centroid row is read from HBM once and scored against
+// all g query heads of its KV head.
 //
-// HBM traffic per step = the float32 centroid table (B * Hkv * nb * D * 4 bytes)
-// plus q; scores (B * Hq * nb * 4 bytes) stay in L2 for the next kernels.
+// Persistent grid, one CTA per SM.  The work is the list of 64-row chunks of
+// every (sequence, KV head) centroid table; each CTA owns a contiguous range of
+// it.  A producer warp streams chunks through a 4-stage shared-memory ring with
+// 1-D bulk copies (the TMA engine; no multicast), each stage also carrying the g
+// query rows of the chunk's KV head; completion is signalled on per-stage
+// mbarriers (transaction bytes) and stages are released by the 8 consumer warps
+// through a second set of mbarriers.  A consumer lane owns D/32 dims of a row
+// and keeps the matching query slices in registers; 32 (row, head) partial dot
+// products are finished with one 31-shuffle butterfly reduce-scatter.
+//
+// Fused append (adakv/runtime.py:43-60): when the step appends n_new tokens, a
+// tenth warp writes them into the K/V cache in place, recomputes every touched
+// block's centroid from its tokens (token-order float32 sum, one IEEE division:
+// bit-identical to a rebuild), stores it, and scores it against the group's
+// queries.  Consumers skip those rows, so there is no ordering hazard between
+// the refresh and the bulk copies of the same chunk.
+//
+// Bytes from HBM per step: the float32 centroid table (B * Hkv * nb * D * 4) plus
+// q; the block scores (B * Hq * nb * 4) are written once and stay in L2.
 #include "kernels.h"
 
 namespace adakv {
@@ -33,120 +43,317 @@ __device__ __forceinline__ void lds_row(const float* p, float (&c)[E]) {
   }
 }
 
+// E consecutive elements of T -> fp32 (E * sizeof(T) is 4, 8 or 16 bytes)
+template <typename T, int E>
+__device__ __forceinline__ void load_vec(const T* p, float (&out)[E]) {
+  if constexpr (sizeof(T) == 4 && E == 4) {
+    const float4 v = *reinterpret_cast<const float4*>(p);
+    out[0] = v.x; out[1] = v.y; out[2] = v.z; out[3] = v.w;
+  } else if constexpr (sizeof(T) == 2 && E == 4) {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    const T* t = reinterpret_cast<const T*>(&u);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) out[e] = to_f32(t[e]);
+  } else if constexpr (sizeof(T) == 2 && E == 2) {
+    const uint32_t u = *reinterpret_cast<const uint32_t*>(p);
+    const T* t = reinterpret_cast<const T*>(&u);
+    out[0] = to_f32(t[0]);
+    out[1] = to_f32(t[1]);
+  } else {
+#pragma unroll
+    for (int e = 0; e < E; ++e) out[e] = to_f32(p[e]);
+  }
+}
+
+template <typename T, int E>
+__device__ __forceinline__ void copy_vec(T* dst, const T* src) {
+#pragma unroll
+  for (int e = 0; e < E; ++e) dst[e] = src[e];
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
 template <typename T, int D, int GP>
-__global__ void __launch_bounds__(kEstThreads) estimate_kernel(EstParams p) {
-  constexpr int E = D / 32;                  // floats per lane per row
-  constexpr int R = 32 / GP;                 // rows per reduce-scatter group
-  constexpr int RPW = kEstRows / (kEstThreads / 32);  // rows per warp (8)
-  constexpr int NG = RPW / R;                // groups per warp
+__global__ void __launch_bounds__(kEstThreads, 1) estimate_kernel(EstParams p) {
+  constexpr int E = D / 32;                             // floats per lane per row
+  constexpr int R = 32 / GP;                            // rows per reduce-scatter group
+  constexpr int RPW = kEstRows / kEstConsumerWarps;     // rows per consumer warp (8)
+  constexpr int NG = RPW / R;                           // groups per warp
+  constexpr int TILE_F = kEstRows * D;                  // floats of centroid rows per stage
+  constexpr int Q_F = (16 * D * (int)sizeof(T) + 15) / 16 * 4;  // up to 16 q rows per stage
+  constexpr int STAGE_F = TILE_F + Q_F;
   static_assert(RPW % R == 0, "rows per warp must be a multiple of the group rows");
-  extern __shared__ __align__(128) float tile[];     // [kEstRows][D]
-  __shared__ __align__(8) uint64_t bar;
-  __shared__ float wmax[kEstThreads / 32][GP];
+  extern __shared__ __align__(128) float ring[];       // [kEstStages][STAGE_F], then 2x[B+1] ints
+  __shared__ __align__(8) uint64_t full_bar[kEstStages];
+  __shared__ __align__(8) uint64_t empty_bar[kEstStages];
+  __shared__ int scan_scratch[33];
 
-  const int chunk = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  pdl_wait();
-  const int S = seq_len_of(p.seq_lens, b, p.max_seq_len);
-  if (S <= 0 || S > p.max_seq_len) {
-    if (tid == 0 && chunk == 0 && kvh == 0) report(p.status, ADAKV_ST_BAD_SEQ_LEN);
-    return;
-  }
-  const int nb = ceil_div(S, p.bs);
-  const int row0 = chunk * kEstRows;
-  if (row0 >= nb) return;
-  const int nrows = imin(kEstRows, nb - row0);
+  int* seq_base = reinterpret_cast<int*>(ring + kEstStages * STAGE_F);  // [B+1] first chunk of seq
+  int* seq_cph = seq_base + p.B + 1;                                     // [B] chunks per KV head
 
-  if (tid == 0) mbar_init(&bar, 1);
-  __syncthreads();
   if (tid == 0) {
-    const uint32_t bytes = (uint32_t)nrows * D * 4u;
-    mbar_arrive_expect_tx(&bar, bytes);
-    bulk_g2s(tile, p.cent + ((int64_t)(b * p.Hkv + kvh) * p.nb_cap + row0) * D, bytes, &bar);
+#pragma unroll
+    for (int s = 0; s < kEstStages; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], kEstConsumerWarps);
+    }
   }
-
-  // this lane's slice of the g queries of the group, in fp32
-  float qr[GP][E];
-  const T* qbase = static_cast<const T*>(p.q.data) + b * p.q.sb + lane * E;
-#pragma unroll
-  for (int j = 0; j < GP; ++j) {
-#pragma unroll
-    for (int e = 0; e < E; ++e)
-      qr[j][e] = (j < p.g) ? to_f32(qbase[(int64_t)(kvh * p.g + j) * p.q.sh + e]) : 0.f;
+  pdl_wait();
+  if (blockIdx.x == 0 && tid == 0 && p.epoch) atomicAdd(p.epoch, 1u);
+  // clear the plan's weight-exchange tags of this call's rows (the plan kernel
+  // starts after this grid completes, so no stale tag can satisfy its barrier)
+  if (p.slots) {
+    for (int r = blockIdx.x * kEstThreads + tid; r < p.B * p.Hq; r += gridDim.x * kEstThreads)
+      p.slots[r].epoch = 0u;
   }
-
-  if (!mbar_wait_bounded(&bar, 0)) {
-    if (lane == 0) report(p.status, ADAKV_ST_WAIT_TIMEOUT);
-    mbar_wait_bounded(&bar, 0);  // give an in-flight copy one more bounded chance to land
-    return;
+  // per-sequence chunk counts and their exclusive prefix
+  int carry = 0;
+  for (int base = 0; base < p.B; base += kEstThreads) {
+    const int b = base + tid;
+    int cnt = 0;
+    if (b < p.B) {
+      const int S = seq_len_of(p.seq_lens, b, p.max_seq_len);
+      const bool ok = S > 0 && S <= p.max_seq_len;
+      if (!ok && blockIdx.x == 0) report(p.status, ADAKV_ST_BAD_SEQ_LEN);
+      const int cph = ok ? ceil_div(ceil_div(S, p.bs), kEstRows) : 0;
+      seq_cph[b] = cph;
+      cnt = cph * p.Hkv;
+    }
+    const int off = block_exclusive_scan(cnt, scan_scratch);
+    if (b < p.B) seq_base[b] = carry + off;
+    carry += scan_scratch[32];
+    __syncthreads();
   }
+  if (tid == 0) seq_base[p.B] = carry;
+  __syncthreads();
+  pdl_launch_dependents();
 
-  float gmax = -INFINITY;
-#pragma unroll
-  for (int grp = 0; grp < NG; ++grp) {
-    const int rbase = warp * RPW + grp * R;
-    float v[32];
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      float c[E];
-      lds_row<E>(tile + (rbase + r) * D + lane * E, c);
-#pragma unroll
-      for (int j = 0; j < GP; ++j) {
-        float acc = 0.f;
-#pragma unroll
-        for (int e = 0; e < E; ++e) acc = fmaf(qr[j][e], c[e], acc);
-        v[r * GP + j] = acc;
+  const int total = seq_base[p.B];
+  const int c_begin = (int)((int64_t)total * blockIdx.x / gridDim.x);
+  const int c_end = (int)((int64_t)total * (blockIdx.x + 1) / gridDim.x);
+  const bool appending = p.n_new > 0 && p.k_new.data != nullptr;
+
+  auto chunk_of = [&](int c, int& b, int& kvh, int& ch) {
+    int lo = 0, hi = p.B;
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (seq_base[mid] <= c) lo = mid; else hi = mid;
+    }
+    b = lo;
+    const int r = c - seq_base[b];
+    kvh = r / seq_cph[b];
+    ch = r - kvh * seq_cph[b];
+  };
+
+  if (warp == kEstConsumerWarps) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      int i = 0;
+      for (int c = c_begin; c < c_end; ++c, ++i) {
+        int b, kvh, ch;
+        chunk_of(c, b, kvh, ch);
+        const int s = i % kEstStages;
+        if (i >= kEstStages && !mbar_wait_bounded(&empty_bar[s], ((i / kEstStages) - 1) & 1)) {
+          report(p.status, ADAKV_ST_WAIT_TIMEOUT);
+          break;
+        }
+        const int S = seq_len_of(p.seq_lens, b, p.max_seq_len);
+        const int nb = ceil_div(S, p.bs);
+        const int row0 = ch * kEstRows;
+        const int nrows = imin(kEstRows, nb - row0);
+        const uint32_t qrow = D * sizeof(T);
+        float* st = ring + s * STAGE_F;
+        mbar_arrive_expect_tx(&full_bar[s], (uint32_t)nrows * D * 4u + (uint32_t)p.g * qrow);
+        bulk_g2s(st, p.cent + ((int64_t)(b * p.Hkv + kvh) * p.nb_cap + row0) * D,
+                 (uint32_t)nrows * D * 4u, &full_bar[s]);
+        const T* qsrc = static_cast<const T*>(p.q.data) + b * p.q.sb + (int64_t)kvh * p.g * p.q.sh;
+        for (int j = 0; j < p.g; ++j)
+          bulk_g2s(reinterpret_cast<char*>(st + TILE_F) + j * qrow, qsrc + j * p.q.sh, qrow,
+                   &full_bar[s]);
       }
     }
-    const float s = warp_reduce_scatter32(v, lane);
-    const int row = rbase + lane / GP, j = lane % GP;
-    if (j < p.g && row < nrows) {
-      p.scores[(int64_t)(b * p.Hq + kvh * p.g + j) * p.score_stride + row0 + row] = s;
-      gmax = fmaxf(gmax, s);
+  } else if (warp == kEstConsumerWarps + 1) {
+    // ---------------- fused append: refresh the touched blocks ----------------
+    if (appending) {
+      for (int pair = blockIdx.x; pair < p.B * p.Hkv; pair += gridDim.x) {
+        const int b = pair / p.Hkv, kvh = pair - b * p.Hkv;
+        const int S = seq_len_of(p.seq_lens, b, p.max_seq_len);
+        if (S <= 0 || S > p.max_seq_len || S < p.n_new) continue;
+        const int S_old = S - p.n_new;
+        const int nb = ceil_div(S, p.bs);
+        const int d = lane * E;
+        T* kc = static_cast<T*>(const_cast<void*>(p.k.data)) + b * p.k.sb + kvh * p.k.sh + d;
+        T* vc = static_cast<T*>(const_cast<void*>(p.v.data)) + b * p.v.sb + kvh * p.v.sh + d;
+        const T* kn = static_cast<const T*>(p.k_new.data) + b * p.k_new.sb + kvh * p.k_new.sh + d;
+        const T* vn = static_cast<const T*>(p.v_new.data) + b * p.v_new.sb + kvh * p.v_new.sh + d;
+        float qr[GP][E];
+        const T* qb = static_cast<const T*>(p.q.data) + b * p.q.sb + (int64_t)kvh * p.g * p.q.sh + d;
+#pragma unroll
+        for (int j = 0; j < GP; ++j) {
+          if (j < p.g) {
+            load_vec<T, E>(qb + j * p.q.sh, qr[j]);
+          } else {
+#pragma unroll
+            for (int e = 0; e < E; ++e) qr[j][e] = 0.f;
+          }
+        }
+        for (int blk = S_old / p.bs; blk < nb; ++blk) {
+          const int t0 = blk * p.bs, t1 = imin(t0 + p.bs, S);
+          float acc[E];
+#pragma unroll
+          for (int e = 0; e < E; ++e) acc[e] = 0.f;
+          for (int base = t0; base < t1; base += 16) {
+            float x[16][E];
+#pragma unroll
+            for (int u = 0; u < 16; ++u) {
+              const int t = base + u;
+              if (t < t1) {
+                if (t >= S_old) {
+                  const T* src = kn + (int64_t)(t - S_old) * p.k_new.ss;
+                  load_vec<T, E>(src, x[u]);
+                  copy_vec<T, E>(kc + (int64_t)t * p.k.ss, src);
+                  copy_vec<T, E>(vc + (int64_t)t * p.v.ss, vn + (int64_t)(t - S_old) * p.v_new.ss);
+                } else {
+                  load_vec<T, E>(kc + (int64_t)t * p.k.ss, x[u]);
+                }
+              }
+            }
+#pragma unroll
+            for (int u = 0; u < 16; ++u) {
+              const int t = base + u;
+              if (t < t1) {
+#pragma unroll
+                for (int e = 0; e < E; ++e) acc[e] = (t == t0) ? x[u][e] : __fadd_rn(acc[e], x[u][e]);
+              }
+            }
+          }
+          const float n = (float)(t1 - t0);
+          float cen[E];
+#pragma unroll
+          for (int e = 0; e < E; ++e) cen[e] = __fdiv_rn(acc[e], n);
+          float* crow = p.cent + ((int64_t)(b * p.Hkv + kvh) * p.nb_cap + blk) * D + d;
+#pragma unroll
+          for (int e = 0; e < E; ++e) crow[e] = cen[e];
+#pragma unroll
+          for (int j = 0; j < GP; ++j) {
+            if (j < p.g) {
+              float part = 0.f;
+#pragma unroll
+              for (int e = 0; e < E; ++e) part = fmaf(qr[j][e], cen[e], part);
+#pragma unroll
+              for (int o = 16; o; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+              if (lane == 0)
+                p.scores[(int64_t)(b * p.Hq + kvh * p.g + j) * p.score_stride + blk] = part;
+            }
+          }
+        }
+      }
+    }
+  } else {
+    // ---------------- consumers ----------------
+    int i = 0;
+    for (int c = c_begin; c < c_end; ++c, ++i) {
+      int b, kvh, ch;
+      chunk_of(c, b, kvh, ch);
+      const int s = i % kEstStages;
+      if (!mbar_wait_bounded(&full_bar[s], (i / kEstStages) & 1)) {
+        if (lane == 0) report(p.status, ADAKV_ST_WAIT_TIMEOUT);
+        break;
+      }
+      const int S = seq_len_of(p.seq_lens, b, p.max_seq_len);
+      const int nb = ceil_div(S, p.bs);
+      const int row0 = ch * kEstRows;
+      const int nrows = imin(kEstRows, nb - row0);
+      // rows refreshed by the append warp are scored there
+      const int skip_from = appending ? (S - p.n_new) / p.bs - row0 : nrows;
+      const int lim = imin(nrows, skip_from);
+      const float* tile = ring + s * STAGE_F;
+      const T* qs = reinterpret_cast<const T*>(tile + TILE_F);
+      float qr[GP][E];
+#pragma unroll
+      for (int j = 0; j < GP; ++j) {
+        if (j < p.g) {
+          load_vec<T, E>(qs + j * D + lane * E, qr[j]);
+        } else {
+#pragma unroll
+          for (int e = 0; e < E; ++e) qr[j][e] = 0.f;
+        }
+      }
+#pragma unroll
+      for (int grp = 0; grp < NG; ++grp) {
+        const int rbase = warp * RPW + grp * R;
+        float v[32];
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          float cr[E];
+          lds_row<E>(tile + (rbase + r) * D + lane * E, cr);
+#pragma unroll
+          for (int j = 0; j < GP; ++j) {
+            float acc = 0.f;
+#pragma unroll
+            for (int e = 0; e < E; ++e) acc = fmaf(qr[j][e], cr[e], acc);
+            v[r * GP + j] = acc;
+          }
+        }
+        const float sc = warp_reduce_scatter32(v, lane);
+        const int row = rbase + lane / GP, j = lane % GP;
+        if (j < p.g && row < lim)
+          p.scores[(int64_t)(b * p.Hq + kvh * p.g + j) * p.score_stride + row0 + row] = sc;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty_bar[s]);
     }
   }
-#pragma unroll
-  for (int off = GP; off < 32; off <<= 1) gmax = fmaxf(gmax, __shfl_xor_sync(0xffffffffu, gmax, off));
-  if (lane < GP) wmax[warp][lane] = gmax;
-  __syncthreads();
-  if (tid < p.g) {
-    float m = wmax[0][tid];
-#pragma unroll
-    for (int w = 1; w < kEstThreads / 32; ++w) m = fmaxf(m, wmax[w][tid]);
-    p.chunkmax[(int64_t)(b * p.Hq + kvh * p.g + tid) * p.chunks_cap + chunk] = m;
+}
+
+size_t estimate_smem_bytes(int dtype, int D, int B) {
+  const size_t tile = (size_t)kEstRows * D * 4;
+  const size_t q = ((size_t)16 * D * (dtype == ADAKV_DTYPE_F32 ? 4 : 2) + 15) / 16 * 16;
+  return kEstStages * (tile + q) + sizeof(int) * (2 * (size_t)B + 2);
+}
+
+template <typename F>
+static cudaError_t for_each_estimate(int dtype, int D, int g, F&& f) {
+#define ADAKV_EST_G(TT, DD)                                      \
+  if (D == DD) {                                                 \
+    if (g <= 4) return f(estimate_kernel<TT, DD, 4>);            \
+    if (g <= 8) return f(estimate_kernel<TT, DD, 8>);            \
+    if (g <= 16) return f(estimate_kernel<TT, DD, 16>);          \
   }
-  pdl_launch_dependents();
-}
-
-template <typename T, int D, int GP>
-static cudaError_t launch_est_t(const EstParams& p, int nb_max, cudaStream_t stream) {
-  const size_t smem = (size_t)kEstRows * D * sizeof(float);  // <= 32 KB: no opt-in needed
-  dim3 grid(ceil_div(imax(nb_max, 1), kEstRows), p.Hkv, p.B);
-  estimate_kernel<T, D, GP><<<grid, kEstThreads, smem, stream>>>(p);
-  return cudaGetLastError();
-}
-
-template <typename T, int D>
-static cudaError_t launch_est_d(const EstParams& p, int nb_max, cudaStream_t stream) {
-  if (p.g <= 4) return launch_est_t<T, D, 4>(p, nb_max, stream);
-  if (p.g <= 8) return launch_est_t<T, D, 8>(p, nb_max, stream);
-  if (p.g <= 16) return launch_est_t<T, D, 16>(p, nb_max, stream);
-  return cudaErrorInvalidValue;
-}
-
-cudaError_t launch_estimate(const EstParams& p, int dtype, int D, int nb_max, cudaStream_t stream) {
-#define ADAKV_EST_CASE(TT)                                              \
-  if (D == 64) return launch_est_d<TT, 64>(p, nb_max, stream);         \
-  if (D == 128) return launch_est_d<TT, 128>(p, nb_max, stream);
   if (dtype == ADAKV_DTYPE_F32) {
-    ADAKV_EST_CASE(float)
+    ADAKV_EST_G(float, 64) ADAKV_EST_G(float, 128)
   } else if (dtype == ADAKV_DTYPE_F16) {
-    ADAKV_EST_CASE(__half)
+    ADAKV_EST_G(__half, 64) ADAKV_EST_G(__half, 128)
   } else if (dtype == ADAKV_DTYPE_BF16) {
-    ADAKV_EST_CASE(__nv_bfloat16)
+    ADAKV_EST_G(__nv_bfloat16, 64) ADAKV_EST_G(__nv_bfloat16, 128)
   }
-#undef ADAKV_EST_CASE
+#undef ADAKV_EST_G
   return cudaErrorInvalidValue;
+}
+
+cudaError_t estimate_kernels_init() {
+  for (int dt = 0; dt < 3; ++dt)
+    for (int D : {64, 128})
+      for (int g : {4, 8, 16}) {
+        const size_t smem = estimate_smem_bytes(dt, D, kEstMaxBatch);
+        cudaError_t e = for_each_estimate(dt, D, g, [&](auto kern) {
+          return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        });
+        if (e != cudaSuccess) return e;
+      }
+  return cudaSuccess;
+}
+
+cudaError_t launch_estimate(const EstParams& p, int dtype, int D, int nb_max, int grid,
+                            cudaStream_t st, const LaunchOpts& o) {
+  (void)nb_max;
+  const size_t smem = estimate_smem_bytes(dtype, D, p.B);
+  return for_each_estimate(dtype, D, p.g, [&](auto kern) {
+    return launch_ex(kern, dim3(grid), dim3(kEstThreads), smem, st, o, p);
+  });
 }
 
 }  // namespace adakv

@@ -2,10 +2,15 @@
 // translation units and the C-ABI layer (capi.cu).
 #pragma once
 
+#include <utility>
+
 #include "common.cuh"
 
 namespace adakv {
 
+// ---------------------------------------------------------------------------
+// (a) centroid build / append / refresh (stand-alone entry points)
+// ---------------------------------------------------------------------------
 struct CentroidParams {
   View k, v;            // caches [B, Hkv, S, D]
   View k_new, v_new;    // [B, Hkv, n_new, D] (append only)
@@ -17,99 +22,160 @@ struct CentroidParams {
   uint32_t* status;
 };
 
+// weight-exchange slot of one (sequence, query head) for the plan barrier
+struct __align__(16) PlanSlot {
+  double w;
+  unsigned int epoch;
+  unsigned int pad;
+};
+
+// ---------------------------------------------------------------------------
+// (b) estimator (+ fused append of the step's new tokens)
+// ---------------------------------------------------------------------------
+constexpr int kEstStages = 4;          // TMA ring depth
+constexpr int kEstConsumerWarps = 8;   // 8 warps x 8 rows = kEstRows
+constexpr int kEstThreads = (kEstConsumerWarps + 2) * 32;  // + producer warp + refresh warp
+constexpr int kEstMaxBatch = 4096;     // sequences per launch (per-sequence chunk prefix in smem)
+
 struct EstParams {
   View q;                 // [B, Hq, D]
-  const float* cent;      // [B, Hkv, nb_cap, D]
+  float* cent;            // [B, Hkv, nb_cap, D]
   int nb_cap;
-  const int* seq_lens;
+  const int* seq_lens;    // NULL -> max_seq_len
   int max_seq_len;
   int B, Hq, Hkv, g, bs;
   float* scores;          // [B, Hq, score_stride]
   int score_stride;
-  float* chunkmax;        // [B, Hq, chunks_cap]
-  int chunks_cap;
+  uint32_t* epoch;        // incremented once per launch (per-call tag for the plan barrier)
+  PlanSlot* slots;        // [B*Hq] weight-exchange slots: tags cleared here, before the plan
+  // fused append: n_new > 0 and k_new.data != NULL
+  View k, v, k_new, v_new;
+  int n_new;
   uint32_t* status;
 };
 
-struct BudgetParams {
+// ---------------------------------------------------------------------------
+// (c) plan: entropy budget + per-sequence weight exchange + top-k
+// ---------------------------------------------------------------------------
+constexpr int kPlanThreads = 1024;
+constexpr int kPlanSmemMaxKeys = 48 * 1024;   // keys staged in smem up to this many blocks
+constexpr int kPlanMaxBlocks = 512 * 1024;    // longest sequence in blocks (bitmap words in smem)  // larger rows are re-read from L2 each pass
+
+
+
+struct PlanParams {
   const int* seq_lens;
   int max_seq_len;
   int B, Hq, bs;
   SelectCfg cfg;
   const float* scores;
   int score_stride;
-  const float* chunkmax;
-  int chunks_cap;
-  double* weights;          // [B*Hq]
-  int* seq_counter;         // [B]   zero between calls
-  int* glob_counter;        //       zero between calls
-  int* sel_lens;            // [B*Hq] out: realised count per head
-  int* head_item_off;       // [B*Hq] seq-local exclusive prefix of items
-  int* seq_items;           // [B+1]  per-seq totals, then global bases
-  int* head_item_base;      // [B*Hq] global index of the head's first item
-  int* total_items;
-  int item_blocks;
+  const uint32_t* epoch;
+  PlanSlot* slots;          // [B*Hq]
+  int* sel_lens;            // [B*Hq] out
+  int* block_table;         // [B*Hq, table_width] out, ascending block ids
+  int table_width;
+  uint32_t* bitmap;         // [B*Hq, bm_words] out, bit j = block j selected
+  int bm_words;
+  int nw_max;               // ceil(ceil(max_seq_len / bs) / 32): sizes the shared buffers
+  int seqs_per_round;       // grid = seqs_per_round * Hq CTAs
   uint32_t* status;
 };
 
-struct SelectParams {
-  const int* seq_lens;
-  int max_seq_len;
-  int B, Hq, bs;
-  int n_sink, n_local;
-  const float* scores;
-  int score_stride;
-  const int* sel_lens;
-  int* block_table;         // [B*Hq, table_width]
-  int table_width;
-  const int* head_item_base;
-  int4* work_hdr;           // {b, h, head_item_base, count}
-  int* work_blk;            // [items, item_blocks]
-  int item_blocks;
-  uint32_t* status;
-};
+// ---------------------------------------------------------------------------
+// (d) attend: one cluster per (sequence, KV head) over the union of the group's blocks
+// ---------------------------------------------------------------------------
+constexpr size_t kAttendSmemMax = 200 * 1024;  // opt-in dynamic shared memory of one attend CTA
 
 struct AttendParams {
   View q, k, v, out;
   const int* seq_lens;
   int max_seq_len;
-  int B, Hq, g;
+  int B, Hq, Hkv, g;
   float sm_scale;
-  const int* block_table;   // only for the stand-alone item builder
-  int table_width;
-  const int* sel_lens;
-  const int4* work_hdr;
-  const int* work_blk;
-  const int* total_items;
-  int item_blocks;
-  int* head_item_base;      // item builder output
-  int4* work_hdr_w;
-  int* work_blk_w;
-  int* total_items_w;
-  int* head_counter;        // [B*Hq], zero between calls
-  float2* part_ml;
-  float* part_o;
+  const uint32_t* bitmap;   // [B*Hq, bm_words]
+  int bm_words;
+  int nw_max;               // ceil(ceil(max_seq_len / bs) / 32)
+  int slice_cap;            // >= union blocks one CTA of the cluster can get
+  int nbt;                  // blocks per gather batch (double buffered)
   uint32_t* status;
 };
 
-// shared memory one select CTA may stage (keys); larger rows re-read L2
-constexpr int kSelectSmemMaxKeys = 50 * 1024;
-// shared memory budget of one attend CTA (K + V tiles of an item)
-constexpr size_t kAttendSmemMax = 200 * 1024;
+struct TableParams {        // block table -> per-head bitmaps (stand-alone attend)
+  const int* block_table;
+  int table_width;
+  const int* sel_lens;
+  const int* seq_lens;
+  int max_seq_len;
+  int B, Hq, bs;
+  uint32_t* bitmap;
+  int bm_words;
+  uint32_t* status;
+};
 
+// ---------------------------------------------------------------------------
+// launch helper: cudaLaunchKernelEx with optional PDL / cooperative / cluster
+// ---------------------------------------------------------------------------
+struct LaunchOpts {
+  bool pdl = false;         // programmatic dependent launch on the previous kernel
+  bool coop = false;        // all CTAs co-resident (they wait on one another)
+  unsigned cluster_x = 0;   // thread-block cluster size along x (0: none)
+};
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_ex(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                             cudaStream_t st, const LaunchOpts& o, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[3];
+  unsigned n = 0;
+  if (o.pdl) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (o.coop) {
+    attr[n].id = cudaLaunchAttributeCooperative;
+    attr[n].val.cooperative = 1;
+    ++n;
+  }
+  if (o.cluster_x) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = o.cluster_x;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
+// ---------------------------------------------------------------------------
+// launchers (one per translation unit)
+// ---------------------------------------------------------------------------
 cudaError_t launch_centroid(const CentroidParams& p, int dtype, int D, int blocks_per_seq,
                             cudaStream_t stream);
-cudaError_t launch_estimate(const EstParams& p, int dtype, int D, int nb_max, cudaStream_t stream);
-cudaError_t launch_budget(const BudgetParams& p, cudaStream_t stream);
-cudaError_t launch_select(const SelectParams& p, int nb_max, cudaStream_t stream);
-cudaError_t launch_attend(const AttendParams& p, int dtype, int D, int bs, int grid,
-                          cudaStream_t stream);
-cudaError_t launch_items(const AttendParams& p, cudaStream_t stream);
+cudaError_t launch_estimate(const EstParams& p, int dtype, int D, int nb_max, int grid,
+                            cudaStream_t stream, const LaunchOpts& o);
+cudaError_t launch_plan(const PlanParams& p, int nb_max, int grid, cudaStream_t stream,
+                        const LaunchOpts& o);
+cudaError_t launch_attend(const AttendParams& p, int dtype, int D, int bs, int cluster,
+                          cudaStream_t stream, const LaunchOpts& o);
+cudaError_t launch_table_bitmap(const TableParams& p, cudaStream_t stream, const LaunchOpts& o);
 
-// once per device (current device): opt-in shared memory sizes
-cudaError_t select_kernels_init();
+// once per device (current device): opt-in shared memory / cluster sizes
+cudaError_t estimate_kernels_init();
+cudaError_t plan_kernels_init();
 cudaError_t attend_kernels_init();
-// attend CTAs resident per SM for this element type / head dim / block size / item size
-int attend_ctas_per_sm(int dtype, int D, int bs, int item_blocks);
+size_t estimate_smem_bytes(int dtype, int D, int B);
+size_t plan_smem_bytes(int nb_max);
+int plan_ctas_per_sm(int nb_max);
+// largest power-of-two cluster size (<= 16) the attend kernel can run with
+int attend_max_cluster(int dtype, int D, int bs, int g, size_t smem);
+size_t attend_smem_bytes(int dtype, int D, int bs, int nbt, int g, int nw_max, int slice_cap);
 
 }  // namespace adakv

@@ -1,148 +1,38 @@
-// (c) Entropy-driven per-head budget and ragged per-head top-k block selection.
+// (c) Entropy-driven per-head budget and ragged per-head top-k block selection,
+// one kernel, one CTA of 1024 threads per (sequence, query head).
 //
-// budget_kernel, one CTA per (b, query head):
-//   z = scores / max(T, 1e-6); p = softmax(z) in float32; the head's weight is
-//   w = -sum(p * log(max(p, 1e-9))) / log(max(nb, 2)) + 1e-6 (float64 after the
-//   division), exactly the formula of adakv/budget.py:28-37.  The softmax maximum
-//   comes from the estimator's per-chunk maxima; two passes over the row (from
-//   L2) give the normaliser and the entropy.  The last CTA of a sequence to
-//   finish (atomic ticket, no spinning) turns the Hq weights into per-head counts
-//   (budget.py:71-86 + selector.py:49-54, half-to-even rounding) and the
-//   per-head attend work-item offsets; the last sequence to finish turns the
-//   per-sequence item totals into global item bases.
-//
-// select_kernel, one CTA of 1024 threads per (b, query head):
-//   keys are the order-preserving uint32 images of the float32 scores, with
-//   sink [0, sink) and local [nb-local, nb) blocks forced to 0xFFFFFFFF (the
-//   reference's +inf bias, selector.py:44-48).  A 4-pass 8-bit MSB radix select
-//   (shared-memory histograms, one warp suffix-scan per pass) finds the k-th
-//   largest key T; blocks with key > T, plus the lowest-indexed blocks with
-//   key == T, are written in ascending block order with two block-wide scans.
-//   The row is staged in shared memory when it fits (nb <= 50K blocks), else
-//   every pass re-reads it from L2.  The same CTA writes the attend work items
-//   (header + up to item_blocks block ids) of its head.
+// 1. The head's score row is staged in shared memory (coalesced loads).
+// 2. Weight, exactly the formula of adakv/budget.py:28-37: z = s / max(T, 1e-6),
+//    p = softmax(z) in float32, w = -sum(p * log(max(p, 1e-9))) / log(max(nb, 2))
+//    + 1e-6 (float64 after the division, as NumPy promotes it).
+// 3. The Hq CTAs of a sequence exchange weights through per-head slots tagged
+//    with the call's epoch (written by the estimator): each CTA publishes
+//    (w, epoch) and one warp polls the sequence's slots (bounded by a 200 ms
+//    wall-clock limit, after which the status word records a timeout).  Every
+//    CTA then sums the Hq weights in the same fixed order, so all heads see the
+//    same total, and derives its count with the reference's arithmetic
+//    (budget.py:71-86, selector.py:49-54; half-to-even rounding).  The launch is
+//    cooperative (all CTAs co-resident) and processes whole sequences per round.
+// 4. Top-k: keys are the order-preserving uint32 images of the scores; sink
+//    [0, sink) and local [nb-local, nb) blocks get 0xFFFFFFFF (the reference's
+//    +inf bias, selector.py:44-48).  A 4-pass MSB radix select over shared
+//    memory finds the k-th largest key T; blocks with key > T and the
+//    lowest-indexed blocks with key == T are selected.
+// 5. Output: warp ballots build the selection bitmap word by word (element
+//    j*1024 + t lands in word j*32 + warp), ties are resolved on the bitmap with
+//    one block scan, and a second scan writes the ascending block table.
 #include "kernels.h"
 
 namespace adakv {
 
-__device__ __forceinline__ float block_max256(float v, float* red) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  v = warp_max(v);
-  if (lane == 0) red[warp] = v;
-  __syncthreads();
-  float r = red[0];
-#pragma unroll
-  for (int w = 1; w < kBudgetThreads / 32; ++w) r = fmaxf(r, red[w]);
-  __syncthreads();
-  return r;
+__device__ __forceinline__ uint32_t ld_acquire_u32(const unsigned int* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
 }
 
-__device__ __forceinline__ double block_sum256(double v, double* red) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  v = warp_sum(v);
-  if (lane == 0) red[warp] = v;
-  __syncthreads();
-  double r = 0.0;
-#pragma unroll
-  for (int w = 0; w < kBudgetThreads / 32; ++w) r += red[w];
-  __syncthreads();
-  return r;
-}
-
-__global__ void __launch_bounds__(kBudgetThreads) budget_kernel(BudgetParams p) {
-  __shared__ float fred[kBudgetThreads / 32];
-  __shared__ double dred[kBudgetThreads / 32];
-  __shared__ int s_flag;
-  __shared__ double s_sumw;
-  __shared__ int scan_scratch[33];
-  const int h = blockIdx.x, b = blockIdx.y, row = b * p.Hq + h, tid = threadIdx.x;
-  pdl_wait();
-  int S = seq_len_of(p.seq_lens, b, p.max_seq_len);
-  if (S < 0 || S > p.max_seq_len) S = 0;  // reported by the estimator
-  const int nb = ceil_div(S, p.bs);
-
-  double w = 0.0;
-  if (nb >= 2 && p.cfg.policy == ADAKV_POLICY_ADAPTIVE) {
-    const int nchunks = ceil_div(nb, kEstRows);
-    float m = -INFINITY;
-    for (int c = tid; c < nchunks; c += kBudgetThreads)
-      m = fmaxf(m, p.chunkmax[(int64_t)row * p.chunks_cap + c]);
-    m = block_max256(m, fred);
-    const float Tf = (float)(p.cfg.temperature > 1e-6 ? p.cfg.temperature : 1e-6);
-    const float zmax = __fdiv_rn(m, Tf);  // max(s / T) == max(s) / T (rounding is monotone)
-    const float* s = p.scores + (int64_t)row * p.score_stride;
-    double zacc = 0.0;
-#pragma unroll 4
-    for (int i = tid; i < nb; i += kBudgetThreads) zacc += (double)expf(__fdiv_rn(s[i], Tf) - zmax);
-    const float Z = (float)block_sum256(zacc, dred);
-    double hacc = 0.0;
-#pragma unroll 4
-    for (int i = tid; i < nb; i += kBudgetThreads) {
-      const float e = expf(__fdiv_rn(s[i], Tf) - zmax);
-      const float pi = __fdiv_rn(e, Z);
-      hacc += (double)__fmul_rn(pi, logf(fmaxf(pi, 1e-9f)));
-    }
-    const float hsum = (float)block_sum256(hacc, dred);
-    w = (double)(-hsum) / log((double)imax(nb, 2)) + 1e-6;
-  }
-  if (tid == 0) p.weights[row] = w;
-
-  // ---- last CTA of this sequence: per-head counts and item offsets ----
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) s_flag = (atomicAdd(&p.seq_counter[b], 1) == p.Hq - 1);
-  __syncthreads();
-  if (!s_flag) return;
-  __threadfence();
-  if (tid == 0) {
-    p.seq_counter[b] = 0;
-    double sw = 0.0;
-    for (int hh = 0; hh < p.Hq; ++hh) sw += __ldcg(&p.weights[b * p.Hq + hh]);
-    s_sumw = sw;
-  }
-  __syncthreads();
-  const SeqBudget sb = seq_budget(nb, p.cfg);
-  int carry = 0;
-  for (int base = 0; base < p.Hq; base += kBudgetThreads) {
-    const int hh = base + tid;
-    int items = 0;
-    if (hh < p.Hq) {
-      const int k = head_count(sb, p.cfg, __ldcg(&p.weights[b * p.Hq + hh]), s_sumw, p.Hq);
-      p.sel_lens[b * p.Hq + hh] = k;
-      items = ceil_div(k, p.item_blocks);
-    }
-    const int off = block_exclusive_scan(items, scan_scratch);
-    if (hh < p.Hq) p.head_item_off[b * p.Hq + hh] = carry + off;
-    carry += scan_scratch[32];
-    __syncthreads();
-  }
-  if (tid == 0) p.seq_items[b] = carry;
-
-  // ---- last sequence overall: global item bases ----
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) s_flag = (atomicAdd(p.glob_counter, 1) == p.B - 1);
-  __syncthreads();
-  if (!s_flag) return;
-  __threadfence();
-  if (tid == 0) *p.glob_counter = 0;
-  carry = 0;
-  for (int base = 0; base < p.B; base += kBudgetThreads) {
-    const int bb = base + tid;
-    const int t = bb < p.B ? __ldcg(&p.seq_items[bb]) : 0;
-    const int off = block_exclusive_scan(t, scan_scratch);
-    if (bb < p.B) p.seq_items[bb] = carry + off;  // now the sequence's base
-    carry += scan_scratch[32];
-    __syncthreads();
-  }
-  if (tid == 0) {
-    p.seq_items[p.B] = carry;
-    *p.total_items = carry;
-  }
-  __syncthreads();
-  for (int r = tid; r < p.B * p.Hq; r += kBudgetThreads)
-    p.head_item_base[r] = __ldcg(&p.seq_items[r / p.Hq]) + __ldcg(&p.head_item_off[r]);
-  pdl_launch_dependents();
+__device__ __forceinline__ void st_release_u32(unsigned int* p, uint32_t v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
 // order-preserving float -> uint32 map; NaN sorts below everything
@@ -152,144 +42,268 @@ __device__ __forceinline__ uint32_t score_key(float f) {
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
+__device__ __forceinline__ float block_max1024(float v, float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  v = warp_max(v);
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    float x = red[lane];
+    x = warp_max(x);
+    if (lane == 0) red[32] = x;
+  }
+  __syncthreads();
+  const float r = red[32];
+  __syncthreads();
+  return r;
+}
+
+__device__ __forceinline__ double block_sum1024(double v, double* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  v = warp_sum(v);
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    double x = red[lane];
+    x = warp_sum(x);
+    if (lane == 0) red[32] = x;
+  }
+  __syncthreads();
+  const double r = red[32];
+  __syncthreads();
+  return r;
+}
+
 template <bool SMEM>
-__global__ void __launch_bounds__(kSelectThreads) select_kernel(SelectParams p) {
-  extern __shared__ uint32_t skeys[];
+__global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanParams p) {
+  extern __shared__ __align__(16) uint32_t sm[];
   __shared__ uint32_t hist[256];
   __shared__ int s_digit, s_above;
   __shared__ int scan_scratch[33];
-  const int h = blockIdx.x, b = blockIdx.y, row = b * p.Hq + h;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  pdl_wait();
-  int S = seq_len_of(p.seq_lens, b, p.max_seq_len);
-  if (S < 0 || S > p.max_seq_len) S = 0;
-  const int nb = ceil_div(S, p.bs);
-  int K = p.sel_lens[row];
-  if (K > p.table_width) {
-    if (tid == 0) report(p.status, ADAKV_ST_BAD_SEL_LEN);
-    K = p.table_width;
-  }
-  if (K <= 0 || nb <= 0) return;
-  const int sink = imin(p.n_sink, nb), local = imin(p.n_local, nb);
-  const float* srow = p.scores + (int64_t)row * p.score_stride;
-  auto make_key = [&](int i) -> uint32_t {
-    return (i < sink || i >= nb - local) ? 0xFFFFFFFFu : score_key(srow[i]);
-  };
-  if (SMEM) {
-    for (int i = tid; i < nb; i += kSelectThreads) skeys[i] = make_key(i);
-    __syncthreads();
-  }
-  auto key = [&](int i) -> uint32_t { return SMEM ? skeys[i] : make_key(i); };
+  __shared__ float fred[33];
+  __shared__ double dred[33];
+  __shared__ double s_sumw;
 
-  uint32_t T = 0;
-  int need = 0x7FFFFFFF;  // K >= nb: everything is selected
-  if (K < nb) {
-    uint32_t prefix = 0, pmask = 0;
-    int rem = K;
-#pragma unroll 1
-    for (int pass = 0; pass < 4; ++pass) {
-      const int shift = 24 - 8 * pass;
-      if (tid < 256) hist[tid] = 0;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  // ballot words are written 32 at a time: round the word count up to 32
+  const int nw_alloc = (p.nw_max + 31) / 32 * 32;
+  uint32_t* keys = sm;                                        // [nw_alloc * 32] (SMEM only)
+  uint32_t* wsel = sm + (SMEM ? nw_alloc * 32 : 0);           // [nw_alloc]
+  uint32_t* weq = wsel + nw_alloc;                            // [nw_alloc]
+
+  pdl_wait();
+  // per-call tag, never 0 (the estimator cleared every tag to 0)
+  const uint32_t ep = (*reinterpret_cast<const volatile uint32_t*>(p.epoch) & 0x7FFFFFFFu) | 0x80000000u;
+  const int h = blockIdx.x % p.Hq;
+  const int slot_seq = blockIdx.x / p.Hq;
+
+  for (int b0 = 0; b0 < p.B; b0 += p.seqs_per_round) {
+    const int b = b0 + slot_seq;
+    if (b >= p.B) break;
+    const int row = b * p.Hq + h;
+    int S = seq_len_of(p.seq_lens, b, p.max_seq_len);
+    if (S < 0 || S > p.max_seq_len) S = 0;  // reported by the estimator
+    const int nb = ceil_div(S, p.bs);
+    const int nw = ceil_div(nb, 32);
+    const float* srow = p.scores + (int64_t)row * p.score_stride;
+
+    if (SMEM) {
+#pragma unroll 8
+      for (int i = tid; i < nb; i += kPlanThreads) keys[i] = __float_as_uint(srow[i]);
       __syncthreads();
-      for (int i = tid; i < nb; i += kSelectThreads) {
-        const uint32_t k = key(i);
-        if ((k & pmask) == prefix) atomicAdd(&hist[(k >> shift) & 0xFFu], 1u);
+    }
+    auto val = [&](int i) -> float { return SMEM ? __uint_as_float(keys[i]) : srow[i]; };
+
+    // ---- entropy weight ----
+    double w = 0.0;
+    if (nb >= 2 && p.cfg.policy == ADAKV_POLICY_ADAPTIVE) {
+      float m = -INFINITY;
+      for (int i = tid; i < nb; i += kPlanThreads) m = fmaxf(m, val(i));
+      m = block_max1024(m, fred);
+      const float Tf = (float)(p.cfg.temperature > 1e-6 ? p.cfg.temperature : 1e-6);
+      const float zmax = __fdiv_rn(m, Tf);  // max(s / T) == max(s) / T (rounding is monotone)
+      double zacc = 0.0;
+      for (int i = tid; i < nb; i += kPlanThreads) zacc += (double)expf(__fdiv_rn(val(i), Tf) - zmax);
+      const float Z = (float)block_sum1024(zacc, dred);
+      double hacc = 0.0;
+      for (int i = tid; i < nb; i += kPlanThreads) {
+        const float e = expf(__fdiv_rn(val(i), Tf) - zmax);
+        const float pi = __fdiv_rn(e, Z);
+        hacc += (double)__fmul_rn(pi, logf(fmaxf(pi, 1e-9f)));
       }
-      __syncthreads();
-      if (warp == 0) {
-        // lane l owns bins 255-8l .. 248-8l (descending)
-        uint32_t c[8], tot = 0;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          c[e] = hist[255 - 8 * lane - e];
-          tot += c[e];
+      const float hsum = (float)block_sum1024(hacc, dred);
+      w = (double)(-hsum) / log((double)imax(nb, 2)) + 1e-6;
+    }
+
+    // ---- exchange weights within the sequence ----
+    if (tid == 0) {
+      p.slots[row].w = w;
+      __threadfence();
+      st_release_u32(&p.slots[row].epoch, ep);
+    }
+    if (warp == 0) {
+      const uint64_t t0 = globaltimer_ns();
+      bool ok = false;
+      while (true) {
+        bool mine = true;
+        for (int hh = lane; hh < p.Hq; hh += 32)
+          mine &= (ld_acquire_u32(&p.slots[b * p.Hq + hh].epoch) == ep);
+        ok = __all_sync(0xffffffffu, mine);
+        if (ok || globaltimer_ns() - t0 > kWaitLimitNs) break;
+      }
+      if (!ok && lane == 0) report(p.status, ADAKV_ST_WAIT_TIMEOUT);
+      double part = 0.0;
+      for (int hh = lane; hh < p.Hq; hh += 32)
+        part += *reinterpret_cast<const volatile double*>(&p.slots[b * p.Hq + hh].w);
+      part = warp_sum(part);  // fixed xor tree: every CTA of the sequence gets the same sum
+      if (lane == 0) s_sumw = part;
+    }
+    __syncthreads();
+    const SeqBudget sbud = seq_budget(nb, p.cfg);
+    const int K = imin(head_count(sbud, p.cfg, w, s_sumw, p.Hq), p.table_width);
+    const int sink = imin(p.cfg.n_sink, nb), local = imin(p.cfg.n_local, nb);
+    auto make_key = [&](int i) -> uint32_t {
+      return (i < sink || i >= nb - local) ? 0xFFFFFFFFu : score_key(val(i));
+    };
+
+    // ---- radix select of the K-th largest key ----
+    uint32_t T = 0;
+    int need = 0x7FFFFFFF;  // K >= nb: every block is selected
+    if (K < nb) {
+      if (SMEM) {
+        for (int i = tid; i < nb; i += kPlanThreads) keys[i] = make_key(i);
+        __syncthreads();
+      }
+      auto key = [&](int i) -> uint32_t { return SMEM ? keys[i] : make_key(i); };
+      uint32_t prefix = 0, pmask = 0;
+      int rem = K;
+#pragma unroll 1
+      for (int pass = 0; pass < 4; ++pass) {
+        const int shift = 24 - 8 * pass;
+        if (tid < 256) hist[tid] = 0;
+        __syncthreads();
+        for (int i = tid; i < nb; i += kPlanThreads) {
+          const uint32_t k = key(i);
+          if ((k & pmask) == prefix) atomicAdd(&hist[(k >> shift) & 0xFFu], 1u);
         }
-        uint32_t incl = tot;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
-          if (lane >= o) incl += y;
-        }
-        const uint32_t excl = incl - tot;
-        if (excl < (uint32_t)rem && (uint32_t)rem <= incl) {
-          uint32_t acc = excl;
+        __syncthreads();
+        if (warp == 0) {
+          uint32_t c[8], tot = 0;
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
-            if (acc + c[e] >= (uint32_t)rem) {
-              s_digit = 255 - 8 * lane - e;
-              s_above = (int)acc;
-              break;
+            c[e] = hist[255 - 8 * lane - e];
+            tot += c[e];
+          }
+          uint32_t incl = tot;
+#pragma unroll
+          for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += y;
+          }
+          const uint32_t excl = incl - tot;
+          if (excl < (uint32_t)rem && (uint32_t)rem <= incl) {
+            uint32_t acc = excl;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              if (acc + c[e] >= (uint32_t)rem) {
+                s_digit = 255 - 8 * lane - e;
+                s_above = (int)acc;
+                break;
+              }
+              acc += c[e];
             }
-            acc += c[e];
           }
         }
+        __syncthreads();
+        rem -= s_above;
+        prefix |= (uint32_t)s_digit << shift;
+        pmask |= 0xFFu << shift;
       }
-      __syncthreads();
-      rem -= s_above;
-      prefix |= (uint32_t)s_digit << shift;
-      pmask |= 0xFFu << shift;
-      __syncthreads();
+      T = prefix;
+      need = rem;
     }
-    T = prefix;
-    need = rem;  // keys equal to T taken, lowest block index first
-  }
 
-  // ---- compaction in ascending block order ----
-  const int E = ceil_div(nb, kSelectThreads);
-  const int beg = imin(tid * E, nb), end = imin(beg + E, nb);
-  int n_gt = 0, n_eq = 0;
-  for (int i = beg; i < end; ++i) {
-    const uint32_t k = key(i);
-    n_gt += (k > T);
-    n_eq += (k == T);
-  }
-  const int eq_before = block_exclusive_scan(n_eq, scan_scratch);
-  const int eq_take = imax(0, imin(n_eq, need - eq_before));
-  const int pos0 = block_exclusive_scan(n_gt + eq_take, scan_scratch);
-  const int C = p.item_blocks;
-  const int item0 = p.head_item_base[row];
-  int* trow = p.block_table + (int64_t)row * p.table_width;
-  int pos = pos0, r = eq_before;
-  for (int i = beg; i < end; ++i) {
-    const uint32_t k = key(i);
-    bool sel = k > T;
-    if (k == T) {
-      sel = r < need;
-      ++r;
-    }
-    if (sel) {
-      if (pos < K) {
-        trow[pos] = i;
-        p.work_blk[(int64_t)(item0 + pos / C) * C + pos % C] = i;
+    // ---- selection bitmap (ballots), ties resolved in index order ----
+    for (int j = 0; j * kPlanThreads < nb; ++j) {
+      const int i = j * kPlanThreads + tid;
+      const bool valid = i < nb;
+      const uint32_t k = valid ? (K < nb ? (SMEM ? keys[i] : make_key(i)) : 1u) : 0u;
+      const uint32_t bgt = __ballot_sync(0xffffffffu, valid && k > T);
+      const uint32_t beq = __ballot_sync(0xffffffffu, valid && k == T);
+      if (lane == 0) {
+        wsel[j * 32 + warp] = bgt;
+        weq[j * 32 + warp] = beq;
       }
-      ++pos;
     }
+    __syncthreads();
+    const int wpt = ceil_div(nw, kPlanThreads);  // words per thread (consecutive)
+    const int w0 = imin(tid * wpt, nw), w1 = imin(w0 + wpt, nw);
+    int n_eq = 0;
+    for (int wi = w0; wi < w1; ++wi) n_eq += __popc(weq[wi]);
+    int eq_before = block_exclusive_scan(n_eq, scan_scratch);
+    int n_sel = 0;
+    for (int wi = w0; wi < w1; ++wi) {
+      uint32_t e = weq[wi];
+      const int take = imax(0, imin(__popc(e), need - eq_before));
+      eq_before += __popc(e);
+      uint32_t low = 0;
+      for (int t = 0; t < take; ++t) {
+        low |= e & (0u - e);
+        e &= e - 1u;
+      }
+      const uint32_t s = wsel[wi] | low;
+      wsel[wi] = s;
+      n_sel += __popc(s);
+    }
+    int pos = block_exclusive_scan(n_sel, scan_scratch);
+    int* trow = p.block_table + (int64_t)row * p.table_width;
+    uint32_t* brow = p.bitmap + (int64_t)row * p.bm_words;
+    for (int wi = w0; wi < w1; ++wi) {
+      uint32_t s = wsel[wi];
+      brow[wi] = s;
+      while (s) {
+        const int bit = __ffs(s) - 1;
+        s &= s - 1u;
+        if (pos < p.table_width) trow[pos] = wi * 32 + bit;
+        ++pos;
+      }
+    }
+    if (tid == 0) p.sel_lens[row] = nb > 0 ? K : 0;
+    __syncthreads();  // shared buffers are reused by the next round
   }
-  const int n_items = ceil_div(K, C);
-  for (int j = tid; j < n_items; j += kSelectThreads)
-    p.work_hdr[item0 + j] = make_int4(b, h, item0, K);
   pdl_launch_dependents();
 }
 
-cudaError_t launch_budget(const BudgetParams& p, cudaStream_t stream) {
-  dim3 grid(p.Hq, p.B);
-  budget_kernel<<<grid, kBudgetThreads, 0, stream>>>(p);
-  return cudaGetLastError();
+size_t plan_smem_bytes(int nb_max) {
+  const int nw_alloc = (ceil_div(imax(nb_max, 1), 32) + 31) / 32 * 32;
+  const bool smem_keys = nb_max <= kPlanSmemMaxKeys;
+  return (size_t)(smem_keys ? nw_alloc * 32 : 0) * 4 + (size_t)2 * nw_alloc * 4;
 }
 
-cudaError_t select_kernels_init() {
-  return cudaFuncSetAttribute(select_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              kSelectSmemMaxKeys * (int)sizeof(uint32_t));
+cudaError_t plan_kernels_init() {
+  cudaError_t e = cudaFuncSetAttribute(plan_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)plan_smem_bytes(kPlanSmemMaxKeys));
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(plan_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              (int)plan_smem_bytes(kPlanMaxBlocks));
 }
 
-cudaError_t launch_select(const SelectParams& p, int nb_max, cudaStream_t stream) {
-  dim3 grid(p.Hq, p.B);
-  if (nb_max <= kSelectSmemMaxKeys) {
-    select_kernel<true><<<grid, kSelectThreads, (size_t)imax(nb_max, 1) * sizeof(uint32_t), stream>>>(p);
-  } else {
-    select_kernel<false><<<grid, kSelectThreads, 0, stream>>>(p);
-  }
-  return cudaGetLastError();
+int plan_ctas_per_sm(int nb_max) {
+  int n = 0;
+  const size_t smem = plan_smem_bytes(nb_max);
+  if (nb_max <= kPlanSmemMaxKeys)
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, plan_kernel<true>, kPlanThreads, smem);
+  else
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, plan_kernel<false>, kPlanThreads, smem);
+  return n;
+}
+
+cudaError_t launch_plan(const PlanParams& p, int nb_max, int grid, cudaStream_t st,
+                        const LaunchOpts& o) {
+  const size_t smem = plan_smem_bytes(nb_max);
+  if (nb_max <= kPlanSmemMaxKeys)
+    return launch_ex(plan_kernel<true>, dim3(grid), dim3(kPlanThreads), smem, st, o, p);
+  return launch_ex(plan_kernel<false>, dim3(grid), dim3(kPlanThreads), smem, st, o, p);
 }
 
 }  // namespace adakv

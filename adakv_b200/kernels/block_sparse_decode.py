@@ -69,7 +69,7 @@ def block_sparse_decode_batched(q, k_cache, v_cache, block_table, sel_lens, bloc
     nbytes = L.adakv_attend_workspace_bytes(geo, width)
     if nbytes == 0:
         _lib.check(_lib.ERR_INVALID)
-    ws = _lib.workspace(nbytes, q.device)
+    ws = _lib.workspace(nbytes, q.device, "attend")
     qv, kv, vv, ov = _lib.view4(q), _lib.view4(k_cache), _lib.view4(v_cache), _lib.view4(out)
     with torch.cuda.device(q.device):
         _lib.check(L.adakv_attend(geo, qv, kv, vv, bt.data_ptr(), width, sl.data_ptr(),

@@ -9,9 +9,10 @@ synthetic K/V/q with planted retrieval blocks (even KV heads) and recency-biased
 local heads (odd KV heads).  The headline is the 131072-token context; 32768 and
 65536 are reported beside it.
 
-One step = append one token (in-place K/V write + trailing-centroid refresh),
-centroid estimator, entropy budget, top-k selection, ragged split-KV attention:
-5 kernels, captured once in a CUDA graph and replayed.  Each step gets a fresh
+One step = append one token (in-place K/V write + trailing-centroid refresh,
+fused into the estimator), centroid estimator, entropy budget + top-k
+selection, ragged split-KV attention over the GQA union: 3 kernels chained
+with programmatic dependent launch, captured once in a CUDA graph and replayed.  Each step gets a fresh
 query (a pool of perturbed queries) and L2 is flushed (256 MB write) between
 steps, outside the timed events.
 
@@ -41,6 +42,7 @@ METRIC = ("µs per decode attention step at 32K/128K/1M ctx; achieved HBM GB/s v
           "roofline")
 CFG = dict(Hq=32, Hkv=8, D=128, bs=16, avg=64, k_min=2, k_max=512, sink=1, local=4, c_min=1)
 HEADLINE_S = 131072
+KERNELS_PER_STEP = 3
 L2_FLUSH_BYTES = 256 << 20
 
 
@@ -153,8 +155,7 @@ def run_ours(S, steps, warmup, seed, device, pool=16, e2e_steps=None):
     q_buf, kt_buf, vt_buf = q_pool[0].clone(), kt_pool[0].clone(), vt_pool[0].clone()
 
     def step():
-        dec.append(kt_buf, vt_buf, advance=False)
-        dec.step(q_buf)
+        dec.step(q_buf, k_new=kt_buf, v_new=vt_buf, advance=False)
 
     # algorithmic bytes per step, averaged over the query pool (outside timing)
     nbytes = []
@@ -209,8 +210,7 @@ def run_ours(S, steps, warmup, seed, device, pool=16, e2e_steps=None):
         qd.copy_(q_h[j], non_blocking=True)
         ktd.copy_(kt_h[j], non_blocking=True)
         vtd.copy_(vt_h[j], non_blocking=True)
-        dec.append(ktd, vtd, advance=False)
-        out = dec.step(qd)
+        out = dec.step(qd, k_new=ktd, v_new=vtd, advance=False)
         out_h.copy_(out, non_blocking=True)
 
     n_e2e = e2e_steps or min(steps, 1000)
@@ -376,17 +376,17 @@ def main():
             "config": {"workload": workload_name(headline),
                        "parallelism": f"replicas x{world} (batch-1 per GPU, no collective)",
                        "l2": "flushed between steps (256 MB write, outside the timed events)",
-                       "timing": "CUDA events per step around one CUDA-graph replay of the 5 kernels"},
+                       "timing": "CUDA events per step around one CUDA-graph replay of the 3 kernels"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": None,
-                         "scope": "whole decode step (all 5 kernels); bytes = fp32 centroid "
+                         "scope": "whole decode step (all 3 kernels); bytes = fp32 centroid "
                                   "table + union of selected K/V blocks per KV head + append",
                          "peak_source": "MEASURED_PEAKS.json hbm_gbs" if peaks else "fallback"},
             "cpu_baseline": cpu,
             "e2e": {"value": r["e2e_us"], "unit": "us", "h2d_bytes_per_step": r["h2d"],
                     "d2h_bytes_per_step": r["d2h"],
-                    "path": "BatchedDecoder.append + .step (C ABI) with pinned host q/k/v in, out back"},
-            "gpu_launches": 5 * args.steps,
+                    "path": "BatchedDecoder.step with the new token (C ABI adakv_decode_step), pinned host q/k/v in, out back"},
+            "gpu_launches": KERNELS_PER_STEP * args.steps,
             "clocks": r["clocks"],
             "contexts": ctx,
         }

@@ -18,7 +18,8 @@
  *   - Pointers are device pointers unless stated otherwise.  Nothing here
  *     allocates device memory: scratch lives in a caller-provided workspace
  *     (size from adakv_*_workspace_bytes, zero-filled once before first use;
- *     the kernels leave its counters at zero again after every call).
+ *     it keeps no state a later call depends on beyond a call counter).
+ *     Calls that share a workspace must be ordered on one stream.
  *   - All work is enqueued on `stream` (a cudaStream_t passed as void*); no
  *     function synchronises the host except adakv_read_status.
  *   - Tensors are [batch, heads, tokens, head_dim] views described by
@@ -164,12 +165,17 @@ int adakv_attend(const adakv_geometry* geo, const adakv_view* q, const adakv_vie
                  const int32_t* sel_lens, const int32_t* seq_lens, float sm_scale,
                  const adakv_view* out, void* workspace, size_t workspace_bytes, void* stream);
 
-/* adakv_plan + attention over its selection, with no host synchronisation
- * in between (adakv/attention.py:250-268, adakv/runtime.py:85-112).
+/* One full decode step with no host synchronisation anywhere
+ * (adakv/attention.py:250-268, adakv/runtime.py:85-112, adakv/runtime.py:43-60):
+ * optionally append n_new tokens per sequence (k_new / v_new [B, Hkv, n_new, D];
+ * n_new = 0 and NULL views to skip; seq_lens[b] is the length AFTER the append)
+ * into k / v in place with the touched centroids refreshed, then adakv_plan,
+ * then attention of every query head over its selection, written to out.
  * The workspace is sized by adakv_plan_workspace_bytes. */
 int adakv_decode_step(const adakv_geometry* geo, const adakv_select_params* sp,
                       const adakv_view* q, const adakv_view* k, const adakv_view* v,
-                      const float* centroid, const int32_t* seq_lens, float sm_scale,
+                      const adakv_view* k_new, const adakv_view* v_new, int32_t n_new,
+                      float* centroid, const int32_t* seq_lens, float sm_scale,
                       int32_t* block_table, int32_t table_width, int32_t* sel_lens,
                       const adakv_view* out, void* workspace, size_t workspace_bytes,
                       void* stream);

@@ -242,7 +242,7 @@ def test_attend_flags_bad_block_ids():
     out = block_sparse_decode(q, K, V, torch.from_numpy(table).cuda(), torch.from_numpy(lens).cuda(),
                               bs)
     torch.cuda.synchronize()
-    ws = _lib.workspace(0, q.device)
+    ws = _lib.workspace(0, q.device, "attend")
     assert _lib.read_status(ws) & _lib.ST_BAD_BLOCK_ID
     # the valid entries are still attended
     good = np.array([[0, 1, 2, 3], [0, 1, 2, 2], [3, 2, 0, 0], [1, 1, 1, 1]], dtype=np.int32)
@@ -376,3 +376,33 @@ def test_budget_trace_and_recall_instruments():
     A.clear_recall_target()
     assert len(tr) == 3 and all(t > 0 for t in tr)
     assert r == 1.0  # the sink block is always covered
+
+
+def test_fused_append_step_equals_separate_append():
+    """The step with new tokens (append fused into the estimator) must equal a
+    stand-alone append followed by a plain step, bit for bit."""
+    _need_cuda()
+    lens = [5000, 3001]
+    case = make_decode_case(60, 2, 32, 8, 128, lens, 16, "bf16")
+    dec_a, q = _decoder(case, 32, 8, 128, avg=32, k_max=256, capacity=5100)
+    dec_b, _ = _decoder(case, 32, 8, 128, avg=32, k_max=256, capacity=5100)
+    gen = torch.Generator(device="cuda").manual_seed(3)
+    for step in range(6):
+        n = 3 if step == 2 else 1
+        kt = torch.randn((2, 8, n, 128), device="cuda", generator=gen).to(torch.bfloat16)
+        vt = torch.randn((2, 8, n, 128), device="cuda", generator=gen).to(torch.bfloat16)
+        qs = (q.float() + 0.3 * torch.randn(q.shape, device="cuda", generator=gen)).to(torch.bfloat16)
+        out_a = dec_a.step(qs, k_new=kt, v_new=vt).clone()
+        dec_b.append(kt, vt)
+        out_b = dec_b.step(qs).clone()
+        assert torch.equal(out_a, out_b), f"step {step}"
+        assert torch.equal(dec_a.centroid, dec_b.centroid)
+        for x, y in zip(dec_a.selected_sets(), dec_b.selected_sets()):
+            np.testing.assert_array_equal(x, y)
+    S = dec_a.host_seq_lens
+    for b in range(2):
+        assert torch.equal(dec_a.k[b, :, :S[b]], dec_b.k[b, :, :S[b]])
+        assert torch.equal(dec_a.v[b, :, :S[b]], dec_b.v[b, :, :S[b]])
+        ref = O.build_centroids(dec_a.k[b, :, :S[b]].float().cpu().numpy(), 16)
+        np.testing.assert_array_equal(dec_a.centroid[b, :, :ref.shape[1]].cpu().numpy(), ref)
+    assert dec_a.status() == 0 and dec_b.status() == 0
