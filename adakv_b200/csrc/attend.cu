@@ -11,8 +11,9 @@
 // selected K/V block is read from HBM exactly once for the whole group (the
 // split-KV axis).  Each CTA gathers its blocks with 16-byte cp.async copies
 // (zero-fill past seq_len) into a double-buffered shared-memory ring, and warp
-// h of the CTA runs the online softmax of query head h over the blocks whose
-// head bit is set: a token row is spread over D*sizeof(T)/16 lanes, dot products
+// group of the CTA (1-4 warps per query head) runs the online softmax of one
+// query head over the blocks whose head bit is set, round-robin between the
+// head's warps: a token row is spread over D*sizeof(T)/16 lanes, dot products
 // finish with xor shuffles, the lane keeps its 16-byte slice of the output.
 // The per-CTA partials (m, l, o) are merged across the cluster through
 // distributed shared memory -- no global scratch, no atomics, no second kernel.
@@ -21,6 +22,9 @@
 // (bs * D * sizeof(T) * 2 bytes per block) plus the selection bitmaps, q and out.
 #include <cooperative_groups.h>
 
+#include <type_traits>
+
+#include "attend_mma.cuh"
 #include "kernels.h"
 
 namespace adakv {
@@ -35,32 +39,49 @@ __device__ __forceinline__ void cp_async_wait_one() {
 
 // shared-memory carve-up of one attend CTA (host and device agree on it)
 struct AttendSmem {
-  size_t kv, hw, list, mask, part, total;
+  size_t kv, hw, uw, list, mask, wpart, part, total;
 };
 
-__host__ __device__ inline AttendSmem attend_smem_layout(int elt, int D, int BS, int nbt, int g,
-                                                         int nw_max, int slice_cap) {
-  auto al = [](size_t x) { return (x + 15) / 16 * 16; };
+// Warps of one CTA.  Tensor-core path: every warp computes all query rows of a
+// block, so warps split the blocks (<= 64 / g warps keeps the per-warp
+// partials small).  CUDA-core path: 1-4 warps per query head.
+__host__ __device__ inline int attend_warps(bool mma, int g) {
+  if (mma) {
+    int w = 64 / g;
+    return w > 16 ? 16 : (w < 4 ? 4 : w);
+  }
+  int wph = 16 / g;
+  wph = wph < 1 ? 1 : (wph > 4 ? 4 : wph);
+  return g * wph;
+}
+
+__host__ __device__ inline AttendSmem attend_smem_layout(int elt, int D, int BS, int nslot, int g,
+                                                         int nw_max, int slice_cap, bool mma) {
+  auto al = [](size_t x) { return (x + 127) / 128 * 128; };
+  const int nwarps = attend_warps(mma, g);
+  const int prow = mma ? g : 1;  // per-warp partial rows
   AttendSmem s;
   s.kv = 0;
-  s.hw = s.kv + al((size_t)2 * 2 * nbt * BS * D * elt);
-  s.list = s.hw + al((size_t)g * nw_max * 4);
+  s.hw = s.kv + al((size_t)2 * nslot * BS * D * elt);
+  s.uw = s.hw + al((size_t)g * nw_max * 4);
+  s.list = s.uw + al((size_t)nw_max * 4);
   s.mask = s.list + al((size_t)slice_cap * 4);
-  s.part = s.mask + al((size_t)slice_cap * 4);
+  s.wpart = s.mask + al((size_t)slice_cap * 4);
+  s.part = s.wpart + al((size_t)nwarps * prow * (D + 2) * 4);
   s.total = s.part + al((size_t)(32 + g * D) * 4);
   return s;
 }
 
-template <typename T, int D, int BS>
+template <typename T, int D, int BS, bool MMA>
 __global__ void __launch_bounds__(kAttendMaxThreads) attend_kernel(AttendParams p) {
   constexpr int VEC = 16 / sizeof(T);       // elements per 16-byte chunk
-  constexpr int LPT = D / VEC;              // lanes per token row
+  constexpr int LPT = D / VEC;              // lanes per token row (CUDA-core path)
   constexpr int TPP = 32 / LPT;             // token rows per warp pass
   constexpr int PASSES = BS / TPP;
   constexpr int ROWC = D / VEC;             // 16-byte chunks per token row
   constexpr int BLK = BS * D;               // elements of one K (or V) block
   static_assert(LPT <= 32 && BS % TPP == 0, "unsupported tile shape");
-  extern __shared__ __align__(16) unsigned char smem[];
+  extern __shared__ __align__(128) unsigned char smem[];
   __shared__ int scan_scratch[33];
 
   cg::cluster_group cl = cg::this_cluster();
@@ -68,14 +89,17 @@ __global__ void __launch_bounds__(kAttendMaxThreads) attend_kernel(AttendParams 
   const int CL = (int)cl.num_blocks();
   const int kvh = blockIdx.y, b = blockIdx.z;
   const int nthr = blockDim.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int g = p.g, NBT = p.nbt;
-  const AttendSmem L = attend_smem_layout(sizeof(T), D, BS, NBT, g, p.nw_max, p.slice_cap);
-  T* kbuf = reinterpret_cast<T*>(smem + L.kv);                 // [2][NBT][BS][D]
-  T* vbuf = kbuf + (size_t)2 * NBT * BLK;
+  const int nwarps = nthr >> 5;
+  const int g = p.g, NSLOT = p.nbt;
+  const AttendSmem L = attend_smem_layout(sizeof(T), D, BS, NSLOT, g, p.nw_max, p.slice_cap, MMA);
+  T* kbuf = reinterpret_cast<T*>(smem + L.kv);                 // [NSLOT][BS][D]
+  T* vbuf = kbuf + (size_t)NSLOT * BLK;                        // [NSLOT][BS][D]
   uint32_t* hw = reinterpret_cast<uint32_t*>(smem + L.hw);     // [g][nw_max] head words
+  uint32_t* uw = reinterpret_cast<uint32_t*>(smem + L.uw);     // [nw_max] union words
   int* list = reinterpret_cast<int*>(smem + L.list);           // [slice_cap] block ids
   uint32_t* lmask = reinterpret_cast<uint32_t*>(smem + L.mask);  // [slice_cap] head bits
-  float* pm = reinterpret_cast<float*>(smem + L.part);         // [16] running max per head
+  float* wpart = reinterpret_cast<float*>(smem + L.wpart);     // per-warp partials
+  float* pm = reinterpret_cast<float*>(smem + L.part);         // [16] CTA running max per head
   float* pl = pm + 16;                                         // [16] denominators
   float* po = pl + 16;                                         // [g][D] numerators
 
@@ -87,170 +111,291 @@ __global__ void __launch_bounds__(kAttendMaxThreads) attend_kernel(AttendParams 
   const int row0 = b * p.Hq + kvh * g;
 
   // ---- the group's selection bitmaps and their union ----
-  for (int idx = tid; idx < g * nw; idx += nthr) {
-    const int hh = idx / nw, w = idx - hh * nw;
-    hw[hh * p.nw_max + w] = p.bitmap[(int64_t)(row0 + hh) * p.bm_words + w];
+  for (int w = tid; w < nw; w += nthr) {
+    uint32_t u = 0;
+    for (int hh = 0; hh < g; ++hh) {
+      const uint32_t x = p.bitmap[(int64_t)(row0 + hh) * p.bm_words + w];
+      hw[hh * p.nw_max + w] = x;
+      u |= x;
+    }
+    uw[w] = u;
   }
   __syncthreads();
-  auto uni = [&](int w) -> uint32_t {
-    uint32_t u = 0;
-    for (int hh = 0; hh < g; ++hh) u |= hw[hh * p.nw_max + w];
-    return u;
-  };
   const int wpt = ceil_div(nw, nthr);
   const int w0 = imin(tid * wpt, nw), w1 = imin(w0 + wpt, nw);
   int cnt = 0;
-  for (int w = w0; w < w1; ++w) cnt += __popc(uni(w));
+  for (int w = w0; w < w1; ++w) cnt += __popc(uw[w]);
   const int before = block_exclusive_scan(cnt, scan_scratch);
   const int U = scan_scratch[32];
   const int lo = (int)((int64_t)U * rank / CL), hi = (int)((int64_t)U * (rank + 1) / CL);
-  int rk = before;
-  for (int w = w0; w < w1 && rk < hi; ++w) {
-    uint32_t u = uni(w);
-    while (u && rk < hi) {
-      const int bit = __ffs(u) - 1;
-      u &= u - 1u;
-      if (rk >= lo) {
-        uint32_t m = 0;
-        for (int hh = 0; hh < g; ++hh) m |= ((hw[hh * p.nw_max + w] >> bit) & 1u) << hh;
-        list[rk - lo] = w * 32 + bit;
-        lmask[rk - lo] = m;
+  if (before < hi && before + cnt > lo) {
+    int rk = before;
+    for (int w = w0; w < w1 && rk < hi; ++w) {
+      uint32_t u = uw[w];
+      const int pc = __popc(u);
+      if (rk + pc <= lo) {  // the whole word lies before this CTA's slice
+        rk += pc;
+        continue;
       }
-      ++rk;
+      while (u && rk < hi) {
+        const int bit = __ffs(u) - 1;
+        u &= u - 1u;
+        if (rk >= lo) {
+          uint32_t m = 0;
+          for (int hh = 0; hh < g; ++hh) m |= ((hw[hh * p.nw_max + w] >> bit) & 1u) << hh;
+          list[rk - lo] = w * 32 + bit;
+          lmask[rk - lo] = m;
+        }
+        ++rk;
+      }
     }
   }
   __syncthreads();
   const int n = hi - lo;
 
-  // ---- gather: double-buffered batches of NBT blocks ----
   const T* kbase = static_cast<const T*>(p.k.data) + b * p.k.sb + kvh * p.k.sh;
   const T* vbase = static_cast<const T*>(p.v.data) + b * p.v.sb + kvh * p.v.sh;
-  auto issue = [&](int batch) {
-    const int first = batch * NBT;
-    const int cntb = imin(NBT, n - first);
-    if (cntb > 0) {
-      T* kd = kbuf + (size_t)(batch & 1) * NBT * BLK;
-      T* vd = vbuf + (size_t)(batch & 1) * NBT * BLK;
-      const int chunks = cntb * BS * ROWC;
-      for (int c = tid; c < chunks; c += nthr) {
-        const int slot = c / (BS * ROWC);
-        const int rem = c - slot * (BS * ROWC);
-        const int tok = rem / ROWC, col = rem - tok * ROWC;
-        const int pos = list[first + slot] * BS + tok;
-        const bool valid = pos < S;
-        const int64_t srow = valid ? (int64_t)pos : 0;
-        const size_t off = (size_t)slot * BLK + tok * D + col * VEC;
-        cp_async16(kd + off, kbase + srow * p.k.ss + col * VEC, valid);
-        cp_async16(vd + off, vbase + srow * p.v.ss + col * VEC, valid);
+  const T* qbase = static_cast<const T*>(p.q.data) + b * p.q.sb + (int64_t)kvh * g * p.q.sh;
+
+  // per-path running state
+  MmaAcc<D> acc;
+  uint32_t qa[D / 16][4];
+  float qf[VEC];
+  float m_run = -INFINITY, l_run = 0.f, o[VEC];
+  const int gid = lane >> 2, tig = lane & 3;
+  if constexpr (MMA) {
+#pragma unroll
+    for (int nn = 0; nn < MmaAcc<D>::NT; ++nn)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc.o[nn][e] = 0.f;
+    acc.m[0] = acc.m[1] = -INFINITY;
+    acc.l[0] = acc.l[1] = 0.f;
+    // A fragments of q: rows = query heads of the group (rows >= g are zero)
+#pragma unroll
+    for (int ks = 0; ks < D / 16; ++ks) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int row = gid + (e & 1) * 8;
+        const int col = ks * 16 + (e >> 1) * 8 + tig * 2;
+        qa[ks][e] = row < g ? *reinterpret_cast<const uint32_t*>(qbase + (int64_t)row * p.q.sh + col)
+                            : 0u;
       }
+    }
+  } else {
+    const int WPH = nwarps / g;
+    const int head = warp / WPH;
+    const int d0 = (lane % LPT) * VEC;
+    const uint4 u = *reinterpret_cast<const uint4*>(qbase + (int64_t)head * p.q.sh + d0);
+    Unpack16<T>::run(u, qf);
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) o[e] = 0.f;
+  }
+  const float scale_log2 = p.sm_scale * 1.4426950408889634f;
+
+  // ---- gather + compute in batches of up to NSLOT blocks (one DRAM round trip each) ----
+  int seen = 0;
+  for (int first = 0; first < n; first += NSLOT) {
+    const int cntb = imin(NSLOT, n - first);
+    const int chunks = cntb * BS * ROWC;
+    for (int c = tid; c < chunks; c += nthr) {
+      const int slot = c / (BS * ROWC);
+      const int rem = c - slot * (BS * ROWC);
+      const int tok = rem / ROWC, col = rem - tok * ROWC;
+      const int pos = list[first + slot] * BS + tok;
+      const bool valid = pos < S;
+      const int64_t srow = valid ? (int64_t)pos : 0;
+      const int pcol = MMA ? (col ^ (tok & 7)) : col;  // swizzle for ldmatrix
+      const size_t off = (size_t)slot * BLK + tok * D + pcol * VEC;
+      cp_async16(kbuf + off, kbase + srow * p.k.ss + col * VEC, valid);
+      cp_async16(vbuf + off, vbase + srow * p.v.ss + col * VEC, valid);
     }
     cp_async_commit();
-  };
-  issue(0);
-  issue(1);
-
-  const int d0 = (lane % LPT) * VEC;
-  const int tl = lane / LPT;
-  float qf[VEC];
-  {
-    const uint4 u = *reinterpret_cast<const uint4*>(static_cast<const T*>(p.q.data) + b * p.q.sb +
-                                                    (int64_t)(kvh * g + warp) * p.q.sh + d0);
-    Unpack16<T>::run(u, qf);
-  }
-  float m_run = -INFINITY, l_run = 0.f;
-  float o[VEC];
-#pragma unroll
-  for (int e = 0; e < VEC; ++e) o[e] = 0.f;
-
-  const int nbatches = ceil_div(n, NBT);
-  for (int bi = 0; bi < nbatches; ++bi) {
-    cp_async_wait_one();
+    cp_async_wait_all();
     __syncthreads();
-    const T* kt = kbuf + (size_t)(bi & 1) * NBT * BLK;
-    const T* vt = vbuf + (size_t)(bi & 1) * NBT * BLK;
-    const int first = bi * NBT;
-    const int cntb = imin(NBT, n - first);
-    for (int slot = 0; slot < cntb; ++slot) {
-      if (!((lmask[first + slot] >> warp) & 1u)) continue;  // warp-uniform
-      const int blk = list[first + slot];
-      float sc[PASSES];
-#pragma unroll
-      for (int pp = 0; pp < PASSES; ++pp) {
-        const int tok = pp * TPP + tl;
-        const uint4 u = *reinterpret_cast<const uint4*>(kt + (size_t)slot * BLK + tok * D + d0);
-        float kf[VEC];
-        Unpack16<T>::run(u, kf);
-        float part = 0.f;
-#pragma unroll
-        for (int e = 0; e < VEC; ++e) part = fmaf(qf[e], kf[e], part);
-#pragma unroll
-        for (int off = LPT / 2; off >= 1; off >>= 1) part += __shfl_xor_sync(0xffffffffu, part, off);
-        sc[pp] = (blk * BS + tok < S) ? part * p.sm_scale : -INFINITY;
+    if constexpr (MMA) {
+      for (int slot = warp; slot < cntb; slot += nwarps) {
+        const int blk = list[first + slot];
+        const int tok_valid = imin(BS, S - blk * BS);
+        mma_block<T, D, BS>(acc, qa, smem_addr(kbuf + (size_t)slot * BLK),
+                            smem_addr(vbuf + (size_t)slot * BLK), lmask[first + slot], tok_valid,
+                            scale_log2, lane);
       }
-      float mb = sc[0];
+    } else {
+      const int WPH = nwarps / g;
+      const int head = warp / WPH, sub = warp - head * WPH;
+      const int d0 = (lane % LPT) * VEC;
+      const int tl = lane / LPT;
+      for (int slot = 0; slot < cntb; ++slot) {
+        if (!((lmask[first + slot] >> head) & 1u)) continue;  // warp-uniform
+        if ((seen++ % WPH) != sub) continue;
+        const int blk = list[first + slot];
+        const T* kt = kbuf + (size_t)slot * BLK;
+        const T* vt = vbuf + (size_t)slot * BLK;
+        float sc[PASSES];
 #pragma unroll
-      for (int pp = 1; pp < PASSES; ++pp) mb = fmaxf(mb, sc[pp]);
+        for (int pp = 0; pp < PASSES; ++pp) {
+          const int tok = pp * TPP + tl;
+          const uint4 u = *reinterpret_cast<const uint4*>(kt + tok * D + d0);
+          float kf[VEC];
+          Unpack16<T>::run(u, kf);
+          float part = 0.f;
 #pragma unroll
-      for (int off = LPT; off < 32; off <<= 1) mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, off));
-      const float m_new = fmaxf(m_run, mb);
-      if (m_new == -INFINITY) continue;
-      const float alpha = expf(m_run - m_new);
-      float l_part = 0.f;
+          for (int e = 0; e < VEC; ++e) part = fmaf(qf[e], kf[e], part);
 #pragma unroll
-      for (int e = 0; e < VEC; ++e) o[e] *= alpha;
+          for (int off = LPT / 2; off >= 1; off >>= 1) part += __shfl_xor_sync(0xffffffffu, part, off);
+          sc[pp] = (blk * BS + tok < S) ? part * scale_log2 : -INFINITY;
+        }
+        float mb = sc[0];
 #pragma unroll
-      for (int pp = 0; pp < PASSES; ++pp) {
-        const int tok = pp * TPP + tl;
-        const float pt = expf(sc[pp] - m_new);
-        l_part += pt;
-        const uint4 u = *reinterpret_cast<const uint4*>(vt + (size_t)slot * BLK + tok * D + d0);
-        float vf[VEC];
-        Unpack16<T>::run(u, vf);
+        for (int pp = 1; pp < PASSES; ++pp) mb = fmaxf(mb, sc[pp]);
 #pragma unroll
-        for (int e = 0; e < VEC; ++e) o[e] = fmaf(pt, vf[e], o[e]);
+        for (int off = LPT; off < 32; off <<= 1) mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, off));
+        const float m_new = fmaxf(m_run, mb);
+        if (m_new == -INFINITY) continue;
+        const float alpha = exp2f(m_run - m_new);
+        float l_part = 0.f;
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) o[e] *= alpha;
+#pragma unroll
+        for (int pp = 0; pp < PASSES; ++pp) {
+          const int tok = pp * TPP + tl;
+          const float pt = exp2f(sc[pp] - m_new);
+          l_part += pt;
+          const uint4 u = *reinterpret_cast<const uint4*>(vt + tok * D + d0);
+          float vf[VEC];
+          Unpack16<T>::run(u, vf);
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) o[e] = fmaf(pt, vf[e], o[e]);
+        }
+        l_run = l_run * alpha + l_part;
+        m_run = m_new;
       }
-      l_run = l_run * alpha + l_part;
-      m_run = m_new;
     }
-    __syncthreads();  // the buffer is refilled next
-    issue(bi + 2);
+    __syncthreads();  // the slots are refilled by the next batch
   }
-  cp_async_wait_all();
 
-  // ---- per-CTA partial of each head ----
+  // ---- warp partials -> CTA partial of each head (max in log2 units) ----
+  if constexpr (MMA) {
+    float l0 = acc.l[0], l1 = acc.l[1];
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+    float* mine = wpart + warp * g * (D + 2);  // [g][D + 2] = m, l, o[D]
 #pragma unroll
-  for (int off = LPT; off < 32; off <<= 1) {
-    l_run += __shfl_xor_sync(0xffffffffu, l_run, off);
+    for (int half = 0; half < 2; ++half) {
+      const int row = gid + half * 8;
+      if (row < g) {
+        float* rp = mine + row * (D + 2);
+        if (tig == 0) {
+          rp[0] = acc.m[half];
+          rp[1] = half ? l1 : l0;
+        }
 #pragma unroll
-    for (int e = 0; e < VEC; ++e) o[e] += __shfl_xor_sync(0xffffffffu, o[e], off);
-  }
-  if (lane < LPT) {
+        for (int nn = 0; nn < MmaAcc<D>::NT; ++nn) {
+          rp[2 + nn * 8 + tig * 2] = acc.o[nn][half * 2];
+          rp[2 + nn * 8 + tig * 2 + 1] = acc.o[nn][half * 2 + 1];
+        }
+      }
+    }
+    __syncthreads();
+    for (int idx = tid; idx < g * D; idx += nthr) {
+      const int hh = idx / D, d = idx - hh * D;
+      float M = -INFINITY;
+      for (int w = 0; w < nwarps; ++w) M = fmaxf(M, wpart[(w * g + hh) * (D + 2)]);
+      float Ls = 0.f, O = 0.f;
+      if (M != -INFINITY) {
+        for (int w = 0; w < nwarps; ++w) {
+          const float* rp = wpart + (w * g + hh) * (D + 2);
+          const float f = (rp[0] == -INFINITY) ? 0.f : exp2f(rp[0] - M);
+          Ls += rp[1] * f;
+          O += rp[2 + d] * f;
+        }
+      }
+      po[hh * D + d] = O;
+      if (d == 0) {
+        pm[hh] = M;
+        pl[hh] = Ls;
+      }
+    }
+  } else {
 #pragma unroll
-    for (int e = 0; e < VEC; ++e) po[warp * D + d0 + e] = o[e];
-  }
-  if (lane == 0) {
-    pm[warp] = m_run;
-    pl[warp] = l_run;
+    for (int off = LPT; off < 32; off <<= 1) {
+      l_run += __shfl_xor_sync(0xffffffffu, l_run, off);
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) o[e] += __shfl_xor_sync(0xffffffffu, o[e], off);
+    }
+    const int d0 = (lane % LPT) * VEC;
+    float* mine = wpart + warp * (D + 2);
+    if (lane < LPT) {
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) mine[2 + d0 + e] = o[e];
+    }
+    if (lane == 0) {
+      mine[0] = m_run;
+      mine[1] = l_run;
+    }
+    __syncthreads();
+    const int WPH = nwarps / g;
+    for (int idx = tid; idx < g * D; idx += nthr) {
+      const int hh = idx / D, d = idx - hh * D;
+      const float* wp = wpart + hh * WPH * (D + 2);
+      float M = -INFINITY;
+      for (int w = 0; w < WPH; ++w) M = fmaxf(M, wp[w * (D + 2)]);
+      float Ls = 0.f, O = 0.f;
+      if (M != -INFINITY) {
+        for (int w = 0; w < WPH; ++w) {
+          const float mw = wp[w * (D + 2)];
+          const float f = (mw == -INFINITY) ? 0.f : exp2f(mw - M);
+          Ls += wp[w * (D + 2) + 1] * f;
+          O += wp[w * (D + 2) + 2 + d] * f;
+        }
+      }
+      po[hh * D + d] = O;
+      if (d == 0) {
+        pm[hh] = M;
+        pl[hh] = Ls;
+      }
+    }
   }
   cl.sync();
 
   // ---- cluster merge: CTA `rank` finalises heads rank, rank + CL, ... ----
+  constexpr int kMaxCl = 16;
   for (int hh = rank; hh < g; hh += CL) {
+    float mc[kMaxCl], lc[kMaxCl];
+#pragma unroll
+    for (int c = 0; c < kMaxCl; ++c) {
+      if (c < CL) {
+        mc[c] = *cl.map_shared_rank(&pm[hh], c);
+        lc[c] = *cl.map_shared_rank(&pl[hh], c);
+      }
+    }
     float M = -INFINITY;
-    for (int c = 0; c < CL; ++c) M = fmaxf(M, *cl.map_shared_rank(&pm[hh], c));
+#pragma unroll
+    for (int c = 0; c < kMaxCl; ++c)
+      if (c < CL) M = fmaxf(M, mc[c]);
+    float f[kMaxCl];
+    float Ls = 0.f;
+#pragma unroll
+    for (int c = 0; c < kMaxCl; ++c) {
+      if (c < CL) {
+        f[c] = (M == -INFINITY || mc[c] == -INFINITY) ? 0.f : exp2f(mc[c] - M);
+        Ls += lc[c] * f[c];
+      }
+    }
     T* orow = static_cast<T*>(const_cast<void*>(p.out.data)) + b * p.out.sb +
               (int64_t)(kvh * g + hh) * p.out.sh;
     for (int d = tid; d < D; d += nthr) {
-      float Lsum = 0.f, O = 0.f;
-      if (M != -INFINITY) {
-        for (int c = 0; c < CL; ++c) {
-          const float mc = *cl.map_shared_rank(&pm[hh], c);
-          const float f = (mc == -INFINITY) ? 0.f : expf(mc - M);
-          Lsum += *cl.map_shared_rank(&pl[hh], c) * f;
-          O += *cl.map_shared_rank(&po[hh * D + d], c) * f;
-        }
-      }
-      orow[d] = from_f32<T>(Lsum > 0.f ? O / Lsum : 0.f);
+      float ov[kMaxCl];
+#pragma unroll
+      for (int c = 0; c < kMaxCl; ++c)
+        if (c < CL) ov[c] = *cl.map_shared_rank(&po[hh * D + d], c);
+      float O = 0.f;
+#pragma unroll
+      for (int c = 0; c < kMaxCl; ++c)
+        if (c < CL) O += ov[c] * f[c];
+      orow[d] = from_f32<T>(Ls > 0.f ? O / Ls : 0.f);
     }
   }
   cl.sync();  // keep this CTA's shared memory alive until every reader is done
@@ -294,7 +439,7 @@ __global__ void __launch_bounds__(256) table_bitmap_kernel(TableParams p) {
 template <typename F>
 static cudaError_t for_each_attend(int dtype, int D, int bs, F&& f) {
 #define ADAKV_ATT_CASE(TT, DD, BB) \
-  if (D == DD && bs == BB) return f(attend_kernel<TT, DD, BB>, (int)sizeof(TT));
+  if (D == DD && bs == BB) return f(attend_kernel<TT, DD, BB, !std::is_same<TT, float>::value>, (int)sizeof(TT));
 #define ADAKV_ATT_T(TT) \
   ADAKV_ATT_CASE(TT, 64, 16) ADAKV_ATT_CASE(TT, 64, 32) ADAKV_ATT_CASE(TT, 128, 16) ADAKV_ATT_CASE(TT, 128, 32)
   if (dtype == ADAKV_DTYPE_F32) {
@@ -309,8 +454,14 @@ static cudaError_t for_each_attend(int dtype, int D, int bs, F&& f) {
   return cudaErrorInvalidValue;
 }
 
+bool attend_uses_mma(int dtype) { return dtype != ADAKV_DTYPE_F32; }
+
+int attend_threads(int dtype, int g) { return 32 * attend_warps(attend_uses_mma(dtype), g); }
+
 size_t attend_smem_bytes(int dtype, int D, int bs, int nbt, int g, int nw_max, int slice_cap) {
-  return attend_smem_layout(dtype == ADAKV_DTYPE_F32 ? 4 : 2, D, bs, nbt, g, nw_max, slice_cap).total;
+  return attend_smem_layout(dtype == ADAKV_DTYPE_F32 ? 4 : 2, D, bs, nbt, g, nw_max, slice_cap,
+                            attend_uses_mma(dtype))
+      .total;
 }
 
 cudaError_t attend_kernels_init() {
@@ -329,28 +480,23 @@ cudaError_t attend_kernels_init() {
                               64 * 1024);
 }
 
-int attend_max_cluster(int dtype, int D, int bs, int g, size_t smem) {
-  int best = 1;
+int attend_active_clusters(int dtype, int D, int bs, int g, size_t smem, int cluster) {
+  int n = 0;
   for_each_attend(dtype, D, bs, [&](auto kern, int) {
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(16, 1, 1);
-    cfg.blockDim = dim3(32 * g, 1, 1);
+    cfg.gridDim = dim3(cluster, 1, 1);
+    cfg.blockDim = dim3(attend_threads(dtype, g), 1, 1);
     cfg.dynamicSmemBytes = smem;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 16;
+    attr[0].val.clusterDim.x = cluster;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    int n = 0;
-    cudaError_t e = cudaOccupancyMaxPotentialClusterSize(&n, kern, &cfg);
-    if (e == cudaSuccess && n > 0) best = n;
-    return e;
+    return cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
   });
-  int c = 1;
-  while (c * 2 <= best && c * 2 <= 16) c *= 2;
-  return c;
+  return n;
 }
 
 cudaError_t launch_attend(const AttendParams& p, int dtype, int D, int bs, int cluster,
@@ -359,7 +505,7 @@ cudaError_t launch_attend(const AttendParams& p, int dtype, int D, int bs, int c
   LaunchOpts oc = o;
   oc.cluster_x = (unsigned)cluster;
   return for_each_attend(dtype, D, bs, [&](auto kern, int) {
-    return launch_ex(kern, dim3(cluster, p.Hkv, p.B), dim3(32 * p.g), smem, st, oc, p);
+    return launch_ex(kern, dim3(cluster, p.Hkv, p.B), dim3(attend_threads(dtype, p.g)), smem, st, oc, p);
   });
 }
 

@@ -48,9 +48,8 @@ int fail(int code, const char* fmt, ...) {
 struct DeviceState {
   bool ready = false;
   int num_sms = 0;
-  bool coop_pdl_ok = true;  // cooperative + programmatic launch accepted together
   std::map<int, int> plan_ctas;                    // nb_max -> plan CTAs per SM
-  std::map<std::tuple<int, int, int, int, size_t>, int> clusters;  // attend shape -> cluster
+  std::map<std::tuple<int, int, int, int, size_t>, int> clusters;  // attend shape -> active clusters
 };
 constexpr int kMaxDevices = 64;
 DeviceState g_dev[kMaxDevices];
@@ -237,6 +236,7 @@ int enqueue_plan(const DeviceState* ds, const adakv_geometry* g, const adakv_sel
     ep.n_new = n_new;
   }
   ep.status = status;
+  ep.stages = estimate_stages(g->dtype, g->head_dim, ep.g, g->batch);
   const int64_t chunks = (int64_t)g->batch * g->n_kv_heads * ceil_div(nb_max, kEstRows);
   const int est_grid = (int)std::max<int64_t>(1, std::min<int64_t>(ds->num_sms, chunks));
   LaunchOpts oe;
@@ -260,6 +260,7 @@ int enqueue_plan(const DeviceState* ds, const adakv_geometry* g, const adakv_sel
   pp.bitmap = ws_at<uint32_t>(ws, L.bitmap);
   pp.bm_words = L.bm_words;
   pp.nw_max = ceil_div(nb_max, 32);
+  pp.ecache = plan_ecache(nb_max) ? 1 : 0;
   pp.status = status;
   int per_sm;
   {
@@ -270,23 +271,17 @@ int enqueue_plan(const DeviceState* ds, const adakv_geometry* g, const adakv_sel
     per_sm = it->second;
   }
   const int capacity = ds->num_sms * per_sm;
-  if (capacity < g->n_q_heads)
+  if (std::min(capacity, ds->num_sms) < g->n_q_heads)
     return fail(ADAKV_ERR_UNSUPPORTED, "n_q_heads %d exceeds the co-resident plan CTAs (%d)",
-                g->n_q_heads, capacity);
-  pp.seqs_per_round = std::min(g->batch, capacity / g->n_q_heads);
+                g->n_q_heads, std::min(capacity, ds->num_sms));
+  // The CTAs of a sequence wait on one another (weight exchange): the grid is
+  // capped at one CTA per SM and at the co-resident capacity, so every CTA is
+  // resident once the estimator drains; the exchange is also bounded in time.
+  pp.seqs_per_round = std::max(1, std::min(g->batch, std::min(capacity, ds->num_sms) / g->n_q_heads));
   const int plan_grid = pp.seqs_per_round * g->n_q_heads;
   LaunchOpts op;
-  op.coop = true;
-  op.pdl = pdl && ds->coop_pdl_ok;
-  cudaError_t e = launch_plan(pp, nb_max, plan_grid, st, op);
-  if (e != cudaSuccess && op.pdl) {
-    // some drivers refuse cooperative + programmatic together: drop the overlap
-    (void)cudaGetLastError();
-    const_cast<DeviceState*>(ds)->coop_pdl_ok = false;
-    op.pdl = false;
-    e = launch_plan(pp, nb_max, plan_grid, st, op);
-  }
-  CUDA_TRY(e);
+  op.pdl = pdl;
+  CUDA_TRY(launch_plan(pp, nb_max, plan_grid, st, op));
   return ADAKV_OK;
 }
 
@@ -314,36 +309,63 @@ int enqueue_attend(const DeviceState* ds, const adakv_geometry* g, const adakv_v
   ap.bm_words = L.bm_words;
   ap.nw_max = ceil_div(nb_max, 32);
   ap.status = ws_at<uint32_t>(ws, L.status);
-  // blocks per gather batch: two buffers of K+V tiles within ~96 KB
+  // blocks per gather batch (one DRAM round trip): as many K+V tiles as fit
+  // beside the other shared buffers
   const size_t per_block = (size_t)g->block_size * g->head_dim * elt_size(g->dtype) * 2;
-  ap.nbt = (int)std::max<size_t>(1, std::min<size_t>(8, (96 * 1024) / (2 * per_block)));
-  int cluster = 16;
+  ap.nbt = (int)std::max<size_t>(1, std::min<size_t>(32, (144 * 1024) / per_block));
+  // Largest cluster (most split of each KV head's union) for which every
+  // (sequence, KV head) cluster of the launch is resident at once; a
+  // 16-CTA cluster needs 16 free SMs in one GPC, so fewer fit than SMs allow.
+  const int groups = g->batch * g->n_kv_heads;
+  int cluster = 0;
   size_t smem = 0;
-  for (;;) {
-    ap.slice_cap = ceil_div(nb_max, cluster) + 1;
-    smem = attend_smem_bytes(g->dtype, g->head_dim, g->block_size, ap.nbt, gq, ap.nw_max,
-                             ap.slice_cap);
+  int best_c = 1;
+  size_t best_smem = 0;
+  int best_nbt = ap.nbt;
+  const int nbt0 = ap.nbt;
+  for (int c = 16; c >= 1; c /= 2) {
+    ap.nbt = nbt0;
+    ap.slice_cap = ceil_div(nb_max, c) + 1;
+    smem = attend_smem_bytes(g->dtype, g->head_dim, g->block_size, ap.nbt, gq, ap.nw_max, ap.slice_cap);
     while (smem > kAttendSmemMax && ap.nbt > 1) {
       --ap.nbt;
-      smem = attend_smem_bytes(g->dtype, g->head_dim, g->block_size, ap.nbt, gq, ap.nw_max,
-                               ap.slice_cap);
+      smem = attend_smem_bytes(g->dtype, g->head_dim, g->block_size, ap.nbt, gq, ap.nw_max, ap.slice_cap);
     }
-    if (smem > kAttendSmemMax)
-      return fail(ADAKV_ERR_UNSUPPORTED, "sequence too long for the attend kernel's shared memory");
-    int best;
+    if (smem > kAttendSmemMax) continue;
+    int active;
     {
       std::lock_guard<std::mutex> lock(g_dev_mu);
-      const auto key = std::make_tuple(g->dtype, g->head_dim, g->block_size, gq, smem);
+      const auto key = std::make_tuple(g->dtype, g->head_dim * 64 + g->block_size, gq, c, smem);
       auto it = ds->clusters.find(key);
       if (it == ds->clusters.end())
         it = const_cast<DeviceState*>(ds)
-                 ->clusters.emplace(key, attend_max_cluster(g->dtype, g->head_dim, g->block_size, gq, smem))
+                 ->clusters.emplace(key, attend_active_clusters(g->dtype, g->head_dim, g->block_size,
+                                                                gq, smem, c))
                  .first;
-      best = it->second;
+      active = it->second;
     }
-    if (best >= cluster || cluster == 1) break;
-    cluster = best;
+    if (active < 1) continue;
+    if (cluster == 0) {  // first feasible size is the fallback
+      best_c = c;
+      best_smem = smem;
+      best_nbt = ap.nbt;
+      cluster = c;
+    }
+    if (active >= groups) {
+      best_c = c;
+      best_smem = smem;
+      best_nbt = ap.nbt;
+      cluster = c;
+      break;
+    }
   }
+  if (cluster == 0)
+    return fail(ADAKV_ERR_UNSUPPORTED, "sequence too long for the attend kernel's shared memory");
+  cluster = best_c;
+  smem = best_smem;
+  ap.nbt = best_nbt;
+  ap.slice_cap = ceil_div(nb_max, cluster) + 1;
+  (void)smem;
   LaunchOpts oa;
   oa.pdl = pdl_enabled();
   CUDA_TRY(launch_attend(ap, g->dtype, g->head_dim, g->block_size, cluster, st, oa));

@@ -43,22 +43,33 @@ __device__ __forceinline__ void lds_row(const float* p, float (&c)[E]) {
   }
 }
 
-// E consecutive elements of T -> fp32 (E * sizeof(T) is 4, 8 or 16 bytes)
+// E consecutive elements of T -> fp32 (E * sizeof(T) is 4, 8 or 16 bytes).
+// Pure register arithmetic: taking the address of a local word would push it
+// to local memory and serialise the surrounding loads.
+__device__ __forceinline__ float lo16_f32(uint32_t w, __nv_bfloat16*) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float hi16_f32(uint32_t w, __nv_bfloat16*) { return __uint_as_float(w & 0xFFFF0000u); }
+__device__ __forceinline__ float lo16_f32(uint32_t w, __half*) {
+  return __half2float(__ushort_as_half((unsigned short)(w & 0xFFFFu)));
+}
+__device__ __forceinline__ float hi16_f32(uint32_t w, __half*) {
+  return __half2float(__ushort_as_half((unsigned short)(w >> 16)));
+}
+
 template <typename T, int E>
 __device__ __forceinline__ void load_vec(const T* p, float (&out)[E]) {
   if constexpr (sizeof(T) == 4 && E == 4) {
     const float4 v = *reinterpret_cast<const float4*>(p);
     out[0] = v.x; out[1] = v.y; out[2] = v.z; out[3] = v.w;
+  } else if constexpr (sizeof(T) == 4 && E == 2) {
+    const float2 v = *reinterpret_cast<const float2*>(p);
+    out[0] = v.x; out[1] = v.y;
   } else if constexpr (sizeof(T) == 2 && E == 4) {
     const uint2 u = *reinterpret_cast<const uint2*>(p);
-    const T* t = reinterpret_cast<const T*>(&u);
-#pragma unroll
-    for (int e = 0; e < 4; ++e) out[e] = to_f32(t[e]);
+    out[0] = lo16_f32(u.x, (T*)nullptr); out[1] = hi16_f32(u.x, (T*)nullptr);
+    out[2] = lo16_f32(u.y, (T*)nullptr); out[3] = hi16_f32(u.y, (T*)nullptr);
   } else if constexpr (sizeof(T) == 2 && E == 2) {
     const uint32_t u = *reinterpret_cast<const uint32_t*>(p);
-    const T* t = reinterpret_cast<const T*>(&u);
-    out[0] = to_f32(t[0]);
-    out[1] = to_f32(t[1]);
+    out[0] = lo16_f32(u, (T*)nullptr); out[1] = hi16_f32(u, (T*)nullptr);
   } else {
 #pragma unroll
     for (int e = 0; e < E; ++e) out[e] = to_f32(p[e]);
@@ -67,9 +78,48 @@ __device__ __forceinline__ void load_vec(const T* p, float (&out)[E]) {
 
 template <typename T, int E>
 __device__ __forceinline__ void copy_vec(T* dst, const T* src) {
+  constexpr int BYTES = E * (int)sizeof(T);
+  if constexpr (BYTES == 16) {
+    *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+  } else if constexpr (BYTES == 8) {
+    *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(src);
+  } else if constexpr (BYTES == 4) {
+    *reinterpret_cast<uint32_t*>(dst) = *reinterpret_cast<const uint32_t*>(src);
+  } else {
 #pragma unroll
-  for (int e = 0; e < E; ++e) dst[e] = src[e];
+    for (int e = 0; e < E; ++e) dst[e] = src[e];
+  }
 }
+
+// E elements of T as one raw register word (8 or 16 bytes) and its fp32 unpack
+template <typename T, int E> struct RawVec;
+template <> struct RawVec<float, 4> {
+  using type = float4;
+  __device__ __forceinline__ static void unpack(const float4& v, float (&o)[4]) {
+    o[0] = v.x; o[1] = v.y; o[2] = v.z; o[3] = v.w;
+  }
+};
+template <> struct RawVec<float, 2> {
+  using type = float2;
+  __device__ __forceinline__ static void unpack(const float2& v, float (&o)[2]) { o[0] = v.x; o[1] = v.y; }
+};
+template <typename H> struct RawVec16x4 {
+  using type = uint2;
+  __device__ __forceinline__ static void unpack(const uint2& u, float (&o)[4]) {
+    o[0] = lo16_f32(u.x, (H*)nullptr); o[1] = hi16_f32(u.x, (H*)nullptr);
+    o[2] = lo16_f32(u.y, (H*)nullptr); o[3] = hi16_f32(u.y, (H*)nullptr);
+  }
+};
+template <typename H> struct RawVec16x2 {
+  using type = uint32_t;
+  __device__ __forceinline__ static void unpack(const uint32_t& u, float (&o)[2]) {
+    o[0] = lo16_f32(u, (H*)nullptr); o[1] = hi16_f32(u, (H*)nullptr);
+  }
+};
+template <> struct RawVec<__nv_bfloat16, 4> : RawVec16x4<__nv_bfloat16> {};
+template <> struct RawVec<__half, 4> : RawVec16x4<__half> {};
+template <> struct RawVec<__nv_bfloat16, 2> : RawVec16x2<__nv_bfloat16> {};
+template <> struct RawVec<__half, 2> : RawVec16x2<__half> {};
 
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
@@ -82,58 +132,25 @@ __global__ void __launch_bounds__(kEstThreads, 1) estimate_kernel(EstParams p) {
   constexpr int RPW = kEstRows / kEstConsumerWarps;     // rows per consumer warp (8)
   constexpr int NG = RPW / R;                           // groups per warp
   constexpr int TILE_F = kEstRows * D;                  // floats of centroid rows per stage
-  constexpr int Q_F = (16 * D * (int)sizeof(T) + 15) / 16 * 4;  // up to 16 q rows per stage
-  constexpr int STAGE_F = TILE_F + Q_F;
   static_assert(RPW % R == 0, "rows per warp must be a multiple of the group rows");
-  extern __shared__ __align__(128) float ring[];       // [kEstStages][STAGE_F], then 2x[B+1] ints
-  __shared__ __align__(8) uint64_t full_bar[kEstStages];
-  __shared__ __align__(8) uint64_t empty_bar[kEstStages];
-  __shared__ int scan_scratch[33];
+  extern __shared__ __align__(128) float ring[];       // [stages][stage_f], then 2x[B+1] ints
+  __shared__ __align__(8) uint64_t full_bar[kEstMaxStages];
+  __shared__ __align__(8) uint64_t empty_bar[kEstMaxStages];
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  int* seq_base = reinterpret_cast<int*>(ring + kEstStages * STAGE_F);  // [B+1] first chunk of seq
-  int* seq_cph = seq_base + p.B + 1;                                     // [B] chunks per KV head
+  const int stages = p.stages;
+  const int qrow = D * (int)sizeof(T);                        // bytes of one q row
+  const int stage_f = TILE_F + (p.g * qrow + 15) / 16 * 4;    // floats per stage (16-B multiple)
+  int* seq_base = reinterpret_cast<int*>(ring + stages * stage_f);  // [B+1] first chunk of seq
+  int* seq_cph = seq_base + p.B + 1;                                 // [B] chunks per KV head
 
   if (tid == 0) {
-#pragma unroll
-    for (int s = 0; s < kEstStages; ++s) {
+    for (int s = 0; s < stages; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], kEstConsumerWarps);
     }
   }
-  pdl_wait();
-  if (blockIdx.x == 0 && tid == 0 && p.epoch) atomicAdd(p.epoch, 1u);
-  // clear the plan's weight-exchange tags of this call's rows (the plan kernel
-  // starts after this grid completes, so no stale tag can satisfy its barrier)
-  if (p.slots) {
-    for (int r = blockIdx.x * kEstThreads + tid; r < p.B * p.Hq; r += gridDim.x * kEstThreads)
-      p.slots[r].epoch = 0u;
-  }
-  // per-sequence chunk counts and their exclusive prefix
-  int carry = 0;
-  for (int base = 0; base < p.B; base += kEstThreads) {
-    const int b = base + tid;
-    int cnt = 0;
-    if (b < p.B) {
-      const int S = seq_len_of(p.seq_lens, b, p.max_seq_len);
-      const bool ok = S > 0 && S <= p.max_seq_len;
-      if (!ok && blockIdx.x == 0) report(p.status, ADAKV_ST_BAD_SEQ_LEN);
-      const int cph = ok ? ceil_div(ceil_div(S, p.bs), kEstRows) : 0;
-      seq_cph[b] = cph;
-      cnt = cph * p.Hkv;
-    }
-    const int off = block_exclusive_scan(cnt, scan_scratch);
-    if (b < p.B) seq_base[b] = carry + off;
-    carry += scan_scratch[32];
-    __syncthreads();
-  }
-  if (tid == 0) seq_base[p.B] = carry;
   __syncthreads();
-  pdl_launch_dependents();
-
-  const int total = seq_base[p.B];
-  const int c_begin = (int)((int64_t)total * blockIdx.x / gridDim.x);
-  const int c_end = (int)((int64_t)total * (blockIdx.x + 1) / gridDim.x);
   const bool appending = p.n_new > 0 && p.k_new.data != nullptr;
 
   auto chunk_of = [&](int c, int& b, int& kvh, int& ch) {
@@ -150,13 +167,44 @@ __global__ void __launch_bounds__(kEstThreads, 1) estimate_kernel(EstParams p) {
 
   if (warp == kEstConsumerWarps) {
     // ---------------- producer ----------------
+    // The centroid table and q are inputs of this call (written before it by
+    // kernels that complete first), so the stream starts before
+    // griddepcontrol.wait, overlapping the previous kernel's tail.  Rows this
+    // call's append refreshes are skipped by the consumers, so reading them
+    // early is harmless.
+    int carry = 0;
+    for (int base = 0; base < p.B; base += 32) {  // per-sequence chunk prefix, one warp
+      const int b = base + lane;
+      int cnt = 0;
+      if (b < p.B) {
+        const int S = seq_len_of(p.seq_lens, b, p.max_seq_len);
+        const bool ok = S > 0 && S <= p.max_seq_len;
+        if (!ok && blockIdx.x == 0) report(p.status, ADAKV_ST_BAD_SEQ_LEN);
+        const int cph = ok ? ceil_div(ceil_div(S, p.bs), kEstRows) : 0;
+        seq_cph[b] = cph;
+        cnt = cph * p.Hkv;
+      }
+      int incl = cnt;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      if (b < p.B) seq_base[b] = carry + incl - cnt;
+      carry += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) seq_base[p.B] = carry;
+    named_bar_sync(1, (kEstConsumerWarps + 1) * 32);  // publish the chunk map to the consumers
     if (lane == 0) {
+      const int total = carry;
+      const int c_begin = (int)((int64_t)total * blockIdx.x / gridDim.x);
+      const int c_end = (int)((int64_t)total * (blockIdx.x + 1) / gridDim.x);
       int i = 0;
       for (int c = c_begin; c < c_end; ++c, ++i) {
         int b, kvh, ch;
         chunk_of(c, b, kvh, ch);
-        const int s = i % kEstStages;
-        if (i >= kEstStages && !mbar_wait_bounded(&empty_bar[s], ((i / kEstStages) - 1) & 1)) {
+        const int s = i % stages;
+        if (i >= stages && !mbar_wait_bounded(&empty_bar[s], ((i / stages) - 1) & 1)) {
           report(p.status, ADAKV_ST_WAIT_TIMEOUT);
           break;
         }
@@ -164,9 +212,8 @@ __global__ void __launch_bounds__(kEstThreads, 1) estimate_kernel(EstParams p) {
         const int nb = ceil_div(S, p.bs);
         const int row0 = ch * kEstRows;
         const int nrows = imin(kEstRows, nb - row0);
-        const uint32_t qrow = D * sizeof(T);
-        float* st = ring + s * STAGE_F;
-        mbar_arrive_expect_tx(&full_bar[s], (uint32_t)nrows * D * 4u + (uint32_t)p.g * qrow);
+        float* st = ring + s * stage_f;
+        mbar_arrive_expect_tx(&full_bar[s], (uint32_t)nrows * D * 4u + (uint32_t)(p.g * qrow));
         bulk_g2s(st, p.cent + ((int64_t)(b * p.Hkv + kvh) * p.nb_cap + row0) * D,
                  (uint32_t)nrows * D * 4u, &full_bar[s]);
         const T* qsrc = static_cast<const T*>(p.q.data) + b * p.q.sb + (int64_t)kvh * p.g * p.q.sh;
@@ -175,8 +222,15 @@ __global__ void __launch_bounds__(kEstThreads, 1) estimate_kernel(EstParams p) {
                    &full_bar[s]);
       }
     }
+    pdl_wait();
   } else if (warp == kEstConsumerWarps + 1) {
-    // ---------------- fused append: refresh the touched blocks ----------------
+    // ---------------- fused append + per-call bookkeeping ----------------
+    // Loads of the touched blocks' old tokens and of the new tokens go out
+    // first, ahead of the bulk stream (old tokens were written by calls that
+    // completed before this grid launched); every write waits for the
+    // previous grid, which may still be reading the slots rewritten here.
+    using Raw = typename RawVec<T, E>::type;
+    bool waited = false;
     if (appending) {
       for (int pair = blockIdx.x; pair < p.B * p.Hkv; pair += gridDim.x) {
         const int b = pair / p.Hkv, kvh = pair - b * p.Hkv;
@@ -189,44 +243,44 @@ __global__ void __launch_bounds__(kEstThreads, 1) estimate_kernel(EstParams p) {
         T* vc = static_cast<T*>(const_cast<void*>(p.v.data)) + b * p.v.sb + kvh * p.v.sh + d;
         const T* kn = static_cast<const T*>(p.k_new.data) + b * p.k_new.sb + kvh * p.k_new.sh + d;
         const T* vn = static_cast<const T*>(p.v_new.data) + b * p.v_new.sb + kvh * p.v_new.sh + d;
-        float qr[GP][E];
         const T* qb = static_cast<const T*>(p.q.data) + b * p.q.sb + (int64_t)kvh * p.g * p.q.sh + d;
-#pragma unroll
-        for (int j = 0; j < GP; ++j) {
-          if (j < p.g) {
-            load_vec<T, E>(qb + j * p.q.sh, qr[j]);
-          } else {
-#pragma unroll
-            for (int e = 0; e < E; ++e) qr[j][e] = 0.f;
-          }
-        }
         for (int blk = S_old / p.bs; blk < nb; ++blk) {
           const int t0 = blk * p.bs, t1 = imin(t0 + p.bs, S);
           float acc[E];
 #pragma unroll
           for (int e = 0; e < E; ++e) acc[e] = 0.f;
           for (int base = t0; base < t1; base += 16) {
-            float x[16][E];
+            Raw x[16];
 #pragma unroll
             for (int u = 0; u < 16; ++u) {
               const int t = base + u;
               if (t < t1) {
-                if (t >= S_old) {
-                  const T* src = kn + (int64_t)(t - S_old) * p.k_new.ss;
-                  load_vec<T, E>(src, x[u]);
-                  copy_vec<T, E>(kc + (int64_t)t * p.k.ss, src);
-                  copy_vec<T, E>(vc + (int64_t)t * p.v.ss, vn + (int64_t)(t - S_old) * p.v_new.ss);
-                } else {
-                  load_vec<T, E>(kc + (int64_t)t * p.k.ss, x[u]);
-                }
+                const T* src = (t >= S_old) ? kn + (int64_t)(t - S_old) * p.k_new.ss
+                                            : kc + (int64_t)t * p.k.ss;
+                x[u] = *reinterpret_cast<const Raw*>(src);
+              }
+            }
+            if (!waited) {
+              pdl_wait();
+              waited = true;
+            }
+#pragma unroll
+            for (int u = 0; u < 16; ++u) {
+              const int t = base + u;
+              if (t < t1 && t >= S_old) {
+                *reinterpret_cast<Raw*>(kc + (int64_t)t * p.k.ss) = x[u];
+                *reinterpret_cast<Raw*>(vc + (int64_t)t * p.v.ss) =
+                    *reinterpret_cast<const Raw*>(vn + (int64_t)(t - S_old) * p.v_new.ss);
               }
             }
 #pragma unroll
             for (int u = 0; u < 16; ++u) {
               const int t = base + u;
               if (t < t1) {
+                float xf[E];
+                RawVec<T, E>::unpack(x[u], xf);
 #pragma unroll
-                for (int e = 0; e < E; ++e) acc[e] = (t == t0) ? x[u][e] : __fadd_rn(acc[e], x[u][e]);
+                for (int e = 0; e < E; ++e) acc[e] = (t == t0) ? xf[e] : __fadd_rn(acc[e], xf[e]);
               }
             }
           }
@@ -237,32 +291,42 @@ __global__ void __launch_bounds__(kEstThreads, 1) estimate_kernel(EstParams p) {
           float* crow = p.cent + ((int64_t)(b * p.Hkv + kvh) * p.nb_cap + blk) * D + d;
 #pragma unroll
           for (int e = 0; e < E; ++e) crow[e] = cen[e];
+          for (int j = 0; j < p.g; ++j) {
+            float qv[E];
+            load_vec<T, E>(qb + j * p.q.sh, qv);
+            float part = 0.f;
 #pragma unroll
-          for (int j = 0; j < GP; ++j) {
-            if (j < p.g) {
-              float part = 0.f;
+            for (int e = 0; e < E; ++e) part = fmaf(qv[e], cen[e], part);
 #pragma unroll
-              for (int e = 0; e < E; ++e) part = fmaf(qr[j][e], cen[e], part);
-#pragma unroll
-              for (int o = 16; o; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
-              if (lane == 0)
-                p.scores[(int64_t)(b * p.Hq + kvh * p.g + j) * p.score_stride + blk] = part;
-            }
+            for (int o = 16; o; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+            if (lane == 0)
+              p.scores[(int64_t)(b * p.Hq + kvh * p.g + j) * p.score_stride + blk] = part;
           }
         }
       }
     }
+    if (!waited) pdl_wait();
+    if (blockIdx.x == 0 && lane == 0 && p.epoch) atomicAdd(p.epoch, 1u);
+    // clear the plan's weight-exchange tags of this call's rows (the plan kernel
+    // starts after this grid completes, so no stale tag can satisfy its barrier)
+    if (p.slots) {
+      for (int r = blockIdx.x * 32 + lane; r < p.B * p.Hq; r += gridDim.x * 32) p.slots[r].epoch = 0u;
+    }
   } else {
     // ---------------- consumers ----------------
+    named_bar_sync(1, (kEstConsumerWarps + 1) * 32);  // chunk map written by the producer warp
+    const int total = seq_base[p.B];
+    const int c_begin = (int)((int64_t)total * blockIdx.x / gridDim.x);
+    const int c_end = (int)((int64_t)total * (blockIdx.x + 1) / gridDim.x);
     int i = 0;
     for (int c = c_begin; c < c_end; ++c, ++i) {
-      int b, kvh, ch;
-      chunk_of(c, b, kvh, ch);
-      const int s = i % kEstStages;
-      if (!mbar_wait_bounded(&full_bar[s], (i / kEstStages) & 1)) {
+      const int s = i % stages;
+      if (!mbar_wait_bounded(&full_bar[s], (i / stages) & 1)) {
         if (lane == 0) report(p.status, ADAKV_ST_WAIT_TIMEOUT);
         break;
       }
+      int b, kvh, ch;
+      chunk_of(c, b, kvh, ch);
       const int S = seq_len_of(p.seq_lens, b, p.max_seq_len);
       const int nb = ceil_div(S, p.bs);
       const int row0 = ch * kEstRows;
@@ -270,7 +334,7 @@ __global__ void __launch_bounds__(kEstThreads, 1) estimate_kernel(EstParams p) {
       // rows refreshed by the append warp are scored there
       const int skip_from = appending ? (S - p.n_new) / p.bs - row0 : nrows;
       const int lim = imin(nrows, skip_from);
-      const float* tile = ring + s * STAGE_F;
+      const float* tile = ring + s * stage_f;
       const T* qs = reinterpret_cast<const T*>(tile + TILE_F);
       float qr[GP][E];
 #pragma unroll
@@ -306,13 +370,27 @@ __global__ void __launch_bounds__(kEstThreads, 1) estimate_kernel(EstParams p) {
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty_bar[s]);
     }
+    pdl_wait();  // (no-op for ordering here; keeps every thread's wait uniform)
   }
+  pdl_launch_dependents();
 }
 
-size_t estimate_smem_bytes(int dtype, int D, int B) {
-  const size_t tile = (size_t)kEstRows * D * 4;
-  const size_t q = ((size_t)16 * D * (dtype == ADAKV_DTYPE_F32 ? 4 : 2) + 15) / 16 * 16;
-  return kEstStages * (tile + q) + sizeof(int) * (2 * (size_t)B + 2);
+int estimate_stage_bytes(int dtype, int D, int g) {
+  const int tile = kEstRows * D * 4;
+  const int q = (g * D * (dtype == ADAKV_DTYPE_F32 ? 4 : 2) + 15) / 16 * 16;
+  return tile + q;
+}
+
+int estimate_stages(int dtype, int D, int g, int B) {
+  const size_t fixed = sizeof(int) * (2 * (size_t)B + 2);
+  const size_t room = kEstSmemBudget > fixed ? kEstSmemBudget - fixed : 0;
+  const int st = (int)(room / estimate_stage_bytes(dtype, D, g));
+  return imax(2, imin(kEstMaxStages, st));
+}
+
+size_t estimate_smem_bytes(int dtype, int D, int g, int B) {
+  return (size_t)estimate_stages(dtype, D, g, B) * estimate_stage_bytes(dtype, D, g) +
+         sizeof(int) * (2 * (size_t)B + 2);
 }
 
 template <typename F>
@@ -338,7 +416,7 @@ cudaError_t estimate_kernels_init() {
   for (int dt = 0; dt < 3; ++dt)
     for (int D : {64, 128})
       for (int g : {4, 8, 16}) {
-        const size_t smem = estimate_smem_bytes(dt, D, kEstMaxBatch);
+        const size_t smem = kEstSmemBudget + 1024;
         cudaError_t e = for_each_estimate(dt, D, g, [&](auto kern) {
           return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         });
@@ -350,7 +428,7 @@ cudaError_t estimate_kernels_init() {
 cudaError_t launch_estimate(const EstParams& p, int dtype, int D, int nb_max, int grid,
                             cudaStream_t st, const LaunchOpts& o) {
   (void)nb_max;
-  const size_t smem = estimate_smem_bytes(dtype, D, p.B);
+  const size_t smem = estimate_smem_bytes(dtype, D, p.g, p.B);
   return for_each_estimate(dtype, D, p.g, [&](auto kern) {
     return launch_ex(kern, dim3(grid), dim3(kEstThreads), smem, st, o, p);
   });

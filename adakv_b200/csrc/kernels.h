@@ -32,10 +32,11 @@ struct __align__(16) PlanSlot {
 // ---------------------------------------------------------------------------
 // (b) estimator (+ fused append of the step's new tokens)
 // ---------------------------------------------------------------------------
-constexpr int kEstStages = 4;          // TMA ring depth
+constexpr int kEstMaxStages = 8;       // TMA ring depth limit
+constexpr size_t kEstSmemBudget = 200 * 1024;  // dynamic shared memory of one estimator CTA
 constexpr int kEstConsumerWarps = 8;   // 8 warps x 8 rows = kEstRows
 constexpr int kEstThreads = (kEstConsumerWarps + 2) * 32;  // + producer warp + refresh warp
-constexpr int kEstMaxBatch = 4096;     // sequences per launch (per-sequence chunk prefix in smem)
+constexpr int kEstMaxBatch = 2048;     // sequences per launch (per-sequence chunk prefix in smem)
 
 struct EstParams {
   View q;                 // [B, Hq, D]
@@ -51,6 +52,7 @@ struct EstParams {
   // fused append: n_new > 0 and k_new.data != NULL
   View k, v, k_new, v_new;
   int n_new;
+  int stages;             // ring depth (estimate_stages)
   uint32_t* status;
 };
 
@@ -59,7 +61,8 @@ struct EstParams {
 // ---------------------------------------------------------------------------
 constexpr int kPlanThreads = 1024;
 constexpr int kPlanSmemMaxKeys = 48 * 1024;   // keys staged in smem up to this many blocks
-constexpr int kPlanMaxBlocks = 512 * 1024;    // longest sequence in blocks (bitmap words in smem)  // larger rows are re-read from L2 each pass
+constexpr int kPlanMaxBlocks = 512 * 1024;    // longest sequence in blocks (bitmap words in smem)
+constexpr int kPlanECacheMax = 24 * 1024;     // exp(z - zmax) cached in smem up to this many blocks  // larger rows are re-read from L2 each pass
 
 
 
@@ -78,6 +81,7 @@ struct PlanParams {
   uint32_t* bitmap;         // [B*Hq, bm_words] out, bit j = block j selected
   int bm_words;
   int nw_max;               // ceil(ceil(max_seq_len / bs) / 32): sizes the shared buffers
+  int ecache;               // cache exp(z - zmax) in shared memory (plan_ecache)
   int seqs_per_round;       // grid = seqs_per_round * Hq CTAs
   uint32_t* status;
 };
@@ -171,11 +175,13 @@ cudaError_t launch_table_bitmap(const TableParams& p, cudaStream_t stream, const
 cudaError_t estimate_kernels_init();
 cudaError_t plan_kernels_init();
 cudaError_t attend_kernels_init();
-size_t estimate_smem_bytes(int dtype, int D, int B);
+size_t estimate_smem_bytes(int dtype, int D, int g, int B);
+int estimate_stages(int dtype, int D, int g, int B);
 size_t plan_smem_bytes(int nb_max);
+bool plan_ecache(int nb_max);
 int plan_ctas_per_sm(int nb_max);
-// largest power-of-two cluster size (<= 16) the attend kernel can run with
-int attend_max_cluster(int dtype, int D, int bs, int g, size_t smem);
+// clusters of `cluster` CTAs of the attend kernel that can be resident at once
+int attend_active_clusters(int dtype, int D, int bs, int g, size_t smem, int cluster);
 size_t attend_smem_bytes(int dtype, int D, int bs, int nbt, int g, int nw_max, int slice_cap);
 
 }  // namespace adakv

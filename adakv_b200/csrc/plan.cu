@@ -11,8 +11,9 @@
 //    wall-clock limit, after which the status word records a timeout).  Every
 //    CTA then sums the Hq weights in the same fixed order, so all heads see the
 //    same total, and derives its count with the reference's arithmetic
-//    (budget.py:71-86, selector.py:49-54; half-to-even rounding).  The launch is
-//    cooperative (all CTAs co-resident) and processes whole sequences per round.
+//    (budget.py:71-86, selector.py:49-54; half-to-even rounding).  The grid is
+//    at most one CTA per SM (so all of it is resident once the estimator
+//    drains) and processes whole sequences per round.
 // 4. Top-k: keys are the order-preserving uint32 images of the scores; sink
 //    [0, sink) and local [nb-local, nb) blocks get 0xFFFFFFFF (the reference's
 //    +inf bias, selector.py:44-48).  A 4-pass MSB radix select over shared
@@ -21,6 +22,8 @@
 // 5. Output: warp ballots build the selection bitmap word by word (element
 //    j*1024 + t lands in word j*32 + warp), ties are resolved on the bitmap with
 //    one block scan, and a second scan writes the ascending block table.
+#include <algorithm>
+
 #include "kernels.h"
 
 namespace adakv {
@@ -40,6 +43,18 @@ __device__ __forceinline__ uint32_t score_key(float f) {
   const uint32_t u = __float_as_uint(f);
   if ((u & 0x7FFFFFFFu) > 0x7F800000u) return 0u;
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+constexpr int kPlanILP = 8;     // row elements per thread per tile (independent chains)
+constexpr int kBuckets = 2048;  // bucket-select histogram bins (2 per thread)
+constexpr int kCandCap = 1024;  // members of the boundary bucket ranked exactly
+
+// bucket of a content score: floor((cmx - s) * scale), clamped to the last
+// bucket (which also takes NaN and -inf); non-decreasing as s decreases
+__device__ __forceinline__ int bucket_of(float s, float cmx, float scale) {
+  const float u = __fmul_rn(__fsub_rn(cmx, s), scale);
+  if (!(u < (float)(kBuckets - 1))) return kBuckets - 1;
+  return u <= 0.f ? 0 : (int)u;
 }
 
 __device__ __forceinline__ float block_max1024(float v, float* red) {
@@ -77,18 +92,21 @@ __device__ __forceinline__ double block_sum1024(double v, double* red) {
 template <bool SMEM>
 __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanParams p) {
   extern __shared__ __align__(16) uint32_t sm[];
-  __shared__ uint32_t hist[256];
-  __shared__ int s_digit, s_above;
+  __shared__ uint32_t hist[kBuckets];
+  __shared__ int s_digit, s_above, s_ncand;
   __shared__ int scan_scratch[33];
-  __shared__ float fred[33];
-  __shared__ double dred[33];
+  __shared__ float fred[33], gred[33];
+  __shared__ double dred[33], dred2[33];
   __shared__ double s_sumw;
+  __shared__ int cand_idx[kCandCap];
+  __shared__ uint32_t cand_key[kCandCap];
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   // ballot words are written 32 at a time: round the word count up to 32
   const int nw_alloc = (p.nw_max + 31) / 32 * 32;
   uint32_t* keys = sm;                                        // [nw_alloc * 32] (SMEM only)
-  uint32_t* wsel = sm + (SMEM ? nw_alloc * 32 : 0);           // [nw_alloc]
+  float* ecache = reinterpret_cast<float*>(sm + (SMEM ? nw_alloc * 32 : 0));  // exp(z - zmax)
+  uint32_t* wsel = reinterpret_cast<uint32_t*>(ecache) + (p.ecache ? nw_alloc * 32 : 0);
   uint32_t* weq = wsel + nw_alloc;                            // [nw_alloc]
 
   pdl_wait();
@@ -108,30 +126,112 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanParams p) {
     const float* srow = p.scores + (int64_t)row * p.score_stride;
 
     if (SMEM) {
-#pragma unroll 8
-      for (int i = tid; i < nb; i += kPlanThreads) keys[i] = __float_as_uint(srow[i]);
+      for (int base = 0; base < nb; base += kPlanThreads * kPlanILP) {
+        float v[kPlanILP];
+#pragma unroll
+        for (int r = 0; r < kPlanILP; ++r) {
+          const int i = base + r * kPlanThreads + tid;
+          v[r] = i < nb ? srow[i] : 0.f;
+        }
+#pragma unroll
+        for (int r = 0; r < kPlanILP; ++r) {
+          const int i = base + r * kPlanThreads + tid;
+          if (i < nb) keys[i] = __float_as_uint(v[r]);
+        }
+      }
       __syncthreads();
     }
     auto val = [&](int i) -> float { return SMEM ? __uint_as_float(keys[i]) : srow[i]; };
 
+    const int sink = imin(p.cfg.n_sink, nb), local = imin(p.cfg.n_local, nb);
+    auto forced = [&](int i) -> bool { return i < sink || i >= nb - local; };
+
+    // ---- one pass of row statistics: max (softmax), content max / mean / spread (top-k) ----
+    float mx = -INFINITY, cmx = -INFINITY, csum_f = 0.f, csq_f = 0.f;
+    for (int base = 0; base < nb; base += kPlanThreads * kPlanILP) {
+#pragma unroll
+      for (int r = 0; r < kPlanILP; ++r) {
+        const int i = base + r * kPlanThreads + tid;
+        if (i < nb) {
+          const float v = val(i);
+          mx = fmaxf(mx, v);
+          if (!forced(i)) {
+            cmx = fmaxf(cmx, v);
+            csum_f += v;
+            csq_f = fmaf(v, v, csq_f);
+          }
+        }
+      }
+    }
+    double csum = csum_f, csq = csq_f;
+    {
+      mx = warp_max(mx);
+      cmx = warp_max(cmx);
+      csum = warp_sum(csum);
+      csq = warp_sum(csq);
+      if (lane == 0) {
+        fred[warp] = mx;
+        gred[warp] = cmx;
+        dred[warp] = csum;
+        dred2[warp] = csq;
+      }
+      __syncthreads();
+      if (warp == 0) {
+        float a = warp_max(fred[lane]), c = warp_max(gred[lane]);
+        double x = warp_sum(dred[lane]), y = warp_sum(dred2[lane]);
+        if (lane == 0) {
+          fred[32] = a;
+          gred[32] = c;
+          dred[32] = x;
+          dred2[32] = y;
+        }
+      }
+      __syncthreads();
+      mx = fred[32];
+      cmx = gred[32];
+      csum = dred[32];
+      csq = dred2[32];
+    }
+
     // ---- entropy weight ----
     double w = 0.0;
     if (nb >= 2 && p.cfg.policy == ADAKV_POLICY_ADAPTIVE) {
-      float m = -INFINITY;
-      for (int i = tid; i < nb; i += kPlanThreads) m = fmaxf(m, val(i));
-      m = block_max1024(m, fred);
+      const float m = mx;
       const float Tf = (float)(p.cfg.temperature > 1e-6 ? p.cfg.temperature : 1e-6);
-      const float zmax = __fdiv_rn(m, Tf);  // max(s / T) == max(s) / T (rounding is monotone)
-      double zacc = 0.0;
-      for (int i = tid; i < nb; i += kPlanThreads) zacc += (double)expf(__fdiv_rn(val(i), Tf) - zmax);
-      const float Z = (float)block_sum1024(zacc, dred);
-      double hacc = 0.0;
-      for (int i = tid; i < nb; i += kPlanThreads) {
-        const float e = expf(__fdiv_rn(val(i), Tf) - zmax);
-        const float pi = __fdiv_rn(e, Z);
-        hacc += (double)__fmul_rn(pi, logf(fmaxf(pi, 1e-9f)));
+      const bool unit_t = (Tf == 1.0f);  // s / 1 == s exactly: skip the division
+      const float zmax = unit_t ? m : __fdiv_rn(m, Tf);  // max(s / T) == max(s) / T (monotone rounding)
+      auto ez = [&](int i) -> float {
+        const float z = unit_t ? val(i) : __fdiv_rn(val(i), Tf);
+        return expf(z - zmax);
+      };
+      // per-thread partial sums in float (at most a few dozen terms each), the
+      // cross-thread sums in double
+      float zpart = 0.f;
+      for (int base = 0; base < nb; base += kPlanThreads * kPlanILP) {
+#pragma unroll
+        for (int r = 0; r < kPlanILP; ++r) {
+          const int i = base + r * kPlanThreads + tid;
+          if (i < nb) {
+            const float e = ez(i);
+            if (p.ecache) ecache[i] = e;
+            zpart += e;
+          }
+        }
       }
-      const float hsum = (float)block_sum1024(hacc, dred);
+      const float Z = (float)block_sum1024((double)zpart, dred);
+      float hpart = 0.f;
+      for (int base = 0; base < nb; base += kPlanThreads * kPlanILP) {
+#pragma unroll
+        for (int r = 0; r < kPlanILP; ++r) {
+          const int i = base + r * kPlanThreads + tid;
+          if (i < nb) {
+            const float e = p.ecache ? ecache[i] : ez(i);
+            const float pi = __fdiv_rn(e, Z);
+            hpart += __fmul_rn(pi, logf(fmaxf(pi, 1e-9f)));
+          }
+        }
+      }
+      const float hsum = (float)block_sum1024((double)hpart, dred);
       w = (double)(-hsum) / log((double)imax(nb, 2)) + 1e-6;
     }
 
@@ -161,20 +261,105 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanParams p) {
     __syncthreads();
     const SeqBudget sbud = seq_budget(nb, p.cfg);
     const int K = imin(head_count(sbud, p.cfg, w, s_sumw, p.Hq), p.table_width);
-    const int sink = imin(p.cfg.n_sink, nb), local = imin(p.cfg.n_local, nb);
-    auto make_key = [&](int i) -> uint32_t {
-      return (i < sink || i >= nb - local) ? 0xFFFFFFFFu : score_key(val(i));
-    };
+    const int n_forced = (sink + local >= nb) ? nb : sink + local;
+    const int Kc = K - n_forced;  // content blocks to pick
 
-    // ---- radix select of the K-th largest key ----
+    // ---- top-k ----
+    // Bucket select: content block i goes to bucket floor((cmx - s_i) * scale),
+    // a non-decreasing function of -s_i (correctly rounded subtraction and
+    // multiplication are monotone), so every block of a lower bucket outranks
+    // every block of a higher one.  Buckets span [cmx - range, cmx] with
+    // range = cmx - mean + sd, fine near the k-th score; blocks past the range
+    // share the last bucket.  One histogram pass finds the bucket holding the
+    // Kc-th block; its few members are ranked exactly by (score, lowest index).
+    // A full MSB radix select takes over when the boundary falls in the last
+    // bucket or holds too many members.
+    bool use_radix = false;
+    int jstar = kBuckets, need_b = 0;
+    float scale = 0.f;
+    if (K < nb && Kc > 0) {
+      const double nc = (double)(nb - n_forced);
+      const double mean = csum / nc;
+      const double var = csq / nc - mean * mean;
+      const double sd = var > 0.0 ? sqrt(var) : 0.0;
+      const double range = (double)cmx - mean + sd;
+      use_radix = !(isfinite(cmx) && range > 0.0 && isfinite(range));
+      if (!use_radix) {
+        scale = (float)((double)(kBuckets - 1) / range);
+        for (int t = tid; t < kBuckets; t += kPlanThreads) hist[t] = 0u;
+        __syncthreads();
+        for (int base = 0; base < nb; base += kPlanThreads * kPlanILP) {
+#pragma unroll
+          for (int r = 0; r < kPlanILP; ++r) {
+            const int i = base + r * kPlanThreads + tid;
+            if (i < nb && !forced(i)) {
+              const int bk = bucket_of(val(i), cmx, scale);
+              if (bk < kBuckets - 1) atomicAdd(&hist[bk], 1u);
+            }
+          }
+        }
+        __syncthreads();
+        // find the bucket holding the Kc-th content block (buckets ascend = scores descend)
+        constexpr int BPT = kBuckets / kPlanThreads;
+        uint32_t cb[BPT], tot = 0;
+#pragma unroll
+        for (int e = 0; e < BPT; ++e) {
+          cb[e] = hist[tid * BPT + e];
+          tot += cb[e];
+        }
+        const int before = block_exclusive_scan((int)tot, scan_scratch);
+        if (tid == 0) s_digit = kBuckets - 1;
+        __syncthreads();
+        if (before < Kc && Kc <= before + (int)tot) {
+          int acc = before;
+#pragma unroll
+          for (int e = 0; e < BPT; ++e) {
+            if (acc + (int)cb[e] >= Kc) {
+              s_digit = tid * BPT + e;
+              s_above = acc;
+              break;
+            }
+            acc += (int)cb[e];
+          }
+        }
+        __syncthreads();
+        jstar = s_digit;
+        if (jstar >= kBuckets - 1 || (int)hist[jstar] > kCandCap) {
+          use_radix = true;
+        } else {
+          need_b = Kc - s_above;
+          if (tid == 0) s_ncand = 0;
+          __syncthreads();
+          for (int base = 0; base < nb; base += kPlanThreads * kPlanILP) {
+#pragma unroll
+            for (int r = 0; r < kPlanILP; ++r) {
+              const int i = base + r * kPlanThreads + tid;
+              if (i < nb && !forced(i)) {
+                const float v = val(i);
+                if (bucket_of(v, cmx, scale) == jstar) {
+                  const int slot = atomicAdd(&s_ncand, 1);
+                  cand_idx[slot] = i;
+                  cand_key[slot] = score_key(v);
+                }
+              }
+            }
+          }
+          __syncthreads();
+        }
+      }
+    }
+
     uint32_t T = 0;
-    int need = 0x7FFFFFFF;  // K >= nb: every block is selected
-    if (K < nb) {
+    int need = 0;  // ties at T resolved in index order (radix path only)
+    if (use_radix) {
       if (SMEM) {
-        for (int i = tid; i < nb; i += kPlanThreads) keys[i] = make_key(i);
+        for (int i = tid; i < nb; i += kPlanThreads)
+          keys[i] = forced(i) ? 0xFFFFFFFFu : score_key(__uint_as_float(keys[i]));
         __syncthreads();
       }
-      auto key = [&](int i) -> uint32_t { return SMEM ? keys[i] : make_key(i); };
+      auto key = [&](int i) -> uint32_t {
+        return SMEM ? keys[i] : (forced(i) ? 0xFFFFFFFFu : score_key(srow[i]));
+      };
       uint32_t prefix = 0, pmask = 0;
       int rem = K;
 #pragma unroll 1
@@ -221,39 +406,72 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanParams p) {
       }
       T = prefix;
       need = rem;
-    }
-
-    // ---- selection bitmap (ballots), ties resolved in index order ----
-    for (int j = 0; j * kPlanThreads < nb; ++j) {
-      const int i = j * kPlanThreads + tid;
-      const bool valid = i < nb;
-      const uint32_t k = valid ? (K < nb ? (SMEM ? keys[i] : make_key(i)) : 1u) : 0u;
-      const uint32_t bgt = __ballot_sync(0xffffffffu, valid && k > T);
-      const uint32_t beq = __ballot_sync(0xffffffffu, valid && k == T);
-      if (lane == 0) {
-        wsel[j * 32 + warp] = bgt;
-        weq[j * 32 + warp] = beq;
+      for (int j = 0; j * kPlanThreads < nb; ++j) {
+        const int i = j * kPlanThreads + tid;
+        const bool valid = i < nb;
+        const uint32_t k = valid ? key(i) : 0u;
+        const uint32_t bgt = __ballot_sync(0xffffffffu, valid && k > T);
+        const uint32_t beq = __ballot_sync(0xffffffffu, valid && k == T);
+        if (lane == 0) {
+          wsel[j * 32 + warp] = bgt;
+          weq[j * 32 + warp] = beq;
+        }
+      }
+    } else {
+      // selected: forced blocks, every content block of a bucket above jstar,
+      // and the need_b best members of bucket jstar
+      const bool all = K >= nb;
+      for (int j = 0; j * kPlanThreads < nb; ++j) {
+        const int i = j * kPlanThreads + tid;
+        bool sel = false;
+        if (i < nb) {
+          if (all || forced(i)) sel = true;
+          else if (Kc > 0 && jstar < kBuckets) sel = bucket_of(val(i), cmx, scale) < jstar;
+        }
+        const uint32_t bsel = __ballot_sync(0xffffffffu, sel);
+        if (lane == 0) {
+          wsel[j * 32 + warp] = bsel;
+          weq[j * 32 + warp] = 0u;
+        }
+      }
+      __syncthreads();
+      if (!all && Kc > 0 && jstar < kBuckets) {
+        const int nc = s_ncand;
+        for (int t = tid; t < nc; t += kPlanThreads) {
+          const uint32_t kt = cand_key[t];
+          const int it = cand_idx[t];
+          int rank = 0;
+          for (int c = 0; c < nc; ++c) {
+            const uint32_t kc = cand_key[c];
+            rank += (kc > kt) || (kc == kt && cand_idx[c] < it);
+          }
+          if (rank < need_b) atomicOr(&wsel[it >> 5], 1u << (it & 31));
+        }
       }
     }
     __syncthreads();
     const int wpt = ceil_div(nw, kPlanThreads);  // words per thread (consecutive)
     const int w0 = imin(tid * wpt, nw), w1 = imin(w0 + wpt, nw);
-    int n_eq = 0;
-    for (int wi = w0; wi < w1; ++wi) n_eq += __popc(weq[wi]);
-    int eq_before = block_exclusive_scan(n_eq, scan_scratch);
     int n_sel = 0;
-    for (int wi = w0; wi < w1; ++wi) {
-      uint32_t e = weq[wi];
-      const int take = imax(0, imin(__popc(e), need - eq_before));
-      eq_before += __popc(e);
-      uint32_t low = 0;
-      for (int t = 0; t < take; ++t) {
-        low |= e & (0u - e);
-        e &= e - 1u;
+    if (use_radix) {
+      int n_eq = 0;
+      for (int wi = w0; wi < w1; ++wi) n_eq += __popc(weq[wi]);
+      int eq_before = block_exclusive_scan(n_eq, scan_scratch);
+      for (int wi = w0; wi < w1; ++wi) {
+        uint32_t e = weq[wi];
+        const int take = imax(0, imin(__popc(e), need - eq_before));
+        eq_before += __popc(e);
+        uint32_t low = 0;
+        for (int t = 0; t < take; ++t) {
+          low |= e & (0u - e);
+          e &= e - 1u;
+        }
+        const uint32_t sw = wsel[wi] | low;
+        wsel[wi] = sw;
+        n_sel += __popc(sw);
       }
-      const uint32_t s = wsel[wi] | low;
-      wsel[wi] = s;
-      n_sel += __popc(s);
+    } else {
+      for (int wi = w0; wi < w1; ++wi) n_sel += __popc(wsel[wi]);
     }
     int pos = block_exclusive_scan(n_sel, scan_scratch);
     int* trow = p.block_table + (int64_t)row * p.table_width;
@@ -274,15 +492,19 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanParams p) {
   pdl_launch_dependents();
 }
 
+bool plan_ecache(int nb_max) { return nb_max <= kPlanECacheMax; }
+
 size_t plan_smem_bytes(int nb_max) {
   const int nw_alloc = (ceil_div(imax(nb_max, 1), 32) + 31) / 32 * 32;
   const bool smem_keys = nb_max <= kPlanSmemMaxKeys;
-  return (size_t)(smem_keys ? nw_alloc * 32 : 0) * 4 + (size_t)2 * nw_alloc * 4;
+  return (size_t)(smem_keys ? nw_alloc * 32 : 0) * 4 +
+         (size_t)(plan_ecache(nb_max) ? nw_alloc * 32 : 0) * 4 + (size_t)2 * nw_alloc * 4;
 }
 
 cudaError_t plan_kernels_init() {
   cudaError_t e = cudaFuncSetAttribute(plan_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)plan_smem_bytes(kPlanSmemMaxKeys));
+                                       (int)std::max(plan_smem_bytes(kPlanSmemMaxKeys),
+                                                     plan_smem_bytes(kPlanECacheMax)));
   if (e != cudaSuccess) return e;
   return cudaFuncSetAttribute(plan_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                               (int)plan_smem_bytes(kPlanMaxBlocks));
