@@ -22,11 +22,11 @@ struct CentroidParams {
   uint32_t* status;
 };
 
-// weight-exchange slot of one (sequence, query head) for the plan barrier
-struct __align__(16) PlanSlot {
-  double w;
-  unsigned int epoch;
-  unsigned int pad;
+// weight-exchange slot of one (sequence, query head) for the plan barrier:
+// one 64-bit word, call tag in the high half (never 0 once written), the
+// head's float32 entropy bits in the low half; written and read whole
+struct __align__(8) PlanSlot {
+  unsigned long long word;
 };
 
 // ---------------------------------------------------------------------------

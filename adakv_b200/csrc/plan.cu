@@ -1,24 +1,29 @@
 // (c) Entropy-driven per-head budget and ragged per-head top-k block selection,
 // one kernel, one CTA of 1024 threads per (sequence, query head).
 //
-// 1. The head's score row is staged in shared memory (coalesced loads).
+// 1. The head's score row is staged in shared memory (coalesced loads) with
+//    its max and content statistics in the same pass.
 // 2. Weight, exactly the formula of adakv/budget.py:28-37: z = s / max(T, 1e-6),
 //    p = softmax(z) in float32, w = -sum(p * log(max(p, 1e-9))) / log(max(nb, 2))
 //    + 1e-6 (float64 after the division, as NumPy promotes it).
-// 3. The Hq CTAs of a sequence exchange weights through per-head slots tagged
-//    with the call's epoch (written by the estimator): each CTA publishes
-//    (w, epoch) and one warp polls the sequence's slots (bounded by a 200 ms
-//    wall-clock limit, after which the status word records a timeout).  Every
-//    CTA then sums the Hq weights in the same fixed order, so all heads see the
+// 3. The Hq CTAs of a sequence exchange entropies through per-head 64-bit
+//    slots (call tag | float32 entropy bits; tags cleared by the estimator):
+//    each CTA publishes its word with one release store and warp 0 polls the
+//    sequence's slots (bounded by a 200 ms wall-clock limit, after which the
+//    status word records a timeout) while the other warps build the top-k
+//    histogram.  Every CTA turns the Hq entropies into weights with the same
+//    arithmetic and sums them in the same fixed order, so all heads see the
 //    same total, and derives its count with the reference's arithmetic
 //    (budget.py:71-86, selector.py:49-54; half-to-even rounding).  The grid is
 //    at most one CTA per SM (so all of it is resident once the estimator
 //    drains) and processes whole sequences per round.
-// 4. Top-k: keys are the order-preserving uint32 images of the scores; sink
-//    [0, sink) and local [nb-local, nb) blocks get 0xFFFFFFFF (the reference's
-//    +inf bias, selector.py:44-48).  A 4-pass MSB radix select over shared
-//    memory finds the k-th largest key T; blocks with key > T and the
-//    lowest-indexed blocks with key == T are selected.
+// 4. Top-k: bucket select over the content blocks (sink [0, sink) and local
+//    [nb-local, nb) are always taken, the reference's +inf bias,
+//    selector.py:44-48): one histogram finds the bucket holding the k-th
+//    score and its members are ranked exactly by (score, lowest index).  A
+//    4-pass MSB radix select over order-preserving uint32 keys is the
+//    fallback; blocks with key > T and the lowest-indexed blocks with key ==
+//    T are selected.
 // 5. Output: warp ballots build the selection bitmap word by word (element
 //    j*1024 + t lands in word j*32 + warp), ties are resolved on the bitmap with
 //    one block scan, and a second scan writes the ascending block table.
@@ -28,14 +33,25 @@
 
 namespace adakv {
 
-__device__ __forceinline__ uint32_t ld_acquire_u32(const unsigned int* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+__device__ __forceinline__ uint64_t ld_acquire_u64(const unsigned long long* p) {
+  uint64_t v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
 
-__device__ __forceinline__ void st_release_u32(unsigned int* p, uint32_t v) {
-  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_release_u64(unsigned long long* p, uint64_t v) {
+  asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// single-barrier block sum: warp results in shared memory, then every warp
+// folds the 32 partials itself (same order in every warp)
+__device__ __forceinline__ double block_sum_1s(double v, double* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  v = warp_sum(v);
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  return warp_sum(lane < (int)(blockDim.x >> 5) ? red[lane] : 0.0);
 }
 
 // order-preserving float -> uint32 map; NaN sorts below everything
@@ -55,38 +71,6 @@ __device__ __forceinline__ int bucket_of(float s, float cmx, float scale) {
   const float u = __fmul_rn(__fsub_rn(cmx, s), scale);
   if (!(u < (float)(kBuckets - 1))) return kBuckets - 1;
   return u <= 0.f ? 0 : (int)u;
-}
-
-__device__ __forceinline__ float block_max1024(float v, float* red) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  v = warp_max(v);
-  if (lane == 0) red[warp] = v;
-  __syncthreads();
-  if (warp == 0) {
-    float x = red[lane];
-    x = warp_max(x);
-    if (lane == 0) red[32] = x;
-  }
-  __syncthreads();
-  const float r = red[32];
-  __syncthreads();
-  return r;
-}
-
-__device__ __forceinline__ double block_sum1024(double v, double* red) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  v = warp_sum(v);
-  if (lane == 0) red[warp] = v;
-  __syncthreads();
-  if (warp == 0) {
-    double x = red[lane];
-    x = warp_sum(x);
-    if (lane == 0) red[32] = x;
-  }
-  __syncthreads();
-  const double r = red[32];
-  __syncthreads();
-  return r;
 }
 
 template <bool SMEM>
@@ -125,76 +109,53 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanParams p) {
     const int nw = ceil_div(nb, 32);
     const float* srow = p.scores + (int64_t)row * p.score_stride;
 
-    if (SMEM) {
-      for (int base = 0; base < nb; base += kPlanThreads * kPlanILP) {
-        float v[kPlanILP];
-#pragma unroll
-        for (int r = 0; r < kPlanILP; ++r) {
-          const int i = base + r * kPlanThreads + tid;
-          v[r] = i < nb ? srow[i] : 0.f;
-        }
-#pragma unroll
-        for (int r = 0; r < kPlanILP; ++r) {
-          const int i = base + r * kPlanThreads + tid;
-          if (i < nb) keys[i] = __float_as_uint(v[r]);
-        }
-      }
-      __syncthreads();
-    }
     auto val = [&](int i) -> float { return SMEM ? __uint_as_float(keys[i]) : srow[i]; };
-
     const int sink = imin(p.cfg.n_sink, nb), local = imin(p.cfg.n_local, nb);
     auto forced = [&](int i) -> bool { return i < sink || i >= nb - local; };
 
-    // ---- one pass of row statistics: max (softmax), content max / mean / spread (top-k) ----
+    // ---- load the row (staged in shared memory) and its statistics in one pass:
+    //      max (softmax), content max / mean / spread (top-k buckets) ----
     float mx = -INFINITY, cmx = -INFINITY, csum_f = 0.f, csq_f = 0.f;
     for (int base = 0; base < nb; base += kPlanThreads * kPlanILP) {
+      float v[kPlanILP];
+#pragma unroll
+      for (int r = 0; r < kPlanILP; ++r) {
+        const int i = base + r * kPlanThreads + tid;
+        v[r] = i < nb ? srow[i] : -INFINITY;
+      }
 #pragma unroll
       for (int r = 0; r < kPlanILP; ++r) {
         const int i = base + r * kPlanThreads + tid;
         if (i < nb) {
-          const float v = val(i);
-          mx = fmaxf(mx, v);
+          if (SMEM) keys[i] = __float_as_uint(v[r]);
+          mx = fmaxf(mx, v[r]);
           if (!forced(i)) {
-            cmx = fmaxf(cmx, v);
-            csum_f += v;
-            csq_f = fmaf(v, v, csq_f);
+            cmx = fmaxf(cmx, v[r]);
+            csum_f += v[r];
+            csq_f = fmaf(v[r], v[r], csq_f);
           }
         }
       }
     }
-    double csum = csum_f, csq = csq_f;
     {
       mx = warp_max(mx);
       cmx = warp_max(cmx);
-      csum = warp_sum(csum);
-      csq = warp_sum(csq);
+      double csum_w = warp_sum((double)csum_f), csq_w = warp_sum((double)csq_f);
+      __syncthreads();
       if (lane == 0) {
         fred[warp] = mx;
         gred[warp] = cmx;
-        dred[warp] = csum;
-        dred2[warp] = csq;
+        dred[warp] = csum_w;
+        dred2[warp] = csq_w;
       }
-      __syncthreads();
-      if (warp == 0) {
-        float a = warp_max(fred[lane]), c = warp_max(gred[lane]);
-        double x = warp_sum(dred[lane]), y = warp_sum(dred2[lane]);
-        if (lane == 0) {
-          fred[32] = a;
-          gred[32] = c;
-          dred[32] = x;
-          dred2[32] = y;
-        }
-      }
-      __syncthreads();
-      mx = fred[32];
-      cmx = gred[32];
-      csum = dred[32];
-      csq = dred2[32];
+      __syncthreads();  // also publishes the staged row
+      mx = warp_max(fred[lane]);
+      cmx = warp_max(gred[lane]);
     }
+    const double csum = warp_sum(dred[lane]), csq = warp_sum(dred2[lane]);
 
-    // ---- entropy weight ----
-    double w = 0.0;
+    // ---- entropy (adakv/budget.py:28-37) ----
+    float ent = 0.f;
     if (nb >= 2 && p.cfg.policy == ADAKV_POLICY_ADAPTIVE) {
       const float m = mx;
       const float Tf = (float)(p.cfg.temperature > 1e-6 ? p.cfg.temperature : 1e-6);
@@ -218,7 +179,7 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanParams p) {
           }
         }
       }
-      const float Z = (float)block_sum1024((double)zpart, dred);
+      const float Z = (float)block_sum_1s((double)zpart, dred);
       float hpart = 0.f;
       for (int base = 0; base < nb; base += kPlanThreads * kPlanILP) {
 #pragma unroll
@@ -231,34 +192,64 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanParams p) {
           }
         }
       }
-      const float hsum = (float)block_sum1024((double)hpart, dred);
-      w = (double)(-hsum) / log((double)imax(nb, 2)) + 1e-6;
+      const float hsum = (float)block_sum_1s((double)hpart, dred);
+      ent = -hsum;
     }
+    auto weight_of = [&](float e) -> double {  // adakv/budget.py:36-37, float64 after the division
+      return (double)e / log((double)imax(nb, 2)) + 1e-6;
+    };
+    const double w = (nb >= 2 && p.cfg.policy == ADAKV_POLICY_ADAPTIVE) ? weight_of(ent) : 0.0;
 
-    // ---- exchange weights within the sequence ----
-    if (tid == 0) {
-      p.slots[row].w = w;
-      __threadfence();
-      st_release_u32(&p.slots[row].epoch, ep);
-    }
+    // ---- publish (entropy, tag) in one 64-bit release store ----
+    unsigned long long* myslot = &p.slots[row].word;
+    if (tid == 0) st_release_u64(myslot, ((uint64_t)ep << 32) | (uint64_t)__float_as_uint(ent));
+
+    // ---- bucket histogram (independent of the budget) while warp 0 waits ----
+    const double nc_d = (double)(nb - imin(nb, sink + local));
+    const double mean_c = nc_d > 0 ? csum / nc_d : 0.0;
+    const double var_c = nc_d > 0 ? csq / nc_d - mean_c * mean_c : 0.0;
+    const double range = (double)cmx - mean_c + (var_c > 0.0 ? sqrt(var_c) : 0.0);
+    const bool buckets_ok = isfinite(cmx) && range > 0.0 && isfinite(range);
+    const float scale = buckets_ok ? (float)((double)(kBuckets - 1) / range) : 0.f;
+    for (int t = tid; t < kBuckets; t += kPlanThreads) hist[t] = 0u;
+    __syncthreads();
     if (warp == 0) {
       const uint64_t t0 = globaltimer_ns();
       bool ok = false;
+      float ents[4];  // Hq <= 128
       while (true) {
         bool mine = true;
-        for (int hh = lane; hh < p.Hq; hh += 32)
-          mine &= (ld_acquire_u32(&p.slots[b * p.Hq + hh].epoch) == ep);
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          const int hh = lane + q4 * 32;
+          if (hh < p.Hq) {
+            const uint64_t v = ld_acquire_u64(&p.slots[b * p.Hq + hh].word);
+            mine &= ((uint32_t)(v >> 32) == ep);
+            ents[q4] = __uint_as_float((uint32_t)v);
+          }
+        }
         ok = __all_sync(0xffffffffu, mine);
         if (ok || globaltimer_ns() - t0 > kWaitLimitNs) break;
       }
       if (!ok && lane == 0) report(p.status, ADAKV_ST_WAIT_TIMEOUT);
       double part = 0.0;
-      for (int hh = lane; hh < p.Hq; hh += 32)
-        part += *reinterpret_cast<const volatile double*>(&p.slots[b * p.Hq + hh].w);
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) {
+        const int hh = lane + q4 * 32;
+        if (hh < p.Hq && p.cfg.policy == ADAKV_POLICY_ADAPTIVE && nb >= 2) part += weight_of(ents[q4]);
+      }
       part = warp_sum(part);  // fixed xor tree: every CTA of the sequence gets the same sum
       if (lane == 0) s_sumw = part;
+    } else if (buckets_ok) {
+      for (int i = tid - 32; i < nb; i += kPlanThreads - 32) {
+        if (!forced(i)) {
+          const int bk = bucket_of(val(i), cmx, scale);
+          if (bk < kBuckets - 1) atomicAdd(&hist[bk], 1u);
+        }
+      }
     }
     __syncthreads();
+    pdl_launch_dependents();  // every CTA is past the exchange: the attend grid may launch
     const SeqBudget sbud = seq_budget(nb, p.cfg);
     const int K = imin(head_count(sbud, p.cfg, w, s_sumw, p.Hq), p.table_width);
     const int n_forced = (sink + local >= nb) ? nb : sink + local;
@@ -276,29 +267,9 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanParams p) {
     // bucket or holds too many members.
     bool use_radix = false;
     int jstar = kBuckets, need_b = 0;
-    float scale = 0.f;
     if (K < nb && Kc > 0) {
-      const double nc = (double)(nb - n_forced);
-      const double mean = csum / nc;
-      const double var = csq / nc - mean * mean;
-      const double sd = var > 0.0 ? sqrt(var) : 0.0;
-      const double range = (double)cmx - mean + sd;
-      use_radix = !(isfinite(cmx) && range > 0.0 && isfinite(range));
+      use_radix = !buckets_ok;
       if (!use_radix) {
-        scale = (float)((double)(kBuckets - 1) / range);
-        for (int t = tid; t < kBuckets; t += kPlanThreads) hist[t] = 0u;
-        __syncthreads();
-        for (int base = 0; base < nb; base += kPlanThreads * kPlanILP) {
-#pragma unroll
-          for (int r = 0; r < kPlanILP; ++r) {
-            const int i = base + r * kPlanThreads + tid;
-            if (i < nb && !forced(i)) {
-              const int bk = bucket_of(val(i), cmx, scale);
-              if (bk < kBuckets - 1) atomicAdd(&hist[bk], 1u);
-            }
-          }
-        }
-        __syncthreads();
         // find the bucket holding the Kc-th content block (buckets ascend = scores descend)
         constexpr int BPT = kBuckets / kPlanThreads;
         uint32_t cb[BPT], tot = 0;
