@@ -599,3 +599,94 @@ int adakv_read_status(void* workspace, uint32_t* status, void* stream) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// adakv_attend_noalloc: adakv_attend with its scratch (status word + selection
+// bitmaps) in a fixed device array of this library instead of a caller
+// workspace.  It has no counterpart in the reference.
+// ---------------------------------------------------------------------------
+namespace {
+
+// Largest scratch the entry point can use: the workspace layout of
+// adakv_attend, i.e. 512 bytes of header plus B * Hq * ceil(nb_cap / 32) * 4
+// bytes of bitmaps (B * Hq = 32 at nb_cap = 8192 takes 32 KiB; 4 MiB covers
+// e.g. B * Hq = 2048 rows at 128K tokens).
+constexpr size_t kNoAllocScratchBytes = 4u << 20;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+// Per-device address of g_noalloc_scratch, resolved once with that device
+// current (a __device__ symbol has one instance per device).
+void* g_noalloc_addr[kMaxDevices];
+
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return fail(ADAKV_ERR_UNSUPPORTED, "device index %d", dev);
+  std::lock_guard<std::mutex> lock(g_dev_mu);
+  if (!g_noalloc_addr[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess)
+      return fail(ADAKV_ERR_CUDA, "cudaGetSymbolAddress(scratch) failed: %s", cudaGetErrorString(e));
+    if (!p || reinterpret_cast<uintptr_t>(p) % 256)
+      return fail(ADAKV_ERR_CUDA, "scratch array is not 256-byte aligned");
+    g_noalloc_addr[dev] = p;
+  }
+  *out = g_noalloc_addr[dev];
+  return ADAKV_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int adakv_attend_noalloc(const adakv_geometry* geo, const adakv_view* q, const adakv_view* k,
+                         const adakv_view* v, const int32_t* block_table, int32_t table_width,
+                         const int32_t* sel_lens, const int32_t* seq_lens, float sm_scale,
+                         const adakv_view* out, uint32_t* status, void* stream) {
+  int rc;
+  if ((rc = check_geometry(geo))) return rc;
+  if ((rc = check_attend_views(geo, q, k, v, out))) return rc;
+  if (!block_table || !sel_lens) return fail(ADAKV_ERR_INVALID, "block_table / sel_lens are NULL");
+  if (table_width < 1) return fail(ADAKV_ERR_INVALID, "table_width must be >= 1");
+  if (!std::isfinite(sm_scale)) return fail(ADAKV_ERR_INVALID, "sm_scale must be finite");
+  if (status && reinterpret_cast<uintptr_t>(status) % 4)
+    return fail(ADAKV_ERR_INVALID, "status must be a 4-byte aligned device pointer");
+  const WsLayout L = make_ws(geo, false);
+  if (L.bytes > kNoAllocScratchBytes)
+    return fail(ADAKV_ERR_INVALID,
+                "adakv_attend_noalloc needs %zu scratch bytes for this geometry, above its fixed "
+                "maximum of %zu (batch * n_q_heads * ceil(nb_cap / 32) * 4 + 512); use "
+                "adakv_attend with a workspace",
+                L.bytes, kNoAllocScratchBytes);
+  DeviceState* ds = nullptr;
+  if ((rc = device_state(&ds))) return rc;
+  void* ws = nullptr;
+  if ((rc = noalloc_scratch(&ws))) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // the status word collects this call's bits: it starts at zero every call;
+  // the bitmap rows are written in full by the table kernel before use
+  CUDA_TRY(cudaMemsetAsync(ws_at<uint32_t>(ws, L.status), 0, sizeof(uint32_t), st));
+  TableParams tp{};
+  tp.block_table = block_table;
+  tp.table_width = table_width;
+  tp.sel_lens = sel_lens;
+  tp.seq_lens = seq_lens;
+  tp.max_seq_len = geo->max_seq_len;
+  tp.B = geo->batch;
+  tp.Hq = geo->n_q_heads;
+  tp.bs = geo->block_size;
+  tp.bitmap = ws_at<uint32_t>(ws, L.bitmap);
+  tp.bm_words = L.bm_words;
+  tp.status = ws_at<uint32_t>(ws, L.status);
+  LaunchOpts ot;
+  ot.pdl = false;  // follows the memset
+  CUDA_TRY(launch_table_bitmap(tp, st, ot));
+  if ((rc = enqueue_attend(ds, geo, q, k, v, out, seq_lens, sm_scale, ws, L, st))) return rc;
+  if (status)
+    CUDA_TRY(cudaMemcpyAsync(status, ws_at<uint32_t>(ws, L.status), sizeof(uint32_t),
+                             cudaMemcpyDeviceToDevice, st));
+  return ADAKV_OK;
+}
+
+}  // extern "C"

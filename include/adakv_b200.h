@@ -165,6 +165,26 @@ int adakv_attend(const adakv_geometry* geo, const adakv_view* q, const adakv_vie
                  const int32_t* sel_lens, const int32_t* seq_lens, float sm_scale,
                  const adakv_view* out, void* workspace, size_t workspace_bytes, void* stream);
 
+/* adakv_attend without a workspace: no counterpart in the reference.
+ *
+ * For callers that cannot hand over device memory: a serving engine that has
+ * given all free memory to its KV-cache pool, or a host language with no
+ * device allocator at hand.  The scratch (status word + selection bitmaps)
+ * is a fixed 4 MiB array inside this library, one per device; a geometry
+ * needing more than batch * n_q_heads * ceil(nb_cap / 32) * 4 + 512 <= 4 MiB
+ * bytes is rejected with ADAKV_ERR_INVALID.  Nothing is allocated on the
+ * device.  The first call on each device looks the array up (and may load
+ * the library's device code): make that first call before any stream capture.
+ * The scratch is shared, so two calls in flight at once on one device (other
+ * streams, other threads) race and corrupt each other; order them on one
+ * stream.  `status` (optional device word, may be NULL) receives this call's
+ * ADAKV_ST_* bits, overwritten each call.  Same inputs and output as
+ * adakv_attend. */
+int adakv_attend_noalloc(const adakv_geometry* geo, const adakv_view* q, const adakv_view* k,
+                         const adakv_view* v, const int32_t* block_table, int32_t table_width,
+                         const int32_t* sel_lens, const int32_t* seq_lens, float sm_scale,
+                         const adakv_view* out, uint32_t* status, void* stream);
+
 /* One full decode step with no host synchronisation anywhere
  * (adakv/attention.py:250-268, adakv/runtime.py:85-112, adakv/runtime.py:43-60):
  * optionally append n_new tokens per sequence (k_new / v_new [B, Hkv, n_new, D];
