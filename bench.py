@@ -44,6 +44,9 @@ CFG = dict(Hq=32, Hkv=8, D=128, bs=16, avg=64, k_min=2, k_max=512, sink=1, local
 HEADLINE_S = 131072
 KERNELS_PER_STEP = 3
 L2_FLUSH_BYTES = 256 << 20
+# DRAM bytes (read + write) of one decode step at each context, summed over the
+# three kernels of one ncu --set full capture (profiles/decode_step_128k_kernels.md)
+NCU_STEP_TRAFFIC = {131072: 33_661_184 + 1_128_448 + 8_756_224}
 
 
 def workload_name(S):
@@ -435,7 +438,7 @@ def main():
                                   "steps. us_isolated_median = one step alone after an L2 flush, "
                                   "launch included")},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": None,
+                         "frac": achieved / peak, "traffic": NCU_STEP_TRAFFIC.get(headline),
                          "scope": "whole decode step (all 3 kernels); bytes = fp32 centroid "
                                   "table + union of selected K/V blocks per KV head + append",
                          "peak_source": "MEASURED_PEAKS.json hbm_gbs" if peaks else "fallback"},
