@@ -1,0 +1,197 @@
+"""Plug the AdaKV decode path into a HuggingFace model (transformers >= 5).
+
+Mirror of the reference's ``adakv/patch.py`` interface:
+
+    from adakv_b200.patch import install_adakv, enable_adakv, disable_adakv, patch_model
+    install_adakv(model); enable_adakv(block_size=16, avg_budget=64)
+    # or: patch_model(model, block_size=16, avg_budget=64)
+    ... model.generate(...) ...
+    disable_adakv()
+
+``adakv_attention_forward`` is registered as the attention implementation
+"adakv" (``adakv/patch.py:90-124``).  Prefill (``q_len > 1``) stays dense
+through SDPA, as in the reference; single-token decode runs the sparse path on
+the device: estimator, entropy budget, top-k and block-sparse attention in
+three kernel launches with no host synchronisation.
+
+Differences from the reference, all on the performance side:
+
+* The reference rebuilds every block centroid from the whole key cache on
+  every decode step of every layer (``patch.py:110``).  Here each layer keeps
+  its float32 centroid table between calls (keyed by the module, like the
+  reference's ``_FROZEN``): the prefill pass builds it from the prompt keys,
+  and each decode step refreshes only the blocks touched by the tokens
+  appended since (``adakv_centroid_refresh``).  The centroids are bit-identical
+  to a full rebuild.
+* Batched decode (``B > 1``) without an attention mask (no padding: every
+  sequence has the key length) runs the same batched kernels; with a mask it
+  goes dense, as the reference does for every ``B != 1`` call (``patch.py:96``).
+
+The H2O / SnapKV eviction baselines (``selection="h2o" | "snapkv"``,
+``patch.py:57-87``) are not part of this path and raise ``NotImplementedError``.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import _lib
+from .attention import record_selection, tracing_enabled
+
+try:
+    from transformers import AttentionInterface
+except Exception:  # pragma: no cover - older layout
+    from transformers.modeling_utils import AttentionInterface
+from transformers.modeling_utils import ALL_ATTENTION_FUNCTIONS
+
+# same keys and defaults as the reference's configuration (adakv/patch.py:43-48)
+_ADAKV_CFG = dict(enabled=True, block_size=16, avg_budget=16, k_min=2, k_max=64,
+                  n_sink_blocks=1, n_local_blocks=4, temperature=1.0,
+                  estimator="centroid", budget_policy="adaptive",
+                  c_min=1, nucleus_p=0.9,
+                  selection="adakv", obs_window=32, pool_kernel=7, h2o_chunk=256)
+_SDPA = ALL_ATTENTION_FUNCTIONS["sdpa"]
+
+
+class _LayerState:
+    """Centroid table of one attention layer: ``cbuf [B, Hkv, cap, D]`` float32,
+    valid for the first ``n`` tokens of the layer's key cache."""
+
+    __slots__ = ("cbuf", "n", "bs", "shape", "dtype", "device")
+
+    def __init__(self):
+        self.cbuf = None
+        self.n = 0
+        self.bs = 0
+        self.shape = None
+        self.dtype = None
+        self.device = None
+
+
+# per-layer state keyed by id(module); cleared by enable_adakv / disable_adakv
+_STATE: dict[int, _LayerState] = {}
+
+
+def _geometry(B, Hq, Hkv, D, bs, S, nb_cap, dtype):
+    return _lib.geometry(B, Hq, Hkv, D, bs, S, nb_cap, _lib.TORCH_DTYPES[dtype])
+
+
+def _sync_centroids(module, key, Hq, bs, rebuild):
+    """Bring the layer's centroid table up to date with ``key [B, Hkv, S, D]``."""
+    B, Hkv, S, D = key.shape
+    st = _STATE.get(id(module))
+    if st is None:
+        st = _STATE[id(module)] = _LayerState()
+    nb = (S + bs - 1) // bs
+    shape = (B, Hkv, D)
+    stale = (st.cbuf is None or st.shape != shape or st.bs != bs or st.dtype != key.dtype
+             or st.device != key.device or st.n > S)
+    rebuild = rebuild or stale
+    if stale or st.cbuf.shape[2] < nb:
+        cap = max(nb, 64, 0 if stale else 2 * st.cbuf.shape[2])
+        buf = torch.empty((B, Hkv, cap, D), dtype=torch.float32, device=key.device)
+        if not rebuild:  # capacity growth: keep the valid rows
+            buf[:, :, : st.cbuf.shape[2]].copy_(st.cbuf)
+        st.cbuf = buf
+    st.shape, st.bs, st.dtype, st.device = shape, bs, key.dtype, key.device
+    geo = _geometry(B, Hq, Hkv, D, bs, S, st.cbuf.shape[2], key.dtype)
+    L = _lib.lib()
+    stream = _lib.stream_ptr(key.device)
+    if rebuild or S - st.n > S // 2:
+        _lib.check(L.adakv_centroid_build(geo, _lib.view4(key), None, st.cbuf.data_ptr(), stream))
+    elif S > st.n:
+        _lib.check(L.adakv_centroid_refresh(geo, _lib.view4(key), S - st.n, None,
+                                            st.cbuf.data_ptr(), stream))
+    st.n = S
+    return st
+
+
+def adakv_attention_forward(module, query, key, value, attention_mask, scaling, dropout=0.0,
+                            **kwargs):
+    """HF attention function (reference ``adakv/patch.py:90-121``).
+
+    ``query [B, Hq, q_len, D]``, ``key`` / ``value [B, Hkv, S, D]``; returns
+    ``(out [B, q_len, Hq, D], None)``."""
+    cfg = _ADAKV_CFG
+    B, Hq, q_len, D = query.shape
+    sel = cfg.get("selection", "adakv")
+    if sel != "adakv":
+        raise NotImplementedError(f"selection={sel!r} (eviction baselines) is not built here")
+    sparse = cfg["enabled"] and q_len == 1 and (B == 1 or attention_mask is None)
+    if not sparse:
+        if cfg["enabled"] and q_len > 1 and query.is_cuda and D in (64, 128):
+            # prompt keys are final for these positions: build the table now
+            with torch.cuda.device(query.device):
+                _sync_centroids(module, key, Hq, cfg["block_size"], rebuild=True)
+        return _SDPA(module, query, key, value, attention_mask=attention_mask, scaling=scaling,
+                     dropout=dropout, **kwargs)
+
+    _lib.require_cuda(query, key, value)
+    if cfg["estimator"] == "minmax":
+        raise NotImplementedError("the minmax (Quest) estimator is not built yet")
+    if cfg["estimator"] != "centroid":
+        raise ValueError(f"unknown estimator: {cfg['estimator']!r}")
+    if key.dtype != query.dtype or value.dtype != query.dtype:
+        raise ValueError("query, key and value must share one dtype")
+    bs = int(cfg["block_size"])
+    _, Hkv, S, _ = key.shape
+    sm_scale = float(scaling) if scaling is not None else 1.0 / math.sqrt(D)
+    with torch.cuda.device(query.device):
+        st = _sync_centroids(module, key, Hq, bs, rebuild=False)
+        sp = _lib.select_params(cfg["avg_budget"], cfg["k_min"], cfg["k_max"],
+                                cfg["n_sink_blocks"], cfg["n_local_blocks"], cfg["c_min"],
+                                cfg["temperature"], cfg["budget_policy"])
+        geo = _geometry(B, Hq, Hkv, D, bs, S, st.cbuf.shape[2], query.dtype)
+        L = _lib.lib()
+        width = L.adakv_plan_table_width(geo, sp)
+        if width < 1:
+            _lib.check(_lib.ERR_INVALID)
+        block_table = torch.empty((B * Hq, width), dtype=torch.int32, device=query.device)
+        sel_lens = torch.empty((B * Hq,), dtype=torch.int32, device=query.device)
+        out = torch.empty((B, 1, Hq, D), dtype=query.dtype, device=query.device)
+        ws = _lib.workspace(L.adakv_plan_workspace_bytes(geo, sp), query.device)
+        q3 = query[:, :, 0, :]
+        if q3.stride(-1) != 1:
+            q3 = q3.contiguous()
+        o3 = out[:, 0]  # [B, Hq, D] view of the [B, 1, Hq, D] output
+        _lib.check(L.adakv_decode_step(
+            geo, sp, _lib.view4(q3), _lib.view4(key), _lib.view4(value), None, None, 0,
+            st.cbuf.data_ptr(), None, sm_scale, block_table.data_ptr(), width,
+            sel_lens.data_ptr(), _lib.view4(o3), ws.data_ptr(), ws.numel(),
+            _lib.stream_ptr(query.device)))
+    if tracing_enabled() and B == 1:
+        record_selection(block_table, sel_lens, (S + bs - 1) // bs)
+    return out, None
+
+
+AttentionInterface.register("adakv", adakv_attention_forward)
+
+
+def install_adakv(model):
+    """Route the model's attention through ``adakv_attention_forward``."""
+    try:
+        model.set_attn_implementation("adakv")
+    except Exception:
+        model.config._attn_implementation = "adakv"
+    return model
+
+
+def enable_adakv(**cfg):
+    """Update the configuration (reference keys) and turn the sparse path on."""
+    _ADAKV_CFG.update(cfg)
+    _ADAKV_CFG["enabled"] = True
+    _STATE.clear()
+
+
+def disable_adakv():
+    """Every call goes dense (SDPA) until ``enable_adakv``."""
+    _ADAKV_CFG["enabled"] = False
+    _STATE.clear()
+
+
+def patch_model(model, block_size=16, avg_budget=16, **cfg):
+    """``install_adakv`` + ``enable_adakv(block_size=..., avg_budget=..., **cfg)``."""
+    install_adakv(model)
+    enable_adakv(block_size=block_size, avg_budget=avg_budget, **cfg)
+    return model
