@@ -48,7 +48,7 @@ int fail(int code, const char* fmt, ...) {
 struct DeviceState {
   bool ready = false;
   int num_sms = 0;
-  std::map<int, int> plan_ctas;                    // nb_max -> plan CTAs per SM
+  std::map<int, int> plan_ctas;                    // nb_max * 16 + cluster -> resident plan clusters
   std::map<std::tuple<int, int, int, int, size_t>, int> clusters;  // attend shape -> active clusters
 };
 constexpr int kMaxDevices = 64;
@@ -181,7 +181,7 @@ WsLayout make_ws(const adakv_geometry* g, bool with_plan) {
   auto take = [&](size_t bytes) { size_t at = o; o = align_up(o + bytes, 256); return at; };
   L.status = take(16);
   L.epoch = take(16);
-  L.slots = with_plan ? take(sizeof(PlanSlot) * rows) : 0;
+  L.slots = with_plan ? take(sizeof(PlanSlot) * rows * kPlanSlotsPerRow) : 0;
   L.scores = with_plan ? take(sizeof(float) * (size_t)rows * L.score_stride) : 0;
   L.bitmap = take(sizeof(uint32_t) * (size_t)rows * L.bm_words);
   L.bytes = o;
@@ -259,29 +259,44 @@ int enqueue_plan(const DeviceState* ds, const adakv_geometry* g, const adakv_sel
   pp.table_width = table_width;
   pp.bitmap = ws_at<uint32_t>(ws, L.bitmap);
   pp.bm_words = L.bm_words;
-  pp.nw_max = ceil_div(nb_max, 32);
-  pp.ecache = plan_ecache(nb_max) ? 1 : 0;
   pp.status = status;
-  int per_sm;
-  {
+  // Cluster size: the largest C in {8, 4, 2} whose slices keep >= 1024 blocks,
+  // with all B * Hq * C CTAs resident at once and at most one per SM (one
+  // round); else C = 1 with as many sequences per round as are resident.
+  // The clusters of a sequence wait on one another (entropy exchange), so the
+  // grid never exceeds what is resident once the estimator drains; the
+  // exchange is also bounded in time.
+  auto active = [&](const PlanLayout& l) {
     std::lock_guard<std::mutex> lock(g_dev_mu);
-    auto it = ds->plan_ctas.find(nb_max);
+    const int key = nb_max * 16 + l.csize;
+    auto it = ds->plan_ctas.find(key);
     if (it == ds->plan_ctas.end())
-      it = const_cast<DeviceState*>(ds)->plan_ctas.emplace(nb_max, plan_ctas_per_sm(nb_max)).first;
-    per_sm = it->second;
+      it = const_cast<DeviceState*>(ds)->plan_ctas.emplace(key, plan_active_clusters(l)).first;
+    return it->second;
+  };
+  const int64_t heads = (int64_t)g->batch * g->n_q_heads;
+  PlanLayout lay = plan_layout(nb_max, 1);
+  for (int c = kPlanMaxCluster; c >= 2; c /= 2) {
+    if (ceil_div(nb_max, c) < 1024 || heads * c > ds->num_sms) continue;
+    const PlanLayout l = plan_layout(nb_max, c);
+    if (l.smem > kPlanSmemMax || active(l) < heads) continue;
+    lay = l;
+    break;
   }
-  const int capacity = ds->num_sms * per_sm;
-  if (std::min(capacity, ds->num_sms) < g->n_q_heads)
-    return fail(ADAKV_ERR_UNSUPPORTED, "n_q_heads %d exceeds the co-resident plan CTAs (%d)",
-                g->n_q_heads, std::min(capacity, ds->num_sms));
-  // The CTAs of a sequence wait on one another (weight exchange): the grid is
-  // capped at one CTA per SM and at the co-resident capacity, so every CTA is
-  // resident once the estimator drains; the exchange is also bounded in time.
-  pp.seqs_per_round = std::max(1, std::min(g->batch, std::min(capacity, ds->num_sms) / g->n_q_heads));
-  const int plan_grid = pp.seqs_per_round * g->n_q_heads;
+  if (lay.smem > kPlanSmemMax)
+    return fail(ADAKV_ERR_UNSUPPORTED, "sequence too long for the plan kernel's shared memory");
+  const int clusters = active(lay);
+  if (clusters < g->n_q_heads)
+    return fail(ADAKV_ERR_UNSUPPORTED, "n_q_heads %d exceeds the co-resident plan clusters (%d)",
+                g->n_q_heads, clusters);
+  pp.csize = lay.csize;
+  pp.slice_cap = lay.slice_cap;
+  pp.ecache = lay.ecache ? 1 : 0;
+  pp.seqs_per_round = std::max(1, std::min(g->batch, clusters / g->n_q_heads));
+  const int plan_grid = pp.seqs_per_round * g->n_q_heads * lay.csize;
   LaunchOpts op;
   op.pdl = pdl;
-  CUDA_TRY(launch_plan(pp, nb_max, plan_grid, st, op));
+  CUDA_TRY(launch_plan(pp, lay, plan_grid, st, op));
   return ADAKV_OK;
 }
 

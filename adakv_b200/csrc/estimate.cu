@@ -310,7 +310,8 @@ __global__ void __launch_bounds__(kEstThreads, 1) estimate_kernel(EstParams p) {
     // clear the plan's weight-exchange tags of this call's rows (the plan kernel
     // starts after this grid completes, so no stale tag can satisfy its barrier)
     if (p.slots) {
-      for (int r = blockIdx.x * 32 + lane; r < p.B * p.Hq; r += gridDim.x * 32) p.slots[r].word = 0ull;
+      for (int r = blockIdx.x * 32 + lane; r < p.B * p.Hq * kPlanSlotsPerRow; r += gridDim.x * 32)
+        p.slots[r].word = 0ull;
     }
   } else {
     // ---------------- consumers ----------------

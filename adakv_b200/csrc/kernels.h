@@ -48,7 +48,7 @@ struct EstParams {
   float* scores;          // [B, Hq, score_stride]
   int score_stride;
   uint32_t* epoch;        // incremented once per launch (per-call tag for the plan barrier)
-  PlanSlot* slots;        // [B*Hq] weight-exchange slots: tags cleared here, before the plan
+  PlanSlot* slots;        // [B*Hq*kPlanSlotsPerRow] exchange slots: cleared here, before the plan
   // fused append: n_new > 0 and k_new.data != NULL
   View k, v, k_new, v_new;
   int n_new;
@@ -59,12 +59,22 @@ struct EstParams {
 // ---------------------------------------------------------------------------
 // (c) plan: entropy budget + per-sequence weight exchange + top-k
 // ---------------------------------------------------------------------------
-constexpr int kPlanThreads = 1024;
-constexpr int kPlanSmemMaxKeys = 48 * 1024;   // keys staged in smem up to this many blocks
+constexpr int kPlanThreads = 512;
+constexpr int kPlanSmemMaxKeys = 32 * 1024;   // slice staged in shared memory up to this many blocks
+constexpr int kPlanECacheMax = 16 * 1024;     // exp(z - zmax) cached in shared memory up to this many
 constexpr int kPlanMaxBlocks = 512 * 1024;    // longest sequence in blocks (bitmap words in smem)
-constexpr int kPlanECacheMax = 24 * 1024;     // exp(z - zmax) cached in smem up to this many blocks  // larger rows are re-read from L2 each pass
+constexpr size_t kPlanSmemMax = 160 * 1024;   // opt-in dynamic shared memory of one plan CTA
+constexpr int kPlanMaxCluster = 8;            // CTAs splitting one head's score row
+constexpr int kPlanSlotsPerRow = 2 * kPlanMaxCluster;  // exchange words per (sequence, head)
 
-
+// shared-memory layout of one plan CTA for a cluster size and longest row
+struct PlanLayout {
+  int csize;       // CTAs per (sequence, head)
+  int slice_cap;   // blocks per CTA (multiple of 32)
+  bool smem_keys;  // slice staged in shared memory (else re-read from L2)
+  bool ecache;     // exp(z - zmax) cached in shared memory
+  size_t smem;     // dynamic shared memory bytes
+};
 
 struct PlanParams {
   const int* seq_lens;
@@ -74,15 +84,16 @@ struct PlanParams {
   const float* scores;
   int score_stride;
   const uint32_t* epoch;
-  PlanSlot* slots;          // [B*Hq]
+  PlanSlot* slots;          // [B*Hq*kPlanSlotsPerRow]
   int* sel_lens;            // [B*Hq] out
   int* block_table;         // [B*Hq, table_width] out, ascending block ids
   int table_width;
   uint32_t* bitmap;         // [B*Hq, bm_words] out, bit j = block j selected
   int bm_words;
-  int nw_max;               // ceil(ceil(max_seq_len / bs) / 32): sizes the shared buffers
-  int ecache;               // cache exp(z - zmax) in shared memory (plan_ecache)
-  int seqs_per_round;       // grid = seqs_per_round * Hq CTAs
+  int csize;                // CTAs of the cluster splitting each row
+  int slice_cap;            // blocks per CTA (PlanLayout::slice_cap)
+  int ecache;               // cache exp(z - zmax) in shared memory (PlanLayout::ecache)
+  int seqs_per_round;       // grid = seqs_per_round * Hq * csize CTAs
   uint32_t* status;
 };
 
@@ -165,7 +176,7 @@ cudaError_t launch_centroid(const CentroidParams& p, int dtype, int D, int block
                             cudaStream_t stream);
 cudaError_t launch_estimate(const EstParams& p, int dtype, int D, int nb_max, int grid,
                             cudaStream_t stream, const LaunchOpts& o);
-cudaError_t launch_plan(const PlanParams& p, int nb_max, int grid, cudaStream_t stream,
+cudaError_t launch_plan(const PlanParams& p, const PlanLayout& l, int grid, cudaStream_t stream,
                         const LaunchOpts& o);
 cudaError_t launch_attend(const AttendParams& p, int dtype, int D, int bs, int cluster,
                           cudaStream_t stream, const LaunchOpts& o);
@@ -177,9 +188,9 @@ cudaError_t plan_kernels_init();
 cudaError_t attend_kernels_init();
 size_t estimate_smem_bytes(int dtype, int D, int g, int B);
 int estimate_stages(int dtype, int D, int g, int B);
-size_t plan_smem_bytes(int nb_max);
-bool plan_ecache(int nb_max);
-int plan_ctas_per_sm(int nb_max);
+PlanLayout plan_layout(int nb_max, int csize);
+// clusters of the plan kernel with layout `l` that can be resident at once
+int plan_active_clusters(const PlanLayout& l);
 // clusters of `cluster` CTAs of the attend kernel that can be resident at once
 int attend_active_clusters(int dtype, int D, int bs, int g, size_t smem, int cluster);
 size_t attend_smem_bytes(int dtype, int D, int bs, int nbt, int g, int nw_max, int slice_cap);

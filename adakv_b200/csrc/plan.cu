@@ -1,57 +1,74 @@
-// (c) Entropy-driven per-head budget and ragged per-head top-k block selection,
-// one kernel, one CTA of 1024 threads per (sequence, query head).
+// (c) Entropy-driven per-head budget and ragged per-head top-k block selection.
 //
-// 1. The head's score row is staged in shared memory (coalesced loads) with
-//    its max and content statistics in the same pass.
-// 2. Weight, exactly the formula of adakv/budget.py:28-37: z = s / max(T, 1e-6),
-//    p = softmax(z) in float32, w = -sum(p * log(max(p, 1e-9))) / log(max(nb, 2))
-//    + 1e-6 (float64 after the division, as NumPy promotes it).
-// 3. The Hq CTAs of a sequence exchange entropies through per-head 64-bit
-//    slots (call tag | float32 entropy bits; tags cleared by the estimator):
-//    each CTA publishes its word with one release store and warp 0 polls the
+// One thread-block cluster of C CTAs (C = 1..8, chosen on the host) per
+// (sequence, query head); CTA r of the cluster owns the blocks
+// [r * L, (r + 1) * L) of the head's score row, L = ceil(nb / C) rounded up to
+// 32 so every CTA owns whole bitmap words.  Row-wide quantities are merged
+// through distributed shared memory: each CTA publishes its partials in a
+// shared struct, `cluster.sync()`, and every CTA folds the C partials in rank
+// order, so all CTAs (and all heads) compute bit-identical row values.
+//
+// 1. Load + statistics: the slice is staged in shared memory; max, content
+//    max, content sum and sum of squares (sink/local blocks excluded).
+// 2. Entropy, the formula of adakv/budget.py:28-37 with z = s / max(T, 1e-6),
+//    e = exp(z - max z) in float32 per block, Z = sum e, p = e / Z:
+//        H = -sum p log(max(p, 1e-9)) = log Z - A / Z - Cc / Z,
+//    A = sum e (z - zmax) (one pass, no per-block division or logarithm) and
+//    Cc = sum over blocks with p < 1e-9 of e (log(1e-9) - (z - zmax) + log Z),
+//    the reference's clamp; sums are float per thread, double across threads.
+// 3. The Hq clusters of a sequence exchange entropies through per-head 64-bit
+//    slots (call tag << 32 | float32 entropy; tags cleared by the estimator):
+//    rank 0 publishes with one release store; warp 0 of every CTA polls the
 //    sequence's slots (bounded by a 200 ms wall-clock limit, after which the
-//    status word records a timeout) while the other warps build the top-k
-//    histogram.  Every CTA turns the Hq entropies into weights with the same
-//    arithmetic and sums them in the same fixed order, so all heads see the
-//    same total, and derives its count with the reference's arithmetic
-//    (budget.py:71-86, selector.py:49-54; half-to-even rounding).  The grid is
-//    at most one CTA per SM (so all of it is resident once the estimator
-//    drains) and processes whole sequences per round.
-// 4. Top-k: bucket select over the content blocks (sink [0, sink) and local
-//    [nb-local, nb) are always taken, the reference's +inf bias,
-//    selector.py:44-48): one histogram finds the bucket holding the k-th
-//    score and its members are ranked exactly by (score, lowest index).  A
-//    4-pass MSB radix select over order-preserving uint32 keys is the
-//    fallback; blocks with key > T and the lowest-indexed blocks with key ==
-//    T are selected.
-// 5. Output: warp ballots build the selection bitmap word by word (element
-//    j*1024 + t lands in word j*32 + warp), ties are resolved on the bitmap with
-//    one block scan, and a second scan writes the ascending block table.
+//    status word records a timeout) while the other warps merge the cluster's
+//    top-k histograms.  Every CTA derives the Hq weights with the same
+//    arithmetic (adakv/budget.py:36-37, float64 after the division), sums them
+//    in a fixed order and computes its count (budget.py:71-86,
+//    selector.py:49-54; half-to-even rounding).
+// 4. Top-k over the content blocks (sink [0, sink) and local [nb-local, nb)
+//    are always taken, the reference's +inf bias, selector.py:44-48): a
+//    2048-bucket histogram over [cmax - range, cmax] (range = cmax - mean +
+//    sd) finds the bucket holding the k-th score; that bucket's members across
+//    the cluster are ranked exactly by (score desc, index asc).  A 4-pass MSB
+//    radix select over order-preserving uint32 keys, merged across the
+//    cluster, is the fallback; its ties at the threshold go to the lowest
+//    indices.
+// 5. Output: warp ballots build the slice's bitmap words; the table is written
+//    in ascending block order at the cluster-wide exclusive prefix of the
+//    per-CTA counts.
+//
+// All CTAs of one sequence must be resident together (they wait on each
+// other's slots): the host sizes the grid from the cluster occupancy.
 #include <algorithm>
+
+#include <cooperative_groups.h>
 
 #include "kernels.h"
 
+namespace cg = cooperative_groups;
+
 namespace adakv {
 
-__device__ __forceinline__ uint64_t ld_acquire_u64(const unsigned long long* p) {
+// Slot words are single-copy atomic 64-bit values that carry their own tag
+// and payload, so relaxed (uncached, gpu-scope) accesses suffice; relaxed
+// loads of different slots are independent and overlap in flight.
+__device__ __forceinline__ uint64_t ld_relaxed_u64(const unsigned long long* p) {
   uint64_t v;
-  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
 
-__device__ __forceinline__ void st_release_u64(unsigned long long* p, uint64_t v) {
-  asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+__device__ __forceinline__ void st_relaxed_u64(unsigned long long* p, uint64_t v) {
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
-// single-barrier block sum: warp results in shared memory, then every warp
-// folds the 32 partials itself (same order in every warp)
-__device__ __forceinline__ double block_sum_1s(double v, double* red) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  v = warp_sum(v);
-  __syncthreads();
-  if (lane == 0) red[warp] = v;
-  __syncthreads();
-  return warp_sum(lane < (int)(blockDim.x >> 5) ? red[lane] : 0.0);
+// split cluster barrier: arrive after this CTA's writes, wait before reading
+// the other CTAs' shared memory
+__device__ __forceinline__ void cluster_arrive_release() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait_acquire() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
 // order-preserving float -> uint32 map; NaN sorts below everything
@@ -61,9 +78,10 @@ __device__ __forceinline__ uint32_t score_key(float f) {
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
-constexpr int kPlanILP = 8;     // row elements per thread per tile (independent chains)
-constexpr int kBuckets = 2048;  // bucket-select histogram bins (2 per thread)
-constexpr int kCandCap = 1024;  // members of the boundary bucket ranked exactly
+constexpr int kPW = kPlanThreads / 32;  // warps per CTA
+constexpr int kPlanILP = 4;             // row elements per thread per tile (independent chains)
+constexpr int kBuckets = 2048;          // bucket-select histogram bins
+constexpr int kCandCap = 1024;          // members of the boundary bucket ranked exactly
 
 // bucket of a content score: floor((cmx - s) * scale), clamped to the last
 // bucket (which also takes NaN and -inf); non-decreasing as s decreases
@@ -73,209 +91,383 @@ __device__ __forceinline__ int bucket_of(float s, float cmx, float scale) {
   return u <= 0.f ? 0 : (int)u;
 }
 
+// per-CTA partials read by the other CTAs of the cluster
+struct PlanPart {
+  float mx, cmx;       // slice max, slice content max
+  double csum, csq;    // content sum / sum of squares
+  float M;             // max z of the slice (softmax partials are relative to it)
+  double Z, A;         // sum e^(z - M), sum e^(z - M) (z - M) over the slice
+  int ncand;           // boundary-bucket candidates gathered by this CTA
+  int nfix;            // blocks this CTA selected before the candidates
+  int n_eq;            // radix path: keys equal to the threshold
+  int n_sel;           // radix path: selected blocks of the slice
+};
+
+// Slot words carry this tag in their high half; the estimator clears every
+// slot to 0 before the plan kernel starts, so a tagged word is this call's.
+constexpr uint32_t kSlotTag = 0xADA0B200u;
+
+// block-wide sum of two doubles; every thread gets the result
+__device__ __forceinline__ void block_sum2(double& a, double& b, double* ra, double* rb) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  a = warp_sum(a);
+  b = warp_sum(b);
+  __syncthreads();  // ra / rb may still be read by a previous reduction
+  if (lane == 0) {
+    ra[warp] = a;
+    rb[warp] = b;
+  }
+  __syncthreads();
+  a = warp_sum(lane < kPW ? ra[lane] : 0.0);
+  b = warp_sum(lane < kPW ? rb[lane] : 0.0);
+}
+
+// exclusive prefix over cluster ranks of an int field, read with one remote
+// load per lane (lane r reads rank r); every lane gets its own prefix and the
+// total in `tot`
+__device__ __forceinline__ int rank_prefix(int v, int& tot) {
+  const int lane = threadIdx.x & 31;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  tot = __shfl_sync(0xffffffffu, x, 31);
+  return x - v;
+}
+
 template <bool SMEM>
 __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanParams p) {
   extern __shared__ __align__(16) uint32_t sm[];
-  __shared__ uint32_t hist[kBuckets];
-  __shared__ int s_digit, s_above, s_ncand;
-  __shared__ int scan_scratch[33];
-  __shared__ float fred[33], gred[33];
-  __shared__ double dred[33], dred2[33];
-  __shared__ double s_sumw;
-  __shared__ int cand_idx[kCandCap];
+  __shared__ __align__(16) uint32_t hist[kBuckets];   // this CTA's histogram (read by the cluster)
+  __shared__ __align__(16) uint32_t ghist[kBuckets];  // the cluster's histogram
+  __shared__ int cand_idx[kCandCap];      // this CTA's boundary candidates (read by the cluster)
   __shared__ uint32_t cand_key[kCandCap];
+  __shared__ int all_idx[kCandCap];       // every candidate of the cluster, rank-major
+  __shared__ uint32_t all_key[kCandCap];
+  __shared__ PlanPart part;
+  __shared__ int s_digit, s_above, s_ncand, s_nfix;
+  __shared__ int s_off[kPlanMaxCluster + 1], s_fix[kPlanMaxCluster], s_taken[kPlanMaxCluster];
+  __shared__ int scan_scratch[33];
+  __shared__ float2 wpart[kPW];
+  __shared__ float wm_s[kPW];
+  __shared__ double wd[kPW][4];
+  __shared__ double dred[kPW], dred2[kPW];
+  __shared__ double s_sumw, s_w;
 
+  cg::cluster_group cl = cg::this_cluster();
+  const int C = p.csize;
+  const int rank = (int)cl.block_rank();
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  // ballot words are written 32 at a time: round the word count up to 32
-  const int nw_alloc = (p.nw_max + 31) / 32 * 32;
-  uint32_t* keys = sm;                                        // [nw_alloc * 32] (SMEM only)
-  float* ecache = reinterpret_cast<float*>(sm + (SMEM ? nw_alloc * 32 : 0));  // exp(z - zmax)
-  uint32_t* wsel = reinterpret_cast<uint32_t*>(ecache) + (p.ecache ? nw_alloc * 32 : 0);
-  uint32_t* weq = wsel + nw_alloc;                            // [nw_alloc]
+  const int slice_cap = p.slice_cap;
+  const int nwl_alloc = (slice_cap / 32 + kPW - 1) / kPW * kPW;  // ballot words, whole passes
+  uint32_t* keys = sm;                                                     // [slice_cap] (SMEM)
+  float* ecache = reinterpret_cast<float*>(sm + (SMEM ? slice_cap : 0));   // [slice_cap] (ecache)
+  uint32_t* wsel = reinterpret_cast<uint32_t*>(ecache) + (p.ecache ? slice_cap : 0);
+  uint32_t* weq = wsel + nwl_alloc;
+  const PlanPart* lane_part = cl.map_shared_rank(&part, lane < C ? lane : 0);  // rank `lane`
 
+  const int group = blockIdx.x / C;
+  const int h = group % p.Hq;
+  const int slot_seq = group / p.Hq;
+  // sequence lengths are inputs of the whole step (the estimator never writes
+  // them): read before waiting for it
+  const int S_first = slot_seq < p.B ? seq_len_of(p.seq_lens, slot_seq, p.max_seq_len) : 0;
   pdl_wait();
-  // per-call tag, never 0 (the estimator cleared every tag to 0)
-  const uint32_t ep = (*reinterpret_cast<const volatile uint32_t*>(p.epoch) & 0x7FFFFFFFu) | 0x80000000u;
-  const int h = blockIdx.x % p.Hq;
-  const int slot_seq = blockIdx.x / p.Hq;
 
   for (int b0 = 0; b0 < p.B; b0 += p.seqs_per_round) {
     const int b = b0 + slot_seq;
-    if (b >= p.B) break;
+    if (b >= p.B) break;  // uniform over the cluster
     const int row = b * p.Hq + h;
-    int S = seq_len_of(p.seq_lens, b, p.max_seq_len);
+    int S = b0 == 0 ? S_first : seq_len_of(p.seq_lens, b, p.max_seq_len);
     if (S < 0 || S > p.max_seq_len) S = 0;  // reported by the estimator
     const int nb = ceil_div(S, p.bs);
-    const int nw = ceil_div(nb, 32);
+    const int L = (ceil_div(nb, C) + 31) / 32 * 32;
+    const int lo = imin(nb, rank * L), hi = imin(nb, lo + L);
+    const int n = hi - lo;
+    const int nwl = ceil_div(n, 32);
     const float* srow = p.scores + (int64_t)row * p.score_stride;
 
-    auto val = [&](int i) -> float { return SMEM ? __uint_as_float(keys[i]) : srow[i]; };
+    auto val = [&](int li) -> float { return SMEM ? __uint_as_float(keys[li]) : srow[lo + li]; };
     const int sink = imin(p.cfg.n_sink, nb), local = imin(p.cfg.n_local, nb);
     auto forced = [&](int i) -> bool { return i < sink || i >= nb - local; };
 
-    // ---- load the row (staged in shared memory) and its statistics in one pass:
-    //      max (softmax), content max / mean / spread (top-k buckets) ----
+    // ---- 1. load the slice: statistics and per-thread softmax partials ----
+    // Each thread keeps (m_t, z_t, a_t) = (max z, sum e^(z - m_t),
+    // sum e^(z - m_t) (z - m_t)) over its blocks, rescaled when m_t grows;
+    // e^(z - m_t) is cached when the slice is one tile (m_t is then final).
+    const bool adaptive = nb >= 2 && p.cfg.policy == ADAKV_POLICY_ADAPTIVE;
+    const float Tf = (float)(p.cfg.temperature > 1e-6 ? p.cfg.temperature : 1e-6);
+    const bool unit_t = (Tf == 1.0f);  // s / 1 == s exactly: skip the division
+    auto zof = [&](float v) -> float { return unit_t ? v : __fdiv_rn(v, Tf); };
+    const bool one_tile = n <= kPlanThreads * kPlanILP;
+    const bool ec = p.ecache && one_tile;
     float mx = -INFINITY, cmx = -INFINITY, csum_f = 0.f, csq_f = 0.f;
-    for (int base = 0; base < nb; base += kPlanThreads * kPlanILP) {
+    float m_t = -INFINITY, z_t = 0.f, a_t = 0.f;
+    for (int base = 0; base < n; base += kPlanThreads * kPlanILP) {
       float v[kPlanILP];
 #pragma unroll
       for (int r = 0; r < kPlanILP; ++r) {
-        const int i = base + r * kPlanThreads + tid;
-        v[r] = i < nb ? srow[i] : -INFINITY;
+        const int li = base + r * kPlanThreads + tid;
+        v[r] = li < n ? srow[lo + li] : -INFINITY;
       }
+      float tm = -INFINITY;
 #pragma unroll
       for (int r = 0; r < kPlanILP; ++r) {
-        const int i = base + r * kPlanThreads + tid;
-        if (i < nb) {
-          if (SMEM) keys[i] = __float_as_uint(v[r]);
+        const int li = base + r * kPlanThreads + tid;
+        if (li < n) {
+          if (SMEM) keys[li] = __float_as_uint(v[r]);
           mx = fmaxf(mx, v[r]);
-          if (!forced(i)) {
+          tm = fmaxf(tm, zof(v[r]));
+          if (!forced(lo + li)) {
             cmx = fmaxf(cmx, v[r]);
             csum_f += v[r];
             csq_f = fmaf(v[r], v[r], csq_f);
           }
         }
       }
+      if (adaptive && tm > m_t) {
+        if (m_t > -INFINITY) {
+          const float sc = expf(m_t - tm);
+          a_t = sc * fmaf(z_t, m_t - tm, a_t);
+          z_t *= sc;
+        }
+        m_t = tm;
+      }
+      if (adaptive) {
+#pragma unroll
+        for (int r = 0; r < kPlanILP; ++r) {
+          const int li = base + r * kPlanThreads + tid;
+          if (li < n) {
+            const float d = zof(v[r]) - m_t;
+            const float e = expf(d);
+            if (ec) ecache[li] = e;
+            z_t += e;
+            if (e > 0.f) a_t = fmaf(e, d, a_t);
+          }
+        }
+      }
     }
+    for (int t = tid; t < kBuckets; t += kPlanThreads) hist[t] = 0u;
+    if (tid < kPlanMaxCluster) s_taken[tid] = 0;
+    if (tid == 0) {
+      s_ncand = 0;
+      s_nfix = 0;
+    }
+    // warp partials (softmax partials rescaled to the warp max), then one
+    // fold of the warps by warp 0, then the cluster
     {
-      mx = warp_max(mx);
-      cmx = warp_max(cmx);
-      double csum_w = warp_sum((double)csum_f), csq_w = warp_sum((double)csq_f);
-      __syncthreads();
+      const float wm = warp_max(m_t);
+      double zw = 0.0, aw = 0.0;
+      if (adaptive && m_t > -INFINITY) {
+        const double sc = exp((double)m_t - (double)wm);
+        zw = (double)z_t * sc;
+        aw = sc * ((double)a_t + (double)z_t * ((double)m_t - (double)wm));
+      }
+      zw = warp_sum(zw);
+      aw = warp_sum(aw);
+      const float wmx = warp_max(mx), wcmx = warp_max(cmx);
+      const double wsum = warp_sum((double)csum_f), wsq = warp_sum((double)csq_f);
       if (lane == 0) {
-        fred[warp] = mx;
-        gred[warp] = cmx;
-        dred[warp] = csum_w;
-        dred2[warp] = csq_w;
+        wpart[warp] = make_float2(wmx, wcmx);
+        wm_s[warp] = wm;
+        wd[warp][0] = zw;
+        wd[warp][1] = aw;
+        wd[warp][2] = wsum;
+        wd[warp][3] = wsq;
       }
-      __syncthreads();  // also publishes the staged row
-      mx = warp_max(fred[lane]);
-      cmx = warp_max(gred[lane]);
     }
-    const double csum = warp_sum(dred[lane]), csq = warp_sum(dred2[lane]);
-
-    // ---- entropy (adakv/budget.py:28-37) ----
-    float ent = 0.f;
-    if (nb >= 2 && p.cfg.policy == ADAKV_POLICY_ADAPTIVE) {
-      const float m = mx;
-      const float Tf = (float)(p.cfg.temperature > 1e-6 ? p.cfg.temperature : 1e-6);
-      const bool unit_t = (Tf == 1.0f);  // s / 1 == s exactly: skip the division
-      const float zmax = unit_t ? m : __fdiv_rn(m, Tf);  // max(s / T) == max(s) / T (monotone rounding)
-      auto ez = [&](int i) -> float {
-        const float z = unit_t ? val(i) : __fdiv_rn(val(i), Tf);
-        return expf(z - zmax);
-      };
-      // per-thread partial sums in float (at most a few dozen terms each), the
-      // cross-thread sums in double
-      float zpart = 0.f;
-      for (int base = 0; base < nb; base += kPlanThreads * kPlanILP) {
-#pragma unroll
-        for (int r = 0; r < kPlanILP; ++r) {
-          const int i = base + r * kPlanThreads + tid;
-          if (i < nb) {
-            const float e = ez(i);
-            if (p.ecache) ecache[i] = e;
-            zpart += e;
-          }
-        }
+    __syncthreads();  // also publishes the staged slice
+    if (warp == 0) {
+      const bool in = lane < kPW;
+      const float M = warp_max(in ? wm_s[lane] : -INFINITY);
+      double z = 0.0, a = 0.0;
+      if (in && wm_s[lane] > -INFINITY) {
+        const double sc = exp((double)wm_s[lane] - (double)M);
+        z = wd[lane][0] * sc;
+        a = sc * (wd[lane][1] + wd[lane][0] * ((double)wm_s[lane] - (double)M));
       }
-      const float Z = (float)block_sum_1s((double)zpart, dred);
-      float hpart = 0.f;
-      for (int base = 0; base < nb; base += kPlanThreads * kPlanILP) {
-#pragma unroll
-        for (int r = 0; r < kPlanILP; ++r) {
-          const int i = base + r * kPlanThreads + tid;
-          if (i < nb) {
-            const float e = p.ecache ? ecache[i] : ez(i);
-            const float pi = __fdiv_rn(e, Z);
-            hpart += __fmul_rn(pi, logf(fmaxf(pi, 1e-9f)));
-          }
-        }
+      z = warp_sum(z);
+      a = warp_sum(a);
+      const float m1 = warp_max(in ? wpart[lane].x : -INFINITY);
+      const float m2 = warp_max(in ? wpart[lane].y : -INFINITY);
+      const double cs = warp_sum(in ? wd[lane][2] : 0.0);
+      const double cq = warp_sum(in ? wd[lane][3] : 0.0);
+      if (lane == 0) {
+        part.mx = m1;
+        part.cmx = m2;
+        part.csum = cs;
+        part.csq = cq;
+        part.M = M;
+        part.Z = z;
+        part.A = a;
       }
-      const float hsum = (float)block_sum_1s((double)hpart, dred);
-      ent = -hsum;
     }
-    auto weight_of = [&](float e) -> double {  // adakv/budget.py:36-37, float64 after the division
-      return (double)e / log((double)imax(nb, 2)) + 1e-6;
-    };
-    const double w = (nb >= 2 && p.cfg.policy == ADAKV_POLICY_ADAPTIVE) ? weight_of(ent) : 0.0;
+    cl.sync();  // (1) slice statistics and softmax partials of every CTA
+    double csum, csq, Ztot = 0.0, Atot = 0.0;
+    {
+      const bool in = lane < C;
+      mx = warp_max(in ? lane_part->mx : -INFINITY);
+      cmx = warp_max(in ? lane_part->cmx : -INFINITY);
+      csum = warp_sum(in ? lane_part->csum : 0.0);
+      csq = warp_sum(in ? lane_part->csq : 0.0);
+      if (adaptive) {
+        const float Mr = in ? lane_part->M : -INFINITY;
+        const float M = warp_max(Mr);
+        double z = 0.0, a = 0.0;
+        if (in && Mr > -INFINITY) {
+          const double zr = lane_part->Z, ar = lane_part->A;
+          const double sc = exp((double)Mr - (double)M);
+          z = zr * sc;
+          a = sc * (ar + zr * ((double)Mr - (double)M));
+        }
+        Ztot = warp_sum(z);
+        Atot = warp_sum(a);
+      }
+    }
 
-    // ---- publish (entropy, tag) in one 64-bit release store ----
-    unsigned long long* myslot = &p.slots[row].word;
-    if (tid == 0) st_release_u64(myslot, ((uint64_t)ep << 32) | (uint64_t)__float_as_uint(ent));
-
-    // ---- bucket histogram (independent of the budget) while warp 0 waits ----
+    // ---- top-k bucket geometry (independent of the budget) ----
     const double nc_d = (double)(nb - imin(nb, sink + local));
     const double mean_c = nc_d > 0 ? csum / nc_d : 0.0;
     const double var_c = nc_d > 0 ? csq / nc_d - mean_c * mean_c : 0.0;
     const double range = (double)cmx - mean_c + (var_c > 0.0 ? sqrt(var_c) : 0.0);
     const bool buckets_ok = isfinite(cmx) && range > 0.0 && isfinite(range);
     const float scale = buckets_ok ? (float)((double)(kBuckets - 1) / range) : 0.f;
-    for (int t = tid; t < kBuckets; t += kPlanThreads) hist[t] = 0u;
+
+    // ---- 2. clamp correction of this slice + the slice's histogram ----
+    // With zmax = max z (= max(s) / T, monotone rounding), d = z - zmax and
+    // e = exp(d) as the reference computes them, H = log Z - A / Z - Cc / Z
+    // where Cc sums e (log(1e-9) - d + log Z) over blocks with e / Z < 1e-9.
+    const float zmax = unit_t ? mx : __fdiv_rn(mx, Tf);
+    float cp = 0.f;
+    {
+      const float Zf = (float)Ztot;
+      const float logZ = adaptive ? (float)log(Ztot) : 0.f;
+      const float ln_floor = logf(1e-9f);
+      const float pre = 2e-9f * Zf;  // p < 1e-9 implies e < 2e-9 * Z
+      const float sc_t = (adaptive && m_t > -INFINITY) ? expf(m_t - zmax) : 0.f;
+      for (int base = 0; base < n; base += kPlanThreads * kPlanILP) {
+#pragma unroll
+        for (int r = 0; r < kPlanILP; ++r) {
+          const int li = base + r * kPlanThreads + tid;
+          if (li < n) {
+            const float v = val(li);
+            if (adaptive) {
+              const float d = __fsub_rn(zof(v), zmax);
+              const float e = ec ? ecache[li] * sc_t : expf(d);
+              if (e > 0.f && e < pre && __fdiv_rn(e, Zf) < 1e-9f)
+                cp = fmaf(e, ln_floor - d + logZ, cp);
+            }
+            if (buckets_ok && !forced(lo + li)) {
+              const int bk = bucket_of(v, cmx, scale);
+              if (bk < kBuckets - 1) atomicAdd(&hist[bk], 1u);
+            }
+          }
+        }
+      }
+    }
+    double t_mine = 0.0;
+    if (adaptive) {
+      double c2 = cp, z2 = 0.0;
+      block_sum2(c2, z2, dred, dred2);
+      // this CTA's share of H: CTA 0 carries log Z - A / Z, every CTA -Cc_r / Z
+      t_mine = (rank == 0 ? log(Ztot) - Atot / Ztot : 0.0) - c2 / Ztot;
+    }
     __syncthreads();
+    cluster_arrive_release();  // (2) this CTA's histogram is complete
+    unsigned long long* slots = &p.slots[0].word;
+    if (tid == 0) {
+      const float thi = (float)t_mine;
+      const float tlo = (float)(t_mine - (double)thi);
+      const size_t at = ((size_t)row * C + rank) * 2;
+      st_relaxed_u64(slots + at, ((uint64_t)kSlotTag << 32) | (uint64_t)__float_as_uint(thi));
+      st_relaxed_u64(slots + at + 1, ((uint64_t)kSlotTag << 32) | (uint64_t)__float_as_uint(tlo));
+    }
+    auto weight_of = [&](double e) -> double {  // adakv/budget.py:36-37, float64 after the division
+      return (double)(float)e / log((double)imax(nb, 2)) + 1e-6;
+    };
+
+    // ---- exchange across the sequence's heads (warp 0) / merge histograms ----
     if (warp == 0) {
       const uint64_t t0 = globaltimer_ns();
       bool ok = false;
-      float ents[4];  // Hq <= 128
+      double ents[4];  // Hq <= 128
       while (true) {
         bool mine = true;
 #pragma unroll
         for (int q4 = 0; q4 < 4; ++q4) {
           const int hh = lane + q4 * 32;
+          double e = 0.0;
           if (hh < p.Hq) {
-            const uint64_t v = ld_acquire_u64(&p.slots[b * p.Hq + hh].word);
-            mine &= ((uint32_t)(v >> 32) == ep);
-            ents[q4] = __uint_as_float((uint32_t)v);
+            const unsigned long long* hs = slots + (size_t)(b * p.Hq + hh) * C * 2;
+#pragma unroll
+            for (int r = 0; r < kPlanMaxCluster; ++r) {
+              if (r < C) {
+                const uint64_t v0 = ld_relaxed_u64(hs + 2 * r);
+                const uint64_t v1 = ld_relaxed_u64(hs + 2 * r + 1);
+                mine &= ((uint32_t)(v0 >> 32) == kSlotTag) && ((uint32_t)(v1 >> 32) == kSlotTag);
+                e += (double)__uint_as_float((uint32_t)v0) + (double)__uint_as_float((uint32_t)v1);
+              }
+            }
           }
+          ents[q4] = e;
         }
         ok = __all_sync(0xffffffffu, mine);
         if (ok || globaltimer_ns() - t0 > kWaitLimitNs) break;
       }
       if (!ok && lane == 0) report(p.status, ADAKV_ST_WAIT_TIMEOUT);
-      double part = 0.0;
+      double ps = 0.0;
 #pragma unroll
       for (int q4 = 0; q4 < 4; ++q4) {
         const int hh = lane + q4 * 32;
-        if (hh < p.Hq && p.cfg.policy == ADAKV_POLICY_ADAPTIVE && nb >= 2) part += weight_of(ents[q4]);
-      }
-      part = warp_sum(part);  // fixed xor tree: every CTA of the sequence gets the same sum
-      if (lane == 0) s_sumw = part;
-    } else if (buckets_ok) {
-      for (int i = tid - 32; i < nb; i += kPlanThreads - 32) {
-        if (!forced(i)) {
-          const int bk = bucket_of(val(i), cmx, scale);
-          if (bk < kBuckets - 1) atomicAdd(&hist[bk], 1u);
+        if (hh < p.Hq && adaptive) {
+          const double wv = weight_of(ents[q4]);
+          ps += wv;
+          if (hh == h) s_w = wv;
         }
+      }
+      ps = warp_sum(ps);  // fixed xor tree: every CTA of the sequence gets the same sum
+      if (lane == 0) s_sumw = ps;
+      cluster_wait_acquire();
+    } else {
+      cluster_wait_acquire();  // every histogram of the cluster is complete
+      for (int j = tid - 32; buckets_ok && j < kBuckets / 4; j += kPlanThreads - 32) {
+        uint4 acc = make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+        for (int r = 0; r < kPlanMaxCluster; ++r) {
+          if (r < C) {
+            const uint4 x = reinterpret_cast<const uint4*>(cl.map_shared_rank(hist, r))[j];
+            acc.x += x.x;
+            acc.y += x.y;
+            acc.z += x.z;
+            acc.w += x.w;
+          }
+        }
+        reinterpret_cast<uint4*>(ghist)[j] = acc;
       }
     }
     __syncthreads();
     pdl_launch_dependents();  // every CTA is past the exchange: the attend grid may launch
     const SeqBudget sbud = seq_budget(nb, p.cfg);
+    const double w = adaptive ? s_w : 0.0;
     const int K = imin(head_count(sbud, p.cfg, w, s_sumw, p.Hq), p.table_width);
     const int n_forced = (sink + local >= nb) ? nb : sink + local;
     const int Kc = K - n_forced;  // content blocks to pick
+    const bool all = K >= nb;
 
-    // ---- top-k ----
-    // Bucket select: content block i goes to bucket floor((cmx - s_i) * scale),
-    // a non-decreasing function of -s_i (correctly rounded subtraction and
-    // multiplication are monotone), so every block of a lower bucket outranks
-    // every block of a higher one.  Buckets span [cmx - range, cmx] with
-    // range = cmx - mean + sd, fine near the k-th score; blocks past the range
-    // share the last bucket.  One histogram pass finds the bucket holding the
-    // Kc-th block; its few members are ranked exactly by (score, lowest index).
-    // A full MSB radix select takes over when the boundary falls in the last
-    // bucket or holds too many members.
+    // ---- 4. top-k ----
     bool use_radix = false;
     int jstar = kBuckets, need_b = 0;
-    if (K < nb && Kc > 0) {
+    if (!all && Kc > 0) {
       use_radix = !buckets_ok;
       if (!use_radix) {
-        // find the bucket holding the Kc-th content block (buckets ascend = scores descend)
+        // the bucket holding the Kc-th content block (buckets ascend = scores descend)
         constexpr int BPT = kBuckets / kPlanThreads;
         uint32_t cb[BPT], tot = 0;
 #pragma unroll
         for (int e = 0; e < BPT; ++e) {
-          cb[e] = hist[tid * BPT + e];
+          cb[e] = ghist[tid * BPT + e];
           tot += cb[e];
         }
         const int before = block_exclusive_scan((int)tot, scan_scratch);
@@ -295,41 +487,96 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanParams p) {
         }
         __syncthreads();
         jstar = s_digit;
-        if (jstar >= kBuckets - 1 || (int)hist[jstar] > kCandCap) {
-          use_radix = true;
-        } else {
-          need_b = Kc - s_above;
-          if (tid == 0) s_ncand = 0;
-          __syncthreads();
-          for (int base = 0; base < nb; base += kPlanThreads * kPlanILP) {
-#pragma unroll
-            for (int r = 0; r < kPlanILP; ++r) {
-              const int i = base + r * kPlanThreads + tid;
-              if (i < nb && !forced(i)) {
-                const float v = val(i);
-                if (bucket_of(v, cmx, scale) == jstar) {
-                  const int slot = atomicAdd(&s_ncand, 1);
-                  cand_idx[slot] = i;
-                  cand_key[slot] = score_key(v);
-                }
-              }
-            }
-          }
-          __syncthreads();
-        }
+        if (jstar >= kBuckets - 1 || (int)ghist[jstar] > kCandCap) use_radix = true;
+        else need_b = Kc - s_above;
       }
     }
+    const bool bucketed = !all && Kc > 0 && !use_radix;
+    if (!use_radix) {
+      // selected: forced blocks, every content block of a bucket above jstar;
+      // the members of bucket jstar are candidates, ranked across the cluster
+      for (int j = 0; j * kPlanThreads < n; ++j) {
+        const int li = j * kPlanThreads + tid;
+        bool sel = false;
+        if (li < n) {
+          if (all || forced(lo + li)) {
+            sel = true;
+          } else if (bucketed) {
+            const float v = val(li);
+            const int bk = bucket_of(v, cmx, scale);
+            sel = bk < jstar;
+            if (bk == jstar) {
+              const int slot = atomicAdd(&s_ncand, 1);
+              cand_idx[slot] = lo + li;
+              cand_key[slot] = score_key(v);
+            }
+          }
+        }
+        const uint32_t bsel = __ballot_sync(0xffffffffu, sel);
+        if (lane == 0) {
+          wsel[j * kPW + warp] = bsel;
+          weq[j * kPW + warp] = 0u;
+          if (bsel) atomicAdd(&s_nfix, __popc(bsel));
+        }
+      }
+      __syncthreads();
+      if (tid == 0) {
+        part.ncand = s_ncand;
+        part.nfix = s_nfix;
+      }
+    }
+    cl.sync();  // (3) candidates and counts of every CTA
 
-    uint32_t T = 0;
-    int need = 0;  // ties at T resolved in index order (radix path only)
-    if (use_radix) {
+    int pos = 0;  // this CTA's first table position
+    if (!use_radix) {
+      if (warp == 0) {
+        const bool in = lane < C;
+        int tot;
+        const int nc = in ? lane_part->ncand : 0;
+        const int off = rank_prefix(nc, tot);
+        if (in) {
+          s_off[lane] = off;
+          s_fix[lane] = lane_part->nfix;
+        }
+        if (lane == 0) s_off[C] = tot;
+      }
+      __syncthreads();
+      const int ntot = bucketed ? s_off[C] : 0;
+      // copy every CTA's candidates (one remote load per entry)
+      for (int u = tid; u < ntot; u += kPlanThreads) {
+        int r = 0;
+        while (r + 1 < C && s_off[r + 1] <= u) ++r;
+        const int t = u - s_off[r];
+        all_key[u] = cl.map_shared_rank(cand_key, r)[t];
+        all_idx[u] = cl.map_shared_rank(cand_idx, r)[t];
+      }
+      __syncthreads();
+      for (int u = tid; u < ntot; u += kPlanThreads) {
+        const uint32_t ku = all_key[u];
+        const int iu = all_idx[u];
+        int rk = 0;
+        for (int c = 0; c < ntot; ++c) {
+          const uint32_t kc = all_key[c];
+          rk += (kc > ku) || (kc == ku && all_idx[c] < iu);
+        }
+        if (rk < need_b) {
+          int r = 0;
+          while (r + 1 < C && s_off[r + 1] <= u) ++r;
+          atomicAdd(&s_taken[r], 1);
+          if (r == rank) atomicOr(&wsel[(iu - lo) >> 5], 1u << ((iu - lo) & 31));
+        }
+      }
+      __syncthreads();
+      for (int r = 0; r < rank; ++r) pos += s_fix[r] + s_taken[r];
+    } else {
+      // ---- radix select over the cluster (fallback) ----
       if (SMEM) {
-        for (int i = tid; i < nb; i += kPlanThreads)
-          keys[i] = forced(i) ? 0xFFFFFFFFu : score_key(__uint_as_float(keys[i]));
+        for (int li = tid; li < n; li += kPlanThreads)
+          keys[li] = forced(lo + li) ? 0xFFFFFFFFu : score_key(__uint_as_float(keys[li]));
         __syncthreads();
       }
-      auto key = [&](int i) -> uint32_t {
-        return SMEM ? keys[i] : (forced(i) ? 0xFFFFFFFFu : score_key(srow[i]));
+      auto key = [&](int li) -> uint32_t {
+        return SMEM ? keys[li] : (forced(lo + li) ? 0xFFFFFFFFu : score_key(srow[lo + li]));
       };
       uint32_t prefix = 0, pmask = 0;
       int rem = K;
@@ -338,18 +585,25 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanParams p) {
         const int shift = 24 - 8 * pass;
         if (tid < 256) hist[tid] = 0;
         __syncthreads();
-        for (int i = tid; i < nb; i += kPlanThreads) {
-          const uint32_t k = key(i);
+        for (int li = tid; li < n; li += kPlanThreads) {
+          const uint32_t k = key(li);
           if ((k & pmask) == prefix) atomicAdd(&hist[(k >> shift) & 0xFFu], 1u);
         }
-        __syncthreads();
+        cl.sync();  // every CTA's digit histogram complete
         if (warp == 0) {
           uint32_t c[8], tot = 0;
 #pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            c[e] = hist[255 - 8 * lane - e];
-            tot += c[e];
+          for (int e = 0; e < 8; ++e) c[e] = 0;
+#pragma unroll
+          for (int r = 0; r < kPlanMaxCluster; ++r) {
+            if (r < C) {
+              const uint32_t* hr = cl.map_shared_rank(hist, r);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) c[e] += hr[255 - 8 * lane - e];
+            }
           }
+#pragma unroll
+          for (int e = 0; e < 8; ++e) tot += c[e];
           uint32_t incl = tot;
 #pragma unroll
           for (int o = 1; o < 32; o <<= 1) {
@@ -370,64 +624,38 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanParams p) {
             }
           }
         }
-        __syncthreads();
+        cl.sync();  // digit read by every CTA before any histogram is cleared again
         rem -= s_above;
         prefix |= (uint32_t)s_digit << shift;
         pmask |= 0xFFu << shift;
       }
-      T = prefix;
-      need = rem;
-      for (int j = 0; j * kPlanThreads < nb; ++j) {
-        const int i = j * kPlanThreads + tid;
-        const bool valid = i < nb;
-        const uint32_t k = valid ? key(i) : 0u;
+      const uint32_t T = prefix;
+      const int need = rem;  // ties at T resolved in index order
+      for (int j = 0; j * kPlanThreads < n; ++j) {
+        const int li = j * kPlanThreads + tid;
+        const bool valid = li < n;
+        const uint32_t k = valid ? key(li) : 0u;
         const uint32_t bgt = __ballot_sync(0xffffffffu, valid && k > T);
         const uint32_t beq = __ballot_sync(0xffffffffu, valid && k == T);
         if (lane == 0) {
-          wsel[j * 32 + warp] = bgt;
-          weq[j * 32 + warp] = beq;
-        }
-      }
-    } else {
-      // selected: forced blocks, every content block of a bucket above jstar,
-      // and the need_b best members of bucket jstar
-      const bool all = K >= nb;
-      for (int j = 0; j * kPlanThreads < nb; ++j) {
-        const int i = j * kPlanThreads + tid;
-        bool sel = false;
-        if (i < nb) {
-          if (all || forced(i)) sel = true;
-          else if (Kc > 0 && jstar < kBuckets) sel = bucket_of(val(i), cmx, scale) < jstar;
-        }
-        const uint32_t bsel = __ballot_sync(0xffffffffu, sel);
-        if (lane == 0) {
-          wsel[j * 32 + warp] = bsel;
-          weq[j * 32 + warp] = 0u;
+          wsel[j * kPW + warp] = bgt;
+          weq[j * kPW + warp] = beq;
         }
       }
       __syncthreads();
-      if (!all && Kc > 0 && jstar < kBuckets) {
-        const int nc = s_ncand;
-        for (int t = tid; t < nc; t += kPlanThreads) {
-          const uint32_t kt = cand_key[t];
-          const int it = cand_idx[t];
-          int rank = 0;
-          for (int c = 0; c < nc; ++c) {
-            const uint32_t kc = cand_key[c];
-            rank += (kc > kt) || (kc == kt && cand_idx[c] < it);
-          }
-          if (rank < need_b) atomicOr(&wsel[it >> 5], 1u << (it & 31));
-        }
-      }
-    }
-    __syncthreads();
-    const int wpt = ceil_div(nw, kPlanThreads);  // words per thread (consecutive)
-    const int w0 = imin(tid * wpt, nw), w1 = imin(w0 + wpt, nw);
-    int n_sel = 0;
-    if (use_radix) {
+      const int wpt = ceil_div(nwl, kPlanThreads);
+      const int w0 = imin(tid * wpt, nwl), w1 = imin(w0 + wpt, nwl);
       int n_eq = 0;
       for (int wi = w0; wi < w1; ++wi) n_eq += __popc(weq[wi]);
       int eq_before = block_exclusive_scan(n_eq, scan_scratch);
+      if (tid == 0) part.n_eq = scan_scratch[32];
+      cl.sync();
+      {
+        int tot;
+        const int pre = rank_prefix(lane < C ? lane_part->n_eq : 0, tot);
+        eq_before += __shfl_sync(0xffffffffu, pre, rank);
+      }
+      int n_sel = 0;
       for (int wi = w0; wi < w1; ++wi) {
         uint32_t e = weq[wi];
         const int take = imax(0, imin(__popc(e), need - eq_before));
@@ -441,62 +669,95 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanParams p) {
         wsel[wi] = sw;
         n_sel += __popc(sw);
       }
-    } else {
-      for (int wi = w0; wi < w1; ++wi) n_sel += __popc(wsel[wi]);
+      const int nb4 = block_exclusive_scan(n_sel, scan_scratch);
+      (void)nb4;
+      if (tid == 0) part.n_sel = scan_scratch[32];
+      cl.sync();
+      int tot;
+      const int pre = rank_prefix(lane < C ? lane_part->n_sel : 0, tot);
+      pos = __shfl_sync(0xffffffffu, pre, rank);
+      __syncthreads();
     }
-    int pos = block_exclusive_scan(n_sel, scan_scratch);
+
+    // ---- 5. bitmap + ascending table ----
+    const int wpt = ceil_div(nwl, kPlanThreads);  // words per thread (consecutive)
+    const int w0 = imin(tid * wpt, nwl), w1 = imin(w0 + wpt, nwl);
+    int n_sel = 0;
+    for (int wi = w0; wi < w1; ++wi) n_sel += __popc(wsel[wi]);
+    pos += block_exclusive_scan(n_sel, scan_scratch);
     int* trow = p.block_table + (int64_t)row * p.table_width;
-    uint32_t* brow = p.bitmap + (int64_t)row * p.bm_words;
+    uint32_t* brow = p.bitmap + (int64_t)row * p.bm_words + lo / 32;
     for (int wi = w0; wi < w1; ++wi) {
       uint32_t s = wsel[wi];
       brow[wi] = s;
       while (s) {
         const int bit = __ffs(s) - 1;
         s &= s - 1u;
-        if (pos < p.table_width) trow[pos] = wi * 32 + bit;
+        if (pos < p.table_width) trow[pos] = lo + wi * 32 + bit;
         ++pos;
       }
     }
-    if (tid == 0) p.sel_lens[row] = nb > 0 ? K : 0;
+    if (rank == 0 && tid == 0) p.sel_lens[row] = nb > 0 ? K : 0;
     __syncthreads();  // shared buffers are reused by the next round
   }
+  cl.sync();  // no CTA leaves while another may still read its shared memory
   pdl_launch_dependents();
 }
 
-bool plan_ecache(int nb_max) { return nb_max <= kPlanECacheMax; }
-
-size_t plan_smem_bytes(int nb_max) {
-  const int nw_alloc = (ceil_div(imax(nb_max, 1), 32) + 31) / 32 * 32;
-  const bool smem_keys = nb_max <= kPlanSmemMaxKeys;
-  return (size_t)(smem_keys ? nw_alloc * 32 : 0) * 4 +
-         (size_t)(plan_ecache(nb_max) ? nw_alloc * 32 : 0) * 4 + (size_t)2 * nw_alloc * 4;
+PlanLayout plan_layout(int nb_max, int csize) {
+  PlanLayout l{};
+  l.csize = csize;
+  l.slice_cap = (ceil_div(imax(nb_max, 1), csize) + 31) / 32 * 32;
+  l.smem_keys = l.slice_cap <= kPlanSmemMaxKeys;
+  l.ecache = l.slice_cap <= kPlanECacheMax;
+  const int nwl_alloc = (l.slice_cap / 32 + kPW - 1) / kPW * kPW;
+  l.smem = (size_t)(l.smem_keys ? l.slice_cap : 0) * 4 + (size_t)(l.ecache ? l.slice_cap : 0) * 4 +
+           (size_t)2 * nwl_alloc * 4;
+  return l;
 }
 
 cudaError_t plan_kernels_init() {
   cudaError_t e = cudaFuncSetAttribute(plan_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)std::max(plan_smem_bytes(kPlanSmemMaxKeys),
-                                                     plan_smem_bytes(kPlanECacheMax)));
+                                       (int)kPlanSmemMax);
   if (e != cudaSuccess) return e;
-  return cudaFuncSetAttribute(plan_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              (int)plan_smem_bytes(kPlanMaxBlocks));
+  e = cudaFuncSetAttribute(plan_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)kPlanSmemMax);
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(plan_kernel<true>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(plan_kernel<false>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
 }
 
-int plan_ctas_per_sm(int nb_max) {
+int plan_active_clusters(const PlanLayout& l) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(l.csize, 1, 1);
+  cfg.blockDim = dim3(kPlanThreads, 1, 1);
+  cfg.dynamicSmemBytes = l.smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = l.csize;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
   int n = 0;
-  const size_t smem = plan_smem_bytes(nb_max);
-  if (nb_max <= kPlanSmemMaxKeys)
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, plan_kernel<true>, kPlanThreads, smem);
-  else
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, plan_kernel<false>, kPlanThreads, smem);
+  const cudaError_t e = l.smem_keys
+                            ? cudaOccupancyMaxActiveClusters(&n, plan_kernel<true>, &cfg)
+                            : cudaOccupancyMaxActiveClusters(&n, plan_kernel<false>, &cfg);
+  if (e != cudaSuccess) {
+    (void)cudaGetLastError();
+    return 0;
+  }
   return n;
 }
 
-cudaError_t launch_plan(const PlanParams& p, int nb_max, int grid, cudaStream_t st,
+cudaError_t launch_plan(const PlanParams& p, const PlanLayout& l, int grid, cudaStream_t st,
                         const LaunchOpts& o) {
-  const size_t smem = plan_smem_bytes(nb_max);
-  if (nb_max <= kPlanSmemMaxKeys)
-    return launch_ex(plan_kernel<true>, dim3(grid), dim3(kPlanThreads), smem, st, o, p);
-  return launch_ex(plan_kernel<false>, dim3(grid), dim3(kPlanThreads), smem, st, o, p);
+  LaunchOpts oc = o;
+  oc.cluster_x = (unsigned)l.csize;
+  if (l.smem_keys)
+    return launch_ex(plan_kernel<true>, dim3(grid), dim3(kPlanThreads), l.smem, st, oc, p);
+  return launch_ex(plan_kernel<false>, dim3(grid), dim3(kPlanThreads), l.smem, st, oc, p);
 }
 
 }  // namespace adakv
