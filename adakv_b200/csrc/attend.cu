@@ -5,23 +5,25 @@
 // of the reference kernel (adakv/kernels/block_sparse_decode.py:51-100) and of
 // the oracle (adakv/reference.py:76-80).
 //
-// One thread-block cluster per (sequence, KV head).  The g query heads of the
-// group select overlapping block sets; the cluster reads their selection
-// bitmaps, forms the union, and splits the union evenly over its CTAs, so every
-// selected K/V block is read from HBM exactly once for the whole group (the
-// split-KV axis).  Each CTA gathers its blocks with 16-byte cp.async copies
-// (zero-fill past seq_len) into a double-buffered shared-memory ring, and warp
-// group of the CTA (1-4 warps per query head) runs the online softmax of one
-// query head over the blocks whose head bit is set, round-robin between the
-// head's warps: a token row is spread over D*sizeof(T)/16 lanes, dot products
-// finish with xor shuffles, the lane keeps its 16-byte slice of the output.
-// The per-CTA partials (m, l, o) are merged across the cluster through
-// distributed shared memory -- no global scratch, no atomics, no second kernel.
+// Grid (SPLIT, Hkv, B).  The g query heads of a KV group select overlapping
+// block sets; every CTA of the group ORs their selection bitmaps into the
+// union and takes the SPLIT-th share of it (the split-KV axis), so each
+// selected K/V block is read from HBM exactly once for the whole group.  A CTA
+// gathers its blocks with 16-byte cp.async copies (zero-fill past seq_len)
+// into a two-stage shared-memory ring and computes online-softmax partials of
+// all g heads; each block is masked per head by the head's own selection.
+// Partials (m, l, o) go to the workspace; the last CTA of the group to finish
+// (an atomic arrival count, reset by that CTA) merges the SPLIT partials in
+// split order and writes out[b, h] for the group.  No CTA waits on another.
+//
+// Tensor-core path (bf16 / fp16): the g rows of the group are the M = 16
+// rows of an m16n8k16 MMA tile (attend_mma.cuh), 8 warps split the blocks of
+// a batch.  CUDA-core path (fp32): 1-4 warps per query head, a token row is
+// spread over D * 4 / 16 lanes and dot products finish with xor shuffles.
 //
 // HBM traffic: the union of the group's selected K/V blocks
-// (bs * D * sizeof(T) * 2 bytes per block) plus the selection bitmaps, q and out.
-#include <cooperative_groups.h>
-
+// (bs * D * sizeof(T) * 2 bytes per block) plus the bitmaps, q, out and the
+// partials (g * (D + 2) * 4 bytes per CTA, L2 resident).
 #include <type_traits>
 
 #include "attend_mma.cuh"
@@ -29,51 +31,42 @@
 
 namespace adakv {
 
-namespace cg = cooperative_groups;
-
-constexpr int kAttendMaxThreads = 512;  // g <= 16 warps
-
-__device__ __forceinline__ void cp_async_wait_one() {
-  asm volatile("cp.async.wait_group 1;" ::: "memory");
-}
+constexpr int kAttendMaxThreads = 512;  // CUDA-core path: g <= 16 warps
+constexpr int kAttendMmaWarps = 8;
 
 // shared-memory carve-up of one attend CTA (host and device agree on it)
 struct AttendSmem {
-  size_t kv, hw, uw, list, mask, wpart, part, total;
+  size_t kv, uw, list, mask, wpart, merge, total;
 };
 
-// Warps of one CTA.  Tensor-core path: every warp computes all query rows of a
-// block, so warps split the blocks (<= 64 / g warps keeps the per-warp
-// partials small).  CUDA-core path: 1-4 warps per query head.
+// Warps of one CTA: tensor-core path, kAttendMmaWarps split the blocks;
+// CUDA-core path, 1-4 warps per query head.
 __host__ __device__ inline int attend_warps(bool mma, int g) {
-  if (mma) {
-    int w = 64 / g;
-    return w > 16 ? 16 : (w < 4 ? 4 : w);
-  }
+  if (mma) return kAttendMmaWarps;
   int wph = 16 / g;
   wph = wph < 1 ? 1 : (wph > 4 ? 4 : wph);
   return g * wph;
 }
 
 __host__ __device__ inline AttendSmem attend_smem_layout(int elt, int D, int BS, int nslot, int g,
-                                                         int nw_max, int slice_cap, bool mma) {
+                                                         int nw_max, int slice_cap, int split,
+                                                         bool mma) {
   auto al = [](size_t x) { return (x + 127) / 128 * 128; };
   const int nwarps = attend_warps(mma, g);
   const int prow = mma ? g : 1;  // per-warp partial rows
   AttendSmem s;
   s.kv = 0;
-  s.hw = s.kv + al((size_t)2 * nslot * BS * D * elt);
-  s.uw = s.hw + al((size_t)g * nw_max * 4);
+  s.uw = s.kv + al((size_t)2 * 2 * nslot * BS * D * elt);  // 2 stages x (K, V)
   s.list = s.uw + al((size_t)nw_max * 4);
   s.mask = s.list + al((size_t)slice_cap * 4);
   s.wpart = s.mask + al((size_t)slice_cap * 4);
-  s.part = s.wpart + al((size_t)nwarps * prow * (D + 2) * 4);
-  s.total = s.part + al((size_t)(32 + g * D) * 4);
+  s.merge = s.wpart + al((size_t)nwarps * prow * (D + 2) * 4);
+  s.total = s.merge + al((size_t)(2 * split * g + g) * 4);
   return s;
 }
 
 template <typename T, int D, int BS, bool MMA>
-__global__ void __launch_bounds__(kAttendMaxThreads) attend_kernel(AttendParams p) {
+__global__ void __launch_bounds__(MMA ? kAttendMmaWarps * 32 : kAttendMaxThreads) attend_kernel(AttendParams p) {
   constexpr int VEC = 16 / sizeof(T);       // elements per 16-byte chunk
   constexpr int LPT = D / VEC;              // lanes per token row (CUDA-core path)
   constexpr int TPP = 32 / LPT;             // token rows per warp pass
@@ -83,81 +76,35 @@ __global__ void __launch_bounds__(kAttendMaxThreads) attend_kernel(AttendParams 
   static_assert(LPT <= 32 && BS % TPP == 0, "unsupported tile shape");
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ int scan_scratch[33];
+  __shared__ int s_last;
 
-  cg::cluster_group cl = cg::this_cluster();
-  const int rank = (int)cl.block_rank();
-  const int CL = (int)cl.num_blocks();
+  const int split = blockIdx.x, SPLIT = gridDim.x;
   const int kvh = blockIdx.y, b = blockIdx.z;
+  const int grp = b * p.Hkv + kvh;
   const int nthr = blockDim.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nwarps = nthr >> 5;
   const int g = p.g, NSLOT = p.nbt;
-  const AttendSmem L = attend_smem_layout(sizeof(T), D, BS, NSLOT, g, p.nw_max, p.slice_cap, MMA);
-  T* kbuf = reinterpret_cast<T*>(smem + L.kv);                 // [NSLOT][BS][D]
-  T* vbuf = kbuf + (size_t)NSLOT * BLK;                        // [NSLOT][BS][D]
-  uint32_t* hw = reinterpret_cast<uint32_t*>(smem + L.hw);     // [g][nw_max] head words
+  const AttendSmem L =
+      attend_smem_layout(sizeof(T), D, BS, NSLOT, g, p.nw_max, p.slice_cap, SPLIT, MMA);
+  T* kvbuf = reinterpret_cast<T*>(smem + L.kv);                // [2][K, V][NSLOT][BS][D]
   uint32_t* uw = reinterpret_cast<uint32_t*>(smem + L.uw);     // [nw_max] union words
   int* list = reinterpret_cast<int*>(smem + L.list);           // [slice_cap] block ids
   uint32_t* lmask = reinterpret_cast<uint32_t*>(smem + L.mask);  // [slice_cap] head bits
   float* wpart = reinterpret_cast<float*>(smem + L.wpart);     // per-warp partials
-  float* pm = reinterpret_cast<float*>(smem + L.part);         // [16] CTA running max per head
-  float* pl = pm + 16;                                         // [16] denominators
-  float* po = pl + 16;                                         // [g][D] numerators
+  float* mf = reinterpret_cast<float*>(smem + L.merge);        // merge: [SPLIT][g] factors
+  float* ml = mf + SPLIT * g;                                  // (spare [SPLIT][g])
+  float* mL = ml + SPLIT * g;                                  // [g] merged denominators
 
-  pdl_wait();
+  // inputs of the whole step (written before the estimator ran): load them
+  // before waiting for the plan
   int S = seq_len_of(p.seq_lens, b, p.max_seq_len);
   if (S < 0 || S > p.max_seq_len) S = 0;
   const int nb = ceil_div(S, BS);
   const int nw = ceil_div(nb, 32);
   const int row0 = b * p.Hq + kvh * g;
-
-  // ---- the group's selection bitmaps and their union ----
-  for (int w = tid; w < nw; w += nthr) {
-    uint32_t u = 0;
-    for (int hh = 0; hh < g; ++hh) {
-      const uint32_t x = p.bitmap[(int64_t)(row0 + hh) * p.bm_words + w];
-      hw[hh * p.nw_max + w] = x;
-      u |= x;
-    }
-    uw[w] = u;
-  }
-  __syncthreads();
-  const int wpt = ceil_div(nw, nthr);
-  const int w0 = imin(tid * wpt, nw), w1 = imin(w0 + wpt, nw);
-  int cnt = 0;
-  for (int w = w0; w < w1; ++w) cnt += __popc(uw[w]);
-  const int before = block_exclusive_scan(cnt, scan_scratch);
-  const int U = scan_scratch[32];
-  const int lo = (int)((int64_t)U * rank / CL), hi = (int)((int64_t)U * (rank + 1) / CL);
-  if (before < hi && before + cnt > lo) {
-    int rk = before;
-    for (int w = w0; w < w1 && rk < hi; ++w) {
-      uint32_t u = uw[w];
-      const int pc = __popc(u);
-      if (rk + pc <= lo) {  // the whole word lies before this CTA's slice
-        rk += pc;
-        continue;
-      }
-      while (u && rk < hi) {
-        const int bit = __ffs(u) - 1;
-        u &= u - 1u;
-        if (rk >= lo) {
-          uint32_t m = 0;
-          for (int hh = 0; hh < g; ++hh) m |= ((hw[hh * p.nw_max + w] >> bit) & 1u) << hh;
-          list[rk - lo] = w * 32 + bit;
-          lmask[rk - lo] = m;
-        }
-        ++rk;
-      }
-    }
-  }
-  __syncthreads();
-  const int n = hi - lo;
-
   const T* kbase = static_cast<const T*>(p.k.data) + b * p.k.sb + kvh * p.k.sh;
   const T* vbase = static_cast<const T*>(p.v.data) + b * p.v.sb + kvh * p.v.sh;
   const T* qbase = static_cast<const T*>(p.q.data) + b * p.q.sb + (int64_t)kvh * g * p.q.sh;
-
-  // per-path running state
   MmaAcc<D> acc;
   uint32_t qa[D / 16][4];
   float qf[VEC];
@@ -191,11 +138,66 @@ __global__ void __launch_bounds__(kAttendMaxThreads) attend_kernel(AttendParams 
     for (int e = 0; e < VEC; ++e) o[e] = 0.f;
   }
   const float scale_log2 = p.sm_scale * 1.4426950408889634f;
+  pdl_wait();
 
-  // ---- gather + compute in batches of up to NSLOT blocks (one DRAM round trip each) ----
-  int seen = 0;
-  for (int first = 0; first < n; first += NSLOT) {
+  // ---- union of the group's selection bitmaps; this CTA's share of it ----
+  const int wpt = ceil_div(nw, nthr);
+  const int w0 = imin(tid * wpt, nw), w1 = imin(w0 + wpt, nw);
+  int cnt = 0;
+  uint32_t x0[16];  // head words of this thread's first word (reused by the enumeration)
+  for (int w = w0; w < w1; ++w) {
+    uint32_t x[16];
+#pragma unroll
+    for (int hh = 0; hh < 16; ++hh)
+      x[hh] = hh < g ? p.bitmap[(int64_t)(row0 + hh) * p.bm_words + w] : 0u;
+    uint32_t u = 0;
+#pragma unroll
+    for (int hh = 0; hh < 16; ++hh) u |= x[hh];
+    if (w == w0) {
+#pragma unroll
+      for (int hh = 0; hh < 16; ++hh) x0[hh] = x[hh];
+    }
+    uw[w] = u;
+    cnt += __popc(u);
+  }
+  const int before = block_exclusive_scan(cnt, scan_scratch);
+  const int U = scan_scratch[32];
+  const int lo = (int)((int64_t)U * split / SPLIT), hi = (int)((int64_t)U * (split + 1) / SPLIT);
+  if (before < hi && before + cnt > lo) {
+    int rk = before;
+    for (int w = w0; w < w1 && rk < hi; ++w) {
+      uint32_t u = uw[w];
+      const int pc = __popc(u);
+      if (rk + pc <= lo) {  // the whole word lies before this CTA's share
+        rk += pc;
+        continue;
+      }
+      uint32_t x[16];
+#pragma unroll
+      for (int hh = 0; hh < 16; ++hh)
+        x[hh] = w == w0 ? x0[hh] : (hh < g ? p.bitmap[(int64_t)(row0 + hh) * p.bm_words + w] : 0u);
+      while (u && rk < hi) {
+        const int bit = __ffs(u) - 1;
+        u &= u - 1u;
+        if (rk >= lo) {
+          uint32_t m = 0;
+#pragma unroll
+          for (int hh = 0; hh < 16; ++hh) m |= ((x[hh] >> bit) & 1u) << hh;
+          list[rk - lo] = w * 32 + bit;
+          lmask[rk - lo] = m;
+        }
+        ++rk;
+      }
+    }
+  }
+  __syncthreads();
+  const int n = hi - lo;
+
+  // ---- two-stage gather ring + compute, NSLOT blocks per stage ----
+  auto issue = [&](int first, int stage) {
     const int cntb = imin(NSLOT, n - first);
+    T* kb = kvbuf + (size_t)stage * 2 * NSLOT * BLK;
+    T* vb = kb + (size_t)NSLOT * BLK;
     const int chunks = cntb * BS * ROWC;
     for (int c = tid; c < chunks; c += nthr) {
       const int slot = c / (BS * ROWC);
@@ -206,18 +208,32 @@ __global__ void __launch_bounds__(kAttendMaxThreads) attend_kernel(AttendParams 
       const int64_t srow = valid ? (int64_t)pos : 0;
       const int pcol = MMA ? (col ^ (tok & 7)) : col;  // swizzle for ldmatrix
       const size_t off = (size_t)slot * BLK + tok * D + pcol * VEC;
-      cp_async16(kbuf + off, kbase + srow * p.k.ss + col * VEC, valid);
-      cp_async16(vbuf + off, vbase + srow * p.v.ss + col * VEC, valid);
+      cp_async16(kb + off, kbase + srow * p.k.ss + col * VEC, valid);
+      cp_async16(vb + off, vbase + srow * p.v.ss + col * VEC, valid);
     }
     cp_async_commit();
-    cp_async_wait_all();
+  };
+  int seen = 0;
+  const int nbatch = ceil_div(n, NSLOT);
+  if (nbatch > 0) issue(0, 0);
+  for (int bi = 0; bi < nbatch; ++bi) {
+    const int first = bi * NSLOT;
+    const int cntb = imin(NSLOT, n - first);
+    if (bi + 1 < nbatch) {
+      issue(first + NSLOT, (bi + 1) & 1);
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      cp_async_wait_all();
+    }
     __syncthreads();
+    const T* kb = kvbuf + (size_t)(bi & 1) * 2 * NSLOT * BLK;
+    const T* vb = kb + (size_t)NSLOT * BLK;
     if constexpr (MMA) {
       for (int slot = warp; slot < cntb; slot += nwarps) {
         const int blk = list[first + slot];
         const int tok_valid = imin(BS, S - blk * BS);
-        mma_block<T, D, BS>(acc, qa, smem_addr(kbuf + (size_t)slot * BLK),
-                            smem_addr(vbuf + (size_t)slot * BLK), lmask[first + slot], tok_valid,
+        mma_block<T, D, BS>(acc, qa, smem_addr(kb + (size_t)slot * BLK),
+                            smem_addr(vb + (size_t)slot * BLK), lmask[first + slot], tok_valid,
                             scale_log2, lane);
       }
     } else {
@@ -229,8 +245,8 @@ __global__ void __launch_bounds__(kAttendMaxThreads) attend_kernel(AttendParams 
         if (!((lmask[first + slot] >> head) & 1u)) continue;  // warp-uniform
         if ((seen++ % WPH) != sub) continue;
         const int blk = list[first + slot];
-        const T* kt = kbuf + (size_t)slot * BLK;
-        const T* vt = vbuf + (size_t)slot * BLK;
+        const T* kt = kb + (size_t)slot * BLK;
+        const T* vt = vb + (size_t)slot * BLK;
         float sc[PASSES];
 #pragma unroll
         for (int pp = 0; pp < PASSES; ++pp) {
@@ -271,10 +287,11 @@ __global__ void __launch_bounds__(kAttendMaxThreads) attend_kernel(AttendParams 
         m_run = m_new;
       }
     }
-    __syncthreads();  // the slots are refilled by the next batch
+    __syncthreads();  // this stage is refilled two batches later
   }
 
-  // ---- warp partials -> CTA partial of each head (max in log2 units) ----
+  // ---- warp partials -> this CTA's partial of each head (max in log2 units) ----
+  float* gpart = p.part + ((size_t)grp * SPLIT + split) * g * (D + 2);  // [g][m, l, o[D]]
   if constexpr (MMA) {
     float l0 = acc.l[0], l1 = acc.l[1];
     l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
@@ -312,10 +329,10 @@ __global__ void __launch_bounds__(kAttendMaxThreads) attend_kernel(AttendParams 
           O += rp[2 + d] * f;
         }
       }
-      po[hh * D + d] = O;
+      gpart[hh * (D + 2) + 2 + d] = O;
       if (d == 0) {
-        pm[hh] = M;
-        pl[hh] = Ls;
+        gpart[hh * (D + 2)] = M;
+        gpart[hh * (D + 2) + 1] = Ls;
       }
     }
   } else {
@@ -351,54 +368,76 @@ __global__ void __launch_bounds__(kAttendMaxThreads) attend_kernel(AttendParams 
           O += wp[w * (D + 2) + 2 + d] * f;
         }
       }
-      po[hh * D + d] = O;
+      gpart[hh * (D + 2) + 2 + d] = O;
       if (d == 0) {
-        pm[hh] = M;
-        pl[hh] = Ls;
+        gpart[hh * (D + 2)] = M;
+        gpart[hh * (D + 2) + 1] = Ls;
       }
     }
   }
-  cl.sync();
 
-  // ---- cluster merge: CTA `rank` finalises heads rank, rank + CL, ... ----
-  constexpr int kMaxCl = 16;
-  for (int hh = rank; hh < g; hh += CL) {
-    float mc[kMaxCl], lc[kMaxCl];
+  // ---- the last CTA of the group merges the SPLIT partials ----
+  // Arrival is one acq_rel atomic by thread 0 after the CTA barrier: release
+  // publishes this CTA's partial (ordered before it by the barrier), acquire
+  // makes the other CTAs' partials visible to the merging CTA.
+  __syncthreads();
+  if (tid == 0) {
+    unsigned prev;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;"
+                 : "=r"(prev)
+                 : "l"(p.counters + grp)
+                 : "memory");
+    s_last = prev == (unsigned)(SPLIT - 1);
+  }
+  __syncthreads();
+  if (!s_last) {
+    pdl_launch_dependents();
+    return;
+  }
+  const float* gp0 = p.part + (size_t)grp * SPLIT * g * (D + 2);
+  const size_t stride = (size_t)g * (D + 2);  // between splits
+  // per-head max over splits and merge factors: warp w takes heads w, w + nwarps, ...
+  static_assert(kAttendMaxSplit <= 64, "two splits per lane");
+  for (int hh = warp; hh < g; hh += nwarps) {
+    float m2[2], l2[2];
 #pragma unroll
-    for (int c = 0; c < kMaxCl; ++c) {
-      if (c < CL) {
-        mc[c] = *cl.map_shared_rank(&pm[hh], c);
-        lc[c] = *cl.map_shared_rank(&pl[hh], c);
-      }
+    for (int q = 0; q < 2; ++q) {
+      const int s2 = lane + 32 * q;
+      const float* pp = gp0 + s2 * stride + hh * (D + 2);
+      m2[q] = s2 < SPLIT ? __ldcg(pp) : -INFINITY;
+      l2[q] = s2 < SPLIT ? __ldcg(pp + 1) : 0.f;
     }
-    float M = -INFINITY;
-#pragma unroll
-    for (int c = 0; c < kMaxCl; ++c)
-      if (c < CL) M = fmaxf(M, mc[c]);
-    float f[kMaxCl];
+    const float M = warp_max(fmaxf(m2[0], m2[1]));
     float Ls = 0.f;
 #pragma unroll
-    for (int c = 0; c < kMaxCl; ++c) {
-      if (c < CL) {
-        f[c] = (M == -INFINITY || mc[c] == -INFINITY) ? 0.f : exp2f(mc[c] - M);
-        Ls += lc[c] * f[c];
-      }
+    for (int q = 0; q < 2; ++q) {
+      const int s2 = lane + 32 * q;
+      const float f = (M == -INFINITY || m2[q] == -INFINITY) ? 0.f : exp2f(m2[q] - M);
+      if (s2 < SPLIT) mf[s2 * g + hh] = f;
+      Ls += l2[q] * f;
     }
+    Ls = warp_sum(Ls);
+    if (lane == 0) mL[hh] = Ls;
+  }
+  __syncthreads();
+  for (int idx = tid; idx < g * D; idx += nthr) {
+    const int hh = idx / D, d = idx - hh * D;
+    const float* src = gp0 + (size_t)hh * (D + 2) + 2 + d;
+    float O = 0.f;
+    for (int s0 = 0; s0 < SPLIT; s0 += 32) {  // up to 32 loads in flight per round trip
+      float v[32];
+#pragma unroll
+      for (int u = 0; u < 32; ++u) v[u] = s0 + u < SPLIT ? __ldcg(src + (size_t)(s0 + u) * stride) : 0.f;
+#pragma unroll
+      for (int u = 0; u < 32; ++u)
+        if (s0 + u < SPLIT) O += mf[(s0 + u) * g + hh] * v[u];
+    }
+    const float Ls = mL[hh];
     T* orow = static_cast<T*>(const_cast<void*>(p.out.data)) + b * p.out.sb +
               (int64_t)(kvh * g + hh) * p.out.sh;
-    for (int d = tid; d < D; d += nthr) {
-      float ov[kMaxCl];
-#pragma unroll
-      for (int c = 0; c < kMaxCl; ++c)
-        if (c < CL) ov[c] = *cl.map_shared_rank(&po[hh * D + d], c);
-      float O = 0.f;
-#pragma unroll
-      for (int c = 0; c < kMaxCl; ++c)
-        if (c < CL) O += ov[c] * f[c];
-      orow[d] = from_f32<T>(Ls > 0.f ? O / Ls : 0.f);
-    }
+    orow[d] = from_f32<T>(Ls > 0.f ? O / Ls : 0.f);
   }
-  cl.sync();  // keep this CTA's shared memory alive until every reader is done
+  if (tid == 0) p.counters[grp] = 0u;  // ready for the next call
   pdl_launch_dependents();
 }
 
@@ -408,6 +447,8 @@ __global__ void __launch_bounds__(256) table_bitmap_kernel(TableParams p) {
   extern __shared__ uint32_t sbits[];
   const int h = blockIdx.x, b = blockIdx.y, row = b * p.Hq + h;
   pdl_wait();
+  if (h == 0 && b == 0 && p.counters)
+    for (int i = threadIdx.x; i < p.ncounters; i += blockDim.x) p.counters[i] = 0u;
   int S = seq_len_of(p.seq_lens, b, p.max_seq_len);
   if (S < 0 || S > p.max_seq_len) {
     if (threadIdx.x == 0 && h == 0) report(p.status, ADAKV_ST_BAD_SEQ_LEN);
@@ -458,9 +499,10 @@ bool attend_uses_mma(int dtype) { return dtype != ADAKV_DTYPE_F32; }
 
 int attend_threads(int dtype, int g) { return 32 * attend_warps(attend_uses_mma(dtype), g); }
 
-size_t attend_smem_bytes(int dtype, int D, int bs, int nbt, int g, int nw_max, int slice_cap) {
+size_t attend_smem_bytes(int dtype, int D, int bs, int nbt, int g, int nw_max, int slice_cap,
+                         int split) {
   return attend_smem_layout(dtype == ADAKV_DTYPE_F32 ? 4 : 2, D, bs, nbt, g, nw_max, slice_cap,
-                            attend_uses_mma(dtype))
+                            split, attend_uses_mma(dtype))
       .total;
 }
 
@@ -469,10 +511,8 @@ cudaError_t attend_kernels_init() {
     for (int D : {64, 128})
       for (int bs : {16, 32}) {
         cudaError_t e = for_each_attend(dt, D, bs, [](auto kern, int) {
-          cudaError_t r = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               (int)kAttendSmemMax);
-          if (r != cudaSuccess) return r;
-          return cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+          return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)kAttendSmemMax);
         });
         if (e != cudaSuccess) return e;
       }
@@ -480,32 +520,11 @@ cudaError_t attend_kernels_init() {
                               64 * 1024);
 }
 
-int attend_active_clusters(int dtype, int D, int bs, int g, size_t smem, int cluster) {
-  int n = 0;
-  for_each_attend(dtype, D, bs, [&](auto kern, int) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(cluster, 1, 1);
-    cfg.blockDim = dim3(attend_threads(dtype, g), 1, 1);
-    cfg.dynamicSmemBytes = smem;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = cluster;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
-  });
-  return n;
-}
-
-cudaError_t launch_attend(const AttendParams& p, int dtype, int D, int bs, int cluster,
+cudaError_t launch_attend(const AttendParams& p, int dtype, int D, int bs, int split,
                           cudaStream_t st, const LaunchOpts& o) {
-  const size_t smem = attend_smem_bytes(dtype, D, bs, p.nbt, p.g, p.nw_max, p.slice_cap);
-  LaunchOpts oc = o;
-  oc.cluster_x = (unsigned)cluster;
+  const size_t smem = attend_smem_bytes(dtype, D, bs, p.nbt, p.g, p.nw_max, p.slice_cap, split);
   return for_each_attend(dtype, D, bs, [&](auto kern, int) {
-    return launch_ex(kern, dim3(cluster, p.Hkv, p.B), dim3(attend_threads(dtype, p.g)), smem, st, oc, p);
+    return launch_ex(kern, dim3(split, p.Hkv, p.B), dim3(attend_threads(dtype, p.g)), smem, st, o, p);
   });
 }
 

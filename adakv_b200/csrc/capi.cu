@@ -49,7 +49,6 @@ struct DeviceState {
   bool ready = false;
   int num_sms = 0;
   std::map<int, int> plan_ctas;                    // nb_max * 16 + cluster -> resident plan clusters
-  std::map<std::tuple<int, int, int, int, size_t>, int> clusters;  // attend shape -> active clusters
 };
 constexpr int kMaxDevices = 64;
 DeviceState g_dev[kMaxDevices];
@@ -164,12 +163,25 @@ View to_view(const adakv_view* v) {
   return r;
 }
 
+// CTAs per (sequence, KV head) of the attend kernel: enough to cover the GPU
+// once for small batches, at most kAttendMaxSlice union blocks per CTA, and
+// no more CTAs than blocks.
+int attend_split(const adakv_geometry* g) {
+  const int groups = g->batch * g->n_kv_heads;
+  const int nb_max = ceil_div(g->max_seq_len, g->block_size);
+  int split = std::max(1, kAttendCtaTarget / groups);
+  split = std::max(split, ceil_div(nb_max, kAttendMaxSlice));
+  split = std::min(split, std::max(1, nb_max));
+  return std::min(split, kAttendMaxSplit);
+}
+
 // Workspace layout (byte offsets into the caller's buffer; every region is
-// 256-byte aligned).  Counters never need resetting: the plan barrier compares
-// per-head slot tags with a per-call epoch that the estimator increments.
+// 256-byte aligned).  Nothing needs resetting between calls: the plan's
+// exchange slots are cleared by the estimator of the same call and the
+// attend arrival counters are reset by the CTA that merges.
 struct WsLayout {
-  size_t status, epoch, slots, scores, bitmap, bytes;
-  int score_stride, bm_words;
+  size_t status, epoch, slots, scores, bitmap, part, counters, bytes;
+  int score_stride, bm_words, split;
 };
 
 WsLayout make_ws(const adakv_geometry* g, bool with_plan) {
@@ -177,6 +189,8 @@ WsLayout make_ws(const adakv_geometry* g, bool with_plan) {
   const int rows = g->batch * g->n_q_heads;
   L.score_stride = (int)align_up((size_t)g->nb_cap, 4);
   L.bm_words = ceil_div(g->nb_cap, 32);
+  L.split = attend_split(g);
+  const int gq = g->n_q_heads / g->n_kv_heads;
   size_t o = 0;
   auto take = [&](size_t bytes) { size_t at = o; o = align_up(o + bytes, 256); return at; };
   L.status = take(16);
@@ -184,6 +198,8 @@ WsLayout make_ws(const adakv_geometry* g, bool with_plan) {
   L.slots = with_plan ? take(sizeof(PlanSlot) * rows * kPlanSlotsPerRow) : 0;
   L.scores = with_plan ? take(sizeof(float) * (size_t)rows * L.score_stride) : 0;
   L.bitmap = take(sizeof(uint32_t) * (size_t)rows * L.bm_words);
+  L.part = take(sizeof(float) * (size_t)g->batch * g->n_kv_heads * L.split * gq * (g->head_dim + 2));
+  L.counters = take(sizeof(uint32_t) * (size_t)g->batch * g->n_kv_heads);
   L.bytes = o;
   return L;
 }
@@ -228,6 +244,7 @@ int enqueue_plan(const DeviceState* ds, const adakv_geometry* g, const adakv_sel
   ep.score_stride = L.score_stride;
   ep.epoch = ws_at<uint32_t>(ws, L.epoch);
   ep.slots = ws_at<PlanSlot>(ws, L.slots);
+  ep.counters = ws_at<uint32_t>(ws, L.counters);
   if (n_new > 0) {
     ep.k = to_view(k);
     ep.v = to_view(v);
@@ -324,66 +341,26 @@ int enqueue_attend(const DeviceState* ds, const adakv_geometry* g, const adakv_v
   ap.bm_words = L.bm_words;
   ap.nw_max = ceil_div(nb_max, 32);
   ap.status = ws_at<uint32_t>(ws, L.status);
-  // blocks per gather batch (one DRAM round trip): as many K+V tiles as fit
-  // beside the other shared buffers
+  ap.part = ws_at<float>(ws, L.part);
+  ap.counters = ws_at<uint32_t>(ws, L.counters);
+  const int split = L.split;
+  ap.slice_cap = ceil_div(nb_max, split) + 1;
+  // blocks per stage of the gather ring: up to 8 (64 KB of K+V per stage for
+  // bf16, D 128, bs 16), fewer when the rest of the shared memory needs room
   const size_t per_block = (size_t)g->block_size * g->head_dim * elt_size(g->dtype) * 2;
-  ap.nbt = (int)std::max<size_t>(1, std::min<size_t>(32, (144 * 1024) / per_block));
-  // Largest cluster (most split of each KV head's union) for which every
-  // (sequence, KV head) cluster of the launch is resident at once; a
-  // 16-CTA cluster needs 16 free SMs in one GPC, so fewer fit than SMs allow.
-  const int groups = g->batch * g->n_kv_heads;
-  int cluster = 0;
-  size_t smem = 0;
-  int best_c = 1;
-  size_t best_smem = 0;
-  int best_nbt = ap.nbt;
-  const int nbt0 = ap.nbt;
-  for (int c = 16; c >= 1; c /= 2) {
-    ap.nbt = nbt0;
-    ap.slice_cap = ceil_div(nb_max, c) + 1;
-    smem = attend_smem_bytes(g->dtype, g->head_dim, g->block_size, ap.nbt, gq, ap.nw_max, ap.slice_cap);
-    while (smem > kAttendSmemMax && ap.nbt > 1) {
-      --ap.nbt;
-      smem = attend_smem_bytes(g->dtype, g->head_dim, g->block_size, ap.nbt, gq, ap.nw_max, ap.slice_cap);
-    }
-    if (smem > kAttendSmemMax) continue;
-    int active;
-    {
-      std::lock_guard<std::mutex> lock(g_dev_mu);
-      const auto key = std::make_tuple(g->dtype, g->head_dim * 64 + g->block_size, gq, c, smem);
-      auto it = ds->clusters.find(key);
-      if (it == ds->clusters.end())
-        it = const_cast<DeviceState*>(ds)
-                 ->clusters.emplace(key, attend_active_clusters(g->dtype, g->head_dim, g->block_size,
-                                                                gq, smem, c))
-                 .first;
-      active = it->second;
-    }
-    if (active < 1) continue;
-    if (cluster == 0) {  // first feasible size is the fallback
-      best_c = c;
-      best_smem = smem;
-      best_nbt = ap.nbt;
-      cluster = c;
-    }
-    if (active >= groups) {
-      best_c = c;
-      best_smem = smem;
-      best_nbt = ap.nbt;
-      cluster = c;
-      break;
-    }
+  ap.nbt = (int)std::max<size_t>(1, std::min<size_t>(8, (64 * 1024) / per_block));
+  size_t smem =
+      attend_smem_bytes(g->dtype, g->head_dim, g->block_size, ap.nbt, gq, ap.nw_max, ap.slice_cap, split);
+  while (smem > kAttendSmemMax && ap.nbt > 1) {
+    --ap.nbt;
+    smem = attend_smem_bytes(g->dtype, g->head_dim, g->block_size, ap.nbt, gq, ap.nw_max,
+                             ap.slice_cap, split);
   }
-  if (cluster == 0)
+  if (smem > kAttendSmemMax)
     return fail(ADAKV_ERR_UNSUPPORTED, "sequence too long for the attend kernel's shared memory");
-  cluster = best_c;
-  smem = best_smem;
-  ap.nbt = best_nbt;
-  ap.slice_cap = ceil_div(nb_max, cluster) + 1;
-  (void)smem;
   LaunchOpts oa;
   oa.pdl = pdl_enabled();
-  CUDA_TRY(launch_attend(ap, g->dtype, g->head_dim, g->block_size, cluster, st, oa));
+  CUDA_TRY(launch_attend(ap, g->dtype, g->head_dim, g->block_size, split, st, oa));
   return ADAKV_OK;
 }
 
@@ -562,6 +539,8 @@ int adakv_attend(const adakv_geometry* geo, const adakv_view* q, const adakv_vie
   tp.bitmap = ws_at<uint32_t>(workspace, L.bitmap);
   tp.bm_words = L.bm_words;
   tp.status = ws_at<uint32_t>(workspace, L.status);
+  tp.counters = ws_at<uint32_t>(workspace, L.counters);
+  tp.ncounters = geo->batch * geo->n_kv_heads;
   LaunchOpts ot;
   ot.pdl = pdl_enabled();
   CUDA_TRY(launch_table_bitmap(tp, st, ot));
@@ -694,6 +673,8 @@ int adakv_attend_noalloc(const adakv_geometry* geo, const adakv_view* q, const a
   tp.bitmap = ws_at<uint32_t>(ws, L.bitmap);
   tp.bm_words = L.bm_words;
   tp.status = ws_at<uint32_t>(ws, L.status);
+  tp.counters = ws_at<uint32_t>(ws, L.counters);
+  tp.ncounters = geo->batch * geo->n_kv_heads;
   LaunchOpts ot;
   ot.pdl = false;  // follows the memset
   CUDA_TRY(launch_table_bitmap(tp, st, ot));

@@ -313,6 +313,9 @@ __global__ void __launch_bounds__(kEstThreads, 1) estimate_kernel(EstParams p) {
       for (int r = blockIdx.x * 32 + lane; r < p.B * p.Hq * kPlanSlotsPerRow; r += gridDim.x * 32)
         p.slots[r].word = 0ull;
     }
+    if (p.counters) {
+      for (int r = blockIdx.x * 32 + lane; r < p.B * p.Hkv; r += gridDim.x * 32) p.counters[r] = 0u;
+    }
   } else {
     // ---------------- consumers ----------------
     named_bar_sync(1, (kEstConsumerWarps + 1) * 32);  // chunk map written by the producer warp

@@ -49,6 +49,7 @@ struct EstParams {
   int score_stride;
   uint32_t* epoch;        // incremented once per launch (per-call tag for the plan barrier)
   PlanSlot* slots;        // [B*Hq*kPlanSlotsPerRow] exchange slots: cleared here, before the plan
+  uint32_t* counters;     // [B*Hkv] attend arrival counts: cleared here, before the attend
   // fused append: n_new > 0 and k_new.data != NULL
   View k, v, k_new, v_new;
   int n_new;
@@ -101,6 +102,9 @@ struct PlanParams {
 // (d) attend: one cluster per (sequence, KV head) over the union of the group's blocks
 // ---------------------------------------------------------------------------
 constexpr size_t kAttendSmemMax = 200 * 1024;  // opt-in dynamic shared memory of one attend CTA
+constexpr int kAttendCtaTarget = 148;  // CTAs per launch the split-KV axis aims for (B200 SMs)
+constexpr int kAttendMaxSplit = 64;    // CTAs per (sequence, KV head)
+constexpr int kAttendMaxSlice = 8192;  // union blocks one CTA takes at most
 
 struct AttendParams {
   View q, k, v, out;
@@ -111,8 +115,10 @@ struct AttendParams {
   const uint32_t* bitmap;   // [B*Hq, bm_words]
   int bm_words;
   int nw_max;               // ceil(ceil(max_seq_len / bs) / 32)
-  int slice_cap;            // >= union blocks one CTA of the cluster can get
-  int nbt;                  // blocks per gather batch (double buffered)
+  int slice_cap;            // >= union blocks one CTA can get
+  int nbt;                  // blocks per stage of the two-stage gather ring
+  float* part;              // [B*Hkv*split, g, D + 2] partials (m, l, o)
+  uint32_t* counters;       // [B*Hkv] arrival counts (zero between calls)
   uint32_t* status;
 };
 
@@ -125,6 +131,8 @@ struct TableParams {        // block table -> per-head bitmaps (stand-alone atte
   int B, Hq, bs;
   uint32_t* bitmap;
   int bm_words;
+  uint32_t* counters;       // [ncounters] attend arrival counts: cleared here, before the attend
+  int ncounters;
   uint32_t* status;
 };
 
@@ -178,7 +186,7 @@ cudaError_t launch_estimate(const EstParams& p, int dtype, int D, int nb_max, in
                             cudaStream_t stream, const LaunchOpts& o);
 cudaError_t launch_plan(const PlanParams& p, const PlanLayout& l, int grid, cudaStream_t stream,
                         const LaunchOpts& o);
-cudaError_t launch_attend(const AttendParams& p, int dtype, int D, int bs, int cluster,
+cudaError_t launch_attend(const AttendParams& p, int dtype, int D, int bs, int split,
                           cudaStream_t stream, const LaunchOpts& o);
 cudaError_t launch_table_bitmap(const TableParams& p, cudaStream_t stream, const LaunchOpts& o);
 
@@ -191,8 +199,7 @@ int estimate_stages(int dtype, int D, int g, int B);
 PlanLayout plan_layout(int nb_max, int csize);
 // clusters of the plan kernel with layout `l` that can be resident at once
 int plan_active_clusters(const PlanLayout& l);
-// clusters of `cluster` CTAs of the attend kernel that can be resident at once
-int attend_active_clusters(int dtype, int D, int bs, int g, size_t smem, int cluster);
-size_t attend_smem_bytes(int dtype, int D, int bs, int nbt, int g, int nw_max, int slice_cap);
+size_t attend_smem_bytes(int dtype, int D, int bs, int nbt, int g, int nw_max, int slice_cap,
+                         int split);
 
 }  // namespace adakv
