@@ -66,6 +66,15 @@ _SIGNATURES = {
                                          ctypes.c_float, _vp, ctypes.c_int32, _vp, _P(View), _vp,
                                          ctypes.c_size_t, _vp]),
     "adakv_read_status": (ctypes.c_int, [_vp, _P(ctypes.c_uint32), _vp]),
+    "adakv_estimate": (ctypes.c_int, [_P(Geometry), _P(View), _vp, _vp, _vp, ctypes.c_int32, _vp,
+                                      ctypes.c_size_t, _vp]),
+    "adakv_select": (ctypes.c_int, [_P(Geometry), _P(SelectParams), _vp, ctypes.c_int32, _vp, _vp,
+                                    ctypes.c_int32, _vp, _vp, ctypes.c_size_t, _vp]),
+    "adakv_attend_partial": (ctypes.c_int, [_P(Geometry), _P(View), _P(View), _P(View), _vp,
+                                            ctypes.c_int32, _vp, ctypes.c_int32, _vp,
+                                            ctypes.c_float, _vp, _vp, _vp, ctypes.c_size_t, _vp]),
+    "adakv_combine": (ctypes.c_int, [ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                     ctypes.c_int32, _vp, _vp, _P(View), _vp]),
     "adakv_attend_noalloc": (ctypes.c_int, [_P(Geometry), _P(View), _P(View), _P(View), _vp,
                                             ctypes.c_int32, _vp, _vp, ctypes.c_float, _P(View),
                                             _vp, _vp]),

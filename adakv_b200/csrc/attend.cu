@@ -92,7 +92,7 @@ __global__ void __launch_bounds__(MMA ? kAttendMmaWarps * 32 : kAttendMaxThreads
   uint32_t* lmask = reinterpret_cast<uint32_t*>(smem + L.mask);  // [slice_cap] head bits
   float* wpart = reinterpret_cast<float*>(smem + L.wpart);     // per-warp partials
   float* mf = reinterpret_cast<float*>(smem + L.merge);        // merge: [SPLIT][g] factors
-  float* ml = mf + SPLIT * g;                                  // (spare [SPLIT][g])
+  float* ml = mf + SPLIT * g;                                  // [g] merged maxima
   float* mL = ml + SPLIT * g;                                  // [g] merged denominators
 
   // inputs of the whole step (written before the estimator ran): load them
@@ -417,7 +417,10 @@ __global__ void __launch_bounds__(MMA ? kAttendMmaWarps * 32 : kAttendMaxThreads
       Ls += l2[q] * f;
     }
     Ls = warp_sum(Ls);
-    if (lane == 0) mL[hh] = Ls;
+    if (lane == 0) {
+      mL[hh] = Ls;
+      ml[hh] = M;
+    }
   }
   __syncthreads();
   for (int idx = tid; idx < g * D; idx += nthr) {
@@ -433,9 +436,20 @@ __global__ void __launch_bounds__(MMA ? kAttendMmaWarps * 32 : kAttendMaxThreads
         if (s0 + u < SPLIT) O += mf[(s0 + u) * g + hh] * v[u];
     }
     const float Ls = mL[hh];
-    T* orow = static_cast<T*>(const_cast<void*>(p.out.data)) + b * p.out.sb +
-              (int64_t)(kvh * g + hh) * p.out.sh;
-    orow[d] = from_f32<T>(Ls > 0.f ? O / Ls : 0.f);
+    const float res = Ls > 0.f ? O / Ls : 0.f;
+    if (p.out_f32) {
+      p.out_f32[(int64_t)(row0 + hh) * D + d] = res;
+    } else {
+      T* orow = static_cast<T*>(const_cast<void*>(p.out.data)) + b * p.out.sb +
+                (int64_t)(kvh * g + hh) * p.out.sh;
+      orow[d] = from_f32<T>(res);
+    }
+  }
+  if (p.lse && tid < g) {
+    // merged max M is in log2 units of (score * sm_scale): lse = M ln 2 + ln L
+    const float M = ml[tid];
+    const float Ls = mL[tid];
+    p.lse[row0 + tid] = (Ls > 0.f && M > -INFINITY) ? M * 0.6931471805599453f + logf(Ls) : -INFINITY;
   }
   if (tid == 0) p.counters[grp] = 0u;  // ready for the next call
   pdl_launch_dependents();
@@ -465,9 +479,9 @@ __global__ void __launch_bounds__(256) table_bitmap_kernel(TableParams p) {
   }
   const int* trow = p.block_table + (int64_t)row * p.table_width;
   for (int i = threadIdx.x; i < k; i += blockDim.x) {
-    const int blk = trow[i];
+    const int blk = trow[i] - p.block_offset;
     if (blk < 0 || blk >= nb) {
-      report(p.status, ADAKV_ST_BAD_BLOCK_ID);
+      if (!p.local_only) report(p.status, ADAKV_ST_BAD_BLOCK_ID);
     } else {
       atomicOr(&sbits[blk >> 5], 1u << (blk & 31));
     }
@@ -526,6 +540,42 @@ cudaError_t launch_attend(const AttendParams& p, int dtype, int D, int bs, int s
   return for_each_attend(dtype, D, bs, [&](auto kern, int) {
     return launch_ex(kern, dim3(split, p.Hkv, p.B), dim3(attend_threads(dtype, p.g)), smem, st, o, p);
   });
+}
+
+// Merge of per-shard attention outputs of one query head (sequence-sharded
+// decode): out = sum_n exp(lse_n - LSE) o_n with LSE = log sum_n exp(lse_n);
+// rows with no selected token anywhere (every lse_n = -inf) produce zeros.
+template <typename T>
+__global__ void __launch_bounds__(128) combine_kernel(CombineParams p) {
+  const int row = blockIdx.x;
+  pdl_wait();
+  float M = -INFINITY;
+  for (int n = 0; n < p.n_parts; ++n) M = fmaxf(M, p.lse[(int64_t)n * p.rows + row]);
+  float den = 0.f;
+  for (int n = 0; n < p.n_parts; ++n) {
+    const float l = p.lse[(int64_t)n * p.rows + row];
+    den += (M == -INFINITY || l == -INFINITY) ? 0.f : expf(l - M);
+  }
+  const int b = row / p.Hq, h = row - b * p.Hq;
+  T* orow = static_cast<T*>(const_cast<void*>(p.out.data)) + b * p.out.sb + (int64_t)h * p.out.sh;
+  for (int d = threadIdx.x; d < p.D; d += blockDim.x) {
+    float acc = 0.f;
+    for (int n = 0; n < p.n_parts; ++n) {
+      const float l = p.lse[(int64_t)n * p.rows + row];
+      if (M == -INFINITY || l == -INFINITY) continue;
+      acc += expf(l - M) * p.parts[((int64_t)n * p.rows + row) * p.D + d];
+    }
+    orow[d] = from_f32<T>(den > 0.f ? acc / den : 0.f);
+  }
+  pdl_launch_dependents();
+}
+
+cudaError_t launch_combine(const CombineParams& p, int dtype, cudaStream_t st, const LaunchOpts& o) {
+  if (dtype == ADAKV_DTYPE_F32)
+    return launch_ex(combine_kernel<float>, dim3(p.rows), dim3(128), 0, st, o, p);
+  if (dtype == ADAKV_DTYPE_F16)
+    return launch_ex(combine_kernel<__half>, dim3(p.rows), dim3(128), 0, st, o, p);
+  return launch_ex(combine_kernel<__nv_bfloat16>, dim3(p.rows), dim3(128), 0, st, o, p);
 }
 
 cudaError_t launch_table_bitmap(const TableParams& p, cudaStream_t st, const LaunchOpts& o) {

@@ -218,6 +218,71 @@ int check_workspace(void* ws, size_t bytes, size_t need) {
   return ADAKV_OK;
 }
 
+// budget + top-k (plan kernel) over score rows already on the device; the
+// exchange slots of the workspace must be cleared before it runs
+int enqueue_select(const DeviceState* ds, const adakv_geometry* g, const adakv_select_params* sp,
+                   const float* scores, int score_stride, const int32_t* seq_lens,
+                   int32_t* block_table, int32_t table_width, int32_t* sel_lens, void* ws,
+                   const WsLayout& L, cudaStream_t st) {
+  const int nb_max = ceil_div(g->max_seq_len, g->block_size);
+  const bool pdl = pdl_enabled();
+  PlanParams pp{};
+  pp.seq_lens = seq_lens;
+  pp.max_seq_len = g->max_seq_len;
+  pp.B = g->batch;
+  pp.Hq = g->n_q_heads;
+  pp.bs = g->block_size;
+  pp.cfg = to_cfg(sp);
+  pp.scores = scores;
+  pp.score_stride = score_stride;
+  pp.epoch = ws_at<uint32_t>(ws, L.epoch);
+  pp.slots = ws_at<PlanSlot>(ws, L.slots);
+  pp.sel_lens = sel_lens;
+  pp.block_table = block_table;
+  pp.table_width = table_width;
+  pp.bitmap = ws_at<uint32_t>(ws, L.bitmap);
+  pp.bm_words = L.bm_words;
+  pp.status = ws_at<uint32_t>(ws, L.status);
+  // Cluster size: the largest C in {8, 4, 2} whose slices keep >= 1024 blocks,
+  // with all B * Hq * C CTAs resident at once and at most one per SM (one
+  // round); else C = 1 with as many sequences per round as are resident.
+  // The clusters of a sequence wait on one another (entropy exchange), so the
+  // grid never exceeds what is resident once the estimator drains; the
+  // exchange is also bounded in time.
+  auto active = [&](const PlanLayout& l) {
+    std::lock_guard<std::mutex> lock(g_dev_mu);
+    const int key = nb_max * 16 + l.csize;
+    auto it = ds->plan_ctas.find(key);
+    if (it == ds->plan_ctas.end())
+      it = const_cast<DeviceState*>(ds)->plan_ctas.emplace(key, plan_active_clusters(l)).first;
+    return it->second;
+  };
+  const int64_t heads = (int64_t)g->batch * g->n_q_heads;
+  PlanLayout lay = plan_layout(nb_max, 1);
+  for (int c = kPlanMaxCluster; c >= 2; c /= 2) {
+    if (ceil_div(nb_max, c) < 1024 || heads * c > ds->num_sms) continue;
+    const PlanLayout l = plan_layout(nb_max, c);
+    if (l.smem > kPlanSmemMax || active(l) < heads) continue;
+    lay = l;
+    break;
+  }
+  if (lay.smem > kPlanSmemMax)
+    return fail(ADAKV_ERR_UNSUPPORTED, "sequence too long for the plan kernel's shared memory");
+  const int clusters = active(lay);
+  if (clusters < g->n_q_heads)
+    return fail(ADAKV_ERR_UNSUPPORTED, "n_q_heads %d exceeds the co-resident plan clusters (%d)",
+                g->n_q_heads, clusters);
+  pp.csize = lay.csize;
+  pp.slice_cap = lay.slice_cap;
+  pp.ecache = lay.ecache ? 1 : 0;
+  pp.seqs_per_round = std::max(1, std::min(g->batch, clusters / g->n_q_heads));
+  const int plan_grid = pp.seqs_per_round * g->n_q_heads * lay.csize;
+  LaunchOpts op;
+  op.pdl = pdl;
+  CUDA_TRY(launch_plan(pp, lay, plan_grid, st, op));
+  return ADAKV_OK;
+}
+
 // estimator (+ fused append) and the plan kernel; shared by adakv_plan and
 // adakv_decode_step
 int enqueue_plan(const DeviceState* ds, const adakv_geometry* g, const adakv_select_params* sp,
@@ -260,68 +325,15 @@ int enqueue_plan(const DeviceState* ds, const adakv_geometry* g, const adakv_sel
   oe.pdl = pdl;
   CUDA_TRY(launch_estimate(ep, g->dtype, g->head_dim, nb_max, est_grid, st, oe));
 
-  PlanParams pp{};
-  pp.seq_lens = seq_lens;
-  pp.max_seq_len = g->max_seq_len;
-  pp.B = g->batch;
-  pp.Hq = g->n_q_heads;
-  pp.bs = g->block_size;
-  pp.cfg = to_cfg(sp);
-  pp.scores = ep.scores;
-  pp.score_stride = L.score_stride;
-  pp.epoch = ep.epoch;
-  pp.slots = ws_at<PlanSlot>(ws, L.slots);
-  pp.sel_lens = sel_lens;
-  pp.block_table = block_table;
-  pp.table_width = table_width;
-  pp.bitmap = ws_at<uint32_t>(ws, L.bitmap);
-  pp.bm_words = L.bm_words;
-  pp.status = status;
-  // Cluster size: the largest C in {8, 4, 2} whose slices keep >= 1024 blocks,
-  // with all B * Hq * C CTAs resident at once and at most one per SM (one
-  // round); else C = 1 with as many sequences per round as are resident.
-  // The clusters of a sequence wait on one another (entropy exchange), so the
-  // grid never exceeds what is resident once the estimator drains; the
-  // exchange is also bounded in time.
-  auto active = [&](const PlanLayout& l) {
-    std::lock_guard<std::mutex> lock(g_dev_mu);
-    const int key = nb_max * 16 + l.csize;
-    auto it = ds->plan_ctas.find(key);
-    if (it == ds->plan_ctas.end())
-      it = const_cast<DeviceState*>(ds)->plan_ctas.emplace(key, plan_active_clusters(l)).first;
-    return it->second;
-  };
-  const int64_t heads = (int64_t)g->batch * g->n_q_heads;
-  PlanLayout lay = plan_layout(nb_max, 1);
-  for (int c = kPlanMaxCluster; c >= 2; c /= 2) {
-    if (ceil_div(nb_max, c) < 1024 || heads * c > ds->num_sms) continue;
-    const PlanLayout l = plan_layout(nb_max, c);
-    if (l.smem > kPlanSmemMax || active(l) < heads) continue;
-    lay = l;
-    break;
-  }
-  if (lay.smem > kPlanSmemMax)
-    return fail(ADAKV_ERR_UNSUPPORTED, "sequence too long for the plan kernel's shared memory");
-  const int clusters = active(lay);
-  if (clusters < g->n_q_heads)
-    return fail(ADAKV_ERR_UNSUPPORTED, "n_q_heads %d exceeds the co-resident plan clusters (%d)",
-                g->n_q_heads, clusters);
-  pp.csize = lay.csize;
-  pp.slice_cap = lay.slice_cap;
-  pp.ecache = lay.ecache ? 1 : 0;
-  pp.seqs_per_round = std::max(1, std::min(g->batch, clusters / g->n_q_heads));
-  const int plan_grid = pp.seqs_per_round * g->n_q_heads * lay.csize;
-  LaunchOpts op;
-  op.pdl = pdl;
-  CUDA_TRY(launch_plan(pp, lay, plan_grid, st, op));
-  return ADAKV_OK;
+  return enqueue_select(ds, g, sp, ep.scores, ep.score_stride, seq_lens, block_table, table_width,
+                        sel_lens, ws, L, st);
 }
 
 // attend over the bitmaps in the workspace
 int enqueue_attend(const DeviceState* ds, const adakv_geometry* g, const adakv_view* q,
                    const adakv_view* k, const adakv_view* v, const adakv_view* out,
                    const int32_t* seq_lens, float sm_scale, void* ws, const WsLayout& L,
-                   cudaStream_t st) {
+                   cudaStream_t st, float* out_f32 = nullptr, float* lse = nullptr) {
   (void)ds;
   const int nb_max = ceil_div(g->max_seq_len, g->block_size);
   const int gq = g->n_q_heads / g->n_kv_heads;
@@ -341,6 +353,8 @@ int enqueue_attend(const DeviceState* ds, const adakv_geometry* g, const adakv_v
   ap.bm_words = L.bm_words;
   ap.nw_max = ceil_div(nb_max, 32);
   ap.status = ws_at<uint32_t>(ws, L.status);
+  ap.out_f32 = out_f32;
+  ap.lse = lse;
   ap.part = ws_at<float>(ws, L.part);
   ap.counters = ws_at<uint32_t>(ws, L.counters);
   const int split = L.split;
@@ -682,6 +696,150 @@ int adakv_attend_noalloc(const adakv_geometry* geo, const adakv_view* q, const a
   if (status)
     CUDA_TRY(cudaMemcpyAsync(status, ws_at<uint32_t>(ws, L.status), sizeof(uint32_t),
                              cudaMemcpyDeviceToDevice, st));
+  return ADAKV_OK;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Sequence-sharded decode (one sequence split over several GPUs by blocks):
+// per-shard scores, selection over the all-gathered score rows, per-shard
+// attention with its log-sum-exp, and the log-sum-exp merge.
+// ---------------------------------------------------------------------------
+extern "C" {
+
+int adakv_estimate(const adakv_geometry* geo, const adakv_view* q, const float* centroid,
+                   const int32_t* seq_lens, float* scores, int32_t score_stride, void* workspace,
+                   size_t workspace_bytes, void* stream) {
+  int rc;
+  if ((rc = check_geometry(geo))) return rc;
+  if ((rc = check_view(q, "q", geo->dtype, false))) return rc;
+  if (!centroid || reinterpret_cast<uintptr_t>(centroid) % 16)
+    return fail(ADAKV_ERR_INVALID, "centroid must be a 16-byte aligned device pointer");
+  if (!scores) return fail(ADAKV_ERR_INVALID, "scores is NULL");
+  if (score_stride < ceil_div(geo->max_seq_len, geo->block_size))
+    return fail(ADAKV_ERR_INVALID, "score_stride %d < blocks of max_seq_len", score_stride);
+  const WsLayout L = make_ws(geo, true);
+  if ((rc = check_workspace(workspace, workspace_bytes, L.bytes))) return rc;
+  DeviceState* ds = nullptr;
+  if ((rc = device_state(&ds))) return rc;
+  const int nb_max = ceil_div(geo->max_seq_len, geo->block_size);
+  EstParams ep{};
+  ep.q = to_view(q);
+  ep.cent = const_cast<float*>(centroid);
+  ep.nb_cap = geo->nb_cap;
+  ep.seq_lens = seq_lens;
+  ep.max_seq_len = geo->max_seq_len;
+  ep.B = geo->batch;
+  ep.Hq = geo->n_q_heads;
+  ep.Hkv = geo->n_kv_heads;
+  ep.g = geo->n_q_heads / geo->n_kv_heads;
+  ep.bs = geo->block_size;
+  ep.scores = scores;
+  ep.score_stride = score_stride;
+  ep.status = ws_at<uint32_t>(workspace, L.status);
+  ep.stages = estimate_stages(geo->dtype, geo->head_dim, ep.g, geo->batch);
+  const int64_t chunks = (int64_t)geo->batch * geo->n_kv_heads * ceil_div(nb_max, kEstRows);
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(ds->num_sms, chunks));
+  LaunchOpts oe;
+  oe.pdl = pdl_enabled();
+  CUDA_TRY(launch_estimate(ep, geo->dtype, geo->head_dim, nb_max, grid,
+                           static_cast<cudaStream_t>(stream), oe));
+  return ADAKV_OK;
+}
+
+int adakv_select(const adakv_geometry* geo, const adakv_select_params* sp, const float* scores,
+                 int32_t score_stride, const int32_t* seq_lens, int32_t* block_table,
+                 int32_t table_width, int32_t* sel_lens, void* workspace, size_t workspace_bytes,
+                 void* stream) {
+  int rc;
+  if ((rc = check_geometry(geo))) return rc;
+  if ((rc = check_params(sp))) return rc;
+  if (!scores) return fail(ADAKV_ERR_INVALID, "scores is NULL");
+  if (score_stride < ceil_div(geo->max_seq_len, geo->block_size))
+    return fail(ADAKV_ERR_INVALID, "score_stride %d < blocks of max_seq_len", score_stride);
+  if (!block_table || !sel_lens) return fail(ADAKV_ERR_INVALID, "block_table / sel_lens are NULL");
+  const int need_w = table_width_for(geo->nb_cap, to_cfg(sp));
+  if (table_width < need_w)
+    return fail(ADAKV_ERR_INVALID, "table_width %d < required %d", table_width, need_w);
+  const WsLayout L = make_ws(geo, true);
+  if ((rc = check_workspace(workspace, workspace_bytes, L.bytes))) return rc;
+  DeviceState* ds = nullptr;
+  if ((rc = device_state(&ds))) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // the exchange slots start cleared (the estimator does this on the fused path)
+  CUDA_TRY(cudaMemsetAsync(ws_at<char>(workspace, L.slots), 0,
+                           sizeof(PlanSlot) * (size_t)geo->batch * geo->n_q_heads * kPlanSlotsPerRow, st));
+  return enqueue_select(ds, geo, sp, scores, score_stride, seq_lens, block_table, table_width,
+                        sel_lens, workspace, L, st);
+}
+
+int adakv_attend_partial(const adakv_geometry* geo, const adakv_view* q, const adakv_view* k,
+                         const adakv_view* v, const int32_t* block_table, int32_t table_width,
+                         const int32_t* sel_lens, int32_t block_offset, const int32_t* seq_lens,
+                         float sm_scale, float* out_f32, float* lse, void* workspace,
+                         size_t workspace_bytes, void* stream) {
+  int rc;
+  if ((rc = check_geometry(geo))) return rc;
+  if ((rc = check_view(q, "q", geo->dtype, false))) return rc;
+  if ((rc = check_view(k, "k", geo->dtype, true))) return rc;
+  if ((rc = check_view(v, "v", geo->dtype, true))) return rc;
+  if (!block_table || !sel_lens) return fail(ADAKV_ERR_INVALID, "block_table / sel_lens are NULL");
+  if (table_width < 1) return fail(ADAKV_ERR_INVALID, "table_width must be >= 1");
+  if (block_offset < 0) return fail(ADAKV_ERR_INVALID, "block_offset must be >= 0");
+  if (!out_f32 || !lse || reinterpret_cast<uintptr_t>(out_f32) % 16)
+    return fail(ADAKV_ERR_INVALID, "out_f32 (16-byte aligned) and lse are required");
+  if (!std::isfinite(sm_scale)) return fail(ADAKV_ERR_INVALID, "sm_scale must be finite");
+  const WsLayout L = make_ws(geo, false);
+  if ((rc = check_workspace(workspace, workspace_bytes, L.bytes))) return rc;
+  DeviceState* ds = nullptr;
+  if ((rc = device_state(&ds))) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  TableParams tp{};
+  tp.block_table = block_table;
+  tp.table_width = table_width;
+  tp.sel_lens = sel_lens;
+  tp.seq_lens = seq_lens;
+  tp.max_seq_len = geo->max_seq_len;
+  tp.B = geo->batch;
+  tp.Hq = geo->n_q_heads;
+  tp.bs = geo->block_size;
+  tp.bitmap = ws_at<uint32_t>(workspace, L.bitmap);
+  tp.bm_words = L.bm_words;
+  tp.counters = ws_at<uint32_t>(workspace, L.counters);
+  tp.ncounters = geo->batch * geo->n_kv_heads;
+  tp.block_offset = block_offset;
+  tp.local_only = 1;
+  tp.status = ws_at<uint32_t>(workspace, L.status);
+  LaunchOpts ot;
+  ot.pdl = pdl_enabled();
+  CUDA_TRY(launch_table_bitmap(tp, st, ot));
+  adakv_view none{};
+  return enqueue_attend(ds, geo, q, k, v, &none, seq_lens, sm_scale, workspace, L, st, out_f32,
+                        lse);
+}
+
+int adakv_combine(int32_t n_parts, int32_t batch, int32_t n_q_heads, int32_t head_dim,
+                  int32_t dtype, const float* parts, const float* lse, const adakv_view* out,
+                  void* stream) {
+  int rc;
+  if (n_parts < 1 || batch < 1 || n_q_heads < 1 || head_dim < 1)
+    return fail(ADAKV_ERR_INVALID, "n_parts, batch, n_q_heads and head_dim must be >= 1");
+  if (dtype < ADAKV_DTYPE_F32 || dtype > ADAKV_DTYPE_BF16)
+    return fail(ADAKV_ERR_INVALID, "unknown dtype %d", dtype);
+  if (!parts || !lse) return fail(ADAKV_ERR_INVALID, "parts / lse are NULL");
+  if ((rc = check_view(out, "out", dtype, false))) return rc;
+  CombineParams cp{};
+  cp.parts = parts;
+  cp.lse = lse;
+  cp.n_parts = n_parts;
+  cp.rows = batch * n_q_heads;
+  cp.D = head_dim;
+  cp.out = to_view(out);
+  cp.Hq = n_q_heads;
+  LaunchOpts oc;
+  oc.pdl = pdl_enabled();
+  CUDA_TRY(launch_combine(cp, dtype, static_cast<cudaStream_t>(stream), oc));
   return ADAKV_OK;
 }
 

@@ -119,7 +119,17 @@ struct AttendParams {
   int nbt;                  // blocks per stage of the two-stage gather ring
   float* part;              // [B*Hkv*split, g, D + 2] partials (m, l, o)
   uint32_t* counters;       // [B*Hkv] arrival counts (zero between calls)
+  float* out_f32;           // optional [B*Hq, D] float32 output instead of `out`
+  float* lse;               // optional [B*Hq] natural-log sum of exp of the scaled scores
   uint32_t* status;
+};
+
+struct CombineParams {      // log-sum-exp merge of per-shard attention outputs
+  const float* parts;       // [n_parts, rows, D]
+  const float* lse;         // [n_parts, rows]
+  int n_parts, rows, D;
+  View out;                 // rows = b * Hq + h -> out[b, h, :]
+  int Hq;
 };
 
 struct TableParams {        // block table -> per-head bitmaps (stand-alone attend)
@@ -133,6 +143,8 @@ struct TableParams {        // block table -> per-head bitmaps (stand-alone atte
   int bm_words;
   uint32_t* counters;       // [ncounters] attend arrival counts: cleared here, before the attend
   int ncounters;
+  int block_offset;         // table ids are global; this cache holds blocks from here on
+  int local_only;           // 1: ids outside [block_offset, block_offset + nb) are skipped silently
   uint32_t* status;
 };
 
@@ -189,6 +201,7 @@ cudaError_t launch_plan(const PlanParams& p, const PlanLayout& l, int grid, cuda
 cudaError_t launch_attend(const AttendParams& p, int dtype, int D, int bs, int split,
                           cudaStream_t stream, const LaunchOpts& o);
 cudaError_t launch_table_bitmap(const TableParams& p, cudaStream_t stream, const LaunchOpts& o);
+cudaError_t launch_combine(const CombineParams& p, int dtype, cudaStream_t stream, const LaunchOpts& o);
 
 // once per device (current device): opt-in shared memory / cluster sizes
 cudaError_t estimate_kernels_init();

@@ -1,0 +1,226 @@
+"""Sequence-sharded AdaKV decode: one long sequence split over several GPUs.
+
+The reference decodes one sequence on one device.  For a context too long to
+serve from one GPU at the wanted latency (1M tokens), the sequence is split
+into contiguous block ranges, one per rank, and each decode step runs as
+
+1. every rank scores the blocks it holds (``adakv_estimate``: q . centroid,
+   GQA folded, the scoring of ``adakv/estimator.py:62-74``);
+2. the ranks all-gather the per-shard score rows (NCCL over NVLink) and
+   concatenate them in block order;
+3. every rank runs the entropy budget and top-k over the full rows
+   (``adakv_select``: ``adakv/budget.py:45-86``, ``adakv/selector.py:18-60``).
+   Identical inputs and arithmetic give identical block tables on every rank,
+   so the selection equals the single-GPU one;
+4. every rank attends over the selected blocks it holds
+   (``adakv_attend_partial``) and returns its normalised output and
+   log-sum-exp per query head;
+5. the ranks all-gather those partials and merge them by log-sum-exp
+   (``adakv_combine``).
+
+Shard ``r`` holds blocks ``[r * L, (r + 1) * L)`` with ``L`` a multiple of 32
+blocks (whole selection-bitmap words); the last rank holds the tail, so the
+sink blocks live on rank 0 and the local window on the last rank.
+
+Collectives go through a small interface: ``TorchGroup`` (``torch.distributed``,
+one process per GPU) or ``emulate_step`` (all shards in one process, for
+tests on one device).
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import _lib
+
+
+def shard_blocks(nb: int, world: int) -> int:
+    """Blocks per rank (a multiple of 32) for a sequence of ``nb`` blocks."""
+    per = -(-nb // world)
+    return max(32, -(-per // 32) * 32)
+
+
+def shard_range(nb: int, world: int, rank: int):
+    """``(first block, block count)`` of rank ``rank``'s shard."""
+    L = shard_blocks(nb, world)
+    lo = min(nb, rank * L)
+    return lo, max(0, min(nb, lo + L) - lo)
+
+
+class ShardCache:
+    """One rank's K/V blocks of the sequence and their centroids.
+
+    ``K``, ``V``: ``[Hkv, S_local, D]`` (tokens ``[tok_lo, tok_lo + S_local)`` of
+    the sequence; ``tok_lo`` a multiple of ``32 * block_size``)."""
+
+    def __init__(self, K, V, block_lo: int, n_q_heads: int, block_size: int, capacity_blocks=None):
+        _lib.require_cuda(K, V)
+        if K.shape != V.shape or K.dim() != 3:
+            raise ValueError("K and V must be [Hkv, S_local, D] of one shape")
+        if block_lo % 32:
+            raise ValueError("a shard must start on a multiple of 32 blocks")
+        self.Hkv, self.S, self.D = K.shape
+        self.Hq, self.bs, self.block_lo = n_q_heads, block_size, block_lo
+        self.k, self.v, self.dtype = K, V, K.dtype
+        self.nb = -(-self.S // block_size)
+        self.cap = max(capacity_blocks or self.nb, self.nb, 1)
+        self.centroid = torch.zeros((self.Hkv, self.cap, self.D), dtype=torch.float32,
+                                    device=K.device)
+        if self.S > 0:
+            with torch.cuda.device(K.device):
+                _lib.check(_lib.lib().adakv_centroid_build(
+                    self._geo(), _lib.view4(K.unsqueeze(0)), None, self.centroid.data_ptr(),
+                    _lib.stream_ptr(K.device)))
+
+    def _geo(self):
+        return _lib.geometry(1, self.Hq, self.Hkv, self.D, self.bs, max(self.S, 1), self.cap,
+                             _lib.TORCH_DTYPES[self.dtype])
+
+    def local_scores(self, q, out):
+        """Scores of this shard's blocks into ``out[:, :nb]`` (``out``: ``[Hq, >= cap]`` fp32)."""
+        if self.S == 0:
+            return out
+        L = _lib.lib()
+        geo = self._geo()
+        ws = _lib.workspace(L.adakv_plan_workspace_bytes(geo, _lib.select_params(1, 1, 1, 0, 0, 0,
+                                                                                 1.0, "fixed")),
+                            q.device, "shard-estimate")
+        with torch.cuda.device(q.device):
+            _lib.check(L.adakv_estimate(geo, _lib.view4(q.unsqueeze(0)), self.centroid.data_ptr(),
+                                        None, out.data_ptr(), out.stride(0), ws.data_ptr(),
+                                        ws.numel(), _lib.stream_ptr(q.device)))
+        return out
+
+    def attend_partial(self, q, block_table, sel_lens, sm_scale):
+        """``(o [Hq, D] fp32, lse [Hq] fp32)`` over the selected blocks held here."""
+        o = torch.zeros((self.Hq, self.D), dtype=torch.float32, device=q.device)
+        lse = torch.full((self.Hq,), -math.inf, dtype=torch.float32, device=q.device)
+        if self.S == 0:
+            return o, lse
+        L = _lib.lib()
+        geo = self._geo()
+        width = block_table.shape[1]
+        ws = _lib.workspace(L.adakv_attend_workspace_bytes(geo, width), q.device, "shard-attend")
+        with torch.cuda.device(q.device):
+            _lib.check(L.adakv_attend_partial(
+                geo, _lib.view4(q.unsqueeze(0)), _lib.view4(self.k.unsqueeze(0)),
+                _lib.view4(self.v.unsqueeze(0)), block_table.data_ptr(), width,
+                sel_lens.data_ptr(), self.block_lo, None, float(sm_scale), o.data_ptr(),
+                lse.data_ptr(), ws.data_ptr(), ws.numel(), _lib.stream_ptr(q.device)))
+        return o, lse
+
+
+class Selector:
+    """Budget + top-k over the full score rows of one sequence (every rank runs it)."""
+
+    def __init__(self, S_total, n_q_heads, n_kv_heads, head_dim, block_size, dtype, device,
+                 avg_budget=64, k_min=2, k_max=64, n_sink_blocks=1, n_local_blocks=4, c_min=1,
+                 temperature=1.0, budget_policy="adaptive"):
+        self.nb = -(-S_total // block_size)
+        self.geo = _lib.geometry(1, n_q_heads, n_kv_heads, head_dim, block_size, S_total, self.nb,
+                                 _lib.TORCH_DTYPES[dtype])
+        self.params = _lib.select_params(avg_budget, k_min, k_max, n_sink_blocks, n_local_blocks,
+                                         c_min, temperature, budget_policy)
+        L = _lib.lib()
+        self.width = L.adakv_plan_table_width(self.geo, self.params)
+        if self.width < 1:
+            _lib.check(_lib.ERR_INVALID)
+        self.table = torch.zeros((n_q_heads, self.width), dtype=torch.int32, device=device)
+        self.sel_lens = torch.zeros((n_q_heads,), dtype=torch.int32, device=device)
+        self.ws = torch.zeros((L.adakv_plan_workspace_bytes(self.geo, self.params),),
+                              dtype=torch.uint8, device=device)
+
+    def select(self, scores):
+        """``scores``: ``[Hq, >= nb]`` fp32 rows in block order -> (table, sel_lens)."""
+        with torch.cuda.device(scores.device):
+            _lib.check(_lib.lib().adakv_select(
+                self.geo, self.params, scores.data_ptr(), scores.stride(0), None,
+                self.table.data_ptr(), self.width, self.sel_lens.data_ptr(), self.ws.data_ptr(),
+                self.ws.numel(), _lib.stream_ptr(scores.device)))
+        return self.table, self.sel_lens
+
+
+def combine(parts, lse, dtype, out=None):
+    """Log-sum-exp merge: ``parts [N, Hq, D]`` fp32, ``lse [N, Hq]`` -> ``[Hq, D]``."""
+    N, Hq, D = parts.shape
+    if out is None:
+        out = torch.empty((Hq, D), dtype=dtype, device=parts.device)
+    parts = parts.contiguous()
+    lse = lse.contiguous()
+    with torch.cuda.device(parts.device):
+        _lib.check(_lib.lib().adakv_combine(N, 1, Hq, D, _lib.TORCH_DTYPES[dtype], parts.data_ptr(),
+                                            lse.data_ptr(), _lib.view4(out.unsqueeze(0)),
+                                            _lib.stream_ptr(parts.device)))
+    return out
+
+
+def _concat_scores(gathered, nb, L):
+    """``gathered [world, Hq, L]`` (rank r holds blocks [r L, (r + 1) L)) -> ``[Hq, nb]``."""
+    world, Hq, _ = gathered.shape
+    return gathered.permute(1, 0, 2).reshape(Hq, world * L)[:, :nb].contiguous()
+
+
+def emulate_step(shards, selector, q, sm_scale=None):
+    """One decode step over all shards in one process (no collectives)."""
+    L = shards[0].cap
+    Hq, D = q.shape
+    gathered = torch.zeros((len(shards), Hq, L), dtype=torch.float32, device=q.device)
+    for r, sh in enumerate(shards):
+        sh.local_scores(q, gathered[r])
+    scores = _concat_scores(gathered, selector.nb, L)
+    table, sel_lens = selector.select(scores)
+    scale = 1.0 / math.sqrt(D) if sm_scale is None else float(sm_scale)
+    parts = [sh.attend_partial(q, table, sel_lens, scale) for sh in shards]
+    o = torch.stack([p[0] for p in parts])
+    lse = torch.stack([p[1] for p in parts])
+    return combine(o, lse, q.dtype), table, sel_lens
+
+
+class TorchGroup:
+    """All-gather over a ``torch.distributed`` process group (NCCL for CUDA tensors)."""
+
+    def __init__(self, group=None):
+        import torch.distributed as dist
+        self.dist = dist
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+
+    def all_gather(self, t):
+        out = torch.empty((self.world,) + tuple(t.shape), dtype=t.dtype, device=t.device)
+        self.dist.all_gather_into_tensor(out, t.contiguous(), group=self.group)
+        return out
+
+
+class ShardedDecoder:
+    """This rank's part of a sequence-sharded decode step.
+
+    ``K_local``/``V_local``: ``[Hkv, S_local, D]``, the tokens of this rank's
+    block range ``shard_range(ceil(S_total / bs), world, rank)``."""
+
+    def __init__(self, K_local, V_local, S_total, n_q_heads, block_size, comm, **select_kw):
+        self.comm = comm
+        self.nb = -(-S_total // block_size)
+        self.L = shard_blocks(self.nb, comm.world)
+        lo, n = shard_range(self.nb, comm.world, comm.rank)
+        if n != -(-K_local.shape[1] // block_size) and K_local.shape[1] > 0:
+            raise ValueError("local K/V do not cover this rank's block range")
+        self.shard = ShardCache(K_local, V_local, lo, n_q_heads, block_size, capacity_blocks=self.L)
+        Hkv, _, D = K_local.shape
+        self.selector = Selector(S_total, n_q_heads, Hkv, D, block_size, K_local.dtype,
+                                 K_local.device, **select_kw)
+        self.scores = torch.zeros((n_q_heads, self.L), dtype=torch.float32, device=K_local.device)
+
+    def step(self, q, sm_scale=None):
+        """``q [Hq, D]`` (identical on every rank) -> ``out [Hq, D]`` on every rank."""
+        Hq, D = q.shape
+        self.shard.local_scores(q, self.scores)
+        gathered = self.comm.all_gather(self.scores)                  # [world, Hq, L]
+        scores = _concat_scores(gathered, self.nb, self.L)
+        table, sel_lens = self.selector.select(scores)
+        scale = 1.0 / math.sqrt(D) if sm_scale is None else float(sm_scale)
+        o, lse = self.shard.attend_partial(q, table, sel_lens, scale)
+        parts = self.comm.all_gather(o)                               # [world, Hq, D]
+        lses = self.comm.all_gather(lse)                              # [world, Hq]
+        return combine(parts, lses, q.dtype)

@@ -332,6 +332,65 @@ def run_cpu(S, seed, max_steps, budget_s, threads):
 
 
 # ---------------------------------------------------------------------------
+# ---------------------------------------------------------------------------
+# cfg4: one 1M-token sequence, sequence-sharded over the ranks (not the default)
+# ---------------------------------------------------------------------------
+CFG4 = dict(Hq=64, Hkv=8, D=128, bs=16, S=1 << 20, avg=256, k_min=2, k_max=1024)
+
+
+def run_cfg4(steps, warmup, world, rank, device):
+    """Eager decode steps of the sharded path (single-GPU step at N=1); returns
+    (us per step on this rank, algorithmic bytes per step of the whole job)."""
+    import torch
+    from adakv_b200.batch import BatchedDecoder
+    from adakv_b200.sharded import ShardedDecoder, TorchGroup, shard_range
+    c = CFG4
+    Hq, Hkv, D, bs, S = c["Hq"], c["Hkv"], c["D"], c["bs"], c["S"]
+    kw = dict(avg_budget=c["avg"], k_min=c["k_min"], k_max=c["k_max"])
+    nb = S // bs
+    lo, n = shard_range(nb, world, rank)
+    t0, t1 = lo * bs, min(S, (lo + n) * bs)
+    g = torch.Generator(device=device).manual_seed(0)
+    q = torch.randn((Hq, D), device=device, generator=g).to(torch.bfloat16)
+    Kl = torch.empty((Hkv, t1 - t0, D), dtype=torch.bfloat16, device=device)
+    Vl = torch.empty_like(Kl)
+    for h in range(Hkv):  # the same values on every rank: rows generated in sequence order
+        gk = torch.Generator(device=device).manual_seed(1000 + h)
+        Kl[h] = torch.randn((S, D), device=device, generator=gk)[t0:t1].to(torch.bfloat16)
+        gv = torch.Generator(device=device).manual_seed(2000 + h)
+        Vl[h] = torch.randn((S, D), device=device, generator=gv)[t0:t1].to(torch.bfloat16)
+    if world == 1:
+        dec = BatchedDecoder(1, Hq, Hkv, D, bs, S, torch.bfloat16, device, **kw)
+        dec.load(Kl[None], Vl[None], [S])
+        step = lambda: dec.step(q[None])
+        sets = lambda: dec.selected_sets()
+    else:
+        dec = ShardedDecoder(Kl, Vl, S, Hq, bs, TorchGroup(), **kw)
+        step = lambda: dec.step(q)
+        sets = lambda: [dec.selector.table[h, : int(dec.selector.sel_lens[h])].cpu().numpy()
+                        for h in range(Hq)]
+    for _ in range(max(3, warmup)):
+        step()
+    torch.cuda.synchronize(device)
+    union = 0
+    ss = sets()
+    g_ = Hq // Hkv
+    for kv in range(Hkv):
+        union += len(set().union(*[set(x.tolist()) for x in ss[kv * g_:(kv + 1) * g_]]))
+    nbytes = Hkv * nb * D * 4 + union * bs * D * 2 * 2
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    a.record()
+    for _ in range(steps):
+        step()
+    b.record()
+    torch.cuda.synchronize(device)
+    return a.elapsed_time(b) * 1000.0 / steps, nbytes
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -344,6 +403,8 @@ def main():
                     help="independent layer states stepped per graph replay")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=["cfg1", "cfg4"], default="cfg1",
+                    help="cfg4: one 1M-token sequence sharded over the ranks (not the headline)")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -379,6 +440,43 @@ def main():
     torch.cuda.set_device(device)
     from adakv_b200 import _lib
     _lib.lib()
+
+    if args.workload == "cfg4":
+        steps = min(args.steps, 200)
+        us, nbytes = run_cfg4(steps, args.warmup, world, rank, device)
+        if world > 1:
+            t = torch.tensor([us], device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            us = float(t.item())
+        if rank == 0:
+            peaks = {}
+            try:
+                with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+                    peaks = json.load(f)
+            except OSError:
+                pass
+            peak = float(peaks.get("hbm_gbs", 6650.0)) * world
+            achieved = nbytes / (us * 1e-6) / 1e9
+            c = CFG4
+            print(json.dumps({
+                "metric": METRIC, "value": us, "unit": "us", "n_gpus": world, "steps": steps,
+                "warmup": args.warmup, "ms_per_step": us / 1000.0, "higher_is_better": False,
+                "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic (seeded Gaussian K/V/q)",
+                "config": {"workload": f"cfg4 one {c['S']}-token sequence, {c['Hq']} q / {c['Hkv']} KV "
+                                       f"heads, head_dim {c['D']}, block {c['bs']}, avg_budget "
+                                       f"{c['avg']}, k_max {c['k_max']}, bf16",
+                           "parallelism": f"sequence-sharded x{world} (NCCL all-gather of scores "
+                                          "and of (o, lse) partials)" if world > 1 else "single GPU",
+                           "timing": "CUDA events around eager steps, max over ranks"},
+                "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                             "frac": achieved / peak, "traffic": None,
+                             "scope": "fp32 centroid table + union of selected K/V blocks, all ranks"},
+            }), flush=True)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
 
     results = {}
     for S in args.contexts:

@@ -10,6 +10,8 @@
  *   adakv_plan             q.centroid estimator, entropy budget, top-k  (b)(c)
  *   adakv_attend           ragged block-sparse split-KV flash decode    (d)
  *   adakv_decode_step      adakv_plan followed by adakv_attend          (b)-(d)
+ *   adakv_estimate / adakv_select / adakv_attend_partial / adakv_combine
+ *                          the same step split for a sequence sharded over GPUs (e)
  *
  * Conventions
  *   - Every function returns ADAKV_OK (0) or an error code; the message of
@@ -203,6 +205,50 @@ int adakv_decode_step(const adakv_geometry* geo, const adakv_select_params* sp,
 /* Synchronise `stream`, copy the workspace's device status word (ADAKV_ST_*
  * bits) to *status and clear it. */
 int adakv_read_status(void* workspace, uint32_t* status, void* stream);
+
+/* ---- sequence-sharded decode (one sequence's blocks split over GPUs) ----
+ * The reference decodes one sequence on one device; these four calls split
+ * its steps so that a long sequence can be sharded by contiguous blocks:
+ * each rank scores its shard (adakv_estimate, the block scoring of
+ * adakv/estimator.py:62-74), the ranks all-gather the score rows, every rank
+ * selects on the full rows (adakv_select, adakv/budget.py:45-86 +
+ * adakv/selector.py:18-60; identical tables everywhere), attends over the
+ * blocks it holds (adakv_attend_partial) and the per-rank outputs are merged
+ * by their log-sum-exp (adakv_combine).  Collectives are the caller's. */
+
+/* Block scores q . centroid of every block of the cache described by `geo`
+ * into scores[(b * Hq + h) * score_stride + j] (float32, unscaled).
+ * Workspace: adakv_plan_workspace_bytes(geo, any params). */
+int adakv_estimate(const adakv_geometry* geo, const adakv_view* q, const float* centroid,
+                   const int32_t* seq_lens, float* scores, int32_t score_stride, void* workspace,
+                   size_t workspace_bytes, void* stream);
+
+/* Entropy budget + top-k over caller-given score rows (the layout written by
+ * adakv_estimate; `geo` describes the whole sequence).  Outputs as adakv_plan. */
+int adakv_select(const adakv_geometry* geo, const adakv_select_params* sp, const float* scores,
+                 int32_t score_stride, const int32_t* seq_lens, int32_t* block_table,
+                 int32_t table_width, int32_t* sel_lens, void* workspace, size_t workspace_bytes,
+                 void* stream);
+
+/* Attention of every query head over the selected blocks that this cache
+ * holds: `block_table` lists global block ids, the cache (`geo`, k, v,
+ * seq_lens) holds global blocks [block_offset, block_offset + nb); other ids
+ * are skipped.  Writes the normalised output out_f32[b * Hq + h][D] (float32)
+ * and lse[b * Hq + h] = log sum over the attended tokens of
+ * exp(q . k * sm_scale) (-inf when the head attends to nothing here).
+ * Workspace: adakv_attend_workspace_bytes(geo, table_width). */
+int adakv_attend_partial(const adakv_geometry* geo, const adakv_view* q, const adakv_view* k,
+                         const adakv_view* v, const int32_t* block_table, int32_t table_width,
+                         const int32_t* sel_lens, int32_t block_offset, const int32_t* seq_lens,
+                         float sm_scale, float* out_f32, float* lse, void* workspace,
+                         size_t workspace_bytes, void* stream);
+
+/* out[b, h] = sum_n exp(lse[n][r] - LSE) parts[n][r][:] with r = b * Hq + h
+ * and LSE = log sum_n exp(lse[n][r]); rows with every lse = -inf get zeros.
+ * parts: [n_parts, batch * n_q_heads, head_dim] float32; lse: [n_parts, rows]. */
+int adakv_combine(int32_t n_parts, int32_t batch, int32_t n_q_heads, int32_t head_dim,
+                  int32_t dtype, const float* parts, const float* lse, const adakv_view* out,
+                  void* stream);
 
 #ifdef __cplusplus
 }

@@ -1,0 +1,122 @@
+"""Sequence-sharded decode on one GPU (shards emulated in one process):
+adakv_estimate / adakv_select / adakv_attend_partial / adakv_combine through
+the C ABI must select exactly what the single-GPU step selects and produce
+the same output; at the cfg4 shape (1M tokens, 64/8 heads) the selection is
+also checked against the oracle's budget and top-k on the GPU scores."""
+import numpy as np
+import pytest
+import torch
+
+from adakv_b200 import _lib
+from adakv_b200.batch import BatchedDecoder
+from adakv_b200.sharded import Selector, ShardCache, emulate_step, shard_blocks, shard_range
+from adakv_b200.synth import make_decode_case
+from oracle import adakv_oracle as O
+
+pytestmark = pytest.mark.gpu
+BF16_TOL = 2e-2
+
+
+def _need_cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+
+
+def _shards(K, V, nb, world, Hq, bs):
+    L = shard_blocks(nb, world)
+    out = []
+    for r in range(world):
+        lo, n = shard_range(nb, world, r)
+        t0, t1 = lo * bs, min(K.shape[1], (lo + n) * bs)
+        out.append(ShardCache(K[:, t0:t1], V[:, t0:t1], lo, Hq, bs, capacity_blocks=L))
+    return out
+
+
+def _single(K, V, q, S, Hq, bs, **kw):
+    Hkv, _, D = K.shape
+    dec = BatchedDecoder(1, Hq, Hkv, D, bs, S, K.dtype, "cuda", **kw)
+    dec.load(K[None], V[None], [S])
+    scores = torch.zeros((Hq, dec.nb_cap), dtype=torch.float32, device="cuda")
+    dec.plan(q[None], scores_out=scores)
+    sets = [np.sort(s) for s in dec.selected_sets()]
+    out = dec.step(q[None])[0].clone()
+    return sets, out, scores
+
+
+@pytest.mark.parametrize("world", [2, 3, 4])
+def test_emulated_shards_match_single_gpu(world):
+    _need_cuda()
+    Hq, Hkv, D, bs, S = 32, 8, 128, 16, 65536 + 7 * 16 + 5
+    kw = dict(avg_budget=64, k_min=2, k_max=512)
+    case = make_decode_case(31, 1, Hq, Hkv, D, S, bs, "bf16")
+    K = torch.from_numpy(case.K[0]).to("cuda", torch.bfloat16)
+    V = torch.from_numpy(case.V[0]).to("cuda", torch.bfloat16)
+    q = torch.from_numpy(case.q[0]).to("cuda", torch.bfloat16)
+    sets1, out1, _ = _single(K, V, q, S, Hq, bs, **kw)
+    nb = -(-S // bs)
+    shards = _shards(K, V, nb, world, Hq, bs)
+    sel = Selector(S, Hq, Hkv, D, bs, torch.bfloat16, "cuda", **kw)
+    out, table, sel_lens = emulate_step(shards, sel, q)
+    torch.cuda.synchronize()
+    bt, sl = table.cpu().numpy(), sel_lens.cpu().numpy()
+    for h in range(Hq):
+        assert np.array_equal(np.sort(bt[h, : sl[h]]), sets1[h]), f"head {h}"
+    err = (out.float() - out1.float()).abs().max().item()
+    assert err < BF16_TOL, f"max abs err vs single GPU {err:.3e}"
+    # against the oracle at this size too
+    ref = O.decode_step(case.q[0], case.K[0], case.V[0], block_size=bs, **kw)
+    err_o = np.abs(out.float().cpu().numpy() - ref["out"]).max()
+    assert err_o < BF16_TOL, f"max abs err vs oracle {err_o:.3e}"
+
+
+def test_cfg4_shape_1m_tokens_sharded_8_ways():
+    """cfg4: one 1,048,576-token sequence, 64 q / 8 KV heads, avg_budget 256."""
+    _need_cuda()
+    Hq, Hkv, D, bs, S = 64, 8, 128, 16, 1 << 20
+    kw = dict(avg_budget=256, k_min=2, k_max=1024)
+    g = torch.Generator(device="cuda").manual_seed(4)
+    q = torch.randn((Hq, D), device="cuda", generator=g)
+    K = torch.randn((Hkv, S, D), device="cuda", generator=g)
+    V = torch.randn((Hkv, S, D), device="cuda", generator=g).to(torch.bfloat16)
+    nb = S // bs
+    # planted retrieval blocks on even KV heads, recency on odd (the synth recipe)
+    qm = q.view(Hkv, Hq // Hkv, D).mean(1)
+    qhat = qm / qm.norm(dim=-1, keepdim=True)
+    for h in range(Hkv):
+        if h % 2 == 0:
+            for blk in torch.randint(0, nb, (4,), device="cuda", generator=g).tolist():
+                K[h, blk * bs:(blk + 1) * bs] += 3.0 * qhat[h]
+        else:
+            t = torch.arange(S, device="cuda", dtype=torch.float32)
+            K[h] += (0.02 * t / 16.0)[:, None] * qhat[h][None, :]
+    K = K.to(torch.bfloat16)
+    q = q.to(torch.bfloat16)
+    sets1, out1, scores = _single(K, V, q, S, Hq, bs, **kw)
+    # selection vs the oracle's budget + top-k on the same (GPU) scores
+    sc = scores[:, :nb].cpu().numpy().astype(np.float32)
+    k, raw = O.allocate_budget(sc, kw["avg_budget"], kw["k_min"], kw["k_max"], 1, 4, 1,
+                               return_raw=True)
+    mask, _ = O.select_blocks(sc, k, 1, 4, 1)
+    n_exact, n_budget, n_score, failures = O.compare_selection(sc, k, raw, mask, sets1, 1, 4, 1)
+    assert not failures, failures[:4]
+    assert n_exact + n_budget + n_score == Hq
+    # 8 emulated shards select the same blocks and give the same output
+    shards = _shards(K, V, nb, 8, Hq, bs)
+    sel = Selector(S, Hq, Hkv, D, bs, torch.bfloat16, "cuda", **kw)
+    out, table, sel_lens = emulate_step(shards, sel, q)
+    torch.cuda.synchronize()
+    bt, sl = table.cpu().numpy(), sel_lens.cpu().numpy()
+    for h in range(Hq):
+        assert np.array_equal(np.sort(bt[h, : sl[h]]), sets1[h]), f"head {h}"
+    err = (out.float() - out1.float()).abs().max().item()
+    assert err < BF16_TOL, f"max abs err vs single GPU {err:.3e}"
+    # attention of a few heads against a float64 evaluation over their blocks
+    for h in (0, 17, 63):
+        blocks = sets1[h]
+        tok = (blocks[:, None] * bs + np.arange(bs)[None, :]).ravel()
+        kk = K[h // (Hq // Hkv), torch.from_numpy(tok).cuda()].double()
+        vv = V[h // (Hq // Hkv), torch.from_numpy(tok).cuda()].double()
+        a = (kk @ q[h].double()) / np.sqrt(D)
+        ref = torch.softmax(a, 0) @ vv
+        e = (out[h].double() - ref).abs().max().item()
+        assert e < BF16_TOL, f"head {h}: {e:.3e}"
