@@ -19,6 +19,24 @@ import torch
 from . import _lib
 
 
+def partition_batch(seq_lens, world):
+    """Contiguous, context-balanced split of a batch over ``world`` ranks (no
+    collective: sequences are independent).  Returns ``[(start, end)]`` per
+    rank; boundaries are placed where the running context sum crosses
+    ``r / world`` of the total."""
+    lens = [int(x) for x in seq_lens]
+    total = sum(lens)
+    bounds, acc, b = [0], 0, 0
+    for r in range(1, world):
+        target = total * r / world
+        while b < len(lens) and acc + lens[b] / 2 <= target:
+            acc += lens[b]
+            b += 1
+        bounds.append(max(b, bounds[-1]))
+    bounds.append(len(lens))
+    return [(bounds[r], bounds[r + 1]) for r in range(world)]
+
+
 class BatchedDecoder:
     def __init__(self, batch, n_q_heads, n_kv_heads, head_dim, block_size, capacity, dtype,
                  device="cuda", avg_budget=64, k_min=2, k_max=64, n_sink_blocks=1,

@@ -112,3 +112,15 @@ def test_shard_ranges_cover_the_sequence_once():
                 assert lo % 32 == 0 or n == 0
                 covered.extend(range(lo, lo + n))
             assert covered == list(range(nb))
+
+
+def test_partition_batch_is_contiguous_and_balanced():
+    from adakv_b200.batch import partition_batch
+    from adakv_b200.synth import ragged_seq_lens
+    lens = ragged_seq_lens(0, 64, 8192, 131072)
+    for world in (1, 2, 4, 8):
+        parts = partition_batch(lens, world)
+        assert parts[0][0] == 0 and parts[-1][1] == 64
+        assert all(a[1] == b[0] for a, b in zip(parts, parts[1:]))
+        sums = [int(lens[a:b].sum()) for a, b in parts]
+        assert max(sums) - min(sums) <= int(lens.max())  # within one sequence of balance
