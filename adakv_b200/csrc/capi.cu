@@ -180,8 +180,8 @@ int attend_split(const adakv_geometry* g) {
 // exchange slots are cleared by the estimator of the same call and the
 // attend arrival counters are reset by the CTA that merges.
 struct WsLayout {
-  size_t status, epoch, slots, scores, bitmap, part, counters, bytes;
-  int score_stride, bm_words, split;
+  size_t status, epoch, slots, scores, stats, bitmap, part, counters, bytes;
+  int score_stride, stats_stride, bm_words, split;
 };
 
 WsLayout make_ws(const adakv_geometry* g, bool with_plan) {
@@ -197,6 +197,8 @@ WsLayout make_ws(const adakv_geometry* g, bool with_plan) {
   L.epoch = take(16);
   L.slots = with_plan ? take(sizeof(PlanSlot) * rows * kPlanSlotsPerRow) : 0;
   L.scores = with_plan ? take(sizeof(float) * (size_t)rows * L.score_stride) : 0;
+  L.stats_stride = ceil_div(g->nb_cap, kEstRows) * kEstConsumerWarps + 1;
+  L.stats = with_plan ? take(sizeof(float) * kStatF * (size_t)rows * L.stats_stride) : 0;
   L.bitmap = take(sizeof(uint32_t) * (size_t)rows * L.bm_words);
   L.part = take(sizeof(float) * (size_t)g->batch * g->n_kv_heads * L.split * gq * (g->head_dim + 2));
   L.counters = take(sizeof(uint32_t) * (size_t)g->batch * g->n_kv_heads);
@@ -221,9 +223,9 @@ int check_workspace(void* ws, size_t bytes, size_t need) {
 // budget + top-k (plan kernel) over score rows already on the device; the
 // exchange slots of the workspace must be cleared before it runs
 int enqueue_select(const DeviceState* ds, const adakv_geometry* g, const adakv_select_params* sp,
-                   const float* scores, int score_stride, const int32_t* seq_lens,
-                   int32_t* block_table, int32_t table_width, int32_t* sel_lens, void* ws,
-                   const WsLayout& L, cudaStream_t st) {
+                   const float* scores, int score_stride, const float* stats,
+                   const int32_t* seq_lens, int32_t* block_table, int32_t table_width,
+                   int32_t* sel_lens, void* ws, const WsLayout& L, cudaStream_t st) {
   const int nb_max = ceil_div(g->max_seq_len, g->block_size);
   const bool pdl = pdl_enabled();
   PlanParams pp{};
@@ -235,6 +237,8 @@ int enqueue_select(const DeviceState* ds, const adakv_geometry* g, const adakv_s
   pp.cfg = to_cfg(sp);
   pp.scores = scores;
   pp.score_stride = score_stride;
+  pp.stats = stats;
+  pp.stats_stride = L.stats_stride;
   pp.epoch = ws_at<uint32_t>(ws, L.epoch);
   pp.slots = ws_at<PlanSlot>(ws, L.slots);
   pp.sel_lens = sel_lens;
@@ -310,6 +314,11 @@ int enqueue_plan(const DeviceState* ds, const adakv_geometry* g, const adakv_sel
   ep.epoch = ws_at<uint32_t>(ws, L.epoch);
   ep.slots = ws_at<PlanSlot>(ws, L.slots);
   ep.counters = ws_at<uint32_t>(ws, L.counters);
+  ep.stats = ws_at<float>(ws, L.stats);
+  ep.stats_stride = L.stats_stride;
+  ep.n_sink = sp->n_sink_blocks;
+  ep.n_local = sp->n_local_blocks;
+  ep.temperature = (float)(sp->temperature > 1e-6 ? sp->temperature : 1e-6);
   if (n_new > 0) {
     ep.k = to_view(k);
     ep.v = to_view(v);
@@ -325,8 +334,8 @@ int enqueue_plan(const DeviceState* ds, const adakv_geometry* g, const adakv_sel
   oe.pdl = pdl;
   CUDA_TRY(launch_estimate(ep, g->dtype, g->head_dim, nb_max, est_grid, st, oe));
 
-  return enqueue_select(ds, g, sp, ep.scores, ep.score_stride, seq_lens, block_table, table_width,
-                        sel_lens, ws, L, st);
+  return enqueue_select(ds, g, sp, ep.scores, ep.score_stride, ep.stats, seq_lens, block_table,
+                        table_width, sel_lens, ws, L, st);
 }
 
 // attend over the bitmaps in the workspace
@@ -737,6 +746,7 @@ int adakv_estimate(const adakv_geometry* geo, const adakv_view* q, const float* 
   ep.bs = geo->block_size;
   ep.scores = scores;
   ep.score_stride = score_stride;
+  ep.temperature = 1.0f;
   ep.status = ws_at<uint32_t>(workspace, L.status);
   ep.stages = estimate_stages(geo->dtype, geo->head_dim, ep.g, geo->batch);
   const int64_t chunks = (int64_t)geo->batch * geo->n_kv_heads * ceil_div(nb_max, kEstRows);
@@ -770,8 +780,8 @@ int adakv_select(const adakv_geometry* geo, const adakv_select_params* sp, const
   // the exchange slots start cleared (the estimator does this on the fused path)
   CUDA_TRY(cudaMemsetAsync(ws_at<char>(workspace, L.slots), 0,
                            sizeof(PlanSlot) * (size_t)geo->batch * geo->n_q_heads * kPlanSlotsPerRow, st));
-  return enqueue_select(ds, geo, sp, scores, score_stride, seq_lens, block_table, table_width,
-                        sel_lens, workspace, L, st);
+  return enqueue_select(ds, geo, sp, scores, score_stride, nullptr, seq_lens, block_table,
+                        table_width, sel_lens, workspace, L, st);
 }
 
 int adakv_attend_partial(const adakv_geometry* geo, const adakv_view* q, const adakv_view* k,

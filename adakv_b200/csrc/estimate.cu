@@ -143,6 +143,8 @@ __global__ void __launch_bounds__(kEstThreads, 1) estimate_kernel(EstParams p) {
   const int stage_f = TILE_F + (p.g * qrow + 15) / 16 * 4;    // floats per stage (16-B multiple)
   int* seq_base = reinterpret_cast<int*>(ring + stages * stage_f);  // [B+1] first chunk of seq
   int* seq_cph = seq_base + p.B + 1;                                 // [B] chunks per KV head
+  const float Tf = p.temperature;
+  const bool unit_t = (Tf == 1.0f);
 
   if (tid == 0) {
     for (int s = 0; s < stages; ++s) {
@@ -231,13 +233,29 @@ __global__ void __launch_bounds__(kEstThreads, 1) estimate_kernel(EstParams p) {
     // previous grid, which may still be reading the slots rewritten here.
     using Raw = typename RawVec<T, E>::type;
     bool waited = false;
+    // the rows the append refreshes are scored here; their softmax partial
+    // goes to the last stats slot of each row (empty when nothing is appended)
+    auto store_tail = [&](int b, int kvh, const SoftPart& t) {
+      if (p.stats && lane < p.g)
+        soft_store(p.stats + ((int64_t)(b * p.Hq + kvh * p.g + lane) * p.stats_stride +
+                              p.stats_stride - 1) * kStatF, t);
+    };
+    if (!appending) {
+      for (int pair = blockIdx.x; pair < p.B * p.Hkv; pair += gridDim.x)
+        store_tail(pair / p.Hkv, pair % p.Hkv, soft_empty());
+    }
     if (appending) {
       for (int pair = blockIdx.x; pair < p.B * p.Hkv; pair += gridDim.x) {
         const int b = pair / p.Hkv, kvh = pair - b * p.Hkv;
         const int S = seq_len_of(p.seq_lens, b, p.max_seq_len);
-        if (S <= 0 || S > p.max_seq_len || S < p.n_new) continue;
+        SoftPart tail = soft_empty();
+        if (S <= 0 || S > p.max_seq_len || S < p.n_new) {
+          store_tail(b, kvh, tail);
+          continue;
+        }
         const int S_old = S - p.n_new;
         const int nb = ceil_div(S, p.bs);
+        const int sink = imin(p.n_sink, nb), local = imin(p.n_local, nb);
         const int d = lane * E;
         T* kc = static_cast<T*>(const_cast<void*>(p.k.data)) + b * p.k.sb + kvh * p.k.sh + d;
         T* vc = static_cast<T*>(const_cast<void*>(p.v.data)) + b * p.v.sb + kvh * p.v.sh + d;
@@ -301,8 +319,12 @@ __global__ void __launch_bounds__(kEstThreads, 1) estimate_kernel(EstParams p) {
             for (int o = 16; o; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
             if (lane == 0)
               p.scores[(int64_t)(b * p.Hq + kvh * p.g + j) * p.score_stride + blk] = part;
+            if (lane == j)
+              soft_add(tail, part, unit_t ? part : __fdiv_rn(part, Tf),
+                       !(blk < sink || blk >= nb - local));
           }
         }
+        store_tail(b, kvh, tail);
       }
     }
     if (!waited) pdl_wait();
@@ -350,6 +372,7 @@ __global__ void __launch_bounds__(kEstThreads, 1) estimate_kernel(EstParams p) {
           for (int e = 0; e < E; ++e) qr[j][e] = 0.f;
         }
       }
+      float scs[NG];  // this lane's scores of the chunk (kept for the softmax partial)
 #pragma unroll
       for (int grp = 0; grp < NG; ++grp) {
         const int rbase = warp * RPW + grp * R;
@@ -367,12 +390,66 @@ __global__ void __launch_bounds__(kEstThreads, 1) estimate_kernel(EstParams p) {
           }
         }
         const float sc = warp_reduce_scatter32(v, lane);
+        scs[grp] = sc;
         const int row = rbase + lane / GP, j = lane % GP;
         if (j < p.g && row < lim)
           p.scores[(int64_t)(b * p.Hq + kvh * p.g + j) * p.score_stride + row0 + row] = sc;
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(&empty_bar[s]);
+      if (lane == 0) mbar_arrive(&empty_bar[s]);  // the stage refills while the partial is built
+      if (p.stats) {
+        // Softmax partial of this warp's rows of each head: maxima over the
+        // lanes of a head first (independent xor shuffles), then one exp per
+        // score relative to the head's warp max, then xor sums.
+        const int sink = imin(p.n_sink, nb), local = imin(p.n_local, nb);
+        float zv[NG];
+        bool ok[NG], cont[NG];
+        float m = -INFINITY, mxl = -INFINITY, cmxl = -INFINITY, csl = 0.f, cql = 0.f;
+#pragma unroll
+        for (int grp = 0; grp < NG; ++grp) {
+          const int row = warp * RPW + grp * R + lane / GP, j = lane % GP;
+          const int blk = row0 + row;
+          ok[grp] = j < p.g && row < lim;
+          cont[grp] = ok[grp] && !(blk < sink || blk >= nb - local);
+          zv[grp] = unit_t ? scs[grp] : __fdiv_rn(scs[grp], Tf);
+          if (ok[grp]) {
+            m = fmaxf(m, zv[grp]);
+            mxl = fmaxf(mxl, scs[grp]);
+          }
+          if (cont[grp]) {
+            cmxl = fmaxf(cmxl, scs[grp]);
+            csl += scs[grp];
+            cql = fmaf(scs[grp], scs[grp], cql);
+          }
+        }
+#pragma unroll
+        for (int o = GP; o < 32; o <<= 1) {
+          m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+          mxl = fmaxf(mxl, __shfl_xor_sync(0xffffffffu, mxl, o));
+          cmxl = fmaxf(cmxl, __shfl_xor_sync(0xffffffffu, cmxl, o));
+        }
+        float zl = 0.f, al = 0.f;
+#pragma unroll
+        for (int grp = 0; grp < NG; ++grp) {
+          if (ok[grp]) {
+            const float d = zv[grp] - m;
+            const float e = expf(d);
+            zl += e;
+            al = fmaf(e, d, al);
+          }
+        }
+#pragma unroll
+        for (int o = GP; o < 32; o <<= 1) {
+          zl += __shfl_xor_sync(0xffffffffu, zl, o);
+          al += __shfl_xor_sync(0xffffffffu, al, o);
+          csl += __shfl_xor_sync(0xffffffffu, csl, o);
+          cql += __shfl_xor_sync(0xffffffffu, cql, o);
+        }
+        const SoftPart part{mxl, cmxl, csl, cql, m, zl, al};
+        if (lane < p.g)
+          soft_store(p.stats + ((int64_t)(b * p.Hq + kvh * p.g + lane) * p.stats_stride +
+                                ch * kEstConsumerWarps + warp) * kStatF, part);
+      }
     }
     pdl_wait();  // (no-op for ordering here; keeps every thread's wait uniform)
   }

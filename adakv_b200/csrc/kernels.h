@@ -33,6 +33,7 @@ struct __align__(8) PlanSlot {
 // (b) estimator (+ fused append of the step's new tokens)
 // ---------------------------------------------------------------------------
 constexpr int kEstMaxStages = 8;       // TMA ring depth limit
+constexpr int kStatF = 8;              // floats per softmax partial
 constexpr size_t kEstSmemBudget = 200 * 1024;  // dynamic shared memory of one estimator CTA
 constexpr int kEstConsumerWarps = 8;   // 8 warps x 8 rows = kEstRows
 constexpr int kEstThreads = (kEstConsumerWarps + 2) * 32;  // + producer warp + refresh warp
@@ -50,6 +51,15 @@ struct EstParams {
   uint32_t* epoch;        // incremented once per launch (per-call tag for the plan barrier)
   PlanSlot* slots;        // [B*Hq*kPlanSlotsPerRow] exchange slots: cleared here, before the plan
   uint32_t* counters;     // [B*Hkv] attend arrival counts: cleared here, before the attend
+  // Per-(head, 64-block chunk, consumer warp) softmax partials for the plan
+  // (nullable): stats[(row * stats_stride + chunk * 8 + warp) * 8 + {max s,
+  // content max, content sum, content sum of squares, m = max z,
+  // sum e^(z - m), sum e^(z - m) (z - m)}], z = s / temperature; the last
+  // slot of a row holds the rows the fused append scored.
+  float* stats;
+  int stats_stride;
+  int n_sink, n_local;    // forced blocks (excluded from the content statistics)
+  float temperature;      // max(T, 1e-6) as float
   // fused append: n_new > 0 and k_new.data != NULL
   View k, v, k_new, v_new;
   int n_new;
@@ -89,6 +99,8 @@ struct PlanParams {
   int* sel_lens;            // [B*Hq] out
   int* block_table;         // [B*Hq, table_width] out, ascending block ids
   int table_width;
+  const float* stats;       // estimator partials (EstParams::stats) or NULL
+  int stats_stride;
   uint32_t* bitmap;         // [B*Hq, bm_words] out, bit j = block j selected
   int bm_words;
   int csize;                // CTAs of the cluster splitting each row
@@ -214,5 +226,76 @@ PlanLayout plan_layout(int nb_max, int csize);
 int plan_active_clusters(const PlanLayout& l);
 size_t attend_smem_bytes(int dtype, int D, int bs, int nbt, int g, int nw_max, int slice_cap,
                          int split);
+
+#ifdef __CUDACC__
+// Softmax partial of a set of blocks of one query head: max score, content
+// max / sum / sum of squares (sink and local blocks excluded), and
+// (m, Z, A) = (max z, sum e^(z - m), sum e^(z - m) (z - m)), z = s / T.
+struct SoftPart {
+  float mx, cmx, cs, cq, m, Z, A;
+};
+
+__device__ __forceinline__ SoftPart soft_empty() {
+  return SoftPart{-INFINITY, -INFINITY, 0.f, 0.f, -INFINITY, 0.f, 0.f};
+}
+
+__device__ __forceinline__ void soft_add(SoftPart& a, float s, float z, bool content) {
+  a.mx = fmaxf(a.mx, s);
+  if (content) {
+    a.cmx = fmaxf(a.cmx, s);
+    a.cs += s;
+    a.cq = fmaf(s, s, a.cq);
+  }
+  if (z > a.m) {
+    const float f = a.m == -INFINITY ? 0.f : expf(a.m - z);
+    a.A = f * fmaf(a.Z, a.m == -INFINITY ? 0.f : a.m - z, a.A);
+    a.Z = fmaf(a.Z, f, 1.f);
+    a.m = z;
+  } else {
+    const float e = expf(z - a.m);
+    a.Z += e;
+    a.A = fmaf(e, z - a.m, a.A);
+  }
+}
+
+__device__ __forceinline__ void soft_merge(SoftPart& a, const SoftPart& b) {
+  a.mx = fmaxf(a.mx, b.mx);
+  a.cmx = fmaxf(a.cmx, b.cmx);
+  a.cs += b.cs;
+  a.cq += b.cq;
+  const float m = fmaxf(a.m, b.m);
+  if (m == -INFINITY) return;
+  const float fa = a.m == -INFINITY ? 0.f : expf(a.m - m);
+  const float fb = b.m == -INFINITY ? 0.f : expf(b.m - m);
+  const float Aa = a.m == -INFINITY ? 0.f : fa * fmaf(a.Z, a.m - m, a.A);
+  const float Ab = b.m == -INFINITY ? 0.f : fb * fmaf(b.Z, b.m - m, b.A);
+  a.Z = a.Z * fa + b.Z * fb;
+  a.A = Aa + Ab;
+  a.m = m;
+}
+
+__device__ __forceinline__ SoftPart soft_shfl_xor(const SoftPart& a, int o) {
+  SoftPart r;
+  r.mx = __shfl_xor_sync(0xffffffffu, a.mx, o);
+  r.cmx = __shfl_xor_sync(0xffffffffu, a.cmx, o);
+  r.cs = __shfl_xor_sync(0xffffffffu, a.cs, o);
+  r.cq = __shfl_xor_sync(0xffffffffu, a.cq, o);
+  r.m = __shfl_xor_sync(0xffffffffu, a.m, o);
+  r.Z = __shfl_xor_sync(0xffffffffu, a.Z, o);
+  r.A = __shfl_xor_sync(0xffffffffu, a.A, o);
+  return r;
+}
+
+__device__ __forceinline__ void soft_store(float* dst, const SoftPart& a) {
+  reinterpret_cast<float4*>(dst)[0] = make_float4(a.mx, a.cmx, a.cs, a.cq);
+  reinterpret_cast<float4*>(dst)[1] = make_float4(a.m, a.Z, a.A, 0.f);
+}
+
+__device__ __forceinline__ SoftPart soft_load(const float* src) {
+  const float4 u = reinterpret_cast<const float4*>(src)[0];
+  const float4 w = reinterpret_cast<const float4*>(src)[1];
+  return SoftPart{u.x, u.y, u.z, u.w, w.x, w.y, w.z};
+}
+#endif  // __CUDACC__
 
 }  // namespace adakv

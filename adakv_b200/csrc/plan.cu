@@ -193,137 +193,205 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanParams p) {
     const int sink = imin(p.cfg.n_sink, nb), local = imin(p.cfg.n_local, nb);
     auto forced = [&](int i) -> bool { return i < sink || i >= nb - local; };
 
-    // ---- 1. load the slice: statistics and per-thread softmax partials ----
-    // Each thread keeps (m_t, z_t, a_t) = (max z, sum e^(z - m_t),
-    // sum e^(z - m_t) (z - m_t)) over its blocks, rescaled when m_t grows;
-    // e^(z - m_t) is cached when the slice is one tile (m_t is then final).
     const bool adaptive = nb >= 2 && p.cfg.policy == ADAKV_POLICY_ADAPTIVE;
     const float Tf = (float)(p.cfg.temperature > 1e-6 ? p.cfg.temperature : 1e-6);
     const bool unit_t = (Tf == 1.0f);  // s / 1 == s exactly: skip the division
     auto zof = [&](float v) -> float { return unit_t ? v : __fdiv_rn(v, Tf); };
-    const bool one_tile = n <= kPlanThreads * kPlanILP;
-    const bool ec = p.ecache && one_tile;
-    float mx = -INFINITY, cmx = -INFINITY, csum_f = 0.f, csq_f = 0.f;
-    float m_t = -INFINITY, z_t = 0.f, a_t = 0.f;
-    for (int base = 0; base < n; base += kPlanThreads * kPlanILP) {
-      float v[kPlanILP];
+    float mx, cmx, m_t = -INFINITY;
+    double csum, csq, Ztot = 0.0, Atot = 0.0;
+    bool ec = false;
+    if (p.stats) {
+      // ---- 1'. stage the slice; the row statistics come from the estimator's
+      //      (chunk, warp) softmax partials, merged here by every CTA alike ----
+      for (int base = 0; base < n; base += kPlanThreads * kPlanILP) {
+        float v[kPlanILP];
 #pragma unroll
-      for (int r = 0; r < kPlanILP; ++r) {
-        const int li = base + r * kPlanThreads + tid;
-        v[r] = li < n ? srow[lo + li] : -INFINITY;
-      }
-      float tm = -INFINITY;
+        for (int r = 0; r < kPlanILP; ++r) {
+          const int li = base + r * kPlanThreads + tid;
+          v[r] = li < n ? srow[lo + li] : 0.f;
+        }
+        if (SMEM) {
 #pragma unroll
-      for (int r = 0; r < kPlanILP; ++r) {
-        const int li = base + r * kPlanThreads + tid;
-        if (li < n) {
-          if (SMEM) keys[li] = __float_as_uint(v[r]);
-          mx = fmaxf(mx, v[r]);
-          tm = fmaxf(tm, zof(v[r]));
-          if (!forced(lo + li)) {
-            cmx = fmaxf(cmx, v[r]);
-            csum_f += v[r];
-            csq_f = fmaf(v[r], v[r], csq_f);
+          for (int r = 0; r < kPlanILP; ++r) {
+            const int li = base + r * kPlanThreads + tid;
+            if (li < n) keys[li] = __float_as_uint(v[r]);
           }
         }
       }
-      if (adaptive && tm > m_t) {
-        if (m_t > -INFINITY) {
-          const float sc = expf(m_t - tm);
-          a_t = sc * fmaf(z_t, m_t - tm, a_t);
-          z_t *= sc;
-        }
-        m_t = tm;
+      const int nparts = ceil_div(nb, kEstRows) * kEstConsumerWarps;
+      const float* prow = p.stats + (int64_t)row * p.stats_stride * kStatF;
+      SoftPart acc = soft_empty();
+      for (int c = tid; c <= nparts; c += kPlanThreads)
+        soft_merge(acc, soft_load(prow + (int64_t)(c < nparts ? c : p.stats_stride - 1) * kStatF));
+      for (int t = tid; t < kBuckets; t += kPlanThreads) hist[t] = 0u;
+      if (tid < kPlanMaxCluster) s_taken[tid] = 0;
+      if (tid == 0) {
+        s_ncand = 0;
+        s_nfix = 0;
       }
-      if (adaptive) {
+      {
+        const float wm = warp_max(acc.m), wmx = warp_max(acc.mx), wcmx = warp_max(acc.cmx);
+        if (lane == 0) {
+          wpart[warp] = make_float2(wmx, wcmx);
+          wm_s[warp] = wm;
+        }
+      }
+      __syncthreads();  // also publishes the staged slice
+      const float M = warp_max(lane < kPW ? wm_s[lane] : -INFINITY);
+      mx = warp_max(lane < kPW ? wpart[lane].x : -INFINITY);
+      cmx = warp_max(lane < kPW ? wpart[lane].y : -INFINITY);
+      {
+        double z = 0.0, a = 0.0;
+        if (acc.m > -INFINITY) {
+          const double f = (double)expf(acc.m - M);
+          z = (double)acc.Z * f;
+          a = f * ((double)acc.A + (double)acc.Z * ((double)acc.m - (double)M));
+        }
+        z = warp_sum(z);
+        a = warp_sum(a);
+        const double cs = warp_sum((double)acc.cs), cq = warp_sum((double)acc.cq);
+        if (lane == 0) {
+          wd[warp][0] = z;
+          wd[warp][1] = a;
+          wd[warp][2] = cs;
+          wd[warp][3] = cq;
+        }
+      }
+      __syncthreads();
+      Ztot = warp_sum(lane < kPW ? wd[lane][0] : 0.0);
+      Atot = warp_sum(lane < kPW ? wd[lane][1] : 0.0);
+      csum = warp_sum(lane < kPW ? wd[lane][2] : 0.0);
+      csq = warp_sum(lane < kPW ? wd[lane][3] : 0.0);
+    } else {
+      // ---- 1. load the slice: statistics and per-thread softmax partials ----
+      // Each thread keeps (m_t, z_t, a_t) = (max z, sum e^(z - m_t),
+      // sum e^(z - m_t) (z - m_t)) over its blocks, rescaled when m_t grows;
+      // e^(z - m_t) is cached when the slice is one tile (m_t is then final).
+      const bool one_tile = n <= kPlanThreads * kPlanILP;
+      ec = p.ecache && one_tile;
+      mx = -INFINITY;
+      cmx = -INFINITY;
+      float csum_f = 0.f, csq_f = 0.f;
+      float z_t = 0.f, a_t = 0.f;
+      for (int base = 0; base < n; base += kPlanThreads * kPlanILP) {
+        float v[kPlanILP];
+#pragma unroll
+        for (int r = 0; r < kPlanILP; ++r) {
+          const int li = base + r * kPlanThreads + tid;
+          v[r] = li < n ? srow[lo + li] : -INFINITY;
+        }
+        float tm = -INFINITY;
 #pragma unroll
         for (int r = 0; r < kPlanILP; ++r) {
           const int li = base + r * kPlanThreads + tid;
           if (li < n) {
-            const float d = zof(v[r]) - m_t;
-            const float e = expf(d);
-            if (ec) ecache[li] = e;
-            z_t += e;
-            if (e > 0.f) a_t = fmaf(e, d, a_t);
+            if (SMEM) keys[li] = __float_as_uint(v[r]);
+            mx = fmaxf(mx, v[r]);
+            tm = fmaxf(tm, zof(v[r]));
+            if (!forced(lo + li)) {
+              cmx = fmaxf(cmx, v[r]);
+              csum_f += v[r];
+              csq_f = fmaf(v[r], v[r], csq_f);
+            }
+          }
+        }
+        if (adaptive && tm > m_t) {
+          if (m_t > -INFINITY) {
+            const float sc = expf(m_t - tm);
+            a_t = sc * fmaf(z_t, m_t - tm, a_t);
+            z_t *= sc;
+          }
+          m_t = tm;
+        }
+        if (adaptive) {
+#pragma unroll
+          for (int r = 0; r < kPlanILP; ++r) {
+            const int li = base + r * kPlanThreads + tid;
+            if (li < n) {
+              const float d = zof(v[r]) - m_t;
+              const float e = expf(d);
+              if (ec) ecache[li] = e;
+              z_t += e;
+              if (e > 0.f) a_t = fmaf(e, d, a_t);
+            }
           }
         }
       }
-    }
-    for (int t = tid; t < kBuckets; t += kPlanThreads) hist[t] = 0u;
-    if (tid < kPlanMaxCluster) s_taken[tid] = 0;
-    if (tid == 0) {
-      s_ncand = 0;
-      s_nfix = 0;
-    }
-    // warp partials (softmax partials rescaled to the warp max), then one
-    // fold of the warps by warp 0, then the cluster
-    {
-      const float wm = warp_max(m_t);
-      double zw = 0.0, aw = 0.0;
-      if (adaptive && m_t > -INFINITY) {
-        const double sc = exp((double)m_t - (double)wm);
-        zw = (double)z_t * sc;
-        aw = sc * ((double)a_t + (double)z_t * ((double)m_t - (double)wm));
+      for (int t = tid; t < kBuckets; t += kPlanThreads) hist[t] = 0u;
+      if (tid < kPlanMaxCluster) s_taken[tid] = 0;
+      if (tid == 0) {
+        s_ncand = 0;
+        s_nfix = 0;
       }
-      zw = warp_sum(zw);
-      aw = warp_sum(aw);
-      const float wmx = warp_max(mx), wcmx = warp_max(cmx);
-      const double wsum = warp_sum((double)csum_f), wsq = warp_sum((double)csq_f);
-      if (lane == 0) {
-        wpart[warp] = make_float2(wmx, wcmx);
-        wm_s[warp] = wm;
-        wd[warp][0] = zw;
-        wd[warp][1] = aw;
-        wd[warp][2] = wsum;
-        wd[warp][3] = wsq;
-      }
-    }
-    __syncthreads();  // also publishes the staged slice
-    if (warp == 0) {
-      const bool in = lane < kPW;
-      const float M = warp_max(in ? wm_s[lane] : -INFINITY);
-      double z = 0.0, a = 0.0;
-      if (in && wm_s[lane] > -INFINITY) {
-        const double sc = exp((double)wm_s[lane] - (double)M);
-        z = wd[lane][0] * sc;
-        a = sc * (wd[lane][1] + wd[lane][0] * ((double)wm_s[lane] - (double)M));
-      }
-      z = warp_sum(z);
-      a = warp_sum(a);
-      const float m1 = warp_max(in ? wpart[lane].x : -INFINITY);
-      const float m2 = warp_max(in ? wpart[lane].y : -INFINITY);
-      const double cs = warp_sum(in ? wd[lane][2] : 0.0);
-      const double cq = warp_sum(in ? wd[lane][3] : 0.0);
-      if (lane == 0) {
-        part.mx = m1;
-        part.cmx = m2;
-        part.csum = cs;
-        part.csq = cq;
-        part.M = M;
-        part.Z = z;
-        part.A = a;
-      }
-    }
-    cl.sync();  // (1) slice statistics and softmax partials of every CTA
-    double csum, csq, Ztot = 0.0, Atot = 0.0;
-    {
-      const bool in = lane < C;
-      mx = warp_max(in ? lane_part->mx : -INFINITY);
-      cmx = warp_max(in ? lane_part->cmx : -INFINITY);
-      csum = warp_sum(in ? lane_part->csum : 0.0);
-      csq = warp_sum(in ? lane_part->csq : 0.0);
-      if (adaptive) {
-        const float Mr = in ? lane_part->M : -INFINITY;
-        const float M = warp_max(Mr);
-        double z = 0.0, a = 0.0;
-        if (in && Mr > -INFINITY) {
-          const double zr = lane_part->Z, ar = lane_part->A;
-          const double sc = exp((double)Mr - (double)M);
-          z = zr * sc;
-          a = sc * (ar + zr * ((double)Mr - (double)M));
+      // warp partials (softmax partials rescaled to the warp max), then one
+      // fold of the warps by warp 0, then the cluster
+      {
+        const float wm = warp_max(m_t);
+        double zw = 0.0, aw = 0.0;
+        if (adaptive && m_t > -INFINITY) {
+          const double sc = exp((double)m_t - (double)wm);
+          zw = (double)z_t * sc;
+          aw = sc * ((double)a_t + (double)z_t * ((double)m_t - (double)wm));
         }
-        Ztot = warp_sum(z);
-        Atot = warp_sum(a);
+        zw = warp_sum(zw);
+        aw = warp_sum(aw);
+        const float wmx = warp_max(mx), wcmx = warp_max(cmx);
+        const double wsum = warp_sum((double)csum_f), wsq = warp_sum((double)csq_f);
+        if (lane == 0) {
+          wpart[warp] = make_float2(wmx, wcmx);
+          wm_s[warp] = wm;
+          wd[warp][0] = zw;
+          wd[warp][1] = aw;
+          wd[warp][2] = wsum;
+          wd[warp][3] = wsq;
+        }
+      }
+      __syncthreads();  // also publishes the staged slice
+      if (warp == 0) {
+        const bool in = lane < kPW;
+        const float M = warp_max(in ? wm_s[lane] : -INFINITY);
+        double z = 0.0, a = 0.0;
+        if (in && wm_s[lane] > -INFINITY) {
+          const double sc = exp((double)wm_s[lane] - (double)M);
+          z = wd[lane][0] * sc;
+          a = sc * (wd[lane][1] + wd[lane][0] * ((double)wm_s[lane] - (double)M));
+        }
+        z = warp_sum(z);
+        a = warp_sum(a);
+        const float m1 = warp_max(in ? wpart[lane].x : -INFINITY);
+        const float m2 = warp_max(in ? wpart[lane].y : -INFINITY);
+        const double cs = warp_sum(in ? wd[lane][2] : 0.0);
+        const double cq = warp_sum(in ? wd[lane][3] : 0.0);
+        if (lane == 0) {
+          part.mx = m1;
+          part.cmx = m2;
+          part.csum = cs;
+          part.csq = cq;
+          part.M = M;
+          part.Z = z;
+          part.A = a;
+        }
+      }
+      cl.sync();  // (1) slice statistics and softmax partials of every CTA
+      {
+        const bool in = lane < C;
+        mx = warp_max(in ? lane_part->mx : -INFINITY);
+        cmx = warp_max(in ? lane_part->cmx : -INFINITY);
+        csum = warp_sum(in ? lane_part->csum : 0.0);
+        csq = warp_sum(in ? lane_part->csq : 0.0);
+        if (adaptive) {
+          const float Mr = in ? lane_part->M : -INFINITY;
+          const float M = warp_max(Mr);
+          double z = 0.0, a = 0.0;
+          if (in && Mr > -INFINITY) {
+            const double zr = lane_part->Z, ar = lane_part->A;
+            const double sc = exp((double)Mr - (double)M);
+            z = zr * sc;
+            a = sc * (ar + zr * ((double)Mr - (double)M));
+          }
+          Ztot = warp_sum(z);
+          Atot = warp_sum(a);
+        }
       }
     }
 
