@@ -229,39 +229,46 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanParams p) {
         s_ncand = 0;
         s_nfix = 0;
       }
+      // warp partials rescaled to the warp max; one barrier; every warp then
+      // folds the kPW warp partials in the same order (identical results)
       {
         const float wm = warp_max(acc.m), wmx = warp_max(acc.mx), wcmx = warp_max(acc.cmx);
-        if (lane == 0) {
-          wpart[warp] = make_float2(wmx, wcmx);
-          wm_s[warp] = wm;
-        }
-      }
-      __syncthreads();  // also publishes the staged slice
-      const float M = warp_max(lane < kPW ? wm_s[lane] : -INFINITY);
-      mx = warp_max(lane < kPW ? wpart[lane].x : -INFINITY);
-      cmx = warp_max(lane < kPW ? wpart[lane].y : -INFINITY);
-      {
         double z = 0.0, a = 0.0;
         if (acc.m > -INFINITY) {
-          const double f = (double)expf(acc.m - M);
+          const double f = (double)expf(acc.m - wm);
           z = (double)acc.Z * f;
-          a = f * ((double)acc.A + (double)acc.Z * ((double)acc.m - (double)M));
+          a = f * ((double)acc.A + (double)acc.Z * ((double)acc.m - (double)wm));
         }
         z = warp_sum(z);
         a = warp_sum(a);
         const double cs = warp_sum((double)acc.cs), cq = warp_sum((double)acc.cq);
         if (lane == 0) {
+          wpart[warp] = make_float2(wmx, wcmx);
+          wm_s[warp] = wm;
           wd[warp][0] = z;
           wd[warp][1] = a;
           wd[warp][2] = cs;
           wd[warp][3] = cq;
         }
       }
-      __syncthreads();
-      Ztot = warp_sum(lane < kPW ? wd[lane][0] : 0.0);
-      Atot = warp_sum(lane < kPW ? wd[lane][1] : 0.0);
-      csum = warp_sum(lane < kPW ? wd[lane][2] : 0.0);
-      csq = warp_sum(lane < kPW ? wd[lane][3] : 0.0);
+      __syncthreads();  // also publishes the staged slice
+      {
+        const bool in = lane < kPW;
+        const float wm = in ? wm_s[lane] : -INFINITY;
+        const float M = warp_max(wm);
+        mx = warp_max(in ? wpart[lane].x : -INFINITY);
+        cmx = warp_max(in ? wpart[lane].y : -INFINITY);
+        double z = 0.0, a = 0.0;
+        if (in && wm > -INFINITY) {
+          const double f = (double)expf(wm - M);
+          z = wd[lane][0] * f;
+          a = f * (wd[lane][1] + wd[lane][0] * ((double)wm - (double)M));
+        }
+        Ztot = warp_sum(z);
+        Atot = warp_sum(a);
+        csum = warp_sum(in ? wd[lane][2] : 0.0);
+        csq = warp_sum(in ? wd[lane][3] : 0.0);
+      }
     } else {
       // ---- 1. load the slice: statistics and per-thread softmax partials ----
       // Each thread keeps (m_t, z_t, a_t) = (max z, sum e^(z - m_t),
@@ -415,6 +422,10 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanParams p) {
       const float ln_floor = logf(1e-9f);
       const float pre = 2e-9f * Zf;  // p < 1e-9 implies e < 2e-9 * Z
       const float sc_t = (adaptive && m_t > -INFINITY) ? expf(m_t - zmax) : 0.f;
+      // p < 1e-9 needs d < log(2e-9 Z); below d_lo the clamp's correction
+      // e (log 1e-9 - log p) is under 1e-18 of H: skip the exp there
+      const float d_hi = adaptive ? logf(pre) : -INFINITY;
+      const float d_lo = d_hi - 25.f;
       for (int base = 0; base < n; base += kPlanThreads * kPlanILP) {
 #pragma unroll
         for (int r = 0; r < kPlanILP; ++r) {
@@ -423,9 +434,11 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanParams p) {
             const float v = val(li);
             if (adaptive) {
               const float d = __fsub_rn(zof(v), zmax);
-              const float e = ec ? ecache[li] * sc_t : expf(d);
-              if (e > 0.f && e < pre && __fdiv_rn(e, Zf) < 1e-9f)
-                cp = fmaf(e, ln_floor - d + logZ, cp);
+              if (d < d_hi && d >= d_lo) {
+                const float e = ec ? ecache[li] * sc_t : expf(d);
+                if (e > 0.f && e < pre && __fdiv_rn(e, Zf) < 1e-9f)
+                  cp = fmaf(e, ln_floor - d + logZ, cp);
+              }
             }
             if (buckets_ok && !forced(lo + li)) {
               const int bk = bucket_of(v, cmx, scale);
