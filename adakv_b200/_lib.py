@@ -75,6 +75,11 @@ _SIGNATURES = {
                                             ctypes.c_float, _vp, _vp, _vp, ctypes.c_size_t, _vp]),
     "adakv_combine": (ctypes.c_int, [ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                      ctypes.c_int32, _vp, _vp, _P(View), _vp]),
+    "adakv_minmax_build": (ctypes.c_int, [_P(Geometry), _P(View), _vp, _vp, _vp, _vp]),
+    "adakv_minmax_refresh": (ctypes.c_int, [_P(Geometry), _P(View), ctypes.c_int32, _vp, _vp, _vp,
+                                            _vp]),
+    "adakv_estimate_minmax": (ctypes.c_int, [_P(Geometry), _P(View), _vp, _vp, _vp, _vp,
+                                             ctypes.c_int32, _vp]),
     "adakv_attend_noalloc": (ctypes.c_int, [_P(Geometry), _P(View), _P(View), _P(View), _vp,
                                             ctypes.c_int32, _vp, _vp, ctypes.c_float, _P(View),
                                             _vp, _vp]),

@@ -123,6 +123,7 @@ class AdaKVCache:
         self._kbuf = None
         self._vbuf = None
         self._cbuf = None
+        self._mmbuf = None  # [2, Hkv, cap, D]: minmax estimator's minima / maxima
         self._len = 0
 
     # geometry of this (batch 1) cache for the C ABI
@@ -143,10 +144,21 @@ class AdaKVCache:
                 buf[:, : self._cbuf.shape[1]] = self._cbuf
             self._cbuf = buf
 
+    def _ensure_minmax_capacity(self, nb: int, device, Hkv: int, D: int):
+        if self._mmbuf is None or self._mmbuf.shape[2] < nb:
+            cap = self._cbuf.shape[1]
+            buf = torch.empty((2, Hkv, cap, D), dtype=torch.float32, device=device)
+            if self._mmbuf is not None:
+                buf[:, :, : self._mmbuf.shape[2]] = self._mmbuf
+            self._mmbuf = buf
+
+    def _minmax_views(self, nb: int):
+        self.kmin = self._mmbuf[0, :, :nb]
+        self.kmax = self._mmbuf[1, :, :nb]
+
     def append_prefill(self, k, v):
-        """Store prefill KV ``[Hkv, S, D]`` and build the centroid table."""
-        if self.estimator == "minmax":
-            raise NotImplementedError("the minmax (Quest) estimator is not built yet")
+        """Store prefill KV ``[Hkv, S, D]`` and build the centroid table (and, for
+        the minmax estimator, the per-block key minima / maxima)."""
         _lib.require_cuda(k, v)
         if k.shape != v.shape or k.dim() != 3:
             raise ValueError("expected k, v of identical shape [Hkv, S, D]")
@@ -163,6 +175,14 @@ class AdaKVCache:
                                                        self._cbuf.data_ptr(),
                                                        _lib.stream_ptr(k.device)))
         self.centroid = self._cbuf[:, :nb]
+        if self.estimator == "minmax":
+            self._mmbuf = None
+            self._ensure_minmax_capacity(nb, k.device, Hkv, D)
+            with torch.cuda.device(k.device):
+                _lib.check(_lib.lib().adakv_minmax_build(
+                    geo, _lib.view4(k.unsqueeze(0)), None, self._mmbuf[0].data_ptr(),
+                    self._mmbuf[1].data_ptr(), _lib.stream_ptr(k.device)))
+            self._minmax_views(nb)
         return self
 
     def append_decode(self, k_t, v_t):
@@ -199,14 +219,22 @@ class AdaKVCache:
         self.k = self._kbuf[:, :need]
         self.v = self._vbuf[:, :need]
         self.centroid = self._cbuf[:, :nb]
+        if self.estimator == "minmax":
+            self._ensure_minmax_capacity(nb, self.k.device, Hkv, D)
+            with torch.cuda.device(self.k.device):
+                _lib.check(_lib.lib().adakv_minmax_refresh(
+                    geo, _lib.view4(self._kbuf.unsqueeze(0)), n, None, self._mmbuf[0].data_ptr(),
+                    self._mmbuf[1].data_ptr(), _lib.stream_ptr(self.k.device)))
+            self._minmax_views(nb)
         return self
 
 
 def _plan_args(q, cache, avg_budget, k_min, k_max, n_sink_blocks, n_local_blocks, temperature,
                estimator, budget_policy, c_min):
     if estimator == "minmax":
-        raise NotImplementedError("the minmax (Quest) estimator is not built yet")
-    if estimator != "centroid":
+        if cache.kmin is None or cache.kmax is None:
+            raise ValueError("minmax estimator needs AdaKVCache(estimator='minmax')")
+    elif estimator != "centroid":
         raise ValueError(f"unknown estimator: {estimator!r}")
     if cache.centroid is None:
         raise ValueError("cache has no centroid table (call append_prefill first)")
@@ -251,9 +279,20 @@ def plan_selection(
     ws = _lib.workspace(nbytes, q.device)
     q = q if q.stride(-1) == 1 else q.contiguous()
     with torch.cuda.device(q.device):
-        _lib.check(L.adakv_plan(geo, sp, _lib.view4(q.unsqueeze(0)), cache._cbuf.data_ptr(), None,
-                                block_table.data_ptr(), width, sel_lens.data_ptr(), None,
-                                ws.data_ptr(), ws.numel(), _lib.stream_ptr(q.device)))
+        if estimator == "minmax":
+            # Quest scores (adakv/attention.py:190-198), then the same budget + top-k
+            scores = torch.empty((Hq, cache._cbuf.shape[1]), dtype=torch.float32, device=q.device)
+            _lib.check(L.adakv_estimate_minmax(geo, _lib.view4(q.unsqueeze(0)),
+                                               cache._mmbuf[0].data_ptr(), cache._mmbuf[1].data_ptr(),
+                                               None, scores.data_ptr(), scores.stride(0),
+                                               _lib.stream_ptr(q.device)))
+            _lib.check(L.adakv_select(geo, sp, scores.data_ptr(), scores.stride(0), None,
+                                      block_table.data_ptr(), width, sel_lens.data_ptr(),
+                                      ws.data_ptr(), ws.numel(), _lib.stream_ptr(q.device)))
+        else:
+            _lib.check(L.adakv_plan(geo, sp, _lib.view4(q.unsqueeze(0)), cache._cbuf.data_ptr(),
+                                    None, block_table.data_ptr(), width, sel_lens.data_ptr(), None,
+                                    ws.data_ptr(), ws.numel(), _lib.stream_ptr(q.device)))
     record_selection(block_table, sel_lens, cache.n_blocks)
     return block_table, sel_lens
 

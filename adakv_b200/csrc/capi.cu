@@ -854,3 +854,84 @@ int adakv_combine(int32_t n_parts, int32_t batch, int32_t n_q_heads, int32_t hea
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// minmax (Quest) estimator: tables and scores; selection then runs through
+// adakv_select and attention through adakv_attend
+// ---------------------------------------------------------------------------
+namespace {
+
+int minmax_common(const adakv_geometry* geo, const float* kmin, const float* kmax) {
+  int rc;
+  if ((rc = check_geometry(geo))) return rc;
+  if (!kmin || !kmax || reinterpret_cast<uintptr_t>(kmin) % 16 || reinterpret_cast<uintptr_t>(kmax) % 16)
+    return fail(ADAKV_ERR_INVALID, "kmin / kmax must be 16-byte aligned device pointers");
+  return ADAKV_OK;
+}
+
+MinmaxParams minmax_params(const adakv_geometry* geo, const int32_t* seq_lens, const float* kmin,
+                           const float* kmax) {
+  MinmaxParams p{};
+  p.seq_lens = seq_lens;
+  p.max_seq_len = geo->max_seq_len;
+  p.B = geo->batch;
+  p.Hq = geo->n_q_heads;
+  p.Hkv = geo->n_kv_heads;
+  p.g = geo->n_q_heads / geo->n_kv_heads;
+  p.bs = geo->block_size;
+  p.nb_cap = geo->nb_cap;
+  p.kmin = const_cast<float*>(kmin);
+  p.kmax = const_cast<float*>(kmax);
+  return p;
+}
+
+}  // namespace
+
+extern "C" {
+
+int adakv_minmax_build(const adakv_geometry* geo, const adakv_view* k, const int32_t* seq_lens,
+                       float* kmin, float* kmax, void* stream) {
+  int rc;
+  if ((rc = minmax_common(geo, kmin, kmax))) return rc;
+  if ((rc = check_view(k, "k", geo->dtype, true))) return rc;
+  MinmaxParams p = minmax_params(geo, seq_lens, kmin, kmax);
+  p.k = to_view(k);
+  CUDA_TRY(launch_minmax_build(p, geo->dtype, geo->head_dim, ceil_div(geo->max_seq_len, geo->block_size),
+                               static_cast<cudaStream_t>(stream)));
+  return ADAKV_OK;
+}
+
+int adakv_minmax_refresh(const adakv_geometry* geo, const adakv_view* k, int32_t n_new,
+                         const int32_t* seq_lens, float* kmin, float* kmax, void* stream) {
+  int rc;
+  if ((rc = minmax_common(geo, kmin, kmax))) return rc;
+  if ((rc = check_view(k, "k", geo->dtype, true))) return rc;
+  if (n_new < 1 || n_new > geo->max_seq_len)
+    return fail(ADAKV_ERR_INVALID, "n_new must be in [1, max_seq_len] (got %d)", n_new);
+  MinmaxParams p = minmax_params(geo, seq_lens, kmin, kmax);
+  p.k = to_view(k);
+  p.n_new = n_new;
+  CUDA_TRY(launch_minmax_build(p, geo->dtype, geo->head_dim, ceil_div(n_new, geo->block_size) + 1,
+                               static_cast<cudaStream_t>(stream)));
+  return ADAKV_OK;
+}
+
+int adakv_estimate_minmax(const adakv_geometry* geo, const adakv_view* q, const float* kmin,
+                          const float* kmax, const int32_t* seq_lens, float* scores,
+                          int32_t score_stride, void* stream) {
+  int rc;
+  if ((rc = minmax_common(geo, kmin, kmax))) return rc;
+  if ((rc = check_view(q, "q", geo->dtype, false))) return rc;
+  if (!scores) return fail(ADAKV_ERR_INVALID, "scores is NULL");
+  if (score_stride < ceil_div(geo->max_seq_len, geo->block_size))
+    return fail(ADAKV_ERR_INVALID, "score_stride %d < blocks of max_seq_len", score_stride);
+  MinmaxParams p = minmax_params(geo, seq_lens, kmin, kmax);
+  p.q = to_view(q);
+  p.scores = scores;
+  p.score_stride = score_stride;
+  CUDA_TRY(launch_minmax_score(p, geo->dtype, geo->head_dim, ceil_div(geo->max_seq_len, geo->block_size),
+                               static_cast<cudaStream_t>(stream)));
+  return ADAKV_OK;
+}
+
+}  // extern "C"

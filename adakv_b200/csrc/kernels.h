@@ -144,6 +144,19 @@ struct CombineParams {      // log-sum-exp merge of per-shard attention outputs
   int Hq;
 };
 
+// (b') minmax (Quest) estimator: tables and scores
+struct MinmaxParams {
+  View k, q;
+  const int* seq_lens;
+  int max_seq_len;
+  int B, Hq, Hkv, g, bs, nb_cap;
+  int n_new;                // build: 0 (every block); refresh: blocks touched by the last n_new tokens
+  float* kmin;              // [B, Hkv, nb_cap, D] float32
+  float* kmax;
+  float* scores;            // [B*Hq, score_stride] (score kernel)
+  int score_stride;
+};
+
 struct TableParams {        // block table -> per-head bitmaps (stand-alone attend)
   const int* block_table;
   int table_width;
@@ -213,6 +226,10 @@ cudaError_t launch_plan(const PlanParams& p, const PlanLayout& l, int grid, cuda
 cudaError_t launch_attend(const AttendParams& p, int dtype, int D, int bs, int split,
                           cudaStream_t stream, const LaunchOpts& o);
 cudaError_t launch_table_bitmap(const TableParams& p, cudaStream_t stream, const LaunchOpts& o);
+cudaError_t launch_minmax_build(const MinmaxParams& p, int dtype, int D, int blocks_per_seq,
+                                cudaStream_t stream);
+cudaError_t launch_minmax_score(const MinmaxParams& p, int dtype, int D, int nb_max,
+                                cudaStream_t stream);
 cudaError_t launch_combine(const CombineParams& p, int dtype, cudaStream_t stream, const LaunchOpts& o);
 
 // once per device (current device): opt-in shared memory / cluster sizes

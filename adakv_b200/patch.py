@@ -58,10 +58,11 @@ class _LayerState:
     """Centroid table of one attention layer: ``cbuf [B, Hkv, cap, D]`` float32,
     valid for the first ``n`` tokens of the layer's key cache."""
 
-    __slots__ = ("cbuf", "n", "bs", "shape", "dtype", "device")
+    __slots__ = ("cbuf", "mm", "n", "bs", "shape", "dtype", "device")
 
     def __init__(self):
         self.cbuf = None
+        self.mm = None  # minmax estimator: [2, B, Hkv, cap, D] key minima / maxima
         self.n = 0
         self.bs = 0
         self.shape = None
@@ -77,8 +78,9 @@ def _geometry(B, Hq, Hkv, D, bs, S, nb_cap, dtype):
     return _lib.geometry(B, Hq, Hkv, D, bs, S, nb_cap, _lib.TORCH_DTYPES[dtype])
 
 
-def _sync_centroids(module, key, Hq, bs, rebuild):
-    """Bring the layer's centroid table up to date with ``key [B, Hkv, S, D]``."""
+def _sync_centroids(module, key, Hq, bs, rebuild, minmax=False):
+    """Bring the layer's centroid table (and, for the minmax estimator, its
+    key minima / maxima) up to date with ``key [B, Hkv, S, D]``."""
     B, Hkv, S, D = key.shape
     st = _STATE.get(id(module))
     if st is None:
@@ -98,11 +100,23 @@ def _sync_centroids(module, key, Hq, bs, rebuild):
     geo = _geometry(B, Hq, Hkv, D, bs, S, st.cbuf.shape[2], key.dtype)
     L = _lib.lib()
     stream = _lib.stream_ptr(key.device)
-    if rebuild or S - st.n > S // 2:
+    full = rebuild or S - st.n > S // 2
+    if full:
         _lib.check(L.adakv_centroid_build(geo, _lib.view4(key), None, st.cbuf.data_ptr(), stream))
     elif S > st.n:
         _lib.check(L.adakv_centroid_refresh(geo, _lib.view4(key), S - st.n, None,
                                             st.cbuf.data_ptr(), stream))
+    if minmax:
+        if st.mm is None or st.mm.shape[1:] != (B, Hkv, st.cbuf.shape[2], D):
+            st.mm = torch.empty((2, B, Hkv, st.cbuf.shape[2], D), dtype=torch.float32,
+                                device=key.device)
+            full = True
+        if full:
+            _lib.check(L.adakv_minmax_build(geo, _lib.view4(key), None, st.mm[0].data_ptr(),
+                                            st.mm[1].data_ptr(), stream))
+        elif S > st.n:
+            _lib.check(L.adakv_minmax_refresh(geo, _lib.view4(key), S - st.n, None,
+                                              st.mm[0].data_ptr(), st.mm[1].data_ptr(), stream))
     st.n = S
     return st
 
@@ -123,22 +137,22 @@ def adakv_attention_forward(module, query, key, value, attention_mask, scaling, 
         if cfg["enabled"] and q_len > 1 and query.is_cuda and D in (64, 128):
             # prompt keys are final for these positions: build the table now
             with torch.cuda.device(query.device):
-                _sync_centroids(module, key, Hq, cfg["block_size"], rebuild=True)
+                _sync_centroids(module, key, Hq, cfg["block_size"], rebuild=True,
+                                minmax=cfg["estimator"] == "minmax")
         return _SDPA(module, query, key, value, attention_mask=attention_mask, scaling=scaling,
                      dropout=dropout, **kwargs)
 
     _lib.require_cuda(query, key, value)
-    if cfg["estimator"] == "minmax":
-        raise NotImplementedError("the minmax (Quest) estimator is not built yet")
-    if cfg["estimator"] != "centroid":
+    if cfg["estimator"] not in ("centroid", "minmax"):
         raise ValueError(f"unknown estimator: {cfg['estimator']!r}")
+    minmax = cfg["estimator"] == "minmax"
     if key.dtype != query.dtype or value.dtype != query.dtype:
         raise ValueError("query, key and value must share one dtype")
     bs = int(cfg["block_size"])
     _, Hkv, S, _ = key.shape
     sm_scale = float(scaling) if scaling is not None else 1.0 / math.sqrt(D)
     with torch.cuda.device(query.device):
-        st = _sync_centroids(module, key, Hq, bs, rebuild=False)
+        st = _sync_centroids(module, key, Hq, bs, rebuild=False, minmax=minmax)
         sp = _lib.select_params(cfg["avg_budget"], cfg["k_min"], cfg["k_max"],
                                 cfg["n_sink_blocks"], cfg["n_local_blocks"], cfg["c_min"],
                                 cfg["temperature"], cfg["budget_policy"])
@@ -155,6 +169,24 @@ def adakv_attention_forward(module, query, key, value, attention_mask, scaling, 
         if q3.stride(-1) != 1:
             q3 = q3.contiguous()
         o3 = out[:, 0]  # [B, Hq, D] view of the [B, 1, Hq, D] output
+        if minmax:
+            # Quest scores, then the same budget + top-k and block-sparse attention
+            scores = torch.empty((B * Hq, st.cbuf.shape[2]), dtype=torch.float32,
+                                 device=query.device)
+            stream = _lib.stream_ptr(query.device)
+            _lib.check(L.adakv_estimate_minmax(geo, _lib.view4(q3), st.mm[0].data_ptr(),
+                                               st.mm[1].data_ptr(), None, scores.data_ptr(),
+                                               scores.stride(0), stream))
+            _lib.check(L.adakv_select(geo, sp, scores.data_ptr(), scores.stride(0), None,
+                                      block_table.data_ptr(), width, sel_lens.data_ptr(),
+                                      ws.data_ptr(), ws.numel(), stream))
+            wa = _lib.workspace(L.adakv_attend_workspace_bytes(geo, width), query.device, "attend")
+            _lib.check(L.adakv_attend(geo, _lib.view4(q3), _lib.view4(key), _lib.view4(value),
+                                      block_table.data_ptr(), width, sel_lens.data_ptr(), None,
+                                      sm_scale, _lib.view4(o3), wa.data_ptr(), wa.numel(), stream))
+            if tracing_enabled() and B == 1:
+                record_selection(block_table, sel_lens, (S + bs - 1) // bs)
+            return out, None
         _lib.check(L.adakv_decode_step(
             geo, sp, _lib.view4(q3), _lib.view4(key), _lib.view4(value), None, None, 0,
             st.cbuf.data_ptr(), None, sm_scale, block_table.data_ptr(), width,

@@ -10,6 +10,8 @@
  *   adakv_plan             q.centroid estimator, entropy budget, top-k  (b)(c)
  *   adakv_attend           ragged block-sparse split-KV flash decode    (d)
  *   adakv_decode_step      adakv_plan followed by adakv_attend          (b)-(d)
+ *   adakv_minmax_build / adakv_minmax_refresh / adakv_estimate_minmax
+ *                          the minmax (Quest) estimator                 (b')
  *   adakv_estimate / adakv_select / adakv_attend_partial / adakv_combine
  *                          the same step split for a sequence sharded over GPUs (e)
  *
@@ -166,6 +168,25 @@ int adakv_attend(const adakv_geometry* geo, const adakv_view* q, const adakv_vie
                  const adakv_view* v, const int32_t* block_table, int32_t table_width,
                  const int32_t* sel_lens, const int32_t* seq_lens, float sm_scale,
                  const adakv_view* out, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- minmax (Quest) estimator (adakv/estimator.py:50-57, 76-79;
+ *      adakv/attention.py:134-138, 190-198) ----
+ * kmin / kmax: [B, Hkv, nb_cap, D] float32 per-block per-dimension key minima
+ * and maxima over the real tokens.  Scores
+ * sum_d max(q_d, 0) kmax_d + min(q_d, 0) kmin_d go to a caller buffer; the
+ * selection then runs through adakv_select and the attention through
+ * adakv_attend. */
+int adakv_minmax_build(const adakv_geometry* geo, const adakv_view* k, const int32_t* seq_lens,
+                       float* kmin, float* kmax, void* stream);
+
+/* Recompute the tables of the blocks touched by the last n_new tokens. */
+int adakv_minmax_refresh(const adakv_geometry* geo, const adakv_view* k, int32_t n_new,
+                         const int32_t* seq_lens, float* kmin, float* kmax, void* stream);
+
+/* scores[(b * Hq + h) * score_stride + j] for every block j of every sequence. */
+int adakv_estimate_minmax(const adakv_geometry* geo, const adakv_view* q, const float* kmin,
+                          const float* kmax, const int32_t* seq_lens, float* scores,
+                          int32_t score_stride, void* stream);
 
 /* adakv_attend without a workspace: no counterpart in the reference.
  *

@@ -97,6 +97,43 @@ def block_scores(q: np.ndarray, centroids: np.ndarray) -> np.ndarray:
     return np.einsum("hd,hbd->hb", q, c)
 
 
+def build_minmax(K: np.ndarray, block_size: int):
+    """Per-block per-dimension key minimum and maximum over real tokens (the
+    "minmax" (Quest) summaries of ``adakv/estimator.py:50-57``).
+
+    K: ``[H, S, D]`` float32 -> ``(kmin, kmax)``, each ``[H, nb, D]`` float32.
+    Minima and maxima are exact, so the result does not depend on order.
+    """
+    K = np.asarray(K, dtype=np.float32)
+    H, S, D = K.shape
+    nb = (S + block_size - 1) // block_size
+    kmin = np.empty((H, nb, D), dtype=np.float32)
+    kmax = np.empty((H, nb, D), dtype=np.float32)
+    for b in range(nb):
+        s, e = b * block_size, min((b + 1) * block_size, S)
+        kmin[:, b] = K[:, s:e].min(axis=1)
+        kmax[:, b] = K[:, s:e].max(axis=1)
+    return kmin, kmax
+
+
+def minmax_scores(q: np.ndarray, kmin: np.ndarray, kmax: np.ndarray) -> np.ndarray:
+    """Quest upper bound of ``max_{k in block} q . k`` per (query head, block),
+    the formula of ``adakv/estimator.py:76-79``:
+    ``sum_d max(q_d, 0) kmax_d + min(q_d, 0) kmin_d``, with the summaries
+    expanded over the GQA group as the reference's caller does.
+
+    q: ``[Hq, D]``; kmin / kmax: ``[Hkv, nb, D]`` -> ``[Hq, nb]`` float32.
+    """
+    q = np.asarray(q, dtype=np.float32)
+    Hq = q.shape[0]
+    g = Hq // kmin.shape[0]
+    kmn = np.repeat(kmin, g, axis=0)
+    kmx = np.repeat(kmax, g, axis=0)
+    qpos = np.clip(q, 0.0, None)[:, None, :]
+    qneg = np.clip(q, None, 0.0)[:, None, :]
+    return (qpos * kmx + qneg * kmn).sum(-1)
+
+
 # --------------------------------------------------------------------------
 # (c) entropy budget
 # --------------------------------------------------------------------------
@@ -276,7 +313,7 @@ def dense_attention(q, K, V, sm_scale=None):
 def decode_step(q, K, V, block_size=16, avg_budget=8, k_min=2, k_max=64,
                 n_sink_blocks=1, n_local_blocks=4, c_min=1, temperature=1.0,
                 policy=POLICY_ADAPTIVE, nucleus_p=0.9, sm_scale=None,
-                centroids=None):
+                centroids=None, estimator="centroid"):
     """One AdaKV decode step for one sequence, ``adakv/reference.py:44-84``.
 
     q: ``[Hq, D]``; K, V: ``[Hkv, S, D]`` (GQA folded).  ``centroids`` may be
@@ -285,9 +322,15 @@ def decode_step(q, K, V, block_size=16, avg_budget=8, k_min=2, k_max=64,
     (unrounded budget), ``counts`` (realised) and ``mask``.
     """
     q = np.asarray(q, dtype=np.float32)
-    if centroids is None:
-        centroids = build_centroids(K, block_size)
-    scores = block_scores(q, centroids)
+    if estimator == "minmax":
+        kmin, kmax = build_minmax(K, block_size)
+        scores = minmax_scores(q, kmin, kmax)
+    elif estimator == "centroid":
+        if centroids is None:
+            centroids = build_centroids(K, block_size)
+        scores = block_scores(q, centroids)
+    else:
+        raise ValueError(f"unknown estimator: {estimator!r}")
     k, raw = allocate_budget(scores, avg_budget, k_min, k_max, n_sink_blocks,
                              n_local_blocks, c_min, temperature, policy, nucleus_p,
                              return_raw=True)

@@ -81,6 +81,14 @@ CASES = {
                         alg=dict(avg_budget=16, k_min=2, k_max=128, n_sink_blocks=1,
                                  n_local_blocks=4, c_min=1, policy="adaptive",
                                  temperature=0.5)),
+    "minmax_fp32": dict(gen=dict(seed=12, Hq=8, Hkv=2, D=128, S=4001, bs=16, dtype="fp32"),
+                        alg=dict(avg_budget=12, k_min=2, k_max=64, n_sink_blocks=1,
+                                 n_local_blocks=4, c_min=1, policy="adaptive",
+                                 estimator="minmax")),
+    "minmax_bf16": dict(gen=dict(seed=13, Hq=32, Hkv=8, D=128, S=8192, bs=16, dtype="bf16"),
+                        alg=dict(avg_budget=64, k_min=2, k_max=512, n_sink_blocks=1,
+                                 n_local_blocks=4, c_min=1, policy="adaptive",
+                                 estimator="minmax")),
     "kmax_cap": dict(gen=dict(seed=11, Hq=32, Hkv=8, D=128, S=4096, bs=16, dtype="fp32"),
                      alg=dict(avg_budget=32, k_min=2, k_max=16, n_sink_blocks=1,
                               n_local_blocks=4, c_min=1, policy="adaptive")),
@@ -114,8 +122,9 @@ def run_case(name, spec, ref, est, bud):
     Kq, Vq = ref.expand_gqa(K, g["Hq"]), ref.expand_gqa(V, g["Hq"])
     temperature = a.pop("temperature", 1.0)
     policy = a.pop("policy")
+    estimator = a.pop("estimator", "centroid")
     nb = (g["S"] + g["bs"] - 1) // g["bs"]
-    summ = est.build_block_summaries(Kq, g["bs"], "centroid")
+    summ = est.build_block_summaries(Kq, g["bs"], estimator)
     scores = est.block_scores(q, summ)
     floor = min(a["n_sink_blocks"], nb) + min(a["n_local_blocks"], nb) + a["c_min"]
     k = bud.allocate_budget(scores, a["avg_budget"], min(a["k_min"], nb), min(a["k_max"], nb),
@@ -132,12 +141,16 @@ def run_case(name, spec, ref, est, bud):
         out, counts, mask = ref.sparse_attention(
             q, Kq, Vq, block_size=g["bs"], avg_budget=a["avg_budget"], k_min=a["k_min"],
             k_max=a["k_max"], n_sink_blocks=a["n_sink_blocks"], n_local_blocks=a["n_local_blocks"],
-            c_min=a["c_min"], budget_policy=policy, return_mask=True)
+            c_min=a["c_min"], budget_policy=policy, estimator=estimator, return_mask=True)
     else:  # sparse_attention has no temperature argument; select from the budget directly
         from adakv_ref.selector import select_blocks
         mask, counts = select_blocks(scores, k, a["n_sink_blocks"], a["n_local_blocks"], a["c_min"])
+    if estimator == "minmax":  # the per-KV-head tables stacked as [2, Hkv, nb, D]
+        table = np.stack([summ["kmin"][:: g["Hq"] // g["Hkv"]], summ["kmax"][:: g["Hq"] // g["Hkv"]]])
+    else:
+        table = summ["centroid"][:: g["Hq"] // g["Hkv"]]
     rec = dict(digest=np.array(input_digest(case)), scores=scores.astype(np.float32),
-               centroid=summ["centroid"][:: g["Hq"] // g["Hkv"]].astype(np.float32),
+               centroid=table.astype(np.float32), estimator=np.array(estimator),
                k=np.asarray(k, dtype=np.int64), raw=np.asarray(raw, dtype=np.float64),
                counts=np.asarray(counts, dtype=np.int64), mask=np.packbits(mask, axis=1),
                nb=np.array(nb))
@@ -146,7 +159,8 @@ def run_case(name, spec, ref, est, bud):
     # the centroid table is large for the big cases; keep only a strided sample of rows
     if rec["centroid"].size > 20_000:
         stride = int(np.ceil(rec["centroid"].size / 20_000)) | 1
-        rec["centroid"] = rec["centroid"][:, ::stride].copy()
+        rec["centroid"] = rec["centroid"][..., ::stride, :].copy() if estimator == "minmax" \
+            else rec["centroid"][:, ::stride].copy()
         rec["centroid_stride"] = np.array(stride)
     np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **rec)
     return counts

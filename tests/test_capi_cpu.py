@@ -145,7 +145,7 @@ def test_python_wrappers_refuse_cpu_tensors():
     with pytest.raises(RuntimeError, match="CUDA"):
         block_sparse_decode(torch.zeros(4, 64), k, k, torch.zeros(4, 2, dtype=torch.int32),
                             torch.ones(4, dtype=torch.int32), 16)
-    with pytest.raises(NotImplementedError):
+    with pytest.raises(RuntimeError, match="CUDA"):
         AdaKVCache(16, estimator="minmax").append_prefill(k, k)
     with pytest.raises(ValueError):
         AdaKVCache(16, estimator="bogus")

@@ -406,3 +406,44 @@ def test_fused_append_step_equals_separate_append():
         ref = O.build_centroids(dec_a.k[b, :, :S[b]].float().cpu().numpy(), 16)
         np.testing.assert_array_equal(dec_a.centroid[b, :, :ref.shape[1]].cpu().numpy(), ref)
     assert dec_a.status() == 0 and dec_b.status() == 0
+
+
+@pytest.mark.parametrize("dtype", ["fp32", "bf16"])
+def test_minmax_estimator_matches_oracle(dtype):
+    """The minmax (Quest) estimator through AdaKVCache / plan_selection:
+    exact min / max tables, scores to float rounding, the oracle's selection up
+    to documented near-ties, and the attention output."""
+    _need_cuda()
+    from adakv_b200.attention import AdaKVCache, plan_selection
+    from adakv_b200.kernels.block_sparse_decode import block_sparse_decode
+    Hq, Hkv, D, bs, S = 16, 4, 128, 16, 3001
+    kw = dict(avg_budget=10, k_min=2, k_max=64, n_sink_blocks=1, n_local_blocks=4)
+    case = make_decode_case(90, 1, Hq, Hkv, D, S, bs, dtype)
+    dt = TORCH[dtype]
+    q = torch.from_numpy(case.q[0]).to("cuda", dt)
+    K = torch.from_numpy(case.K[0]).to("cuda", dt)
+    V = torch.from_numpy(case.V[0]).to("cuda", dt)
+    cache = AdaKVCache(bs, estimator="minmax").append_prefill(K, V)
+    kmin, kmax = O.build_minmax(case.K[0], bs)
+    assert np.array_equal(cache.kmin.cpu().numpy(), kmin)
+    assert np.array_equal(cache.kmax.cpu().numpy(), kmax)
+    bt, sl = plan_selection(q, cache, estimator="minmax", **kw)
+    torch.cuda.synchronize()
+    scores = O.minmax_scores(case.q[0], kmin, kmax)
+    k, raw = O.allocate_budget(scores, kw["avg_budget"], kw["k_min"], kw["k_max"], 1, 4, 1,
+                               return_raw=True)
+    mask, _ = O.select_blocks(scores, k, 1, 4, 1)
+    sets = [bt[h, : int(sl[h])].cpu().numpy() for h in range(Hq)]
+    _, _, _, failures = O.compare_selection(scores, k, raw, mask, sets, 1, 4, 1)
+    assert not failures, failures[:4]
+    out = block_sparse_decode(q, cache.k, cache.v, bt, sl, bs)
+    ref = O.decode_step(case.q[0], case.K[0], case.V[0], block_size=bs, estimator="minmax", **kw)
+    err = np.abs(out.float().cpu().numpy() - ref["out"]).max()
+    assert err < TOL[dtype], f"max abs err {err:.3e}"
+    # append keeps the tables equal to a rebuild
+    kt = torch.from_numpy(case.K[0][:, -3:]).to("cuda", dt)
+    cache.append_decode(kt, kt)
+    K2 = np.concatenate([case.K[0], case.K[0][:, -3:]], axis=1)
+    kmin2, kmax2 = O.build_minmax(K2, bs)
+    assert np.array_equal(cache.kmin.cpu().numpy(), kmin2)
+    assert np.array_equal(cache.kmax.cpu().numpy(), kmax2)

@@ -187,3 +187,27 @@ def test_patch_model_sparse_generate_runs_bf16():
     # 2 layers x 7 decode calls recorded, mean budget near the target of 16
     assert len(trace) == 14
     assert all(8 <= t <= 64 for t in trace)
+
+
+def test_minmax_estimator_through_patch():
+    _need_cuda()
+    from adakv_b200 import patch
+    Hq, Hkv, D, bs, P, steps = 8, 2, 64, 16, 700, 5
+    patch.enable_adakv(block_size=bs, avg_budget=8, k_max=64, estimator="minmax")
+    case = make_decode_case(14, 1, Hq, Hkv, D, P + steps, bs, "fp32")
+    Kall = torch.from_numpy(case.K[0]).cuda()[None]
+    Vall = torch.from_numpy(case.V[0]).cuda()[None]
+    layer = _Layer()
+    rng = np.random.default_rng(15)
+    qp = torch.from_numpy(rng.standard_normal((1, Hq, 3, D), dtype=np.float32)).cuda()
+    patch.adakv_attention_forward(layer, qp, Kall[:, :, :P], Vall[:, :, :P], None, D ** -0.5)
+    for t in range(steps):
+        S = P + t + 1
+        qn = rng.standard_normal((Hq, D), dtype=np.float32)
+        q = torch.from_numpy(qn).cuda()[None, :, None, :]
+        out, _ = patch.adakv_attention_forward(layer, q, Kall[:, :, :S].clone(),
+                                               Vall[:, :, :S].clone(), None, D ** -0.5)
+        ref = O.decode_step(qn, case.K[0][:, :S], case.V[0][:, :S], block_size=bs, avg_budget=8,
+                            k_max=64, sm_scale=D ** -0.5, estimator="minmax")
+        err = np.abs(out[0, 0].cpu().numpy() - ref["out"]).max()
+        assert err < TOL["fp32"], f"step {t}: {err:.3e}"

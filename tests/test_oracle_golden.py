@@ -35,11 +35,17 @@ def test_oracle_matches_reference_golden(name):
     q, K, V = case.q[0], case.K[0], case.V[0]
     nb = int(gold["nb"])
 
-    cent = O.build_centroids(K, g["bs"])
     stride = int(gold.get("centroid_stride", 1))
-    assert np.array_equal(cent[:, ::stride], gold["centroid"]), "centroid table differs"
-
-    scores = O.block_scores(q, cent)
+    if a.pop("estimator", "centroid") == "minmax":
+        kmin, kmax = O.build_minmax(K, g["bs"])
+        assert str(gold["estimator"]) == "minmax"
+        assert np.array_equal(np.stack([kmin, kmax])[..., ::stride, :], gold["centroid"]), \
+            "min/max tables differ"
+        scores = O.minmax_scores(q, kmin, kmax)
+    else:
+        cent = O.build_centroids(K, g["bs"])
+        assert np.array_equal(cent[:, ::stride], gold["centroid"]), "centroid table differs"
+        scores = O.block_scores(q, cent)
     assert scores.dtype == np.float32
     assert np.array_equal(scores, gold["scores"]), "block scores differ"
 
