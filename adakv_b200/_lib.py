@@ -16,12 +16,13 @@ import torch
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libadakv_b200.so")
 
 DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2
-POLICY_FIXED, POLICY_ADAPTIVE = 0, 1
+POLICY_FIXED, POLICY_ADAPTIVE, POLICY_NUCLEUS = 0, 1, 2
 OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_CUDA = 0, 1, 2, 3
 ST_WAIT_TIMEOUT, ST_BAD_BLOCK_ID, ST_BAD_SEL_LEN, ST_BAD_SEQ_LEN = 1, 2, 4, 8
 
 TORCH_DTYPES = {torch.float32: DTYPE_F32, torch.float16: DTYPE_F16, torch.bfloat16: DTYPE_BF16}
-POLICIES = {"fixed": POLICY_FIXED, "adaptive": POLICY_ADAPTIVE}
+POLICIES = {"fixed": POLICY_FIXED, "adaptive": POLICY_ADAPTIVE,
+            "adaptive_nucleus": POLICY_NUCLEUS}
 
 
 class Geometry(ctypes.Structure):
@@ -40,7 +41,8 @@ class SelectParams(ctypes.Structure):
     _fields_ = [("avg_budget", ctypes.c_double), ("temperature", ctypes.c_double),
                 ("k_min", ctypes.c_int32), ("k_max", ctypes.c_int32),
                 ("n_sink_blocks", ctypes.c_int32), ("n_local_blocks", ctypes.c_int32),
-                ("c_min", ctypes.c_int32), ("policy", ctypes.c_int32)]
+                ("c_min", ctypes.c_int32), ("policy", ctypes.c_int32),
+                ("nucleus_p", ctypes.c_double)]
 
 
 _P = ctypes.POINTER
@@ -150,14 +152,12 @@ def stream_ptr(device) -> int:
 
 
 def select_params(avg_budget, k_min=2, k_max=64, n_sink_blocks=1, n_local_blocks=4, c_min=1,
-                  temperature=1.0, budget_policy="adaptive") -> SelectParams:
+                  temperature=1.0, budget_policy="adaptive", nucleus_p=0.9) -> SelectParams:
     if budget_policy not in POLICIES:
-        if budget_policy == "adaptive_nucleus":
-            raise NotImplementedError("budget_policy='adaptive_nucleus' is not built yet")
-        raise ValueError(f"unknown budget_policy: {budget_policy!r}")
+        raise ValueError(f"unknown budget policy: {budget_policy!r}")
     return SelectParams(float(avg_budget), float(temperature), int(k_min), int(k_max),
                         int(n_sink_blocks), int(n_local_blocks), int(c_min),
-                        POLICIES[budget_policy])
+                        POLICIES[budget_policy], float(nucleus_p))
 
 
 def geometry(batch, n_q_heads, n_kv_heads, head_dim, block_size, max_seq_len, nb_cap,

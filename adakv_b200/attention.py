@@ -230,7 +230,7 @@ class AdaKVCache:
 
 
 def _plan_args(q, cache, avg_budget, k_min, k_max, n_sink_blocks, n_local_blocks, temperature,
-               estimator, budget_policy, c_min):
+               estimator, budget_policy, c_min, nucleus_p=0.9):
     if estimator == "minmax":
         if cache.kmin is None or cache.kmax is None:
             raise ValueError("minmax estimator needs AdaKVCache(estimator='minmax')")
@@ -242,7 +242,7 @@ def _plan_args(q, cache, avg_budget, k_min, k_max, n_sink_blocks, n_local_blocks
     if q.dim() != 2:
         raise ValueError("q must be [n_q_heads, head_dim]")
     sp = _lib.select_params(avg_budget, k_min, k_max, n_sink_blocks, n_local_blocks, c_min,
-                            temperature, budget_policy)
+                            temperature, budget_policy, nucleus_p)
     geo = cache._geometry(q.shape[0], _lib.dtype_code(q))
     return geo, sp
 
@@ -267,7 +267,7 @@ def plan_selection(
     its ``sel_lens[h]`` blocks in ascending order, entries past that are unspecified.
     """
     geo, sp = _plan_args(q, cache, avg_budget, k_min, k_max, n_sink_blocks, n_local_blocks,
-                         temperature, estimator, budget_policy, c_min)
+                         temperature, estimator, budget_policy, c_min, nucleus_p)
     L = _lib.lib()
     width = L.adakv_plan_table_width(geo, sp)
     if width < 1:

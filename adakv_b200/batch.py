@@ -40,7 +40,8 @@ def partition_batch(seq_lens, world):
 class BatchedDecoder:
     def __init__(self, batch, n_q_heads, n_kv_heads, head_dim, block_size, capacity, dtype,
                  device="cuda", avg_budget=64, k_min=2, k_max=64, n_sink_blocks=1,
-                 n_local_blocks=4, c_min=1, temperature=1.0, budget_policy="adaptive"):
+                 n_local_blocks=4, c_min=1, temperature=1.0, budget_policy="adaptive",
+                 nucleus_p=0.9):
         self.device = torch.device(device)
         if self.device.type != "cuda":
             raise RuntimeError("BatchedDecoder needs a CUDA device (no CPU fallback)")
@@ -48,7 +49,7 @@ class BatchedDecoder:
         self.bs, self.capacity, self.dtype = block_size, capacity, dtype
         self.nb_cap = (capacity + block_size - 1) // block_size
         self.params = _lib.select_params(avg_budget, k_min, k_max, n_sink_blocks, n_local_blocks,
-                                         c_min, temperature, budget_policy)
+                                         c_min, temperature, budget_policy, nucleus_p)
         self.k = torch.zeros((batch, n_kv_heads, capacity, head_dim), dtype=dtype, device=device)
         self.v = torch.zeros_like(self.k)
         self.centroid = torch.zeros((batch, n_kv_heads, self.nb_cap, head_dim), dtype=torch.float32,

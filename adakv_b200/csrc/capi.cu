@@ -136,8 +136,11 @@ int check_params(const adakv_select_params* sp) {
       sp->c_min < 0)
     return fail(ADAKV_ERR_INVALID,
                 "need k_min >= 0, k_max >= 1, n_sink_blocks >= 0, n_local_blocks >= 0, c_min >= 0");
-  if (sp->policy != ADAKV_POLICY_FIXED && sp->policy != ADAKV_POLICY_ADAPTIVE)
+  if (sp->policy != ADAKV_POLICY_FIXED && sp->policy != ADAKV_POLICY_ADAPTIVE &&
+      sp->policy != ADAKV_POLICY_NUCLEUS)
     return fail(ADAKV_ERR_INVALID, "unknown budget_policy %d", sp->policy);
+  if (sp->policy == ADAKV_POLICY_NUCLEUS && !std::isfinite(sp->nucleus_p))
+    return fail(ADAKV_ERR_INVALID, "nucleus_p must be finite");
   return ADAKV_OK;
 }
 
@@ -151,6 +154,7 @@ SelectCfg to_cfg(const adakv_select_params* sp) {
   c.n_local = sp->n_local_blocks;
   c.c_min = sp->c_min;
   c.policy = sp->policy;
+  c.nucleus_p = sp->nucleus_p;
   return c;
 }
 

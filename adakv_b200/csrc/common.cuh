@@ -32,6 +32,7 @@ struct SelectCfg {
   double avg_budget;
   double temperature;
   int k_min, k_max, n_sink, n_local, c_min, policy;
+  double nucleus_p;
 };
 
 __host__ __device__ inline int ceil_div(int a, int b) { return (a + b - 1) / b; }

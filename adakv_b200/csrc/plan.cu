@@ -16,6 +16,10 @@
 //    A = sum e (z - zmax) (one pass, no per-block division or logarithm) and
 //    Cc = sum over blocks with p < 1e-9 of e (log(1e-9) - (z - zmax) + log Z),
 //    the reference's clamp; sums are float per thread, double across threads.
+//    Nucleus policy (budget.py:38-41) instead: the weight is 1 + the number of
+//    blocks, in descending probability order, whose cumulative softmax mass
+//    stays below nucleus_p, found by an MSB radix select over the score keys
+//    whose histograms hold probability mass (float32 p, summed in double).
 // 3. The Hq clusters of a sequence exchange entropies through per-head 64-bit
 //    slots (call tag << 32 | float32 entropy; tags cleared by the estimator):
 //    rank 0 publishes with one release store; warp 0 of every CTA polls the
@@ -155,6 +159,10 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanParams p) {
   __shared__ double wd[kPW][4];
   __shared__ double dred[kPW], dred2[kPW];
   __shared__ double s_sumw, s_w;
+  __shared__ double nmass[256];          // nucleus: probability mass per key digit
+  __shared__ uint32_t ncnt[256];
+  __shared__ int s_ndigit, s_ncnt_above, s_ncnt_digit;
+  __shared__ double s_nmass_above;
 
   cg::cluster_group cl = cg::this_cluster();
   const int C = p.csize;
@@ -194,6 +202,8 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanParams p) {
     auto forced = [&](int i) -> bool { return i < sink || i >= nb - local; };
 
     const bool adaptive = nb >= 2 && p.cfg.policy == ADAKV_POLICY_ADAPTIVE;
+    const bool nucleus = nb >= 2 && p.cfg.policy == ADAKV_POLICY_NUCLEUS;
+    const bool soft = adaptive || nucleus;  // the row's softmax (Z) is needed
     const float Tf = (float)(p.cfg.temperature > 1e-6 ? p.cfg.temperature : 1e-6);
     const bool unit_t = (Tf == 1.0f);  // s / 1 == s exactly: skip the division
     auto zof = [&](float v) -> float { return unit_t ? v : __fdiv_rn(v, Tf); };
@@ -302,7 +312,7 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanParams p) {
             }
           }
         }
-        if (adaptive && tm > m_t) {
+        if (soft && tm > m_t) {
           if (m_t > -INFINITY) {
             const float sc = expf(m_t - tm);
             a_t = sc * fmaf(z_t, m_t - tm, a_t);
@@ -310,7 +320,7 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanParams p) {
           }
           m_t = tm;
         }
-        if (adaptive) {
+        if (soft) {
 #pragma unroll
           for (int r = 0; r < kPlanILP; ++r) {
             const int li = base + r * kPlanThreads + tid;
@@ -335,7 +345,7 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanParams p) {
       {
         const float wm = warp_max(m_t);
         double zw = 0.0, aw = 0.0;
-        if (adaptive && m_t > -INFINITY) {
+        if (soft && m_t > -INFINITY) {
           const double sc = exp((double)m_t - (double)wm);
           zw = (double)z_t * sc;
           aw = sc * ((double)a_t + (double)z_t * ((double)m_t - (double)wm));
@@ -386,7 +396,7 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanParams p) {
         cmx = warp_max(in ? lane_part->cmx : -INFINITY);
         csum = warp_sum(in ? lane_part->csum : 0.0);
         csq = warp_sum(in ? lane_part->csq : 0.0);
-        if (adaptive) {
+        if (soft) {
           const float Mr = in ? lane_part->M : -INFINITY;
           const float M = warp_max(Mr);
           double z = 0.0, a = 0.0;
@@ -448,7 +458,123 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanParams p) {
         }
       }
     }
+    // ---- nucleus weight (adakv/budget.py:38-41): the blocks, in descending
+    //      probability order, whose cumulative softmax mass stays below
+    //      nucleus_p.  MSB radix select over the score keys with histograms of
+    //      probability mass (p = e / Z in float32, summed in double) merged over
+    //      the cluster; ties at the threshold key share one probability. ----
+    int ncount = 0;
+    if (nucleus) {
+      const float Zf = (float)Ztot;
+      const double P = p.cfg.nucleus_p;
+      uint32_t prefix = 0, pmask = 0;
+      double above = 0.0;  // mass of the blocks ranked above the current prefix
+      int n_above = 0;
+      bool all = false;
+#pragma unroll 1
+      for (int pass = 0; pass < 4; ++pass) {
+        const int shift = 24 - 8 * pass;
+        for (int t = tid; t < 256; t += kPlanThreads) {
+          nmass[t] = 0.0;
+          ncnt[t] = 0u;
+        }
+        __syncthreads();
+        for (int li = tid; li < n; li += kPlanThreads) {
+          const float v = val(li);
+          const uint32_t k = score_key(v);
+          if ((k & pmask) == prefix) {
+            const float pr = __fdiv_rn(expf(__fsub_rn(zof(v), zmax)), Zf);
+            const int dg = (k >> shift) & 0xFF;
+            atomicAdd(&nmass[dg], (double)pr);
+            atomicAdd(&ncnt[dg], 1u);
+          }
+        }
+        cl.sync();  // every CTA's histograms complete
+        if (warp == 0) {
+          double m8[8], tot = 0.0;
+          int c8[8], ctot = 0;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            m8[e] = 0.0;
+            c8[e] = 0;
+          }
+#pragma unroll
+          for (int r = 0; r < kPlanMaxCluster; ++r) {
+            if (r < C) {
+              const double* mr = cl.map_shared_rank(nmass, r);
+              const uint32_t* cr = cl.map_shared_rank(ncnt, r);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                m8[e] += mr[255 - 8 * lane - e];
+                c8[e] += (int)cr[255 - 8 * lane - e];
+              }
+            }
+          }
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            tot += m8[e];
+            ctot += c8[e];
+          }
+          double incl = tot;
+          int cincl = ctot;
+#pragma unroll
+          for (int o = 1; o < 32; o <<= 1) {
+            const double y = __shfl_up_sync(0xffffffffu, incl, o);
+            const int cy = __shfl_up_sync(0xffffffffu, cincl, o);
+            if (lane >= o) {
+              incl += y;
+              cincl += cy;
+            }
+          }
+          // below the first pass the prefix's mass bounds the target (rounding)
+          const double all_mass = __shfl_sync(0xffffffffu, incl, 31);
+          const double Pu = pass > 0 ? fmin(P, above + all_mass) : P;
+          const double excl = incl - tot;
+          const int cexcl = cincl - ctot;
+          if (lane == 0) s_ndigit = -1;
+          __syncwarp();
+          if (above + excl < Pu && Pu <= above + incl) {
+            double acc = excl;
+            int cacc = cexcl;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              if (above + acc + m8[e] >= Pu) {
+                s_ndigit = 255 - 8 * lane - e;
+                s_nmass_above = acc;
+                s_ncnt_above = cacc;
+                s_ncnt_digit = c8[e];
+                break;
+              }
+              acc += m8[e];
+              cacc += c8[e];
+            }
+          }
+        }
+        cl.sync();  // digit read by every CTA before the histograms are cleared again
+        if (s_ndigit < 0) {  // all the mass is below nucleus_p (same in every CTA)
+          all = true;
+          break;
+        }
+        above += s_nmass_above;
+        n_above += s_ncnt_above;
+        prefix |= (uint32_t)s_ndigit << shift;
+        pmask |= 0xFFu << shift;
+      }
+      if (all) {
+        ncount = nb;
+      } else {
+        // the s_ncnt_digit blocks whose key equals the threshold share one probability
+        const uint32_t T = prefix;
+        const float sT = __uint_as_float((T & 0x80000000u) ? (T & 0x7FFFFFFFu) : ~T);
+        const double pT = (double)__fdiv_rn(expf(__fsub_rn(zof(sT), zmax)), Zf);
+        const int E = s_ncnt_digit;
+        long long ties = pT > 0.0 ? (long long)ceil((P - above) / pT) - 1 : (long long)E;
+        ties = ties < 0 ? 0 : (ties > E ? E : ties);
+        ncount = n_above + (int)ties;
+      }
+    }
     double t_mine = 0.0;
+    if (nucleus) t_mine = rank == 0 ? (double)(ncount + 1) : 0.0;  // weight = count + 1
     if (adaptive) {
       double c2 = cp, z2 = 0.0;
       block_sum2(c2, z2, dred, dred2);
@@ -465,8 +591,10 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanParams p) {
       st_relaxed_u64(slots + at, ((uint64_t)kSlotTag << 32) | (uint64_t)__float_as_uint(thi));
       st_relaxed_u64(slots + at + 1, ((uint64_t)kSlotTag << 32) | (uint64_t)__float_as_uint(tlo));
     }
-    auto weight_of = [&](double e) -> double {  // adakv/budget.py:36-37, float64 after the division
-      return (double)(float)e / log((double)imax(nb, 2)) + 1e-6;
+    auto weight_of = [&](double e) -> double {
+      // entropy: adakv/budget.py:36-37, float64 after the division; nucleus:
+      // the published count + 1 (budget.py:41)
+      return nucleus ? e : (double)(float)e / log((double)imax(nb, 2)) + 1e-6;
     };
 
     // ---- exchange across the sequence's heads (warp 0) / merge histograms ----
@@ -502,7 +630,7 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanParams p) {
 #pragma unroll
       for (int q4 = 0; q4 < 4; ++q4) {
         const int hh = lane + q4 * 32;
-        if (hh < p.Hq && adaptive) {
+        if (hh < p.Hq && soft) {
           const double wv = weight_of(ents[q4]);
           ps += wv;
           if (hh == h) s_w = wv;
@@ -531,7 +659,7 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanParams p) {
     __syncthreads();
     pdl_launch_dependents();  // every CTA is past the exchange: the attend grid may launch
     const SeqBudget sbud = seq_budget(nb, p.cfg);
-    const double w = adaptive ? s_w : 0.0;
+    const double w = soft ? s_w : 0.0;
     const int K = imin(head_count(sbud, p.cfg, w, s_sumw, p.Hq), p.table_width);
     const int n_forced = (sink + local >= nb) ? nb : sink + local;
     const int Kc = K - n_forced;  // content blocks to pick

@@ -155,7 +155,7 @@ def adakv_attention_forward(module, query, key, value, attention_mask, scaling, 
         st = _sync_centroids(module, key, Hq, bs, rebuild=False, minmax=minmax)
         sp = _lib.select_params(cfg["avg_budget"], cfg["k_min"], cfg["k_max"],
                                 cfg["n_sink_blocks"], cfg["n_local_blocks"], cfg["c_min"],
-                                cfg["temperature"], cfg["budget_policy"])
+                                cfg["temperature"], cfg["budget_policy"], cfg["nucleus_p"])
         geo = _geometry(B, Hq, Hkv, D, bs, S, st.cbuf.shape[2], query.dtype)
         L = _lib.lib()
         width = L.adakv_plan_table_width(geo, sp)

@@ -116,12 +116,12 @@ class Selector:
 
     def __init__(self, S_total, n_q_heads, n_kv_heads, head_dim, block_size, dtype, device,
                  avg_budget=64, k_min=2, k_max=64, n_sink_blocks=1, n_local_blocks=4, c_min=1,
-                 temperature=1.0, budget_policy="adaptive"):
+                 temperature=1.0, budget_policy="adaptive", nucleus_p=0.9):
         self.nb = -(-S_total // block_size)
         self.geo = _lib.geometry(1, n_q_heads, n_kv_heads, head_dim, block_size, S_total, self.nb,
                                  _lib.TORCH_DTYPES[dtype])
         self.params = _lib.select_params(avg_budget, k_min, k_max, n_sink_blocks, n_local_blocks,
-                                         c_min, temperature, budget_policy)
+                                         c_min, temperature, budget_policy, nucleus_p)
         L = _lib.lib()
         self.width = L.adakv_plan_table_width(self.geo, self.params)
         if self.width < 1:

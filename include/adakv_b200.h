@@ -50,7 +50,7 @@
 extern "C" {
 #endif
 
-#define ADAKV_B200_ABI_VERSION 1
+#define ADAKV_B200_ABI_VERSION 2
 
 /* element types of q / K / V / out */
 #define ADAKV_DTYPE_F32 0
@@ -60,6 +60,8 @@ extern "C" {
 /* budget policies (adakv/budget.py:45-86) */
 #define ADAKV_POLICY_FIXED 0    /* every head gets round(target) blocks           */
 #define ADAKV_POLICY_ADAPTIVE 1 /* surplus split by normalised score entropy       */
+#define ADAKV_POLICY_NUCLEUS 2  /* surplus split by the blocks holding nucleus_p of
+                                   the softmax mass (budget.py:38-41)              */
 
 /* return codes */
 #define ADAKV_OK 0
@@ -96,7 +98,7 @@ typedef struct adakv_view {
 /* Selection knobs, named and defaulted as plan_selection
  * (adakv/attention.py:149-162): avg_budget, k_min=2, k_max=64,
  * n_sink_blocks=1, n_local_blocks=4, c_min=1, temperature=1.0,
- * policy=ADAKV_POLICY_ADAPTIVE. */
+ * policy=ADAKV_POLICY_ADAPTIVE, nucleus_p=0.9. */
 typedef struct adakv_select_params {
   double avg_budget;
   double temperature;
@@ -106,6 +108,7 @@ typedef struct adakv_select_params {
   int32_t n_local_blocks;
   int32_t c_min;
   int32_t policy;
+  double nucleus_p; /* ADAKV_POLICY_NUCLEUS: cumulative mass target (0.9)   */
 } adakv_select_params;
 
 /* ABI version of the loaded library (ADAKV_B200_ABI_VERSION). */

@@ -55,7 +55,7 @@ def test_no_torch_in_the_abi():
 
 
 def test_abi_version(lib):
-    assert lib.adakv_abi_version() == 1
+    assert lib.adakv_abi_version() == 2
 
 
 def geo(**kw):
@@ -67,7 +67,7 @@ def geo(**kw):
 
 def params(**kw):
     d = dict(avg_budget=64.0, temperature=1.0, k_min=2, k_max=512, n_sink_blocks=1,
-             n_local_blocks=4, c_min=1, policy=_lib.POLICY_ADAPTIVE)
+             n_local_blocks=4, c_min=1, policy=_lib.POLICY_ADAPTIVE, nucleus_p=0.9)
     d.update(kw)
     return _lib.SelectParams(*[d[f] for f, _ in _lib.SelectParams._fields_])
 

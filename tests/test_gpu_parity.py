@@ -447,3 +447,33 @@ def test_minmax_estimator_matches_oracle(dtype):
     kmin2, kmax2 = O.build_minmax(K2, bs)
     assert np.array_equal(cache.kmin.cpu().numpy(), kmin2)
     assert np.array_equal(cache.kmax.cpu().numpy(), kmax2)
+
+
+@pytest.mark.parametrize("Hq,Hkv,D,S,avg,kmax", [(12, 2, 64, 320, 8, 256),
+                                                 (32, 8, 128, 8192, 64, 512),
+                                                 (32, 8, 128, 65536 + 9, 64, 512)])
+def test_nucleus_policy_matches_oracle(Hq, Hkv, D, S, avg, kmax):
+    """budget_policy='adaptive_nucleus' (adakv/budget.py:38-41): per-head weight
+    = number of blocks, in descending probability order, whose cumulative
+    softmax mass stays below nucleus_p, plus one.  The GPU budget and selection
+    must equal the oracle's on the GPU's own scores."""
+    _need_cuda()
+    from adakv_b200.batch import BatchedDecoder
+    bs = 16
+    case = make_decode_case(55, 1, Hq, Hkv, D, S, bs, "bf16")
+    dt = torch.bfloat16
+    kw = dict(avg_budget=avg, k_min=2, k_max=kmax, budget_policy="adaptive_nucleus", nucleus_p=0.9)
+    dec = BatchedDecoder(1, Hq, Hkv, D, bs, S, dt, "cuda", **kw)
+    dec.load(torch.from_numpy(case.K).to("cuda", dt), torch.from_numpy(case.V).to("cuda", dt), [S])
+    scores = torch.zeros((Hq, dec.nb_cap), dtype=torch.float32, device="cuda")
+    dec.plan(torch.from_numpy(case.q).to("cuda", dt), scores_out=scores)
+    sets = dec.selected_sets()
+    assert dec.status() == 0
+    nb = -(-S // bs)
+    sc = scores[:, :nb].cpu().numpy()
+    k, raw = O.allocate_budget(sc, avg, 2, kmax, 1, 4, 1, policy="adaptive_nucleus",
+                               nucleus_p=0.9, return_raw=True)
+    mask, _ = O.select_blocks(sc, k, 1, 4, 1)
+    n_exact, n_budget, n_score, failures = O.compare_selection(sc, k, raw, mask, sets, 1, 4, 1)
+    assert not failures, failures[:4]
+    assert n_exact + n_budget + n_score == Hq
