@@ -478,10 +478,12 @@ def main():
         if rank != 0:
             return
         threads = os.cpu_count() or 1
-        times = run_cpu(headline, args.seed, max(args.steps, 1), 60.0, threads)
+        warm = max(0, args.warmup)
+        times = run_cpu(headline, args.seed, max(args.steps, 1) + warm, 60.0, threads)
+        times = times[warm:] if len(times) > warm + 1 else times[-1:]  # untimed warm-up steps
         v = float(np.mean(times))
         line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "us", "n_gpus": args.gpus,
-                "steps": len(times), "warmup": 0, "ms_per_step": v / 1000.0,
+                "steps": len(times), "warmup": warm, "ms_per_step": v / 1000.0,
                 "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
                 "data": "synthetic", "config": {"workload": workload_name(headline)},
                 "cpu_baseline": {"value": v, "unit": "us", "cores": threads, "kind": "port",
