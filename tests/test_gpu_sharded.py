@@ -120,3 +120,36 @@ def test_cfg4_shape_1m_tokens_sharded_8_ways():
         ref = torch.softmax(a, 0) @ vv
         e = (out[h].double() - ref).abs().max().item()
         assert e < BF16_TOL, f"head {h}: {e:.3e}"
+
+
+def test_2m_tokens_plan_reads_rows_from_l2():
+    """2,097,152 tokens, 32/8 heads: each plan CTA's slice (65,536 blocks) is
+    above the shared-memory staging limit, so the selection reads the score
+    rows from L2 (the non-staged plan kernel).  Selection against the oracle's
+    budget + top-k on the GPU scores; a few heads' outputs in float64."""
+    _need_cuda()
+    Hq, Hkv, D, bs, S = 32, 8, 128, 16, 1 << 21
+    kw = dict(avg_budget=64, k_min=2, k_max=512)
+    g = torch.Generator(device="cuda").manual_seed(6)
+    q = torch.randn((Hq, D), device="cuda", generator=g).to(torch.bfloat16)
+    K = torch.randn((Hkv, S, D), device="cuda", generator=g).to(torch.bfloat16)
+    V = torch.randn((Hkv, S, D), device="cuda", generator=g).to(torch.bfloat16)
+    nb = S // bs
+    for h in range(0, Hkv, 2):  # planted retrieval blocks
+        for blk in torch.randint(0, nb, (4,), device="cuda", generator=g).tolist():
+            K[h, blk * bs:(blk + 1) * bs] += 3.0 * q[h * (Hq // Hkv)].float().div(
+                q[h * (Hq // Hkv)].float().norm()).to(torch.bfloat16)
+    sets, out, scores = _single(K, V, q, S, Hq, bs, **kw)
+    sc = scores[:, :nb].cpu().numpy()
+    k, raw = O.allocate_budget(sc, kw["avg_budget"], kw["k_min"], kw["k_max"], 1, 4, 1,
+                               return_raw=True)
+    mask, _ = O.select_blocks(sc, k, 1, 4, 1)
+    n_exact, n_budget, n_score, failures = O.compare_selection(sc, k, raw, mask, sets, 1, 4, 1)
+    assert not failures, failures[:4]
+    for h in (0, 21):
+        blocks = sets[h]
+        tok = torch.from_numpy((blocks[:, None] * bs + np.arange(bs)[None, :]).ravel()).cuda()
+        kk = K[h // (Hq // Hkv), tok].double()
+        vv = V[h // (Hq // Hkv), tok].double()
+        ref = torch.softmax((kk @ q[h].double()) / np.sqrt(D), 0) @ vv
+        assert (out[h].double() - ref).abs().max().item() < BF16_TOL
