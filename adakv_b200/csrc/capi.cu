@@ -282,7 +282,6 @@ int enqueue_select(const DeviceState* ds, const adakv_geometry* g, const adakv_s
                 g->n_q_heads, clusters);
   pp.csize = lay.csize;
   pp.slice_cap = lay.slice_cap;
-  pp.ecache = lay.ecache ? 1 : 0;
   pp.seqs_per_round = std::max(1, std::min(g->batch, clusters / g->n_q_heads));
   const int plan_grid = pp.seqs_per_round * g->n_q_heads * lay.csize;
   LaunchOpts op;

@@ -221,6 +221,12 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src, bool vali
                "r"(n)
                : "memory");
 }
+// the first `bytes` (0..16) of 16 B; the rest of the destination zero-filled
+__device__ __forceinline__ void cp_async16_n(void* dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(dst)), "l"(src),
+               "r"(bytes)
+               : "memory");
+}
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 

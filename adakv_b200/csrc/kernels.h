@@ -72,9 +72,8 @@ struct EstParams {
 // ---------------------------------------------------------------------------
 constexpr int kPlanThreads = 512;
 constexpr int kPlanSmemMaxKeys = 32 * 1024;   // slice staged in shared memory up to this many blocks
-constexpr int kPlanECacheMax = 16 * 1024;     // exp(z - zmax) cached in shared memory up to this many
 constexpr int kPlanMaxBlocks = 512 * 1024;    // longest sequence in blocks (bitmap words in smem)
-constexpr size_t kPlanSmemMax = 160 * 1024;   // opt-in dynamic shared memory of one plan CTA
+constexpr size_t kPlanSmemMax = 184 * 1024;   // opt-in dynamic shared memory of one plan CTA
 constexpr int kPlanMaxCluster = 8;            // CTAs splitting one head's score row
 constexpr int kPlanSlotsPerRow = 2 * kPlanMaxCluster;  // exchange words per (sequence, head)
 
@@ -83,7 +82,6 @@ struct PlanLayout {
   int csize;       // CTAs per (sequence, head)
   int slice_cap;   // blocks per CTA (multiple of 32)
   bool smem_keys;  // slice staged in shared memory (else re-read from L2)
-  bool ecache;     // exp(z - zmax) cached in shared memory
   size_t smem;     // dynamic shared memory bytes
 };
 
@@ -105,7 +103,6 @@ struct PlanParams {
   int bm_words;
   int csize;                // CTAs of the cluster splitting each row
   int slice_cap;            // blocks per CTA (PlanLayout::slice_cap)
-  int ecache;               // cache exp(z - zmax) in shared memory (PlanLayout::ecache)
   int seqs_per_round;       // grid = seqs_per_round * Hq * csize CTAs
   uint32_t* status;
 };

@@ -44,6 +44,7 @@
 // All CTAs of one sequence must be resident together (they wait on each
 // other's slots): the host sizes the grid from the cluster occupancy.
 #include <algorithm>
+#include <type_traits>
 
 #include <cooperative_groups.h>
 
@@ -86,6 +87,16 @@ constexpr int kPW = kPlanThreads / 32;  // warps per CTA
 constexpr int kPlanILP = 4;             // row elements per thread per tile (independent chains)
 constexpr int kBuckets = 2048;          // bucket-select histogram bins
 constexpr int kCandCap = 1024;          // members of the boundary bucket ranked exactly
+constexpr int kFloorKeys = 8192;        // slice length from which the bucket floor and lists pay
+constexpr int kListCap = 24;            // bucket-range blocks a thread lists
+constexpr int kWinCap = 16;             // clamp-window blocks a thread defers
+constexpr int kPassRun = 8;             // keys per thread and tile of the pass (2 runs of 4)
+
+// floor(w) for 0 <= w < 2^23 (0 for w <= 0) without a float -> int conversion:
+// adding 2^23 rounding toward zero leaves floor(w) in the low mantissa bits
+__device__ __forceinline__ int bucket_floor(float w) {
+  return __float_as_int(__fadd_rz(fmaxf(w, 0.f), 8388608.f)) - 0x4B000000;
+}
 
 // bucket of a content score: floor((cmx - s) * scale), clamped to the last
 // bucket (which also takes NaN and -inf); non-decreasing as s decreases
@@ -157,6 +168,7 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanParams p) {
   __shared__ float2 wpart[kPW];
   __shared__ float wm_s[kPW];
   __shared__ double wd[kPW][4];
+  __shared__ int s_cl_over;                        // a thread's list overflowed
   __shared__ double dred[kPW], dred2[kPW];
   __shared__ double s_sumw, s_w;
   __shared__ double nmass[256];          // nucleus: probability mass per key digit
@@ -171,9 +183,13 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanParams p) {
   const int slice_cap = p.slice_cap;
   const int nwl_alloc = (slice_cap / 32 + kPW - 1) / kPW * kPW;  // ballot words, whole passes
   uint32_t* keys = sm;                                                     // [slice_cap] (SMEM)
-  float* ecache = reinterpret_cast<float*>(sm + (SMEM ? slice_cap : 0));   // [slice_cap] (ecache)
-  uint32_t* wsel = reinterpret_cast<uint32_t*>(ecache) + (p.ecache ? slice_cap : 0);
+  uint32_t* wsel = sm + (SMEM ? slice_cap : 0);
   uint32_t* weq = wsel + nwl_alloc;
+  // per-thread lists of slice indices, column `tid` (16-bit when the slice is
+  // staged, so at most kPlanSmemMaxKeys long)
+  using LIdx = typename std::conditional<SMEM, uint16_t, uint32_t>::type;
+  LIdx* clist = reinterpret_cast<LIdx*>(weq + nwl_alloc);  // [kListCap][threads] bucket range
+  LIdx* wlist = clist + kListCap * kPlanThreads;           // [kWinCap][threads] clamp window
   const PlanPart* lane_part = cl.map_shared_rank(&part, lane < C ? lane : 0);  // rank `lane`
 
   const int group = blockIdx.x / C;
@@ -198,6 +214,20 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanParams p) {
     const float* srow = p.scores + (int64_t)row * p.score_stride;
 
     auto val = [&](int li) -> float { return SMEM ? __uint_as_float(keys[li]) : srow[lo + li]; };
+    // stage the slice in shared memory: 16-byte cp.async (every load of the
+    // slice in flight at once) when it is 16-byte aligned, else plain loads;
+    // the caller waits (cp_async_wait_all) before its next barrier
+    auto stage_issue = [&]() {
+      const float* src = srow + lo;
+      if ((reinterpret_cast<uintptr_t>(src) & 15u) == 0) {
+        for (int i = 4 * tid; i < n; i += 4 * kPlanThreads)
+          cp_async16_n(keys + i, src + i, (uint32_t)imin(4, n - i) * 4u);
+        cp_async_commit();
+      } else {
+#pragma unroll 4
+        for (int li = tid; li < n; li += kPlanThreads) keys[li] = __float_as_uint(src[li]);
+      }
+    };
     const int sink = imin(p.cfg.n_sink, nb), local = imin(p.cfg.n_local, nb);
     auto forced = [&](int i) -> bool { return i < sink || i >= nb - local; };
 
@@ -209,35 +239,31 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanParams p) {
     auto zof = [&](float v) -> float { return unit_t ? v : __fdiv_rn(v, Tf); };
     float mx, cmx, m_t = -INFINITY;
     double csum, csq, Ztot = 0.0, Atot = 0.0;
-    bool ec = false;
     if (p.stats) {
-      // ---- 1'. stage the slice; the row statistics come from the estimator's
-      //      (chunk, warp) softmax partials, merged here by every CTA alike ----
-      for (int base = 0; base < n; base += kPlanThreads * kPlanILP) {
-        float v[kPlanILP];
-#pragma unroll
-        for (int r = 0; r < kPlanILP; ++r) {
-          const int li = base + r * kPlanThreads + tid;
-          v[r] = li < n ? srow[lo + li] : 0.f;
-        }
-        if (SMEM) {
-#pragma unroll
-          for (int r = 0; r < kPlanILP; ++r) {
-            const int li = base + r * kPlanThreads + tid;
-            if (li < n) keys[li] = __float_as_uint(v[r]);
-          }
-        }
-      }
+      // ---- 1'. stage the slice while the row statistics are merged from the
+      //      estimator's (chunk, warp) softmax partials, by every CTA alike ----
+      if (SMEM) stage_issue();
       const int nparts = ceil_div(nb, kEstRows) * kEstConsumerWarps;
       const float* prow = p.stats + (int64_t)row * p.stats_stride * kStatF;
       SoftPart acc = soft_empty();
-      for (int c = tid; c <= nparts; c += kPlanThreads)
-        soft_merge(acc, soft_load(prow + (int64_t)(c < nparts ? c : p.stats_stride - 1) * kStatF));
+      constexpr int PU = 4;  // partial loads in flight per thread
+      for (int c0 = tid; c0 <= nparts; c0 += kPlanThreads * PU) {
+        SoftPart t[PU];
+#pragma unroll
+        for (int u = 0; u < PU; ++u) {
+          const int c = c0 + u * kPlanThreads;
+          t[u] = c <= nparts ? soft_load(prow + (int64_t)(c < nparts ? c : p.stats_stride - 1) * kStatF)
+                             : soft_empty();
+        }
+#pragma unroll
+        for (int u = 0; u < PU; ++u) soft_merge(acc, t[u]);
+      }
       for (int t = tid; t < kBuckets; t += kPlanThreads) hist[t] = 0u;
       if (tid < kPlanMaxCluster) s_taken[tid] = 0;
       if (tid == 0) {
         s_ncand = 0;
         s_nfix = 0;
+        s_cl_over = 0;
       }
       // warp partials rescaled to the warp max; one barrier; every warp then
       // folds the kPW warp partials in the same order (identical results)
@@ -261,6 +287,7 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanParams p) {
           wd[warp][3] = cq;
         }
       }
+      if (SMEM) cp_async_wait_all();
       __syncthreads();  // also publishes the staged slice
       {
         const bool in = lane < kPW;
@@ -282,27 +309,28 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanParams p) {
     } else {
       // ---- 1. load the slice: statistics and per-thread softmax partials ----
       // Each thread keeps (m_t, z_t, a_t) = (max z, sum e^(z - m_t),
-      // sum e^(z - m_t) (z - m_t)) over its blocks, rescaled when m_t grows;
-      // e^(z - m_t) is cached when the slice is one tile (m_t is then final).
-      const bool one_tile = n <= kPlanThreads * kPlanILP;
-      ec = p.ecache && one_tile;
+      // sum e^(z - m_t) (z - m_t)) over its blocks, rescaled when m_t grows.
       mx = -INFINITY;
       cmx = -INFINITY;
       float csum_f = 0.f, csq_f = 0.f;
       float z_t = 0.f, a_t = 0.f;
+      if (SMEM) {
+        stage_issue();
+        cp_async_wait_all();
+        __syncthreads();
+      }
       for (int base = 0; base < n; base += kPlanThreads * kPlanILP) {
         float v[kPlanILP];
 #pragma unroll
         for (int r = 0; r < kPlanILP; ++r) {
           const int li = base + r * kPlanThreads + tid;
-          v[r] = li < n ? srow[lo + li] : -INFINITY;
+          v[r] = li < n ? val(li) : -INFINITY;
         }
         float tm = -INFINITY;
 #pragma unroll
         for (int r = 0; r < kPlanILP; ++r) {
           const int li = base + r * kPlanThreads + tid;
           if (li < n) {
-            if (SMEM) keys[li] = __float_as_uint(v[r]);
             mx = fmaxf(mx, v[r]);
             tm = fmaxf(tm, zof(v[r]));
             if (!forced(lo + li)) {
@@ -327,7 +355,6 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanParams p) {
             if (li < n) {
               const float d = zof(v[r]) - m_t;
               const float e = expf(d);
-              if (ec) ecache[li] = e;
               z_t += e;
               if (e > 0.f) a_t = fmaf(e, d, a_t);
             }
@@ -339,6 +366,7 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanParams p) {
       if (tid == 0) {
         s_ncand = 0;
         s_nfix = 0;
+        s_cl_over = 0;
       }
       // warp partials (softmax partials rescaled to the warp max), then one
       // fold of the warps by warp 0, then the cluster
@@ -416,46 +444,123 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanParams p) {
     const double nc_d = (double)(nb - imin(nb, sink + local));
     const double mean_c = nc_d > 0 ? csum / nc_d : 0.0;
     const double var_c = nc_d > 0 ? csq / nc_d - mean_c * mean_c : 0.0;
-    const double range = (double)cmx - mean_c + (var_c > 0.0 ? sqrt(var_c) : 0.0);
+    const double sd_c = var_c > 0.0 ? sqrt(var_c) : 0.0;
+    // Bucket floor: the content score with about 4 x table_width content
+    // blocks above it under a normal fit of the row, never below mean - sd.
+    // Only blocks above it are histogrammed and listed as selection
+    // candidates; a histogram holding fewer blocks than the row picks sends
+    // the row to the radix select, so the floor affects speed only.
+    // (long slices only: a short slice's passes are cheaper than the fit)
+    const bool long_slice = L >= kFloorKeys;  // L is the same in every CTA of the row
+    double floor_c = mean_c - sd_c;
+    if (long_slice) {
+      const double want = 4.0 * (double)p.table_width;
+      if (nc_d > 0.0 && want < 0.8 * nc_d)
+        floor_c = fmax(floor_c, mean_c + (double)normcdfinvf((float)(1.0 - want / nc_d)) * sd_c);
+    }
+    const double range = (double)cmx - floor_c;
     const bool buckets_ok = isfinite(cmx) && range > 0.0 && isfinite(range);
     const float scale = buckets_ok ? (float)((double)(kBuckets - 1) / range) : 0.f;
 
-    // ---- 2. clamp correction of this slice + the slice's histogram ----
+    // ---- 2. clamp correction of this slice, and the histogram and list of
+    //      its content blocks above the bucket floor ----
     // With zmax = max z (= max(s) / T, monotone rounding), d = z - zmax and
     // e = exp(d) as the reference computes them, H = log Z - A / Z - Cc / Z
     // where Cc sums e (log(1e-9) - d + log Z) over blocks with e / Z < 1e-9.
+    // On long slices both kinds of rare block are set aside per thread
+    // (column `tid` of a shared table, so a warp's stores are conflict-free)
+    // and finished after the pass: the per-key work is a few compares and
+    // predicated stores.
     const float zmax = unit_t ? mx : __fdiv_rn(mx, Tf);
     float cp = 0.f;
+    int ncl = 0;  // blocks this thread listed
     {
       const float Zf = (float)Ztot;
       const float logZ = adaptive ? (float)log(Ztot) : 0.f;
       const float ln_floor = logf(1e-9f);
       const float pre = 2e-9f * Zf;  // p < 1e-9 implies e < 2e-9 * Z
-      const float sc_t = (adaptive && m_t > -INFINITY) ? expf(m_t - zmax) : 0.f;
       // p < 1e-9 needs d < log(2e-9 Z); below d_lo the clamp's correction
       // e (log 1e-9 - log p) is under 1e-18 of H: skip the exp there
       const float d_hi = adaptive ? logf(pre) : -INFINITY;
       const float d_lo = d_hi - 25.f;
-      for (int base = 0; base < n; base += kPlanThreads * kPlanILP) {
+      auto corr = [&](float d) {
+        const float e = expf(d);
+        if (e > 0.f && e < pre && __fdiv_rn(e, Zf) < 1e-9f) cp = fmaf(e, ln_floor - d + logZ, cp);
+      };
+      if (!long_slice) {
+        // short slice: one inline pass (the deferred lists do not pay here)
+        for (int base = 0; base < n; base += kPlanThreads * kPlanILP) {
 #pragma unroll
-        for (int r = 0; r < kPlanILP; ++r) {
-          const int li = base + r * kPlanThreads + tid;
-          if (li < n) {
-            const float v = val(li);
-            if (adaptive) {
-              const float d = __fsub_rn(zof(v), zmax);
-              if (d < d_hi && d >= d_lo) {
-                const float e = ec ? ecache[li] * sc_t : expf(d);
-                if (e > 0.f && e < pre && __fdiv_rn(e, Zf) < 1e-9f)
-                  cp = fmaf(e, ln_floor - d + logZ, cp);
+          for (int r = 0; r < kPlanILP; ++r) {
+            const int li = base + r * kPlanThreads + tid;
+            if (li < n) {
+              const float v = val(li);
+              if (adaptive) {
+                const float d = __fsub_rn(zof(v), zmax);
+                if (d < d_hi && d >= d_lo) corr(d);
               }
-            }
-            if (buckets_ok && !forced(lo + li)) {
-              const int bk = bucket_of(v, cmx, scale);
-              if (bk < kBuckets - 1) atomicAdd(&hist[bk], 1u);
+              if (buckets_ok && !forced(lo + li)) {
+                const int bk = bucket_of(v, cmx, scale);
+                if (bk < kBuckets - 1) atomicAdd(&hist[bk], 1u);
+              }
             }
           }
         }
+      } else {
+        int nwin = 0;
+        auto flush = [&]() {
+          for (int i = 0; i < nwin; ++i) corr(__fsub_rn(zof(val((int)wlist[i * kPlanThreads + tid])), zmax));
+          nwin = 0;
+        };
+        // 2 runs of 4 consecutive keys per thread and tile (vector shared loads
+        // when the slice is staged); a window list that might not take another
+        // tile is finished first, so it never overflows
+        for (int base = 0; base < n; base += kPassRun * kPlanThreads) {
+          float vv[kPassRun];
+#pragma unroll
+          for (int u = 0; u < kPassRun / 4; ++u) {
+            const int li0 = base + u * 4 * kPlanThreads + 4 * tid;
+            if (SMEM) {
+              if (li0 < n) {
+                const uint4 w4 = *reinterpret_cast<const uint4*>(keys + li0);
+                vv[4 * u + 0] = __uint_as_float(w4.x);
+                vv[4 * u + 1] = __uint_as_float(w4.y);
+                vv[4 * u + 2] = __uint_as_float(w4.z);
+                vv[4 * u + 3] = __uint_as_float(w4.w);
+              }
+            } else {
+#pragma unroll
+              for (int e = 0; e < 4; ++e) vv[4 * u + e] = li0 + e < n ? srow[lo + li0 + e] : 0.f;
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < kPassRun / 4; ++u) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int li = base + u * 4 * kPlanThreads + 4 * tid + e;
+              const bool valid = li < n;
+              const float v = vv[4 * u + e];
+              if (adaptive) {
+                const float d = __fsub_rn(zof(v), zmax);
+                const bool win = valid && d < d_hi && d >= d_lo;
+                if (win) wlist[nwin * kPlanThreads + tid] = (LIdx)li;
+                nwin += win;
+              }
+              // in the bucket range: bucket_of(v) < kBuckets - 1; a full list
+              // keeps counting (the selection then scans the slice)
+              const float w = __fmul_rn(__fsub_rn(cmx, v), scale);
+              const bool in = buckets_ok && valid && w < (float)(kBuckets - 1) && !forced(lo + li);
+              if (in) {
+                atomicAdd(&hist[bucket_floor(w)], 1u);
+                clist[imin(ncl, kListCap - 1) * kPlanThreads + tid] = (LIdx)li;
+              }
+              ncl += in;
+            }
+          }
+          if (nwin > kWinCap - kPassRun) flush();
+        }
+        flush();
+        if (ncl > kListCap) s_cl_over = 1;
       }
     }
     // ---- nucleus weight (adakv/budget.py:38-41): the blocks, in descending
@@ -701,33 +806,73 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanParams p) {
       }
     }
     const bool bucketed = !all && Kc > 0 && !use_radix;
-    if (!use_radix) {
-      // selected: forced blocks, every content block of a bucket above jstar;
-      // the members of bucket jstar are candidates, ranked across the cluster
-      for (int j = 0; j * kPlanThreads < n; ++j) {
-        const int li = j * kPlanThreads + tid;
-        bool sel = false;
-        if (li < n) {
-          if (all || forced(lo + li)) {
-            sel = true;
-          } else if (bucketed) {
-            const float v = val(li);
-            const int bk = bucket_of(v, cmx, scale);
-            sel = bk < jstar;
-            if (bk == jstar) {
-              const int slot = atomicAdd(&s_ncand, 1);
-              cand_idx[slot] = lo + li;
-              cand_key[slot] = score_key(v);
-            }
-          }
-        }
-        const uint32_t bsel = __ballot_sync(0xffffffffu, sel);
-        if (lane == 0) {
-          wsel[j * kPW + warp] = bsel;
-          weq[j * kPW + warp] = 0u;
-          if (bsel) atomicAdd(&s_nfix, __popc(bsel));
+    if (bucketed && long_slice && !s_cl_over) {
+      // every warp's list is complete: the forced blocks, then the listed
+      // blocks of buckets above jstar; the members of bucket jstar are
+      // candidates, ranked across the cluster
+      for (int wi = tid; wi < nwl; wi += kPlanThreads) wsel[wi] = 0u;
+      __syncthreads();
+      int cnt = 0;
+      const int f1 = imin(sink, hi), f2 = imax(nb - local, lo);
+      for (int i = lo + tid; i < f1; i += kPlanThreads, ++cnt)
+        atomicOr(&wsel[(i - lo) >> 5], 1u << ((i - lo) & 31));
+      for (int i = f2 + tid; i < hi; i += kPlanThreads, ++cnt)
+        atomicOr(&wsel[(i - lo) >> 5], 1u << ((i - lo) & 31));
+      for (int i = 0; i < ncl; ++i) {
+        const int li = (int)clist[i * kPlanThreads + tid];
+        const float v = val(li);
+        const int bk = bucket_floor(__fmul_rn(__fsub_rn(cmx, v), scale));
+        if (bk < jstar) {
+          atomicOr(&wsel[li >> 5], 1u << (li & 31));
+          ++cnt;
+        } else if (bk == jstar) {
+          const int slot = atomicAdd(&s_ncand, 1);
+          cand_idx[slot] = lo + li;
+          cand_key[slot] = score_key(v);
         }
       }
+#pragma unroll
+      for (int o = 16; o; o >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
+      if (lane == 0 && cnt) atomicAdd(&s_nfix, cnt);
+      __syncthreads();
+      if (tid == 0) {
+        part.ncand = s_ncand;
+        part.nfix = s_nfix;
+      }
+    } else if (!use_radix) {
+      // selected: forced blocks, every content block of a bucket above jstar;
+      // the members of bucket jstar are candidates, ranked across the cluster
+      int nfix = 0;  // lane 0: blocks this warp selected
+      for (int j0 = 0; j0 * kPlanThreads < n; j0 += 4) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int j = j0 + u;
+          if (j * kPlanThreads >= n) break;  // uniform over the CTA
+          const int li = j * kPlanThreads + tid;
+          bool sel = false;
+          if (li < n) {
+            if (all || forced(lo + li)) {
+              sel = true;
+            } else if (bucketed) {
+              const float v = val(li);
+              const int bk = bucket_of(v, cmx, scale);
+              sel = bk < jstar;
+              if (bk == jstar) {
+                const int slot = atomicAdd(&s_ncand, 1);
+                cand_idx[slot] = lo + li;
+                cand_key[slot] = score_key(v);
+              }
+            }
+          }
+          const uint32_t bsel = __ballot_sync(0xffffffffu, sel);
+          if (lane == 0) {
+            wsel[j * kPW + warp] = bsel;
+            weq[j * kPW + warp] = 0u;
+            nfix += __popc(bsel);
+          }
+        }
+      }
+      if (lane == 0 && nfix) atomicAdd(&s_nfix, nfix);
       __syncthreads();
       if (tid == 0) {
         part.ncand = s_ncand;
@@ -918,10 +1063,11 @@ PlanLayout plan_layout(int nb_max, int csize) {
   l.csize = csize;
   l.slice_cap = (ceil_div(imax(nb_max, 1), csize) + 31) / 32 * 32;
   l.smem_keys = l.slice_cap <= kPlanSmemMaxKeys;
-  l.ecache = l.slice_cap <= kPlanECacheMax;
   const int nwl_alloc = (l.slice_cap / 32 + kPW - 1) / kPW * kPW;
-  l.smem = (size_t)(l.smem_keys ? l.slice_cap : 0) * 4 + (size_t)(l.ecache ? l.slice_cap : 0) * 4 +
-           (size_t)2 * nwl_alloc * 4;
+  // the per-thread lists exist for slices long enough to use them
+  const bool lists = l.slice_cap >= kFloorKeys;
+  l.smem = (size_t)(l.smem_keys ? l.slice_cap : 0) * 4 + (size_t)2 * nwl_alloc * 4 +
+           (lists ? (size_t)(kListCap + kWinCap) * kPlanThreads * (l.smem_keys ? 2 : 4) : 0);
   return l;
 }
 

@@ -153,3 +153,40 @@ def test_2m_tokens_plan_reads_rows_from_l2():
         vv = V[h // (Hq // Hkv), tok].double()
         ref = torch.softmax((kk @ q[h].double()) / np.sqrt(D), 0) @ vv
         assert (out[h].double() - ref).abs().max().item() < BF16_TOL
+
+
+@pytest.mark.parametrize("case", ["floor_miss", "list_overflow", "normal"])
+def test_long_slice_selection_paths(case):
+    """Score rows long enough (32,768 blocks per plan CTA) for the bucket
+    floor and the per-thread candidate lists, shaped so that each path is
+    taken: a thin upper tail that leaves fewer blocks above the normal-fit
+    floor than the row picks (radix select), a table width so wide that the
+    floor drops to mean - sd and the lists overflow (full scan), and plain
+    Gaussian rows (compact selection).  adakv_select against the oracle's
+    budget + top-k on the same scores."""
+    _need_cuda()
+    Hq, Hkv, D, bs, S = 64, 8, 128, 16, 1 << 20
+    nb = S // bs
+    g = torch.Generator(device="cuda").manual_seed(11)
+    sc = torch.randn((Hq, nb), device="cuda", generator=g)
+    kw = dict(avg_budget=256, k_min=2, k_max=1024)
+    if case == "floor_miss":
+        # 1 % of the blocks far above the rest: the fit puts the floor above
+        # the bulk, and the planted blocks alone are fewer than the budgets
+        kw = dict(avg_budget=1000, k_min=900, k_max=1024)
+        idx = torch.randint(0, nb, (Hq, nb // 100), device="cuda", generator=g)
+        sc.scatter_(1, idx, 100.0 + torch.rand((Hq, nb // 100), device="cuda", generator=g))
+    elif case == "list_overflow":
+        kw = dict(avg_budget=12000, k_min=2, k_max=16384)
+    sel = Selector(S, Hq, Hkv, D, bs, torch.bfloat16, "cuda", **kw)
+    table, sel_lens = sel.select(sc)
+    torch.cuda.synchronize()
+    bt, sl = table.cpu().numpy(), sel_lens.cpu().numpy()
+    sets = [np.sort(bt[h, : sl[h]]) for h in range(Hq)]
+    s = sc.cpu().numpy().astype(np.float32)
+    k, raw = O.allocate_budget(s, kw["avg_budget"], kw["k_min"], kw["k_max"], 1, 4, 1,
+                               return_raw=True)
+    mask, _ = O.select_blocks(s, k, 1, 4, 1)
+    n_exact, n_budget, n_score, failures = O.compare_selection(s, k, raw, mask, sets, 1, 4, 1)
+    assert not failures, failures[:4]
+    assert n_exact + n_budget + n_score == Hq
