@@ -141,24 +141,29 @@ __global__ void __launch_bounds__(MMA ? kAttendMmaWarps * 32 : kAttendMaxThreads
   pdl_wait();
 
   // ---- union of the group's selection bitmaps; this CTA's share of it ----
+  // Each thread ORs a run of consecutive words, four words' loads in flight
+  // at a time; the share is then enumerated from the union in shared memory
+  // and every listed block's head mask is fetched in one parallel pass.
   const int wpt = ceil_div(nw, nthr);
   const int w0 = imin(tid * wpt, nw), w1 = imin(w0 + wpt, nw);
   int cnt = 0;
-  uint32_t x0[16];  // head words of this thread's first word (reused by the enumeration)
-  for (int w = w0; w < w1; ++w) {
-    uint32_t x[16];
+  for (int wb = w0; wb < w1; wb += 4) {
+    uint32_t u4[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
-    for (int hh = 0; hh < 16; ++hh)
-      x[hh] = hh < g ? p.bitmap[(int64_t)(row0 + hh) * p.bm_words + w] : 0u;
-    uint32_t u = 0;
+    for (int k = 0; k < 4; ++k) {
+      if (wb + k < w1) {
 #pragma unroll
-    for (int hh = 0; hh < 16; ++hh) u |= x[hh];
-    if (w == w0) {
-#pragma unroll
-      for (int hh = 0; hh < 16; ++hh) x0[hh] = x[hh];
+        for (int hh = 0; hh < 16; ++hh)
+          if (hh < g) u4[k] |= p.bitmap[(int64_t)(row0 + hh) * p.bm_words + wb + k];
+      }
     }
-    uw[w] = u;
-    cnt += __popc(u);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      if (wb + k < w1) {
+        uw[wb + k] = u4[k];
+        cnt += __popc(u4[k]);
+      }
+    }
   }
   const int before = block_exclusive_scan(cnt, scan_scratch);
   const int U = scan_scratch[32];
@@ -172,23 +177,22 @@ __global__ void __launch_bounds__(MMA ? kAttendMmaWarps * 32 : kAttendMaxThreads
         rk += pc;
         continue;
       }
-      uint32_t x[16];
-#pragma unroll
-      for (int hh = 0; hh < 16; ++hh)
-        x[hh] = w == w0 ? x0[hh] : (hh < g ? p.bitmap[(int64_t)(row0 + hh) * p.bm_words + w] : 0u);
       while (u && rk < hi) {
         const int bit = __ffs(u) - 1;
         u &= u - 1u;
-        if (rk >= lo) {
-          uint32_t m = 0;
-#pragma unroll
-          for (int hh = 0; hh < 16; ++hh) m |= ((x[hh] >> bit) & 1u) << hh;
-          list[rk - lo] = w * 32 + bit;
-          lmask[rk - lo] = m;
-        }
+        if (rk >= lo) list[rk - lo] = w * 32 + bit;
         ++rk;
       }
     }
+  }
+  __syncthreads();
+  for (int i = tid; i < hi - lo; i += nthr) {
+    const int id = list[i], w = id >> 5, bit = id & 31;
+    uint32_t m = 0;
+#pragma unroll
+    for (int hh = 0; hh < 16; ++hh)
+      if (hh < g) m |= ((p.bitmap[(int64_t)(row0 + hh) * p.bm_words + w] >> bit) & 1u) << hh;
+    lmask[i] = m;
   }
   __syncthreads();
   const int n = hi - lo;
