@@ -152,7 +152,10 @@ __device__ __forceinline__ int rank_prefix(int v, int& tot) {
   return x - v;
 }
 
-template <bool SMEM>
+// SMEM: the slice is staged in shared memory; LONG: the layout has room for
+// the per-thread lists of the long-slice pass (a short-slice instantiation
+// leaves that code out, which keeps its instruction footprint small)
+template <bool SMEM, bool LONG>
 __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanParams p) {
   extern __shared__ __align__(16) uint32_t sm[];
   __shared__ __align__(16) uint32_t hist[kBuckets];   // this CTA's histogram (read by the cluster)
@@ -451,7 +454,7 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanParams p) {
     // candidates; a histogram holding fewer blocks than the row picks sends
     // the row to the radix select, so the floor affects speed only.
     // (long slices only: a short slice's passes are cheaper than the fit)
-    const bool long_slice = L >= kFloorKeys;  // L is the same in every CTA of the row
+    const bool long_slice = LONG && L >= kFloorKeys;  // L is the same in every CTA of the row
     double floor_c = mean_c - sd_c;
     if (long_slice) {
       const double want = 4.0 * (double)p.table_width;
@@ -1071,16 +1074,22 @@ PlanLayout plan_layout(int nb_max, int csize) {
   return l;
 }
 
+using PlanKernel = void (*)(PlanParams);
+
+// the instantiation a layout runs (slices beyond the staging limit are long)
+static PlanKernel plan_kernel_for(const PlanLayout& l) {
+  if (!l.smem_keys) return plan_kernel<false, true>;
+  return l.slice_cap >= kFloorKeys ? plan_kernel<true, true> : plan_kernel<true, false>;
+}
+
 cudaError_t plan_kernels_init() {
-  cudaError_t e = cudaFuncSetAttribute(plan_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)kPlanSmemMax);
-  if (e != cudaSuccess) return e;
-  e = cudaFuncSetAttribute(plan_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)kPlanSmemMax);
-  if (e != cudaSuccess) return e;
-  e = cudaFuncSetAttribute(plan_kernel<true>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-  if (e != cudaSuccess) return e;
-  return cudaFuncSetAttribute(plan_kernel<false>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  for (PlanKernel k : {plan_kernel<true, false>, plan_kernel<true, true>, plan_kernel<false, true>}) {
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPlanSmemMax);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
 }
 
 int plan_active_clusters(const PlanLayout& l) {
@@ -1096,9 +1105,7 @@ int plan_active_clusters(const PlanLayout& l) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   int n = 0;
-  const cudaError_t e = l.smem_keys
-                            ? cudaOccupancyMaxActiveClusters(&n, plan_kernel<true>, &cfg)
-                            : cudaOccupancyMaxActiveClusters(&n, plan_kernel<false>, &cfg);
+  const cudaError_t e = cudaOccupancyMaxActiveClusters(&n, plan_kernel_for(l), &cfg);
   if (e != cudaSuccess) {
     (void)cudaGetLastError();
     return 0;
@@ -1110,9 +1117,7 @@ cudaError_t launch_plan(const PlanParams& p, const PlanLayout& l, int grid, cuda
                         const LaunchOpts& o) {
   LaunchOpts oc = o;
   oc.cluster_x = (unsigned)l.csize;
-  if (l.smem_keys)
-    return launch_ex(plan_kernel<true>, dim3(grid), dim3(kPlanThreads), l.smem, st, oc, p);
-  return launch_ex(plan_kernel<false>, dim3(grid), dim3(kPlanThreads), l.smem, st, oc, p);
+  return launch_ex(plan_kernel_for(l), dim3(grid), dim3(kPlanThreads), l.smem, st, oc, p);
 }
 
 }  // namespace adakv
