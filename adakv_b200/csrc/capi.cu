@@ -259,10 +259,11 @@ int enqueue_select(const DeviceState* ds, const adakv_geometry* g, const adakv_s
   // exchange is also bounded in time.
   auto active = [&](const PlanLayout& l) {
     std::lock_guard<std::mutex> lock(g_dev_mu);
-    const int key = nb_max * 16 + l.csize;
+    const bool nucleus = sp->policy == ADAKV_POLICY_NUCLEUS;
+    const int key = (nb_max * 16 + l.csize) * 2 + (nucleus ? 1 : 0);
     auto it = ds->plan_ctas.find(key);
     if (it == ds->plan_ctas.end())
-      it = const_cast<DeviceState*>(ds)->plan_ctas.emplace(key, plan_active_clusters(l)).first;
+      it = const_cast<DeviceState*>(ds)->plan_ctas.emplace(key, plan_active_clusters(l, nucleus)).first;
     return it->second;
   };
   const int64_t heads = (int64_t)g->batch * g->n_q_heads;

@@ -237,7 +237,7 @@ size_t estimate_smem_bytes(int dtype, int D, int g, int B);
 int estimate_stages(int dtype, int D, int g, int B);
 PlanLayout plan_layout(int nb_max, int csize);
 // clusters of the plan kernel with layout `l` that can be resident at once
-int plan_active_clusters(const PlanLayout& l);
+int plan_active_clusters(const PlanLayout& l, bool nucleus);
 size_t attend_smem_bytes(int dtype, int D, int bs, int nbt, int g, int nw_max, int slice_cap,
                          int split);
 

@@ -153,9 +153,10 @@ __device__ __forceinline__ int rank_prefix(int v, int& tot) {
 }
 
 // SMEM: the slice is staged in shared memory; LONG: the layout has room for
-// the per-thread lists of the long-slice pass (a short-slice instantiation
-// leaves that code out, which keeps its instruction footprint small)
-template <bool SMEM, bool LONG>
+// the per-thread lists of the long-slice pass; NUC: the nucleus policy's
+// mass-weighted select is compiled in.  Instantiations leave out the code they
+// never run, which keeps the instruction footprint of the common ones small.
+template <bool SMEM, bool LONG, bool NUC>
 __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanParams p) {
   extern __shared__ __align__(16) uint32_t sm[];
   __shared__ __align__(16) uint32_t hist[kBuckets];   // this CTA's histogram (read by the cluster)
@@ -235,7 +236,7 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanParams p) {
     auto forced = [&](int i) -> bool { return i < sink || i >= nb - local; };
 
     const bool adaptive = nb >= 2 && p.cfg.policy == ADAKV_POLICY_ADAPTIVE;
-    const bool nucleus = nb >= 2 && p.cfg.policy == ADAKV_POLICY_NUCLEUS;
+    const bool nucleus = NUC && nb >= 2 && p.cfg.policy == ADAKV_POLICY_NUCLEUS;
     const bool soft = adaptive || nucleus;  // the row's softmax (Z) is needed
     const float Tf = (float)(p.cfg.temperature > 1e-6 ? p.cfg.temperature : 1e-6);
     const bool unit_t = (Tf == 1.0f);  // s / 1 == s exactly: skip the division
@@ -1076,14 +1077,20 @@ PlanLayout plan_layout(int nb_max, int csize) {
 
 using PlanKernel = void (*)(PlanParams);
 
-// the instantiation a layout runs (slices beyond the staging limit are long)
-static PlanKernel plan_kernel_for(const PlanLayout& l) {
-  if (!l.smem_keys) return plan_kernel<false, true>;
-  return l.slice_cap >= kFloorKeys ? plan_kernel<true, true> : plan_kernel<true, false>;
+// the instantiation a layout and policy run (slices beyond the staging limit are long)
+static PlanKernel plan_kernel_for(const PlanLayout& l, bool nucleus) {
+  if (nucleus) {
+    if (!l.smem_keys) return plan_kernel<false, true, true>;
+    return l.slice_cap >= kFloorKeys ? plan_kernel<true, true, true> : plan_kernel<true, false, true>;
+  }
+  if (!l.smem_keys) return plan_kernel<false, true, false>;
+  return l.slice_cap >= kFloorKeys ? plan_kernel<true, true, false> : plan_kernel<true, false, false>;
 }
 
 cudaError_t plan_kernels_init() {
-  for (PlanKernel k : {plan_kernel<true, false>, plan_kernel<true, true>, plan_kernel<false, true>}) {
+  for (PlanKernel k : {plan_kernel<true, false, false>, plan_kernel<true, true, false>,
+                       plan_kernel<false, true, false>, plan_kernel<true, false, true>,
+                       plan_kernel<true, true, true>, plan_kernel<false, true, true>}) {
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPlanSmemMax);
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
@@ -1092,7 +1099,7 @@ cudaError_t plan_kernels_init() {
   return cudaSuccess;
 }
 
-int plan_active_clusters(const PlanLayout& l) {
+int plan_active_clusters(const PlanLayout& l, bool nucleus) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(l.csize, 1, 1);
   cfg.blockDim = dim3(kPlanThreads, 1, 1);
@@ -1105,7 +1112,7 @@ int plan_active_clusters(const PlanLayout& l) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   int n = 0;
-  const cudaError_t e = cudaOccupancyMaxActiveClusters(&n, plan_kernel_for(l), &cfg);
+  const cudaError_t e = cudaOccupancyMaxActiveClusters(&n, plan_kernel_for(l, nucleus), &cfg);
   if (e != cudaSuccess) {
     (void)cudaGetLastError();
     return 0;
@@ -1117,7 +1124,8 @@ cudaError_t launch_plan(const PlanParams& p, const PlanLayout& l, int grid, cuda
                         const LaunchOpts& o) {
   LaunchOpts oc = o;
   oc.cluster_x = (unsigned)l.csize;
-  return launch_ex(plan_kernel_for(l), dim3(grid), dim3(kPlanThreads), l.smem, st, oc, p);
+  return launch_ex(plan_kernel_for(l, p.cfg.policy == ADAKV_POLICY_NUCLEUS), dim3(grid),
+                   dim3(kPlanThreads), l.smem, st, oc, p);
 }
 
 }  // namespace adakv
