@@ -344,6 +344,8 @@ __global__ void __launch_bounds__(kEstThreads, 1) estimate_kernel(EstParams p) {
     const int total = seq_base[p.B];
     const int c_begin = (int)((int64_t)total * blockIdx.x / gridDim.x);
     const int c_end = (int)((int64_t)total * (blockIdx.x + 1) / gridDim.x);
+    float qr[GP][E];  // the group's query slices, reloaded when the (sequence, KV head) changes
+    int qrun = -1;
     int i = 0;
     for (int c = c_begin; c < c_end; ++c, ++i) {
       const int s = i % stages;
@@ -361,15 +363,18 @@ __global__ void __launch_bounds__(kEstThreads, 1) estimate_kernel(EstParams p) {
       const int skip_from = appending ? (S - p.n_new) / p.bs - row0 : nrows;
       const int lim = imin(nrows, skip_from);
       const float* tile = ring + s * stage_f;
-      const T* qs = reinterpret_cast<const T*>(tile + TILE_F);
-      float qr[GP][E];
+      // (groups of 4 heads reload every chunk: measured faster there)
+      if (GP < 8 || b * p.Hkv + kvh != qrun) {
+        qrun = b * p.Hkv + kvh;
+        const T* qs = reinterpret_cast<const T*>(tile + TILE_F);
 #pragma unroll
-      for (int j = 0; j < GP; ++j) {
-        if (j < p.g) {
-          load_vec<T, E>(qs + j * D + lane * E, qr[j]);
-        } else {
+        for (int j = 0; j < GP; ++j) {
+          if (j < p.g) {
+            load_vec<T, E>(qs + j * D + lane * E, qr[j]);
+          } else {
 #pragma unroll
-          for (int e = 0; e < E; ++e) qr[j][e] = 0.f;
+            for (int e = 0; e < E; ++e) qr[j][e] = 0.f;
+          }
         }
       }
       float scs[NG];  // this lane's scores of the chunk (kept for the softmax partial)
