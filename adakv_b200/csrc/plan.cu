@@ -251,13 +251,22 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanParams p) {
       const float* prow = p.stats + (int64_t)row * p.stats_stride * kStatF;
       SoftPart acc = soft_empty();
       constexpr int PU = 4;  // partial loads in flight per thread
-      for (int c0 = tid; c0 <= nparts; c0 += kPlanThreads * PU) {
+      // partials c in [0, nparts], the last being the append's slot; a
+      // long-slice CTA merges only its rank's share of them and the cluster
+      // folds the C results below (a short slice's CTA merges them all)
+      int c_lo = 0, c_hi = nparts + 1;
+      if (LONG) {
+        const int share = ceil_div(nparts + 1, C);
+        c_lo = imin(nparts + 1, rank * share);
+        c_hi = imin(nparts + 1, c_lo + share);
+      }
+      for (int c0 = c_lo + tid; c0 < c_hi; c0 += kPlanThreads * PU) {
         SoftPart t[PU];
 #pragma unroll
         for (int u = 0; u < PU; ++u) {
           const int c = c0 + u * kPlanThreads;
-          t[u] = c <= nparts ? soft_load(prow + (int64_t)(c < nparts ? c : p.stats_stride - 1) * kStatF)
-                             : soft_empty();
+          t[u] = c < c_hi ? soft_load(prow + (int64_t)(c < nparts ? c : p.stats_stride - 1) * kStatF)
+                          : soft_empty();
         }
 #pragma unroll
         for (int u = 0; u < PU; ++u) soft_merge(acc, t[u]);
@@ -309,6 +318,34 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanParams p) {
         Atot = warp_sum(a);
         csum = warp_sum(in ? wd[lane][2] : 0.0);
         csq = warp_sum(in ? wd[lane][3] : 0.0);
+        if (LONG && tid == 0) {
+          part.mx = mx;
+          part.cmx = cmx;
+          part.csum = csum;
+          part.csq = csq;
+          part.M = M;
+          part.Z = Ztot;
+          part.A = Atot;
+        }
+      }
+      if (LONG) {
+        cl.sync();  // (1') every CTA's share of the partials is merged
+        const bool in = lane < C;
+        mx = warp_max(in ? lane_part->mx : -INFINITY);
+        cmx = warp_max(in ? lane_part->cmx : -INFINITY);
+        csum = warp_sum(in ? lane_part->csum : 0.0);
+        csq = warp_sum(in ? lane_part->csq : 0.0);
+        const float Mr = in ? lane_part->M : -INFINITY;
+        const float M = warp_max(Mr);
+        double z = 0.0, a = 0.0;
+        if (in && Mr > -INFINITY) {
+          const double zr = lane_part->Z, ar = lane_part->A;
+          const double sc = exp((double)Mr - (double)M);
+          z = zr * sc;
+          a = sc * (ar + zr * ((double)Mr - (double)M));
+        }
+        Ztot = warp_sum(z);
+        Atot = warp_sum(a);
       }
     } else {
       // ---- 1. load the slice: statistics and per-thread softmax partials ----
