@@ -67,6 +67,13 @@ class BatchedDecoder:
         self.ws_bytes = L.adakv_plan_workspace_bytes(geo, self.params)
         self.workspace = torch.zeros((self.ws_bytes,), dtype=torch.uint8, device=device)
         self.out = torch.zeros((batch, n_q_heads, head_dim), dtype=dtype, device=device)
+        # The per-step C-ABI arguments that never change, built once: a decode
+        # step is short enough (tens of microseconds) that rebuilding them
+        # would keep the GPU waiting for the host.
+        self._geo = geo
+        self._kview, self._vview = _lib.view4(self.k), _lib.view4(self.v)
+        self._dev_index = (self.device.index if self.device.index is not None
+                           else torch.cuda.current_device())
 
     def geometry(self, max_seq_len=None):
         return _lib.geometry(self.B, self.Hq, self.Hkv, self.D, self.bs,
@@ -139,13 +146,15 @@ class BatchedDecoder:
                 self.host_seq_lens = [s + n_new for s in self.host_seq_lens]
                 self.seq_lens.add_(n_new)
             kn, vn = _lib.view4(k_new), _lib.view4(v_new)
-        with torch.cuda.device(self.device):
-            _lib.check(_lib.lib().adakv_decode_step(
-                self.geometry(), self.params, _lib.view4(q), _lib.view4(self.k),
-                _lib.view4(self.v), kn, vn, n_new, self.centroid.data_ptr(),
-                self.seq_lens.data_ptr(), scale, self.block_table.data_ptr(), self.table_width,
-                self.sel_lens.data_ptr(), _lib.view4(out), self.workspace.data_ptr(),
-                self.ws_bytes, self._stream()))
+        args = (self._geo, self.params, _lib.view4(q), self._kview, self._vview, kn, vn, n_new,
+                self.centroid.data_ptr(), self.seq_lens.data_ptr(), scale,
+                self.block_table.data_ptr(), self.table_width, self.sel_lens.data_ptr(),
+                _lib.view4(out), self.workspace.data_ptr(), self.ws_bytes, self._stream())
+        if torch.cuda.current_device() == self._dev_index:
+            _lib.check(_lib.lib().adakv_decode_step(*args))
+        else:
+            with torch.cuda.device(self.device):
+                _lib.check(_lib.lib().adakv_decode_step(*args))
         return out
 
     def attend(self, q, block_table, sel_lens, sm_scale=None, out=None):
