@@ -46,7 +46,7 @@ KERNELS_PER_STEP = 3
 L2_FLUSH_BYTES = 256 << 20
 # DRAM bytes (read + write) of one decode step at each context, summed over the
 # three kernels of one ncu --set full capture (profiles/decode_step_128k_kernels.md)
-NCU_STEP_TRAFFIC = {131072: 33_661_696 + 2_189_824 + 8_763_136}
+NCU_STEP_TRAFFIC = {131072: 33_661_440 + 2_195_456 + 8_765_184}
 
 
 def workload_name(S):
