@@ -166,6 +166,18 @@ __global__ void __launch_bounds__(kEstThreads, 1) estimate_kernel(EstParams p) {
     kvh = r / seq_cph[b];
     ch = r - kvh * seq_cph[b];
   };
+  // the chunk after (b, kvh, ch) in the list (sequences without chunks skipped)
+  auto chunk_next = [&](int& b, int& kvh, int& ch) {
+    if (++ch == seq_cph[b]) {
+      ch = 0;
+      if (++kvh == p.Hkv) {
+        kvh = 0;
+        do {
+          ++b;
+        } while (b < p.B && seq_cph[b] == 0);
+      }
+    }
+  };
 
   if (warp == kEstConsumerWarps) {
     // ---------------- producer ----------------
@@ -201,12 +213,11 @@ __global__ void __launch_bounds__(kEstThreads, 1) estimate_kernel(EstParams p) {
       const int total = carry;
       const int c_begin = (int)((int64_t)total * blockIdx.x / gridDim.x);
       const int c_end = (int)((int64_t)total * (blockIdx.x + 1) / gridDim.x);
-      int i = 0;
-      for (int c = c_begin; c < c_end; ++c, ++i) {
-        int b, kvh, ch;
-        chunk_of(c, b, kvh, ch);
-        const int s = i % stages;
-        if (i >= stages && !mbar_wait_bounded(&empty_bar[s], ((i / stages) - 1) & 1)) {
+      int b = 0, kvh = 0, ch = 0;
+      if (c_begin < c_end) chunk_of(c_begin, b, kvh, ch);
+      int s = 0, ph = 0;  // ring slot of the chunk and its use count's parity
+      for (int c = c_begin, i = 0; c < c_end; ++c, ++i) {
+        if (i >= stages && !mbar_wait_bounded(&empty_bar[s], ph ^ 1)) {
           report(p.status, ADAKV_ST_WAIT_TIMEOUT);
           break;
         }
@@ -222,6 +233,11 @@ __global__ void __launch_bounds__(kEstThreads, 1) estimate_kernel(EstParams p) {
         for (int j = 0; j < p.g; ++j)
           bulk_g2s(reinterpret_cast<char*>(st + TILE_F) + j * qrow, qsrc + j * p.q.sh, qrow,
                    &full_bar[s]);
+        chunk_next(b, kvh, ch);
+        if (++s == stages) {
+          s = 0;
+          ph ^= 1;
+        }
       }
     }
     pdl_wait();
@@ -346,15 +362,14 @@ __global__ void __launch_bounds__(kEstThreads, 1) estimate_kernel(EstParams p) {
     const int c_end = (int)((int64_t)total * (blockIdx.x + 1) / gridDim.x);
     float qr[GP][E];  // the group's query slices, reloaded when the (sequence, KV head) changes
     int qrun = -1;
-    int i = 0;
-    for (int c = c_begin; c < c_end; ++c, ++i) {
-      const int s = i % stages;
-      if (!mbar_wait_bounded(&full_bar[s], (i / stages) & 1)) {
+    int b = 0, kvh = 0, ch = 0;
+    if (c_begin < c_end) chunk_of(c_begin, b, kvh, ch);
+    int s = 0, ph = 0;  // ring slot of the chunk and its use count's parity
+    for (int c = c_begin; c < c_end; ++c) {
+      if (!mbar_wait_bounded(&full_bar[s], ph)) {
         if (lane == 0) report(p.status, ADAKV_ST_WAIT_TIMEOUT);
         break;
       }
-      int b, kvh, ch;
-      chunk_of(c, b, kvh, ch);
       const int S = seq_len_of(p.seq_lens, b, p.max_seq_len);
       const int nb = ceil_div(S, p.bs);
       const int row0 = ch * kEstRows;
@@ -454,6 +469,11 @@ __global__ void __launch_bounds__(kEstThreads, 1) estimate_kernel(EstParams p) {
         if (lane < p.g)
           soft_store(p.stats + ((int64_t)(b * p.Hq + kvh * p.g + lane) * p.stats_stride +
                                 ch * kEstConsumerWarps + warp) * kStatF, part);
+      }
+      chunk_next(b, kvh, ch);
+      if (++s == stages) {
+        s = 0;
+        ph ^= 1;
       }
     }
     pdl_wait();  // (no-op for ordering here; keeps every thread's wait uniform)
