@@ -215,28 +215,66 @@ __global__ void __launch_bounds__(kEstThreads, 1) estimate_kernel(EstParams p) {
       const int c_end = (int)((int64_t)total * (blockIdx.x + 1) / gridDim.x);
       int b = 0, kvh = 0, ch = 0;
       if (c_begin < c_end) chunk_of(c_begin, b, kvh, ch);
-      int s = 0, ph = 0;  // ring slot of the chunk and its use count's parity
-      for (int c = c_begin, i = 0; c < c_end; ++c, ++i) {
-        if (i >= stages && !mbar_wait_bounded(&empty_bar[s], ph ^ 1)) {
-          report(p.status, ADAKV_ST_WAIT_TIMEOUT);
-          break;
+      if constexpr (GP >= 8) {
+        int s = 0, ph = 0;  // ring slot of the chunk and its use count's parity
+        int nb_b = -1, nb = 0;  // sequence whose block count is in nb
+        int run = -1;           // (sequence, KV head) whose queries the consumers hold
+        for (int c = c_begin, i = 0; c < c_end; ++c, ++i) {
+          if (i >= stages && !mbar_wait_bounded(&empty_bar[s], ph ^ 1)) {
+            report(p.status, ADAKV_ST_WAIT_TIMEOUT);
+            break;
+          }
+          if (b != nb_b) {
+            nb_b = b;
+            nb = ceil_div(seq_len_of(p.seq_lens, b, p.max_seq_len), p.bs);
+          }
+          const int row0 = ch * kEstRows;
+          const int nrows = imin(kEstRows, nb - row0);
+          float* st = ring + s * stage_f;
+          // the query rows travel with the first chunk of each run only (the
+          // consumers keep them in registers)
+          const bool with_q = b * p.Hkv + kvh != run;
+          run = b * p.Hkv + kvh;
+          mbar_arrive_expect_tx(&full_bar[s],
+                                (uint32_t)nrows * D * 4u + (with_q ? (uint32_t)(p.g * qrow) : 0u));
+          bulk_g2s(st, p.cent + ((int64_t)(b * p.Hkv + kvh) * p.nb_cap + row0) * D,
+                   (uint32_t)nrows * D * 4u, &full_bar[s]);
+          if (with_q) {
+            const T* qsrc = static_cast<const T*>(p.q.data) + b * p.q.sb + (int64_t)kvh * p.g * p.q.sh;
+            for (int j = 0; j < p.g; ++j)
+              bulk_g2s(reinterpret_cast<char*>(st + TILE_F) + j * qrow, qsrc + j * p.q.sh, qrow,
+                       &full_bar[s]);
+          }
+          chunk_next(b, kvh, ch);
+          if (++s == stages) {
+            s = 0;
+            ph ^= 1;
+          }
         }
-        const int S = seq_len_of(p.seq_lens, b, p.max_seq_len);
-        const int nb = ceil_div(S, p.bs);
-        const int row0 = ch * kEstRows;
-        const int nrows = imin(kEstRows, nb - row0);
-        float* st = ring + s * stage_f;
-        mbar_arrive_expect_tx(&full_bar[s], (uint32_t)nrows * D * 4u + (uint32_t)(p.g * qrow));
-        bulk_g2s(st, p.cent + ((int64_t)(b * p.Hkv + kvh) * p.nb_cap + row0) * D,
-                 (uint32_t)nrows * D * 4u, &full_bar[s]);
-        const T* qsrc = static_cast<const T*>(p.q.data) + b * p.q.sb + (int64_t)kvh * p.g * p.q.sh;
-        for (int j = 0; j < p.g; ++j)
-          bulk_g2s(reinterpret_cast<char*>(st + TILE_F) + j * qrow, qsrc + j * p.q.sh, qrow,
-                   &full_bar[s]);
-        chunk_next(b, kvh, ch);
-        if (++s == stages) {
-          s = 0;
-          ph ^= 1;
+      } else {  // groups of 4: q rows in every stage (measured faster there)
+        int s = 0, ph = 0;  // ring slot of the chunk and its use count's parity
+        for (int c = c_begin, i = 0; c < c_end; ++c, ++i) {
+          if (i >= stages && !mbar_wait_bounded(&empty_bar[s], ph ^ 1)) {
+            report(p.status, ADAKV_ST_WAIT_TIMEOUT);
+            break;
+          }
+          const int S = seq_len_of(p.seq_lens, b, p.max_seq_len);
+          const int nb = ceil_div(S, p.bs);
+          const int row0 = ch * kEstRows;
+          const int nrows = imin(kEstRows, nb - row0);
+          float* st = ring + s * stage_f;
+          mbar_arrive_expect_tx(&full_bar[s], (uint32_t)nrows * D * 4u + (uint32_t)(p.g * qrow));
+          bulk_g2s(st, p.cent + ((int64_t)(b * p.Hkv + kvh) * p.nb_cap + row0) * D,
+                   (uint32_t)nrows * D * 4u, &full_bar[s]);
+          const T* qsrc = static_cast<const T*>(p.q.data) + b * p.q.sb + (int64_t)kvh * p.g * p.q.sh;
+          for (int j = 0; j < p.g; ++j)
+            bulk_g2s(reinterpret_cast<char*>(st + TILE_F) + j * qrow, qsrc + j * p.q.sh, qrow,
+                     &full_bar[s]);
+          chunk_next(b, kvh, ch);
+          if (++s == stages) {
+            s = 0;
+            ph ^= 1;
+          }
         }
       }
     }
@@ -360,7 +398,7 @@ __global__ void __launch_bounds__(kEstThreads, 1) estimate_kernel(EstParams p) {
     const int total = seq_base[p.B];
     const int c_begin = (int)((int64_t)total * blockIdx.x / gridDim.x);
     const int c_end = (int)((int64_t)total * (blockIdx.x + 1) / gridDim.x);
-    float qr[GP][E];  // the group's query slices, reloaded when the (sequence, KV head) changes
+    float qr[GP][E];  // the group's query slices, loaded when the (sequence, KV head) changes
     int qrun = -1;
     int b = 0, kvh = 0, ch = 0;
     if (c_begin < c_end) chunk_of(c_begin, b, kvh, ch);
@@ -378,7 +416,7 @@ __global__ void __launch_bounds__(kEstThreads, 1) estimate_kernel(EstParams p) {
       const int skip_from = appending ? (S - p.n_new) / p.bs - row0 : nrows;
       const int lim = imin(nrows, skip_from);
       const float* tile = ring + s * stage_f;
-      // (groups of 4 heads reload every chunk: measured faster there)
+      // groups of 8+ heads: only the first chunk of a run carries q (producer)
       if (GP < 8 || b * p.Hkv + kvh != qrun) {
         qrun = b * p.Hkv + kvh;
         const T* qs = reinterpret_cast<const T*>(tile + TILE_F);
