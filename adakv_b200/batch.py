@@ -157,6 +157,20 @@ class BatchedDecoder:
                 _lib.check(_lib.lib().adakv_decode_step(*args))
         return out
 
+    def graphed(self, n_new=1, advance=True, sm_scale=None):
+        """One decode step captured in a CUDA graph over decoder-owned buffers.
+
+        Returns a :class:`GraphedStep`: write the step's query into ``.q``
+        (``[B, Hq, D]``) and its ``n_new`` new tokens into ``.k_new`` /
+        ``.v_new`` (``[B, Hkv, n_new, D]``) -- all three are views of one
+        device buffer, ``.inputs``, so a host staging row can fill them with
+        one copy -- then call it; the output is ``.out``.  A replay launches
+        the step's three kernels from one graph instead of three host calls,
+        which keeps the GPU from waiting on the host between decode steps.
+        One step without append runs first (device set-up that cannot be
+        captured); it writes only the plan outputs and ``.out``."""
+        return GraphedStep(self, n_new, advance, sm_scale)
+
     def attend(self, q, block_table, sel_lens, sm_scale=None, out=None):
         """Attention over a caller-given table (``adakv_attend``)."""
         from .kernels.block_sparse_decode import block_sparse_decode_batched
@@ -173,3 +187,38 @@ class BatchedDecoder:
         bt = self.block_table.cpu().numpy()
         sl = self.sel_lens.cpu().numpy()
         return [bt[r, : sl[r]] for r in range(bt.shape[0])]
+
+
+class GraphedStep:
+    """A decode step of a :class:`BatchedDecoder` replayed from a CUDA graph
+    (see :meth:`BatchedDecoder.graphed`)."""
+
+    def __init__(self, dec, n_new, advance, sm_scale):
+        self.dec, self.n_new, self.advance = dec, int(n_new), bool(advance)
+        B, Hq, Hkv, D = dec.B, dec.Hq, dec.Hkv, dec.D
+        nq, nk = B * Hq * D, B * Hkv * self.n_new * D
+        self.inputs = torch.zeros(nq + 2 * nk, dtype=dec.dtype, device=dec.device)
+        self.q = self.inputs[:nq].view(B, Hq, D)
+        self.k_new = self.inputs[nq:nq + nk].view(B, Hkv, self.n_new, D)
+        self.v_new = self.inputs[nq + nk:].view(B, Hkv, self.n_new, D)
+        self.out = dec.out
+        with torch.cuda.device(dec.device):
+            dec.step(self.q, sm_scale=sm_scale)  # set-up outside the capture (no append)
+            self.graph = torch.cuda.CUDAGraph()
+            host_lens = list(dec.host_seq_lens)
+            with torch.cuda.graph(self.graph):
+                dec.step(self.q, sm_scale=sm_scale, k_new=self.k_new, v_new=self.v_new,
+                         advance=self.advance)
+            # capture records the step (its length increment included) without
+            # running it: the host copy of the lengths moves on replay only
+            dec.host_seq_lens = host_lens
+
+    def __call__(self):
+        """Replay the step on the current stream; returns ``.out``."""
+        dec = self.dec
+        if self.advance:
+            if max(dec.host_seq_lens) + self.n_new > dec.capacity:
+                raise ValueError("cache capacity exceeded")
+            dec.host_seq_lens = [s + self.n_new for s in dec.host_seq_lens]
+        self.graph.replay()
+        return self.out
