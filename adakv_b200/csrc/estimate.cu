@@ -403,12 +403,16 @@ __global__ void __launch_bounds__(kEstThreads, 1) estimate_kernel(EstParams p) {
     int b = 0, kvh = 0, ch = 0;
     if (c_begin < c_end) chunk_of(c_begin, b, kvh, ch);
     int s = 0, ph = 0;  // ring slot of the chunk and its use count's parity
+    int S_b = -1, S = 0;
     for (int c = c_begin; c < c_end; ++c) {
+      if (b != S_b) {  // the sequence's length, read once per sequence
+        S_b = b;
+        S = seq_len_of(p.seq_lens, b, p.max_seq_len);
+      }
       if (!mbar_wait_bounded(&full_bar[s], ph)) {
         if (lane == 0) report(p.status, ADAKV_ST_WAIT_TIMEOUT);
         break;
       }
-      const int S = seq_len_of(p.seq_lens, b, p.max_seq_len);
       const int nb = ceil_div(S, p.bs);
       const int row0 = ch * kEstRows;
       const int nrows = imin(kEstRows, nb - row0);
