@@ -202,6 +202,9 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanParams p) {
   // sequence lengths are inputs of the whole step (the estimator never writes
   // them): read before waiting for it
   const int S_first = slot_seq < p.B ? seq_len_of(p.seq_lens, slot_seq, p.max_seq_len) : 0;
+  // log(nb) of the entropy weight, off the exchange's critical path
+  const double lognb_first =
+      log((double)imax(ceil_div((S_first < 0 || S_first > p.max_seq_len) ? 0 : S_first, p.bs), 2));
   pdl_wait();
 
   for (int b0 = 0; b0 < p.B; b0 += p.seqs_per_round) {
@@ -211,6 +214,7 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanParams p) {
     int S = b0 == 0 ? S_first : seq_len_of(p.seq_lens, b, p.max_seq_len);
     if (S < 0 || S > p.max_seq_len) S = 0;  // reported by the estimator
     const int nb = ceil_div(S, p.bs);
+    const double lognb = b0 == 0 ? lognb_first : log((double)imax(nb, 2));
     const int L = (ceil_div(nb, C) + 31) / 32 * 32;
     const int lo = imin(nb, rank * L), hi = imin(nb, lo + L);
     const int n = hi - lo;
@@ -740,7 +744,7 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanParams p) {
     auto weight_of = [&](double e) -> double {
       // entropy: adakv/budget.py:36-37, float64 after the division; nucleus:
       // the published count + 1 (budget.py:41)
-      return nucleus ? e : (double)(float)e / log((double)imax(nb, 2)) + 1e-6;
+      return nucleus ? e : (double)(float)e / lognb + 1e-6;
     };
 
     // ---- exchange across the sequence's heads (warp 0) / merge histograms ----
