@@ -85,7 +85,14 @@ _SIGNATURES = {
     "adakv_attend_noalloc": (ctypes.c_int, [_P(Geometry), _P(View), _P(View), _P(View), _vp,
                                             ctypes.c_int32, _vp, _vp, ctypes.c_float, _P(View),
                                             _vp, _vp]),
+    "adakv_set_status_sink": (ctypes.c_int, [_vp, _vp, _vp]),
+    "adakv_read_scores": (ctypes.c_int, [_P(Geometry), _vp, ctypes.c_size_t, _vp, ctypes.c_int32,
+                                         _vp]),
+    "adakv_debug_knob": (ctypes.c_int, [ctypes.c_int32, ctypes.c_int64]),
+    "adakv_last_path": (ctypes.c_int, [_vp]),
 }
+
+KNOB_WAIT_NS, KNOB_FLAGS, KNOB_STEP_PATH = 1, 2, 3
 
 _lib = None
 _lock = threading.Lock()
@@ -167,10 +174,58 @@ def geometry(batch, n_q_heads, n_kv_heads, head_dim, block_size, max_seq_len, nb
 
 
 # ---------------------------------------------------------------------------
+# device status surfaced on the host without synchronising
+# ---------------------------------------------------------------------------
+class StatusSink:
+    """A page-locked host word the kernels of one workspace write their
+    ``ADAKV_ST_*`` bits to (``adakv_set_status_sink``).  :meth:`raise_if_set`
+    is a plain host read: a failed step (a bounded device wait that ran out,
+    a bad block id or sequence length) raises on the next call that checks,
+    without a device synchronisation on the decode path."""
+
+    def __init__(self, ws: torch.Tensor):
+        self.word = torch.zeros(1, dtype=torch.int32).pin_memory()
+        self._view = self.word.numpy()
+        with torch.cuda.device(ws.device):
+            rc = lib().adakv_set_status_sink(ws.data_ptr(), self.word.data_ptr(),
+                                             stream_ptr(ws.device))
+        self.ok = rc == OK
+        if not self.ok:
+            raise RuntimeError("adakv_set_status_sink failed: "
+                               + lib().adakv_last_error().decode(errors="replace"))
+
+    def bits(self) -> int:
+        return int(self._view[0])
+
+    def clear(self) -> None:
+        self._view[0] = 0
+
+    def raise_if_set(self) -> None:
+        bits = self.bits()
+        if bits:
+            raise RuntimeError(describe_status(bits))
+
+
+def describe_status(bits: int) -> str:
+    names = []
+    if bits & ST_WAIT_TIMEOUT:
+        names.append("a bounded device wait timed out (results of that call are not valid)")
+    if bits & ST_BAD_BLOCK_ID:
+        names.append("a block table entry was outside [0, n_blocks)")
+    if bits & ST_BAD_SEL_LEN:
+        names.append("a sel_lens entry exceeded the table width")
+    if bits & ST_BAD_SEQ_LEN:
+        names.append("a sequence length was outside [1, max_seq_len]")
+    return f"adakv device status 0x{bits:x}: " + "; ".join(names or ["unknown bits"])
+
+
+# ---------------------------------------------------------------------------
 # workspace: one zero-initialised device buffer per (device, stream, kind),
-# grown on demand.  Calls that share one are ordered by their stream.
+# grown on demand, each with its status sink.  Calls that share one are
+# ordered by their stream.
 # ---------------------------------------------------------------------------
 _workspaces: dict = {}
+_sinks: dict = {}
 
 
 def workspace(nbytes: int, device, kind: str = "plan") -> torch.Tensor:
@@ -180,11 +235,31 @@ def workspace(nbytes: int, device, kind: str = "plan") -> torch.Tensor:
     if ws is None or ws.numel() < nbytes:
         ws = torch.zeros(max(int(nbytes), 256), dtype=torch.uint8, device=device)
         _workspaces[key] = ws
+        _sinks[ws.data_ptr()] = StatusSink(ws)
     return ws
+
+
+def sink_of(ws: torch.Tensor):
+    return _sinks.get(ws.data_ptr())
+
+
+def raise_if_failed(ws: torch.Tensor) -> None:
+    """Raise if a kernel that used ``ws`` reported a status bit (host read, no sync)."""
+    s = _sinks.get(ws.data_ptr())
+    if s is not None:
+        s.raise_if_set()
 
 
 def read_status(ws: torch.Tensor) -> int:
     """Synchronise and return (and clear) the device status bits of a workspace."""
     out = ctypes.c_uint32(0)
     check(lib().adakv_read_status(ws.data_ptr(), ctypes.byref(out), stream_ptr(ws.device)))
+    s = _sinks.get(ws.data_ptr())
+    if s is not None:
+        s.clear()
     return int(out.value)
+
+
+def debug_knob(knob: int, value: int) -> None:
+    """Test-only process-wide knobs (``adakv_debug_knob``); 0 restores the default."""
+    check(lib().adakv_debug_knob(int(knob), int(value)))

@@ -260,12 +260,22 @@ def plan_selection(
     budget_policy: str = "adaptive",
     c_min: int = 1,
     nucleus_p: float = 0.9,
+    order: str = "score",
 ):
     """Score blocks, allocate per-head budgets, select blocks (reference signature).
 
-    Returns ``(block_table [Hq, W] int32, sel_lens [Hq] int32)``; row ``h`` lists
-    its ``sel_lens[h]`` blocks in ascending order, entries past that are unspecified.
+    Returns ``(block_table [Hq, max_sel] int32, sel_lens [Hq] int32)`` in the
+    reference's format (``adakv/attention.py:229-244``): row ``h`` lists its
+    ``sel_lens[h]`` blocks in descending order of the sink/local-biased score
+    (forced blocks first, in ascending block order; score ties by ascending
+    block index), and ``max_sel = sel_lens.max()`` is read back to the host as
+    the reference does (``attention.py:242``); entries past ``sel_lens[h]`` are
+    unspecified.  ``order="ascending"`` skips the reordering and the host read:
+    rows are then in ascending block order and the width is the largest count
+    the knobs allow (the C ABI's ``adakv_plan`` layout).
     """
+    if order not in ("score", "ascending"):
+        raise ValueError(f"unknown order: {order!r}")
     geo, sp = _plan_args(q, cache, avg_budget, k_min, k_max, n_sink_blocks, n_local_blocks,
                          temperature, estimator, budget_policy, c_min, nucleus_p)
     L = _lib.lib()
@@ -290,11 +300,37 @@ def plan_selection(
                                       block_table.data_ptr(), width, sel_lens.data_ptr(),
                                       ws.data_ptr(), ws.numel(), _lib.stream_ptr(q.device)))
         else:
+            scores = None
+            if order == "score":
+                scores = torch.empty((Hq, cache._cbuf.shape[1]), dtype=torch.float32,
+                                     device=q.device)
             _lib.check(L.adakv_plan(geo, sp, _lib.view4(q.unsqueeze(0)), cache._cbuf.data_ptr(),
-                                    None, block_table.data_ptr(), width, sel_lens.data_ptr(), None,
+                                    None, block_table.data_ptr(), width, sel_lens.data_ptr(),
+                                    scores.data_ptr() if scores is not None else None,
                                     ws.data_ptr(), ws.numel(), _lib.stream_ptr(q.device)))
+        _lib.raise_if_failed(ws)
+        if order == "score":
+            block_table = _score_order(block_table, sel_lens, scores, cache.n_blocks,
+                                       n_sink_blocks, n_local_blocks)
     record_selection(block_table, sel_lens, cache.n_blocks)
     return block_table, sel_lens
+
+
+def _score_order(block_table, sel_lens, scores, nb, n_sink_blocks, n_local_blocks):
+    """Rows of ascending block ids -> the reference's order (``attention.py:229-234``:
+    ``+inf`` on sink / local blocks, descending sort), width ``sel_lens.max()``."""
+    max_sel = max(int(sel_lens.max().item()), 1)  # host read, as attention.py:242
+    ids = block_table[:, :max_sel].long()
+    valid = torch.arange(max_sel, device=ids.device)[None, :] < sel_lens[:, None]
+    ids = torch.where(valid, ids, torch.zeros_like(ids))
+    key = torch.gather(scores[:, :max(nb, 1)], 1, ids.clamp_max(max(nb, 1) - 1)).double()
+    sink, local = min(n_sink_blocks, nb), min(n_local_blocks, nb)
+    forced = (ids < sink) | (ids >= nb - local)
+    key = torch.where(forced, torch.full_like(key, float("inf")), key)
+    key = torch.where(valid, key, torch.full_like(key, float("-inf")))
+    # rows are ascending, so a stable descending sort breaks ties by ascending block id
+    perm = torch.sort(key, dim=1, descending=True, stable=True).indices
+    return torch.gather(block_table[:, :max_sel], 1, perm).contiguous()
 
 
 def adakv_decode_attention(
@@ -334,6 +370,7 @@ def _decode(q, cache, avg_budget, k_min, k_max, n_sink_blocks, n_local_blocks, t
             float(sm_scale),
             block_table.data_ptr(), width, sel_lens.data_ptr(), _lib.view4(out.unsqueeze(0)),
             ws.data_ptr(), ws.numel(), _lib.stream_ptr(q.device)))
+    _lib.raise_if_failed(ws)
     if tracing_enabled():
         record_selection(block_table, sel_lens, cache.n_blocks)
     return out

@@ -66,6 +66,9 @@ class BatchedDecoder:
         self.sel_lens = torch.zeros((batch * n_q_heads,), dtype=torch.int32, device=device)
         self.ws_bytes = L.adakv_plan_workspace_bytes(geo, self.params)
         self.workspace = torch.zeros((self.ws_bytes,), dtype=torch.uint8, device=device)
+        # kernels write their ADAKV_ST_* bits to this host word too: a failed
+        # step raises on the next call without a device synchronisation
+        self.sink = _lib.StatusSink(self.workspace)
         self.out = torch.zeros((batch, n_q_heads, head_dim), dtype=dtype, device=device)
         # The per-step C-ABI arguments that never change, built once: a decode
         # step is short enough (tens of microseconds) that rebuilding them
@@ -146,6 +149,7 @@ class BatchedDecoder:
                 self.host_seq_lens = [s + n_new for s in self.host_seq_lens]
                 self.seq_lens.add_(n_new)
             kn, vn = _lib.view4(k_new), _lib.view4(v_new)
+        self.sink.raise_if_set()
         args = (self._geo, self.params, _lib.view4(q), self._kview, self._vview, kn, vn, n_new,
                 self.centroid.data_ptr(), self.seq_lens.data_ptr(), scale,
                 self.block_table.data_ptr(), self.table_width, self.sel_lens.data_ptr(),
@@ -180,7 +184,24 @@ class BatchedDecoder:
 
     def status(self) -> int:
         """Synchronise; return and clear the device status bits (ADAKV_ST_*)."""
-        return _lib.read_status(self.workspace)
+        bits = _lib.read_status(self.workspace)
+        self.sink.clear()
+        return bits
+
+    def last_path(self) -> int:
+        """2 if the last step ran as the one-kernel step, 1 as the kernel chain."""
+        return int(_lib.lib().adakv_last_path(self.workspace.data_ptr()))
+
+    def scores(self, out=None):
+        """Block scores ``[B, Hq, nb]`` (float32, q . centroid) of the last step / plan."""
+        nb = self.nb_cap
+        out = torch.empty((self.B, self.Hq, nb), dtype=torch.float32, device=self.device) \
+            if out is None else out
+        with torch.cuda.device(self.device):
+            _lib.check(_lib.lib().adakv_read_scores(self._geo, self.workspace.data_ptr(),
+                                                    self.ws_bytes, out.data_ptr(), out.stride(1),
+                                                    self._stream()))
+        return out
 
     def selected_sets(self):
         """Host copy of the selection: list over rows (b*Hq + h) of block-id arrays."""
@@ -216,6 +237,7 @@ class GraphedStep:
     def __call__(self):
         """Replay the step on the current stream; returns ``.out``."""
         dec = self.dec
+        dec.sink.raise_if_set()
         if self.advance:
             if max(dec.host_seq_lens) + self.n_new > dec.capacity:
                 raise ValueError("cache capacity exceeded")

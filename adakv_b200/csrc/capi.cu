@@ -11,7 +11,9 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <atomic>
 #include <map>
+#include <unordered_map>
 #include <mutex>
 #include <tuple>
 #include <string>
@@ -48,8 +50,19 @@ int fail(int code, const char* fmt, ...) {
 struct DeviceState {
   bool ready = false;
   int num_sms = 0;
+  bool step_ok = false;                            // the one-kernel step can run one CTA per SM
   std::map<int, int> plan_ctas;                    // nb_max * 16 + cluster -> resident plan clusters
 };
+
+// Test-only knobs (adakv_debug_knob), all off by default.
+std::atomic<int64_t> g_dbg_wait_ns{0};   // bound of device waits in ns (0: kWaitLimitNs)
+std::atomic<int> g_dbg_flags{0};         // bit 0: head 0 never publishes its entropy
+std::atomic<int> g_dbg_path{0};          // decode step: 0 automatic, 1 three kernels, 2 one kernel
+
+uint64_t wait_limit_ns() {
+  const int64_t v = g_dbg_wait_ns.load();
+  return v > 0 ? (uint64_t)v : kWaitLimitNs;
+}
 constexpr int kMaxDevices = 64;
 DeviceState g_dev[kMaxDevices];
 std::mutex g_dev_mu;
@@ -73,6 +86,8 @@ int device_state(DeviceState** out) {
     CUDA_TRY(estimate_kernels_init());
     CUDA_TRY(plan_kernels_init());
     CUDA_TRY(attend_kernels_init());
+    CUDA_TRY(step_kernels_init());
+    s.step_ok = s.num_sms >= 1;
     s.ready = true;
   }
   *out = &s;
@@ -93,6 +108,10 @@ int check_geometry(const adakv_geometry* g) {
   if (g->n_q_heads % g->n_kv_heads)
     return fail(ADAKV_ERR_INVALID, "n_q_heads must be a multiple of n_kv_heads (Hq=%d Hkv=%d)",
                 g->n_q_heads, g->n_kv_heads);
+  if (g->n_q_heads > 128)
+    return fail(ADAKV_ERR_UNSUPPORTED,
+                "n_q_heads %d > 128 (the per-sequence entropy exchange covers at most 128 heads)",
+                g->n_q_heads);
   if (g->n_q_heads / g->n_kv_heads > 16)
     return fail(ADAKV_ERR_UNSUPPORTED, "GQA group size %d > 16", g->n_q_heads / g->n_kv_heads);
   if (g->head_dim != 64 && g->head_dim != 128)
@@ -186,7 +205,19 @@ int attend_split(const adakv_geometry* g) {
 struct WsLayout {
   size_t status, epoch, slots, scores, stats, bitmap, part, counters, bytes;
   int score_stride, stats_stride, bm_words, split;
+  // one-kernel step (present when the geometry can take it)
+  bool fused;
+  size_t fepoch, fscores, fhslot, fbitmap, fpart;
+  int fs_stride, fb_stride;
 };
+
+// Geometries the one-kernel step is built for (policy and grid are checked at launch).
+bool step_geometry_ok(const adakv_geometry* g) {
+  const int gq = g->n_q_heads / g->n_kv_heads;
+  const int nb_max = ceil_div(g->max_seq_len, g->block_size);
+  return step_kernel_built(g->dtype, g->head_dim, g->block_size, gq) && g->batch <= kStepMaxBatch &&
+         (int64_t)g->batch * g->n_q_heads <= kStepMaxHeads && nb_max <= kStepMaxBlocks;
+}
 
 WsLayout make_ws(const adakv_geometry* g, bool with_plan) {
   WsLayout L{};
@@ -206,6 +237,16 @@ WsLayout make_ws(const adakv_geometry* g, bool with_plan) {
   L.bitmap = take(sizeof(uint32_t) * (size_t)rows * L.bm_words);
   L.part = take(sizeof(float) * (size_t)g->batch * g->n_kv_heads * L.split * gq * (g->head_dim + 2));
   L.counters = take(sizeof(uint32_t) * (size_t)g->batch * g->n_kv_heads);
+  L.fused = with_plan && step_geometry_ok(g);
+  if (L.fused) {
+    L.fs_stride = (int)align_up((size_t)g->nb_cap, 4);
+    L.fb_stride = (int)align_up((size_t)L.bm_words, 2);
+    L.fepoch = take(16);
+    L.fscores = take(8 * (size_t)rows * L.fs_stride);
+    L.fhslot = take(8 * (size_t)rows);
+    L.fbitmap = take(8 * (size_t)rows * L.fb_stride);
+    L.fpart = take(8 * (size_t)kStepMaxGrid * gq * (g->head_dim + 2));
+  }
   L.bytes = o;
   return L;
 }
@@ -251,6 +292,8 @@ int enqueue_select(const DeviceState* ds, const adakv_geometry* g, const adakv_s
   pp.bitmap = ws_at<uint32_t>(ws, L.bitmap);
   pp.bm_words = L.bm_words;
   pp.status = ws_at<uint32_t>(ws, L.status);
+  pp.wait_ns = wait_limit_ns();
+  pp.debug_flags = g_dbg_flags.load();
   // Cluster size: the largest C in {8, 4, 2} whose slices keep >= 1024 blocks,
   // with all B * Hq * C CTAs resident at once and at most one per SM (one
   // round); else C = 1 with as many sequences per round as are resident.
@@ -388,6 +431,89 @@ int enqueue_attend(const DeviceState* ds, const adakv_geometry* g, const adakv_v
   LaunchOpts oa;
   oa.pdl = pdl_enabled();
   CUDA_TRY(launch_attend(ap, g->dtype, g->head_dim, g->block_size, split, st, oa));
+  return ADAKV_OK;
+}
+
+// Which decode-step path last wrote a workspace's scores (adakv_read_scores).
+std::unordered_map<const void*, bool> g_last_fused;
+
+void note_path(const void* ws, bool fused) {
+  std::lock_guard<std::mutex> lock(g_dev_mu);
+  g_last_fused[ws] = fused;
+}
+
+// The one-kernel step for this call, or why not (the three-kernel chain then runs).
+bool step_applies(const DeviceState* ds, const adakv_geometry* g, const adakv_select_params* sp,
+                  const WsLayout& L, int* grid_out) {
+  const int path = g_dbg_path.load();
+  if (path == 1 || !L.fused || !ds->step_ok) return false;
+  static const bool env_off = [] {
+    const char* e = getenv("ADAKV_FUSED");
+    return e && e[0] == '0';
+  }();
+  if (env_off && path != 2) return false;
+  if (sp->policy == ADAKV_POLICY_NUCLEUS) return false;
+  const int grid = std::min(ds->num_sms, kStepMaxGrid);
+  const int heads = g->batch * g->n_q_heads, groups = g->batch * g->n_kv_heads;
+  if (grid < heads || grid < groups) return false;
+  // ring stages of one CTA: its rows in 64-row stages plus one per (sequence, KV head) it crosses
+  const int64_t rows = (int64_t)groups * ceil_div(g->max_seq_len, g->block_size);
+  const int64_t per = (rows + grid - 1) / grid;
+  if ((per + kStepRows - 1) / kStepRows + std::min<int64_t>(groups, per) + 1 > kStepMaxDesc) return false;
+  *grid_out = grid;
+  return true;
+}
+
+int enqueue_step(const adakv_geometry* g, const adakv_select_params* sp, const adakv_view* q,
+                 const adakv_view* k, const adakv_view* v, const adakv_view* k_new,
+                 const adakv_view* v_new, int n_new, float* centroid, const int32_t* seq_lens,
+                 float sm_scale, int32_t* block_table, int32_t table_width, int32_t* sel_lens,
+                 const adakv_view* out, void* ws, const WsLayout& L, int grid, cudaStream_t st) {
+  const int gq = g->n_q_heads / g->n_kv_heads;
+  const int nb_max = ceil_div(g->max_seq_len, g->block_size);
+  StepParams p{};
+  p.q = to_view(q);
+  p.k = to_view(k);
+  p.v = to_view(v);
+  p.out = to_view(out);
+  if (n_new > 0) {
+    p.k_new = to_view(k_new);
+    p.v_new = to_view(v_new);
+  }
+  p.cent = centroid;
+  p.nb_cap = g->nb_cap;
+  p.seq_lens = seq_lens;
+  p.max_seq_len = g->max_seq_len;
+  p.B = g->batch;
+  p.Hq = g->n_q_heads;
+  p.Hkv = g->n_kv_heads;
+  p.bs = g->block_size;
+  p.n_new = n_new;
+  p.cfg = to_cfg(sp);
+  p.sm_scale = sm_scale;
+  p.block_table = block_table;
+  p.table_width = table_width;
+  p.sel_lens = sel_lens;
+  p.lse = nullptr;
+  p.status = ws_at<uint32_t>(ws, L.status);
+  p.epoch = ws_at<uint32_t>(ws, L.fepoch);
+  p.scores = ws_at<unsigned long long>(ws, L.fscores);
+  p.fs_stride = L.fs_stride;
+  p.hslot = ws_at<unsigned long long>(ws, L.fhslot);
+  p.bitmap = ws_at<unsigned long long>(ws, L.fbitmap);
+  p.fb_stride = L.fb_stride;
+  p.part = ws_at<unsigned long long>(ws, L.fpart);
+  p.nb_max = nb_max;
+  p.wait_ns = wait_limit_ns();
+  p.debug_flags = g_dbg_flags.load();
+  const int min_split = grid / (g->batch * g->n_kv_heads);
+  const size_t smem = step_smem_bytes(g->head_dim, gq, nb_max, min_split, &p.nbt, &p.slice_cap);
+  if (smem > kStepSmemMax)
+    return fail(ADAKV_ERR_UNSUPPORTED, "sequence too long for the one-kernel step");
+  LaunchOpts o;
+  o.pdl = pdl_enabled();
+  CUDA_TRY(launch_step(p, g->dtype, g->head_dim, gq, grid, smem, st, o));
+  note_path(ws, true);
   return ADAKV_OK;
 }
 
@@ -530,6 +656,7 @@ int adakv_plan(const adakv_geometry* geo, const adakv_select_params* sp, const a
   if ((rc = enqueue_plan(ds, geo, sp, q, const_cast<float*>(centroid), seq_lens, nullptr, nullptr,
                          nullptr, nullptr, 0, block_table, table_width, sel_lens, workspace, L, st)))
     return rc;
+  note_path(workspace, false);
   if (scores_out) {
     CUDA_TRY(cudaMemcpy2DAsync(scores_out, sizeof(float) * geo->nb_cap,
                                ws_at<float>(workspace, L.scores), sizeof(float) * L.score_stride,
@@ -603,10 +730,81 @@ int adakv_decode_step(const adakv_geometry* geo, const adakv_select_params* sp,
   DeviceState* ds = nullptr;
   if ((rc = device_state(&ds))) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int grid = 0;
+  if (step_applies(ds, geo, sp, L, &grid))
+    return enqueue_step(geo, sp, q, k, v, k_new, v_new, n_new, centroid, seq_lens, sm_scale,
+                        block_table, table_width, sel_lens, out, workspace, L, grid, st);
   if ((rc = enqueue_plan(ds, geo, sp, q, centroid, seq_lens, k, v, k_new, v_new, n_new,
                          block_table, table_width, sel_lens, workspace, L, st)))
     return rc;
+  note_path(workspace, false);
   return enqueue_attend(ds, geo, q, k, v, out, seq_lens, sm_scale, workspace, L, st);
+}
+
+int adakv_read_scores(const adakv_geometry* geo, void* workspace, size_t workspace_bytes,
+                      float* scores_out, int32_t score_stride, void* stream) {
+  int rc;
+  if ((rc = check_geometry(geo))) return rc;
+  const WsLayout L = make_ws(geo, true);
+  if ((rc = check_workspace(workspace, workspace_bytes, L.bytes))) return rc;
+  if (!scores_out) return fail(ADAKV_ERR_INVALID, "scores_out is NULL");
+  const int nb_max = ceil_div(geo->max_seq_len, geo->block_size);
+  if (score_stride < nb_max)
+    return fail(ADAKV_ERR_INVALID, "score_stride %d < blocks of max_seq_len (%d)", score_stride, nb_max);
+  bool fused = false;
+  {
+    std::lock_guard<std::mutex> lock(g_dev_mu);
+    auto it = g_last_fused.find(workspace);
+    if (it == g_last_fused.end())
+      return fail(ADAKV_ERR_INVALID, "no decode step or plan has run on this workspace");
+    fused = it->second;
+  }
+  CUDA_TRY(launch_step_scores(fused, ws_at<unsigned long long>(workspace, L.fscores), L.fs_stride,
+                              ws_at<float>(workspace, L.scores), L.score_stride,
+                              geo->batch * geo->n_q_heads, nb_max, scores_out, score_stride,
+                              static_cast<cudaStream_t>(stream)));
+  return ADAKV_OK;
+}
+
+int adakv_last_path(const void* workspace) {
+  std::lock_guard<std::mutex> lock(g_dev_mu);
+  auto it = g_last_fused.find(workspace);
+  if (it == g_last_fused.end()) return 0;
+  return it->second ? 2 : 1;
+}
+
+int adakv_set_status_sink(void* workspace, uint32_t* host_word, void* stream) {
+  if (!workspace) return fail(ADAKV_ERR_INVALID, "workspace is NULL");
+  void* dev = nullptr;
+  if (host_word) {
+    const cudaError_t e = cudaHostGetDevicePointer(&dev, host_word, 0);
+    if (e != cudaSuccess)
+      return fail(ADAKV_ERR_INVALID, "host_word is not mapped page-locked memory: %s",
+                  cudaGetErrorString(e));
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  CUDA_TRY(cudaMemcpyAsync(static_cast<char*>(workspace) + 8, &dev, sizeof(dev),
+                           cudaMemcpyHostToDevice, st));
+  CUDA_TRY(cudaStreamSynchronize(st));
+  return ADAKV_OK;
+}
+
+int adakv_debug_knob(int32_t knob, int64_t value) {
+  switch (knob) {
+    case ADAKV_KNOB_WAIT_NS:
+      if (value < 0) return fail(ADAKV_ERR_INVALID, "wait limit must be >= 0 ns");
+      g_dbg_wait_ns.store(value);
+      return ADAKV_OK;
+    case ADAKV_KNOB_FLAGS:
+      g_dbg_flags.store((int)value);
+      return ADAKV_OK;
+    case ADAKV_KNOB_STEP_PATH:
+      if (value < 0 || value > 2) return fail(ADAKV_ERR_INVALID, "step path must be 0, 1 or 2");
+      g_dbg_path.store((int)value);
+      return ADAKV_OK;
+    default:
+      return fail(ADAKV_ERR_INVALID, "unknown knob %d", knob);
+  }
 }
 
 int adakv_read_status(void* workspace, uint32_t* status, void* stream) {
@@ -628,10 +826,13 @@ int adakv_read_status(void* workspace, uint32_t* status, void* stream) {
 // ---------------------------------------------------------------------------
 namespace {
 
-// Largest scratch the entry point can use: the workspace layout of
-// adakv_attend, i.e. 512 bytes of header plus B * Hq * ceil(nb_cap / 32) * 4
-// bytes of bitmaps (B * Hq = 32 at nb_cap = 8192 takes 32 KiB; 4 MiB covers
-// e.g. B * Hq = 2048 rows at 128K tokens).
+// Largest scratch the entry point can use.  A call needs exactly
+// adakv_attend_workspace_bytes(geo, table_width) bytes of it: the status
+// header, the selection bitmaps (B * Hq * ceil(nb_cap / 32) * 4 bytes), the
+// split-KV partials (B * Hkv * split * (Hq / Hkv) * (head_dim + 2) * 4 bytes,
+// split = CTAs per KV head, about 148 / (B * Hkv) for small batches) and the
+// arrival counters, each region 256-byte aligned.  Batch 1 at 128K tokens
+// (32 q / 8 KV heads, D 128) needs about 0.33 MiB.
 constexpr size_t kNoAllocScratchBytes = 4u << 20;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
@@ -676,8 +877,8 @@ int adakv_attend_noalloc(const adakv_geometry* geo, const adakv_view* q, const a
   const WsLayout L = make_ws(geo, false);
   if (L.bytes > kNoAllocScratchBytes)
     return fail(ADAKV_ERR_INVALID,
-                "adakv_attend_noalloc needs %zu scratch bytes for this geometry, above its fixed "
-                "maximum of %zu (batch * n_q_heads * ceil(nb_cap / 32) * 4 + 512); use "
+                "adakv_attend_noalloc needs %zu scratch bytes for this geometry "
+                "(adakv_attend_workspace_bytes), above its fixed maximum of %zu; use "
                 "adakv_attend with a workspace",
                 L.bytes, kNoAllocScratchBytes);
   DeviceState* ds = nullptr;

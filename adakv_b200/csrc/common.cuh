@@ -110,8 +110,72 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   return t;
 }
 
+// order-preserving float -> uint32 map; NaN sorts below everything
+__device__ __forceinline__ uint32_t order_key(float f) {
+  const uint32_t u = __float_as_uint(f);
+  if ((u & 0x7FFFFFFFu) > 0x7F800000u) return 0u;
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// Status words live at the start of a workspace (16 bytes reserved): bytes
+// 0..3 collect the ADAKV_ST_* bits, bytes 8..15 optionally hold the device
+// address of a host-mapped word (adakv_set_status_sink) that is written on
+// every report, so that a host can see a failure without synchronising.
 __device__ __forceinline__ void report(uint32_t* status, uint32_t bits) {
-  if (status) atomicOr(status, bits);
+  if (status) {
+    atomicOr(status, bits);
+    uint32_t* sink = *reinterpret_cast<uint32_t* volatile*>(reinterpret_cast<char*>(status) + 8);
+    if (sink) asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(sink), "r"(bits) : "memory");
+  }
+}
+
+// --- tagged 64-bit words (call tag << 32 | 32-bit payload) ------------------
+// A word written whole with one 64-bit store is read whole by one 64-bit
+// load, so a reader that sees this call's tag also sees this call's payload;
+// words of earlier calls carry older tags.  No counter has to be reset.
+__device__ __forceinline__ unsigned long long tword(uint32_t tag, uint32_t bits) {
+  return (static_cast<unsigned long long>(tag) << 32) | bits;
+}
+__device__ __forceinline__ bool tag_is(unsigned long long w, uint32_t tag) {
+  return static_cast<uint32_t>(w >> 32) == tag;
+}
+__device__ __forceinline__ unsigned long long ldr_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void ldr_u64x2(const unsigned long long* p, unsigned long long& a,
+                                          unsigned long long& b) {
+  asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+__device__ __forceinline__ void str_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+
+// One thread's bounded wait budget for a phase: the first wait starts the
+// clock; once `limit` ns have passed the thread stops waiting (`dead`) and
+// uses whatever it reads, and the caller reports ADAKV_ST_WAIT_TIMEOUT.
+struct PollBudget {
+  uint64_t limit;
+  uint64_t t0;
+  bool dead;
+};
+
+// Re-read *p until its tag is `tag` (w = the first read), within the budget.
+__device__ __forceinline__ unsigned long long wait_tagged(const unsigned long long* p,
+                                                          unsigned long long w, uint32_t tag,
+                                                          PollBudget& pb) {
+  if (tag_is(w, tag) || pb.dead) return w;
+  if (pb.t0 == 0) pb.t0 = globaltimer_ns();
+  while (true) {
+    w = ldr_u64(p);
+    if (tag_is(w, tag)) return w;
+    if (globaltimer_ns() - pb.t0 > pb.limit) {
+      pb.dead = true;
+      return w;
+    }
+  }
 }
 
 __device__ __forceinline__ int seq_len_of(const int* seq_lens, int b, int max_seq_len) {

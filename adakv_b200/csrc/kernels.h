@@ -105,6 +105,8 @@ struct PlanParams {
   int slice_cap;            // blocks per CTA (PlanLayout::slice_cap)
   int seqs_per_round;       // grid = seqs_per_round * Hq * csize CTAs
   uint32_t* status;
+  uint64_t wait_ns;         // bound of the entropy exchange wait
+  int debug_flags;          // test-only: bit 0 = head 0 never publishes its entropy
 };
 
 // ---------------------------------------------------------------------------
@@ -139,6 +141,51 @@ struct CombineParams {      // log-sum-exp merge of per-shard attention outputs
   int n_parts, rows, D;
   View out;                 // rows = b * Hq + h -> out[b, h, :]
   int Hq;
+};
+
+// ---------------------------------------------------------------------------
+// (a)-(d) one decode step in one persistent kernel (step.cu)
+// ---------------------------------------------------------------------------
+constexpr int kStepThreads = 256;       // 8 warps: estimator consumers, selection, MMA attend
+constexpr int kStepRows = 64;           // centroid rows per estimator ring stage
+constexpr int kStepStages = 4;          // estimator ring depth
+constexpr int kStepMaxDesc = 192;       // ring stages one CTA streams at most
+constexpr int kStepMaxBatch = 32;       // sequences per call
+constexpr int kStepMaxHeads = 128;      // B * Hq (one selection CTA per query head)
+constexpr int kStepMaxBlocks = 32768;   // blocks per sequence (the score row is staged in smem)
+constexpr int kStepMaxGrid = 256;       // CTAs (one per SM)
+constexpr int kStepOrderCap = 4096;     // bucket-sorted candidate blocks per head
+constexpr int kStepCandCap = 1024;      // boundary-bucket members ranked exactly
+constexpr size_t kStepSmemMax = 220 * 1024;
+
+struct StepParams {
+  View q, k, v, out, k_new, v_new;
+  float* cent;                 // [B, Hkv, nb_cap, D] float32
+  int nb_cap;
+  const int* seq_lens;
+  int max_seq_len;
+  int B, Hq, Hkv, bs;
+  int n_new;                   // tokens appended by this step (0: none)
+  SelectCfg cfg;
+  float sm_scale;
+  int* block_table;            // [B*Hq, table_width] out, ascending block ids
+  int table_width;
+  int* sel_lens;               // [B*Hq] out
+  float* lse;                  // optional [B*Hq]
+  // workspace (tagged words: call tag << 32 | payload)
+  uint32_t* status;
+  uint32_t* epoch;             // [0] call counter, [1] CTAs done
+  unsigned long long* scores;  // [B*Hq, fs_stride] block scores
+  int fs_stride;
+  unsigned long long* hslot;   // [B*Hq] entropy of each head
+  unsigned long long* bitmap;  // [B*Hq, fb_stride] selection bitmaps
+  int fb_stride;
+  unsigned long long* part;    // [grid, g, D + 2] attention partials (m, l, o) per CTA
+  int nbt;                     // K/V blocks per gather stage
+  int slice_cap;               // union blocks one attend CTA takes at most
+  int nb_max;                  // ceil(max_seq_len / bs)
+  uint64_t wait_ns;            // bound of every device-side wait
+  int debug_flags;             // test-only: bit 0 = head 0 never publishes its entropy
 };
 
 // (b') minmax (Quest) estimator: tables and scores
@@ -228,6 +275,15 @@ cudaError_t launch_minmax_build(const MinmaxParams& p, int dtype, int D, int blo
 cudaError_t launch_minmax_score(const MinmaxParams& p, int dtype, int D, int nb_max,
                                 cudaStream_t stream);
 cudaError_t launch_combine(const CombineParams& p, int dtype, cudaStream_t stream, const LaunchOpts& o);
+cudaError_t launch_step(const StepParams& p, int dtype, int D, int g, int grid, size_t smem,
+                        cudaStream_t stream, const LaunchOpts& o);
+cudaError_t launch_step_scores(bool fused, const unsigned long long* fscores,
+                               int fs_stride, const float* scores, int score_stride, int rows,
+                               int nb, float* out, int out_stride, cudaStream_t stream);
+cudaError_t step_kernels_init();
+// dynamic shared memory of the step kernel and its gather-ring depth
+size_t step_smem_bytes(int D, int g, int nb_max, int min_split, int* nbt, int* slice_cap);
+bool step_kernel_built(int dtype, int D, int bs, int g);
 
 // once per device (current device): opt-in shared memory / cluster sizes
 cudaError_t estimate_kernels_init();

@@ -734,7 +734,7 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanParams p) {
     __syncthreads();
     cluster_arrive_release();  // (2) this CTA's histogram is complete
     unsigned long long* slots = &p.slots[0].word;
-    if (tid == 0) {
+    if (tid == 0 && !((p.debug_flags & 1) && row == 0)) {
       const float thi = (float)t_mine;
       const float tlo = (float)(t_mine - (double)thi);
       const size_t at = ((size_t)row * C + rank) * 2;
@@ -773,7 +773,7 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanParams p) {
           ents[q4] = e;
         }
         ok = __all_sync(0xffffffffu, mine);
-        if (ok || globaltimer_ns() - t0 > kWaitLimitNs) break;
+        if (ok || globaltimer_ns() - t0 > p.wait_ns) break;
       }
       if (!ok && lane == 0) report(p.status, ADAKV_ST_WAIT_TIMEOUT);
       double ps = 0.0;

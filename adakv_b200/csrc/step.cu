@@ -1,0 +1,1149 @@
+// (a)-(d) One AdaKV decode step in one persistent kernel.
+//
+// One CTA per SM (256 threads).  The step's three dependent stages run as
+// phases of the same grid, handing data to one another through tagged 64-bit
+// words in the workspace (call tag << 32 | payload): a reader polls a word
+// until it carries this call's tag, so a phase starts as soon as the words it
+// needs exist, with no kernel boundary, grid barrier or counter reset.  Every
+// poll is bounded in time; on expiry the status word records
+// ADAKV_ST_WAIT_TIMEOUT and the kernel runs to completion on what it has.
+//
+// Phase A -- append + estimator (adakv/runtime.py:43-60, adakv/estimator.py:73-74).
+//   The (sequence, KV head, block) rows of every centroid table form one list,
+//   split evenly over the CTAs.  A CTA streams its rows through a 4-stage ring
+//   of 64-row stages with 1-D bulk copies (TMA engine, no multicast); each
+//   stage is refilled by the last warp to finish with it.  A warp scores 8
+//   rows per stage against the g query heads of the row's KV head: LPR = 2g
+//   lanes share a row (D / LPR dims each, queries in registers) and one
+//   reduce-scatter over those lanes leaves every head's score in a lane.
+//   Scores go out as tagged words.  When the step appends tokens, warp 7 of
+//   CTA (b * Hkv + kvh) first writes them into the K/V cache, recomputes the
+//   touched blocks' centroids from their tokens (token-order float32 sum, one
+//   IEEE division: bit-identical to a rebuild) and scores those rows itself.
+//
+// Phase B -- entropy budget + top-k (adakv/budget.py:28-86, adakv/selector.py:18-60).
+//   CTA r < B * Hq owns query head r.  It reads the head's score row into
+//   shared memory, computes the row's max, content statistics and softmax sums
+//   (float per thread, double across threads), the entropy
+//   H = log Z - A / Z - Cc / Z (Cc: the reference's max(p, 1e-9) clamp), and
+//   publishes H.  Warp 0 then polls the H of every head of the sequence while
+//   warps 1-7 histogram the content scores into 2048 buckets below the content
+//   max and bucket-sort the blocks of the buckets any budget can reach.  With
+//   the weights, every CTA derives the same per-head counts (fixed-order sums,
+//   half-to-even rounding); a head's selection is then the forced sink/local
+//   blocks, every block of the buckets above the threshold bucket, and the
+//   exactly ranked (score desc, index asc) top members of that bucket.  An
+//   exact 4-pass radix select over order-preserving keys covers the rows the
+//   buckets cannot resolve.  The selection bitmap goes out as tagged words;
+//   the ascending block table and sel_lens follow.
+//
+// Phase C -- block-sparse split-KV flash decode (adakv/kernels/block_sparse_decode.py:51-100).
+//   The CTAs are split into B * Hkv contiguous groups, one per (sequence, KV
+//   head).  A CTA polls the g selection bitmaps of its group, ORs them into the
+//   union, takes its share of it and gathers those K/V blocks (16-byte
+//   cp.async, zero-filled past seq_len, XOR-swizzled tiles) for an m16n8k16
+//   tensor-core pass over the g query rows (each head masked by its own
+//   selection), then publishes its (m, l, o) partial.  The group's first CTA
+//   merges the partials in split order and writes out[b, h].
+//
+// HBM traffic: the float32 centroid tables, the union of the selected K/V
+// blocks and the appended tokens; scores, bitmaps and partials stay in L2.
+//
+// Memory ordering across CTAs: words are relaxed gpu-scope loads and stores;
+// the appended K/V tokens reach the attend phase through release/acquire
+// fences around the score and bitmap words (refresh warp: fence before its
+// score words; selection CTA: fence after reading the row and before the
+// bitmap; attend CTA: fence after reading the bitmaps).
+//
+// All CTAs must be resident at once (they wait on one another): the host
+// launches at most one CTA per SM, and every wait is bounded.
+#include "attend_mma.cuh"
+#include "kernels.h"
+
+namespace adakv {
+
+namespace {
+
+constexpr int kSW = kStepThreads / 32;  // warps per CTA
+constexpr int kBk = 2048;               // selection buckets
+constexpr int kDebugSkipPublish = 1;
+
+__device__ __forceinline__ float h16lo(uint32_t w, const __nv_bfloat16*) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float h16hi(uint32_t w, const __nv_bfloat16*) {
+  return __uint_as_float(w & 0xFFFF0000u);
+}
+__device__ __forceinline__ float h16lo(uint32_t w, const __half*) {
+  return __half2float(__ushort_as_half(static_cast<unsigned short>(w & 0xFFFFu)));
+}
+__device__ __forceinline__ float h16hi(uint32_t w, const __half*) {
+  return __half2float(__ushort_as_half(static_cast<unsigned short>(w >> 16)));
+}
+
+// four consecutive 16-bit elements -> fp32
+template <typename T>
+__device__ __forceinline__ void load4(const T* p, float (&f)[4]) {
+  const uint2 u = *reinterpret_cast<const uint2*>(p);
+  f[0] = h16lo(u.x, (const T*)nullptr);
+  f[1] = h16hi(u.x, (const T*)nullptr);
+  f[2] = h16lo(u.y, (const T*)nullptr);
+  f[3] = h16hi(u.y, (const T*)nullptr);
+}
+
+// Reduce-scatter of G per-lane partial sums over groups of LPR lanes (lane
+// bits below LPR): afterwards every lane holds the group-wide sum of head
+// (sub >> log2(LPR / G)) (sub = lane % LPR); the last levels are plain
+// all-reduces of that one value.
+template <int G, int LPR>
+__device__ __forceinline__ float reduce_heads(float (&v)[G], int lane) {
+#pragma unroll
+  for (int lvl = 0; (LPR >> (lvl + 1)) >= 1; ++lvl) {
+    const int off = LPR >> (lvl + 1);
+    const int nv = G >> lvl;
+    if (nv > 1) {
+      const int half = nv / 2;
+      const bool upper = (lane & off) != 0;
+#pragma unroll
+      for (int i = 0; i < half; ++i) {
+        const float send = upper ? v[i] : v[i + half];
+        const float keep = upper ? v[i + half] : v[i];
+        v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+      }
+    } else {
+      v[0] += __shfl_xor_sync(0xffffffffu, v[0], off);
+    }
+  }
+  return v[0];
+}
+
+// bucket of a content score: floor((cmx - s) * scale), clamped to the last
+// bucket (which also takes NaN and -inf); non-decreasing as s decreases
+__device__ __forceinline__ int bucket_of(float s, float cmx, float scale) {
+  const float u = __fmul_rn(__fsub_rn(cmx, s), scale);
+  if (!(u < (float)(kBk - 1))) return kBk - 1;
+  return u <= 0.f ? 0 : (int)u;
+}
+
+// block-wide reduction: every thread gets the same result (warp xor trees,
+// then the kSW warp values folded in warp order)
+__device__ __forceinline__ void block_max2(float& a, float& b, float (*red)[4]) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  a = warp_max(a);
+  b = warp_max(b);
+  __syncthreads();
+  if (lane == 0) {
+    red[warp][0] = a;
+    red[warp][1] = b;
+  }
+  __syncthreads();
+  a = red[0][0];
+  b = red[0][1];
+#pragma unroll
+  for (int w = 1; w < kSW; ++w) {
+    a = fmaxf(a, red[w][0]);
+    b = fmaxf(b, red[w][1]);
+  }
+}
+__device__ __forceinline__ void block_sum2d(double& a, double& b, double (*red)[4]) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  a = warp_sum(a);
+  b = warp_sum(b);
+  __syncthreads();
+  if (lane == 0) {
+    red[warp][0] = a;
+    red[warp][1] = b;
+  }
+  __syncthreads();
+  a = 0.0;
+  b = 0.0;
+#pragma unroll
+  for (int w = 0; w < kSW; ++w) {
+    a += red[w][0];
+    b += red[w][1];
+  }
+}
+
+// shared-memory carve-up of one step CTA; the three phases reuse the same bytes
+struct StepSmem {
+  size_t ring;                                      // phase A
+  size_t srow, sbits, hist, pre, fill, order, b_end;  // phase B
+  size_t kv, uw, hw, list, mask, wpart, merge, c_end;  // phase C
+  size_t total;
+};
+
+__host__ __device__ inline StepSmem step_smem_layout(int D, int g, int nb_max, int nbt, int slice_cap) {
+  auto al = [](size_t x) { return (x + 127) / 128 * 128; };
+  const int nw = (nb_max + 31) / 32;
+  StepSmem s;
+  s.ring = al((size_t)kStepStages * kStepRows * D * 4);
+  s.srow = 0;
+  s.sbits = s.srow + al((size_t)nb_max * 4);
+  s.hist = s.sbits + al((size_t)nw * 4);
+  s.pre = s.hist + al((size_t)kBk * 4);
+  s.fill = s.pre + al((size_t)kBk * 4);
+  s.order = s.fill + al((size_t)(kBk > nw ? kBk : nw) * 4);
+  s.b_end = s.order + al((size_t)kStepOrderCap * 4);
+  s.kv = 0;
+  s.uw = s.kv + al((size_t)2 * 2 * nbt * 16 * D * 2);
+  s.hw = s.uw + al((size_t)nw * 4);
+  s.list = s.hw + al((size_t)g * nw * 4);
+  s.mask = s.list + al((size_t)slice_cap * 4);
+  s.wpart = s.mask + al((size_t)slice_cap * 4);
+  s.merge = s.wpart + al((size_t)kSW * g * (D + 2) * 4);
+  s.c_end = s.merge + al((size_t)(kStepMaxGrid * g + 2 * g) * 4);
+  size_t t = s.ring;
+  t = t > s.b_end ? t : s.b_end;
+  t = t > s.c_end ? t : s.c_end;
+  s.total = t;
+  return s;
+}
+
+// a sequence takes part when 1 <= S <= max_seq_len and it holds the appended tokens
+__device__ __forceinline__ int valid_len(const StepParams& p, int b) {
+  const int S = seq_len_of(p.seq_lens, b, p.max_seq_len);
+  const bool ok = S > 0 && S <= p.max_seq_len && (p.n_new <= 0 || S >= p.n_new);
+  return ok ? S : 0;
+}
+
+}  // namespace
+
+template <typename T, int D, int G>
+__global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepParams p) {
+  constexpr int BS = 16;
+  constexpr int LPR = 2 * G;             // lanes per centroid row
+  constexpr int RPP = 32 / LPR;          // rows per warp pass
+  constexpr int RPW = kStepRows / kSW;   // rows per warp and stage
+  constexpr int PASSES = RPW / RPP;
+  constexpr int DL = D / LPR;            // dims per lane
+  constexpr int CH = DL / 4;             // float4 chunks per lane and row
+  constexpr int E = D / 32;              // dims per lane in the refresh warp
+  constexpr int VEC = 8;                 // 16-bit elements per 16-byte chunk
+  constexpr int ROWC = D / VEC;          // 16-byte chunks per token row
+  constexpr int BLK = BS * D;            // elements of one K (or V) block
+  static_assert(CH >= 1 && RPW % RPP == 0 && E == 4, "unsupported step shape");
+
+  extern __shared__ __align__(128) unsigned char sm[];
+  __shared__ __align__(8) uint64_t full_bar[kStepStages];
+  __shared__ int rel_cnt[kStepStages];
+  __shared__ int4 sdesc[kStepMaxDesc];
+  __shared__ int s_nstage;
+  __shared__ int s_S[kStepMaxBatch];
+  __shared__ int s_rb[kStepMaxBatch + 1];
+  __shared__ uint32_t s_tag;
+  __shared__ float redf[kSW][4];
+  __shared__ double redd[kSW][4];
+  __shared__ int scan_scratch[33];
+  __shared__ double s_w, s_sumw;
+  __shared__ int s_blim, s_jstar, s_over, s_digit, s_above, s_last;
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int GRID = gridDim.x, cta = blockIdx.x;
+  const bool appending = p.n_new > 0 && p.k_new.data != nullptr;
+
+  // Nothing is read before the previous kernel on the stream has completed:
+  // q, the caches, the centroid table and seq_lens may all be its outputs.
+  pdl_wait();
+
+  // ---------------------------------------------------------------- set-up
+  if (tid == 0) {
+    const uint32_t e = *reinterpret_cast<volatile uint32_t*>(p.epoch);
+    s_tag = (e + 1u) ? e + 1u : 1u;
+    for (int s = 0; s < kStepStages; ++s) {
+      mbar_init(&full_bar[s], 1);
+      rel_cnt[s] = 0;
+    }
+  }
+  if (tid < p.B) {
+    const int S = valid_len(p, tid);
+    s_S[tid] = S;
+    if (S == 0 && cta == 0) report(p.status, ADAKV_ST_BAD_SEQ_LEN);
+  }
+  __syncthreads();
+  const uint32_t tag = s_tag;
+  if (warp == 0) {  // row list prefix over the sequences (B <= 32)
+    const int nbb = lane < p.B ? ceil_div(s_S[lane], BS) : 0;
+    const int cnt = p.Hkv * nbb;
+    int incl = cnt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    if (lane < p.B) s_rb[lane] = incl - cnt;
+    if (lane == 31) s_rb[p.B] = incl;
+    __syncwarp();
+    if (lane == 0) {
+      // this CTA's rows [r0, r1) as ring stages of <= 64 rows of one (sequence, KV head)
+      const int R = s_rb[p.B];
+      const int r0 = (int)((int64_t)R * cta / GRID), r1 = (int)((int64_t)R * (cta + 1) / GRID);
+      int r = r0, ns = 0, b = 0;
+      while (r < r1) {
+        while (r >= s_rb[b + 1]) ++b;
+        const int nb = ceil_div(s_S[b], BS);
+        const int loc = r - s_rb[b];
+        const int kvh = loc / nb, j = loc - kvh * nb;
+        const int n = imin(kStepRows, imin(nb - j, r1 - r));
+        const int skip = appending ? (s_S[b] - p.n_new) / BS : nb;  // first refreshed block
+        if (ns == kStepMaxDesc) {  // the host sizes grids so that this cannot happen
+          report(p.status, ADAKV_ST_WAIT_TIMEOUT);
+          break;
+        }
+        sdesc[ns++] = make_int4(b * p.Hkv + kvh, j, n, imax(0, skip - j));
+        r += n;
+      }
+      s_nstage = ns;
+    }
+  }
+  __syncthreads();
+  const int nstage = s_nstage;
+  float* ring = reinterpret_cast<float*>(sm);
+  auto issue = [&](int i, int slot) {
+    const int4 d = sdesc[i];
+    const uint32_t bytes = (uint32_t)d.z * D * 4u;
+    mbar_arrive_expect_tx(&full_bar[slot], bytes);
+    bulk_g2s(ring + slot * kStepRows * D, p.cent + ((int64_t)d.x * p.nb_cap + d.y) * D, bytes,
+             &full_bar[slot]);
+  };
+  if (tid == 0)
+    for (int i = 0; i < imin(kStepStages, nstage); ++i) issue(i, i);
+
+  // ---------------------------------------------------------------- phase A
+  // fused append: warp 7 of CTA (b * Hkv + kvh) refreshes that table's tail
+  if (appending && warp == kSW - 1 && cta < p.B * p.Hkv) {
+    const int b = cta / p.Hkv, kvh = cta - b * p.Hkv;
+    const int S = s_S[b];
+    if (S > 0) {
+      const int S_old = S - p.n_new;
+      const int nb = ceil_div(S, BS);
+      const int d = lane * E;
+      T* kc = static_cast<T*>(const_cast<void*>(p.k.data)) + b * p.k.sb + kvh * p.k.sh + d;
+      T* vc = static_cast<T*>(const_cast<void*>(p.v.data)) + b * p.v.sb + kvh * p.v.sh + d;
+      const T* kn = static_cast<const T*>(p.k_new.data) + b * p.k_new.sb + kvh * p.k_new.sh + d;
+      const T* vn = static_cast<const T*>(p.v_new.data) + b * p.v_new.sb + kvh * p.v_new.sh + d;
+      const T* qb = static_cast<const T*>(p.q.data) + b * p.q.sb + (int64_t)kvh * G * p.q.sh + d;
+      float qv[G][E];
+#pragma unroll
+      for (int j = 0; j < G; ++j) load4<T>(qb + j * p.q.sh, qv[j]);
+      for (int blk = S_old / BS; blk < nb; ++blk) {
+        const int t0 = blk * BS, t1 = imin(t0 + BS, S);
+        uint2 x[BS];
+#pragma unroll
+        for (int u = 0; u < BS; ++u) {
+          const int t = t0 + u;
+          if (t < t1) {
+            const T* src = (t >= S_old) ? kn + (int64_t)(t - S_old) * p.k_new.ss : kc + (int64_t)t * p.k.ss;
+            x[u] = *reinterpret_cast<const uint2*>(src);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < BS; ++u) {
+          const int t = t0 + u;
+          if (t < t1 && t >= S_old) {
+            *reinterpret_cast<uint2*>(kc + (int64_t)t * p.k.ss) = x[u];
+            *reinterpret_cast<uint2*>(vc + (int64_t)t * p.v.ss) =
+                *reinterpret_cast<const uint2*>(vn + (int64_t)(t - S_old) * p.v_new.ss);
+          }
+        }
+        float acc[E];
+#pragma unroll
+        for (int u = 0; u < BS; ++u) {
+          const int t = t0 + u;
+          if (t < t1) {
+            const float xf[4] = {h16lo(x[u].x, (const T*)nullptr), h16hi(x[u].x, (const T*)nullptr),
+                                 h16lo(x[u].y, (const T*)nullptr), h16hi(x[u].y, (const T*)nullptr)};
+#pragma unroll
+            for (int e = 0; e < E; ++e) acc[e] = (t == t0) ? xf[e] : __fadd_rn(acc[e], xf[e]);
+          }
+        }
+        const float nf = (float)(t1 - t0);
+        float cen[E];
+#pragma unroll
+        for (int e = 0; e < E; ++e) cen[e] = __fdiv_rn(acc[e], nf);
+        float* crow = p.cent + ((int64_t)(b * p.Hkv + kvh) * p.nb_cap + blk) * D + d;
+        *reinterpret_cast<float4*>(crow) = make_float4(cen[0], cen[1], cen[2], cen[3]);
+        float sc[G];
+#pragma unroll
+        for (int j = 0; j < G; ++j) {
+          float part = 0.f;
+#pragma unroll
+          for (int e = 0; e < E; ++e) part = fmaf(qv[j][e], cen[e], part);
+#pragma unroll
+          for (int o = 16; o; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+          sc[j] = part;
+        }
+        // the cache writes of every lane are ordered before the score words
+        __syncwarp();
+        fence_acq_rel_gpu();
+#pragma unroll
+        for (int j = 0; j < G; ++j)
+          if (lane == j)
+            str_u64(p.scores + (size_t)(b * p.Hq + kvh * G + j) * p.fs_stride + blk,
+                    tword(tag, __float_as_uint(sc[j])));
+      }
+    }
+  }
+  {
+    const int sub = lane % LPR, rin = lane / LPR;
+    float qf[G][DL];
+    int qrun = -1;
+    for (int i = 0; i < nstage; ++i) {
+      const int slot = i % kStepStages;
+      const uint32_t par = (uint32_t)(i / kStepStages) & 1u;
+      if (!mbar_wait_bounded(&full_bar[slot], par)) {
+        if (lane == 0) report(p.status, ADAKV_ST_WAIT_TIMEOUT);
+        break;
+      }
+      const int4 d = sdesc[i];
+      const int b = d.x / p.Hkv, kvh = d.x - b * p.Hkv;
+      if (d.x != qrun) {
+        qrun = d.x;
+        const T* qb = static_cast<const T*>(p.q.data) + b * p.q.sb + (int64_t)kvh * G * p.q.sh;
+#pragma unroll
+        for (int h = 0; h < G; ++h)
+#pragma unroll
+          for (int k = 0; k < CH; ++k) {
+            float f[4];
+            load4<T>(qb + h * p.q.sh + 4 * (sub + LPR * k), f);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) qf[h][4 * k + e] = f[e];
+          }
+      }
+      const float* tile = ring + slot * kStepRows * D;
+      unsigned long long* srow0 = p.scores + (size_t)(b * p.Hq + kvh * G) * p.fs_stride + d.y;
+#pragma unroll
+      for (int pp = 0; pp < PASSES; ++pp) {
+        const int row = warp * RPW + pp * RPP + rin;
+        float acc[G];
+#pragma unroll
+        for (int h = 0; h < G; ++h) acc[h] = 0.f;
+        if (row < d.z) {
+          const float* rp = tile + row * D;
+#pragma unroll
+          for (int k = 0; k < CH; ++k) {
+            const float4 c = *reinterpret_cast<const float4*>(rp + 4 * (sub + LPR * k));
+#pragma unroll
+            for (int h = 0; h < G; ++h) {
+              acc[h] = fmaf(qf[h][4 * k + 0], c.x, acc[h]);
+              acc[h] = fmaf(qf[h][4 * k + 1], c.y, acc[h]);
+              acc[h] = fmaf(qf[h][4 * k + 2], c.z, acc[h]);
+              acc[h] = fmaf(qf[h][4 * k + 3], c.w, acc[h]);
+            }
+          }
+        }
+        const float s = reduce_heads<G, LPR>(acc, lane);
+        if ((sub & 1) == 0 && row < d.z && row < d.w)
+          str_u64(srow0 + (size_t)(sub >> 1) * p.fs_stride + row, tword(tag, __float_as_uint(s)));
+      }
+      __syncwarp();
+      if (lane == 0) {
+        const int old = atomicAdd(&rel_cnt[slot], 1);
+        if (old == kSW - 1) {  // last warp out refills the stage
+          rel_cnt[slot] = 0;
+          if (i + kStepStages < nstage) issue(i + kStepStages, slot);
+        }
+      }
+    }
+  }
+  __syncthreads();  // the ring is drained: its bytes are reused below
+
+  // ---------------------------------------------------------------- phase B
+  if (cta < p.B * p.Hq) {
+    const int hr = cta, b = hr / p.Hq, h = hr - b * p.Hq;
+    const int nb = ceil_div(s_S[b], BS);
+    const int nw = ceil_div(nb, 32);
+    const StepSmem L = step_smem_layout(D, G, p.nb_max, p.nbt, p.slice_cap);
+    float* srow = reinterpret_cast<float*>(sm + L.srow);
+    uint32_t* sbits = reinterpret_cast<uint32_t*>(sm + L.sbits);
+    uint32_t* hist = reinterpret_cast<uint32_t*>(sm + L.hist);
+    uint32_t* pre = reinterpret_cast<uint32_t*>(sm + L.pre);
+    uint32_t* fill = reinterpret_cast<uint32_t*>(sm + L.fill);
+    int* order = reinterpret_cast<int*>(sm + L.order);
+    const SelectCfg& cf = p.cfg;
+    const int sink = imin(cf.n_sink, nb), local = imin(cf.n_local, nb);
+    auto forced = [&](int j) -> bool { return j < sink || j >= nb - local; };
+    const bool adaptive = nb >= 2 && cf.policy == ADAKV_POLICY_ADAPTIVE;
+    const float Tf = (float)(cf.temperature > 1e-6 ? cf.temperature : 1e-6);
+    const bool unit_t = (Tf == 1.0f);
+    auto zof = [&](float v) -> float { return unit_t ? v : __fdiv_rn(v, Tf); };
+
+    for (int t = tid; t < kBk; t += kStepThreads) {
+      hist[t] = 0u;
+      fill[t] = 0u;
+    }
+    for (int w = tid; w < nw; w += kStepThreads) sbits[w] = 0u;
+    if (tid == 0) {
+      s_over = 0;
+      s_jstar = -1;
+      s_blim = -1;
+    }
+
+    // ---- the head's score row: tagged words -> floats in shared memory ----
+    {
+      PollBudget pb{p.wait_ns, 0, false};
+      const unsigned long long* src = p.scores + (size_t)hr * p.fs_stride;
+      constexpr int U = 4;
+      for (int j0 = 2 * tid; j0 < nb; j0 += 2 * kStepThreads * U) {
+        unsigned long long w[U][2];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int j = j0 + 2 * kStepThreads * u;
+          if (j < nb) ldr_u64x2(src + j, w[u][0], w[u][1]);
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int j = j0 + 2 * kStepThreads * u;
+          if (j < nb) {
+            w[u][0] = wait_tagged(src + j, w[u][0], tag, pb);
+            srow[j] = __uint_as_float((uint32_t)w[u][0]);
+            if (j + 1 < nb) {
+              w[u][1] = wait_tagged(src + j + 1, w[u][1], tag, pb);
+              srow[j + 1] = __uint_as_float((uint32_t)w[u][1]);
+            }
+          }
+        }
+      }
+      if (pb.dead) report(p.status, ADAKV_ST_WAIT_TIMEOUT);
+      fence_acq_rel_gpu();  // acquire: the refreshed K/V tokens precede these scores
+    }
+    __syncthreads();
+
+    // ---- row statistics (pass 1) ----
+    float mx = -INFINITY, cmx = -INFINITY;
+    double csum, csq;
+    {
+      float cs = 0.f, cq = 0.f;
+      for (int j = tid; j < nb; j += kStepThreads) {
+        const float v = srow[j];
+        mx = fmaxf(mx, v);
+        if (!forced(j)) {
+          cmx = fmaxf(cmx, v);
+          cs += v;
+          cq = fmaf(v, v, cq);
+        }
+      }
+      csum = cs;
+      csq = cq;
+      block_max2(mx, cmx, redf);
+      block_sum2d(csum, csq, redd);
+    }
+    // ---- softmax sums (pass 2) and the clamp correction (pass 3) ----
+    double H = 0.0;
+    if (adaptive) {
+      const float zmax = zof(mx);
+      double Z, A;
+      {
+        float z_t = 0.f, a_t = 0.f;
+        for (int j = tid; j < nb; j += kStepThreads) {
+          const float dd = __fsub_rn(zof(srow[j]), zmax);
+          const float e = expf(dd);
+          z_t += e;
+          if (e > 0.f) a_t = fmaf(e, dd, a_t);
+        }
+        Z = z_t;
+        A = a_t;
+        block_sum2d(Z, A, redd);
+      }
+      // H = log Z - A / Z - Cc / Z with Cc = sum over blocks with e / Z < 1e-9
+      // of e (log(1e-9) - d + log Z): the reference's max(p, 1e-9)
+      double Cc = 0.0;
+      {
+        const float Zf = (float)Z;
+        const float logZ = (float)log(Z);
+        const float ln_floor = logf(1e-9f);
+        const float pre_lim = 2e-9f * Zf;
+        const float d_hi = logf(pre_lim), d_lo = d_hi - 25.f;
+        float cp = 0.f;
+        for (int j = tid; j < nb; j += kStepThreads) {
+          const float dd = __fsub_rn(zof(srow[j]), zmax);
+          if (dd < d_hi && dd >= d_lo) {
+            const float e = expf(dd);
+            if (e > 0.f && e < pre_lim && __fdiv_rn(e, Zf) < 1e-9f) cp = fmaf(e, ln_floor - dd + logZ, cp);
+          }
+        }
+        Cc = cp;
+        double dummy = 0.0;
+        block_sum2d(Cc, dummy, redd);
+      }
+      H = log(Z) - A / Z - Cc / Z;
+      if (tid == 0 && !((p.debug_flags & kDebugSkipPublish) && hr == 0))
+        str_u64(p.hslot + hr, tword(tag, __float_as_uint((float)H)));
+    }
+
+    // ---- bucket geometry (the same in every CTA of the row: block-uniform values) ----
+    const double nc_d = (double)(nb - imin(nb, sink + local));
+    const double mean_c = nc_d > 0 ? csum / nc_d : 0.0;
+    const double var_c = nc_d > 0 ? csq / nc_d - mean_c * mean_c : 0.0;
+    const double sd_c = var_c > 0.0 ? sqrt(var_c) : 0.0;
+    const double range = (double)cmx - (mean_c - sd_c);
+    const bool buckets_ok = isfinite(cmx) && range > 0.0 && isfinite(range);
+    const float scale = buckets_ok ? (float)((double)(kBk - 1) / range) : 0.f;
+
+    if (warp == 0) {
+      // ---- entropies of every head of the sequence -> weights ----
+      if (adaptive) {
+        PollBudget pb{p.wait_ns, 0, false};
+        const double lognb = log((double)imax(nb, 2));
+        double ps = 0.0, mine = 0.0;
+#pragma unroll
+        for (int q4 = 0; q4 < kStepMaxHeads / 32; ++q4) {
+          const int hh = lane + q4 * 32;
+          if (hh < p.Hq) {
+            const unsigned long long* a = p.hslot + b * p.Hq + hh;
+            const unsigned long long w = wait_tagged(a, ldr_u64(a), tag, pb);
+            const double wv = (double)__uint_as_float((uint32_t)w) / lognb + 1e-6;
+            ps += wv;
+            if (hh == h) mine = wv;
+          }
+        }
+        if (__any_sync(0xffffffffu, pb.dead) && lane == 0) report(p.status, ADAKV_ST_WAIT_TIMEOUT);
+        ps = warp_sum(ps);  // fixed xor tree: every CTA of the sequence gets the same sum
+        mine = warp_sum(mine);
+        if (lane == 0) {
+          s_sumw = ps;
+          s_w = mine;
+        }
+      }
+    } else if (buckets_ok) {
+      // ---- warps 1-7: content histogram, bucket prefix, bucket sort ----
+      const int t7 = tid - 32, n7 = kStepThreads - 32;
+      for (int j = t7; j < nb; j += n7) {
+        if (!forced(j)) {
+          const int bk = bucket_of(srow[j], cmx, scale);
+          if (bk < kBk - 1) atomicAdd(&hist[bk], 1u);
+        }
+      }
+      named_bar_sync(1, n7);
+      if (warp == 1) {
+        constexpr int PL = kBk / 32;  // buckets per lane
+        uint32_t tot = 0;
+        for (int e = 0; e < PL; ++e) tot += hist[lane * PL + e];
+        uint32_t incl = tot;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += y;
+        }
+        const uint32_t total = __shfl_sync(0xffffffffu, incl, 31);
+        // buckets any count of this geometry can reach: up to the table width
+        const uint32_t cap = imin((int)total, p.table_width);
+        uint32_t acc = incl - tot;
+        for (int e = 0; e < PL; ++e) {
+          const int bk = lane * PL + e;
+          const uint32_t c = hist[bk];
+          pre[bk] = acc;
+          if (cap > 0 && acc < cap && cap <= acc + c) s_blim = bk;
+          acc += c;
+        }
+      }
+      named_bar_sync(1, n7);
+      const int blim = s_blim;
+      if (blim >= 0) {
+        for (int j = t7; j < nb; j += n7) {
+          if (!forced(j)) {
+            const int bk = bucket_of(srow[j], cmx, scale);
+            if (bk <= blim) {
+              const uint32_t pos = pre[bk] + atomicAdd(&fill[bk], 1u);
+              if (pos < (uint32_t)kStepOrderCap) order[pos] = j;
+              else s_over = 1;
+            }
+          }
+        }
+      }
+    }
+    __syncthreads();
+
+    // ---- this head's count (budget.py:71-86, selector.py:49-54) ----
+    const SeqBudget sbud = seq_budget(nb, cf);
+    const double w_h = adaptive ? s_w : 0.0, sum_w = adaptive ? s_sumw : 0.0;
+    const int K = imin(head_count(sbud, cf, w_h, sum_w, p.Hq), p.table_width);
+    const int n_forced = (sink + local >= nb) ? nb : sink + local;
+    const int Kc = K - n_forced;
+    const bool all = K >= nb;
+
+    // forced blocks (the reference's +inf bias, selector.py:44-48)
+    if (all) {
+      for (int w = tid; w < nw; w += kStepThreads)
+        sbits[w] = (w * 32 + 32 <= nb) ? 0xFFFFFFFFu : ((1u << (nb - w * 32)) - 1u);
+    } else {
+      for (int j = tid; j < sink; j += kStepThreads) atomicOr(&sbits[j >> 5], 1u << (j & 31));
+      for (int j = nb - local + tid; j < nb; j += kStepThreads) atomicOr(&sbits[j >> 5], 1u << (j & 31));
+    }
+    bool use_radix = false;
+    if (!all && Kc > 0) {
+      use_radix = !buckets_ok || s_over != 0 || s_blim < 0;
+      if (!use_radix) {
+        for (int i = tid; i < kBk; i += kStepThreads)
+          if (pre[i] < (uint32_t)Kc && (uint32_t)Kc <= pre[i] + hist[i]) s_jstar = i;
+        __syncthreads();
+        const int js = s_jstar;
+        use_radix = js < 0 || js > s_blim || (int)hist[js] > kStepCandCap;
+        if (!use_radix) {
+          const int above = (int)pre[js], nc = (int)hist[js], need = Kc - above;
+          for (int i = tid; i < above; i += kStepThreads) {
+            const int j = order[i];
+            atomicOr(&sbits[j >> 5], 1u << (j & 31));
+          }
+          for (int u = tid; u < nc; u += kStepThreads) {
+            const int ju = order[above + u];
+            const uint32_t ku = order_key(srow[ju]);
+            int rk = 0;
+            for (int c = 0; c < nc; ++c) {
+              const int jc = order[above + c];
+              const uint32_t kc = order_key(srow[jc]);
+              rk += (kc > ku) || (kc == ku && jc < ju);
+            }
+            if (rk < need) atomicOr(&sbits[ju >> 5], 1u << (ju & 31));
+          }
+        }
+      }
+    }
+    if (use_radix) {
+      // ---- exact radix select of the top K keys (forced blocks = max key),
+      //      ties at the threshold to the lowest block indices ----
+      __syncthreads();
+      for (int j = tid; j < nb; j += kStepThreads)
+        srow[j] = __uint_as_float(forced(j) ? 0xFFFFFFFFu : order_key(srow[j]));
+      uint32_t prefix = 0, pmask = 0;
+      int rem = K;
+#pragma unroll 1
+      for (int pass = 0; pass < 4; ++pass) {
+        const int shift = 24 - 8 * pass;
+        __syncthreads();
+        for (int t = tid; t < 256; t += kStepThreads) hist[t] = 0u;
+        __syncthreads();
+        for (int j = tid; j < nb; j += kStepThreads) {
+          const uint32_t k = __float_as_uint(srow[j]);
+          if ((k & pmask) == prefix) atomicAdd(&hist[(k >> shift) & 0xFFu], 1u);
+        }
+        __syncthreads();
+        if (warp == 0) {
+          uint32_t c[8], tot = 0;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            c[e] = hist[255 - 8 * lane - e];
+            tot += c[e];
+          }
+          uint32_t incl = tot;
+#pragma unroll
+          for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += y;
+          }
+          const uint32_t excl = incl - tot;
+          if (excl < (uint32_t)rem && (uint32_t)rem <= incl) {
+            uint32_t acc = excl;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              if (acc + c[e] >= (uint32_t)rem) {
+                s_digit = 255 - 8 * lane - e;
+                s_above = (int)acc;
+                break;
+              }
+              acc += c[e];
+            }
+          }
+        }
+        __syncthreads();
+        rem -= s_above;
+        prefix |= (uint32_t)s_digit << shift;
+        pmask |= 0xFFu << shift;
+      }
+      // keys above the threshold, then the first `rem` keys equal to it in index order
+      uint32_t* weq = fill;  // [nw]
+      for (int w = warp; w < nw; w += kSW) {
+        const int j = w * 32 + lane;
+        const uint32_t k = j < nb ? __float_as_uint(srow[j]) : 0u;
+        const uint32_t gt = __ballot_sync(0xffffffffu, j < nb && k > prefix);
+        const uint32_t eq = __ballot_sync(0xffffffffu, j < nb && k == prefix);
+        if (lane == 0) {
+          sbits[w] = gt;
+          weq[w] = eq;
+        }
+      }
+      __syncthreads();
+      const int wpt = ceil_div(nw, kStepThreads);
+      const int w0 = imin(tid * wpt, nw), w1 = imin(w0 + wpt, nw);
+      int n_eq = 0;
+      for (int w = w0; w < w1; ++w) n_eq += __popc(weq[w]);
+      int eq_before = block_exclusive_scan(n_eq, scan_scratch);
+      for (int w = w0; w < w1; ++w) {
+        uint32_t e = weq[w];
+        const int take = imax(0, imin(__popc(e), rem - eq_before));
+        eq_before += __popc(e);
+        uint32_t low = 0;
+        for (int t = 0; t < take; ++t) {
+          low |= e & (0u - e);
+          e &= e - 1u;
+        }
+        sbits[w] |= low;
+      }
+    }
+    __syncthreads();
+
+    // ---- publish the bitmap (release: the refreshed tokens precede it) ----
+    fence_acq_rel_gpu();
+    for (int w = tid; w < nw; w += kStepThreads)
+      str_u64(p.bitmap + (size_t)hr * p.fb_stride + w, tword(tag, sbits[w]));
+    // ---- ascending block table and count ----
+    {
+      const int wpt = ceil_div(nw, kStepThreads);
+      const int w0 = imin(tid * wpt, nw), w1 = imin(w0 + wpt, nw);
+      int cnt = 0;
+      for (int w = w0; w < w1; ++w) cnt += __popc(sbits[w]);
+      int pos = block_exclusive_scan(cnt, scan_scratch);
+      const int total = scan_scratch[32];
+      int* trow = p.block_table + (int64_t)hr * p.table_width;
+      for (int w = w0; w < w1; ++w) {
+        uint32_t s = sbits[w];
+        while (s) {
+          const int bit = __ffs(s) - 1;
+          s &= s - 1u;
+          if (pos < p.table_width) trow[pos] = w * 32 + bit;
+          ++pos;
+        }
+      }
+      if (tid == 0) p.sel_lens[hr] = total;
+    }
+    __syncthreads();  // phase C reuses the shared memory
+  }
+
+  // ---------------------------------------------------------------- phase C
+  pdl_launch_dependents();
+  {
+    const int NG = p.B * p.Hkv;
+    const int gi = (int)(((int64_t)(cta + 1) * NG - 1) / GRID);
+    const int c_first = (int)((int64_t)gi * GRID / NG), c_next = (int)((int64_t)(gi + 1) * GRID / NG);
+    const int split = cta - c_first, SPLIT = c_next - c_first;
+    const int b = gi / p.Hkv, kvh = gi - b * p.Hkv;
+    const int S = s_S[b];
+    const int nb = ceil_div(S, BS);
+    const int nw = ceil_div(nb, 32);
+    const int row0 = b * p.Hq + kvh * G;
+    const StepSmem L = step_smem_layout(D, G, p.nb_max, p.nbt, p.slice_cap);
+    T* kvbuf = reinterpret_cast<T*>(sm + L.kv);
+    uint32_t* uw = reinterpret_cast<uint32_t*>(sm + L.uw);
+    uint32_t* hw = reinterpret_cast<uint32_t*>(sm + L.hw);
+    int* list = reinterpret_cast<int*>(sm + L.list);
+    uint32_t* lmask = reinterpret_cast<uint32_t*>(sm + L.mask);
+    float* wpart = reinterpret_cast<float*>(sm + L.wpart);
+    float* mf = reinterpret_cast<float*>(sm + L.merge);
+    float* ml = mf + kStepMaxGrid * G;
+    float* mL = ml + G;
+    const T* kbase = static_cast<const T*>(p.k.data) + b * p.k.sb + kvh * p.k.sh;
+    const T* vbase = static_cast<const T*>(p.v.data) + b * p.v.sb + kvh * p.v.sh;
+    const T* qbase = static_cast<const T*>(p.q.data) + b * p.q.sb + (int64_t)kvh * G * p.q.sh;
+    const int gid = lane >> 2, tig = lane & 3;
+    MmaAcc<D> acc;
+    uint32_t qa[D / 16][4];
+#pragma unroll
+    for (int nn = 0; nn < MmaAcc<D>::NT; ++nn)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc.o[nn][e] = 0.f;
+    acc.m[0] = acc.m[1] = -INFINITY;
+    acc.l[0] = acc.l[1] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < D / 16; ++ks) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int r = gid + (e & 1) * 8;
+        const int col = ks * 16 + (e >> 1) * 8 + tig * 2;
+        qa[ks][e] = r < G ? *reinterpret_cast<const uint32_t*>(qbase + (int64_t)r * p.q.sh + col) : 0u;
+      }
+    }
+    const float scale_log2 = p.sm_scale * 1.4426950408889634f;
+
+    // ---- the group's bitmaps (this call's words) -> union, head words ----
+    const int wpt = ceil_div(nw, kStepThreads);
+    const int w0 = imin(tid * wpt, nw), w1 = imin(w0 + wpt, nw);
+    int cnt = 0;
+    {
+      PollBudget pb{p.wait_ns, 0, false};
+      for (int w = w0; w < w1; ++w) {
+        unsigned long long x[G];
+#pragma unroll
+        for (int hh = 0; hh < G; ++hh) x[hh] = ldr_u64(p.bitmap + (size_t)(row0 + hh) * p.fb_stride + w);
+        uint32_t u = 0;
+#pragma unroll
+        for (int hh = 0; hh < G; ++hh) {
+          const unsigned long long* a = p.bitmap + (size_t)(row0 + hh) * p.fb_stride + w;
+          const uint32_t v = (uint32_t)wait_tagged(a, x[hh], tag, pb);
+          hw[hh * nw + w] = v;
+          u |= v;
+        }
+        uw[w] = u;
+        cnt += __popc(u);
+      }
+      if (pb.dead) report(p.status, ADAKV_ST_WAIT_TIMEOUT);
+      fence_acq_rel_gpu();  // acquire: the appended K/V tokens are visible below
+    }
+    const int before = block_exclusive_scan(cnt, scan_scratch);
+    const int U = scan_scratch[32];
+    const int lo = (int)((int64_t)U * split / SPLIT), hi = (int)((int64_t)U * (split + 1) / SPLIT);
+    if (before < hi && before + cnt > lo) {
+      int rk = before;
+      for (int w = w0; w < w1 && rk < hi; ++w) {
+        uint32_t u = uw[w];
+        const int pc = __popc(u);
+        if (rk + pc <= lo) {
+          rk += pc;
+          continue;
+        }
+        while (u && rk < hi) {
+          const int bit = __ffs(u) - 1;
+          u &= u - 1u;
+          if (rk >= lo && rk - lo < p.slice_cap) list[rk - lo] = w * 32 + bit;
+          ++rk;
+        }
+      }
+    }
+    __syncthreads();
+    const int n = imin(hi - lo, p.slice_cap);
+    for (int i = tid; i < n; i += kStepThreads) {
+      const int id = list[i], w = id >> 5, bit = id & 31;
+      uint32_t m = 0;
+#pragma unroll
+      for (int hh = 0; hh < G; ++hh) m |= ((hw[hh * nw + w] >> bit) & 1u) << hh;
+      lmask[i] = m;
+    }
+    __syncthreads();
+
+    // ---- two-stage gather ring + tensor-core attention, NSLOT blocks per stage ----
+    const int NSLOT = p.nbt;
+    auto issue_kv = [&](int first, int stage) {
+      const int cntb = imin(NSLOT, n - first);
+      T* kb = kvbuf + (size_t)stage * 2 * NSLOT * BLK;
+      T* vb = kb + (size_t)NSLOT * BLK;
+      const int chunks = cntb * BS * ROWC;
+      for (int c = tid; c < chunks; c += kStepThreads) {
+        const int slot = c / (BS * ROWC);
+        const int rem = c - slot * (BS * ROWC);
+        const int tok = rem / ROWC, col = rem - tok * ROWC;
+        const int pos = list[first + slot] * BS + tok;
+        const bool valid = pos < S;
+        const int64_t srow_ = valid ? (int64_t)pos : 0;
+        const size_t off = (size_t)slot * BLK + tok * D + (col ^ (tok & 7)) * VEC;
+        cp_async16(kb + off, kbase + srow_ * p.k.ss + col * VEC, valid);
+        cp_async16(vb + off, vbase + srow_ * p.v.ss + col * VEC, valid);
+      }
+      cp_async_commit();
+    };
+    const int nbatch = ceil_div(n, NSLOT);
+    if (nbatch > 0) issue_kv(0, 0);
+    for (int bi = 0; bi < nbatch; ++bi) {
+      const int first = bi * NSLOT;
+      const int cntb = imin(NSLOT, n - first);
+      if (bi + 1 < nbatch) {
+        issue_kv(first + NSLOT, (bi + 1) & 1);
+        asm volatile("cp.async.wait_group 1;" ::: "memory");
+      } else {
+        cp_async_wait_all();
+      }
+      __syncthreads();
+      const T* kb = kvbuf + (size_t)(bi & 1) * 2 * NSLOT * BLK;
+      const T* vb = kb + (size_t)NSLOT * BLK;
+      for (int slot = warp; slot < cntb; slot += kSW) {
+        const int blk = list[first + slot];
+        const int tok_valid = imin(BS, S - blk * BS);
+        mma_block<T, D, BS>(acc, qa, smem_addr(kb + (size_t)slot * BLK), smem_addr(vb + (size_t)slot * BLK),
+                            lmask[first + slot], tok_valid, scale_log2, lane);
+      }
+      __syncthreads();  // this stage is refilled two batches later
+    }
+
+    // ---- warp partials -> this CTA's partial (m in log2 units, l, o) ----
+    {
+      float l0 = acc.l[0], l1 = acc.l[1];
+      l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+      l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+      l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+      l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+      float* mine = wpart + warp * G * (D + 2);
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const int r = gid + half * 8;
+        if (r < G) {
+          float* rp = mine + r * (D + 2);
+          if (tig == 0) {
+            rp[0] = acc.m[half];
+            rp[1] = half ? l1 : l0;
+          }
+#pragma unroll
+          for (int nn = 0; nn < MmaAcc<D>::NT; ++nn) {
+            rp[2 + nn * 8 + tig * 2] = acc.o[nn][half * 2];
+            rp[2 + nn * 8 + tig * 2 + 1] = acc.o[nn][half * 2 + 1];
+          }
+        }
+      }
+    }
+    __syncthreads();
+    unsigned long long* gpart = p.part + (size_t)cta * G * (D + 2);
+    for (int idx = tid; idx < G * D; idx += kStepThreads) {
+      const int hh = idx / D, dd = idx - hh * D;
+      float M = -INFINITY;
+      for (int w = 0; w < kSW; ++w) M = fmaxf(M, wpart[(w * G + hh) * (D + 2)]);
+      float Ls = 0.f, O = 0.f;
+      if (M != -INFINITY) {
+        for (int w = 0; w < kSW; ++w) {
+          const float* rp = wpart + (w * G + hh) * (D + 2);
+          const float f = (rp[0] == -INFINITY) ? 0.f : exp2f(rp[0] - M);
+          Ls += rp[1] * f;
+          O += rp[2 + dd] * f;
+        }
+      }
+      str_u64(gpart + hh * (D + 2) + 2 + dd, tword(tag, __float_as_uint(O)));
+      if (dd == 0) {
+        str_u64(gpart + hh * (D + 2), tword(tag, __float_as_uint(M)));
+        str_u64(gpart + hh * (D + 2) + 1, tword(tag, __float_as_uint(Ls)));
+      }
+    }
+
+    // ---- the group's first CTA merges the SPLIT partials in split order ----
+    if (split == 0) {
+      PollBudget pb{p.wait_ns, 0, false};
+      const unsigned long long* gp0 = p.part + (size_t)c_first * G * (D + 2);
+      const size_t stride = (size_t)G * (D + 2);
+      for (int hh = warp; hh < G; hh += kSW) {
+        float Mx = -INFINITY;
+        for (int s0 = lane; s0 < SPLIT; s0 += 32) {
+          const unsigned long long* a = gp0 + s0 * stride + hh * (D + 2);
+          const float m = __uint_as_float((uint32_t)wait_tagged(a, ldr_u64(a), tag, pb));
+          mf[s0 * G + hh] = m;
+          Mx = fmaxf(Mx, m);
+        }
+        Mx = warp_max(Mx);
+        float Ls = 0.f;
+        for (int s0 = lane; s0 < SPLIT; s0 += 32) {
+          const unsigned long long* a = gp0 + s0 * stride + hh * (D + 2) + 1;
+          const float l = __uint_as_float((uint32_t)wait_tagged(a, ldr_u64(a), tag, pb));
+          const float m = mf[s0 * G + hh];
+          const float f = (Mx == -INFINITY || m == -INFINITY) ? 0.f : exp2f(m - Mx);
+          mf[s0 * G + hh] = f;
+          Ls += l * f;
+        }
+        Ls = warp_sum(Ls);
+        if (lane == 0) {
+          mL[hh] = Ls;
+          ml[hh] = Mx;
+        }
+      }
+      __syncthreads();
+      for (int idx = tid; idx < G * D; idx += kStepThreads) {
+        const int hh = idx / D, dd = idx - hh * D;
+        const unsigned long long* src = gp0 + (size_t)hh * (D + 2) + 2 + dd;
+        float O = 0.f;
+        for (int s0 = 0; s0 < SPLIT; s0 += 16) {
+          unsigned long long v[16];
+#pragma unroll
+          for (int u = 0; u < 16; ++u) v[u] = s0 + u < SPLIT ? ldr_u64(src + (size_t)(s0 + u) * stride) : 0ull;
+#pragma unroll
+          for (int u = 0; u < 16; ++u)
+            if (s0 + u < SPLIT) {
+              const uint64_t x = wait_tagged(src + (size_t)(s0 + u) * stride, v[u], tag, pb);
+              O += mf[(s0 + u) * G + hh] * __uint_as_float((uint32_t)x);
+            }
+        }
+        const float Ls = mL[hh];
+        const float res = Ls > 0.f ? O / Ls : 0.f;
+        T* orow = static_cast<T*>(const_cast<void*>(p.out.data)) + b * p.out.sb + (int64_t)(kvh * G + hh) * p.out.sh;
+        orow[dd] = from_f32<T>(res);
+      }
+      if (p.lse && tid < G) {
+        const float M = ml[tid], Ls = mL[tid];
+        p.lse[row0 + tid] = (Ls > 0.f && M > -INFINITY) ? M * 0.6931471805599453f + logf(Ls) : -INFINITY;
+      }
+      if (pb.dead) report(p.status, ADAKV_ST_WAIT_TIMEOUT);
+    }
+  }
+
+  // ---------------------------------------------------------------- call tag
+  // The last CTA to finish advances the call counter (every CTA read it at
+  // its start), so the next call's words carry a new tag.
+  __syncthreads();
+  if (tid == 0) {
+    unsigned prev;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(p.epoch + 1) : "memory");
+    if (prev == (unsigned)(GRID - 1)) {
+      p.epoch[1] = 0u;
+      p.epoch[0] = tag;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// last step's block scores -> float rows (either path's layout)
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) step_scores_kernel(bool fused, const unsigned long long* fscores,
+                                                          int fs_stride, const float* scores,
+                                                          int score_stride, int nb, float* out,
+                                                          int out_stride) {
+  const int r = blockIdx.x;
+  for (int j = threadIdx.x; j < nb; j += blockDim.x) {
+    float v;
+    if (fused) v = __uint_as_float((uint32_t)fscores[(size_t)r * fs_stride + j]);
+    else v = scores[(size_t)r * score_stride + j];
+    out[(size_t)r * out_stride + j] = v;
+  }
+}
+
+cudaError_t launch_step_scores(bool fused, const unsigned long long* fscores, int fs_stride,
+                               const float* scores, int score_stride, int rows, int nb, float* out,
+                               int out_stride, cudaStream_t st) {
+  step_scores_kernel<<<rows, 256, 0, st>>>(fused, fscores, fs_stride, scores, score_stride, nb, out,
+                                           out_stride);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+template <typename F>
+static cudaError_t for_each_step(int dtype, int D, int g, F&& f) {
+#define ADAKV_STEP_CASE(TT, DD, GG) \
+  if (D == DD && g == GG) return f(step_kernel<TT, DD, GG>);
+#define ADAKV_STEP_T(TT) ADAKV_STEP_CASE(TT, 128, 4) ADAKV_STEP_CASE(TT, 128, 8)
+  if (dtype == ADAKV_DTYPE_BF16) {
+    ADAKV_STEP_T(__nv_bfloat16)
+  } else if (dtype == ADAKV_DTYPE_F16) {
+    ADAKV_STEP_T(__half)
+  }
+#undef ADAKV_STEP_T
+#undef ADAKV_STEP_CASE
+  return cudaErrorInvalidValue;
+}
+
+bool step_kernel_built(int dtype, int D, int bs, int g) {
+  return (dtype == ADAKV_DTYPE_BF16 || dtype == ADAKV_DTYPE_F16) && D == 128 && bs == 16 &&
+         (g == 4 || g == 8);
+}
+
+size_t step_smem_bytes(int D, int g, int nb_max, int min_split, int* nbt, int* slice_cap) {
+  const int sc = ceil_div(imax(nb_max, 1), imax(min_split, 1)) + 1;
+  int t = 8;
+  StepSmem s = step_smem_layout(D, g, nb_max, t, sc);
+  while (s.total > kStepSmemMax && t > 1) {
+    --t;
+    s = step_smem_layout(D, g, nb_max, t, sc);
+  }
+  if (nbt) *nbt = t;
+  if (slice_cap) *slice_cap = sc;
+  return s.total;
+}
+
+cudaError_t step_kernels_init() {
+  for (int dt : {ADAKV_DTYPE_F16, ADAKV_DTYPE_BF16})
+    for (int g : {4, 8}) {
+      cudaError_t e = for_each_step(dt, 128, g, [](auto kern) {
+        return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kStepSmemMax);
+      });
+      if (e != cudaSuccess) return e;
+    }
+  return cudaSuccess;
+}
+
+cudaError_t launch_step(const StepParams& p, int dtype, int D, int g, int grid, size_t smem,
+                        cudaStream_t st, const LaunchOpts& o) {
+  return for_each_step(dtype, D, g, [&](auto kern) {
+    return launch_ex(kern, dim3(grid), dim3(kStepThreads), smem, st, o, p);
+  });
+}
+
+}  // namespace adakv

@@ -165,6 +165,7 @@ def adakv_attention_forward(module, query, key, value, attention_mask, scaling, 
         sel_lens = torch.empty((B * Hq,), dtype=torch.int32, device=query.device)
         out = torch.empty((B, 1, Hq, D), dtype=query.dtype, device=query.device)
         ws = _lib.workspace(L.adakv_plan_workspace_bytes(geo, sp), query.device)
+        _lib.raise_if_failed(ws)  # a failure an earlier call reported (host read, no sync)
         q3 = query[:, :, 0, :]
         if q3.stride(-1) != 1:
             q3 = q3.contiguous()

@@ -43,11 +43,17 @@ def round_to_dtype(x: np.ndarray, dtype: str) -> np.ndarray:
     if dtype == "fp16":
         return x.astype(np.float16).astype(np.float32)
     if dtype == "bf16":
-        u = x.view(np.uint32).astype(np.uint64)
+        # round to nearest even on the upper 16 bits; in uint32 arithmetic only
+        # NaN patterns can wrap, and those are restored below
+        u = x.view(np.uint32)
+        r = (u >> np.uint32(16)) & np.uint32(1)
+        r += np.uint32(0x7FFF)
+        r += u
+        r &= np.uint32(0xFFFF0000)
+        out = r.view(np.float32)
         nan = np.isnan(x)
-        u = (u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000
-        out = u.astype(np.uint32).view(np.float32)
-        out[nan] = np.nan
+        if nan.any():
+            out[nan] = np.nan
         return out
     raise ValueError(f"unknown dtype {dtype!r}")
 

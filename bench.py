@@ -9,12 +9,15 @@ synthetic K/V/q with planted retrieval blocks (even KV heads) and recency-biased
 local heads (odd KV heads).  The headline is the 131072-token context; 32768 and
 65536 are reported beside it.
 
-One step = append one token (in-place K/V write + trailing-centroid refresh,
-fused into the estimator), centroid estimator, entropy budget + top-k
-selection, ragged split-KV attention over the GQA union: 3 kernels chained
-with programmatic dependent launch.  As in a model forward pass, 8 independent
-layer states are stepped in one CUDA graph (working set > L2); the timed
-region replays it back to back.
+One step = append one token (in-place K/V write + trailing-centroid refresh),
+centroid estimator, entropy budget + top-k selection, ragged split-KV
+attention over the GQA union, all in one persistent kernel launch (the
+three-kernel chain runs where that kernel does not apply, or with
+ADAKV_FUSED=0).  As in a model forward pass, 8 independent layer states are
+stepped in turn inside one CUDA graph (working set > L2).  Each step reads
+nothing before the previous kernel on the stream has completed
+(griddepcontrol.wait first), so consecutive steps never overlap; a chain
+where each layer's query is the previous layer's output is timed beside it.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
@@ -42,16 +45,29 @@ METRIC = ("µs per decode attention step at 32K/128K/1M ctx; achieved HBM GB/s v
           "roofline")
 CFG = dict(Hq=32, Hkv=8, D=128, bs=16, avg=64, k_min=2, k_max=512, sink=1, local=4, c_min=1)
 HEADLINE_S = 131072
-KERNELS_PER_STEP = 3
 L2_FLUSH_BYTES = 256 << 20
-# DRAM bytes (read + write) of one decode step at each context, summed over the
-# three kernels of one ncu --set full capture (profiles/decode_step_128k_kernels.md)
-NCU_STEP_TRAFFIC = {131072: 33_661_440 + 2_195_456 + 8_765_184}
+MIN_TIMED_S = 0.25  # the K timed steps are repeated until the timed region lasts this long
+# DRAM bytes (read + write) of one decode step at 128K from one ncu capture of
+# the step (dram__bytes_read.sum + dram__bytes_write.sum); None until captured
+NCU_STEP_TRAFFIC = {}
 
 
 def workload_name(S):
     return (f"cfg1 Llama-3.1-8B attention decode: batch 1, 32 q / 8 KV heads, head_dim 128, "
             f"ctx {S}, block 16, avg_budget 64, k_max 512, entropy budget, bf16")
+
+
+def bench_config(S, world, layers=8):
+    """The ``config`` of both arms' JSON lines (one dict, same keys)."""
+    return {"workload": workload_name(S),
+            "parallelism": f"replicas x{world} (batch-1 per GPU, no collective)",
+            "l2": (f"inputs larger than L2: {layers} independent layer states (own K/V cache + "
+                   "fp32 centroid table) stepped in turn"),
+            "timing": ("CUDA events around the K timed steps (a CUDA graph of layer steps, "
+                       f"repeated until the region lasts >= {MIN_TIMED_S} s); value = elapsed / "
+                       "steps timed. us_isolated_median = one step alone after an L2 flush, launch "
+                       "included; us_dependent = steps where each layer's query is the previous "
+                       "layer's output")}
 
 
 # ---------------------------------------------------------------------------
@@ -195,18 +211,44 @@ def run_ours(S, steps, warmup, seed, device, layers=8, pool=16, e2e_steps=None):
         for _ in range(2):
             step(li)
     torch.cuda.synchronize(device)
+    kernels_per_step = 1 if decs[0].last_path() == 2 else 3
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph):
         for li in range(layers):
             step(li)
+    full, rest = divmod(steps, layers)
+    tail = None
+    if rest:
+        tail = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(tail):
+            for li in range(rest):
+                step(li)
     one = torch.cuda.CUDAGraph()
     with torch.cuda.graph(one):
         step(0)
+    # dependency chain: each layer's query is the previous layer's output
+    dep = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(dep):
+        q_in = bufs[0][0]
+        for li in range(layers):
+            _, kt, vt = bufs[li]
+            q_in = decs[li].step(q_in, k_new=kt, v_new=vt, advance=False)
 
-    reps = max(1, -(-steps // layers))
+    def timed_steps():  # exactly `steps` decode steps
+        for _ in range(full):
+            graph.replay()
+        if tail is not None:
+            tail.replay()
+
     for _ in range(max(warmup, 3)):
         graph.replay()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    timed_steps()
+    b.record(stream)
     torch.cuda.synchronize(device)
+    est = max(a.elapsed_time(b) * 1e-3, 1e-6)
+    reps = max(1, int(np.ceil(MIN_TIMED_S / est)))
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
           for _ in range(reps)]
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -214,20 +256,34 @@ def run_ours(S, steps, warmup, seed, device, layers=8, pool=16, e2e_steps=None):
         t0.record(stream)
         for r in range(reps):
             ev[r][0].record(stream)
-            graph.replay()
+            timed_steps()
             ev[r][1].record(stream)
         t1.record(stream)
         torch.cuda.synchronize(device)
     clocks = clk.summary()
     total_us = t0.elapsed_time(t1) * 1000.0
-    per_replay = [s.elapsed_time(e) * 1000.0 / layers for s, e in ev]
-    timed_steps = reps * layers
+    per_rep = [x.elapsed_time(y) * 1000.0 / steps for x, y in ev]
+    timed_steps_n = reps * steps
+
+    dep_reps = max(3, min(200, reps * full))
+    for _ in range(3):
+        dep.replay()
+    d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    d0.record(stream)
+    for _ in range(dep_reps):
+        dep.replay()
+    d1.record(stream)
+    torch.cuda.synchronize(device)
+    us_dep = d0.elapsed_time(d1) * 1000.0 / (dep_reps * layers)
+    for dec in decs:
+        if dec.status() != 0:
+            raise RuntimeError("device status flags set during the timed steps")
 
     # isolated single step: L2 flushed (write then read a 256 MB buffer, leaving
     # L2 clean), one graph launch of one step between two events
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
     iso = []
-    for r in range(min(200, steps) + 3):
+    for r in range(min(200, max(steps, 20)) + 3):
         flush.zero_()
         flush.sum(dtype=torch.int64)
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -258,7 +314,7 @@ def run_ours(S, steps, warmup, seed, device, layers=8, pool=16, e2e_steps=None):
         out = dec.step(qd, k_new=ktd, v_new=vtd, advance=False)
         out_h.copy_(out, non_blocking=True)
 
-    n_e2e = e2e_steps or min(steps, 500)
+    n_e2e = e2e_steps or min(max(steps, 50), 500)
     e2e = []
     for r in range(n_e2e + 3):
         flush.zero_()
@@ -273,9 +329,10 @@ def run_ours(S, steps, warmup, seed, device, layers=8, pool=16, e2e_steps=None):
     us_e2e = [a.elapsed_time(b) * 1000.0 for a, b in e2e]
     h2d = in_h[0].numel() * 2
     d2h = out_h.numel() * 2
-    return dict(us_step=total_us / timed_steps, us_replay=per_replay, us_iso=iso_us, us_e2e=us_e2e,
-                bytes=bytes_per_step, detail=detail, clocks=clocks, h2d=h2d, d2h=d2h,
-                steps=timed_steps, e2e_steps=n_e2e, layers=layers)
+    return dict(us_step=total_us / timed_steps_n, us_replay=per_rep, us_iso=iso_us, us_e2e=us_e2e,
+                us_dep=us_dep, bytes=bytes_per_step, detail=detail, clocks=clocks, h2d=h2d,
+                d2h=d2h, steps=steps, reps=reps, e2e_steps=n_e2e, layers=layers,
+                kernels_per_step=kernels_per_step)
 
 
 # ---------------------------------------------------------------------------
@@ -466,6 +523,46 @@ def run_cfg2(steps, warmup, world, rank, device, seed=0):
     return a.elapsed_time(b) * 1000.0 / steps, nbytes
 
 
+def run_partitioned(steps, warmup, world, rank, device, seed):
+    """cfg2 (ragged batch of 64 split by sequence, no collective) and cfg4 (one
+    1M-token sequence sharded over the ranks) at this world size: whole-job
+    us per step (max over ranks) and the fraction of the aggregate HBM
+    roofline (measured copy bandwidth x ranks)."""
+    import torch
+    import torch.distributed as dist
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except OSError:
+        pass
+    peak = float(peaks.get("hbm_gbs", 6650.0))
+    out = {}
+    for name in ("cfg2", "cfg4"):
+        n = min(steps, 200)
+        torch.cuda.synchronize(device)
+        if name == "cfg2":
+            us, nbytes = run_cfg2(n, warmup, world, rank, device, seed)
+        else:
+            us, nbytes = run_cfg4(n, warmup, world, rank, device)
+        if world > 1:
+            t = torch.tensor([us, float(nbytes)], device=device, dtype=torch.float64)
+            dist.all_reduce(t[:1], op=dist.ReduceOp.MAX)
+            if name == "cfg2":
+                dist.all_reduce(t[1:], op=dist.ReduceOp.SUM)
+            us, nbytes = float(t[0]), float(t[1])
+        achieved = nbytes / (us * 1e-6) / 1e9
+        out[name] = {"us": us, "n": world, "achieved_gbs": achieved,
+                     "frac": achieved / (peak * world), "bytes_per_step": nbytes, "steps": n,
+                     "scaling": "strong"}
+        torch.cuda.empty_cache()
+    out["cfg2"]["workload"] = (f"ragged batch {CFG2['B']}, contexts U[{CFG2['lo']}, {CFG2['hi']}], "
+                               f"avg_budget {CFG2['avg']}, split by sequence, no collective")
+    out["cfg4"]["workload"] = (f"one {CFG4['S']}-token sequence, {CFG4['Hq']} q / {CFG4['Hkv']} KV "
+                               f"heads, avg_budget {CFG4['avg']}, sequence-sharded")
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -481,6 +578,8 @@ def main():
     ap.add_argument("--workload", choices=["cfg1", "cfg2", "cfg4"], default="cfg1",
                     help="cfg2: ragged batch of 64 split by sequence; cfg4: one 1M-token "
                          "sequence sharded over the ranks (neither is the headline)")
+    ap.add_argument("--no-partitioned", action="store_true",
+                    help="skip the cfg2 / cfg4 measurements reported beside the headline")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -497,9 +596,10 @@ def main():
         times = times[warm:] if len(times) > warm + 1 else times[-1:]  # untimed warm-up steps
         v = float(np.mean(times))
         line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "us", "n_gpus": args.gpus,
-                "steps": len(times), "warmup": warm, "ms_per_step": v / 1000.0,
+                "steps": len(times), "repeats": 1, "warmup": warm, "ms_per_step": v / 1000.0,
                 "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-                "data": "synthetic", "config": {"workload": workload_name(headline)},
+                "data": "synthetic (seeded Gaussian K/V/q, planted retrieval blocks, recency heads)",
+                "config": bench_config(headline, args.gpus, args.layers),
                 "cpu_baseline": {"value": v, "unit": "us", "cores": threads, "kind": "port",
                                  "sample": f"{len(times)} full decode steps at ctx {headline} "
                                            f"(NumPy oracle port, {threads} threads over KV heads)"},
@@ -601,6 +701,10 @@ def main():
         results[S] = r
         torch.cuda.empty_cache()
 
+    partitioned = None
+    if not args.no_partitioned:
+        partitioned = run_partitioned(args.steps, args.warmup, world, rank, device, args.seed)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         times = run_cpu(headline, args.seed, 10_000, args.cpu_seconds, 1)
@@ -623,36 +727,35 @@ def main():
         for S, rr in results.items():
             a = rr["bytes"] / (rr["mean_us"] * 1e-6) / 1e9
             ctx[str(S)] = {"us": rr["mean_us"],
-                           "us_replay_median": float(np.median(rr["us_replay"])),
+                           "us_repeat_median": float(np.median(rr["us_replay"])),
                            "us_isolated_median": float(np.median(rr["us_iso"])),
+                           "us_dependent": rr["us_dep"],
+                           "kernels_per_step": rr["kernels_per_step"],
                            "e2e_us": rr["e2e_us"],
                            "bytes_per_step": rr["bytes"], "achieved_gbs": a, "frac": a / peak,
                            **{k: v2 for k, v2 in rr["detail"].items()}}
         line = {
             "metric": METRIC, "value": v, "unit": "us", "n_gpus": world, "steps": r["steps"],
+            "repeats": r["reps"],
             "warmup": args.warmup, "ms_per_step": v / 1000.0, "higher_is_better": False,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded Gaussian K/V/q, planted retrieval blocks, recency heads)",
-            "config": {"workload": workload_name(headline),
-                       "parallelism": f"replicas x{world} (batch-1 per GPU, no collective)",
-                       "l2": (f"inputs larger than L2: {r['layers']} independent layer states "
-                              "(own K/V cache + fp32 centroid table) stepped in turn"),
-                       "timing": (f"CUDA events around back-to-back replays of one CUDA graph of "
-                                  f"{r['layers']} layer steps (3 kernels each); value = elapsed / "
-                                  "steps. us_isolated_median = one step alone after an L2 flush, "
-                                  "launch included")},
+            "config": bench_config(headline, world, r["layers"]),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": NCU_STEP_TRAFFIC.get(headline),
-                         "scope": "whole decode step (all 3 kernels); bytes = fp32 centroid "
-                                  "table + union of selected K/V blocks per KV head + append",
+                         "scope": (f"whole decode step ({r['kernels_per_step']} kernel launch"
+                                   f"{'es' if r['kernels_per_step'] > 1 else ''}); bytes = fp32 "
+                                   "centroid table + union of selected K/V blocks per KV head + "
+                                   "append"),
                          "peak_source": "MEASURED_PEAKS.json hbm_gbs" if peaks else "fallback"},
             "cpu_baseline": cpu,
             "e2e": {"value": r["e2e_us"], "unit": "us", "h2d_bytes_per_step": r["h2d"],
                     "d2h_bytes_per_step": r["d2h"],
                     "path": "BatchedDecoder.step with the new token (C ABI adakv_decode_step), pinned host q/k/v in, out back"},
-            "gpu_launches": KERNELS_PER_STEP * r["steps"],
+            "gpu_launches": r["kernels_per_step"] * r["steps"] * r["reps"],
             "clocks": r["clocks"],
             "contexts": ctx,
+            "partitioned": partitioned,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

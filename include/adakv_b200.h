@@ -19,11 +19,21 @@
  *   - Every function returns ADAKV_OK (0) or an error code; the message of
  *     the last error on the calling thread is returned by adakv_last_error().
  *     Arguments are validated on the host before anything is launched.
- *   - Pointers are device pointers unless stated otherwise.  Nothing here
+ *   - Pointers are device pointers unless stated otherwise.  No call
  *     allocates device memory: scratch lives in a caller-provided workspace
  *     (size from adakv_*_workspace_bytes, zero-filled once before first use;
- *     it keeps no state a later call depends on beyond a call counter).
- *     Calls that share a workspace must be ordered on one stream.
+ *     it keeps no state a later call depends on beyond call counters).
+ *     Calls that share a workspace must be ordered on one stream.  The one
+ *     exception is adakv_attend_noalloc's scratch: a fixed 4 MiB __device__
+ *     array of the library, present on every device the library's device
+ *     code is loaded on (4 MiB of device memory each), whether or not that
+ *     entry point is ever called.
+ *   - Inputs (q, K/V, centroids, seq_lens, tables) must be complete when the
+ *     call is enqueued: the decode kernels use programmatic dependent launch
+ *     and some of them read their inputs before waiting for the previous
+ *     kernel on the stream to finish, so a producer of those inputs must not
+ *     itself be a kernel that triggers its dependents early (before its last
+ *     write).  The one-kernel adakv_decode_step reads nothing before that wait.
  *   - All work is enqueued on `stream` (a cudaStream_t passed as void*); no
  *     function synchronises the host except adakv_read_status.
  *   - Tensors are [batch, heads, tokens, head_dim] views described by
@@ -195,11 +205,13 @@ int adakv_estimate_minmax(const adakv_geometry* geo, const adakv_view* q, const 
  *
  * For callers that cannot hand over device memory: a serving engine that has
  * given all free memory to its KV-cache pool, or a host language with no
- * device allocator at hand.  The scratch (status word + selection bitmaps)
- * is a fixed 4 MiB array inside this library, one per device; a geometry
- * needing more than batch * n_q_heads * ceil(nb_cap / 32) * 4 + 512 <= 4 MiB
- * bytes is rejected with ADAKV_ERR_INVALID.  Nothing is allocated on the
- * device.  The first call on each device looks the array up (and may load
+ * device allocator at hand.  The scratch (status word, selection bitmaps,
+ * split-KV partials, arrival counters) is a fixed 4 MiB array inside this
+ * library, one per device; a call needs exactly
+ * adakv_attend_workspace_bytes(geo, table_width) bytes of it, and a geometry
+ * needing more than 4 MiB is rejected with ADAKV_ERR_INVALID (batch 1 at 128K
+ * tokens, 32 q / 8 KV heads, D 128, needs about 0.33 MiB).  Nothing is
+ * allocated on the device by the call.  The first call on each device looks the array up (and may load
  * the library's device code): make that first call before any stream capture.
  * The scratch is shared, so two calls in flight at once on one device (other
  * streams, other threads) race and corrupt each other; order them on one
@@ -229,6 +241,42 @@ int adakv_decode_step(const adakv_geometry* geo, const adakv_select_params* sp,
 /* Synchronise `stream`, copy the workspace's device status word (ADAKV_ST_*
  * bits) to *status and clear it. */
 int adakv_read_status(void* workspace, uint32_t* status, void* stream);
+
+/* Let the kernels that use `workspace` also write their ADAKV_ST_* bits to
+ * `host_word`, a page-locked host word mapped into the device address space
+ * (cudaHostAlloc / cudaHostRegister with mapping; NULL detaches).  A host
+ * can then notice a failed step without synchronising: the word stays 0
+ * until some kernel reports.  Synchronises `stream` once (set-up call).
+ * No counterpart in the reference (its errors are host exceptions). */
+int adakv_set_status_sink(void* workspace, uint32_t* host_word, void* stream);
+
+/* Block scores (q . centroid, float32, unscaled) of the last adakv_plan or
+ * adakv_decode_step enqueued on `workspace`, into
+ * scores_out[(b * Hq + h) * score_stride + j] for j < ceil(max_seq_len / block_size).
+ * The scores the reference's plan_selection computes
+ * (adakv/attention.py:187-189), for inspection and tests. */
+int adakv_read_scores(const adakv_geometry* geo, void* workspace, size_t workspace_bytes,
+                      float* scores_out, int32_t score_stride, void* stream);
+
+/* How the last adakv_plan / adakv_decode_step enqueued on `workspace` ran:
+ * 0 nothing yet, 1 as the estimator / plan / attend kernel chain (three
+ * launches; adakv_plan: two), 2 as the one-kernel decode step.  Host-side
+ * bookkeeping, no device access. */
+int adakv_last_path(const void* workspace);
+
+/* Test-only knobs, process-wide, all off (0) by default.  No counterpart in
+ * the reference.
+ *   ADAKV_KNOB_WAIT_NS    bound of every bounded device wait, in ns (0: 200 ms)
+ *   ADAKV_KNOB_FLAGS      bit 0: the entropy of query head 0 of sequence 0 is
+ *                         never published, so the per-sequence exchange of the
+ *                         budget waits out its bound (failure-detection tests)
+ *   ADAKV_KNOB_STEP_PATH  adakv_decode_step: 0 picks the one-kernel step when
+ *                         it applies, 1 forces the three-kernel chain, 2
+ *                         prefers the one-kernel step even when ADAKV_FUSED=0 */
+#define ADAKV_KNOB_WAIT_NS 1
+#define ADAKV_KNOB_FLAGS 2
+#define ADAKV_KNOB_STEP_PATH 3
+int adakv_debug_knob(int32_t knob, int64_t value);
 
 /* ---- sequence-sharded decode (one sequence's blocks split over GPUs) ----
  * The reference decodes one sequence on one device; these four calls split

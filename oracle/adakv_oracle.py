@@ -345,7 +345,7 @@ def decode_step(q, K, V, block_size=16, avg_budget=8, k_min=2, k_max=64,
 # --------------------------------------------------------------------------
 def compare_selection(scores, k_oracle, raw_oracle, mask_oracle, sets_gpu,
                       n_sink_blocks, n_local_blocks, c_min,
-                      score_rel_tol=1e-6, budget_tol=1e-4):
+                      score_rel_tol=1e-6, budget_tol=1e-5):
     """Classify GPU-vs-oracle selection differences head by head.
 
     Returns ``(n_exact, n_budget_near_ties, n_score_near_ties, failures)``.
@@ -354,7 +354,9 @@ def compare_selection(scores, k_oracle, raw_oracle, mask_oracle, sets_gpu,
 
     * budget near-tie: the counts differ by one and the oracle's unrounded
       budget ``lo + extra`` lies within ``budget_tol`` of a ``.5`` rounding
-      boundary (the GPU sums the entropy in a different order);
+      boundary (the GPU sums the entropy in a different order: the weights
+      agree to about 1e-7 relative, which moves a raw budget of ~64 by well
+      under 1e-5);
     * score near-tie: the blocks in the symmetric difference all have
       scores within ``score_rel_tol`` (relative) of each other.
     """

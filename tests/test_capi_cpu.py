@@ -156,3 +156,58 @@ def test_missing_library_fails_loudly(monkeypatch, tmp_path):
     monkeypatch.setattr(_lib, "_lib", None)
     with pytest.raises(RuntimeError, match="no CPU fallback"):
         _lib.lib()
+
+
+def test_more_than_128_query_heads_are_rejected(lib):
+    """The per-sequence entropy exchange covers at most 128 query heads: a larger
+    geometry must fail on the host instead of dropping heads from the budget."""
+    assert lib.adakv_plan_workspace_bytes(geo(n_q_heads=160, n_kv_heads=10), params()) == 0
+    assert "128" in lib.adakv_last_error().decode()
+    q = _lib.View(0x1000, 4096, 128, 0)
+    rc = lib.adakv_decode_step(geo(n_q_heads=256, n_kv_heads=16), params(), q, q, q, None, None, 0,
+                               0x1000, None, 0.1, 0x1000, 512, 0x1000, q, 0x1000, 1 << 30, None)
+    assert rc == _lib.ERR_UNSUPPORTED and "128" in lib.adakv_last_error().decode()
+    assert lib.adakv_plan_workspace_bytes(geo(n_q_heads=128, n_kv_heads=8), params()) > 0
+
+
+def test_debug_knobs_validate_and_reset(lib):
+    assert lib.adakv_debug_knob(99, 1) == _lib.ERR_INVALID
+    assert lib.adakv_debug_knob(_lib.KNOB_WAIT_NS, -5) == _lib.ERR_INVALID
+    assert lib.adakv_debug_knob(_lib.KNOB_STEP_PATH, 3) == _lib.ERR_INVALID
+    for knob, v in ((_lib.KNOB_WAIT_NS, 1000), (_lib.KNOB_FLAGS, 1), (_lib.KNOB_STEP_PATH, 1)):
+        assert lib.adakv_debug_knob(knob, v) == _lib.OK
+        assert lib.adakv_debug_knob(knob, 0) == _lib.OK
+
+
+def test_read_scores_and_status_sink_validate_on_the_host(lib):
+    g = geo()
+    ws = lib.adakv_plan_workspace_bytes(g, params())
+    # nothing has run on this (fake, aligned) workspace address
+    assert lib.adakv_read_scores(g, 0x100000, ws, 0x1000, 256, None) == _lib.ERR_INVALID
+    assert "no decode step" in lib.adakv_last_error().decode()
+    assert lib.adakv_read_scores(g, 0x100000, ws, 0x1000, 10, None) == _lib.ERR_INVALID
+    assert lib.adakv_read_scores(g, 0x100000, 64, 0x1000, 256, None) == _lib.ERR_INVALID
+    assert lib.adakv_set_status_sink(None, None, None) == _lib.ERR_INVALID
+
+
+def test_one_kernel_step_workspace_covers_its_regions(lib):
+    """Geometries the one-kernel step takes get its tagged-word regions too:
+    scores (8 bytes per block and head), bitmaps and per-CTA partials."""
+    small = lib.adakv_plan_workspace_bytes(geo(dtype=_lib.DTYPE_F32), params())
+    fused = lib.adakv_plan_workspace_bytes(geo(), params())
+    assert fused > small + 32 * 256 * 8
+
+
+def test_noalloc_limit_counts_the_split_kv_partials(lib):
+    """adakv_attend_noalloc's 4 MiB limit is adakv_attend_workspace_bytes: a
+    geometry whose bitmaps alone are far below it but whose split-KV partials
+    push it over is rejected on the host, with that byte count in the message."""
+    g = geo(batch=128, n_q_heads=32, n_kv_heads=8, max_seq_len=65536, nb_cap=4096)
+    need = lib.adakv_attend_workspace_bytes(g, 64)
+    bitmaps = 128 * 32 * ((4096 + 31) // 32) * 4
+    assert bitmaps + 512 < (4 << 20) < need
+    v = _lib.View(0x1000, 1 << 20, 1 << 16, 128)
+    rc = lib.adakv_attend_noalloc(g, v, v, v, 0x1000, 64, 0x1000, None, 0.1, v, None, None)
+    assert rc == _lib.ERR_INVALID
+    msg = lib.adakv_last_error().decode()
+    assert str(need) in msg and "adakv_attend_workspace_bytes" in msg

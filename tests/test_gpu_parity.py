@@ -334,6 +334,20 @@ def test_reference_api_shapes_and_semantics():
     for h in range(Hq):
         ids = set(bt[h, : int(sl[h])].tolist())
         assert {0, 1, nb - 3, nb - 2, nb - 1} <= ids, "sink + local blocks are forced"
+    # the reference's table format (attention.py:229-244): width max_sel, forced
+    # blocks first, then descending score
+    assert bt.shape[1] == int(sl.max())
+    ref_scores = O.block_scores(case.q[0], O.build_centroids(case.K[0], bs))
+    for h in range(Hq):
+        row = bt[h, : int(sl[h])].tolist()
+        assert row[:5] == [0, 1, nb - 3, nb - 2, nb - 1], row[:6]
+        sc = ref_scores[h, row[5:]]
+        assert np.all(np.diff(sc) <= 1e-6 * max(np.abs(sc).max(), 1e-30)), "not descending"
+    bta, sla = plan_selection(q, cache, avg_budget=6, n_sink_blocks=2, n_local_blocks=3,
+                              order="ascending")
+    assert torch.equal(sla, sl)
+    for h in range(Hq):
+        assert sorted(bt[h, : int(sl[h])].tolist()) == bta[h, : int(sl[h])].tolist()
     # full budget == dense attention
     out = adakv_decode_attention(q, cache, avg_budget=nb, k_min=nb, k_max=nb)
     dense = O.dense_attention(case.q[0], case.K[0], case.V[0])

@@ -63,10 +63,21 @@ def test_emulated_shards_match_single_gpu(world):
         assert np.array_equal(np.sort(bt[h, : sl[h]]), sets1[h]), f"head {h}"
     err = (out.float() - out1.float()).abs().max().item()
     assert err < BF16_TOL, f"max abs err vs single GPU {err:.3e}"
-    # against the oracle at this size too
+    # against the oracle at this size too: the selection (up to classified
+    # near-ties) and the output over the selected blocks
     ref = O.decode_step(case.q[0], case.K[0], case.V[0], block_size=bs, **kw)
-    err_o = np.abs(out.float().cpu().numpy() - ref["out"]).max()
+    sets = [bt[h, : sl[h]] for h in range(Hq)]
+    _, _, _, fails = O.compare_selection(ref["scores"], ref["k"], ref["raw"], ref["mask"], sets,
+                                         1, 4, 1)
+    assert not fails, f"selection differs from the oracle: {fails[:3]}"
+    mask = np.zeros_like(ref["mask"])
+    for h in range(Hq):
+        mask[h, sets[h]] = True
+    want = O.attend_mask(case.q[0], case.K[0], case.V[0], mask, bs)
+    err_o = np.abs(out.float().cpu().numpy() - want).max()
     assert err_o < BF16_TOL, f"max abs err vs oracle {err_o:.3e}"
+    exact = np.all(mask == ref["mask"], axis=1)
+    assert np.abs(out.float().cpu().numpy()[exact] - ref["out"][exact]).max() < BF16_TOL
 
 
 def test_cfg4_shape_1m_tokens_sharded_8_ways():
