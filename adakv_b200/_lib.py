@@ -90,6 +90,8 @@ _SIGNATURES = {
                                          _vp]),
     "adakv_debug_knob": (ctypes.c_int, [ctypes.c_int32, ctypes.c_int64]),
     "adakv_last_path": (ctypes.c_int, [_vp]),
+    "adakv_debug_timeline": (ctypes.c_int, [_P(Geometry), _vp, ctypes.c_size_t, _vp, ctypes.c_int32,
+                                            _vp]),
 }
 
 KNOB_WAIT_NS, KNOB_FLAGS, KNOB_STEP_PATH = 1, 2, 3

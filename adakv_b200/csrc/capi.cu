@@ -52,6 +52,7 @@ struct DeviceState {
   int num_sms = 0;
   bool step_ok = false;                            // the one-kernel step can run one CTA per SM
   std::map<int, int> plan_ctas;                    // nb_max * 16 + cluster -> resident plan clusters
+  std::map<std::tuple<int, int, int, size_t>, int> step_clusters;  // (dtype, g, csize, smem) -> resident
 };
 
 // Test-only knobs (adakv_debug_knob), all off by default.
@@ -205,9 +206,10 @@ int attend_split(const adakv_geometry* g) {
 struct WsLayout {
   size_t status, epoch, slots, scores, stats, bitmap, part, counters, bytes;
   int score_stride, stats_stride, bm_words, split;
-  // one-kernel step (present when the geometry can take it)
+  // one-kernel step (present when the geometry can take it); its state words
+  // sit at a fixed offset, its regions depend on B, Hq, Hkv, D and nb_cap only
   bool fused;
-  size_t fepoch, fscores, fhslot, fbitmap, fpart;
+  size_t fstate, fscores, fhslot, fbitmap, fready, fpart, fpready, ftimeline, fbegin, fend;
   int fs_stride, fb_stride;
 };
 
@@ -229,7 +231,22 @@ WsLayout make_ws(const adakv_geometry* g, bool with_plan) {
   size_t o = 0;
   auto take = [&](size_t bytes) { size_t at = o; o = align_up(o + bytes, 256); return at; };
   L.status = take(16);
+  L.fstate = take(32);  // one-kernel step: calls completed, CTAs done, arrival counter
   L.epoch = take(16);
+  L.fused = with_plan && step_geometry_ok(g);
+  L.fbegin = o;
+  if (L.fused) {
+    L.fs_stride = (int)align_up((size_t)g->nb_cap, 4);
+    L.fb_stride = (int)align_up((size_t)ceil_div(g->nb_cap, 32), 2);
+    L.fscores = take(4 * (size_t)rows * L.fs_stride);
+    L.fhslot = take(8 * (size_t)rows);
+    L.fbitmap = take(4 * (size_t)rows * L.fb_stride);
+    L.fready = take(8 * (size_t)rows * 8);  // one word per cluster rank (<= 8)
+    L.fpart = take(4 * (size_t)kStepMaxGrid * gq * (g->head_dim + 2));
+    L.fpready = take(8 * (size_t)kStepMaxGrid);
+    L.ftimeline = take(8 * (size_t)kStepMaxGrid * kStepTimelineSlots);
+  }
+  L.fend = o;
   L.slots = with_plan ? take(sizeof(PlanSlot) * rows * kPlanSlotsPerRow) : 0;
   L.scores = with_plan ? take(sizeof(float) * (size_t)rows * L.score_stride) : 0;
   L.stats_stride = ceil_div(g->nb_cap, kEstRows) * kEstConsumerWarps + 1;
@@ -237,16 +254,6 @@ WsLayout make_ws(const adakv_geometry* g, bool with_plan) {
   L.bitmap = take(sizeof(uint32_t) * (size_t)rows * L.bm_words);
   L.part = take(sizeof(float) * (size_t)g->batch * g->n_kv_heads * L.split * gq * (g->head_dim + 2));
   L.counters = take(sizeof(uint32_t) * (size_t)g->batch * g->n_kv_heads);
-  L.fused = with_plan && step_geometry_ok(g);
-  if (L.fused) {
-    L.fs_stride = (int)align_up((size_t)g->nb_cap, 4);
-    L.fb_stride = (int)align_up((size_t)L.bm_words, 2);
-    L.fepoch = take(16);
-    L.fscores = take(8 * (size_t)rows * L.fs_stride);
-    L.fhslot = take(8 * (size_t)rows);
-    L.fbitmap = take(8 * (size_t)rows * L.fb_stride);
-    L.fpart = take(8 * (size_t)kStepMaxGrid * gq * (g->head_dim + 2));
-  }
   L.bytes = o;
   return L;
 }
@@ -436,15 +443,27 @@ int enqueue_attend(const DeviceState* ds, const adakv_geometry* g, const adakv_v
 
 // Which decode-step path last wrote a workspace's scores (adakv_read_scores).
 std::unordered_map<const void*, bool> g_last_fused;
+// Layout of the one-kernel step's regions last used in a workspace: when it
+// changes (first use, another geometry on a shared buffer) its state words
+// and tagged regions are zeroed, so no stale word can carry a current tag.
+std::unordered_map<const void*, std::pair<size_t, size_t>> g_step_layout;
 
 void note_path(const void* ws, bool fused) {
   std::lock_guard<std::mutex> lock(g_dev_mu);
   g_last_fused[ws] = fused;
 }
 
+// Launch shape of the one-kernel step.
+struct StepPlan {
+  int grid, csize, nbt, slice_cap;
+  size_t smem;
+};
+
 // The one-kernel step for this call, or why not (the three-kernel chain then runs).
-bool step_applies(const DeviceState* ds, const adakv_geometry* g, const adakv_select_params* sp,
-                  const WsLayout& L, int* grid_out) {
+// The cluster size is the largest of 8 / 4 / 2 / 1 CTAs per query head that
+// keeps every CTA of the grid resident (one per SM) and slices of >= 256 blocks.
+bool step_applies(DeviceState* ds, const adakv_geometry* g, const adakv_select_params* sp,
+                  const WsLayout& L, StepPlan* out) {
   const int path = g_dbg_path.load();
   if (path == 1 || !L.fused || !ds->step_ok) return false;
   static const bool env_off = [] {
@@ -453,22 +472,49 @@ bool step_applies(const DeviceState* ds, const adakv_geometry* g, const adakv_se
   }();
   if (env_off && path != 2) return false;
   if (sp->policy == ADAKV_POLICY_NUCLEUS) return false;
-  const int grid = std::min(ds->num_sms, kStepMaxGrid);
+  const int gq = g->n_q_heads / g->n_kv_heads;
+  const int nb_max = ceil_div(g->max_seq_len, g->block_size);
   const int heads = g->batch * g->n_q_heads, groups = g->batch * g->n_kv_heads;
-  if (grid < heads || grid < groups) return false;
-  // ring stages of one CTA: its rows in 64-row stages plus one per (sequence, KV head) it crosses
-  const int64_t rows = (int64_t)groups * ceil_div(g->max_seq_len, g->block_size);
-  const int64_t per = (rows + grid - 1) / grid;
-  if ((per + kStepRows - 1) / kStepRows + std::min<int64_t>(groups, per) + 1 > kStepMaxDesc) return false;
-  *grid_out = grid;
-  return true;
+  const int64_t rows = (int64_t)groups * nb_max;
+  for (int c : {8, 4, 2, 1}) {
+    if (gq * c > 32 || (c > 1 && nb_max / c < 256)) continue;
+    int grid = std::min(ds->num_sms, kStepMaxGrid) / c * c;
+    if (grid < heads * c || grid < groups) continue;
+    StepPlan sp_{};
+    sp_.csize = c;
+    sp_.smem = step_smem_bytes(g->head_dim, gq, nb_max, grid / groups, c, &sp_.nbt, &sp_.slice_cap);
+    if (sp_.smem > kStepSmemMax) continue;
+    int active;
+    {
+      std::lock_guard<std::mutex> lock(g_dev_mu);
+      const auto key = std::make_tuple(g->dtype, gq, c, sp_.smem);
+      auto it = ds->step_clusters.find(key);
+      if (it == ds->step_clusters.end())
+        it = ds->step_clusters
+                 .emplace(key, step_active_clusters(g->dtype, g->head_dim, gq, c, sp_.smem))
+                 .first;
+      active = it->second;
+    }
+    grid = std::min(grid, active * c);
+    if (grid < heads * c || grid < groups) continue;
+    // ring stages of one CTA: its rows in 64-row stages plus one per (sequence, KV head) it crosses
+    const int64_t per = (rows + grid - 1) / grid;
+    if ((per + kStepRows - 1) / kStepRows + std::min<int64_t>(groups, per) + 1 > kStepMaxDesc) continue;
+    sp_.grid = grid;
+    sp_.smem = step_smem_bytes(g->head_dim, gq, nb_max, grid / groups, c, &sp_.nbt, &sp_.slice_cap);
+    *out = sp_;
+    return true;
+  }
+  return false;
 }
 
 int enqueue_step(const adakv_geometry* g, const adakv_select_params* sp, const adakv_view* q,
                  const adakv_view* k, const adakv_view* v, const adakv_view* k_new,
                  const adakv_view* v_new, int n_new, float* centroid, const int32_t* seq_lens,
                  float sm_scale, int32_t* block_table, int32_t table_width, int32_t* sel_lens,
-                 const adakv_view* out, void* ws, const WsLayout& L, int grid, cudaStream_t st) {
+                 const adakv_view* out, void* ws, const WsLayout& L, const StepPlan& plan,
+                 cudaStream_t st) {
+  const int grid = plan.grid;
   const int gq = g->n_q_heads / g->n_kv_heads;
   const int nb_max = ceil_div(g->max_seq_len, g->block_size);
   StepParams p{};
@@ -496,20 +542,45 @@ int enqueue_step(const adakv_geometry* g, const adakv_select_params* sp, const a
   p.sel_lens = sel_lens;
   p.lse = nullptr;
   p.status = ws_at<uint32_t>(ws, L.status);
-  p.epoch = ws_at<uint32_t>(ws, L.fepoch);
-  p.scores = ws_at<unsigned long long>(ws, L.fscores);
+  p.epoch = ws_at<uint32_t>(ws, L.fstate);
+  p.arrive = ws_at<unsigned long long>(ws, L.fstate + 8);
+  p.scores = ws_at<float>(ws, L.fscores);
   p.fs_stride = L.fs_stride;
   p.hslot = ws_at<unsigned long long>(ws, L.fhslot);
-  p.bitmap = ws_at<unsigned long long>(ws, L.fbitmap);
+  p.bitmap = ws_at<uint32_t>(ws, L.fbitmap);
   p.fb_stride = L.fb_stride;
-  p.part = ws_at<unsigned long long>(ws, L.fpart);
+  p.ready = ws_at<unsigned long long>(ws, L.fready);
+  p.part = ws_at<float>(ws, L.fpart);
+  p.pready = ws_at<unsigned long long>(ws, L.fpready);
   p.nb_max = nb_max;
   p.wait_ns = wait_limit_ns();
   p.debug_flags = g_dbg_flags.load();
-  const int min_split = grid / (g->batch * g->n_kv_heads);
-  const size_t smem = step_smem_bytes(g->head_dim, gq, nb_max, min_split, &p.nbt, &p.slice_cap);
-  if (smem > kStepSmemMax)
-    return fail(ADAKV_ERR_UNSUPPORTED, "sequence too long for the one-kernel step");
+  p.timeline = ws_at<unsigned long long>(ws, L.ftimeline);
+  {
+    const std::pair<size_t, size_t> sig(L.fend - L.fbegin, (size_t)grid * 16 + plan.csize);
+    bool fresh;
+    {
+      std::lock_guard<std::mutex> lock(g_dev_mu);
+      auto it = g_step_layout.find(ws);
+      fresh = it == g_step_layout.end() || it->second != sig;
+    }
+    if (fresh) {
+      cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+      CUDA_TRY(cudaStreamIsCapturing(st, &cs));
+      if (cs != cudaStreamCaptureStatusNone)
+        return fail(ADAKV_ERR_INVALID,
+                    "the first adakv_decode_step on a workspace (or on a new geometry) must run "
+                    "before stream capture: it initialises the workspace");
+      CUDA_TRY(cudaMemsetAsync(ws_at<char>(ws, L.fstate), 0, 32, st));
+      CUDA_TRY(cudaMemsetAsync(ws_at<char>(ws, L.fbegin), 0, L.fend - L.fbegin, st));
+      std::lock_guard<std::mutex> lock(g_dev_mu);
+      g_step_layout[ws] = sig;
+    }
+  }
+  p.csize = plan.csize;
+  p.nbt = plan.nbt;
+  p.slice_cap = plan.slice_cap;
+  const size_t smem = plan.smem;
   LaunchOpts o;
   o.pdl = pdl_enabled();
   CUDA_TRY(launch_step(p, g->dtype, g->head_dim, gq, grid, smem, st, o));
@@ -730,10 +801,10 @@ int adakv_decode_step(const adakv_geometry* geo, const adakv_select_params* sp,
   DeviceState* ds = nullptr;
   if ((rc = device_state(&ds))) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  int grid = 0;
-  if (step_applies(ds, geo, sp, L, &grid))
+  StepPlan plan{};
+  if (step_applies(ds, geo, sp, L, &plan))
     return enqueue_step(geo, sp, q, k, v, k_new, v_new, n_new, centroid, seq_lens, sm_scale,
-                        block_table, table_width, sel_lens, out, workspace, L, grid, st);
+                        block_table, table_width, sel_lens, out, workspace, L, plan, st);
   if ((rc = enqueue_plan(ds, geo, sp, q, centroid, seq_lens, k, v, k_new, v_new, n_new,
                          block_table, table_width, sel_lens, workspace, L, st)))
     return rc;
@@ -759,7 +830,7 @@ int adakv_read_scores(const adakv_geometry* geo, void* workspace, size_t workspa
       return fail(ADAKV_ERR_INVALID, "no decode step or plan has run on this workspace");
     fused = it->second;
   }
-  CUDA_TRY(launch_step_scores(fused, ws_at<unsigned long long>(workspace, L.fscores), L.fs_stride,
+  CUDA_TRY(launch_step_scores(fused, ws_at<float>(workspace, L.fscores), L.fs_stride,
                               ws_at<float>(workspace, L.scores), L.score_stride,
                               geo->batch * geo->n_q_heads, nb_max, scores_out, score_stride,
                               static_cast<cudaStream_t>(stream)));
@@ -786,6 +857,22 @@ int adakv_set_status_sink(void* workspace, uint32_t* host_word, void* stream) {
   CUDA_TRY(cudaMemcpyAsync(static_cast<char*>(workspace) + 8, &dev, sizeof(dev),
                            cudaMemcpyHostToDevice, st));
   CUDA_TRY(cudaStreamSynchronize(st));
+  return ADAKV_OK;
+}
+
+int adakv_debug_timeline(const adakv_geometry* geo, void* workspace, size_t workspace_bytes,
+                         uint64_t* out, int32_t max_ctas, void* stream) {
+  int rc;
+  if ((rc = check_geometry(geo))) return rc;
+  const WsLayout L = make_ws(geo, true);
+  if ((rc = check_workspace(workspace, workspace_bytes, L.bytes))) return rc;
+  if (!L.fused) return fail(ADAKV_ERR_INVALID, "this geometry does not run the one-kernel step");
+  if (!out || max_ctas < 1) return fail(ADAKV_ERR_INVALID, "out is NULL or max_ctas < 1");
+  const int n = std::min(max_ctas, kStepMaxGrid);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  CUDA_TRY(cudaStreamSynchronize(st));
+  CUDA_TRY(cudaMemcpy(out, ws_at<char>(workspace, L.ftimeline),
+                      sizeof(uint64_t) * kStepTimelineSlots * (size_t)n, cudaMemcpyDeviceToHost));
   return ADAKV_OK;
 }
 

@@ -104,9 +104,11 @@ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 // ---------------------------------------------------------------------------
 #ifdef __CUDACC__
 
+// (the memory clobber keeps the read in place relative to barriers and memory
+// operations, so timestamps and time limits measure what they bracket)
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t) : : "memory");
   return t;
 }
 
@@ -161,6 +163,42 @@ struct PollBudget {
   uint64_t t0;
   bool dead;
 };
+
+// Words w[i] (i < n) of base[i * stride], first read already in w: re-read
+// every word that does not carry `tag` yet, all of a round's loads in flight
+// together, until each one does or the budget runs out.  One round trip
+// after the last word lands, however many words were late.
+template <int N>
+__device__ __forceinline__ void wait_tagged_n(const unsigned long long* base, size_t stride,
+                                              unsigned long long (&w)[N], int n, uint32_t tag,
+                                              PollBudget& pb) {
+  while (!pb.dead) {
+    bool all = true;
+#pragma unroll
+    for (int i = 0; i < N; ++i)
+      if (i < n && !tag_is(w[i], tag)) all = false;
+    if (all) return;
+    const uint64_t now = globaltimer_ns();
+    if (pb.t0 == 0) {
+      pb.t0 = now;
+    } else if (now - pb.t0 > pb.limit) {
+      pb.dead = true;
+      return;
+    }
+#pragma unroll
+    for (int i = 0; i < N; ++i)
+      if (i < n && !tag_is(w[i], tag)) w[i] = ldr_u64(base + i * stride);
+  }
+}
+
+__device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_release_add_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
 
 // Re-read *p until its tag is `tag` (w = the first read), within the budget.
 __device__ __forceinline__ unsigned long long wait_tagged(const unsigned long long* p,

@@ -409,7 +409,9 @@ __global__ void __launch_bounds__(kEstThreads, 1) estimate_kernel(EstParams p) {
         S_b = b;
         S = seq_len_of(p.seq_lens, b, p.max_seq_len);
       }
-      if (!mbar_wait_bounded(&full_bar[s], ph)) {
+      // a lane that gives up makes the whole warp give up: the shuffles below
+      // need every lane
+      if (!__all_sync(0xffffffffu, mbar_wait_bounded(&full_bar[s], ph))) {
         if (lane == 0) report(p.status, ADAKV_ST_WAIT_TIMEOUT);
         break;
       }

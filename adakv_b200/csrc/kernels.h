@@ -148,7 +148,7 @@ struct CombineParams {      // log-sum-exp merge of per-shard attention outputs
 // ---------------------------------------------------------------------------
 constexpr int kStepThreads = 256;       // 8 warps: estimator consumers, selection, MMA attend
 constexpr int kStepRows = 64;           // centroid rows per estimator ring stage
-constexpr int kStepStages = 4;          // estimator ring depth
+constexpr int kStepStages = 6;          // estimator ring depth
 constexpr int kStepMaxDesc = 192;       // ring stages one CTA streams at most
 constexpr int kStepMaxBatch = 32;       // sequences per call
 constexpr int kStepMaxHeads = 128;      // B * Hq (one selection CTA per query head)
@@ -174,19 +174,26 @@ struct StepParams {
   float* lse;                  // optional [B*Hq]
   // workspace (tagged words: call tag << 32 | payload)
   uint32_t* status;
-  uint32_t* epoch;             // [0] call counter, [1] CTAs done
-  unsigned long long* scores;  // [B*Hq, fs_stride] block scores
+  uint32_t* epoch;             // [0] calls completed, [1] CTAs done in this call
+  unsigned long long* arrive;  // CTAs past the estimator phase, over all calls (monotonic)
+  float* scores;               // [B*Hq, fs_stride] block scores (plain floats)
   int fs_stride;
-  unsigned long long* hslot;   // [B*Hq] entropy of each head
-  unsigned long long* bitmap;  // [B*Hq, fb_stride] selection bitmaps
+  unsigned long long* hslot;   // [B*Hq] entropy of each head (tagged)
+  uint32_t* bitmap;            // [B*Hq, fb_stride] selection bitmaps
   int fb_stride;
-  unsigned long long* part;    // [grid, g, D + 2] attention partials (m, l, o) per CTA
+  unsigned long long* ready;   // [B*Hq, csize] a cluster rank's bitmap words are out (tagged, release)
+  float* part;                 // [grid, g, D + 2] attention partials (m, l, o) per CTA
+  unsigned long long* pready;  // [grid] a CTA's partial is complete (tagged, release)
+  int csize;                   // CTAs (one cluster) per query head in the selection phase
   int nbt;                     // K/V blocks per gather stage
   int slice_cap;               // union blocks one attend CTA takes at most
   int nb_max;                  // ceil(max_seq_len / bs)
   uint64_t wait_ns;            // bound of every device-side wait
-  int debug_flags;             // test-only: bit 0 = head 0 never publishes its entropy
+  int debug_flags;             // test-only: bit 0 = head 0 never publishes its entropy,
+                               // bit 1 = record per-CTA phase timestamps in `timeline`
+  unsigned long long* timeline;  // [grid, 8] globaltimer stamps (debug)
 };
+constexpr int kStepTimelineSlots = 24;
 
 // (b') minmax (Quest) estimator: tables and scores
 struct MinmaxParams {
@@ -277,12 +284,14 @@ cudaError_t launch_minmax_score(const MinmaxParams& p, int dtype, int D, int nb_
 cudaError_t launch_combine(const CombineParams& p, int dtype, cudaStream_t stream, const LaunchOpts& o);
 cudaError_t launch_step(const StepParams& p, int dtype, int D, int g, int grid, size_t smem,
                         cudaStream_t stream, const LaunchOpts& o);
-cudaError_t launch_step_scores(bool fused, const unsigned long long* fscores,
+cudaError_t launch_step_scores(bool fused, const float* fscores,
                                int fs_stride, const float* scores, int score_stride, int rows,
                                int nb, float* out, int out_stride, cudaStream_t stream);
 cudaError_t step_kernels_init();
 // dynamic shared memory of the step kernel and its gather-ring depth
-size_t step_smem_bytes(int D, int g, int nb_max, int min_split, int* nbt, int* slice_cap);
+size_t step_smem_bytes(int D, int g, int nb_max, int min_split, int csize, int* nbt, int* slice_cap);
+// clusters of `csize` step CTAs with `smem` bytes that can be resident at once
+int step_active_clusters(int dtype, int D, int g, int csize, size_t smem);
 bool step_kernel_built(int dtype, int D, int bs, int g);
 
 // once per device (current device): opt-in shared memory / cluster sizes

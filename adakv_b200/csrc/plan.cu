@@ -773,7 +773,11 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanParams p) {
           ents[q4] = e;
         }
         ok = __all_sync(0xffffffffu, mine);
-        if (ok || globaltimer_ns() - t0 > p.wait_ns) break;
+        // lanes may read the timer at different moments: lane 0 decides for
+        // the warp, so no lane leaves the loop (and its warp-wide __all_sync)
+        // while another stays in it
+        const bool expired = __shfl_sync(0xffffffffu, globaltimer_ns() - t0 > p.wait_ns, 0);
+        if (ok || expired) break;
       }
       if (!ok && lane == 0) report(p.status, ADAKV_ST_WAIT_TIMEOUT);
       double ps = 0.0;

@@ -1,11 +1,16 @@
 // (a)-(d) One AdaKV decode step in one persistent kernel.
 //
 // One CTA per SM (256 threads).  The step's three dependent stages run as
-// phases of the same grid, handing data to one another through tagged 64-bit
-// words in the workspace (call tag << 32 | payload): a reader polls a word
-// until it carries this call's tag, so a phase starts as soon as the words it
-// needs exist, with no kernel boundary, grid barrier or counter reset.  Every
-// poll is bounded in time; on expiry the status word records
+// phases of the same grid with no kernel boundary between them:
+//   A -> B: every CTA adds one to a monotonic arrival counter (release) when
+//           its scores are written; a selection CTA waits for this call's
+//           GRID arrivals (acquire) and reads its score row in one batch;
+//   B -> B, B -> C, C -> C: the head entropies, the selection bitmaps and the
+//           attention partials are tagged 64-bit words (call tag << 32 |
+//           payload): a reader re-reads, all at once, the words that do not
+//           carry this call's tag yet, so it proceeds one round trip after the
+//           last one lands, and nothing has to be reset between calls.
+// Every wait is bounded in time; on expiry the status word records
 // ADAKV_ST_WAIT_TIMEOUT and the kernel runs to completion on what it has.
 //
 // Phase A -- append + estimator (adakv/runtime.py:43-60, adakv/estimator.py:73-74).
@@ -49,16 +54,19 @@
 // HBM traffic: the float32 centroid tables, the union of the selected K/V
 // blocks and the appended tokens; scores, bitmaps and partials stay in L2.
 //
-// Memory ordering across CTAs: words are relaxed gpu-scope loads and stores;
-// the appended K/V tokens reach the attend phase through release/acquire
-// fences around the score and bitmap words (refresh warp: fence before its
-// score words; selection CTA: fence after reading the row and before the
-// bitmap; attend CTA: fence after reading the bitmaps).
+// Memory ordering across CTAs: the appended K/V tokens reach the attend phase
+// through the arrival counter (release after the cache writes, acquire by the
+// selection CTA) and fences around the bitmap words (selection CTA: fence
+// before publishing; attend CTA: fence after reading them).
 //
 // All CTAs must be resident at once (they wait on one another): the host
 // launches at most one CTA per SM, and every wait is bounded.
+#include <cooperative_groups.h>
+
 #include "attend_mma.cuh"
 #include "kernels.h"
+
+namespace cg = cooperative_groups;
 
 namespace adakv {
 
@@ -67,6 +75,13 @@ namespace {
 constexpr int kSW = kStepThreads / 32;  // warps per CTA
 constexpr int kBk = 2048;               // selection buckets
 constexpr int kDebugSkipPublish = 1;
+constexpr int kDebugTimeline = 2;
+
+// debug timeline: globaltimer stamp `slot` of this CTA (one thread calls it)
+#define STEP_STAMP(slot) \
+  do { \
+    if (p.debug_flags & kDebugTimeline) p.timeline[cta * kStepTimelineSlots + (slot)] = globaltimer_ns(); \
+  } while (0)
 
 __device__ __forceinline__ float h16lo(uint32_t w, const __nv_bfloat16*) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float h16hi(uint32_t w, const __nv_bfloat16*) {
@@ -123,26 +138,8 @@ __device__ __forceinline__ int bucket_of(float s, float cmx, float scale) {
   return u <= 0.f ? 0 : (int)u;
 }
 
-// block-wide reduction: every thread gets the same result (warp xor trees,
-// then the kSW warp values folded in warp order)
-__device__ __forceinline__ void block_max2(float& a, float& b, float (*red)[4]) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  a = warp_max(a);
-  b = warp_max(b);
-  __syncthreads();
-  if (lane == 0) {
-    red[warp][0] = a;
-    red[warp][1] = b;
-  }
-  __syncthreads();
-  a = red[0][0];
-  b = red[0][1];
-#pragma unroll
-  for (int w = 1; w < kSW; ++w) {
-    a = fmaxf(a, red[w][0]);
-    b = fmaxf(b, red[w][1]);
-  }
-}
+// block-wide sums of two doubles: every thread gets the same result (warp
+// xor trees, then the kSW warp values folded in warp order)
 __device__ __forceinline__ void block_sum2d(double& a, double& b, double (*red)[4]) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   a = warp_sum(a);
@@ -162,26 +159,153 @@ __device__ __forceinline__ void block_sum2d(double& a, double& b, double (*red)[
   }
 }
 
+// max, content max (every thread gets them) and content sum / sum of squares
+// (float per thread, double across threads) in one reduction round
+__device__ __forceinline__ void block_stats(float m1, float m2, float s1, float s2, float (*redf)[4],
+                                            double (*redd)[4], float& mx, float& cmx, double& cs,
+                                            double& cq) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  m1 = warp_max(m1);
+  m2 = warp_max(m2);
+  double d1 = warp_sum((double)s1), d2 = warp_sum((double)s2);
+  __syncthreads();
+  if (lane == 0) {
+    redf[warp][0] = m1;
+    redf[warp][1] = m2;
+    redd[warp][0] = d1;
+    redd[warp][1] = d2;
+  }
+  __syncthreads();
+  mx = redf[0][0];
+  cmx = redf[0][1];
+  cs = 0.0;
+  cq = 0.0;
+#pragma unroll
+  for (int w = 0; w < kSW; ++w) {
+    mx = fmaxf(mx, redf[w][0]);
+    cmx = fmaxf(cmx, redf[w][1]);
+    cs += redd[w][0];
+    cq += redd[w][1];
+  }
+}
+
+
+// Exact top-K of one score row by a 4-pass MSB radix select over order-preserving
+// keys (forced sink / local blocks take the largest key), ties at the threshold
+// to the lowest block indices; the selection is ORed into sbits (its forced
+// bits may already be set).  The fallback for rows the buckets cannot resolve,
+// kept out of line so that its code is not fetched on the common path.
+// srow is overwritten with the keys; hist (256 words) and weq (nw words) are scratch.
+__device__ __noinline__ void radix_select_top(float* srow, int nb, int sink, int local, int K,
+                                              uint32_t* hist, uint32_t* weq, uint32_t* sbits,
+                                              int* scan_scratch, int* s_digit, int* s_above) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nw = ceil_div(nb, 32);
+  __syncthreads();
+  for (int j = tid; j < nb; j += kStepThreads) {
+    const bool f = j < sink || j >= nb - local;
+    srow[j] = __uint_as_float(f ? 0xFFFFFFFFu : order_key(srow[j]));
+  }
+  uint32_t prefix = 0, pmask = 0;
+  int rem = K;
+#pragma unroll 1
+  for (int pass = 0; pass < 4; ++pass) {
+    const int shift = 24 - 8 * pass;
+    __syncthreads();
+    for (int t = tid; t < 256; t += kStepThreads) hist[t] = 0u;
+    __syncthreads();
+    for (int j = tid; j < nb; j += kStepThreads) {
+      const uint32_t k = __float_as_uint(srow[j]);
+      if ((k & pmask) == prefix) atomicAdd(&hist[(k >> shift) & 0xFFu], 1u);
+    }
+    __syncthreads();
+    if (warp == 0) {
+      uint32_t c[8], tot = 0;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        c[e] = hist[255 - 8 * lane - e];
+        tot += c[e];
+      }
+      uint32_t incl = tot;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      const uint32_t excl = incl - tot;
+      if (excl < (uint32_t)rem && (uint32_t)rem <= incl) {
+        uint32_t acc = excl;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          if (acc + c[e] >= (uint32_t)rem) {
+            *s_digit = 255 - 8 * lane - e;
+            *s_above = (int)acc;
+            break;
+          }
+          acc += c[e];
+        }
+      }
+    }
+    __syncthreads();
+    rem -= *s_above;
+    prefix |= (uint32_t)*s_digit << shift;
+    pmask |= 0xFFu << shift;
+  }
+  // keys above the threshold, then the first `rem` keys equal to it in index order
+  for (int w = warp; w < nw; w += kSW) {
+    const int j = w * 32 + lane;
+    const uint32_t k = j < nb ? __float_as_uint(srow[j]) : 0u;
+    const uint32_t gt = __ballot_sync(0xffffffffu, j < nb && k > prefix);
+    const uint32_t eq = __ballot_sync(0xffffffffu, j < nb && k == prefix);
+    if (lane == 0) {
+      sbits[w] |= gt;
+      weq[w] = eq;
+    }
+  }
+  __syncthreads();
+  const int wpt = ceil_div(nw, kStepThreads);
+  const int w0 = imin(tid * wpt, nw), w1 = imin(w0 + wpt, nw);
+  int n_eq = 0;
+  for (int w = w0; w < w1; ++w) n_eq += __popc(weq[w]);
+  int eq_before = block_exclusive_scan(n_eq, scan_scratch);
+  for (int w = w0; w < w1; ++w) {
+    uint32_t e = weq[w];
+    const int take = imax(0, imin(__popc(e), rem - eq_before));
+    eq_before += __popc(e);
+    uint32_t low = 0;
+    for (int t = 0; t < take; ++t) {
+      low |= e & (0u - e);
+      e &= e - 1u;
+    }
+    sbits[w] |= low;
+  }
+}
+
 // shared-memory carve-up of one step CTA; the three phases reuse the same bytes
 struct StepSmem {
-  size_t ring;                                      // phase A
-  size_t srow, sbits, hist, pre, fill, order, b_end;  // phase B
-  size_t kv, uw, hw, list, mask, wpart, merge, c_end;  // phase C
+  size_t ring;                                                      // phase A
+  size_t srow, sbk, sbits, hist, ghist, ckey, cidx, akey, aidx, b_end;  // phase B
+  size_t kv, uw, hw, list, mask, wpart, merge, c_end;               // phase C
   size_t total;
 };
 
-__host__ __device__ inline StepSmem step_smem_layout(int D, int g, int nb_max, int nbt, int slice_cap) {
+__host__ __device__ inline StepSmem step_smem_layout(int D, int g, int nb_max, int nbt, int slice_cap,
+                                                     int csize) {
   auto al = [](size_t x) { return (x + 127) / 128 * 128; };
   const int nw = (nb_max + 31) / 32;
+  const int ls = ((nb_max + csize - 1) / csize + 31) / 32 * 32;  // slice of one cluster rank
   StepSmem s;
-  s.ring = al((size_t)kStepStages * kStepRows * D * 4);
-  s.srow = 0;
-  s.sbits = s.srow + al((size_t)nb_max * 4);
+  s.ring = al((size_t)kStepStages * (kStepRows * D * 4 + g * D * 2));
+  s.srow = 0;  // the slice; the whole row on the exact (radix) path
+  s.sbk = s.srow + al((size_t)nb_max * 4);
+  s.sbits = s.sbk + al((size_t)ls * 2);
   s.hist = s.sbits + al((size_t)nw * 4);
-  s.pre = s.hist + al((size_t)kBk * 4);
-  s.fill = s.pre + al((size_t)kBk * 4);
-  s.order = s.fill + al((size_t)(kBk > nw ? kBk : nw) * 4);
-  s.b_end = s.order + al((size_t)kStepOrderCap * 4);
+  s.ghist = s.hist + al((size_t)kBk * 4);
+  s.ckey = s.ghist + al((size_t)(kBk > nw ? kBk : nw) * 4);
+  s.cidx = s.ckey + al((size_t)kStepCandCap * 4);
+  s.akey = s.cidx + al((size_t)kStepCandCap * 4);
+  s.aidx = s.akey + al((size_t)kStepCandCap * 4);
+  s.b_end = s.aidx + al((size_t)kStepCandCap * 4);
   s.kv = 0;
   s.uw = s.kv + al((size_t)2 * 2 * nbt * 16 * D * 2);
   s.hw = s.uw + al((size_t)nw * 4);
@@ -189,13 +313,22 @@ __host__ __device__ inline StepSmem step_smem_layout(int D, int g, int nb_max, i
   s.mask = s.list + al((size_t)slice_cap * 4);
   s.wpart = s.mask + al((size_t)slice_cap * 4);
   s.merge = s.wpart + al((size_t)kSW * g * (D + 2) * 4);
-  s.c_end = s.merge + al((size_t)(kStepMaxGrid * g + 2 * g) * 4);
+  s.c_end = s.merge + al((size_t)(2 * kStepMaxGrid * g + 2 * g) * 4);
   size_t t = s.ring;
   t = t > s.b_end ? t : s.b_end;
   t = t > s.c_end ? t : s.c_end;
   s.total = t;
   return s;
 }
+
+// One cluster rank's share of a head's row statistics, read by the other
+// ranks through distributed shared memory.
+struct RankPart {
+  float mx, cmx, m;        // max score, content max, max z
+  double cs, cq, Z, A;     // content sum / sum of squares; sum e^(z - m), sum e^(z - m) (z - m)
+  double Cc;               // clamp correction of the slice
+  int ncand, nsel;         // threshold-bucket candidates; selected blocks of the slice
+};
 
 // a sequence takes part when 1 <= S <= max_seq_len and it holds the appended tokens
 __device__ __forceinline__ int valid_len(const StepParams& p, int b) {
@@ -233,7 +366,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepParams p) {
   __shared__ double redd[kSW][4];
   __shared__ int scan_scratch[33];
   __shared__ double s_w, s_sumw;
-  __shared__ int s_blim, s_jstar, s_over, s_digit, s_above, s_last;
+  __shared__ int s_jstar, s_digit, s_above, s_ncand;
+  __shared__ RankPart s_part;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int GRID = gridDim.x, cta = blockIdx.x;
@@ -245,6 +379,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepParams p) {
 
   // ---------------------------------------------------------------- set-up
   if (tid == 0) {
+    STEP_STAMP(0);
     const uint32_t e = *reinterpret_cast<volatile uint32_t*>(p.epoch);
     s_tag = (e + 1u) ? e + 1u : 1u;
     for (int s = 0; s < kStepStages; ++s) {
@@ -295,14 +430,38 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepParams p) {
   }
   __syncthreads();
   const int nstage = s_nstage;
+  // ring stage: kStepRows centroid rows (fp32), then the G query rows of
+  // the stage's KV head (T), both brought by the TMA engine
+  constexpr int STAGE_F = kStepRows * D + G * D * (int)sizeof(T) / 4;  // floats per stage
   float* ring = reinterpret_cast<float*>(sm);
   auto issue = [&](int i, int slot) {
     const int4 d = sdesc[i];
     const uint32_t bytes = (uint32_t)d.z * D * 4u;
-    mbar_arrive_expect_tx(&full_bar[slot], bytes);
-    bulk_g2s(ring + slot * kStepRows * D, p.cent + ((int64_t)d.x * p.nb_cap + d.y) * D, bytes,
-             &full_bar[slot]);
+    const int b = d.x / p.Hkv, kvh = d.x - b * p.Hkv;
+    float* st = ring + slot * STAGE_F;
+    mbar_arrive_expect_tx(&full_bar[slot], bytes + (uint32_t)(G * D * sizeof(T)));
+    bulk_g2s(st, p.cent + ((int64_t)d.x * p.nb_cap + d.y) * D, bytes, &full_bar[slot]);
+    const T* qsrc = static_cast<const T*>(p.q.data) + b * p.q.sb + (int64_t)kvh * G * p.q.sh;
+#pragma unroll
+    for (int j = 0; j < G; ++j)
+      bulk_g2s(reinterpret_cast<T*>(st + kStepRows * D) + j * D, qsrc + j * p.q.sh,
+               (uint32_t)(D * sizeof(T)), &full_bar[slot]);
   };
+  // the append refresh reads the touched block's older tokens: warm L2 with
+  // them before this CTA's estimator burst fills the DRAM queues
+  if (appending && warp == kSW - 1 && cta < p.B * p.Hkv) {
+    const int b = cta / p.Hkv, kvh = cta - b * p.Hkv;
+    const int S = s_S[b];
+    if (S > 0) {
+      const int S_old = S - p.n_new;
+      const T* kc = static_cast<const T*>(p.k.data) + b * p.k.sb + kvh * p.k.sh;
+      for (int t = (S_old / BS) * BS + (lane >> 1); t < S_old; t += 16) {
+        const char* row = reinterpret_cast<const char*>(kc + (int64_t)t * p.k.ss);
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(row + (lane & 1) * 128) : "memory");
+      }
+    }
+  }
+  __syncthreads();
   if (tid == 0)
     for (int i = 0; i < imin(kStepStages, nstage); ++i) issue(i, i);
 
@@ -370,14 +529,9 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepParams p) {
           for (int o = 16; o; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
           sc[j] = part;
         }
-        // the cache writes of every lane are ordered before the score words
-        __syncwarp();
-        fence_acq_rel_gpu();
 #pragma unroll
         for (int j = 0; j < G; ++j)
-          if (lane == j)
-            str_u64(p.scores + (size_t)(b * p.Hq + kvh * G + j) * p.fs_stride + blk,
-                    tword(tag, __float_as_uint(sc[j])));
+          if (lane == j) p.scores[(size_t)(b * p.Hq + kvh * G + j) * p.fs_stride + blk] = sc[j];
       }
     }
   }
@@ -388,27 +542,33 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepParams p) {
     for (int i = 0; i < nstage; ++i) {
       const int slot = i % kStepStages;
       const uint32_t par = (uint32_t)(i / kStepStages) & 1u;
-      if (!mbar_wait_bounded(&full_bar[slot], par)) {
+      // a lane that gives up makes the whole warp give up: the reduce-scatter
+      // below needs every lane
+      if (!__all_sync(0xffffffffu, mbar_wait_bounded(&full_bar[slot], par))) {
         if (lane == 0) report(p.status, ADAKV_ST_WAIT_TIMEOUT);
         break;
       }
+      if (warp == 0 && lane == 0) {
+        if (i == 0) STEP_STAMP(8);
+        if (i == nstage - 1) STEP_STAMP(9);
+      }
       const int4 d = sdesc[i];
       const int b = d.x / p.Hkv, kvh = d.x - b * p.Hkv;
-      if (d.x != qrun) {
+      const float* tile = ring + slot * STAGE_F;
+      if (d.x != qrun) {  // queries of a new (sequence, KV head) run, from the stage
         qrun = d.x;
-        const T* qb = static_cast<const T*>(p.q.data) + b * p.q.sb + (int64_t)kvh * G * p.q.sh;
+        const T* qs = reinterpret_cast<const T*>(tile + kStepRows * D);
 #pragma unroll
         for (int h = 0; h < G; ++h)
 #pragma unroll
           for (int k = 0; k < CH; ++k) {
             float f[4];
-            load4<T>(qb + h * p.q.sh + 4 * (sub + LPR * k), f);
+            load4<T>(qs + h * D + 4 * (sub + LPR * k), f);
 #pragma unroll
             for (int e = 0; e < 4; ++e) qf[h][4 * k + e] = f[e];
           }
       }
-      const float* tile = ring + slot * kStepRows * D;
-      unsigned long long* srow0 = p.scores + (size_t)(b * p.Hq + kvh * G) * p.fs_stride + d.y;
+      float* srow0 = p.scores + (size_t)(b * p.Hq + kvh * G) * p.fs_stride + d.y;
 #pragma unroll
       for (int pp = 0; pp < PASSES; ++pp) {
         const int row = warp * RPW + pp * RPP + rin;
@@ -430,8 +590,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepParams p) {
           }
         }
         const float s = reduce_heads<G, LPR>(acc, lane);
-        if ((sub & 1) == 0 && row < d.z && row < d.w)
-          str_u64(srow0 + (size_t)(sub >> 1) * p.fs_stride + row, tword(tag, __float_as_uint(s)));
+        if ((sub & 1) == 0 && row < d.z && row < d.w) srow0[(size_t)(sub >> 1) * p.fs_stride + row] = s;
       }
       __syncwarp();
       if (lane == 0) {
@@ -443,20 +602,36 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepParams p) {
       }
     }
   }
-  __syncthreads();  // the ring is drained: its bytes are reused below
+  __syncthreads();  // the ring is drained (its bytes are reused below); every score is written
+  if (tid == 0) {
+    fence_acq_rel_gpu();
+    red_release_add_u64(p.arrive, 1ull);
+    STEP_STAMP(1);
+  }
 
   // ---------------------------------------------------------------- phase B
-  if (cta < p.B * p.Hq) {
-    const int hr = cta, b = hr / p.Hq, h = hr - b * p.Hq;
+  // One thread-block cluster of CL CTAs per query head; rank r owns blocks
+  // [r Ls, (r + 1) Ls) of the row (Ls a multiple of 32: whole bitmap words).
+  const int CL = p.csize;
+  const bool head_cta = cta < p.B * p.Hq * CL;
+  if (head_cta) {
+    cg::cluster_group cl = cg::this_cluster();
+    const int hr = cta / CL, rank = cta - hr * CL;
+    const int b = hr / p.Hq, h = hr - b * p.Hq;
     const int nb = ceil_div(s_S[b], BS);
-    const int nw = ceil_div(nb, 32);
-    const StepSmem L = step_smem_layout(D, G, p.nb_max, p.nbt, p.slice_cap);
-    float* srow = reinterpret_cast<float*>(sm + L.srow);
+    const int Ls = (ceil_div(nb, CL) + 31) / 32 * 32;
+    const int lo = imin(nb, rank * Ls), hi = imin(nb, lo + Ls), n = hi - lo;
+    const int nwl = ceil_div(n, 32), w_lo = lo / 32;
+    const StepSmem L = step_smem_layout(D, G, p.nb_max, p.nbt, p.slice_cap, CL);
+    float* srow = reinterpret_cast<float*>(sm + L.srow);        // the slice (li = j - lo)
+    uint16_t* sbk = reinterpret_cast<uint16_t*>(sm + L.sbk);    // bucket of each slice block
     uint32_t* sbits = reinterpret_cast<uint32_t*>(sm + L.sbits);
-    uint32_t* hist = reinterpret_cast<uint32_t*>(sm + L.hist);
-    uint32_t* pre = reinterpret_cast<uint32_t*>(sm + L.pre);
-    uint32_t* fill = reinterpret_cast<uint32_t*>(sm + L.fill);
-    int* order = reinterpret_cast<int*>(sm + L.order);
+    uint32_t* hist = reinterpret_cast<uint32_t*>(sm + L.hist);  // this rank's histogram
+    uint32_t* ghist = reinterpret_cast<uint32_t*>(sm + L.ghist);  // the cluster's
+    uint32_t* ckey = reinterpret_cast<uint32_t*>(sm + L.ckey);    // this rank's candidates
+    int* cidx = reinterpret_cast<int*>(sm + L.cidx);
+    uint32_t* akey = reinterpret_cast<uint32_t*>(sm + L.akey);    // every rank's candidates
+    int* aidx = reinterpret_cast<int*>(sm + L.aidx);
     const SelectCfg& cf = p.cfg;
     const int sink = imin(cf.n_sink, nb), local = imin(cf.n_local, nb);
     auto forced = [&](int j) -> bool { return j < sink || j >= nb - local; };
@@ -465,110 +640,142 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepParams p) {
     const bool unit_t = (Tf == 1.0f);
     auto zof = [&](float v) -> float { return unit_t ? v : __fdiv_rn(v, Tf); };
 
-    for (int t = tid; t < kBk; t += kStepThreads) {
-      hist[t] = 0u;
-      fill[t] = 0u;
-    }
-    for (int w = tid; w < nw; w += kStepThreads) sbits[w] = 0u;
+    for (int t = tid; t < kBk; t += kStepThreads) hist[t] = 0u;
     if (tid == 0) {
-      s_over = 0;
+      s_ncand = 0;
       s_jstar = -1;
-      s_blim = -1;
     }
 
-    // ---- the head's score row: tagged words -> floats in shared memory ----
-    {
-      PollBudget pb{p.wait_ns, 0, false};
-      const unsigned long long* src = p.scores + (size_t)hr * p.fs_stride;
-      constexpr int U = 4;
-      for (int j0 = 2 * tid; j0 < nb; j0 += 2 * kStepThreads * U) {
-        unsigned long long w[U][2];
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-          const int j = j0 + 2 * kStepThreads * u;
-          if (j < nb) ldr_u64x2(src + j, w[u][0], w[u][1]);
+    // ---- every CTA's scores are out (this call's GRID arrivals), then the
+    //      slice in one batch of L2 loads ----
+    if (tid == 0) {
+      const unsigned long long target = (unsigned long long)tag * (unsigned long long)GRID;
+      if (ld_acquire_u64(p.arrive) < target) {
+        const uint64_t t0 = globaltimer_ns();
+        while (ld_acquire_u64(p.arrive) < target) {
+          if (globaltimer_ns() - t0 > p.wait_ns) {
+            report(p.status, ADAKV_ST_WAIT_TIMEOUT);
+            break;
+          }
         }
+      }
+    }
+    __syncthreads();
+    const float* grow = p.scores + (size_t)hr * p.fs_stride;  // 16-byte aligned rows
+    for (int j = 4 * tid; j < n; j += 4 * kStepThreads)
+      *reinterpret_cast<float4*>(srow + j) = __ldcg(reinterpret_cast<const float4*>(grow + lo + j));
+    __syncthreads();
+    if (tid == 0) STEP_STAMP(2);
+    const int nch = ceil_div(n, 4);
+    const float4* srow4 = reinterpret_cast<const float4*>(srow);
+
+    // ---- pass 1: max, content max / sum / sum of squares and the softmax sums
+    //      (online per thread: m = max z, Z = sum e^(z - m), A = sum e^(z - m) (z - m)) ----
+    {
+      float m1 = -INFINITY, m2 = -INFINITY, cs = 0.f, cq = 0.f, mt = -INFINITY, zt = 0.f, at = 0.f;
+#pragma unroll 1
+      for (int c = tid; c < nch; c += kStepThreads) {
+        const float4 x = srow4[c];
+        const float v[4] = {x.x, x.y, x.z, x.w};
+        float zc[4], cm = -INFINITY;
 #pragma unroll
-        for (int u = 0; u < U; ++u) {
-          const int j = j0 + 2 * kStepThreads * u;
-          if (j < nb) {
-            w[u][0] = wait_tagged(src + j, w[u][0], tag, pb);
-            srow[j] = __uint_as_float((uint32_t)w[u][0]);
-            if (j + 1 < nb) {
-              w[u][1] = wait_tagged(src + j + 1, w[u][1], tag, pb);
-              srow[j + 1] = __uint_as_float((uint32_t)w[u][1]);
+        for (int e = 0; e < 4; ++e) {
+          const int j = lo + 4 * c + e;
+          const bool in = 4 * c + e < n;
+          zc[e] = in ? zof(v[e]) : -INFINITY;
+          if (in) {
+            m1 = fmaxf(m1, v[e]);
+            cm = fmaxf(cm, zc[e]);
+            if (!forced(j)) {
+              m2 = fmaxf(m2, v[e]);
+              cs += v[e];
+              cq = fmaf(v[e], v[e], cq);
+            }
+          }
+        }
+        if (adaptive && cm > mt) {  // rescale to the new running max
+          if (mt > -INFINITY) {
+            const float f = expf(mt - cm);
+            at = f * fmaf(zt, mt - cm, at);
+            zt *= f;
+          }
+          mt = cm;
+        }
+        if (adaptive) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            if (zc[e] > -INFINITY) {
+              const float dd = zc[e] - mt;
+              const float ex = expf(dd);
+              zt += ex;
+              if (ex > 0.f) at = fmaf(ex, dd, at);
             }
           }
         }
       }
-      if (pb.dead) report(p.status, ADAKV_ST_WAIT_TIMEOUT);
-      fence_acq_rel_gpu();  // acquire: the refreshed K/V tokens precede these scores
-    }
-    __syncthreads();
-
-    // ---- row statistics (pass 1) ----
-    float mx = -INFINITY, cmx = -INFINITY;
-    double csum, csq;
-    {
-      float cs = 0.f, cq = 0.f;
-      for (int j = tid; j < nb; j += kStepThreads) {
-        const float v = srow[j];
-        mx = fmaxf(mx, v);
-        if (!forced(j)) {
-          cmx = fmaxf(cmx, v);
-          cs += v;
-          cq = fmaf(v, v, cq);
-        }
+      // this rank's part: maxima and sums over the CTA, softmax sums rescaled
+      // to the CTA max (double across threads)
+      float mx, cmx;
+      double csum, csq;
+      block_stats(m1, m2, cs, cq, redf, redd, mx, cmx, csum, csq);
+      const float wm = warp_max(mt);
+      double zw = 0.0, aw = 0.0;
+      if (mt > -INFINITY) {
+        const double f = exp((double)mt - (double)wm);
+        zw = (double)zt * f;
+        aw = f * ((double)at + (double)zt * ((double)mt - (double)wm));
       }
-      csum = cs;
-      csq = cq;
-      block_max2(mx, cmx, redf);
-      block_sum2d(csum, csq, redd);
-    }
-    // ---- softmax sums (pass 2) and the clamp correction (pass 3) ----
-    double H = 0.0;
-    if (adaptive) {
-      const float zmax = zof(mx);
-      double Z, A;
-      {
-        float z_t = 0.f, a_t = 0.f;
-        for (int j = tid; j < nb; j += kStepThreads) {
-          const float dd = __fsub_rn(zof(srow[j]), zmax);
-          const float e = expf(dd);
-          z_t += e;
-          if (e > 0.f) a_t = fmaf(e, dd, a_t);
-        }
-        Z = z_t;
-        A = a_t;
-        block_sum2d(Z, A, redd);
+      zw = warp_sum(zw);
+      aw = warp_sum(aw);
+      if (lane == 0) {
+        redf[warp][2] = wm;
+        redd[warp][2] = zw;
+        redd[warp][3] = aw;
       }
-      // H = log Z - A / Z - Cc / Z with Cc = sum over blocks with e / Z < 1e-9
-      // of e (log(1e-9) - d + log Z): the reference's max(p, 1e-9)
-      double Cc = 0.0;
-      {
-        const float Zf = (float)Z;
-        const float logZ = (float)log(Z);
-        const float ln_floor = logf(1e-9f);
-        const float pre_lim = 2e-9f * Zf;
-        const float d_hi = logf(pre_lim), d_lo = d_hi - 25.f;
-        float cp = 0.f;
-        for (int j = tid; j < nb; j += kStepThreads) {
-          const float dd = __fsub_rn(zof(srow[j]), zmax);
-          if (dd < d_hi && dd >= d_lo) {
-            const float e = expf(dd);
-            if (e > 0.f && e < pre_lim && __fdiv_rn(e, Zf) < 1e-9f) cp = fmaf(e, ln_floor - dd + logZ, cp);
+      __syncthreads();
+      if (tid == 0) {
+        float M = -INFINITY;
+        for (int w = 0; w < kSW; ++w) M = fmaxf(M, redf[w][2]);
+        double Z = 0.0, A = 0.0;
+        for (int w = 0; w < kSW; ++w) {
+          const float mw = redf[w][2];
+          if (mw > -INFINITY) {
+            const double f = exp((double)mw - (double)M);
+            Z += redd[w][2] * f;
+            A += f * (redd[w][3] + redd[w][2] * ((double)mw - (double)M));
           }
         }
-        Cc = cp;
-        double dummy = 0.0;
-        block_sum2d(Cc, dummy, redd);
+        s_part.mx = mx;
+        s_part.cmx = cmx;
+        s_part.m = M;
+        s_part.cs = csum;
+        s_part.cq = csq;
+        s_part.Z = Z;
+        s_part.A = A;
       }
-      H = log(Z) - A / Z - Cc / Z;
-      if (tid == 0 && !((p.debug_flags & kDebugSkipPublish) && hr == 0))
-        str_u64(p.hslot + hr, tword(tag, __float_as_uint((float)H)));
     }
-
-    // ---- bucket geometry (the same in every CTA of the row: block-uniform values) ----
+    cl.sync();  // (1) every rank's part is written
+    if (tid == 0) STEP_STAMP(10);
+    // ---- the row's statistics, folded over the ranks in rank order (the same
+    //      arithmetic in every CTA of the cluster) ----
+    float mx = -INFINITY, cmx = -INFINITY, M = -INFINITY;
+    double csum = 0.0, csq = 0.0, Z = 0.0, A = 0.0;
+    for (int r = 0; r < CL; ++r) {
+      const RankPart* rp = cl.map_shared_rank(&s_part, r);
+      mx = fmaxf(mx, rp->mx);
+      cmx = fmaxf(cmx, rp->cmx);
+      M = fmaxf(M, rp->m);
+      csum += rp->cs;
+      csq += rp->cq;
+    }
+    for (int r = 0; r < CL; ++r) {
+      const RankPart* rp = cl.map_shared_rank(&s_part, r);
+      if (rp->m > -INFINITY) {
+        const double f = exp((double)rp->m - (double)M);
+        Z += rp->Z * f;
+        A += f * (rp->A + rp->Z * ((double)rp->m - (double)M));
+      }
+    }
     const double nc_d = (double)(nb - imin(nb, sink + local));
     const double mean_c = nc_d > 0 ? csum / nc_d : 0.0;
     const double var_c = nc_d > 0 ? csq / nc_d - mean_c * mean_c : 0.0;
@@ -576,80 +783,105 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepParams p) {
     const double range = (double)cmx - (mean_c - sd_c);
     const bool buckets_ok = isfinite(cmx) && range > 0.0 && isfinite(range);
     const float scale = buckets_ok ? (float)((double)(kBk - 1) / range) : 0.f;
+    const float zmax = M;  // = max over the row of s / T
 
-    if (warp == 0) {
-      // ---- entropies of every head of the sequence -> weights ----
-      if (adaptive) {
-        PollBudget pb{p.wait_ns, 0, false};
-        const double lognb = log((double)imax(nb, 2));
-        double ps = 0.0, mine = 0.0;
+    // ---- pass 2: clamp correction, content histogram, each block's bucket ----
+    {
+      float cp = 0.f;
+      const float Zf = (float)Z;
+      const float logZ = adaptive ? (float)log(Z) : 0.f;
+      const float ln_floor = logf(1e-9f);
+      const float pre_lim = 2e-9f * Zf;
+      const float d_hi = adaptive ? logf(pre_lim) : -INFINITY, d_lo = d_hi - 25.f;
+#pragma unroll 1
+      for (int c = tid; c < nch; c += kStepThreads) {
+        const float4 x = srow4[c];
+        const float v[4] = {x.x, x.y, x.z, x.w};
+        uint32_t bk4[4];
 #pragma unroll
-        for (int q4 = 0; q4 < kStepMaxHeads / 32; ++q4) {
-          const int hh = lane + q4 * 32;
-          if (hh < p.Hq) {
-            const unsigned long long* a = p.hslot + b * p.Hq + hh;
-            const unsigned long long w = wait_tagged(a, ldr_u64(a), tag, pb);
-            const double wv = (double)__uint_as_float((uint32_t)w) / lognb + 1e-6;
-            ps += wv;
-            if (hh == h) mine = wv;
+        for (int e = 0; e < 4; ++e) {
+          const int li = 4 * c + e, j = lo + li;
+          const bool in = li < n;
+          int bk = kBk - 1;
+          if (in && buckets_ok && !forced(j)) {
+            bk = bucket_of(v[e], cmx, scale);
+            if (bk < kBk - 1) atomicAdd(&hist[bk], 1u);
           }
-        }
-        if (__any_sync(0xffffffffu, pb.dead) && lane == 0) report(p.status, ADAKV_ST_WAIT_TIMEOUT);
-        ps = warp_sum(ps);  // fixed xor tree: every CTA of the sequence gets the same sum
-        mine = warp_sum(mine);
-        if (lane == 0) {
-          s_sumw = ps;
-          s_w = mine;
-        }
-      }
-    } else if (buckets_ok) {
-      // ---- warps 1-7: content histogram, bucket prefix, bucket sort ----
-      const int t7 = tid - 32, n7 = kStepThreads - 32;
-      for (int j = t7; j < nb; j += n7) {
-        if (!forced(j)) {
-          const int bk = bucket_of(srow[j], cmx, scale);
-          if (bk < kBk - 1) atomicAdd(&hist[bk], 1u);
-        }
-      }
-      named_bar_sync(1, n7);
-      if (warp == 1) {
-        constexpr int PL = kBk / 32;  // buckets per lane
-        uint32_t tot = 0;
-        for (int e = 0; e < PL; ++e) tot += hist[lane * PL + e];
-        uint32_t incl = tot;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
-          if (lane >= o) incl += y;
-        }
-        const uint32_t total = __shfl_sync(0xffffffffu, incl, 31);
-        // buckets any count of this geometry can reach: up to the table width
-        const uint32_t cap = imin((int)total, p.table_width);
-        uint32_t acc = incl - tot;
-        for (int e = 0; e < PL; ++e) {
-          const int bk = lane * PL + e;
-          const uint32_t c = hist[bk];
-          pre[bk] = acc;
-          if (cap > 0 && acc < cap && cap <= acc + c) s_blim = bk;
-          acc += c;
-        }
-      }
-      named_bar_sync(1, n7);
-      const int blim = s_blim;
-      if (blim >= 0) {
-        for (int j = t7; j < nb; j += n7) {
-          if (!forced(j)) {
-            const int bk = bucket_of(srow[j], cmx, scale);
-            if (bk <= blim) {
-              const uint32_t pos = pre[bk] + atomicAdd(&fill[bk], 1u);
-              if (pos < (uint32_t)kStepOrderCap) order[pos] = j;
-              else s_over = 1;
+          bk4[e] = (uint32_t)bk;
+          if (adaptive && in) {
+            const float dd = __fsub_rn(zof(v[e]), zmax);
+            if (dd < d_hi && dd >= d_lo) {
+              const float ex = expf(dd);
+              if (ex > 0.f && ex < pre_lim && __fdiv_rn(ex, Zf) < 1e-9f) cp = fmaf(ex, ln_floor - dd + logZ, cp);
             }
           }
         }
+        reinterpret_cast<uint2*>(sbk)[c] = make_uint2(bk4[0] | (bk4[1] << 16), bk4[2] | (bk4[3] << 16));
+      }
+      double c2 = cp, dummy = 0.0;
+      block_sum2d(c2, dummy, redd);
+      if (tid == 0) {
+        s_part.Cc = c2;
+        STEP_STAMP(16);
+      }
+    }
+    cl.sync();  // (2) every rank's histogram and clamp correction
+    if (tid == 0) STEP_STAMP(17);
+    // the cluster's histogram (thread t: buckets [8t, 8t + 8)) and the entropy
+    {
+      static_assert(kBk == 8 * kStepThreads, "8 buckets per thread");
+      uint4 s0 = make_uint4(0u, 0u, 0u, 0u), s1 = s0;
+      for (int r = 0; r < CL; ++r) {
+        const uint4* rh = reinterpret_cast<const uint4*>(cl.map_shared_rank(hist, r));
+        const uint4 x0 = rh[2 * tid], x1 = rh[2 * tid + 1];
+        s0.x += x0.x; s0.y += x0.y; s0.z += x0.z; s0.w += x0.w;
+        s1.x += x1.x; s1.y += x1.y; s1.z += x1.z; s1.w += x1.w;
+      }
+      reinterpret_cast<uint4*>(ghist)[2 * tid] = s0;
+      reinterpret_cast<uint4*>(ghist)[2 * tid + 1] = s1;
+      if (adaptive && tid == 0) {
+        double Cc = 0.0;
+        for (int r = 0; r < CL; ++r) Cc += cl.map_shared_rank(&s_part, r)->Cc;
+        // entropy, adakv/budget.py:36-37 with the max(p, 1e-9) clamp
+        const double H = log(Z) - A / Z - Cc / Z;
+        if (rank == 0 && !((p.debug_flags & kDebugSkipPublish) && hr == 0))
+          str_u64(p.hslot + hr, tword(tag, __float_as_uint((float)H)));
+        STEP_STAMP(11);
+      }
+    }
+
+    // ---- the sequence's entropies -> this head's weight and the weight sum ----
+    if (warp == 0 && adaptive) {
+      PollBudget pb{p.wait_ns, 0, false};
+      const double lognb = log((double)imax(nb, 2));
+      constexpr int NQ = kStepMaxHeads / 32;
+      const unsigned long long* base = p.hslot + b * p.Hq + lane;
+      const int nq = lane < p.Hq ? ceil_div(p.Hq - lane, 32) : 0;
+      unsigned long long w[NQ];
+#pragma unroll
+      for (int q4 = 0; q4 < NQ; ++q4) w[q4] = q4 < nq ? ldr_u64(base + q4 * 32) : 0ull;
+      wait_tagged_n<NQ>(base, 32, w, nq, tag, pb);
+      double ps = 0.0, mine = 0.0;
+#pragma unroll
+      for (int q4 = 0; q4 < NQ; ++q4) {
+        const int hh = lane + q4 * 32;
+        if (q4 < nq) {
+          // entropy weight, adakv/budget.py:36-37: float32 entropy / log(nb) in float64
+          const double wv = (double)__uint_as_float((uint32_t)w[q4]) / lognb + 1e-6;
+          ps += wv;
+          if (hh == h) mine = wv;
+        }
+      }
+      if (__any_sync(0xffffffffu, pb.dead) && lane == 0) report(p.status, ADAKV_ST_WAIT_TIMEOUT);
+      ps = warp_sum(ps);  // fixed xor tree: every CTA of the sequence gets the same sum
+      mine = warp_sum(mine);
+      if (lane == 0) {
+        s_sumw = ps;
+        s_w = mine;
       }
     }
     __syncthreads();
+    if (tid == 0) STEP_STAMP(3);
 
     // ---- this head's count (budget.py:71-86, selector.py:49-54) ----
     const SeqBudget sbud = seq_budget(nb, cf);
@@ -659,151 +891,143 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepParams p) {
     const int Kc = K - n_forced;
     const bool all = K >= nb;
 
-    // forced blocks (the reference's +inf bias, selector.py:44-48)
-    if (all) {
-      for (int w = tid; w < nw; w += kStepThreads)
-        sbits[w] = (w * 32 + 32 <= nb) ? 0xFFFFFFFFu : ((1u << (nb - w * 32)) - 1u);
-    } else {
-      for (int j = tid; j < sink; j += kStepThreads) atomicOr(&sbits[j >> 5], 1u << (j & 31));
-      for (int j = nb - local + tid; j < nb; j += kStepThreads) atomicOr(&sbits[j >> 5], 1u << (j & 31));
-    }
-    bool use_radix = false;
-    if (!all && Kc > 0) {
-      use_radix = !buckets_ok || s_over != 0 || s_blim < 0;
-      if (!use_radix) {
-        for (int i = tid; i < kBk; i += kStepThreads)
-          if (pre[i] < (uint32_t)Kc && (uint32_t)Kc <= pre[i] + hist[i]) s_jstar = i;
-        __syncthreads();
-        const int js = s_jstar;
-        use_radix = js < 0 || js > s_blim || (int)hist[js] > kStepCandCap;
-        if (!use_radix) {
-          const int above = (int)pre[js], nc = (int)hist[js], need = Kc - above;
-          for (int i = tid; i < above; i += kStepThreads) {
-            const int j = order[i];
-            atomicOr(&sbits[j >> 5], 1u << (j & 31));
-          }
-          for (int u = tid; u < nc; u += kStepThreads) {
-            const int ju = order[above + u];
-            const uint32_t ku = order_key(srow[ju]);
-            int rk = 0;
-            for (int c = 0; c < nc; ++c) {
-              const int jc = order[above + c];
-              const uint32_t kc = order_key(srow[jc]);
-              rk += (kc > ku) || (kc == ku && jc < ju);
-            }
-            if (rk < need) atomicOr(&sbits[ju >> 5], 1u << (ju & 31));
-          }
-        }
-      }
-    }
-    if (use_radix) {
-      // ---- exact radix select of the top K keys (forced blocks = max key),
-      //      ties at the threshold to the lowest block indices ----
-      __syncthreads();
-      for (int j = tid; j < nb; j += kStepThreads)
-        srow[j] = __uint_as_float(forced(j) ? 0xFFFFFFFFu : order_key(srow[j]));
-      uint32_t prefix = 0, pmask = 0;
-      int rem = K;
-#pragma unroll 1
-      for (int pass = 0; pass < 4; ++pass) {
-        const int shift = 24 - 8 * pass;
-        __syncthreads();
-        for (int t = tid; t < 256; t += kStepThreads) hist[t] = 0u;
-        __syncthreads();
-        for (int j = tid; j < nb; j += kStepThreads) {
-          const uint32_t k = __float_as_uint(srow[j]);
-          if ((k & pmask) == prefix) atomicAdd(&hist[(k >> shift) & 0xFFu], 1u);
-        }
-        __syncthreads();
-        if (warp == 0) {
-          uint32_t c[8], tot = 0;
+    // ---- threshold bucket: the one holding the Kc-th content block ----
+    int js = -1, need = 0;
+    if (!all && Kc > 0 && buckets_ok) {
+      const uint4 h0 = reinterpret_cast<const uint4*>(ghist)[2 * tid];
+      const uint4 h1 = reinterpret_cast<const uint4*>(ghist)[2 * tid + 1];
+      const uint32_t c8[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+      uint32_t tot = 0;
 #pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            c[e] = hist[255 - 8 * lane - e];
-            tot += c[e];
-          }
-          uint32_t incl = tot;
+      for (int e = 0; e < 8; ++e) tot += c8[e];
+      uint32_t acc = (uint32_t)block_exclusive_scan((int)tot, scan_scratch);
 #pragma unroll
-          for (int o = 1; o < 32; o <<= 1) {
-            const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
-            if (lane >= o) incl += y;
-          }
-          const uint32_t excl = incl - tot;
-          if (excl < (uint32_t)rem && (uint32_t)rem <= incl) {
-            uint32_t acc = excl;
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              if (acc + c[e] >= (uint32_t)rem) {
-                s_digit = 255 - 8 * lane - e;
-                s_above = (int)acc;
-                break;
-              }
-              acc += c[e];
-            }
-          }
+      for (int e = 0; e < 8; ++e) {
+        if (acc < (uint32_t)Kc && (uint32_t)Kc <= acc + c8[e]) {
+          s_jstar = 8 * tid + e;
+          s_digit = Kc - (int)acc;  // members of the threshold bucket to take
         }
-        __syncthreads();
-        rem -= s_above;
-        prefix |= (uint32_t)s_digit << shift;
-        pmask |= 0xFFu << shift;
-      }
-      // keys above the threshold, then the first `rem` keys equal to it in index order
-      uint32_t* weq = fill;  // [nw]
-      for (int w = warp; w < nw; w += kSW) {
-        const int j = w * 32 + lane;
-        const uint32_t k = j < nb ? __float_as_uint(srow[j]) : 0u;
-        const uint32_t gt = __ballot_sync(0xffffffffu, j < nb && k > prefix);
-        const uint32_t eq = __ballot_sync(0xffffffffu, j < nb && k == prefix);
-        if (lane == 0) {
-          sbits[w] = gt;
-          weq[w] = eq;
-        }
+        acc += c8[e];
       }
       __syncthreads();
-      const int wpt = ceil_div(nw, kStepThreads);
-      const int w0 = imin(tid * wpt, nw), w1 = imin(w0 + wpt, nw);
-      int n_eq = 0;
-      for (int w = w0; w < w1; ++w) n_eq += __popc(weq[w]);
-      int eq_before = block_exclusive_scan(n_eq, scan_scratch);
-      for (int w = w0; w < w1; ++w) {
-        uint32_t e = weq[w];
-        const int take = imax(0, imin(__popc(e), rem - eq_before));
-        eq_before += __popc(e);
-        uint32_t low = 0;
-        for (int t = 0; t < take; ++t) {
-          low |= e & (0u - e);
-          e &= e - 1u;
-        }
-        sbits[w] |= low;
-      }
+      js = s_jstar;
+      need = s_digit;
     }
-    __syncthreads();
+    if (tid == 0) STEP_STAMP(20);
+    // the exact fallback: no usable bucket range, or a crowded threshold bucket
+    const bool exact = !all && Kc > 0 && (js < 0 || js >= kBk - 1 || (int)ghist[js] > kStepCandCap);
 
-    // ---- publish the bitmap (release: the refreshed tokens precede it) ----
-    fence_acq_rel_gpu();
-    for (int w = tid; w < nw; w += kStepThreads)
-      str_u64(p.bitmap + (size_t)hr * p.fb_stride + w, tword(tag, sbits[w]));
-    // ---- ascending block table and count ----
+    if (!exact) {
+      // ---- this rank's slice: forced blocks, buckets above the threshold,
+      //      candidates of the threshold bucket ----
+      for (int w = warp; w < nwl; w += kSW) {
+        const int li = w * 32 + lane, j = lo + li;
+        const bool in = li < n;
+        const int bk = in ? (int)sbk[li] : kBk - 1;
+        const bool sel = in && (all || forced(j) || (Kc > 0 && bk < js));
+        const bool cand = in && !all && Kc > 0 && bk == js && !forced(j);
+        const uint32_t sb = __ballot_sync(0xffffffffu, sel);
+        if (cand) {
+          const int slot = atomicAdd(&s_ncand, 1);
+          ckey[slot] = order_key(srow[li]);
+          cidx[slot] = j;
+        }
+        if (lane == 0) sbits[w] = sb;
+      }
+      __syncthreads();
+      if (tid == 0) s_part.ncand = s_ncand;
+    }
+    cl.sync();  // (3) every rank's candidates
+    if (tid == 0) STEP_STAMP(12);
+    if (exact) {
+      // rank 0 ranks the whole row exactly (radix select); the other ranks publish nothing
+      if (rank == 0) {
+        const int nw = ceil_div(nb, 32);
+        for (int j = 4 * tid; j < nb; j += 4 * kStepThreads)
+          *reinterpret_cast<float4*>(srow + j) = __ldcg(reinterpret_cast<const float4*>(grow + j));
+        for (int w = tid; w < nw; w += kStepThreads) sbits[w] = 0u;
+        __syncthreads();
+        radix_select_top(srow, nb, sink, local, K, hist, ghist, sbits, scan_scratch, &s_digit, &s_above);
+        __syncthreads();
+      }
+    } else if (!all && Kc > 0) {
+      // every rank's candidates, in rank order; each rank decides its own
+      // by exact rank (score desc, index asc) among all of them
+      int off = 0, tot = 0;
+      for (int r = 0; r < CL; ++r) {
+        const int nc = cl.map_shared_rank(&s_part, r)->ncand;
+        if (r < rank) off += nc;
+        tot += nc;
+      }
+      int base = 0;
+      for (int r = 0; r < CL; ++r) {
+        const int nc = cl.map_shared_rank(&s_part, r)->ncand;
+        const uint32_t* rk = cl.map_shared_rank(ckey, r);
+        const int* ri = cl.map_shared_rank(cidx, r);
+        for (int u = tid; u < nc; u += kStepThreads) {
+          akey[base + u] = rk[u];
+          aidx[base + u] = ri[u];
+        }
+        base += nc;
+      }
+      __syncthreads();
+      const int mine = s_ncand;
+      for (int u = tid; u < mine; u += kStepThreads) {
+        const uint32_t ku = akey[off + u];
+        const int iu = aidx[off + u];
+        int rk = 0;
+        for (int c2 = 0; c2 < tot; ++c2) {
+          const uint32_t kc = akey[c2];
+          rk += (kc > ku) || (kc == ku && aidx[c2] < iu);
+        }
+        if (rk < need) atomicOr(&sbits[(iu - lo) >> 5], 1u << ((iu - lo) & 31));
+      }
+      __syncthreads();
+    }
+    if (tid == 0) STEP_STAMP(14);
+
+    // ---- publish this rank's bitmap words and its ascending table segment ----
+    const bool writes = !exact || rank == 0;
+    const int wb = exact ? 0 : w_lo, wn = exact ? ceil_div(nb, 32) : nwl;
     {
-      const int wpt = ceil_div(nw, kStepThreads);
-      const int w0 = imin(tid * wpt, nw), w1 = imin(w0 + wpt, nw);
+      uint32_t* brow = p.bitmap + (size_t)hr * p.fb_stride + wb;
+      for (int w = tid; w < wn && writes; w += kStepThreads) brow[w] = sbits[w];
+      const int wpt = ceil_div(wn, kStepThreads);
+      const int w0 = imin(tid * wpt, wn), w1 = imin(w0 + wpt, wn);
       int cnt = 0;
-      for (int w = w0; w < w1; ++w) cnt += __popc(sbits[w]);
+      for (int w = w0; w < w1 && writes; ++w) cnt += __popc(sbits[w]);
       int pos = block_exclusive_scan(cnt, scan_scratch);
-      const int total = scan_scratch[32];
+      if (tid == 0) s_part.nsel = writes ? scan_scratch[32] : 0;
+      cl.sync();  // (4) every rank's count; after this no rank reads another's shared memory
+      if (tid == 0) STEP_STAMP(18);
+      int before = 0, total = 0;
+      for (int r = 0; r < CL; ++r) {
+        const int ns = cl.map_shared_rank(&s_part, r)->nsel;
+        if (r < rank) before += ns;
+        total += ns;
+      }
+      pos += before;
       int* trow = p.block_table + (int64_t)hr * p.table_width;
-      for (int w = w0; w < w1; ++w) {
-        uint32_t s = sbits[w];
-        while (s) {
-          const int bit = __ffs(s) - 1;
-          s &= s - 1u;
-          if (pos < p.table_width) trow[pos] = w * 32 + bit;
+      for (int w = w0; w < w1 && writes; ++w) {
+        uint32_t sw = sbits[w];
+        while (sw) {
+          const int bit = __ffs(sw) - 1;
+          sw &= sw - 1u;
+          if (pos < p.table_width) trow[pos] = (wb + w) * 32 + bit;
           ++pos;
         }
       }
-      if (tid == 0) p.sel_lens[hr] = total;
+      if (rank == 0 && tid == 0) p.sel_lens[hr] = total;
     }
-    __syncthreads();  // phase C reuses the shared memory
+    __syncthreads();
+    if (tid == 0) {
+      fence_acq_rel_gpu();  // release: the bitmap words, and the appended tokens acquired above
+      str_u64(p.ready + (size_t)hr * CL + rank, tword(tag, 1u));
+      STEP_STAMP(4);
+    }
+    // (the ranks still read each other's s_part after barrier 4: keep every
+    // CTA of the cluster resident until they are done; see the end of the kernel)
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
   }
 
   // ---------------------------------------------------------------- phase C
@@ -818,7 +1042,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepParams p) {
     const int nb = ceil_div(S, BS);
     const int nw = ceil_div(nb, 32);
     const int row0 = b * p.Hq + kvh * G;
-    const StepSmem L = step_smem_layout(D, G, p.nb_max, p.nbt, p.slice_cap);
+    const StepSmem L = step_smem_layout(D, G, p.nb_max, p.nbt, p.slice_cap, CL);
     T* kvbuf = reinterpret_cast<T*>(sm + L.kv);
     uint32_t* uw = reinterpret_cast<uint32_t*>(sm + L.uw);
     uint32_t* hw = reinterpret_cast<uint32_t*>(sm + L.hw);
@@ -826,7 +1050,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepParams p) {
     uint32_t* lmask = reinterpret_cast<uint32_t*>(sm + L.mask);
     float* wpart = reinterpret_cast<float*>(sm + L.wpart);
     float* mf = reinterpret_cast<float*>(sm + L.merge);
-    float* ml = mf + kStepMaxGrid * G;
+    float* ml = mf + 2 * kStepMaxGrid * G;
     float* mL = ml + G;
     const T* kbase = static_cast<const T*>(p.k.data) + b * p.k.sb + kvh * p.k.sh;
     const T* vbase = static_cast<const T*>(p.v.data) + b * p.v.sb + kvh * p.v.sh;
@@ -851,29 +1075,30 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepParams p) {
     }
     const float scale_log2 = p.sm_scale * 1.4426950408889634f;
 
-    // ---- the group's bitmaps (this call's words) -> union, head words ----
+    // ---- the group's G bitmaps: warp 0 waits for the G x CL ready words ----
+    if (warp == 0) {
+      PollBudget pb{p.wait_ns, 0, false};
+      const int nr = G * CL;  // <= 32
+      unsigned long long x[1] = {lane < nr ? ldr_u64(p.ready + (size_t)row0 * CL + lane) : 0ull};
+      wait_tagged_n<1>(p.ready + (size_t)row0 * CL + lane, 1, x, lane < nr ? 1 : 0, tag, pb);
+      if (__any_sync(0xffffffffu, pb.dead) && lane == 0) report(p.status, ADAKV_ST_WAIT_TIMEOUT);
+      fence_acq_rel_gpu();  // acquire: the bitmaps and the appended K/V tokens
+    }
+    __syncthreads();
+    if (tid == 0) STEP_STAMP(5);
     const int wpt = ceil_div(nw, kStepThreads);
     const int w0 = imin(tid * wpt, nw), w1 = imin(w0 + wpt, nw);
     int cnt = 0;
-    {
-      PollBudget pb{p.wait_ns, 0, false};
-      for (int w = w0; w < w1; ++w) {
-        unsigned long long x[G];
+    for (int w = w0; w < w1; ++w) {
+      uint32_t u = 0;
 #pragma unroll
-        for (int hh = 0; hh < G; ++hh) x[hh] = ldr_u64(p.bitmap + (size_t)(row0 + hh) * p.fb_stride + w);
-        uint32_t u = 0;
-#pragma unroll
-        for (int hh = 0; hh < G; ++hh) {
-          const unsigned long long* a = p.bitmap + (size_t)(row0 + hh) * p.fb_stride + w;
-          const uint32_t v = (uint32_t)wait_tagged(a, x[hh], tag, pb);
-          hw[hh * nw + w] = v;
-          u |= v;
-        }
-        uw[w] = u;
-        cnt += __popc(u);
+      for (int hh = 0; hh < G; ++hh) {
+        const uint32_t v = __ldcg(p.bitmap + (size_t)(row0 + hh) * p.fb_stride + w);
+        hw[hh * nw + w] = v;
+        u |= v;
       }
-      if (pb.dead) report(p.status, ADAKV_ST_WAIT_TIMEOUT);
-      fence_acq_rel_gpu();  // acquire: the appended K/V tokens are visible below
+      uw[w] = u;
+      cnt += __popc(u);
     }
     const int before = block_exclusive_scan(cnt, scan_scratch);
     const int U = scan_scratch[32];
@@ -948,6 +1173,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepParams p) {
       }
       __syncthreads();  // this stage is refilled two batches later
     }
+    if (tid == 0) STEP_STAMP(13);
 
     // ---- warp partials -> this CTA's partial (m in log2 units, l, o) ----
     {
@@ -975,7 +1201,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepParams p) {
       }
     }
     __syncthreads();
-    unsigned long long* gpart = p.part + (size_t)cta * G * (D + 2);
+    float* gpart = p.part + (size_t)cta * G * (D + 2);
     for (int idx = tid; idx < G * D; idx += kStepThreads) {
       const int hh = idx / D, dd = idx - hh * D;
       float M = -INFINITY;
@@ -989,31 +1215,48 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepParams p) {
           O += rp[2 + dd] * f;
         }
       }
-      str_u64(gpart + hh * (D + 2) + 2 + dd, tword(tag, __float_as_uint(O)));
+      gpart[hh * (D + 2) + 2 + dd] = O;
       if (dd == 0) {
-        str_u64(gpart + hh * (D + 2), tword(tag, __float_as_uint(M)));
-        str_u64(gpart + hh * (D + 2) + 1, tword(tag, __float_as_uint(Ls)));
+        gpart[hh * (D + 2)] = M;
+        gpart[hh * (D + 2) + 1] = Ls;
       }
+    }
+    __syncthreads();
+    if (tid == 0) {
+      fence_acq_rel_gpu();  // release: this CTA's partial
+      str_u64(p.pready + cta, tword(tag, 1u));
+      STEP_STAMP(6);
     }
 
     // ---- the group's first CTA merges the SPLIT partials in split order ----
     if (split == 0) {
-      PollBudget pb{p.wait_ns, 0, false};
-      const unsigned long long* gp0 = p.part + (size_t)c_first * G * (D + 2);
+      if (warp == 0) {
+        PollBudget pb{p.wait_ns, 0, false};
+        constexpr int NP = kStepMaxGrid / 32;
+        const unsigned long long* base = p.pready + c_first + lane;
+        const int np = lane < SPLIT ? ceil_div(SPLIT - lane, 32) : 0;
+        unsigned long long x[NP];
+#pragma unroll
+        for (int i = 0; i < NP; ++i) x[i] = i < np ? ldr_u64(base + i * 32) : 0ull;
+        wait_tagged_n<NP>(base, 32, x, np, tag, pb);
+        if (__any_sync(0xffffffffu, pb.dead) && lane == 0) report(p.status, ADAKV_ST_WAIT_TIMEOUT);
+        fence_acq_rel_gpu();  // acquire: the partials
+      }
+      __syncthreads();
+      const float* gp0 = p.part + (size_t)c_first * G * (D + 2);
       const size_t stride = (size_t)G * (D + 2);
       for (int hh = warp; hh < G; hh += kSW) {
         float Mx = -INFINITY;
         for (int s0 = lane; s0 < SPLIT; s0 += 32) {
-          const unsigned long long* a = gp0 + s0 * stride + hh * (D + 2);
-          const float m = __uint_as_float((uint32_t)wait_tagged(a, ldr_u64(a), tag, pb));
+          const float m = __ldcg(gp0 + s0 * stride + hh * (D + 2));
           mf[s0 * G + hh] = m;
+          mf[(kStepMaxGrid + s0) * G + hh] = __ldcg(gp0 + s0 * stride + hh * (D + 2) + 1);
           Mx = fmaxf(Mx, m);
         }
         Mx = warp_max(Mx);
         float Ls = 0.f;
         for (int s0 = lane; s0 < SPLIT; s0 += 32) {
-          const unsigned long long* a = gp0 + s0 * stride + hh * (D + 2) + 1;
-          const float l = __uint_as_float((uint32_t)wait_tagged(a, ldr_u64(a), tag, pb));
+          const float l = mf[(kStepMaxGrid + s0) * G + hh];
           const float m = mf[s0 * G + hh];
           const float f = (Mx == -INFINITY || m == -INFINITY) ? 0.f : exp2f(m - Mx);
           mf[s0 * G + hh] = f;
@@ -1028,18 +1271,15 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepParams p) {
       __syncthreads();
       for (int idx = tid; idx < G * D; idx += kStepThreads) {
         const int hh = idx / D, dd = idx - hh * D;
-        const unsigned long long* src = gp0 + (size_t)hh * (D + 2) + 2 + dd;
+        const float* src = gp0 + (size_t)hh * (D + 2) + 2 + dd;
         float O = 0.f;
         for (int s0 = 0; s0 < SPLIT; s0 += 16) {
-          unsigned long long v[16];
+          float v[16];
 #pragma unroll
-          for (int u = 0; u < 16; ++u) v[u] = s0 + u < SPLIT ? ldr_u64(src + (size_t)(s0 + u) * stride) : 0ull;
+          for (int u = 0; u < 16; ++u) v[u] = s0 + u < SPLIT ? __ldcg(src + (size_t)(s0 + u) * stride) : 0.f;
 #pragma unroll
           for (int u = 0; u < 16; ++u)
-            if (s0 + u < SPLIT) {
-              const uint64_t x = wait_tagged(src + (size_t)(s0 + u) * stride, v[u], tag, pb);
-              O += mf[(s0 + u) * G + hh] * __uint_as_float((uint32_t)x);
-            }
+            if (s0 + u < SPLIT) O += mf[(s0 + u) * G + hh] * v[u];
         }
         const float Ls = mL[hh];
         const float res = Ls > 0.f ? O / Ls : 0.f;
@@ -1050,15 +1290,18 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepParams p) {
         const float M = ml[tid], Ls = mL[tid];
         p.lse[row0 + tid] = (Ls > 0.f && M > -INFINITY) ? M * 0.6931471805599453f + logf(Ls) : -INFINITY;
       }
-      if (pb.dead) report(p.status, ADAKV_ST_WAIT_TIMEOUT);
     }
   }
+
+  // peers may still read this CTA's s_part until they arrive
+  if (head_cta) asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 
   // ---------------------------------------------------------------- call tag
   // The last CTA to finish advances the call counter (every CTA read it at
   // its start), so the next call's words carry a new tag.
   __syncthreads();
   if (tid == 0) {
+    STEP_STAMP(7);
     unsigned prev;
     asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(p.epoch + 1) : "memory");
     if (prev == (unsigned)(GRID - 1)) {
@@ -1071,20 +1314,20 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepParams p) {
 // ---------------------------------------------------------------------------
 // last step's block scores -> float rows (either path's layout)
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(256) step_scores_kernel(bool fused, const unsigned long long* fscores,
+__global__ void __launch_bounds__(256) step_scores_kernel(bool fused, const float* fscores,
                                                           int fs_stride, const float* scores,
                                                           int score_stride, int nb, float* out,
                                                           int out_stride) {
   const int r = blockIdx.x;
   for (int j = threadIdx.x; j < nb; j += blockDim.x) {
     float v;
-    if (fused) v = __uint_as_float((uint32_t)fscores[(size_t)r * fs_stride + j]);
+    if (fused) v = fscores[(size_t)r * fs_stride + j];
     else v = scores[(size_t)r * score_stride + j];
     out[(size_t)r * out_stride + j] = v;
   }
 }
 
-cudaError_t launch_step_scores(bool fused, const unsigned long long* fscores, int fs_stride,
+cudaError_t launch_step_scores(bool fused, const float* fscores, int fs_stride,
                                const float* scores, int score_stride, int rows, int nb, float* out,
                                int out_stride, cudaStream_t st) {
   step_scores_kernel<<<rows, 256, 0, st>>>(fused, fscores, fs_stride, scores, score_stride, nb, out,
@@ -1115,13 +1358,13 @@ bool step_kernel_built(int dtype, int D, int bs, int g) {
          (g == 4 || g == 8);
 }
 
-size_t step_smem_bytes(int D, int g, int nb_max, int min_split, int* nbt, int* slice_cap) {
+size_t step_smem_bytes(int D, int g, int nb_max, int min_split, int csize, int* nbt, int* slice_cap) {
   const int sc = ceil_div(imax(nb_max, 1), imax(min_split, 1)) + 1;
   int t = 8;
-  StepSmem s = step_smem_layout(D, g, nb_max, t, sc);
+  StepSmem s = step_smem_layout(D, g, nb_max, t, sc, csize);
   while (s.total > kStepSmemMax && t > 1) {
     --t;
-    s = step_smem_layout(D, g, nb_max, t, sc);
+    s = step_smem_layout(D, g, nb_max, t, sc, csize);
   }
   if (nbt) *nbt = t;
   if (slice_cap) *slice_cap = sc;
@@ -1141,9 +1384,34 @@ cudaError_t step_kernels_init() {
 
 cudaError_t launch_step(const StepParams& p, int dtype, int D, int g, int grid, size_t smem,
                         cudaStream_t st, const LaunchOpts& o) {
+  LaunchOpts oc = o;
+  oc.cluster_x = (unsigned)p.csize;
   return for_each_step(dtype, D, g, [&](auto kern) {
-    return launch_ex(kern, dim3(grid), dim3(kStepThreads), smem, st, o, p);
+    return launch_ex(kern, dim3(grid), dim3(kStepThreads), smem, st, oc, p);
   });
+}
+
+int step_active_clusters(int dtype, int D, int g, int csize, size_t smem) {
+  int n = 0;
+  const cudaError_t e = for_each_step(dtype, D, g, [&](auto kern) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(csize, 1, 1);
+    cfg.blockDim = dim3(kStepThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = csize;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
+  });
+  if (e != cudaSuccess) {
+    (void)cudaGetLastError();
+    return 0;
+  }
+  return n;
 }
 
 }  // namespace adakv

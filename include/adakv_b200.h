@@ -278,6 +278,19 @@ int adakv_last_path(const void* workspace);
 #define ADAKV_KNOB_STEP_PATH 3
 int adakv_debug_knob(int32_t knob, int64_t value);
 
+/* Test-only: with ADAKV_KNOB_FLAGS bit 1 set, the one-kernel step records per
+ * CTA 24 words: globaltimer stamps (ns) of its phase boundaries, in order
+ * start, estimator end, score row loaded, budgets known, bitmap published,
+ * group bitmaps read, partial published, end, first and last estimator
+ * stage arrived, row statistics, entropy published, bucket sort done,
+ * gather done, selection done, one word of selection-path flags, softmax
+ * sums, clamp correction, histogram, bucket prefix, bucket sort (3 spare).
+ * Synchronises `stream`, copies max_ctas * 24 words of the last step on
+ * `workspace` to the host array `out`.  No counterpart in the
+ * reference. */
+int adakv_debug_timeline(const adakv_geometry* geo, void* workspace, size_t workspace_bytes,
+                         uint64_t* out, int32_t max_ctas, void* stream);
+
 /* ---- sequence-sharded decode (one sequence's blocks split over GPUs) ----
  * The reference decodes one sequence on one device; these four calls split
  * its steps so that a long sequence can be sharded by contiguous blocks:
