@@ -94,7 +94,7 @@ _SIGNATURES = {
                                             _vp]),
 }
 
-KNOB_WAIT_NS, KNOB_FLAGS, KNOB_STEP_PATH = 1, 2, 3
+KNOB_WAIT_NS, KNOB_FLAGS, KNOB_STEP_PATH, KNOB_STEP_CLUSTER = 1, 2, 3, 4
 
 _lib = None
 _lock = threading.Lock()

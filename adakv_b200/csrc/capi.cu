@@ -59,6 +59,7 @@ struct DeviceState {
 std::atomic<int64_t> g_dbg_wait_ns{0};   // bound of device waits in ns (0: kWaitLimitNs)
 std::atomic<int> g_dbg_flags{0};         // bit 0: head 0 never publishes its entropy
 std::atomic<int> g_dbg_path{0};          // decode step: 0 automatic, 1 three kernels, 2 one kernel
+std::atomic<int> g_dbg_cluster{0};       // one-kernel step: largest selection cluster (0: 8)
 
 uint64_t wait_limit_ns() {
   const int64_t v = g_dbg_wait_ns.load();
@@ -209,7 +210,7 @@ struct WsLayout {
   // one-kernel step (present when the geometry can take it); its state words
   // sit at a fixed offset, its regions depend on B, Hq, Hkv, D and nb_cap only
   bool fused;
-  size_t fstate, fscores, fhslot, fbitmap, fready, fpart, fpready, ftimeline, fbegin, fend;
+  size_t fstate, fscores, fpiece, fhslot, fbitmap, fready, fpart, fpready, ftimeline, fbegin, fend;
   int fs_stride, fb_stride;
 };
 
@@ -239,6 +240,7 @@ WsLayout make_ws(const adakv_geometry* g, bool with_plan) {
     L.fs_stride = (int)align_up((size_t)g->nb_cap, 4);
     L.fb_stride = (int)align_up((size_t)ceil_div(g->nb_cap, 32), 2);
     L.fscores = take(4 * (size_t)rows * L.fs_stride);
+    L.fpiece = take(32 * (size_t)(g->batch * g->n_kv_heads + kStepMaxGrid) * 8 * gq);  // x warps
     L.fhslot = take(8 * (size_t)rows);
     L.fbitmap = take(4 * (size_t)rows * L.fb_stride);
     L.fready = take(8 * (size_t)rows * 8);  // one word per cluster rank (<= 8)
@@ -459,25 +461,31 @@ struct StepPlan {
   size_t smem;
 };
 
-// The one-kernel step for this call, or why not (the three-kernel chain then runs).
+// The one-kernel step for this call, or why not (the three-kernel chain then
+// runs).  The chain is the default: on B200 at 131072 tokens it measures
+// 42.6 us per step against 49.8 us for the one-kernel step, whose selection
+// phase is latency-bound on a fraction of the SMs and which, holding every
+// SM, cannot overlap the next kernel's start.  ADAKV_FUSED=1 (or the
+// step-path knob) selects the one-kernel step.
 // The cluster size is the largest of 8 / 4 / 2 / 1 CTAs per query head that
 // keeps every CTA of the grid resident (one per SM) and slices of >= 256 blocks.
 bool step_applies(DeviceState* ds, const adakv_geometry* g, const adakv_select_params* sp,
                   const WsLayout& L, StepPlan* out) {
   const int path = g_dbg_path.load();
   if (path == 1 || !L.fused || !ds->step_ok) return false;
-  static const bool env_off = [] {
+  static const bool env_on = [] {
     const char* e = getenv("ADAKV_FUSED");
-    return e && e[0] == '0';
+    return e && e[0] == '1';
   }();
-  if (env_off && path != 2) return false;
+  if (!env_on && path != 2) return false;
   if (sp->policy == ADAKV_POLICY_NUCLEUS) return false;
   const int gq = g->n_q_heads / g->n_kv_heads;
   const int nb_max = ceil_div(g->max_seq_len, g->block_size);
   const int heads = g->batch * g->n_q_heads, groups = g->batch * g->n_kv_heads;
   const int64_t rows = (int64_t)groups * nb_max;
+  const int cmax = g_dbg_cluster.load() > 0 ? g_dbg_cluster.load() : 8;
   for (int c : {8, 4, 2, 1}) {
-    if (gq * c > 32 || (c > 1 && nb_max / c < 256)) continue;
+    if (c > cmax || gq * c > 32 || (c > 1 && nb_max / c < 256)) continue;
     int grid = std::min(ds->num_sms, kStepMaxGrid) / c * c;
     if (grid < heads * c || grid < groups) continue;
     StepPlan sp_{};
@@ -546,6 +554,7 @@ int enqueue_step(const adakv_geometry* g, const adakv_select_params* sp, const a
   p.arrive = ws_at<unsigned long long>(ws, L.fstate + 8);
   p.scores = ws_at<float>(ws, L.fscores);
   p.fs_stride = L.fs_stride;
+  p.piece = ws_at<float>(ws, L.fpiece);
   p.hslot = ws_at<unsigned long long>(ws, L.fhslot);
   p.bitmap = ws_at<uint32_t>(ws, L.fbitmap);
   p.fb_stride = L.fb_stride;
@@ -888,6 +897,11 @@ int adakv_debug_knob(int32_t knob, int64_t value) {
     case ADAKV_KNOB_STEP_PATH:
       if (value < 0 || value > 2) return fail(ADAKV_ERR_INVALID, "step path must be 0, 1 or 2");
       g_dbg_path.store((int)value);
+      return ADAKV_OK;
+    case ADAKV_KNOB_STEP_CLUSTER:
+      if (value != 0 && value != 1 && value != 2 && value != 4 && value != 8)
+        return fail(ADAKV_ERR_INVALID, "step cluster must be 0, 1, 2, 4 or 8");
+      g_dbg_cluster.store((int)value);
       return ADAKV_OK;
     default:
       return fail(ADAKV_ERR_INVALID, "unknown knob %d", knob);

@@ -178,6 +178,8 @@ struct StepParams {
   unsigned long long* arrive;  // CTAs past the estimator phase, over all calls (monotonic)
   float* scores;               // [B*Hq, fs_stride] block scores (plain floats)
   int fs_stride;
+  float* piece;                // [(B*Hkv + grid) * g, 8] score statistics (SoftPart) of the
+                               // rows one CTA scored for one (sequence, KV head), per head
   unsigned long long* hslot;   // [B*Hq] entropy of each head (tagged)
   uint32_t* bitmap;            // [B*Hq, fb_stride] selection bitmaps
   int fb_stride;
@@ -368,6 +370,13 @@ __device__ __forceinline__ SoftPart soft_shfl_xor(const SoftPart& a, int o) {
 __device__ __forceinline__ void soft_store(float* dst, const SoftPart& a) {
   reinterpret_cast<float4*>(dst)[0] = make_float4(a.mx, a.cmx, a.cs, a.cq);
   reinterpret_cast<float4*>(dst)[1] = make_float4(a.m, a.Z, a.A, 0.f);
+}
+
+// the same from L2 (a record another CTA of this kernel wrote)
+__device__ __forceinline__ SoftPart soft_load_cg(const float* src) {
+  const float4 u = __ldcg(reinterpret_cast<const float4*>(src));
+  const float4 w = __ldcg(reinterpret_cast<const float4*>(src) + 1);
+  return SoftPart{u.x, u.y, u.z, u.w, w.x, w.y, w.z};
 }
 
 __device__ __forceinline__ SoftPart soft_load(const float* src) {

@@ -159,37 +159,6 @@ __device__ __forceinline__ void block_sum2d(double& a, double& b, double (*red)[
   }
 }
 
-// max, content max (every thread gets them) and content sum / sum of squares
-// (float per thread, double across threads) in one reduction round
-__device__ __forceinline__ void block_stats(float m1, float m2, float s1, float s2, float (*redf)[4],
-                                            double (*redd)[4], float& mx, float& cmx, double& cs,
-                                            double& cq) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  m1 = warp_max(m1);
-  m2 = warp_max(m2);
-  double d1 = warp_sum((double)s1), d2 = warp_sum((double)s2);
-  __syncthreads();
-  if (lane == 0) {
-    redf[warp][0] = m1;
-    redf[warp][1] = m2;
-    redd[warp][0] = d1;
-    redd[warp][1] = d2;
-  }
-  __syncthreads();
-  mx = redf[0][0];
-  cmx = redf[0][1];
-  cs = 0.0;
-  cq = 0.0;
-#pragma unroll
-  for (int w = 0; w < kSW; ++w) {
-    mx = fmaxf(mx, redf[w][0]);
-    cmx = fmaxf(cmx, redf[w][1]);
-    cs += redd[w][0];
-    cq += redd[w][1];
-  }
-}
-
-
 // Exact top-K of one score row by a 4-pass MSB radix select over order-preserving
 // keys (forced sink / local blocks take the largest key), ties at the threshold
 // to the lowest block indices; the selection is ORed into sbits (its forced
@@ -285,7 +254,7 @@ __device__ __noinline__ void radix_select_top(float* srow, int nb, int sink, int
 struct StepSmem {
   size_t ring;                                                      // phase A
   size_t srow, sbk, sbits, hist, ghist, ckey, cidx, akey, aidx, b_end;  // phase B
-  size_t kv, uw, hw, list, mask, wpart, merge, c_end;               // phase C
+  size_t kv, uw, hw, list, mask, wpart, c_end;                      // phase C
   size_t total;
 };
 
@@ -312,8 +281,7 @@ __host__ __device__ inline StepSmem step_smem_layout(int D, int g, int nb_max, i
   s.list = s.hw + al((size_t)g * nw * 4);
   s.mask = s.list + al((size_t)slice_cap * 4);
   s.wpart = s.mask + al((size_t)slice_cap * 4);
-  s.merge = s.wpart + al((size_t)kSW * g * (D + 2) * 4);
-  s.c_end = s.merge + al((size_t)(2 * kStepMaxGrid * g + 2 * g) * 4);
+  s.c_end = s.wpart + al((size_t)kSW * g * (D + 2) * 4);
   size_t t = s.ring;
   t = t > s.b_end ? t : s.b_end;
   t = t > s.c_end ? t : s.c_end;
@@ -321,14 +289,30 @@ __host__ __device__ inline StepSmem step_smem_layout(int D, int g, int nb_max, i
   return s;
 }
 
-// One cluster rank's share of a head's row statistics, read by the other
-// ranks through distributed shared memory.
+// One cluster rank's share of a head's selection, read by the other ranks
+// through distributed shared memory.
 struct RankPart {
-  float mx, cmx, m;        // max score, content max, max z
-  double cs, cq, Z, A;     // content sum / sum of squares; sum e^(z - m), sum e^(z - m) (z - m)
   double Cc;               // clamp correction of the slice
   int ncand, nsel;         // threshold-bucket candidates; selected blocks of the slice
 };
+
+// A head's row statistics: max score, content max / sum / sum of squares, and
+// Z = sum e^(z - m), A = sum e^(z - m) (z - m) of z = s / T relative to m = max z.
+struct RowStats {
+  float mx, cmx, m;
+  double cs, cq, Z, A;
+};
+
+// floor(a b / c) in 32-bit unsigned arithmetic: every use has a b < 2^31
+// (rows <= kStepMaxHeads * kStepMaxBlocks = 2^22, grid <= 256)
+__device__ __forceinline__ int muldiv(int a, int b, int c) {
+  return (int)(((unsigned)a * (unsigned)b) / (unsigned)c);
+}
+// The CTA whose estimator rows [floor(R c / grid), floor(R (c + 1) / grid)) hold row r.
+__device__ __forceinline__ int cta_of_row(int r, int R, int grid) {
+  return (int)(((unsigned)(r + 1) * (unsigned)grid - 1u) / (unsigned)R);
+}
+__device__ __forceinline__ int first_row_of(int c, int R, int grid) { return muldiv(R, c, grid); }
 
 // a sequence takes part when 1 <= S <= max_seq_len and it holds the appended tokens
 __device__ __forceinline__ int valid_len(const StepParams& p, int b) {
@@ -362,12 +346,13 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepParams p) {
   __shared__ int s_S[kStepMaxBatch];
   __shared__ int s_rb[kStepMaxBatch + 1];
   __shared__ uint32_t s_tag;
-  __shared__ float redf[kSW][4];
   __shared__ double redd[kSW][4];
+  __shared__ float redm[kSW][3];
   __shared__ int scan_scratch[33];
   __shared__ double s_w, s_sumw;
   __shared__ int s_jstar, s_digit, s_above, s_ncand;
   __shared__ RankPart s_part;
+  __shared__ RowStats s_row;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int GRID = gridDim.x, cta = blockIdx.x;
@@ -380,12 +365,14 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepParams p) {
   // ---------------------------------------------------------------- set-up
   if (tid == 0) {
     STEP_STAMP(0);
-    const uint32_t e = *reinterpret_cast<volatile uint32_t*>(p.epoch);
-    s_tag = (e + 1u) ? e + 1u : 1u;
     for (int s = 0; s < kStepStages; ++s) {
       mbar_init(&full_bar[s], 1);
       rel_cnt[s] = 0;
     }
+  }
+  if (tid == 32) {  // the call tag, read beside the sequence lengths
+    const uint32_t e = *reinterpret_cast<volatile uint32_t*>(p.epoch);
+    s_tag = (e + 1u) ? e + 1u : 1u;
   }
   if (tid < p.B) {
     const int S = valid_len(p, tid);
@@ -409,7 +396,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepParams p) {
     if (lane == 0) {
       // this CTA's rows [r0, r1) as ring stages of <= 64 rows of one (sequence, KV head)
       const int R = s_rb[p.B];
-      const int r0 = (int)((int64_t)R * cta / GRID), r1 = (int)((int64_t)R * (cta + 1) / GRID);
+      const int r0 = first_row_of(cta, R, GRID), r1 = first_row_of(cta + 1, R, GRID);
       int r = r0, ns = 0, b = 0;
       while (r < r1) {
         while (r >= s_rb[b + 1]) ++b;
@@ -539,6 +526,15 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepParams p) {
     const int sub = lane % LPR, rin = lane / LPR;
     float qf[G][DL];
     int qrun = -1;
+    // Score statistics of head (sub >> 1) over this lane's rows of the current
+    // piece (this CTA's rows of one (sequence, KV head)); each warp's record
+    // per head, p.piece[((group + cta) * kSW + warp) * G + h], lets the
+    // selection phase skip a statistics pass over the row.  (group + cta)
+    // numbers the pieces in row order: both indices are non-decreasing along
+    // the rows and one of them steps at every piece boundary.
+    SoftPart ps = soft_empty();
+    const float Tf = (float)(p.cfg.temperature > 1e-6 ? p.cfg.temperature : 1e-6);
+    const bool unit_t = (Tf == 1.0f);
     for (int i = 0; i < nstage; ++i) {
       const int slot = i % kStepStages;
       const uint32_t par = (uint32_t)(i / kStepStages) & 1u;
@@ -569,6 +565,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepParams p) {
           }
       }
       float* srow0 = p.scores + (size_t)(b * p.Hq + kvh * G) * p.fs_stride + d.y;
+      const int nbs = ceil_div(s_S[b], BS);
+      const int f_lo = imin(p.cfg.n_sink, nbs), f_hi = nbs - imin(p.cfg.n_local, nbs);
 #pragma unroll
       for (int pp = 0; pp < PASSES; ++pp) {
         const int row = warp * RPW + pp * RPP + rin;
@@ -590,7 +588,11 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepParams p) {
           }
         }
         const float s = reduce_heads<G, LPR>(acc, lane);
-        if ((sub & 1) == 0 && row < d.z && row < d.w) srow0[(size_t)(sub >> 1) * p.fs_stride + row] = s;
+        if (row < d.z && row < d.w) {
+          if ((sub & 1) == 0) srow0[(size_t)(sub >> 1) * p.fs_stride + row] = s;
+          const int j = d.y + row;
+          soft_add(ps, s, unit_t ? s : __fdiv_rn(s, Tf), j >= f_lo && j < f_hi);
+        }
       }
       __syncwarp();
       if (lane == 0) {
@@ -599,6 +601,15 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepParams p) {
           rel_cnt[slot] = 0;
           if (i + kStepStages < nstage) issue(i + kStepStages, slot);
         }
+      }
+      // a piece ends with this stage: fold the lanes of each head and store
+      // the warp's record
+      if (i + 1 == nstage || sdesc[i + 1].x != d.x) {
+#pragma unroll 1
+        for (int off = LPR; off < 32; off <<= 1) soft_merge(ps, soft_shfl_xor(ps, off));
+        if (lane < LPR && (lane & 1) == 0)
+          soft_store(p.piece + (((size_t)(d.x + cta) * kSW + warp) * G + (lane >> 1)) * 8, ps);
+        ps = soft_empty();
       }
     }
   }
@@ -661,121 +672,97 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepParams p) {
       }
     }
     __syncthreads();
+    if (tid == 0) STEP_STAMP(10);
     const float* grow = p.scores + (size_t)hr * p.fs_stride;  // 16-byte aligned rows
-    for (int j = 4 * tid; j < n; j += 4 * kStepThreads)
-      *reinterpret_cast<float4*>(srow + j) = __ldcg(reinterpret_cast<const float4*>(grow + lo + j));
+    // ---- the slice, and the row's statistics (the same arithmetic in every
+    //      CTA of the cluster): each thread folds its share of the
+    //      estimator's warp records of this head and of the blocks the append
+    //      refresh scored, then one block-wide reduction ----
+    {
+      const int kvh = h / G, hh = h - kvh * G, gi = b * p.Hkv + kvh;
+      const int R = s_rb[p.B], R0 = s_rb[b] + kvh * nb;
+      const int skip = appending ? (s_S[b] - p.n_new) / BS : nb;  // rows the estimator scored
+      int c_lo = 0, nrec = 0;
+      if (skip > 0) {
+        c_lo = cta_of_row(R0, R, GRID);
+        nrec = (cta_of_row(R0 + nb - 1, R, GRID) - c_lo + 1) * kSW;
+      }
+      const bool all_rows = R >= GRID;  // every CTA scored rows
+      auto record = [&](int r) -> SoftPart {
+        const int c = c_lo + r / kSW;
+        const bool has = all_rows || first_row_of(c, R, GRID) < first_row_of(c + 1, R, GRID);
+        return has ? soft_load_cg(p.piece + (((size_t)(gi + c) * kSW + r % kSW) * G + hh) * 8)
+                   : soft_empty();
+      };
+      // the first two records of this thread stay in flight over the slice copy
+      SoftPart acc = tid < nrec ? record(tid) : soft_empty();
+      const SoftPart t1 = tid + kStepThreads < nrec ? record(tid + kStepThreads) : soft_empty();
+      constexpr int ST = 4 * kStepThreads;
+      for (int j0 = 4 * tid; j0 < n; j0 += 4 * ST) {
+        float4 x[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (j0 + u * ST < n) x[u] = __ldcg(reinterpret_cast<const float4*>(grow + lo + j0 + u * ST));
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (j0 + u * ST < n) *reinterpret_cast<float4*>(srow + j0 + u * ST) = x[u];
+      }
+      soft_merge(acc, t1);
+      for (int r = tid + 2 * kStepThreads; r < nrec; r += kStepThreads) soft_merge(acc, record(r));
+      for (int j = skip + tid; j < nb; j += kStepThreads) {
+        const float v = __ldcg(grow + j);
+        soft_add(acc, v, zof(v), !forced(j));
+      }
+      // threads rescaled to their warp max, double sums over fixed xor trees,
+      // then the kSW warp results folded the same way by every warp
+      float M = warp_max(acc.m);
+      float mx = warp_max(acc.mx), cmx = warp_max(acc.cmx);
+      double z = 0.0, a = 0.0;
+      if (acc.m > -INFINITY) {
+        const double f = (double)expf(acc.m - M);
+        z = (double)acc.Z * f;
+        a = f * ((double)acc.A + (double)acc.Z * ((double)acc.m - (double)M));
+      }
+      z = warp_sum(z);
+      a = warp_sum(a);
+      double cs = warp_sum((double)acc.cs), cq = warp_sum((double)acc.cq);
+      if (lane == 0) {
+        redm[warp][0] = M;
+        redm[warp][1] = mx;
+        redm[warp][2] = cmx;
+        redd[warp][0] = z;
+        redd[warp][1] = a;
+        redd[warp][2] = cs;
+        redd[warp][3] = cq;
+      }
+      __syncthreads();
+      const bool wl = lane < kSW;
+      const float wm = wl ? redm[lane][0] : -INFINITY;
+      M = warp_max(wm);
+      mx = warp_max(wl ? redm[lane][1] : -INFINITY);
+      cmx = warp_max(wl ? redm[lane][2] : -INFINITY);
+      z = 0.0;
+      a = 0.0;
+      if (wl && wm > -INFINITY) {
+        const double f = (double)expf(wm - M);
+        z = redd[lane][0] * f;
+        a = f * (redd[lane][1] + redd[lane][0] * ((double)wm - (double)M));
+      }
+      z = warp_sum(z);
+      a = warp_sum(a);
+      cs = warp_sum(wl ? redd[lane][2] : 0.0);
+      cq = warp_sum(wl ? redd[lane][3] : 0.0);
+      if (tid == 0) {
+        s_row = RowStats{mx, cmx, M, cs, cq, z, a};
+        STEP_STAMP(19);
+      }
+    }
     __syncthreads();
     if (tid == 0) STEP_STAMP(2);
     const int nch = ceil_div(n, 4);
     const float4* srow4 = reinterpret_cast<const float4*>(srow);
-
-    // ---- pass 1: max, content max / sum / sum of squares and the softmax sums
-    //      (online per thread: m = max z, Z = sum e^(z - m), A = sum e^(z - m) (z - m)) ----
-    {
-      float m1 = -INFINITY, m2 = -INFINITY, cs = 0.f, cq = 0.f, mt = -INFINITY, zt = 0.f, at = 0.f;
-#pragma unroll 1
-      for (int c = tid; c < nch; c += kStepThreads) {
-        const float4 x = srow4[c];
-        const float v[4] = {x.x, x.y, x.z, x.w};
-        float zc[4], cm = -INFINITY;
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int j = lo + 4 * c + e;
-          const bool in = 4 * c + e < n;
-          zc[e] = in ? zof(v[e]) : -INFINITY;
-          if (in) {
-            m1 = fmaxf(m1, v[e]);
-            cm = fmaxf(cm, zc[e]);
-            if (!forced(j)) {
-              m2 = fmaxf(m2, v[e]);
-              cs += v[e];
-              cq = fmaf(v[e], v[e], cq);
-            }
-          }
-        }
-        if (adaptive && cm > mt) {  // rescale to the new running max
-          if (mt > -INFINITY) {
-            const float f = expf(mt - cm);
-            at = f * fmaf(zt, mt - cm, at);
-            zt *= f;
-          }
-          mt = cm;
-        }
-        if (adaptive) {
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            if (zc[e] > -INFINITY) {
-              const float dd = zc[e] - mt;
-              const float ex = expf(dd);
-              zt += ex;
-              if (ex > 0.f) at = fmaf(ex, dd, at);
-            }
-          }
-        }
-      }
-      // this rank's part: maxima and sums over the CTA, softmax sums rescaled
-      // to the CTA max (double across threads)
-      float mx, cmx;
-      double csum, csq;
-      block_stats(m1, m2, cs, cq, redf, redd, mx, cmx, csum, csq);
-      const float wm = warp_max(mt);
-      double zw = 0.0, aw = 0.0;
-      if (mt > -INFINITY) {
-        const double f = exp((double)mt - (double)wm);
-        zw = (double)zt * f;
-        aw = f * ((double)at + (double)zt * ((double)mt - (double)wm));
-      }
-      zw = warp_sum(zw);
-      aw = warp_sum(aw);
-      if (lane == 0) {
-        redf[warp][2] = wm;
-        redd[warp][2] = zw;
-        redd[warp][3] = aw;
-      }
-      __syncthreads();
-      if (tid == 0) {
-        float M = -INFINITY;
-        for (int w = 0; w < kSW; ++w) M = fmaxf(M, redf[w][2]);
-        double Z = 0.0, A = 0.0;
-        for (int w = 0; w < kSW; ++w) {
-          const float mw = redf[w][2];
-          if (mw > -INFINITY) {
-            const double f = exp((double)mw - (double)M);
-            Z += redd[w][2] * f;
-            A += f * (redd[w][3] + redd[w][2] * ((double)mw - (double)M));
-          }
-        }
-        s_part.mx = mx;
-        s_part.cmx = cmx;
-        s_part.m = M;
-        s_part.cs = csum;
-        s_part.cq = csq;
-        s_part.Z = Z;
-        s_part.A = A;
-      }
-    }
-    cl.sync();  // (1) every rank's part is written
-    if (tid == 0) STEP_STAMP(10);
-    // ---- the row's statistics, folded over the ranks in rank order (the same
-    //      arithmetic in every CTA of the cluster) ----
-    float mx = -INFINITY, cmx = -INFINITY, M = -INFINITY;
-    double csum = 0.0, csq = 0.0, Z = 0.0, A = 0.0;
-    for (int r = 0; r < CL; ++r) {
-      const RankPart* rp = cl.map_shared_rank(&s_part, r);
-      mx = fmaxf(mx, rp->mx);
-      cmx = fmaxf(cmx, rp->cmx);
-      M = fmaxf(M, rp->m);
-      csum += rp->cs;
-      csq += rp->cq;
-    }
-    for (int r = 0; r < CL; ++r) {
-      const RankPart* rp = cl.map_shared_rank(&s_part, r);
-      if (rp->m > -INFINITY) {
-        const double f = exp((double)rp->m - (double)M);
-        Z += rp->Z * f;
-        A += f * (rp->A + rp->Z * ((double)rp->m - (double)M));
-      }
-    }
+    const float cmx = s_row.cmx, M = s_row.m;
+    const double csum = s_row.cs, csq = s_row.cq, Z = s_row.Z, A = s_row.A;
     const double nc_d = (double)(nb - imin(nb, sink + local));
     const double mean_c = nc_d > 0 ? csum / nc_d : 0.0;
     const double var_c = nc_d > 0 ? csq / nc_d - mean_c * mean_c : 0.0;
@@ -785,39 +772,63 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepParams p) {
     const float scale = buckets_ok ? (float)((double)(kBk - 1) / range) : 0.f;
     const float zmax = M;  // = max over the row of s / T
 
-    // ---- pass 2: clamp correction, content histogram, each block's bucket ----
+    // ---- pass 2: clamp correction, content histogram, each block's bucket
+    //      (8 blocks per thread and iteration) ----
     {
-      float cp = 0.f;
+      float cpa = 0.f, cpb = 0.f;
       const float Zf = (float)Z;
       const float logZ = adaptive ? (float)log(Z) : 0.f;
-      const float ln_floor = logf(1e-9f);
-      const float pre_lim = 2e-9f * Zf;
-      const float d_hi = adaptive ? logf(pre_lim) : -INFINITY, d_lo = d_hi - 25.f;
+      const float cst = logf(1e-9f) + logZ;
+      const float d_hi = adaptive ? logf(2e-9f * Zf) : -INFINITY, d_lo = d_hi - 25.f;
+      // a block is clamped when p = e / Z (float, rounded) < 1e-9; decided
+      // from the fast product e' * (1 / Z), e' = __expf (relative error
+      // < 5e-6 on this window), unless it lies within 1e-5 of the bound, where
+      // the rounded quotient of expf is taken
+      const float invZ = 1.f / Zf;
+      const float clamp_lo = 1e-9f * (1.f - 1e-5f), clamp_hi = 1e-9f * (1.f + 1e-5f);
 #pragma unroll 1
-      for (int c = tid; c < nch; c += kStepThreads) {
+      for (int c = tid; c < nch; c += 2 * kStepThreads) {
+        const int c2 = c + kStepThreads;
         const float4 x = srow4[c];
-        const float v[4] = {x.x, x.y, x.z, x.w};
-        uint32_t bk4[4];
+        const float4 y = c2 < nch ? srow4[c2] : make_float4(0.f, 0.f, 0.f, 0.f);
+        const float v[8] = {x.x, x.y, x.z, x.w, y.x, y.y, y.z, y.w};
+        // branch-free per block; the rare near-bound clamp decisions after
+        uint32_t bk8[8];
+        bool band[8];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int li = 4 * c + e, j = lo + li;
+        for (int e = 0; e < 8; ++e) {
+          const int li = 4 * (e < 4 ? c : c2) + (e & 3), j = lo + li;
           const bool in = li < n;
-          int bk = kBk - 1;
-          if (in && buckets_ok && !forced(j)) {
-            bk = bucket_of(v[e], cmx, scale);
-            if (bk < kBk - 1) atomicAdd(&hist[bk], 1u);
-          }
-          bk4[e] = (uint32_t)bk;
-          if (adaptive && in) {
-            const float dd = __fsub_rn(zof(v[e]), zmax);
-            if (dd < d_hi && dd >= d_lo) {
-              const float ex = expf(dd);
-              if (ex > 0.f && ex < pre_lim && __fdiv_rn(ex, Zf) < 1e-9f) cp = fmaf(ex, ln_floor - dd + logZ, cp);
+          const bool content = in && buckets_ok && !forced(j);
+          const int bk = content ? bucket_of(v[e], cmx, scale) : kBk - 1;
+          atomicAdd(&hist[bk], bk < kBk - 1 ? 1u : 0u);
+          bk8[e] = (uint32_t)bk;
+          const float dd = __fsub_rn(zof(v[e]), zmax);
+          const bool win = adaptive && in && dd < d_hi && dd >= d_lo;
+          const float ex = __expf(dd);
+          const float pr = ex * invZ;
+          band[e] = win && pr >= clamp_lo && pr <= clamp_hi;
+          const float t = (win && ex > 0.f && pr < clamp_lo) ? ex * (cst - dd) : 0.f;
+          if (e & 1) cpb += t; else cpa += t;
+        }
+        bool any_band = false;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) any_band |= band[e];
+        if (any_band) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            if (band[e]) {
+              const float dd = __fsub_rn(zof(v[e]), zmax);
+              const float ea = expf(dd);
+              if (ea > 0.f && __fdiv_rn(ea, Zf) < 1e-9f) cpa += __expf(dd) * (cst - dd);
             }
           }
         }
-        reinterpret_cast<uint2*>(sbk)[c] = make_uint2(bk4[0] | (bk4[1] << 16), bk4[2] | (bk4[3] << 16));
+        reinterpret_cast<uint2*>(sbk)[c] = make_uint2(bk8[0] | (bk8[1] << 16), bk8[2] | (bk8[3] << 16));
+        if (c2 < nch)
+          reinterpret_cast<uint2*>(sbk)[c2] = make_uint2(bk8[4] | (bk8[5] << 16), bk8[6] | (bk8[7] << 16));
       }
+      const float cp = cpa + cpb;
       double c2 = cp, dummy = 0.0;
       block_sum2d(c2, dummy, redd);
       if (tid == 0) {
@@ -918,24 +929,40 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepParams p) {
     const bool exact = !all && Kc > 0 && (js < 0 || js >= kBk - 1 || (int)ghist[js] > kStepCandCap);
 
     if (!exact) {
-      // ---- this rank's slice: forced blocks, buckets above the threshold,
-      //      candidates of the threshold bucket ----
-      for (int w = warp; w < nwl; w += kSW) {
-        const int li = w * 32 + lane, j = lo + li;
-        const bool in = li < n;
-        const int bk = in ? (int)sbk[li] : kBk - 1;
-        const bool sel = in && (all || forced(j) || (Kc > 0 && bk < js));
-        const bool cand = in && !all && Kc > 0 && bk == js && !forced(j);
-        const uint32_t sb = __ballot_sync(0xffffffffu, sel);
-        if (cand) {
-          const int slot = atomicAdd(&s_ncand, 1);
-          ckey[slot] = order_key(srow[li]);
-          cidx[slot] = j;
+      // ---- this rank's slice, 8 blocks (one uint4 of buckets) per thread and
+      //      four threads per bitmap word: forced blocks, buckets above the
+      //      threshold, candidates of the threshold bucket ----
+      const int nq = 4 * nwl;
+      for (int g0 = 0; g0 < nq; g0 += kStepThreads) {
+        const int g = g0 + tid;
+        uint32_t sb = 0u;
+        if (g < nq) {
+          const uint4 u = reinterpret_cast<const uint4*>(sbk)[g];
+          const uint32_t pr[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const int li = 8 * g + e, j = lo + li;
+            const int bk = (int)((e & 1) ? pr[e >> 1] >> 16 : pr[e >> 1] & 0xFFFFu);
+            const bool in = li < n;
+            const bool sel = in && (all || forced(j) || (Kc > 0 && bk < js));
+            const bool cand = in && !all && Kc > 0 && bk == js && !forced(j);
+            sb |= (uint32_t)sel << (8 * (g & 3) + e);
+            if (cand) {
+              const int slot = atomicAdd(&s_ncand, 1);
+              ckey[slot] = order_key(srow[li]);
+              cidx[slot] = j;
+            }
+          }
         }
-        if (lane == 0) sbits[w] = sb;
+        sb |= __shfl_xor_sync(0xffffffffu, sb, 1);
+        sb |= __shfl_xor_sync(0xffffffffu, sb, 2);
+        if (g < nq && (g & 3) == 0) sbits[g >> 2] = sb;
       }
       __syncthreads();
-      if (tid == 0) s_part.ncand = s_ncand;
+      if (tid == 0) {
+        s_part.ncand = s_ncand;
+        STEP_STAMP(21);
+      }
     }
     cl.sync();  // (3) every rank's candidates
     if (tid == 0) STEP_STAMP(12);
@@ -1034,8 +1061,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepParams p) {
   pdl_launch_dependents();
   {
     const int NG = p.B * p.Hkv;
-    const int gi = (int)(((int64_t)(cta + 1) * NG - 1) / GRID);
-    const int c_first = (int)((int64_t)gi * GRID / NG), c_next = (int)((int64_t)(gi + 1) * GRID / NG);
+    const int gi = cta_of_row(cta, GRID, NG);  // CTAs split over the NG groups like rows over CTAs
+    const int c_first = muldiv(gi, GRID, NG), c_next = muldiv(gi + 1, GRID, NG);
     const int split = cta - c_first, SPLIT = c_next - c_first;
     const int b = gi / p.Hkv, kvh = gi - b * p.Hkv;
     const int S = s_S[b];
@@ -1049,9 +1076,6 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepParams p) {
     int* list = reinterpret_cast<int*>(sm + L.list);
     uint32_t* lmask = reinterpret_cast<uint32_t*>(sm + L.mask);
     float* wpart = reinterpret_cast<float*>(sm + L.wpart);
-    float* mf = reinterpret_cast<float*>(sm + L.merge);
-    float* ml = mf + 2 * kStepMaxGrid * G;
-    float* mL = ml + G;
     const T* kbase = static_cast<const T*>(p.k.data) + b * p.k.sb + kvh * p.k.sh;
     const T* vbase = static_cast<const T*>(p.v.data) + b * p.v.sb + kvh * p.v.sh;
     const T* qbase = static_cast<const T*>(p.q.data) + b * p.q.sb + (int64_t)kvh * G * p.q.sh;
@@ -1102,7 +1126,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepParams p) {
     }
     const int before = block_exclusive_scan(cnt, scan_scratch);
     const int U = scan_scratch[32];
-    const int lo = (int)((int64_t)U * split / SPLIT), hi = (int)((int64_t)U * (split + 1) / SPLIT);
+    const int lo = muldiv(U, split, SPLIT), hi = muldiv(U, split + 1, SPLIT);
     if (before < hi && before + cnt > lo) {
       int rk = before;
       for (int w = w0; w < w1 && rk < hi; ++w) {
@@ -1121,6 +1145,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepParams p) {
       }
     }
     __syncthreads();
+    if (tid == 0) STEP_STAMP(22);
     const int n = imin(hi - lo, p.slice_cap);
     for (int i = tid; i < n; i += kStepThreads) {
       const int id = list[i], w = id >> 5, bit = id & 31;
@@ -1201,6 +1226,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepParams p) {
       }
     }
     __syncthreads();
+    if (tid == 0) STEP_STAMP(23);
     float* gpart = p.part + (size_t)cta * G * (D + 2);
     for (int idx = tid; idx < G * D; idx += kStepThreads) {
       const int hh = idx / D, dd = idx - hh * D;
@@ -1228,8 +1254,11 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepParams p) {
       STEP_STAMP(6);
     }
 
-    // ---- the group's first CTA merges the SPLIT partials in split order ----
-    if (split == 0) {
+    // ---- the group's SPLIT partials, merged in split order by every CTA of
+    //      the group for its own share of the output columns: warp w takes
+    //      head w % G and half (G = 4) or all (G = 8) of the share, its lanes
+    //      the splits ----
+    {
       if (warp == 0) {
         PollBudget pb{p.wait_ns, 0, false};
         constexpr int NP = kStepMaxGrid / 32;
@@ -1243,52 +1272,42 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepParams p) {
         fence_acq_rel_gpu();  // acquire: the partials
       }
       __syncthreads();
-      const float* gp0 = p.part + (size_t)c_first * G * (D + 2);
       const size_t stride = (size_t)G * (D + 2);
-      for (int hh = warp; hh < G; hh += kSW) {
-        float Mx = -INFINITY;
+      const int d_lo = muldiv(D, split, SPLIT), d_hi = muldiv(D, split + 1, SPLIT);
+      constexpr int WPH = kSW / G;  // warps per head
+      static_assert(kSW % G == 0, "whole warps per head");
+      const int hh = warp % G, wp = warp / G;
+      const int cpw = ceil_div(d_hi - d_lo, WPH);
+      const int cb = d_lo + wp * cpw, ce = imin(d_hi, cb + cpw);
+      const float* ph = p.part + (size_t)c_first * stride + hh * (D + 2);
+      T* orow = static_cast<T*>(const_cast<void*>(p.out.data)) + b * p.out.sb + (int64_t)(kvh * G + hh) * p.out.sh;
+      for (int c0 = cb; c0 < ce; c0 += 4) {
+        float Ml = -INFINITY, Ll = 0.f, Ol[4] = {0.f, 0.f, 0.f, 0.f};
         for (int s0 = lane; s0 < SPLIT; s0 += 32) {
-          const float m = __ldcg(gp0 + s0 * stride + hh * (D + 2));
-          mf[s0 * G + hh] = m;
-          mf[(kStepMaxGrid + s0) * G + hh] = __ldcg(gp0 + s0 * stride + hh * (D + 2) + 1);
-          Mx = fmaxf(Mx, m);
-        }
-        Mx = warp_max(Mx);
-        float Ls = 0.f;
-        for (int s0 = lane; s0 < SPLIT; s0 += 32) {
-          const float l = mf[(kStepMaxGrid + s0) * G + hh];
-          const float m = mf[s0 * G + hh];
-          const float f = (Mx == -INFINITY || m == -INFINITY) ? 0.f : exp2f(m - Mx);
-          mf[s0 * G + hh] = f;
-          Ls += l * f;
-        }
-        Ls = warp_sum(Ls);
-        if (lane == 0) {
-          mL[hh] = Ls;
-          ml[hh] = Mx;
-        }
-      }
-      __syncthreads();
-      for (int idx = tid; idx < G * D; idx += kStepThreads) {
-        const int hh = idx / D, dd = idx - hh * D;
-        const float* src = gp0 + (size_t)hh * (D + 2) + 2 + dd;
-        float O = 0.f;
-        for (int s0 = 0; s0 < SPLIT; s0 += 16) {
-          float v[16];
+          const float* src = ph + (size_t)s0 * stride;
+          const float m = __ldcg(src), l = __ldcg(src + 1);
+          float o[4];
 #pragma unroll
-          for (int u = 0; u < 16; ++u) v[u] = s0 + u < SPLIT ? __ldcg(src + (size_t)(s0 + u) * stride) : 0.f;
+          for (int u = 0; u < 4; ++u) o[u] = c0 + u < ce ? __ldcg(src + 2 + c0 + u) : 0.f;
+          if (m > -INFINITY) {
+            const float Mn = fmaxf(Ml, m);
+            const float fa = Ml == -INFINITY ? 0.f : exp2f(Ml - Mn), fb = exp2f(m - Mn);
+            Ll = Ll * fa + l * fb;
 #pragma unroll
-          for (int u = 0; u < 16; ++u)
-            if (s0 + u < SPLIT) O += mf[(s0 + u) * G + hh] * v[u];
+            for (int u = 0; u < 4; ++u) Ol[u] = Ol[u] * fa + o[u] * fb;
+            Ml = Mn;
+          }
         }
-        const float Ls = mL[hh];
-        const float res = Ls > 0.f ? O / Ls : 0.f;
-        T* orow = static_cast<T*>(const_cast<void*>(p.out.data)) + b * p.out.sb + (int64_t)(kvh * G + hh) * p.out.sh;
-        orow[dd] = from_f32<T>(res);
-      }
-      if (p.lse && tid < G) {
-        const float M = ml[tid], Ls = mL[tid];
-        p.lse[row0 + tid] = (Ls > 0.f && M > -INFINITY) ? M * 0.6931471805599453f + logf(Ls) : -INFINITY;
+        const float M = warp_max(Ml);
+        const float f = Ml == -INFINITY ? 0.f : exp2f(Ml - M);
+        const float Ls = warp_sum(Ll * f);
+        float O[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) O[u] = warp_sum(Ol[u] * f);
+        const float ol = lane == 0 ? O[0] : lane == 1 ? O[1] : lane == 2 ? O[2] : O[3];
+        if (lane < 4 && c0 + lane < ce) orow[c0 + lane] = from_f32<T>(Ls > 0.f ? ol / Ls : 0.f);
+        if (p.lse && split == SPLIT - 1 && wp == 0 && c0 == cb && lane == 0)
+          p.lse[row0 + hh] = (Ls > 0.f && M > -INFINITY) ? M * 0.6931471805599453f + logf(Ls) : -INFINITY;
       }
     }
   }

@@ -11,13 +11,12 @@ local heads (odd KV heads).  The headline is the 131072-token context; 32768 and
 
 One step = append one token (in-place K/V write + trailing-centroid refresh),
 centroid estimator, entropy budget + top-k selection, ragged split-KV
-attention over the GQA union, all in one persistent kernel launch (the
-three-kernel chain runs where that kernel does not apply, or with
-ADAKV_FUSED=0).  As in a model forward pass, 8 independent layer states are
-stepped in turn inside one CUDA graph (working set > L2).  Each step reads
-nothing before the previous kernel on the stream has completed
-(griddepcontrol.wait first), so consecutive steps never overlap; a chain
-where each layer's query is the previous layer's output is timed beside it.
+attention over the GQA union, as three kernels chained with programmatic
+dependent launch (the library's default; the one-kernel persistent step that
+ADAKV_FUSED=1 selects is timed beside it under ``one_kernel_step``).  As in a
+model forward pass, 8 independent layer states are stepped in turn inside one
+CUDA graph (working set > L2); a chain where each layer's query is the
+previous layer's output, and one isolated step, are timed beside it.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
@@ -47,9 +46,11 @@ CFG = dict(Hq=32, Hkv=8, D=128, bs=16, avg=64, k_min=2, k_max=512, sink=1, local
 HEADLINE_S = 131072
 L2_FLUSH_BYTES = 256 << 20
 MIN_TIMED_S = 0.25  # the K timed steps are repeated until the timed region lasts this long
-# DRAM bytes (read + write) of one decode step at 128K from one ncu capture of
-# the step (dram__bytes_read.sum + dram__bytes_write.sum); None until captured
-NCU_STEP_TRAFFIC = {}
+# DRAM bytes (read + write) of one decode step at 128K from one ncu capture
+# (dram__bytes_read.sum + dram__bytes_write.sum of the estimate, plan and
+# attend launches of one step: 33,662,720 + 2,194,688 + 8,768,000; the step
+# writes no DRAM bytes the counters see, its outputs stay in L2)
+NCU_STEP_TRAFFIC = {131072: 44_625_408}
 
 
 def workload_name(S):
@@ -580,6 +581,11 @@ def main():
                          "sequence sharded over the ranks (neither is the headline)")
     ap.add_argument("--no-partitioned", action="store_true",
                     help="skip the cfg2 / cfg4 measurements reported beside the headline")
+    ap.add_argument("--path", choices=["chain", "one_kernel"], default="chain",
+                    help="decode-step path of the timed contexts (default: the library default, "
+                         "the three-kernel chain)")
+    ap.add_argument("--no-one-kernel", action="store_true",
+                    help="skip timing the one-kernel persistent step beside the default chain")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -618,6 +624,8 @@ def main():
     torch.cuda.set_device(device)
     from adakv_b200 import _lib
     _lib.lib()
+    if args.path == "one_kernel":
+        _lib.debug_knob(_lib.KNOB_STEP_PATH, 2)
 
     if args.workload in ("cfg2", "cfg4"):
         steps = min(args.steps, 200)
@@ -701,6 +709,20 @@ def main():
         results[S] = r
         torch.cuda.empty_cache()
 
+    one_kernel = None
+    if world == 1 and not args.no_one_kernel and args.path == "chain":
+        # the same headline workload through the one-kernel persistent step
+        _lib.debug_knob(_lib.KNOB_STEP_PATH, 2)
+        try:
+            ro = run_ours(headline, args.steps, args.warmup, args.seed, device, layers=args.layers)
+        finally:
+            _lib.debug_knob(_lib.KNOB_STEP_PATH, 0)
+        if ro["kernels_per_step"] == 1:
+            one_kernel = {"us": float(ro["us_step"]), "us_isolated_median": float(np.median(ro["us_iso"])),
+                          "us_dependent": ro["us_dep"], "e2e_us": float(np.mean(ro["us_e2e"])),
+                          "note": "ADAKV_FUSED=1 path, same workload and timing as value"}
+        torch.cuda.empty_cache()
+
     partitioned = None
     if not args.no_partitioned:
         partitioned = run_partitioned(args.steps, args.warmup, world, rank, device, args.seed)
@@ -755,6 +777,7 @@ def main():
             "gpu_launches": r["kernels_per_step"] * r["steps"] * r["reps"],
             "clocks": r["clocks"],
             "contexts": ctx,
+            "one_kernel_step": one_kernel,
             "partitioned": partitioned,
         }
         print(json.dumps(line), flush=True)

@@ -229,7 +229,11 @@ int adakv_attend_noalloc(const adakv_geometry* geo, const adakv_view* q, const a
  * n_new = 0 and NULL views to skip; seq_lens[b] is the length AFTER the append)
  * into k / v in place with the touched centroids refreshed, then adakv_plan,
  * then attention of every query head over its selection, written to out.
- * The workspace is sized by adakv_plan_workspace_bytes. */
+ * The workspace is sized by adakv_plan_workspace_bytes.  By default the step
+ * is three PDL-chained kernels (estimator, plan, attend); with ADAKV_FUSED=1
+ * in the environment (read once) it is one persistent kernel where that
+ * kernel applies (adaptive or fixed policy, B * Hq <= 128, head_dim 128,
+ * g = 4 or 8, block 16); both give the same selection. */
 int adakv_decode_step(const adakv_geometry* geo, const adakv_select_params* sp,
                       const adakv_view* q, const adakv_view* k, const adakv_view* v,
                       const adakv_view* k_new, const adakv_view* v_new, int32_t n_new,
@@ -270,12 +274,17 @@ int adakv_last_path(const void* workspace);
  *   ADAKV_KNOB_FLAGS      bit 0: the entropy of query head 0 of sequence 0 is
  *                         never published, so the per-sequence exchange of the
  *                         budget waits out its bound (failure-detection tests)
- *   ADAKV_KNOB_STEP_PATH  adakv_decode_step: 0 picks the one-kernel step when
- *                         it applies, 1 forces the three-kernel chain, 2
- *                         prefers the one-kernel step even when ADAKV_FUSED=0 */
+ *   ADAKV_KNOB_STEP_PATH  adakv_decode_step: 0 runs the three-kernel chain
+ *                         (or the one-kernel step where it applies when the
+ *                         environment has ADAKV_FUSED=1), 1 forces the chain,
+ *                         2 picks the one-kernel step wherever it applies
+ *   ADAKV_KNOB_STEP_CLUSTER  largest thread-block cluster (1, 2, 4 or 8 CTAs)
+ *                         one query head's selection may span in the one-kernel
+ *                         step (0: 8) */
 #define ADAKV_KNOB_WAIT_NS 1
 #define ADAKV_KNOB_FLAGS 2
 #define ADAKV_KNOB_STEP_PATH 3
+#define ADAKV_KNOB_STEP_CLUSTER 4
 int adakv_debug_knob(int32_t knob, int64_t value);
 
 /* Test-only: with ADAKV_KNOB_FLAGS bit 1 set, the one-kernel step records per

@@ -174,7 +174,9 @@ def test_debug_knobs_validate_and_reset(lib):
     assert lib.adakv_debug_knob(99, 1) == _lib.ERR_INVALID
     assert lib.adakv_debug_knob(_lib.KNOB_WAIT_NS, -5) == _lib.ERR_INVALID
     assert lib.adakv_debug_knob(_lib.KNOB_STEP_PATH, 3) == _lib.ERR_INVALID
-    for knob, v in ((_lib.KNOB_WAIT_NS, 1000), (_lib.KNOB_FLAGS, 1), (_lib.KNOB_STEP_PATH, 1)):
+    assert lib.adakv_debug_knob(_lib.KNOB_STEP_CLUSTER, 3) == _lib.ERR_INVALID
+    for knob, v in ((_lib.KNOB_WAIT_NS, 1000), (_lib.KNOB_FLAGS, 1), (_lib.KNOB_STEP_PATH, 1),
+                    (_lib.KNOB_STEP_CLUSTER, 4)):
         assert lib.adakv_debug_knob(knob, v) == _lib.OK
         assert lib.adakv_debug_knob(knob, 0) == _lib.OK
 

@@ -1,5 +1,7 @@
-"""The one-kernel decode step (``adakv_decode_step`` on the persistent kernel)
-against the NumPy oracle, on identical seeded inputs (needs a B200).
+"""The one-kernel decode step (``adakv_decode_step`` on the persistent kernel,
+``ADAKV_KNOB_STEP_PATH`` = 2) against the NumPy oracle, on identical seeded
+inputs (needs a B200); the headline-size cases also run the default
+three-kernel chain.
 
 Bars: block scores within 2e-6 relative of the float64 oracle; selected block
 sets identical per head except documented near-ties (score gap < 1e-6
@@ -29,8 +31,10 @@ BUDGET_TOL = 1e-5
 def _need_cuda_and_reset_knobs():
     if not torch.cuda.is_available():
         pytest.skip("CUDA device required")
+    # the one-kernel step unless a test picks the chain (the library default)
+    _lib.debug_knob(_lib.KNOB_STEP_PATH, 2)
     yield
-    for knob in (_lib.KNOB_WAIT_NS, _lib.KNOB_FLAGS, _lib.KNOB_STEP_PATH):
+    for knob in (_lib.KNOB_WAIT_NS, _lib.KNOB_FLAGS, _lib.KNOB_STEP_PATH, _lib.KNOB_STEP_CLUSTER):
         _lib.debug_knob(knob, 0)
 
 
@@ -108,17 +112,38 @@ STEP_CASES = [
 ]
 
 
+@pytest.mark.parametrize("path", [1, 2], ids=["chain", "one_kernel"])
 @pytest.mark.parametrize("seed,Hq,Hkv,S,dtype,avg,kmax,extra", STEP_CASES)
-def test_step_matches_oracle(seed, Hq, Hkv, S, dtype, avg, kmax, extra):
+def test_step_matches_oracle(seed, Hq, Hkv, S, dtype, avg, kmax, extra, path):
     bs = 16
     kw = _kw(avg, kmax, **extra)
+    _lib.debug_knob(_lib.KNOB_STEP_PATH, path)
     case = make_decode_case(seed, 1, Hq, Hkv, 128, S, bs, dtype)
     dec, q = _decoder(case, Hq, Hkv, kw)
     out = dec.step(q).float().cpu().numpy()[0]
+    assert dec.last_path() == path
     sc = dec.scores().cpu().numpy()[0]
     res = _oracle(case.q[0], case.K[0], case.V[0], bs, kw)
     _check_seq(res, dec.selected_sets(), sc, out, case.q[0], case.K[0], case.V[0], bs, kw, f"S={S}")
     assert dec.status() == 0
+
+
+@pytest.mark.parametrize("cluster", [1, 2, 4])
+@pytest.mark.parametrize("seed,S", [(26, 131072), (27, 40000), (28, 250007)])
+def test_step_cluster_sizes_match_oracle(seed, S, cluster):
+    """The selection phase on 1, 2 or 4 CTAs per query head (the cluster merges
+    histograms and candidates through distributed shared memory)."""
+    bs, Hq, Hkv = 16, 32, 8
+    kw = _kw(64, 512)
+    _lib.debug_knob(_lib.KNOB_STEP_CLUSTER, cluster)
+    case = make_decode_case(seed, 1, Hq, Hkv, 128, S, bs, "bf16")
+    dec, q = _decoder(case, Hq, Hkv, kw)
+    out = dec.step(q).float().cpu().numpy()[0]
+    assert dec.last_path() == 2
+    sc = dec.scores().cpu().numpy()[0]
+    res = _oracle(case.q[0], case.K[0], case.V[0], bs, kw)
+    _check_seq(res, dec.selected_sets(), sc, out, case.q[0], case.K[0], case.V[0], bs, kw,
+               f"S={S} cluster<={cluster}")
 
 
 def test_step_batched_ragged():
