@@ -288,12 +288,16 @@ int adakv_last_path(const void* workspace);
 int adakv_debug_knob(int32_t knob, int64_t value);
 
 /* Test-only: with ADAKV_KNOB_FLAGS bit 1 set, the one-kernel step records per
- * CTA 24 words: globaltimer stamps (ns) of its phase boundaries, in order
- * start, estimator end, score row loaded, budgets known, bitmap published,
- * group bitmaps read, partial published, end, first and last estimator
- * stage arrived, row statistics, entropy published, bucket sort done,
- * gather done, selection done, one word of selection-path flags, softmax
- * sums, clamp correction, histogram, bucket prefix, bucket sort (3 spare).
+ * CTA 24 words, globaltimer stamps (ns; 0 where the CTA has no such phase).
+ * Word: 0 start, 1 estimator done, 2 score slice and row statistics ready,
+ * 3 budget weights known, 4 bitmap and table published, 5 group bitmaps
+ * read, 6 attention partial published, 7 end, 8 / 9 first / last estimator
+ * stage arrived, 10 every estimator CTA arrived, 11 entropy published,
+ * 12 cluster candidates visible, 13 gather and MMA done, 14 candidates
+ * ranked, 15 unused, 16 histogram and clamp pass done, 17 cluster
+ * histograms visible, 18 cluster counts visible, 19 estimator records
+ * folded, 20 threshold bucket found, 21 bitmap words marked, 22 union list
+ * built, 23 warp partials combined.  adakv_b200.step_timeline prints them.
  * Synchronises `stream`, copies max_ctas * 24 words of the last step on
  * `workspace` to the host array `out`.  No counterpart in the
  * reference. */
