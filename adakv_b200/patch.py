@@ -23,6 +23,11 @@ Differences from the reference, all on the performance side:
   and each decode step refreshes only the blocks touched by the tokens
   appended since (``adakv_centroid_refresh``).  The centroids are bit-identical
   to a full rebuild.
+* With ``adakv_b200.hf_cache.AdaKVStaticCache`` as the model's cache, the K / V
+  live in preallocated per-layer buffers (no per-step concatenation) and the
+  cache's own update writes each token and refreshes its block's centroid in
+  one launch (the prompt's table is built while the prefill writes the cache);
+  this function then uses that table as it stands.
 * Batched decode (``B > 1``) without an attention mask (no padding: every
   sequence has the key length) runs the same batched kernels; with a mask it
   goes dense, as the reference does for every ``B != 1`` call (``patch.py:96``).
@@ -37,6 +42,7 @@ import math
 import torch
 
 from . import _lib
+from . import hf_cache as _hf_cache
 from .attention import record_selection, tracing_enabled
 
 try:
@@ -133,8 +139,11 @@ def adakv_attention_forward(module, query, key, value, attention_mask, scaling, 
     if sel != "adakv":
         raise NotImplementedError(f"selection={sel!r} (eviction baselines) is not built here")
     sparse = cfg["enabled"] and q_len == 1 and (B == 1 or attention_mask is None)
+    ext = None  # a preallocated cache layer whose centroid table is already current
+    if cfg["enabled"] and cfg["estimator"] == "centroid" and query.is_cuda:
+        ext = _hf_cache.layer_of(key, int(cfg["block_size"]))
     if not sparse:
-        if cfg["enabled"] and q_len > 1 and query.is_cuda and D in (64, 128):
+        if cfg["enabled"] and q_len > 1 and query.is_cuda and D in (64, 128) and ext is None:
             # prompt keys are final for these positions: build the table now
             with torch.cuda.device(query.device):
                 _sync_centroids(module, key, Hq, cfg["block_size"], rebuild=True,
@@ -152,11 +161,15 @@ def adakv_attention_forward(module, query, key, value, attention_mask, scaling, 
     _, Hkv, S, _ = key.shape
     sm_scale = float(scaling) if scaling is not None else 1.0 / math.sqrt(D)
     with torch.cuda.device(query.device):
-        st = _sync_centroids(module, key, Hq, bs, rebuild=False, minmax=minmax)
+        if ext is not None:
+            st, cbuf = None, ext.centroid
+        else:
+            st = _sync_centroids(module, key, Hq, bs, rebuild=False, minmax=minmax)
+            cbuf = st.cbuf
         sp = _lib.select_params(cfg["avg_budget"], cfg["k_min"], cfg["k_max"],
                                 cfg["n_sink_blocks"], cfg["n_local_blocks"], cfg["c_min"],
                                 cfg["temperature"], cfg["budget_policy"], cfg["nucleus_p"])
-        geo = _geometry(B, Hq, Hkv, D, bs, S, st.cbuf.shape[2], query.dtype)
+        geo = _geometry(B, Hq, Hkv, D, bs, S, cbuf.shape[2], query.dtype)
         L = _lib.lib()
         width = L.adakv_plan_table_width(geo, sp)
         if width < 1:
@@ -172,7 +185,7 @@ def adakv_attention_forward(module, query, key, value, attention_mask, scaling, 
         o3 = out[:, 0]  # [B, Hq, D] view of the [B, 1, Hq, D] output
         if minmax:
             # Quest scores, then the same budget + top-k and block-sparse attention
-            scores = torch.empty((B * Hq, st.cbuf.shape[2]), dtype=torch.float32,
+            scores = torch.empty((B * Hq, cbuf.shape[2]), dtype=torch.float32,
                                  device=query.device)
             stream = _lib.stream_ptr(query.device)
             _lib.check(L.adakv_estimate_minmax(geo, _lib.view4(q3), st.mm[0].data_ptr(),
@@ -190,7 +203,7 @@ def adakv_attention_forward(module, query, key, value, attention_mask, scaling, 
             return out, None
         _lib.check(L.adakv_decode_step(
             geo, sp, _lib.view4(q3), _lib.view4(key), _lib.view4(value), None, None, 0,
-            st.cbuf.data_ptr(), None, sm_scale, block_table.data_ptr(), width,
+            cbuf.data_ptr(), None, sm_scale, block_table.data_ptr(), width,
             sel_lens.data_ptr(), _lib.view4(o3), ws.data_ptr(), ws.numel(),
             _lib.stream_ptr(query.device)))
     if tracing_enabled() and B == 1:

@@ -524,6 +524,104 @@ def run_cfg2(steps, warmup, world, rank, device, seed=0):
     return a.elapsed_time(b) * 1000.0 / steps, nbytes
 
 
+CFG3 = dict(B=8, S=131072, new=256, layers=32, hidden=4096, heads=32, kv=8, ffn=14336,
+            vocab=128256, bs=16, avg=64, chunk=2048)
+
+
+def run_cfg3(world, rank, device, seed, prefill="synthetic", warmup=3, overrides=None):
+    """cfg3: a random-init Llama-3.1-8B (bf16) patched with
+    ``patch_model(block_size=16, avg_budget=64)`` over an
+    ``AdaKVStaticCache``; a 128K-token context per sequence, then greedy
+    decode steps at batch 8 on this rank.  ``prefill="model"`` runs the
+    model's dense prefill over seeded random token ids in 2048-token chunks;
+    ``"synthetic"`` writes seeded Gaussian K / V straight into the cache through
+    the same fused write + centroid build (the 128K x 8 dense prefill costs
+    minutes of GPU and is not the measured quantity).  Returns a dict of
+    measurements of this rank."""
+    import torch
+    from transformers import LlamaConfig, LlamaForCausalLM
+    from adakv_b200 import patch
+    from adakv_b200.hf_cache import AdaKVStaticCache
+    c = dict(CFG3)
+    c.update(overrides or {})
+    B, S, new = c["B"], c["S"], c["new"]
+    cfg = LlamaConfig(hidden_size=c["hidden"], intermediate_size=c["ffn"],
+                      num_hidden_layers=c["layers"], num_attention_heads=c["heads"],
+                      num_key_value_heads=c["kv"], head_dim=c["hidden"] // c["heads"],
+                      vocab_size=c["vocab"], max_position_embeddings=S + new + warmup + 64,
+                      rope_theta=500000.0, rms_norm_eps=1e-5, tie_word_embeddings=False,
+                      bos_token_id=1, eos_token_id=2, pad_token_id=0)
+    torch.manual_seed(seed + rank)
+    with torch.device(device):
+        model = LlamaForCausalLM._from_config(cfg, torch_dtype=torch.bfloat16).eval()
+    patch.patch_model(model, block_size=c["bs"], avg_budget=c["avg"])
+    D, Hkv = c["hidden"] // c["heads"], c["kv"]
+    cache = AdaKVStaticCache(cfg, max_cache_len=S + new + warmup, block_size=c["bs"])
+    g = torch.Generator(device=device).manual_seed(seed + rank)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    fill_ms = None
+    with torch.no_grad():
+        if prefill == "model":
+            ids = torch.randint(3, c["vocab"], (B, S), device=device, generator=g)
+            for s0 in range(0, S, c["chunk"]):
+                out = model(input_ids=ids[:, s0:s0 + c["chunk"]], past_key_values=cache,
+                            use_cache=True, logits_to_keep=1)
+            tok = out.logits[:, -1].argmax(-1, keepdim=True)
+        else:
+            for li, layer in enumerate(cache.layers):
+                if li == 0:
+                    torch.cuda.synchronize(device)
+                    ev[0].record()
+                for s0 in range(0, S, c["chunk"]):
+                    n = min(c["chunk"], S - s0)
+                    k = torch.randn((B, Hkv, n, D), device=device, dtype=torch.bfloat16, generator=g)
+                    v = torch.randn((B, Hkv, n, D), device=device, dtype=torch.bfloat16, generator=g)
+                    layer.update(k, v)
+                if li == 0:
+                    ev[1].record()
+                    torch.cuda.synchronize(device)
+                    fill_ms = ev[0].elapsed_time(ev[1])  # includes generating the random chunks
+            tok = torch.randint(3, c["vocab"], (B, 1), device=device, generator=g)
+
+        def decode(n_steps, tok):
+            for _ in range(n_steps):
+                out = model(input_ids=tok, past_key_values=cache, use_cache=True, logits_to_keep=1)
+                tok = out.logits[:, -1].argmax(-1, keepdim=True)
+            return tok
+
+        tok = decode(warmup, tok)
+        torch.cuda.synchronize(device)
+        ev[0].record()
+        tok = decode(new, tok)
+        ev[1].record()
+        torch.cuda.synchronize(device)
+        ms = ev[0].elapsed_time(ev[1])
+        # the same steps with attention dense over the same cache (the
+        # reference's route for every batched call, adakv/patch.py:96-100)
+        for layer in cache.layers:
+            layer.crop(S + warmup)
+        patch.disable_adakv()
+        n_dense = min(new, 16)
+        dense_ms = None
+        try:
+            torch.cuda.synchronize(device)
+            ev[0].record()
+            decode(n_dense, tok)
+            ev[1].record()
+            torch.cuda.synchronize(device)
+            dense_ms = ev[0].elapsed_time(ev[1])
+        except torch.OutOfMemoryError:  # dense attention's temporaries may not fit beside the cache
+            torch.cuda.empty_cache()
+        patch.enable_adakv()
+    del model, cache
+    torch.cuda.empty_cache()
+    return {"tokens_per_s": B * new / (ms / 1e3), "ms_per_step": ms / new, "steps": new,
+            "batch": B, "context": S,
+            "dense_tokens_per_s": B * n_dense / (dense_ms / 1e3) if dense_ms else None,
+            "dense_ms_per_step": dense_ms / n_dense if dense_ms else None, "prefill": prefill,
+            "fused_fill_ms_one_layer": fill_ms}
+
+
 def run_partitioned(steps, warmup, world, rank, device, seed):
     """cfg2 (ragged batch of 64 split by sequence, no collective) and cfg4 (one
     1M-token sequence sharded over the ranks) at this world size: whole-job
@@ -576,9 +674,14 @@ def main():
                     help="independent layer states stepped per graph replay")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["cfg1", "cfg2", "cfg4"], default="cfg1",
-                    help="cfg2: ragged batch of 64 split by sequence; cfg4: one 1M-token "
-                         "sequence sharded over the ranks (neither is the headline)")
+    ap.add_argument("--workload", choices=["cfg1", "cfg2", "cfg3", "cfg4"], default="cfg1",
+                    help="cfg2: ragged batch of 64 split by sequence; cfg3: random-init "
+                         "Llama-3.1-8B decode at batch 8 per GPU over a 128K context "
+                         "(data parallel, tokens/s); cfg4: one 1M-token sequence sharded "
+                         "over the ranks (none is the headline)")
+    ap.add_argument("--cfg3-prefill", choices=["synthetic", "model"], default="synthetic",
+                    help="cfg3 context: seeded K/V written through the cache (default) or "
+                         "the model's dense prefill over random token ids")
     ap.add_argument("--no-partitioned", action="store_true",
                     help="skip the cfg2 / cfg4 measurements reported beside the headline")
     ap.add_argument("--path", choices=["chain", "one_kernel"], default="chain",
@@ -626,6 +729,39 @@ def main():
     _lib.lib()
     if args.path == "one_kernel":
         _lib.debug_knob(_lib.KNOB_STEP_PATH, 2)
+
+    if args.workload == "cfg3":
+        r = run_cfg3(world, rank, device, args.seed, prefill=args.cfg3_prefill,
+                     warmup=max(args.warmup, 1))
+        tps, ms = r["tokens_per_s"], r["ms_per_step"]
+        if world > 1:
+            t = torch.tensor([tps, ms], device=device, dtype=torch.float64)
+            dist.all_reduce(t[:1], op=dist.ReduceOp.SUM)   # whole-job tokens/s
+            dist.all_reduce(t[1:], op=dist.ReduceOp.MAX)
+            tps, ms = float(t[0]), float(t[1])
+        if rank == 0:
+            print(json.dumps({
+                "metric": "end-to-end decode tokens/s (cfg3)", "value": tps, "unit": "tokens/s",
+                "n_gpus": world, "steps": r["steps"], "warmup": max(args.warmup, 1),
+                "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "bf16",
+                "data": f"synthetic (random-init weights; context {r['prefill']})",
+                "config": {"workload": "cfg3 random-init Llama-3.1-8B (32 layers, hidden 4096, "
+                                       "32/8 heads, FFN 14336, vocab 128256), patch_model("
+                                       "block_size=16, avg_budget=64), AdaKVStaticCache, "
+                                       f"batch {r['batch']} per GPU, context {r['context']}, "
+                                       f"{r['steps']} greedy decode steps",
+                           "parallelism": f"data parallel x{world}, no collective",
+                           "timing": "CUDA events around the decode steps (eager HF forward)"},
+                "dense_same_cache": {"tokens_per_s": (r["dense_tokens_per_s"] or 0.0) * world or None,
+                                     "ms_per_step": r["dense_ms_per_step"],
+                                     "note": "attention dense (SDPA) over the same cache, rank 0"},
+                "fused_fill_ms_one_layer": r["fused_fill_ms_one_layer"],
+            }), flush=True)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
 
     if args.workload in ("cfg2", "cfg4"):
         steps = min(args.steps, 200)

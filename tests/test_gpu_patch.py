@@ -211,3 +211,42 @@ def test_minmax_estimator_through_patch():
                             k_max=64, sm_scale=D ** -0.5, estimator="minmax")
         err = np.abs(out[0, 0].cpu().numpy() - ref["out"]).max()
         assert err < TOL["fp32"], f"step {t}: {err:.3e}"
+
+
+def test_static_cache_generate_matches_dynamic_cache():
+    """adakv_b200.hf_cache.AdaKVStaticCache: preallocated per-layer K/V whose
+    update writes the tokens and rebuilds the touched blocks' centroids in one
+    launch (the prompt's table while the prefill writes the cache).  Greedy
+    generation through it equals generation through HF's DynamicCache, and
+    every layer's table equals a fresh build from the cache's keys."""
+    _need_cuda()
+    from adakv_b200 import _lib, patch
+    from adakv_b200.hf_cache import AdaKVStaticCache
+    model = _tiny_llama(torch.float32)
+    ids = torch.randint(3, 512, (2, 900), device="cuda", generator=torch.Generator(
+        device="cuda").manual_seed(3))
+    n_new = 10
+    patch.patch_model(model, block_size=16, avg_budget=8, k_max=64)
+    with torch.no_grad():
+        dyn = model.generate(ids, max_new_tokens=n_new, do_sample=False, output_logits=True,
+                             return_dict_in_generate=True)
+        cache = AdaKVStaticCache(model.config, max_cache_len=ids.shape[1] + n_new)
+        sta = model.generate(ids, past_key_values=cache, max_new_tokens=n_new, do_sample=False,
+                             output_logits=True, return_dict_in_generate=True)
+    assert torch.equal(dyn.sequences, sta.sequences)
+    for a, b in zip(dyn.logits, sta.logits):
+        assert (a - b).abs().max().item() < 1e-3
+    S = ids.shape[1] + n_new - 1  # the last generated token is never fed back
+    L = _lib.lib()
+    for layer in cache.layers:
+        assert layer.fused and layer.get_seq_length() == S
+        B, Hkv, _, D = layer.keys.shape
+        ref = torch.empty_like(layer.centroid)
+        geo = _lib.geometry(B, Hkv, Hkv, D, 16, S, ref.shape[2], _lib.TORCH_DTYPES[torch.float32])
+        _lib.check(L.adakv_centroid_build(geo, _lib.view4(layer.keys), None, ref.data_ptr(),
+                                          _lib.stream_ptr(ref.device)))
+        nb = -(-S // 16)
+        assert torch.equal(layer.centroid[:, :, :nb], ref[:, :, :nb])
+    with pytest.raises(ValueError, match="holds"):
+        cache.layers[0].update(torch.zeros(2, 2, 2, 64, device="cuda"),
+                               torch.zeros(2, 2, 2, 64, device="cuda"))
