@@ -92,6 +92,10 @@ _SIGNATURES = {
     "adakv_last_path": (ctypes.c_int, [_vp]),
     "adakv_debug_timeline": (ctypes.c_int, [_P(Geometry), _vp, ctypes.c_size_t, _vp, ctypes.c_int32,
                                             _vp]),
+    "adakv_importance_workspace_bytes": (ctypes.c_size_t, [_P(Geometry), ctypes.c_int32]),
+    "adakv_key_importance": (ctypes.c_int, [_P(Geometry), _P(View), _P(View), ctypes.c_int32,
+                                            ctypes.c_float, _vp, ctypes.c_int32, _vp, ctypes.c_size_t,
+                                            _vp]),
 }
 
 KNOB_WAIT_NS, KNOB_FLAGS, KNOB_STEP_PATH, KNOB_STEP_CLUSTER = 1, 2, 3, 4

@@ -1159,6 +1159,43 @@ int adakv_combine(int32_t n_parts, int32_t batch, int32_t n_q_heads, int32_t hea
   return ADAKV_OK;
 }
 
+size_t adakv_importance_workspace_bytes(const adakv_geometry* geo, int32_t n_query) {
+  if (!geo || n_query < 1 || geo->batch < 1 || geo->n_q_heads < 1) return 0;
+  return 2 * sizeof(float) * (size_t)geo->batch * geo->n_q_heads * (size_t)n_query + 256;
+}
+
+int adakv_key_importance(const adakv_geometry* geo, const adakv_view* q, const adakv_view* k,
+                         int32_t n_query, float sm_scale, float* importance, int32_t imp_stride,
+                         void* workspace, size_t workspace_bytes, void* stream) {
+  int rc;
+  if ((rc = check_geometry(geo))) return rc;
+  if ((rc = check_view(q, "q", geo->dtype, true))) return rc;
+  if ((rc = check_view(k, "k", geo->dtype, true))) return rc;
+  if (n_query < 1 || n_query > geo->max_seq_len)
+    return fail(ADAKV_ERR_INVALID, "n_query must be in [1, max_seq_len] (got %d)", n_query);
+  if (!importance || imp_stride < geo->max_seq_len)
+    return fail(ADAKV_ERR_INVALID, "importance is NULL or imp_stride %d < max_seq_len %d", imp_stride,
+                geo->max_seq_len);
+  if (!(sm_scale > 0.f)) return fail(ADAKV_ERR_INVALID, "sm_scale must be > 0");
+  if ((rc = check_workspace(workspace, workspace_bytes, adakv_importance_workspace_bytes(geo, n_query))))
+    return rc;
+  ImportanceParams p{};
+  p.q = to_view(q);
+  p.k = to_view(k);
+  p.B = geo->batch;
+  p.Hq = geo->n_q_heads;
+  p.Hkv = geo->n_kv_heads;
+  p.S = geo->max_seq_len;
+  p.n_query = n_query;
+  p.scale = sm_scale;
+  p.row_m = static_cast<float*>(workspace);
+  p.row_l = p.row_m + (size_t)geo->batch * geo->n_q_heads * n_query;
+  p.imp = importance;
+  p.imp_stride = imp_stride;
+  CUDA_TRY(launch_importance(p, geo->dtype, geo->head_dim, static_cast<cudaStream_t>(stream)));
+  return ADAKV_OK;
+}
+
 }  // extern "C"
 
 // ---------------------------------------------------------------------------

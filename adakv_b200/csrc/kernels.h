@@ -143,6 +143,17 @@ struct CombineParams {      // log-sum-exp merge of per-shard attention outputs
   int Hq;
 };
 
+struct ImportanceParams {   // H2O / SnapKV per-key attention importance (importance.cu)
+  View q, k;                // [B, Hq, S, D] prompt queries, [B, Hkv, S, D] keys
+  int B, Hq, Hkv, S;
+  int n_query;              // the last n_query query rows attend (S: H2O, the window: SnapKV)
+  float scale;
+  float* row_m;             // [B, Hq, n_query] row max of the scaled logits (workspace)
+  float* row_l;             // [B, Hq, n_query] row sum of exp(logit - max) (workspace)
+  float* imp;               // [B * Hq, imp_stride] float32 out
+  int imp_stride;
+};
+
 // ---------------------------------------------------------------------------
 // (a)-(d) one decode step in one persistent kernel (step.cu)
 // ---------------------------------------------------------------------------
@@ -284,6 +295,7 @@ cudaError_t launch_minmax_build(const MinmaxParams& p, int dtype, int D, int blo
 cudaError_t launch_minmax_score(const MinmaxParams& p, int dtype, int D, int nb_max,
                                 cudaStream_t stream);
 cudaError_t launch_combine(const CombineParams& p, int dtype, cudaStream_t stream, const LaunchOpts& o);
+cudaError_t launch_importance(const ImportanceParams& p, int dtype, int D, cudaStream_t stream);
 cudaError_t launch_step(const StepParams& p, int dtype, int D, int g, int grid, size_t smem,
                         cudaStream_t stream, const LaunchOpts& o);
 cudaError_t launch_step_scores(bool fused, const float* fscores,

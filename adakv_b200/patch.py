@@ -33,7 +33,12 @@ Differences from the reference, all on the performance side:
   goes dense, as the reference does for every ``B != 1`` call (``patch.py:96``).
 
 The H2O / SnapKV eviction baselines (``selection="h2o" | "snapkv"``,
-``patch.py:57-87``) are not part of this path and raise ``NotImplementedError``.
+``patch.py:57-87``): the single-sequence prefill call freezes each layer's
+retained block set from the prompt's (Q, K) (``adakv_b200.baselines_rt``:
+the importance kernel, SnapKV's max-pool, the library's fixed-budget top-k)
+and still returns dense attention; each decode step then attends to the frozen
+set plus the sink blocks and the current local window through the same
+block-sparse attention kernel.
 """
 from __future__ import annotations
 
@@ -42,6 +47,7 @@ import math
 import torch
 
 from . import _lib
+from . import baselines_rt as _brt
 from . import hf_cache as _hf_cache
 from .attention import record_selection, tracing_enabled
 
@@ -78,6 +84,54 @@ class _LayerState:
 
 # per-layer state keyed by id(module); cleared by enable_adakv / disable_adakv
 _STATE: dict[int, _LayerState] = {}
+# per-layer frozen retained-block mask [Hq, nb_prefill] of the eviction
+# baselines, keyed by id(module) (the reference's _FROZEN, patch.py:55-58)
+_FROZEN: dict[int, torch.Tensor] = {}
+
+
+def _capture_frozen(module, query, key, cfg, sel):
+    """Freeze this layer's retained block set from the prompt (reference
+    ``patch.py:60-76``); the prefill output stays dense."""
+    L, D = key.shape[2], key.shape[3]
+    n_query = L if sel == "h2o" else int(min(cfg["obs_window"], L))
+    imp = _brt.key_importance(query, key, n_query, sm_scale=1.0 / math.sqrt(D))
+    if sel == "snapkv":
+        imp = _brt._pool(imp, int(cfg["pool_kernel"]))
+    _FROZEN[id(module)] = _brt.retain_blocks_torch(
+        imp, int(cfg["block_size"]), L, int(cfg["avg_budget"]), int(cfg["n_sink_blocks"]),
+        int(cfg["n_local_blocks"]), int(cfg["c_min"]))
+
+
+def _frozen_decode(module, query, key, value, scaling, cfg):
+    """One decode step over the layer's frozen set (reference ``patch.py:79-87``,
+    then its block-sparse kernel)."""
+    B, Hq, _, D = query.shape
+    bs = int(cfg["block_size"])
+    S = key.shape[2]
+    nb_now = (S + bs - 1) // bs
+    fmask = _FROZEN.get(id(module))
+    if fmask is None:  # prefill not seen: attend to everything
+        fmask = torch.ones((Hq, nb_now), dtype=torch.bool, device=query.device)
+    bt, sl = _brt.frozen_decode_block_table(fmask, nb_now, int(cfg["n_sink_blocks"]),
+                                            int(cfg["n_local_blocks"]))
+    if tracing_enabled():
+        record_selection(bt, sl, nb_now)
+    sm_scale = float(scaling) if scaling is not None else 1.0 / math.sqrt(D)
+    out = torch.empty((B, 1, Hq, D), dtype=query.dtype, device=query.device)
+    q3 = query[:, :, 0, :]
+    if q3.stride(-1) != 1:
+        q3 = q3.contiguous()
+    geo = _geometry(B, Hq, key.shape[1], D, bs, S, nb_now, query.dtype)
+    L = _lib.lib()
+    width = bt.shape[1]
+    with torch.cuda.device(query.device):
+        wa = _lib.workspace(L.adakv_attend_workspace_bytes(geo, width), query.device, "attend")
+        _lib.raise_if_failed(wa)
+        _lib.check(L.adakv_attend(geo, _lib.view4(q3), _lib.view4(key), _lib.view4(value),
+                                  bt.data_ptr(), width, sl.data_ptr(), None, sm_scale,
+                                  _lib.view4(out[:, 0]), wa.data_ptr(), wa.numel(),
+                                  _lib.stream_ptr(query.device)))
+    return out, None
 
 
 def _geometry(B, Hq, Hkv, D, bs, S, nb_cap, dtype):
@@ -136,8 +190,18 @@ def adakv_attention_forward(module, query, key, value, attention_mask, scaling, 
     cfg = _ADAKV_CFG
     B, Hq, q_len, D = query.shape
     sel = cfg.get("selection", "adakv")
+    if sel not in ("adakv", "h2o", "snapkv"):
+        raise ValueError(f"unknown selection: {sel!r}")
     if sel != "adakv":
-        raise NotImplementedError(f"selection={sel!r} (eviction baselines) is not built here")
+        if not cfg["enabled"] or B != 1 or not query.is_cuda or D not in (64, 128):
+            return _SDPA(module, query, key, value, attention_mask=attention_mask, scaling=scaling,
+                         dropout=dropout, **kwargs)
+        if q_len > 1:  # prefill: freeze the retained set, return dense attention
+            _capture_frozen(module, query, key, cfg, sel)
+            return _SDPA(module, query, key, value, attention_mask=attention_mask, scaling=scaling,
+                         dropout=dropout, **kwargs)
+        _lib.require_cuda(query, key, value)
+        return _frozen_decode(module, query, key, value, scaling, cfg)
     sparse = cfg["enabled"] and q_len == 1 and (B == 1 or attention_mask is None)
     ext = None  # a preallocated cache layer whose centroid table is already current
     if cfg["enabled"] and cfg["estimator"] == "centroid" and query.is_cuda:
@@ -228,12 +292,14 @@ def enable_adakv(**cfg):
     _ADAKV_CFG.update(cfg)
     _ADAKV_CFG["enabled"] = True
     _STATE.clear()
+    _FROZEN.clear()  # frozen masks of a previous configuration
 
 
 def disable_adakv():
     """Every call goes dense (SDPA) until ``enable_adakv``."""
     _ADAKV_CFG["enabled"] = False
     _STATE.clear()
+    _FROZEN.clear()
 
 
 def patch_model(model, block_size=16, avg_budget=16, **cfg):

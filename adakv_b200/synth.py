@@ -100,3 +100,15 @@ def ragged_seq_lens(seed: int, batch: int, lo: int = 8192, hi: int = 131072) -> 
     """Per-sequence contexts drawn uniformly from ``[lo, hi]`` (seeded)."""
     rng = np.random.default_rng(seed + 1_000_003)
     return rng.integers(lo, hi + 1, size=batch).astype(np.int32)
+
+
+def make_prefill_case(seed: int, Hq: int, Hkv: int, D: int, S: int):
+    """Seeded prompt queries and keys for the H2O / SnapKV baselines, as the
+    reference's baseline tests draw them (Gaussian, scale 0.5): ``Q [Hq, S, D]``,
+    ``K, V [Hkv, S, D]`` and one decode query ``q [Hq, D]``, all float32."""
+    rng = np.random.default_rng(seed)
+    Q = (rng.standard_normal((Hq, S, D)) * 0.5).astype(np.float32)
+    K = (rng.standard_normal((Hkv, S, D)) * 0.5).astype(np.float32)
+    V = rng.standard_normal((Hkv, S, D)).astype(np.float32)
+    q = (rng.standard_normal((Hq, D)) * 0.5).astype(np.float32)
+    return Q, K, V, q

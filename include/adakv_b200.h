@@ -44,6 +44,7 @@
  * Reference interfaces replaced (paths inside the adakv project):
  *   adakv/attention.py:119-139  AdaKVCache.append_prefill   -> adakv_centroid_build
  *   adakv/runtime.py:43-60      update_cache_decode         -> adakv_kv_append
+ *   adakv/baselines_rt.py:43-81 h2o/snapkv_key_importance_torch -> adakv_key_importance
  *   adakv/attention.py:141-146  AdaKVCache.append_decode    -> adakv_kv_append
  *   adakv/attention.py:149-247  plan_selection              -> adakv_plan
  *   adakv/kernels/block_sparse_decode.py:103-135 block_sparse_decode -> adakv_attend
@@ -241,6 +242,22 @@ int adakv_decode_step(const adakv_geometry* geo, const adakv_select_params* sp,
                       int32_t* block_table, int32_t table_width, int32_t* sel_lens,
                       const adakv_view* out, void* workspace, size_t workspace_bytes,
                       void* stream);
+
+/* Per-key attention importance of the H2O / SnapKV eviction baselines
+ * (adakv/baselines.py:69-117, adakv/baselines_rt.py:43-81): the last n_query
+ * prompt query rows (n_query = S: H2O's accumulated attention; the
+ * observation window: SnapKV, before its max-pool) attend causally to the S
+ * keys with scale sm_scale, and
+ *   importance[(b * Hq + h) * imp_stride + j] = sum over those rows i >= j of
+ *   softmax_i(j), float32, j < S = max_seq_len.
+ * q: [B, Hq, S, D] views; k: [B, Hkv, S, D] (read per KV head, not expanded);
+ * the workspace holds the rows' softmax maxima and sums
+ * (adakv_importance_workspace_bytes).  O(S * n_query * D) work, run once per
+ * prompt; deterministic (no atomics). */
+size_t adakv_importance_workspace_bytes(const adakv_geometry* geo, int32_t n_query);
+int adakv_key_importance(const adakv_geometry* geo, const adakv_view* q, const adakv_view* k,
+                         int32_t n_query, float sm_scale, float* importance, int32_t imp_stride,
+                         void* workspace, size_t workspace_bytes, void* stream);
 
 /* Synchronise `stream`, copy the workspace's device status word (ADAKV_ST_*
  * bits) to *status and clear it. */

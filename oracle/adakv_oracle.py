@@ -398,3 +398,84 @@ def compare_selection(scores, k_oracle, raw_oracle, mask_oracle, sets_gpu,
             failures.append((h, f"set differs: gpu-only {a[:8].tolist()} "
                                 f"oracle-only {b[:8].tolist()} rel gap {gap / scale:.3e}"))
     return n_exact, n_budget, n_score, failures
+
+
+# --------------------------------------------------------------------------
+# (f4) H2O / SnapKV frozen-selection baselines (reference adakv/baselines.py)
+# --------------------------------------------------------------------------
+def _causal_importance(Q: np.ndarray, K: np.ndarray, q_first: int) -> np.ndarray:
+    """Sum over query rows i in [q_first, S) of each row's causal softmax over
+    the keys j <= i, in float64 (``baselines.py:69-83``, ``101-116``).
+    ``Q, K : [H, S, D]`` (query heads); returns ``[H, S]`` float64."""
+    H, S, D = K.shape
+    Qw = Q[:, q_first:, :].astype(np.float64)
+    logits = np.einsum("hwd,hjd->hwj", Qw, K.astype(np.float64)) / np.sqrt(D)
+    pos = np.arange(q_first, S)[:, None]
+    logits = np.where(np.arange(S)[None, :] <= pos, logits, -np.inf)
+    logits = logits - logits.max(axis=2, keepdims=True)
+    e = np.exp(logits)
+    return (e / e.sum(axis=2, keepdims=True)).sum(axis=1)
+
+
+def h2o_key_importance(Q: np.ndarray, K: np.ndarray) -> np.ndarray:
+    """H2O's accumulated attention per key over every causal prompt query
+    (``baselines.py:69-83``); ``[H, S]`` float32."""
+    return _causal_importance(Q, K, 0).astype(np.float32)
+
+
+def snapkv_key_importance(Q: np.ndarray, K: np.ndarray, obs_window: int = 32,
+                          pool_kernel: int = 7) -> np.ndarray:
+    """SnapKV: attention from the last ``obs_window`` queries, then a
+    same-length max-pool over key positions with edge padding
+    (``baselines.py:86-117``); ``[H, S]`` float32."""
+    H, S, D = K.shape
+    w = int(min(obs_window, S))
+    imp = _causal_importance(Q, K, S - w)
+    if pool_kernel > 1:
+        pad = pool_kernel // 2
+        xp = np.concatenate([np.repeat(imp[:, :1], pad, axis=1), imp,
+                             np.repeat(imp[:, -1:], pad, axis=1)], axis=1)
+        win = np.lib.stride_tricks.sliding_window_view(xp, pool_kernel, axis=1)
+        imp = win.max(axis=2)
+    return imp.astype(np.float32)
+
+
+def retain_blocks(importance: np.ndarray, block_size: int, n_real: int, budget: int,
+                  n_sink_blocks: int = 1, n_local_blocks: int = 4, c_min: int = 1) -> np.ndarray:
+    """Fixed-budget retention: forced sink and local blocks plus the top content
+    blocks by summed importance, ``k = min(max(budget, sink + local + c_min), nb)``
+    blocks per head (``baselines.py:121-163``); ties to the lowest block index.
+    Returns ``[H, nb]`` bool."""
+    H = importance.shape[0]
+    nb = (n_real + block_size - 1) // block_size
+    imp = np.zeros((H, nb * block_size), dtype=np.float64)
+    imp[:, :n_real] = importance[:, :n_real]
+    blk = imp.reshape(H, nb, block_size).sum(axis=2)
+    sink, local = min(n_sink_blocks, nb), min(n_local_blocks, nb)
+    biased = blk.copy()
+    biased[:, :sink] = np.inf
+    if local:
+        biased[:, nb - local:] = np.inf
+    k = min(max(int(budget), min(sink + local + c_min, nb)), nb)
+    order = np.argsort(-biased, axis=1, kind="stable")
+    mask = np.zeros((H, nb), dtype=bool)
+    np.put_along_axis(mask, order[:, :k], True, axis=1)
+    mask[:, :sink] = True
+    if local:
+        mask[:, nb - local:] = True
+    return mask
+
+
+def frozen_decode_mask(fmask: np.ndarray, nb_now: int, n_sink_blocks: int,
+                       n_local_blocks: int) -> np.ndarray:
+    """The frozen prefill selection extended to ``nb_now`` blocks: content stays
+    as frozen, sink and the current local window are forced
+    (``baselines_rt.py:176-205``)."""
+    H, nbp = fmask.shape
+    m = np.zeros((H, nb_now), dtype=bool)
+    m[:, :nbp] = fmask
+    m[:, :min(n_sink_blocks, nb_now)] = True
+    local = min(n_local_blocks, nb_now)
+    if local:
+        m[:, nb_now - local:] = True
+    return m

@@ -13,7 +13,10 @@ by :func:`adakv_b200.synth.make_decode_case`:
 * ``budget.allocate_budget`` with the floor ``reference.sparse_attention``
   passes (``adakv/reference.py:71-73``), plus its unrounded ``lo + extra``;
 * ``reference.sparse_attention(..., return_mask=True)`` for the block mask,
-  counts and the attention output (``adakv/reference.py:44-84``).
+  counts and the attention output (``adakv/reference.py:44-84``);
+* the H2O / SnapKV baselines: ``baselines.h2o_key_importance``,
+  ``snapkv_key_importance``, ``retain_blocks``, ``frozen_sparse_attention``
+  and ``baselines_rt.frozen_decode_block_table`` (``baselines_*.npz``).
 
 Each case is written to ``tests/golden/<name>.npz`` together with a SHA-256
 of the generated inputs, so the tests can detect generator drift.  The
@@ -166,6 +169,50 @@ def run_case(name, spec, ref, est, bud):
     return counts
 
 
+# H2O / SnapKV eviction baselines (adakv/baselines.py, adakv/baselines_rt.py):
+# inputs from adakv_b200.synth.make_prefill_case, keys expanded to the query
+# heads for the reference's per-query-head functions.
+BASELINE_CASES = {
+    "baselines_h6": dict(seed=20, Hq=6, Hkv=6, D=64, S=384, bs=16, sink=1, local=2, c_min=1,
+                         budgets=(6, 8, 12), window=32, pool=7),
+    "baselines_gqa4": dict(seed=21, Hq=8, Hkv=2, D=128, S=517, bs=16, sink=1, local=4, c_min=1,
+                           budgets=(8, 16), window=32, pool=7),
+}
+
+
+def run_baseline_case(name, spec, path):
+    from adakv_b200.synth import make_prefill_case
+    import importlib as il
+    bl = il.import_module("adakv_ref.baselines")
+    rt = il.import_module("adakv_ref.baselines_rt")
+    import torch
+    c = spec
+    Q, K, V, q = make_prefill_case(c["seed"], c["Hq"], c["Hkv"], c["D"], c["S"])
+    g = c["Hq"] // c["Hkv"]
+    Kq, Vq = np.repeat(K, g, axis=0), np.repeat(V, g, axis=0)
+    h2o = bl.h2o_key_importance(Q, Kq)
+    snap = bl.snapkv_key_importance(Q, Kq, obs_window=c["window"], pool_kernel=c["pool"])
+    rec = dict(h2o=h2o, snapkv=snap)
+    digest = hashlib.sha256()
+    for a in (Q, K, V, q):
+        digest.update(np.ascontiguousarray(a).tobytes())
+    rec["digest"] = np.array(digest.hexdigest())
+    nb = (c["S"] + c["bs"] - 1) // c["bs"]
+    for bud in c["budgets"]:
+        for kind, imp in (("h2o", h2o), ("snapkv", snap)):
+            m = bl.retain_blocks(imp, c["bs"], c["S"], bud, c["sink"], c["local"], c["c_min"])
+            rec[f"mask_{kind}_{bud}"] = m
+            # the decode-time table two blocks later, and one frozen decode step
+            bt, sl = rt.frozen_decode_block_table(torch.from_numpy(m), nb + 2, c["sink"], c["local"])
+            dm = np.zeros((c["Hq"], nb + 2), dtype=bool)
+            for h in range(c["Hq"]):
+                dm[h, bt[h, :int(sl[h])].numpy()] = True
+            rec[f"decode_mask_{kind}_{bud}"] = dm
+            out, _ = bl.frozen_sparse_attention(q, Kq, Vq, m, c["bs"])
+            rec[f"out_{kind}_{bud}"] = np.asarray(out, dtype=np.float64)
+    np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **rec)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path of the reference project")
@@ -177,6 +224,11 @@ def main():
             continue
         counts = run_case(name, spec, ref, est, bud)
         print(f"{name}: counts mean {np.mean(counts):.2f} min {np.min(counts)} max {np.max(counts)}")
+    for name, spec in BASELINE_CASES.items():
+        if args.only and name not in args.only:
+            continue
+        run_baseline_case(name, spec, args.reference)
+        print(f"{name}: written")
 
 
 if __name__ == "__main__":

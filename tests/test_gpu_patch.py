@@ -127,14 +127,69 @@ def test_disabled_and_masked_batches_go_dense():
     assert torch.equal(out1, ref1)
 
 
-def test_eviction_baselines_are_not_built():
+@pytest.mark.parametrize("sel", ["h2o", "snapkv"])
+def test_eviction_baselines_through_patch_match_oracle(sel):
+    """selection="h2o" / "snapkv": the prefill call freezes each head's retained
+    blocks (the oracle's mask), and the decode steps attend to the frozen set
+    plus the sink and the current local window (the oracle's frozen attention)."""
     _need_cuda()
     from adakv_b200 import patch
-    patch.enable_adakv(selection="h2o")
-    q = torch.zeros((1, 8, 1, 64), device="cuda")
-    K = torch.zeros((1, 2, 64, 64), device="cuda")
-    with pytest.raises(NotImplementedError):
-        patch.adakv_attention_forward(_Layer(), q, K, K, None, 0.125)
+    from adakv_b200.synth import make_prefill_case
+    Hq, Hkv, D, bs, P, steps = 8, 2, 64, 16, 700, 20
+    cfg = dict(block_size=bs, avg_budget=12, n_sink_blocks=1, n_local_blocks=3, c_min=1,
+               selection=sel, obs_window=32, pool_kernel=7)
+    patch.enable_adakv(**cfg)
+    Q, K, V, _ = make_prefill_case(40, Hq, Hkv, D, P + steps)
+    Kt = torch.from_numpy(K).cuda()[None]
+    Vt = torch.from_numpy(V).cuda()[None]
+    layer = _Layer()
+    out_p, _ = patch.adakv_attention_forward(layer, torch.from_numpy(Q[:, :P]).cuda()[None],
+                                             Kt[:, :, :P], Vt[:, :, :P], None, D ** -0.5)
+    g = Hq // Hkv
+    Kq = np.repeat(K[:, :P], g, axis=0)
+    imp = (O.h2o_key_importance(Q[:, :P], Kq) if sel == "h2o"
+           else O.snapkv_key_importance(Q[:, :P], Kq, 32, 7))
+    fmask = O.retain_blocks(imp, bs, P, 12, 1, 3, 1)
+    assert np.array_equal(patch._FROZEN[id(layer)].cpu().numpy(), fmask)
+    rng = np.random.default_rng(41)
+    for t in range(steps):
+        S = P + t + 1
+        qn = rng.standard_normal((Hq, D)).astype(np.float32)
+        q = torch.from_numpy(qn).cuda()[None, :, None, :]
+        out, _ = patch.adakv_attention_forward(layer, q, Kt[:, :, :S], Vt[:, :, :S], None, D ** -0.5)
+        dm = O.frozen_decode_mask(fmask, (S + bs - 1) // bs, 1, 3)
+        ref = O.attend_mask(qn, K[:, :S], V[:, :S], dm, bs)
+        assert np.abs(out[0, 0].cpu().numpy() - ref).max() < TOL["fp32"]
+
+
+@pytest.mark.parametrize("dtype,Hq,Hkv,D,S", [("fp32", 6, 6, 64, 384), ("fp32", 8, 2, 128, 517),
+                                               ("bf16", 16, 4, 128, 1500)])
+def test_key_importance_matches_oracle(dtype, Hq, Hkv, D, S):
+    """adakv_key_importance (GQA, per KV head) against the float64 oracle at the
+    reference's own bar (1e-4 relative), and the retained masks equal."""
+    _need_cuda()
+    from adakv_b200 import baselines_rt as RT
+    from adakv_b200.synth import make_prefill_case
+    Q, K, _, _ = make_prefill_case(42, Hq, Hkv, D, S)
+    Q, K = round_to_dtype(Q, dtype), round_to_dtype(K, dtype)
+    dt = TORCH[dtype]
+    q = torch.from_numpy(Q).cuda().to(dt)[None]
+    k = torch.from_numpy(K).cuda().to(dt)[None]
+    Kq = np.repeat(K, Hq // Hkv, axis=0)
+    for n_query, ref in ((S, O.h2o_key_importance(Q, Kq)),
+                         (32, O.snapkv_key_importance(Q, Kq, 32, 1))):
+        got = RT.key_importance(q, k, n_query).cpu().numpy()
+        rel = np.abs(got - ref).max() / np.abs(ref).max()
+        assert rel < 1e-4, f"n_query {n_query}: rel err {rel:.2e}"
+    # the reference-layout entry points (keys expanded) and the retained masks
+    if Hq == Hkv:
+        Qt, Kt = torch.from_numpy(Q).cuda(), torch.from_numpy(K).cuda()
+        for budget in (6, 8, 12):
+            m = RT.h2o_retained_mask_torch(Qt, Kt, 16, budget, 1, 2, 1).cpu().numpy()
+            assert np.array_equal(m, O.retain_blocks(O.h2o_key_importance(Q, K), 16, S, budget, 1, 2, 1))
+            m = RT.snapkv_retained_mask_torch(Qt, Kt, 16, budget, 32, 7, 1, 2, 1).cpu().numpy()
+            ref = O.retain_blocks(O.snapkv_key_importance(Q, K, 32, 7), 16, S, budget, 1, 2, 1)
+            assert np.array_equal(m, ref)
 
 
 def _tiny_llama(dtype):

@@ -125,3 +125,36 @@ def test_compare_selection_classifies_near_ties():
     m5, _ = O.select_blocks(s3, np.array([5]), 1, 1, 1)
     res = O.compare_selection(s3, np.array([5]), np.array([4.50001]), m5, [[0, 5, 2, 3]], 1, 1, 1)
     assert res[1] == 1 and not res[3]
+
+
+@pytest.mark.parametrize("name", sorted(__import__("tests.golden.make_golden",
+                                                   fromlist=["BASELINE_CASES"]).BASELINE_CASES))
+def test_baseline_oracle_matches_reference_golden(name):
+    """H2O / SnapKV: importance to 1e-6 relative, retained masks (every budget),
+    the frozen decode-time mask and the frozen attention output, against the
+    reference's own outputs."""
+    import hashlib
+    from adakv_b200.synth import make_prefill_case
+    from tests.golden.make_golden import BASELINE_CASES
+    c = BASELINE_CASES[name]
+    gold = _load(name)
+    Q, K, V, q = make_prefill_case(c["seed"], c["Hq"], c["Hkv"], c["D"], c["S"])
+    h = hashlib.sha256()
+    for a in (Q, K, V, q):
+        h.update(np.ascontiguousarray(a).tobytes())
+    assert h.hexdigest() == str(gold["digest"]), "seeded generator drifted"
+    g = c["Hq"] // c["Hkv"]
+    Kq, Vq = np.repeat(K, g, axis=0), np.repeat(V, g, axis=0)
+    h2o = O.h2o_key_importance(Q, Kq)
+    snap = O.snapkv_key_importance(Q, Kq, c["window"], c["pool"])
+    for got, ref in ((h2o, gold["h2o"]), (snap, gold["snapkv"])):
+        assert np.abs(got - ref).max() <= 1e-6 * np.abs(ref).max()
+    nb = (c["S"] + c["bs"] - 1) // c["bs"]
+    for bud in c["budgets"]:
+        for kind, imp in (("h2o", h2o), ("snapkv", snap)):
+            m = O.retain_blocks(imp, c["bs"], c["S"], bud, c["sink"], c["local"], c["c_min"])
+            assert np.array_equal(m, gold[f"mask_{kind}_{bud}"]), f"{kind} budget {bud}"
+            dm = O.frozen_decode_mask(m, nb + 2, c["sink"], c["local"])
+            assert np.array_equal(dm, gold[f"decode_mask_{kind}_{bud}"])
+            out = O.attend_mask(q, K, V, m, c["bs"])
+            assert np.abs(out - gold[f"out_{kind}_{bud}"]).max() < 1e-6
