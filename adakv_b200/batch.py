@@ -136,8 +136,15 @@ class BatchedDecoder:
         With ``k_new`` / ``v_new`` (``[B, Hkv, n, D]``) the step first appends those
         tokens (fused into the estimator kernel: in-place cache write + centroid
         refresh).  ``advance=False`` overwrites the last ``n`` tokens instead of
-        growing the sequences (fixed-context benchmarking)."""
+        growing the sequences (fixed-context benchmarking).  ``out`` may be a
+        page-locked host tensor (``pin_memory()``, mapped into the device's
+        address space): the attention kernel then writes the result straight
+        into host memory, with no separate device-to-host copy."""
         out = self.out if out is None else out
+        if not out.is_cuda and not out.is_pinned():
+            raise ValueError("out must be a CUDA tensor or a page-locked host tensor")
+        if out.shape != self.out.shape or out.dtype != self.out.dtype:
+            raise ValueError(f"out must be {tuple(self.out.shape)} {self.out.dtype}")
         scale = 1.0 / math.sqrt(self.D) if sm_scale is None else float(sm_scale)
         n_new = 0
         kn = vn = None

@@ -42,3 +42,33 @@ def test_graphed_step_matches_eager(advance):
         assert torch.equal(graph.seq_lens, eager.seq_lens)
     assert torch.equal(graph.k, eager.k) and torch.equal(graph.centroid, eager.centroid)
     assert graph.status() == 0 and eager.status() == 0
+
+
+@pytest.mark.parametrize("path", [1, 2], ids=["chain", "one_kernel"])
+def test_step_writes_output_into_pinned_host_memory(path):
+    """``step(out=<page-locked host tensor>)``: the attention kernel writes the
+    result straight into mapped host memory, bit-identical to the device output."""
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    from adakv_b200 import _lib
+    B, Hq, Hkv, D, bs, S = 1, 32, 8, 128, 16, 20000
+    g = torch.Generator(device="cuda").manual_seed(4)
+    K = torch.randn((B, Hkv, S, D), device="cuda", generator=g).to(torch.bfloat16)
+    V = torch.randn((B, Hkv, S, D), device="cuda", generator=g).to(torch.bfloat16)
+    dec = BatchedDecoder(B, Hq, Hkv, D, bs, S, torch.bfloat16, "cuda", avg_budget=64, k_max=512)
+    dec.load(K, V, [S])
+    q = torch.randn((B, Hq, D), device="cuda", generator=g).to(torch.bfloat16)
+    kn = torch.randn((B, Hkv, 1, D), device="cuda", generator=g).to(torch.bfloat16)
+    host = torch.zeros((B, Hq, D), dtype=torch.bfloat16).pin_memory()
+    _lib.debug_knob(_lib.KNOB_STEP_PATH, path)
+    try:
+        ref = dec.step(q, k_new=kn, v_new=kn, advance=False).clone()
+        dec.step(q, k_new=kn, v_new=kn, advance=False, out=host)
+        torch.cuda.synchronize()
+        assert dec.last_path() == path
+    finally:
+        _lib.debug_knob(_lib.KNOB_STEP_PATH, 0)
+    assert torch.equal(host, ref.cpu())
+    with pytest.raises(ValueError):
+        dec.step(q, out=torch.zeros((B, Hq, D), dtype=torch.bfloat16))  # pageable host memory
+    assert dec.status() == 0
