@@ -235,9 +235,20 @@ _sinks: dict = {}
 
 
 def workspace(nbytes: int, device, kind: str = "plan") -> torch.Tensor:
+    """The cached workspace of ``kind`` for the current stream of ``device``
+    (zeroed on allocation, status sink attached).  While the stream is being
+    captured into a CUDA graph, nothing may be allocated or synchronised: the
+    workspace the same ``kind`` already has on this device is reused (the
+    capture is ordered after the eager calls that created it)."""
     device = torch.device(device)
     key = (device.index, stream_ptr(device), kind)
     ws = _workspaces.get(key)
+    if (ws is None or ws.numel() < nbytes) and torch.cuda.is_current_stream_capturing():
+        for (idx, _, k), w in _workspaces.items():
+            if idx == device.index and k == kind and w.numel() >= nbytes:
+                return w
+        raise ValueError(f"no {kind!r} workspace of {nbytes} bytes exists on cuda:{device.index}: "
+                         "make one eager call before capturing the stream")
     if ws is None or ws.numel() < nbytes:
         ws = torch.zeros(max(int(nbytes), 256), dtype=torch.uint8, device=device)
         _workspaces[key] = ws

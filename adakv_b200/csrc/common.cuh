@@ -270,7 +270,7 @@ __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
-// --- mbarrier + 1-D bulk copy (TMA engine, no multicast) -------------------
+// --- mbarrier + 1-D bulk copy (TMA engine, one CTA per copy) ---------------
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count)
                : "memory");

@@ -9,7 +9,7 @@
 // Persistent grid, one CTA per SM.  The work is the list of 64-row chunks of
 // every (sequence, KV head) centroid table; each CTA owns a contiguous range of
 // it.  A producer warp streams chunks through a 4-stage shared-memory ring with
-// 1-D bulk copies (the TMA engine; no multicast), each stage also carrying the g
+// 1-D bulk copies (the TMA engine, one CTA per copy), each stage also carrying the g
 // query rows of the chunk's KV head; completion is signalled on per-stage
 // mbarriers (transaction bytes) and stages are released by the 8 consumer warps
 // through a second set of mbarriers.  A consumer lane owns D/32 dims of a row

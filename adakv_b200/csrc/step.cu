@@ -16,7 +16,7 @@
 // Phase A -- append + estimator (adakv/runtime.py:43-60, adakv/estimator.py:73-74).
 //   The (sequence, KV head, block) rows of every centroid table form one list,
 //   split evenly over the CTAs.  A CTA streams its rows through a 4-stage ring
-//   of 64-row stages with 1-D bulk copies (TMA engine, no multicast); each
+//   of 64-row stages with 1-D bulk copies (TMA engine, one CTA per copy); each
 //   stage is refilled by the last warp to finish with it.  A warp scores 8
 //   rows per stage against the g query heads of the row's KV head: LPR = 2g
 //   lanes share a row (D / LPR dims each, queries in registers) and one

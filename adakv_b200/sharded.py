@@ -67,6 +67,7 @@ class ShardCache:
         self.cap = max(capacity_blocks or self.nb, self.nb, 1)
         self.centroid = torch.zeros((self.Hkv, self.cap, self.D), dtype=torch.float32,
                                     device=K.device)
+        self._ws = {}
         if self.S > 0:
             with torch.cuda.device(K.device):
                 _lib.check(_lib.lib().adakv_centroid_build(
@@ -77,15 +78,22 @@ class ShardCache:
         return _lib.geometry(1, self.Hq, self.Hkv, self.D, self.bs, max(self.S, 1), self.cap,
                              _lib.TORCH_DTYPES[self.dtype])
 
+    def _workspace(self, nbytes, device, kind):
+        """This shard's workspace of ``kind``, allocated on first use and kept
+        (a replay of a captured step must find the same buffer)."""
+        ws = self._ws.get(kind)
+        if ws is None or ws.numel() < nbytes:
+            ws = self._ws[kind] = _lib.workspace(nbytes, device, kind)
+        return ws
+
     def local_scores(self, q, out):
         """Scores of this shard's blocks into ``out[:, :nb]`` (``out``: ``[Hq, >= cap]`` fp32)."""
         if self.S == 0:
             return out
         L = _lib.lib()
         geo = self._geo()
-        ws = _lib.workspace(L.adakv_plan_workspace_bytes(geo, _lib.select_params(1, 1, 1, 0, 0, 0,
-                                                                                 1.0, "fixed")),
-                            q.device, "shard-estimate")
+        ws = self._workspace(L.adakv_plan_workspace_bytes(geo, _lib.select_params(
+            1, 1, 1, 0, 0, 0, 1.0, "fixed")), q.device, "shard-estimate")
         with torch.cuda.device(q.device):
             _lib.check(L.adakv_estimate(geo, _lib.view4(q.unsqueeze(0)), self.centroid.data_ptr(),
                                         None, out.data_ptr(), out.stride(0), ws.data_ptr(),
@@ -101,7 +109,7 @@ class ShardCache:
         L = _lib.lib()
         geo = self._geo()
         width = block_table.shape[1]
-        ws = _lib.workspace(L.adakv_attend_workspace_bytes(geo, width), q.device, "shard-attend")
+        ws = self._workspace(L.adakv_attend_workspace_bytes(geo, width), q.device, "shard-attend")
         with torch.cuda.device(q.device):
             _lib.check(L.adakv_attend_partial(
                 geo, _lib.view4(q.unsqueeze(0)), _lib.view4(self.k.unsqueeze(0)),
