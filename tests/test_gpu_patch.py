@@ -12,7 +12,7 @@ from adakv_b200.synth import make_decode_case, round_to_dtype
 pytestmark = pytest.mark.gpu
 
 TOL = {"fp32": 1e-3, "bf16": 2e-2}
-TORCH = {"fp32": torch.float32, "bf16": torch.bfloat16}
+TORCH = {"fp32": torch.float32, "bf16": torch.bfloat16, "fp16": torch.float16}
 
 
 def _need_cuda():
@@ -163,7 +163,7 @@ def test_eviction_baselines_through_patch_match_oracle(sel):
 
 
 @pytest.mark.parametrize("dtype,Hq,Hkv,D,S", [("fp32", 6, 6, 64, 384), ("fp32", 8, 2, 128, 517),
-                                               ("bf16", 16, 4, 128, 1500)])
+                                               ("bf16", 16, 4, 128, 1500), ("fp16", 8, 2, 64, 300)])
 def test_key_importance_matches_oracle(dtype, Hq, Hkv, D, S):
     """adakv_key_importance (GQA, per KV head) against the float64 oracle at the
     reference's own bar (1e-4 relative), and the retained masks equal."""
@@ -305,3 +305,18 @@ def test_static_cache_generate_matches_dynamic_cache():
     with pytest.raises(ValueError, match="holds"):
         cache.layers[0].update(torch.zeros(2, 2, 2, 64, device="cuda"),
                                torch.zeros(2, 2, 2, 64, device="cuda"))
+
+
+def test_key_importance_batched_rows_are_independent():
+    """B = 2 in one launch: each sequence's importance equals its own oracle."""
+    _need_cuda()
+    from adakv_b200 import baselines_rt as RT
+    from adakv_b200.synth import make_prefill_case
+    Hq, Hkv, D, S = 8, 2, 128, 333
+    cases = [make_prefill_case(50 + b, Hq, Hkv, D, S) for b in range(2)]
+    q = torch.stack([torch.from_numpy(c[0]) for c in cases]).cuda()
+    k = torch.stack([torch.from_numpy(c[1]) for c in cases]).cuda()
+    got = RT.key_importance(q, k, S).cpu().numpy().reshape(2, Hq, S)
+    for b, (Q, K, _, _) in enumerate(cases):
+        ref = O.h2o_key_importance(Q, np.repeat(K, Hq // Hkv, axis=0))
+        assert np.abs(got[b] - ref).max() / np.abs(ref).max() < 1e-4
