@@ -528,9 +528,14 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanParams p) {
       // e (log 1e-9 - log p) is under 1e-18 of H: skip the exp there
       const float d_hi = adaptive ? logf(pre) : -INFINITY;
       const float d_lo = d_hi - 25.f;
+      // p = e / Z rounded to float is below 1e-9f exactly when e <= mid * Z,
+      // mid = the midpoint between 1e-9f and the float below it (a tie rounds
+      // down: 1e-9f has an odd significand); mid * Z is exact in double
+      // (25 + 24 significant bits), so no division is needed
+      const double clamp_mz = 0.5 * ((double)nextafterf(1e-9f, 0.f) + (double)1e-9f) * (double)Zf;
       auto corr = [&](float d) {
         const float e = expf(d);
-        if (e > 0.f && e < pre && __fdiv_rn(e, Zf) < 1e-9f) cp = fmaf(e, ln_floor - d + logZ, cp);
+        if (e > 0.f && e < pre && (double)e <= clamp_mz) cp = fmaf(e, ln_floor - d + logZ, cp);
       };
       if (!long_slice) {
         // short slice: one inline pass (the deferred lists do not pay here)

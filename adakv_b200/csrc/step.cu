@@ -786,6 +786,11 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepParams p) {
       // the rounded quotient of expf is taken
       const float invZ = 1.f / Zf;
       const float clamp_lo = 1e-9f * (1.f - 1e-5f), clamp_hi = 1e-9f * (1.f + 1e-5f);
+      // near the bound: e / Z rounded to float is below 1e-9f exactly when
+      // e <= mid * Z, mid = the midpoint between 1e-9f and the float below it
+      // (1e-9f has an odd significand, so a tie rounds down; the product is
+      // exact in double)
+      const double clamp_mz = 0.5 * ((double)nextafterf(1e-9f, 0.f) + (double)1e-9f) * (double)Zf;
 #pragma unroll 1
       for (int c = tid; c < nch; c += 2 * kStepThreads) {
         const int c2 = c + kStepThreads;
@@ -820,7 +825,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(StepParams p) {
             if (band[e]) {
               const float dd = __fsub_rn(zof(v[e]), zmax);
               const float ea = expf(dd);
-              if (ea > 0.f && __fdiv_rn(ea, Zf) < 1e-9f) cpa += __expf(dd) * (cst - dd);
+              if (ea > 0.f && (double)ea <= clamp_mz) cpa += __expf(dd) * (cst - dd);
             }
           }
         }
