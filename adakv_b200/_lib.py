@@ -13,7 +13,10 @@ import threading
 
 import torch
 
-LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libadakv_b200.so")
+# the package's own build; ADAKV_LIB names another copy of the library (an
+# installed build, or an alternative build to compare against)
+LIB_PATH = os.environ.get("ADAKV_LIB") or os.path.join(os.path.dirname(os.path.abspath(__file__)),
+                                                       "libadakv_b200.so")
 
 DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2
 POLICY_FIXED, POLICY_ADAPTIVE, POLICY_NUCLEUS = 0, 1, 2

@@ -517,11 +517,13 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanParams p) {
     // and finished after the pass: the per-key work is a few compares and
     // predicated stores.
     const float zmax = unit_t ? mx : __fdiv_rn(mx, Tf);
+    // log Z once, for the clamp terms (float) and the entropy (double)
+    const double logZd = adaptive ? log(Ztot) : 0.0;
     float cp = 0.f;
     int ncl = 0;  // blocks this thread listed
     {
       const float Zf = (float)Ztot;
-      const float logZ = adaptive ? (float)log(Ztot) : 0.f;
+      const float logZ = (float)logZd;
       const float ln_floor = logf(1e-9f);
       const float pre = 2e-9f * Zf;  // p < 1e-9 implies e < 2e-9 * Z
       // p < 1e-9 needs d < log(2e-9 Z); below d_lo the clamp's correction
@@ -734,7 +736,7 @@ __global__ void __launch_bounds__(kPlanThreads, 1) plan_kernel(PlanParams p) {
       double c2 = cp, z2 = 0.0;
       block_sum2(c2, z2, dred, dred2);
       // this CTA's share of H: CTA 0 carries log Z - A / Z, every CTA -Cc_r / Z
-      t_mine = (rank == 0 ? log(Ztot) - Atot / Ztot : 0.0) - c2 / Ztot;
+      t_mine = (rank == 0 ? logZd - Atot / Ztot : 0.0) - c2 / Ztot;
     }
     __syncthreads();
     cluster_arrive_release();  // (2) this CTA's histogram is complete
