@@ -96,6 +96,7 @@ _SIGNATURES = {
     "adakv_debug_timeline": (ctypes.c_int, [_P(Geometry), _vp, ctypes.c_size_t, _vp, ctypes.c_int32,
                                             _vp]),
     "adakv_importance_workspace_bytes": (ctypes.c_size_t, [_P(Geometry), ctypes.c_int32]),
+    "adakv_stage": (ctypes.c_int, [_vp, _vp, ctypes.c_size_t, _vp]),
     "adakv_key_importance": (ctypes.c_int, [_P(Geometry), _P(View), _P(View), ctypes.c_int32,
                                             ctypes.c_float, _vp, ctypes.c_int32, _vp, ctypes.c_size_t,
                                             _vp]),

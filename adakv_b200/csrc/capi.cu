@@ -853,6 +853,28 @@ int adakv_last_path(const void* workspace) {
   return it->second ? 2 : 1;
 }
 
+int adakv_stage(void* dst, const void* src, size_t bytes, void* stream) {
+  if (!dst || !src) return fail(ADAKV_ERR_INVALID, "dst / src are NULL");
+  if (bytes == 0) return ADAKV_OK;
+  if (reinterpret_cast<uintptr_t>(dst) % 16 || reinterpret_cast<uintptr_t>(src) % 16)
+    return fail(ADAKV_ERR_INVALID, "dst and src must be 16-byte aligned");
+  cudaPointerAttributes da{}, sa{};
+  CUDA_TRY(cudaPointerGetAttributes(&da, dst));
+  CUDA_TRY(cudaPointerGetAttributes(&sa, src));
+  if (da.type != cudaMemoryTypeDevice && da.type != cudaMemoryTypeManaged)
+    return fail(ADAKV_ERR_INVALID, "dst must be device memory");
+  const void* s = src;
+  if (sa.type == cudaMemoryTypeHost) {
+    if (!sa.devicePointer)
+      return fail(ADAKV_ERR_INVALID, "src is page-locked host memory without a device mapping");
+    s = sa.devicePointer;
+  } else if (sa.type == cudaMemoryTypeUnregistered) {
+    return fail(ADAKV_ERR_INVALID, "src must be device or page-locked host memory");
+  }
+  CUDA_TRY(launch_stage(s, dst, bytes, static_cast<cudaStream_t>(stream)));
+  return ADAKV_OK;
+}
+
 int adakv_set_status_sink(void* workspace, uint32_t* host_word, void* stream) {
   if (!workspace) return fail(ADAKV_ERR_INVALID, "workspace is NULL");
   void* dev = nullptr;

@@ -296,6 +296,7 @@ cudaError_t launch_minmax_score(const MinmaxParams& p, int dtype, int D, int nb_
                                 cudaStream_t stream);
 cudaError_t launch_combine(const CombineParams& p, int dtype, cudaStream_t stream, const LaunchOpts& o);
 cudaError_t launch_importance(const ImportanceParams& p, int dtype, int D, cudaStream_t stream);
+cudaError_t launch_stage(const void* src, void* dst, size_t bytes, cudaStream_t stream);
 cudaError_t launch_step(const StepParams& p, int dtype, int D, int g, int grid, size_t smem,
                         cudaStream_t stream, const LaunchOpts& o);
 cudaError_t launch_step_scores(bool fused, const float* fscores,

@@ -271,6 +271,15 @@ int adakv_read_status(void* workspace, uint32_t* status, void* stream);
  * No counterpart in the reference (its errors are host exceptions). */
 int adakv_set_status_sink(void* workspace, uint32_t* host_word, void* stream);
 
+/* Copy `bytes` from `src` (device memory, or page-locked host memory mapped
+ * into the device's address space) to device memory `dst` on `stream`, with a
+ * kernel that reads the source directly.  Meant for a decode step's few KB of
+ * inputs (q and the new K / V rows) arriving from the host: for transfers this
+ * small a copy-engine transfer's fixed cost dominates (about 11 us for a 12 KB
+ * row on B200), while the kernel finishes in a few us.  Both addresses 16-byte
+ * aligned.  No counterpart in the reference (its inputs are torch tensors). */
+int adakv_stage(void* dst, const void* src, size_t bytes, void* stream);
+
 /* Block scores (q . centroid, float32, unscaled) of the last adakv_plan or
  * adakv_decode_step enqueued on `workspace`, into
  * scores_out[(b * Hq + h) * score_stride + j] for j < ceil(max_seq_len / block_size).

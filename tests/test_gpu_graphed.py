@@ -72,3 +72,29 @@ def test_step_writes_output_into_pinned_host_memory(path):
     with pytest.raises(ValueError):
         dec.step(q, out=torch.zeros((B, Hq, D), dtype=torch.bfloat16))  # pageable host memory
     assert dec.status() == 0
+
+
+@pytest.mark.parametrize("nbytes", [16, 12288, 12290, 1 << 20])
+def test_stage_copies_pinned_host_rows(nbytes):
+    """adakv_stage (through ``batch.stage``): a page-locked host row, and a
+    device tensor, copied into device memory byte for byte, also at an offset
+    into a larger pinned buffer and with a tail that is not a multiple of 16."""
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    from adakv_b200.batch import stage
+    g = torch.Generator().manual_seed(nbytes)
+    host = torch.randint(0, 256, (2 * nbytes + 64,), dtype=torch.uint8, generator=g).pin_memory()
+    for off in (0, 48):
+        src = host[off:off + nbytes]
+        dst = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+        stage(dst, src)
+        torch.cuda.synchronize()
+        assert torch.equal(dst.cpu(), src)
+    dev_src = host[:nbytes].cuda()
+    dst = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+    stage(dst, dev_src)
+    assert torch.equal(dst, dev_src)
+    with pytest.raises(ValueError):
+        stage(dst, host[:nbytes].clone())  # pageable host memory
+    with pytest.raises(ValueError):
+        stage(dst, host[:nbytes - 1])      # size mismatch
