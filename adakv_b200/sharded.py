@@ -100,10 +100,17 @@ class ShardCache:
                                         ws.numel(), _lib.stream_ptr(q.device)))
         return out
 
-    def attend_partial(self, q, block_table, sel_lens, sm_scale):
-        """``(o [Hq, D] fp32, lse [Hq] fp32)`` over the selected blocks held here."""
-        o = torch.zeros((self.Hq, self.D), dtype=torch.float32, device=q.device)
-        lse = torch.full((self.Hq,), -math.inf, dtype=torch.float32, device=q.device)
+    def attend_partial(self, q, block_table, sel_lens, sm_scale, packed=None):
+        """``(o [Hq, D] fp32, lse [Hq] fp32)`` over the selected blocks held here.
+        With ``packed`` (float32, ``Hq * (D + 1)`` elements) both are views of it,
+        o first, so one collective can carry them."""
+        n = self.Hq * self.D
+        if packed is None:
+            packed = torch.empty(n + self.Hq, dtype=torch.float32, device=q.device)
+        o = packed[:n].view(self.Hq, self.D)
+        lse = packed[n:n + self.Hq]
+        o.zero_()
+        lse.fill_(-math.inf)
         if self.S == 0:
             return o, lse
         L = _lib.lib()
@@ -228,7 +235,9 @@ class ShardedDecoder:
         scores = _concat_scores(gathered, self.nb, self.L)
         table, sel_lens = self.selector.select(scores)
         scale = 1.0 / math.sqrt(D) if sm_scale is None else float(sm_scale)
-        o, lse = self.shard.attend_partial(q, table, sel_lens, scale)
-        parts = self.comm.all_gather(o)                               # [world, Hq, D]
-        lses = self.comm.all_gather(lse)                              # [world, Hq]
+        packed = torch.empty(Hq * D + Hq, dtype=torch.float32, device=q.device)
+        self.shard.attend_partial(q, table, sel_lens, scale, packed=packed)
+        g = self.comm.all_gather(packed)                             # [world, Hq * (D + 1)]
+        parts = g[:, :Hq * D].reshape(g.shape[0], Hq, D)             # one collective for (o, lse)
+        lses = g[:, Hq * D:]
         return combine(parts, lses, q.dtype)

@@ -201,3 +201,35 @@ def test_long_slice_selection_paths(case):
     n_exact, n_budget, n_score, failures = O.compare_selection(s, k, raw, mask, sets, 1, 4, 1)
     assert not failures, failures[:4]
     assert n_exact + n_budget + n_score == Hq
+
+
+class _OneRank:
+    """A communicator of one rank (all-gathers are a leading axis of 1)."""
+    world, rank = 1, 0
+
+    def all_gather(self, t):
+        return t.unsqueeze(0)
+
+
+def test_sharded_decoder_one_rank_equals_single_gpu_step():
+    """ShardedDecoder.step with one rank (its packed (o, lse) exchange included)
+    gives the single-GPU step's selection and output."""
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    from adakv_b200.batch import BatchedDecoder
+    from adakv_b200.sharded import ShardedDecoder
+    Hq, Hkv, D, bs, S = 32, 8, 128, 16, 20000 + 5
+    kw = dict(avg_budget=64, k_min=2, k_max=512)
+    g = torch.Generator(device="cuda").manual_seed(11)
+    q = torch.randn((Hq, D), device="cuda", generator=g).to(torch.bfloat16)
+    K = torch.randn((Hkv, S, D), device="cuda", generator=g).to(torch.bfloat16)
+    V = torch.randn((Hkv, S, D), device="cuda", generator=g).to(torch.bfloat16)
+    sd = ShardedDecoder(K, V, S, Hq, bs, _OneRank(), **kw)
+    out = sd.step(q)
+    ref_dec = BatchedDecoder(1, Hq, Hkv, D, bs, S, torch.bfloat16, "cuda", **kw)
+    ref_dec.load(K[None], V[None], [S])
+    ref = ref_dec.step(q[None])[0]
+    sets = [sd.selector.table[h, : int(sd.selector.sel_lens[h])].cpu().numpy() for h in range(Hq)]
+    for a, b in zip(sets, ref_dec.selected_sets()):
+        assert np.array_equal(np.sort(a), np.sort(b))
+    assert (out.float() - ref.float()).abs().max().item() < 2e-2
