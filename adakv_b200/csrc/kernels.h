@@ -165,7 +165,6 @@ constexpr int kStepMaxBatch = 32;       // sequences per call
 constexpr int kStepMaxHeads = 128;      // B * Hq (one selection CTA per query head)
 constexpr int kStepMaxBlocks = 32768;   // blocks per sequence (the score row is staged in smem)
 constexpr int kStepMaxGrid = 256;       // CTAs (one per SM)
-constexpr int kStepOrderCap = 4096;     // bucket-sorted candidate blocks per head
 constexpr int kStepCandCap = 1024;      // boundary-bucket members ranked exactly
 constexpr size_t kStepSmemMax = 220 * 1024;
 
@@ -204,7 +203,7 @@ struct StepParams {
   uint64_t wait_ns;            // bound of every device-side wait
   int debug_flags;             // test-only: bit 0 = head 0 never publishes its entropy,
                                // bit 1 = record per-CTA phase timestamps in `timeline`
-  unsigned long long* timeline;  // [grid, 8] globaltimer stamps (debug)
+  unsigned long long* timeline;  // [grid, kStepTimelineSlots] globaltimer stamps (debug)
 };
 constexpr int kStepTimelineSlots = 24;
 

@@ -1,66 +1,75 @@
 // (a)-(d) One AdaKV decode step in one persistent kernel.
 //
-// One CTA per SM (256 threads).  The step's three dependent stages run as
-// phases of the same grid with no kernel boundary between them:
+// One CTA per SM (256 threads), launched as thread-block clusters of C CTAs
+// (C chosen by the host).  The step's three dependent stages run as phases of
+// the same grid with no kernel boundary between them:
 //   A -> B: every CTA adds one to a monotonic arrival counter (release) when
-//           its scores are written; a selection CTA waits for this call's
-//           GRID arrivals (acquire) and reads its score row in one batch;
-//   B -> B, B -> C, C -> C: the head entropies, the selection bitmaps and the
-//           attention partials are tagged 64-bit words (call tag << 32 |
-//           payload): a reader re-reads, all at once, the words that do not
-//           carry this call's tag yet, so it proceeds one round trip after the
-//           last one lands, and nothing has to be reset between calls.
+//           its scores and statistics records are written; a selection CTA
+//           waits for this call's GRID arrivals (acquire);
+//   B -> B, B -> C, C -> C: the head entropies, the ready words of the
+//           selection bitmaps and the attention partials' flags are tagged
+//           64-bit words (call tag << 32 | payload): a reader re-reads, all at
+//           once, the words that do not carry this call's tag yet, so it
+//           proceeds one round trip after the last one lands, and nothing has
+//           to be reset between calls.
 // Every wait is bounded in time; on expiry the status word records
 // ADAKV_ST_WAIT_TIMEOUT and the kernel runs to completion on what it has.
 //
 // Phase A -- append + estimator (adakv/runtime.py:43-60, adakv/estimator.py:73-74).
 //   The (sequence, KV head, block) rows of every centroid table form one list,
-//   split evenly over the CTAs.  A CTA streams its rows through a 4-stage ring
+//   split evenly over the CTAs.  A CTA streams its rows through a 6-stage ring
 //   of 64-row stages with 1-D bulk copies (TMA engine, one CTA per copy); each
 //   stage is refilled by the last warp to finish with it.  A warp scores 8
 //   rows per stage against the g query heads of the row's KV head: LPR = 2g
 //   lanes share a row (D / LPR dims each, queries in registers) and one
 //   reduce-scatter over those lanes leaves every head's score in a lane.
-//   Scores go out as tagged words.  When the step appends tokens, warp 7 of
-//   CTA (b * Hkv + kvh) first writes them into the K/V cache, recomputes the
-//   touched blocks' centroids from their tokens (token-order float32 sum, one
-//   IEEE division: bit-identical to a rebuild) and scores those rows itself.
+//   Scores go out as plain floats, and each warp folds them per head into a
+//   softmax record (max, content max / sum / sum of squares, m, Z, A) stored
+//   once per (sequence, KV head) run of its CTA.  When the step appends
+//   tokens, warp 7 of CTA (b * Hkv + kvh) first writes them into the K/V
+//   cache, recomputes the touched blocks' centroids from their tokens
+//   (token-order float32 sum, one IEEE division: bit-identical to a rebuild)
+//   and scores those rows itself.
 //
 // Phase B -- entropy budget + top-k (adakv/budget.py:28-86, adakv/selector.py:18-60).
-//   CTA r < B * Hq owns query head r.  It reads the head's score row into
-//   shared memory, computes the row's max, content statistics and softmax sums
-//   (float per thread, double across threads), the entropy
-//   H = log Z - A / Z - Cc / Z (Cc: the reference's max(p, 1e-9) clamp), and
-//   publishes H.  Warp 0 then polls the H of every head of the sequence while
-//   warps 1-7 histogram the content scores into 2048 buckets below the content
-//   max and bucket-sort the blocks of the buckets any budget can reach.  With
-//   the weights, every CTA derives the same per-head counts (fixed-order sums,
-//   half-to-even rounding); a head's selection is then the forced sink/local
+//   One cluster of C CTAs per query head; rank r owns a 32-aligned slice of
+//   the score row.  Every CTA folds the head's estimator records (and the
+//   rows the append scored) into the row's max, content statistics and
+//   softmax sums, the same arithmetic in every rank; one pass over the slice
+//   builds the 2048-bucket content histogram and the clamp correction of the
+//   entropy H = log Z - A / Z - Cc / Z (Cc: the reference's max(p, 1e-9)
+//   clamp); histograms and clamp terms merge through distributed shared
+//   memory and rank 0 publishes H.  Warp 0 polls the H of every head of the
+//   sequence; every CTA derives the same per-head counts (fixed-order sums,
+//   half-to-even rounding).  A head's selection is the forced sink/local
 //   blocks, every block of the buckets above the threshold bucket, and the
-//   exactly ranked (score desc, index asc) top members of that bucket.  An
-//   exact 4-pass radix select over order-preserving keys covers the rows the
-//   buckets cannot resolve.  The selection bitmap goes out as tagged words;
-//   the ascending block table and sel_lens follow.
+//   exactly ranked (score desc, index asc) top members of that bucket,
+//   gathered from every rank; an exact 4-pass radix select over
+//   order-preserving keys covers the rows the buckets cannot resolve.  Each
+//   rank writes its bitmap words and table segment, then a ready word.
 //
 // Phase C -- block-sparse split-KV flash decode (adakv/kernels/block_sparse_decode.py:51-100).
 //   The CTAs are split into B * Hkv contiguous groups, one per (sequence, KV
-//   head).  A CTA polls the g selection bitmaps of its group, ORs them into the
-//   union, takes its share of it and gathers those K/V blocks (16-byte
-//   cp.async, zero-filled past seq_len, XOR-swizzled tiles) for an m16n8k16
-//   tensor-core pass over the g query rows (each head masked by its own
-//   selection), then publishes its (m, l, o) partial.  The group's first CTA
-//   merges the partials in split order and writes out[b, h].
+//   head).  A CTA polls the ready words of its group's g heads, ORs their
+//   bitmaps into the union, takes its share of it and gathers those K/V blocks
+//   (16-byte cp.async, zero-filled past seq_len, XOR-swizzled tiles) for an
+//   m16n8k16 tensor-core pass over the g query rows (each head masked by its
+//   own selection), then publishes its (m, l, o) partial.  Every CTA of the
+//   group then merges all the group's partials, in split order, for its own
+//   share of the output columns.
 //
 // HBM traffic: the float32 centroid tables, the union of the selected K/V
-// blocks and the appended tokens; scores, bitmaps and partials stay in L2.
+// blocks and the appended tokens; scores, records, bitmaps and partials stay
+// in L2.
 //
 // Memory ordering across CTAs: the appended K/V tokens reach the attend phase
 // through the arrival counter (release after the cache writes, acquire by the
-// selection CTA) and fences around the bitmap words (selection CTA: fence
+// selection CTA) and fences around the ready words (selection CTA: fence
 // before publishing; attend CTA: fence after reading them).
 //
 // All CTAs must be resident at once (they wait on one another): the host
-// launches at most one CTA per SM, and every wait is bounded.
+// launches at most one CTA per SM, sized by the cluster occupancy, and every
+// wait is bounded.
 #include <cooperative_groups.h>
 
 #include "attend_mma.cuh"
