@@ -98,6 +98,12 @@ class AdaKVCacheLayer(CacheLayerMixin):
         if (B, Hkv, D) != (self._k.shape[0], self._k.shape[1], self._k.shape[3]):
             raise ValueError(f"key states {tuple(key_states.shape)} do not fit the cache "
                              f"{tuple(self._k.shape)}")
+        if value_states.shape != key_states.shape:
+            raise ValueError(f"value states {tuple(value_states.shape)} differ from the key "
+                             f"states {tuple(key_states.shape)}")
+        if key_states.dtype != self.dtype or value_states.dtype != self.dtype or \
+                key_states.device != self.device or value_states.device != self.device:
+            raise ValueError(f"key / value states must be {self.dtype} on {self.device}")
         S = self.n + n_new
         if S > self.max_cache_len:
             raise ValueError(f"AdaKVStaticCache holds {self.max_cache_len} tokens per layer; "

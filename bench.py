@@ -556,7 +556,7 @@ def run_cfg3(world, rank, device, seed, prefill="synthetic", warmup=3, overrides
                       bos_token_id=1, eos_token_id=2, pad_token_id=0)
     torch.manual_seed(seed + rank)
     with torch.device(device):
-        model = LlamaForCausalLM._from_config(cfg, torch_dtype=torch.bfloat16).eval()
+        model = LlamaForCausalLM._from_config(cfg, dtype=torch.bfloat16).eval()
     patch.patch_model(model, block_size=c["bs"], avg_budget=c["avg"])
     D, Hkv = c["hidden"] // c["heads"], c["kv"]
     cache = AdaKVStaticCache(cfg, max_cache_len=S + new + warmup, block_size=c["bs"])

@@ -70,3 +70,12 @@ def test_frozen_decode_table_matches_oracle():
         mask_to_block_table(torch.tensor([[True, False], [True, True]]))
     with pytest.raises(ValueError):
         frozen_decode_block_table(torch.from_numpy(fmask), nbp - 1, 1, 4)
+
+
+def test_cache_layer_rejects_mismatched_states():
+    layer = AdaKVCacheLayer(max_cache_len=16, block_size=16)
+    layer.update(torch.randn(1, 2, 3, 8), torch.randn(1, 2, 3, 8))
+    with pytest.raises(ValueError, match="float32"):
+        layer.update(torch.randn(1, 2, 1, 8, dtype=torch.float64), torch.randn(1, 2, 1, 8, dtype=torch.float64))
+    with pytest.raises(ValueError, match="differ"):
+        layer.update(torch.randn(1, 2, 1, 8), torch.randn(1, 2, 2, 8))
