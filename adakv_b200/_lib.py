@@ -80,6 +80,15 @@ _SIGNATURES = {
                                             ctypes.c_float, _vp, _vp, _vp, ctypes.c_size_t, _vp]),
     "adakv_combine": (ctypes.c_int, [ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                      ctypes.c_int32, _vp, _vp, _P(View), _vp]),
+    "adakv_shard_record_bytes": (ctypes.c_size_t, [_P(Geometry), _P(SelectParams)]),
+    "adakv_shard_prep": (ctypes.c_int, [_P(Geometry), _P(SelectParams), _vp, ctypes.c_int32,
+                                        ctypes.c_int32, ctypes.c_int32, _vp, _vp]),
+    "adakv_shard_clamp": (ctypes.c_int, [_P(Geometry), _P(SelectParams), _vp, ctypes.c_int32,
+                                         ctypes.c_int32, ctypes.c_int32, _vp, ctypes.c_size_t,
+                                         ctypes.c_int32, _vp, _vp]),
+    "adakv_shard_finish": (ctypes.c_int, [_P(Geometry), _P(SelectParams), _vp, ctypes.c_size_t,
+                                          _vp, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                          ctypes.c_int32, _vp, ctypes.c_int32, _vp, _vp, _vp]),
     "adakv_minmax_build": (ctypes.c_int, [_P(Geometry), _P(View), _vp, _vp, _vp, _vp]),
     "adakv_minmax_refresh": (ctypes.c_int, [_P(Geometry), _P(View), ctypes.c_int32, _vp, _vp, _vp,
                                             _vp]),

@@ -89,6 +89,7 @@ int device_state(DeviceState** out) {
     CUDA_TRY(plan_kernels_init());
     CUDA_TRY(attend_kernels_init());
     CUDA_TRY(step_kernels_init());
+    CUDA_TRY(shard_kernels_init());
     s.step_ok = s.num_sms >= 1;
     s.ready = true;
   }
@@ -1178,6 +1179,174 @@ int adakv_combine(int32_t n_parts, int32_t batch, int32_t n_q_heads, int32_t hea
   LaunchOpts oc;
   oc.pdl = pdl_enabled();
   CUDA_TRY(launch_combine(cp, dtype, static_cast<cudaStream_t>(stream), oc));
+  return ADAKV_OK;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Sequence-sharded selection from exchanged statistics: no score rows cross
+// between ranks, only per-head statistics, candidate lists and clamp terms.
+// ---------------------------------------------------------------------------
+namespace {
+
+struct ShardGeo {
+  int nb, cap, cap_pad, table_width;
+  SelectCfg cfg;
+  size_t record_bytes;
+};
+
+int shard_geo(const adakv_geometry* geo, const adakv_select_params* sp, ShardGeo* g) {
+  int rc;
+  if ((rc = check_geometry(geo))) return rc;
+  if ((rc = check_params(sp))) return rc;
+  if (geo->batch != 1)
+    return fail(ADAKV_ERR_INVALID, "the sharded selection takes one sequence (batch %d)", geo->batch);
+  if (sp->policy == ADAKV_POLICY_NUCLEUS)
+    return fail(ADAKV_ERR_UNSUPPORTED,
+                "the nucleus policy ranks the whole row's mass: exchange the rows (adakv_select)");
+  g->cfg = to_cfg(sp);
+  g->nb = ceil_div(geo->max_seq_len, geo->block_size);
+  g->table_width = table_width_for(geo->nb_cap, g->cfg);
+  const SeqBudget sb = seq_budget(g->nb, g->cfg);
+  const int kmax = std::min(std::min(std::max(sb.hi, sb.floor_sel), g->nb), g->table_width);
+  const int n_forced = (sb.sink + sb.local >= g->nb) ? g->nb : sb.sink + sb.local;
+  g->cap = std::max(0, kmax - n_forced);
+  if (g->cap > kShardListCap)
+    return fail(ADAKV_ERR_UNSUPPORTED, "%d candidates per head exceed the sharded selection's %d",
+                g->cap, kShardListCap);
+  if (align_up((size_t)geo->n_q_heads * sizeof(double), 16) + kShardFinishStage > kShardFinishSmemMax)
+    return fail(ADAKV_ERR_UNSUPPORTED, "n_q_heads %d too large for the sharded selection",
+                geo->n_q_heads);
+  g->cap_pad = (g->cap + 1) / 2 * 2;
+  g->record_bytes = (size_t)geo->n_q_heads * (kShardStatD * sizeof(double) +
+                                              (size_t)g->cap_pad * sizeof(unsigned long long));
+  return ADAKV_OK;
+}
+
+int shard_range_ok(const ShardGeo& g, const float* scores, int32_t score_stride, int32_t block_lo,
+                   int32_t n_local) {
+  if (block_lo < 0 || n_local < 0 || (int64_t)block_lo + n_local > g.nb)
+    return fail(ADAKV_ERR_INVALID, "shard [%d, %d + %d) outside the sequence's %d blocks", block_lo,
+                block_lo, n_local, g.nb);
+  if (n_local > 0 && (!scores || score_stride < n_local))
+    return fail(ADAKV_ERR_INVALID, "scores is NULL or score_stride %d < n_local %d", score_stride,
+                n_local);
+  return ADAKV_OK;
+}
+
+int shard_records_ok(const ShardGeo& g, const void* records, size_t record_stride, int32_t world) {
+  if (world < 1 || world > kShardMaxWorld)
+    return fail(ADAKV_ERR_INVALID, "world %d outside [1, %d]", world, kShardMaxWorld);
+  if (!records || reinterpret_cast<uintptr_t>(records) % 16 || record_stride % 16 ||
+      record_stride < g.record_bytes)
+    return fail(ADAKV_ERR_INVALID,
+                "records must be 16-byte aligned, record_stride a multiple of 16 and >= %zu",
+                g.record_bytes);
+  return ADAKV_OK;
+}
+
+ShardSelParams shard_params(const adakv_geometry* geo, const ShardGeo& g, const float* scores,
+                            int32_t score_stride, int32_t block_lo, int32_t n_local) {
+  ShardSelParams p{};
+  p.scores = scores;
+  p.score_stride = score_stride;
+  p.n_local = n_local;
+  p.block_lo = block_lo;
+  p.nb = g.nb;
+  p.Hq = geo->n_q_heads;
+  p.cfg = g.cfg;
+  p.cap = g.cap;
+  p.cap_pad = g.cap_pad;
+  p.table_width = g.table_width;
+  p.world = 1;
+  return p;
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t adakv_shard_record_bytes(const adakv_geometry* geo, const adakv_select_params* sp) {
+  ShardGeo g;
+  if (!geo || !sp || shard_geo(geo, sp, &g) != ADAKV_OK) return 0;
+  return g.record_bytes;
+}
+
+int adakv_shard_prep(const adakv_geometry* geo, const adakv_select_params* sp, const float* scores,
+                     int32_t score_stride, int32_t block_lo, int32_t n_local, void* record,
+                     void* stream) {
+  int rc;
+  ShardGeo g;
+  if ((rc = shard_geo(geo, sp, &g))) return rc;
+  if ((rc = shard_range_ok(g, scores, score_stride, block_lo, n_local))) return rc;
+  if (!record || reinterpret_cast<uintptr_t>(record) % 16)
+    return fail(ADAKV_ERR_INVALID, "record must be a 16-byte aligned device pointer");
+  DeviceState* ds = nullptr;
+  if ((rc = device_state(&ds))) return rc;
+  ShardSelParams p = shard_params(geo, g, scores, score_stride, block_lo, n_local);
+  p.xmine = static_cast<unsigned char*>(record);
+  LaunchOpts o;
+  o.pdl = pdl_enabled();
+  CUDA_TRY(launch_shard_select(0, p, static_cast<cudaStream_t>(stream), o));
+  return ADAKV_OK;
+}
+
+int adakv_shard_clamp(const adakv_geometry* geo, const adakv_select_params* sp, const float* scores,
+                      int32_t score_stride, int32_t block_lo, int32_t n_local, const void* records,
+                      size_t record_stride, int32_t world, double* cc, void* stream) {
+  int rc;
+  ShardGeo g;
+  if ((rc = shard_geo(geo, sp, &g))) return rc;
+  if ((rc = shard_range_ok(g, scores, score_stride, block_lo, n_local))) return rc;
+  if ((rc = shard_records_ok(g, records, record_stride, world))) return rc;
+  if (!cc) return fail(ADAKV_ERR_INVALID, "cc is NULL");
+  DeviceState* ds = nullptr;
+  if ((rc = device_state(&ds))) return rc;
+  ShardSelParams p = shard_params(geo, g, scores, score_stride, block_lo, n_local);
+  p.xall = static_cast<const unsigned char*>(records);
+  p.xstride = record_stride;
+  p.world = world;
+  p.cc_mine = cc;
+  LaunchOpts o;
+  o.pdl = pdl_enabled();
+  CUDA_TRY(launch_shard_select(1, p, static_cast<cudaStream_t>(stream), o));
+  return ADAKV_OK;
+}
+
+int adakv_shard_finish(const adakv_geometry* geo, const adakv_select_params* sp,
+                       const void* records, size_t record_stride, const double* cc_all,
+                       int32_t world, int32_t rank, int32_t block_lo, int32_t n_local,
+                       int32_t* block_table, int32_t table_width, int32_t* sel_lens,
+                       uint32_t* status, void* stream) {
+  int rc;
+  ShardGeo g;
+  if ((rc = shard_geo(geo, sp, &g))) return rc;
+  if (block_lo < 0 || n_local < 0 || (int64_t)block_lo + n_local > g.nb)
+    return fail(ADAKV_ERR_INVALID, "shard [%d, %d + %d) outside the sequence's %d blocks", block_lo,
+                block_lo, n_local, g.nb);
+  if ((rc = shard_records_ok(g, records, record_stride, world))) return rc;
+  if (rank < 0 || rank >= world) return fail(ADAKV_ERR_INVALID, "rank %d outside [0, %d)", rank, world);
+  if (sp->policy == ADAKV_POLICY_ADAPTIVE && !cc_all)
+    return fail(ADAKV_ERR_INVALID, "the adaptive policy needs every shard's clamp terms (cc_all)");
+  if (!block_table || !sel_lens) return fail(ADAKV_ERR_INVALID, "block_table / sel_lens are NULL");
+  if (table_width < g.table_width)
+    return fail(ADAKV_ERR_INVALID, "table_width %d < required %d", table_width, g.table_width);
+  DeviceState* ds = nullptr;
+  if ((rc = device_state(&ds))) return rc;
+  ShardSelParams p = shard_params(geo, g, nullptr, 0, block_lo, n_local);
+  p.xall = static_cast<const unsigned char*>(records);
+  p.xstride = record_stride;
+  p.world = world;
+  p.rank = rank;
+  p.cc_all = cc_all;
+  p.block_table = block_table;
+  p.out_width = table_width;
+  p.sel_lens = sel_lens;
+  p.status = status;
+  LaunchOpts o;
+  o.pdl = pdl_enabled();
+  CUDA_TRY(launch_shard_select(2, p, static_cast<cudaStream_t>(stream), o));
   return ADAKV_OK;
 }
 

@@ -237,6 +237,45 @@ struct TableParams {        // block table -> per-head bitmaps (stand-alone atte
 };
 
 // ---------------------------------------------------------------------------
+// sequence-sharded selection from exchanged statistics (shard_select.cu)
+// ---------------------------------------------------------------------------
+constexpr int kShardThreads = 1024;
+constexpr int kShardListCap = 4096;     // candidates one shard keeps per head at most
+constexpr int kShardStageCap = 32768;   // score-row floats staged in shared memory
+constexpr int kShardSortBuckets = 2048; // counting-sort buckets of the candidate keys
+constexpr int kShardStatD = 8;          // doubles of one head's statistics record
+constexpr int kShardFinishThreads = 512;
+constexpr int kShardFinishStage = 160 * 1024;       // candidate lists staged in shared memory up to
+constexpr size_t kShardFinishSmemMax = 200 * 1024;  // opt-in dynamic shared memory of a finish CTA
+constexpr int kShardMaxWorld = 64;
+
+// One rank's exchange record: Hq statistics records of kShardStatD doubles
+// (max score, content max, content sum, content sum of squares, max z,
+// Z = sum e^(z - max z), A = sum e^(z - max z) (z - max z), candidates kept),
+// then Hq candidate lists of cap_pad 64-bit keys (order key of the score << 32
+// | ~global block id), sorted descending.
+struct ShardSelParams {
+  const float* scores;        // [Hq, score_stride] this shard's score rows
+  int score_stride;
+  int n_local, block_lo;      // blocks of this shard and its first global block
+  int nb;                     // blocks of the whole sequence
+  int Hq;
+  SelectCfg cfg;
+  int cap, cap_pad;           // candidates per head at most, list stride
+  size_t xstride;             // bytes between ranks' exchange records in xall
+  int world, rank;
+  unsigned char* xmine;       // this rank's exchange record (prep writes it)
+  const unsigned char* xall;  // [world] exchange records in rank order
+  double* cc_mine;            // [Hq] this shard's clamp term (clamp writes it)
+  const double* cc_all;       // [world, Hq] every shard's clamp term (NULL: none)
+  int table_width;            // the whole sequence's per-head count cap
+  int* block_table;           // [Hq, out_width] this rank's selected global block ids
+  int out_width;
+  int* sel_lens;              // [Hq]
+  uint32_t* status;
+};
+
+// ---------------------------------------------------------------------------
 // launch helper: cudaLaunchKernelEx with optional PDL / cooperative / cluster
 // ---------------------------------------------------------------------------
 struct LaunchOpts {
@@ -296,6 +335,11 @@ cudaError_t launch_minmax_score(const MinmaxParams& p, int dtype, int D, int nb_
 cudaError_t launch_combine(const CombineParams& p, int dtype, cudaStream_t stream, const LaunchOpts& o);
 cudaError_t launch_importance(const ImportanceParams& p, int dtype, int D, cudaStream_t stream);
 cudaError_t launch_stage(const void* src, void* dst, size_t bytes, cudaStream_t stream);
+// sharded selection: stage 0 = statistics + candidates, 1 = clamp term, 2 = budgets + table
+cudaError_t launch_shard_select(int stage, const ShardSelParams& p, cudaStream_t stream,
+                                const LaunchOpts& o);
+size_t shard_finish_smem(int Hq, int world, int cap_pad);
+cudaError_t shard_kernels_init();
 cudaError_t launch_step(const StepParams& p, int dtype, int D, int g, int grid, size_t smem,
                         cudaStream_t stream, const LaunchOpts& o);
 cudaError_t launch_step_scores(bool fused, const float* fscores,

@@ -6,16 +6,18 @@ into contiguous block ranges, one per rank, and each decode step runs as
 
 1. every rank scores the blocks it holds (``adakv_estimate``: q . centroid,
    GQA folded, the scoring of ``adakv/estimator.py:62-74``);
-2. the ranks all-gather the per-shard score rows (NCCL over NVLink) and
-   concatenate them in block order;
-3. every rank runs the entropy budget and top-k over the full rows
-   (``adakv_select``: ``adakv/budget.py:45-86``, ``adakv/selector.py:18-60``).
-   Identical inputs and arithmetic give identical block tables on every rank,
-   so the selection equals the single-GPU one;
-4. every rank attends over the selected blocks it holds
+2. the selection (entropy budget and top-k over each head's whole row,
+   ``adakv/budget.py:45-86``, ``adakv/selector.py:18-60``), by default from
+   exchanged statistics (``StatsSelector``): each rank all-gathers per-head
+   softmax statistics plus its shard's sorted top content candidates, then
+   one clamp term per head, and every rank derives the same budgets and keeps
+   the selected blocks it holds.  No score row leaves its rank.  The nucleus
+   policy, which ranks the whole row's probability mass, instead all-gathers
+   the score rows and selects on them (``Selector``, ``selection="rows"``);
+3. every rank attends over the selected blocks it holds
    (``adakv_attend_partial``) and returns its normalised output and
    log-sum-exp per query head;
-5. the ranks all-gather those partials and merge them by log-sum-exp
+4. the ranks all-gather those partials and merge them by log-sum-exp
    (``adakv_combine``).
 
 Shard ``r`` holds blocks ``[r * L, (r + 1) * L)`` with ``L`` a multiple of 32
@@ -23,8 +25,8 @@ blocks (whole selection-bitmap words); the last rank holds the tail, so the
 sink blocks live on rank 0 and the local window on the last rank.
 
 Collectives go through a small interface: ``TorchGroup`` (``torch.distributed``,
-one process per GPU) or ``emulate_step`` (all shards in one process, for
-tests on one device).
+one process per GPU) or the ``emulate_*`` functions (all shards in one
+process, for tests on one device).
 """
 from __future__ import annotations
 
@@ -156,6 +158,81 @@ class Selector:
         return self.table, self.sel_lens
 
 
+class StatsSelector:
+    """One rank's part of the selection from exchanged statistics
+    (``adakv_shard_prep`` / ``adakv_shard_clamp`` / ``adakv_shard_finish``).
+
+    ``prep`` writes this rank's record (per head: softmax statistics and the
+    shard's top content candidates, sorted); once every rank's records are
+    gathered, ``clamp`` gives this shard's clamp terms of the entropy
+    (adaptive policy); once those are gathered too, ``finish`` writes this
+    rank's block table: the selected blocks it holds, as global ids."""
+
+    def __init__(self, S_total, n_q_heads, n_kv_heads, head_dim, block_size, dtype, device,
+                 block_lo, n_local, avg_budget=64, k_min=2, k_max=64, n_sink_blocks=1,
+                 n_local_blocks=4, c_min=1, temperature=1.0, budget_policy="adaptive",
+                 nucleus_p=0.9):
+        self.nb = -(-S_total // block_size)
+        if block_lo < 0 or n_local < 0 or block_lo + n_local > self.nb:
+            raise ValueError("the shard's blocks must lie inside the sequence")
+        self.geo = _lib.geometry(1, n_q_heads, n_kv_heads, head_dim, block_size, S_total, self.nb,
+                                 _lib.TORCH_DTYPES[dtype])
+        self.params = _lib.select_params(avg_budget, k_min, k_max, n_sink_blocks, n_local_blocks,
+                                         c_min, temperature, budget_policy, nucleus_p)
+        L = _lib.lib()
+        self.record_bytes = L.adakv_shard_record_bytes(self.geo, self.params)
+        if self.record_bytes == 0:
+            raise ValueError("the statistics exchange does not apply here (batch 1 and the fixed "
+                             "or adaptive policy only): "
+                             + L.adakv_last_error().decode(errors="replace"))
+        self.width = L.adakv_plan_table_width(self.geo, self.params)
+        self.adaptive = budget_policy == "adaptive"
+        self.block_lo, self.n_local, self.Hq = block_lo, n_local, n_q_heads
+        self.record = torch.zeros((self.record_bytes,), dtype=torch.uint8, device=device)
+        self.cc = torch.zeros((n_q_heads,), dtype=torch.float64, device=device)
+        self.table = torch.zeros((n_q_heads, self.width), dtype=torch.int32, device=device)
+        self.sel_lens = torch.zeros((n_q_heads,), dtype=torch.int32, device=device)
+        self.status = torch.zeros((4,), dtype=torch.int32, device=device)
+
+    @staticmethod
+    def applies(budget_policy="adaptive", batch=1):
+        return batch == 1 and budget_policy in ("fixed", "adaptive")
+
+    def prep(self, scores):
+        """``scores``: this shard's rows ``[Hq, >= n_local]`` fp32 -> the record (uint8)."""
+        with torch.cuda.device(self.record.device):
+            _lib.check(_lib.lib().adakv_shard_prep(
+                self.geo, self.params, scores.data_ptr(), scores.stride(0), self.block_lo,
+                self.n_local, self.record.data_ptr(), _lib.stream_ptr(self.record.device)))
+        return self.record
+
+    def clamp(self, scores, records):
+        """``records``: ``[world, record_bytes]`` uint8 in rank order -> ``cc [Hq]`` fp64."""
+        records = records.contiguous()
+        with torch.cuda.device(self.record.device):
+            _lib.check(_lib.lib().adakv_shard_clamp(
+                self.geo, self.params, scores.data_ptr(), scores.stride(0), self.block_lo,
+                self.n_local, records.data_ptr(), records.stride(0), records.shape[0],
+                self.cc.data_ptr(), _lib.stream_ptr(self.record.device)))
+        return self.cc
+
+    def finish(self, records, ccs, rank):
+        """Every rank's records and clamp terms (``[world, Hq]`` fp64, or None
+        for the fixed policy) -> this rank's ``(table, sel_lens)``."""
+        records = records.contiguous()
+        cc_ptr = None
+        if ccs is not None:
+            ccs = ccs.contiguous()
+            cc_ptr = ccs.data_ptr()
+        with torch.cuda.device(self.record.device):
+            _lib.check(_lib.lib().adakv_shard_finish(
+                self.geo, self.params, records.data_ptr(), records.stride(0), cc_ptr,
+                records.shape[0], rank, self.block_lo, self.n_local, self.table.data_ptr(),
+                self.width, self.sel_lens.data_ptr(), self.status.data_ptr(),
+                _lib.stream_ptr(self.record.device)))
+        return self.table, self.sel_lens
+
+
 def combine(parts, lse, dtype, out=None):
     """Log-sum-exp merge: ``parts [N, Hq, D]`` fp32, ``lse [N, Hq]`` -> ``[Hq, D]``."""
     N, Hq, D = parts.shape
@@ -192,6 +269,30 @@ def emulate_step(shards, selector, q, sm_scale=None):
     return combine(o, lse, q.dtype), table, sel_lens
 
 
+def emulate_step_stats(shards, selectors, q, sm_scale=None):
+    """One decode step over all shards in one process with the statistics
+    exchange (``selectors[r]``: shard r's ``StatsSelector``).  Returns the
+    output and each rank's ``(table, sel_lens)``."""
+    Hq, D = q.shape
+    L = shards[0].cap
+    world = len(shards)
+    scores = torch.zeros((world, Hq, L), dtype=torch.float32, device=q.device)
+    recs = []
+    for r, (sh, st) in enumerate(zip(shards, selectors)):
+        sh.local_scores(q, scores[r])
+        recs.append(st.prep(scores[r]).clone())
+    records = torch.stack(recs)
+    ccs = None
+    if selectors[0].adaptive:
+        ccs = torch.stack([st.clamp(scores[r], records).clone() for r, st in enumerate(selectors)])
+    picks = [tuple(t.clone() for t in st.finish(records, ccs, r)) for r, st in enumerate(selectors)]
+    scale = 1.0 / math.sqrt(D) if sm_scale is None else float(sm_scale)
+    parts = [sh.attend_partial(q, t, n, scale) for sh, (t, n) in zip(shards, picks)]
+    o = torch.stack([p[0] for p in parts])
+    lse = torch.stack([p[1] for p in parts])
+    return combine(o, lse, q.dtype), picks
+
+
 class TorchGroup:
     """All-gather over a ``torch.distributed`` process group (NCCL for CUDA tensors)."""
 
@@ -212,9 +313,13 @@ class ShardedDecoder:
     """This rank's part of a sequence-sharded decode step.
 
     ``K_local``/``V_local``: ``[Hkv, S_local, D]``, the tokens of this rank's
-    block range ``shard_range(ceil(S_total / bs), world, rank)``."""
+    block range ``shard_range(ceil(S_total / bs), world, rank)``.
+    ``selection``: ``"stats"`` (exchange statistics and candidates; fixed and
+    adaptive policies), ``"rows"`` (all-gather the score rows; any policy) or
+    ``"auto"`` (stats where it applies)."""
 
-    def __init__(self, K_local, V_local, S_total, n_q_heads, block_size, comm, **select_kw):
+    def __init__(self, K_local, V_local, S_total, n_q_heads, block_size, comm, selection="auto",
+                 **select_kw):
         self.comm = comm
         self.nb = -(-S_total // block_size)
         self.L = shard_blocks(self.nb, comm.world)
@@ -223,17 +328,34 @@ class ShardedDecoder:
             raise ValueError("local K/V do not cover this rank's block range")
         self.shard = ShardCache(K_local, V_local, lo, n_q_heads, block_size, capacity_blocks=self.L)
         Hkv, _, D = K_local.shape
-        self.selector = Selector(S_total, n_q_heads, Hkv, D, block_size, K_local.dtype,
-                                 K_local.device, **select_kw)
+        policy = select_kw.get("budget_policy", "adaptive")
+        if selection not in ("auto", "stats", "rows"):
+            raise ValueError(f"unknown selection exchange {selection!r}")
+        use_stats = selection == "stats" or (selection == "auto" and StatsSelector.applies(policy))
+        self.stats_sel = self.selector = None
+        if use_stats:
+            self.stats_sel = StatsSelector(S_total, n_q_heads, Hkv, D, block_size, K_local.dtype,
+                                           K_local.device, lo, n, **select_kw)
+        else:
+            self.selector = Selector(S_total, n_q_heads, Hkv, D, block_size, K_local.dtype,
+                                     K_local.device, **select_kw)
         self.scores = torch.zeros((n_q_heads, self.L), dtype=torch.float32, device=K_local.device)
+
+    def select(self):
+        """This rank's ``(block table, sel_lens)`` from the current scores."""
+        if self.stats_sel is not None:
+            s = self.stats_sel
+            recs = self.comm.all_gather(s.prep(self.scores))          # [world, record_bytes]
+            ccs = self.comm.all_gather(s.clamp(self.scores, recs)) if s.adaptive else None
+            return s.finish(recs, ccs, self.comm.rank)
+        gathered = self.comm.all_gather(self.scores)                  # [world, Hq, L]
+        return self.selector.select(_concat_scores(gathered, self.nb, self.L))
 
     def step(self, q, sm_scale=None):
         """``q [Hq, D]`` (identical on every rank) -> ``out [Hq, D]`` on every rank."""
         Hq, D = q.shape
         self.shard.local_scores(q, self.scores)
-        gathered = self.comm.all_gather(self.scores)                  # [world, Hq, L]
-        scores = _concat_scores(gathered, self.nb, self.L)
-        table, sel_lens = self.selector.select(scores)
+        table, sel_lens = self.select()
         scale = 1.0 / math.sqrt(D) if sm_scale is None else float(sm_scale)
         packed = torch.empty(Hq * D + Hq, dtype=torch.float32, device=q.device)
         self.shard.attend_partial(q, table, sel_lens, scale, packed=packed)

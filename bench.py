@@ -404,8 +404,11 @@ CFG4 = dict(Hq=64, Hkv=8, D=128, bs=16, S=1 << 20, avg=256, k_min=2, k_max=1024)
 
 
 def run_cfg4(steps, warmup, world, rank, device):
-    """Eager decode steps of the sharded path (single-GPU step at N=1); returns
-    (us per step on this rank, algorithmic bytes per step of the whole job)."""
+    """Decode steps of the sharded path (single-GPU step at N=1), each captured
+    in a CUDA graph and replayed.  Returns {exchange: (us per step on this
+    rank, algorithmic bytes per step of the whole job)}: at N=1 {"single": ...};
+    at N>1 the selection from exchanged statistics ("stats", the default) and
+    the all-gather of the score rows ("rows") on the same shards."""
     import torch
     from adakv_b200.batch import BatchedDecoder
     from adakv_b200.sharded import ShardedDecoder, TorchGroup, shard_range
@@ -427,43 +430,53 @@ def run_cfg4(steps, warmup, world, rank, device):
     if world == 1:
         dec = BatchedDecoder(1, Hq, Hkv, D, bs, S, torch.bfloat16, device, **kw)
         dec.load(Kl[None], Vl[None], [S])
-        step = lambda: dec.step(q[None])
-        sets = lambda: dec.selected_sets()
+        variants = {"single": (lambda: dec.step(q[None]), lambda: dec.selected_sets())}
     else:
-        dec = ShardedDecoder(Kl, Vl, S, Hq, bs, TorchGroup(), **kw)
-        step = lambda: dec.step(q)
-        sets = lambda: [dec.selector.table[h, : int(dec.selector.sel_lens[h])].cpu().numpy()
-                        for h in range(Hq)]
-    for _ in range(max(3, warmup)):
-        step()
-    torch.cuda.synchronize(device)
-    union = 0
-    ss = sets()
-    g_ = Hq // Hkv
-    for kv in range(Hkv):
-        union += len(set().union(*[set(x.tolist()) for x in ss[kv * g_:(kv + 1) * g_]]))
-    nbytes = Hkv * nb * D * 4 + union * bs * D * 2 * 2
-    # one step (NCCL collectives included) captured in a CUDA graph: the timed
-    # replays measure device time, not Python launch overhead
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
-        step()
-    for _ in range(3):
-        graph.replay()
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if world > 1:
-        import torch.distributed as dist
-        dist.barrier()
-    torch.cuda.synchronize(device)
-    a.record()
-    for _ in range(steps):
-        graph.replay()
-    b.record()
-    torch.cuda.synchronize(device)
-    us = a.elapsed_time(b) * 1000.0 / steps
-    del graph  # a graph holding NCCL calls must go before the process group
-    torch.cuda.synchronize(device)
-    return us, nbytes
+        variants = {}
+        for ex in ("stats", "rows"):
+            d = ShardedDecoder(Kl, Vl, S, Hq, bs, TorchGroup(), selection=ex, **kw)
+
+            def sets(d=d):
+                sel = d.stats_sel if d.stats_sel is not None else d.selector
+                return [sel.table[h, : int(sel.sel_lens[h])].cpu().numpy() for h in range(Hq)]
+            variants[ex] = ((lambda d=d: d.step(q)), sets)
+    out = {}
+    for ex, (step, sets) in variants.items():
+        for _ in range(max(3, warmup)):
+            step()
+        torch.cuda.synchronize(device)
+        union = 0
+        ss = sets()
+        g_ = Hq // Hkv
+        for kv in range(Hkv):
+            union += len(set().union(*[set(x.tolist()) for x in ss[kv * g_:(kv + 1) * g_]]))
+        if ex == "stats":  # each rank holds its own picks: the job's union is their sum
+            import torch.distributed as dist
+            t = torch.tensor([union], device=device, dtype=torch.int64)
+            dist.all_reduce(t)
+            union = int(t.item())
+        nbytes = Hkv * nb * D * 4 + union * bs * D * 2 * 2
+        # one step (NCCL collectives included) captured in a CUDA graph: the
+        # timed replays measure device time, not Python launch overhead
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step()
+        for _ in range(3):
+            graph.replay()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+        torch.cuda.synchronize(device)
+        a.record()
+        for _ in range(steps):
+            graph.replay()
+        b.record()
+        torch.cuda.synchronize(device)
+        out[ex] = (a.elapsed_time(b) * 1000.0 / steps, nbytes)
+        del graph  # a graph holding NCCL calls must go before the process group
+        torch.cuda.synchronize(device)
+    return out
 
 
 # ---------------------------------------------------------------------------
@@ -643,10 +656,16 @@ def run_partitioned(steps, warmup, world, rank, device, seed):
     for name in ("cfg2", "cfg4"):
         n = min(steps, 200)
         torch.cuda.synchronize(device)
+        rows_us = None
         if name == "cfg2":
             us, nbytes = run_cfg2(n, warmup, world, rank, device, seed)
         else:
-            us, nbytes = run_cfg4(n, warmup, world, rank, device)
+            r4 = run_cfg4(n, warmup, world, rank, device)
+            us, nbytes = r4["single"] if world == 1 else r4["stats"]
+            if world > 1:
+                t = torch.tensor([r4["rows"][0]], device=device, dtype=torch.float64)
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                rows_us = float(t[0])
         if world > 1:
             t = torch.tensor([us, float(nbytes)], device=device, dtype=torch.float64)
             dist.all_reduce(t[:1], op=dist.ReduceOp.MAX)
@@ -657,11 +676,14 @@ def run_partitioned(steps, warmup, world, rank, device, seed):
         out[name] = {"us": us, "n": world, "achieved_gbs": achieved,
                      "frac": achieved / (peak * world), "bytes_per_step": nbytes, "steps": n,
                      "scaling": "strong"}
+        if rows_us is not None:
+            out[name]["us_row_exchange"] = rows_us
         torch.cuda.empty_cache()
     out["cfg2"]["workload"] = (f"ragged batch {CFG2['B']}, contexts U[{CFG2['lo']}, {CFG2['hi']}], "
                                f"avg_budget {CFG2['avg']}, split by sequence, no collective")
     out["cfg4"]["workload"] = (f"one {CFG4['S']}-token sequence, {CFG4['Hq']} q / {CFG4['Hkv']} KV "
-                               f"heads, avg_budget {CFG4['avg']}, sequence-sharded")
+                               f"heads, avg_budget {CFG4['avg']}, sequence-sharded (selection from "
+                               f"exchanged statistics; us_row_exchange: score rows all-gathered)")
     return out
 
 
@@ -768,8 +790,14 @@ def main():
 
     if args.workload in ("cfg2", "cfg4"):
         steps = min(args.steps, 200)
+        rows_us = None
         if args.workload == "cfg4":
-            us, nbytes = run_cfg4(steps, args.warmup, world, rank, device)
+            r4 = run_cfg4(steps, args.warmup, world, rank, device)
+            us, nbytes = r4["single"] if world == 1 else r4["stats"]
+            if world > 1:
+                t = torch.tensor([r4["rows"][0]], device=device, dtype=torch.float64)
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                rows_us = float(t[0])
         else:
             us, nbytes = run_cfg2(steps, args.warmup, world, rank, device, args.seed)
         if world > 1:
@@ -818,13 +846,15 @@ def main():
                 "config": {"workload": f"cfg4 one {c['S']}-token sequence, {c['Hq']} q / {c['Hkv']} KV "
                                        f"heads, head_dim {c['D']}, block {c['bs']}, avg_budget "
                                        f"{c['avg']}, k_max {c['k_max']}, bf16",
-                           "parallelism": f"sequence-sharded x{world} (NCCL all-gather of scores "
-                                          "and of (o, lse) partials)" if world > 1 else "single GPU",
+                           "parallelism": f"sequence-sharded x{world} (NCCL all-gathers of per-head "
+                                          "statistics + shard candidates, of clamp terms and of "
+                                          "(o, lse) partials)" if world > 1 else "single GPU",
                            "timing": "CUDA events around CUDA-graph replays of one step "
                                      "(collectives included), max over ranks"},
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                              "frac": achieved / peak, "traffic": None,
                              "scope": "fp32 centroid table + union of selected K/V blocks, all ranks"},
+                "us_row_exchange": rows_us,
             }), flush=True)
         if world > 1:
             dist.barrier()

@@ -374,6 +374,45 @@ int adakv_combine(int32_t n_parts, int32_t batch, int32_t n_q_heads, int32_t hea
                   int32_t dtype, const float* parts, const float* lse, const adakv_view* out,
                   void* stream);
 
+/* ---- sequence-sharded selection from exchanged statistics ----
+ * Replaces the score-row all-gather + adakv_select above for the fixed and
+ * adaptive policies (adakv/budget.py:45-86, adakv/selector.py:18-60 over the
+ * whole row), exchanging per head only softmax statistics, a sorted list of
+ * the shard's top content candidates and one clamp term:
+ *   1. adakv_shard_prep     this shard's record (statistics + candidates);
+ *   2. all-gather the records (rank order);
+ *   3. adakv_shard_clamp    this shard's clamp terms (adaptive policy only);
+ *   4. all-gather the clamp terms (float64 [world][Hq]);
+ *   5. adakv_shard_finish   every head's budget and this rank's table rows:
+ *      the global ids of the selected blocks this shard holds.
+ * The union of the ranks' rows is the head's selection; every rank derives
+ * the same budgets.  `geo` describes the whole sequence (batch 1, no
+ * seq_lens: max_seq_len tokens); shard blocks are [block_lo,
+ * block_lo + n_local) and `scores` this shard's rows [Hq][score_stride]
+ * (adakv_estimate's layout).  Collectives are the caller's. */
+
+/* Bytes of one rank's record; 0 when the path does not apply (batch != 1,
+ * nucleus policy, more than 4096 candidates per head). */
+size_t adakv_shard_record_bytes(const adakv_geometry* geo, const adakv_select_params* sp);
+
+int adakv_shard_prep(const adakv_geometry* geo, const adakv_select_params* sp, const float* scores,
+                     int32_t score_stride, int32_t block_lo, int32_t n_local, void* record,
+                     void* stream);
+
+/* cc[Hq] float64; `records`: world records, record_stride bytes apart. */
+int adakv_shard_clamp(const adakv_geometry* geo, const adakv_select_params* sp, const float* scores,
+                      int32_t score_stride, int32_t block_lo, int32_t n_local, const void* records,
+                      size_t record_stride, int32_t world, double* cc, void* stream);
+
+/* block_table [Hq][table_width] (table_width >= adakv_plan_table_width),
+ * sel_lens [Hq]; cc_all may be NULL for the fixed policy; status: optional
+ * device word for ADAKV_ST_* bits. */
+int adakv_shard_finish(const adakv_geometry* geo, const adakv_select_params* sp,
+                       const void* records, size_t record_stride, const double* cc_all,
+                       int32_t world, int32_t rank, int32_t block_lo, int32_t n_local,
+                       int32_t* block_table, int32_t table_width, int32_t* sel_lens,
+                       uint32_t* status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -213,3 +213,38 @@ def test_noalloc_limit_counts_the_split_kv_partials(lib):
     assert rc == _lib.ERR_INVALID
     msg = lib.adakv_last_error().decode()
     assert str(need) in msg and "adakv_attend_workspace_bytes" in msg
+
+
+def test_shard_selection_sizes_and_validation(lib):
+    """The statistics-exchange selection: record size for the cfg4 shape,
+    0 where it does not apply, and host-side argument checks that return
+    before any CUDA call."""
+    geo = _lib.geometry(1, 64, 8, 128, 16, 1 << 20, 65536, _lib.DTYPE_BF16)
+    sp = _lib.select_params(256, 2, 1024, 1, 4, 1)
+    cap_pad = 1020  # 1024 - 5 forced blocks, rounded up to an even count
+    assert lib.adakv_shard_record_bytes(geo, sp) == 64 * (8 * 8 + cap_pad * 8)
+    nuc = _lib.select_params(256, 2, 1024, 1, 4, 1, 1.0, "adaptive_nucleus")
+    assert lib.adakv_shard_record_bytes(geo, nuc) == 0
+    assert b"nucleus" in lib.adakv_last_error()
+    geo2 = _lib.geometry(2, 64, 8, 128, 16, 1 << 20, 65536, _lib.DTYPE_BF16)
+    assert lib.adakv_shard_record_bytes(geo2, sp) == 0
+    wide = _lib.select_params(8000, 2, 8000, 1, 4, 1)
+    assert lib.adakv_shard_record_bytes(geo, wide) == 0
+    rec = ctypes.c_void_p(1 << 20)  # never dereferenced: validation fails first
+    # a shard outside the sequence
+    assert lib.adakv_shard_prep(geo, sp, rec, 40000, 40000, 40000, rec, None) == _lib.ERR_INVALID
+    # misaligned record
+    assert lib.adakv_shard_prep(geo, sp, rec, 32768, 0, 32768, 8, None) == _lib.ERR_INVALID
+    # world / record stride
+    assert lib.adakv_shard_clamp(geo, sp, rec, 32768, 0, 32768, rec, 1 << 20, 0, rec,
+                                 None) == _lib.ERR_INVALID
+    assert lib.adakv_shard_clamp(geo, sp, rec, 32768, 0, 32768, rec, 1000, 2, rec,
+                                 None) == _lib.ERR_INVALID
+    # rank outside the world
+    assert lib.adakv_shard_finish(geo, sp, rec, 1 << 20, rec, 2, 2, 0, 32768, rec, 1024, rec,
+                                  None, None) == _lib.ERR_INVALID
+    # the adaptive policy needs the clamp terms; the table must be wide enough
+    assert lib.adakv_shard_finish(geo, sp, rec, 1 << 20, None, 2, 0, 0, 32768, rec, 1024, rec,
+                                  None, None) == _lib.ERR_INVALID
+    assert lib.adakv_shard_finish(geo, sp, rec, 1 << 20, rec, 2, 0, 0, 32768, rec, 1000, rec,
+                                  None, None) == _lib.ERR_INVALID

@@ -1,6 +1,7 @@
 """Sequence-sharded decode over NCCL: one process per GPU (2-4 GPUs when the
-box has them, skipped otherwise).  Every rank must return the output the
-single-GPU step computes on rank 0's device."""
+box has them, skipped otherwise), with the selection from exchanged
+statistics and with the score-row all-gather.  Every rank must return the
+output the single-GPU step computes on rank 0's device."""
 import os
 import socket
 
@@ -29,7 +30,7 @@ def _inputs(dev):
     return q, K, V
 
 
-def _rank(rank, world, port, results):
+def _rank(rank, world, port, results, selection):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     from datetime import timedelta
     import torch.distributed as dist
@@ -44,7 +45,7 @@ def _rank(rank, world, port, results):
         lo, n = shard_range(nb, world, rank)
         t0, t1 = lo * BS, min(S, (lo + n) * BS)
         dec = ShardedDecoder(K[:, t0:t1].contiguous(), V[:, t0:t1].contiguous(), S, Hq, BS,
-                             TorchGroup(), **KW)
+                             TorchGroup(), selection=selection, **KW)
         del K, V
         out = dec.step(q)
         out2 = dec.step(q)  # a second step reuses every buffer
@@ -65,14 +66,16 @@ def _rank(rank, world, port, results):
         dist.destroy_process_group()
 
 
-def test_sharded_decode_over_nccl():
+@pytest.mark.parametrize("selection", ["stats", "rows"])
+def test_sharded_decode_over_nccl(selection):
     if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
         pytest.skip("needs 2 or more GPUs")
     world = min(4, torch.cuda.device_count())
     ctx = mp.get_context("spawn")
     results = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank, args=(r, world, port, results)) for r in range(world)]
+    procs = [ctx.Process(target=_rank, args=(r, world, port, results, selection))
+             for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
