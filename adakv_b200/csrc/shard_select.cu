@@ -66,45 +66,38 @@ __device__ __forceinline__ const unsigned long long* cands_of(const ShardSelPara
          (size_t)h * p.cap_pad;
 }
 
-// Merged max score, max z, Z and A of head hh over every rank's record,
-// computed by one warp (lane l reads ranks l and l + 32): the same inputs
-// give the same result wherever it runs, so every rank agrees.
-__device__ __forceinline__ void merge_head_warp(const ShardSelParams& p, int hh, float& mx, float& M,
-                                                double& Z, double& A) {
-  const int lane = threadIdx.x & 31;
-  float mxl = -INFINITY, Mr[2];
-  double zr[2], ar[2];
-#pragma unroll
-  for (int k = 0; k < 2; ++k) {
-    const int r = lane + 32 * k;
-    Mr[k] = -INFINITY;
-    zr[k] = ar[k] = 0.0;
-    if (r < p.world) {
-      const double* st = stats_of(p, r, hh);
-      mxl = fmaxf(mxl, (float)st[0]);
-      Mr[k] = (float)st[4];
-      zr[k] = st[5];
-      ar[k] = st[6];
+// Merged max score, max z, Z and A of head hh over every rank's record, in
+// rank order: the same inputs give the same result wherever it runs, so
+// every rank agrees.
+__device__ __forceinline__ void merge_head(const ShardSelParams& p, int hh, float& mx, float& M,
+                                           double& Z, double& A) {
+  mx = -INFINITY;
+  M = -INFINITY;
+#pragma unroll 8
+  for (int r = 0; r < p.world; ++r) {
+    const double* st = stats_of(p, r, hh);
+    mx = fmaxf(mx, (float)st[0]);
+    M = fmaxf(M, (float)st[4]);
+  }
+  Z = 0.0;
+  A = 0.0;
+#pragma unroll 8
+  for (int r = 0; r < p.world; ++r) {
+    const double* st = stats_of(p, r, hh);
+    const float Mr = (float)st[4];
+    if (Mr > -INFINITY) {
+      const double sc = exp((double)Mr - (double)M);
+      Z += st[5] * sc;
+      A += sc * (st[6] + st[5] * ((double)Mr - (double)M));
     }
   }
-  mx = warp_max(mxl);
-  M = warp_max(fmaxf(Mr[0], Mr[1]));
-  double z = 0.0, a = 0.0;
-#pragma unroll
-  for (int k = 0; k < 2; ++k) {
-    if (Mr[k] > -INFINITY) {
-      const double sc = exp((double)Mr[k] - (double)M);
-      z += zr[k] * sc;
-      a += sc * (ar[k] + zr[k] * ((double)Mr[k] - (double)M));
-    }
-  }
-  Z = warp_sum(z);
-  A = warp_sum(a);
 }
 
 constexpr int kSweepU = 8;  // row loads in flight per thread in a sweep
 
 // ---- stage 0: statistics and the shard's top content candidates ----------
+// UNIT_T: temperature 1 (z = s exactly, no division)
+template <bool UNIT_T>
 __global__ void __launch_bounds__(kShardThreads, 1) shard_prep_kernel(ShardSelParams p) {
   extern __shared__ __align__(16) unsigned char smem[];
   unsigned long long* list = reinterpret_cast<unsigned long long*>(smem);  // [kShardListCap] gathered
@@ -114,113 +107,98 @@ __global__ void __launch_bounds__(kShardThreads, 1) shard_prep_kernel(ShardSelPa
   float* srow = reinterpret_cast<float*>(bfill + kShardSortBuckets);     // staged row
   __shared__ float wf[32][3];
   __shared__ double wd[32][4];
-  __shared__ int wi[32];
   __shared__ int red[33];
-  __shared__ int s_n, s_ncont;
+  __shared__ int s_n;
   __shared__ float s_mx, s_cmx, s_cmn, s_M;
   __shared__ double s_csum, s_csq, s_Z, s_A;
 
   const int h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int n = p.n_local, lo = p.block_lo, nb = p.nb;
   const int sink = imin(p.cfg.n_sink, nb), local = imin(p.cfg.n_local, nb);
-  auto content = [&](int gi) { return gi >= sink && gi < nb - local; };
+  // content (neither sink nor local-window) blocks of the shard: [c0, c1)
+  const int c0 = imin(n, imax(0, sink - lo)), c1 = imax(c0, imin(n, nb - local - lo));
+  const int ncont = c1 - c0;
   const bool staged = n <= kShardStageCap;
   const float* row = p.scores + (int64_t)h * p.score_stride;
   const bool soft = nb >= 2 && p.cfg.policy == ADAKV_POLICY_ADAPTIVE;
   const float Tf = (float)(p.cfg.temperature > 1e-6 ? p.cfg.temperature : 1e-6);
-  const bool unit_t = (Tf == 1.0f);
+  auto zof = [&](float v) -> float { return UNIT_T ? v : __fdiv_rn(v, Tf); };
+  auto val = [&](int li) -> float { return staged ? srow[li] : row[li]; };
   pdl_wait();  // the scores come from the estimator
 
-  auto val = [&](int li) -> float { return staged ? srow[li] : row[li]; };
-  // fn(li, v) over the shard's row, kSweepU loads in flight per thread
-  auto sweep = [&](auto&& fn) {
-    for (int base = 0; base < n; base += kShardThreads * kSweepU) {
-      float v[kSweepU];
-#pragma unroll
-      for (int u = 0; u < kSweepU; ++u) {
-        const int li = base + u * kShardThreads + tid;
-        v[u] = li < n ? val(li) : 0.f;
-      }
-#pragma unroll
-      for (int u = 0; u < kSweepU; ++u) {
-        const int li = base + u * kShardThreads + tid;
-        if (li < n) fn(li, v[u]);
-      }
-    }
-  };
-  if (staged) {
-    for (int base = 0; base < n; base += kShardThreads * kSweepU) {
-      float v[kSweepU];
-#pragma unroll
-      for (int u = 0; u < kSweepU; ++u) {
-        const int li = base + u * kShardThreads + tid;
-        v[u] = li < n ? row[li] : 0.f;
-      }
-#pragma unroll
-      for (int u = 0; u < kSweepU; ++u) {
-        const int li = base + u * kShardThreads + tid;
-        if (li < n) srow[li] = v[u];
-      }
-    }
-    __syncthreads();
-  }
-
-  // ---- 1. statistics: max score and max z, content max / min / sum / sum of
-  //      squares; then Z and A relative to the shard's max z ----
+  // ---- 1. stage the row (kSweepU loads in flight per thread) and fold the
+  //      max score and the content max / min / sum / sum of squares ----
   float mx = -INFINITY, cmx = -INFINITY, cmn = INFINITY, csum = 0.f, csq = 0.f;
-  int nc = 0;
-  sweep([&](int li, float v) {
-    mx = fmaxf(mx, v);
-    if (content(lo + li)) {
-      cmx = fmaxf(cmx, v);
-      cmn = fminf(cmn, v);
-      csum += v;
-      csq = fmaf(v, v, csq);
-      ++nc;
+  for (int base = 0; base < n; base += kShardThreads * kSweepU) {
+    float v[kSweepU];
+#pragma unroll
+    for (int u = 0; u < kSweepU; ++u) {
+      const int li = base + u * kShardThreads + tid;
+      v[u] = li < n ? row[li] : -INFINITY;
     }
-  });
+#pragma unroll
+    for (int u = 0; u < kSweepU; ++u) {
+      const int li = base + u * kShardThreads + tid;
+      if (li < n) {
+        if (staged) srow[li] = v[u];
+        mx = fmaxf(mx, v[u]);
+        if (li >= c0 && li < c1) {
+          cmx = fmaxf(cmx, v[u]);
+          cmn = fminf(cmn, v[u]);
+          csum += v[u];
+          csq = fmaf(v[u], v[u], csq);
+        }
+      }
+    }
+  }
   {
     const float wmx = warp_max(mx), wcmx = warp_max(cmx), wcmn = -warp_max(-cmn);
     const double ws = warp_sum((double)csum), wq = warp_sum((double)csq);
-    const int wn = __reduce_add_sync(0xffffffffu, nc);
     if (lane == 0) {
       wf[warp][0] = wcmn;
       wf[warp][1] = wmx;
       wf[warp][2] = wcmx;
       wd[warp][2] = ws;
       wd[warp][3] = wq;
-      wi[warp] = wn;
     }
   }
-  __syncthreads();
+  __syncthreads();  // also publishes the staged row
   if (warp == 0) {
     const float m1 = warp_max(wf[lane][1]), m2 = warp_max(wf[lane][2]);
     const float m0 = -warp_max(-wf[lane][0]);
     const double cs = warp_sum(wd[lane][2]), cq = warp_sum(wd[lane][3]);
-    const int ncont = __reduce_add_sync(0xffffffffu, wi[lane]);
     if (lane == 0) {
       s_mx = m1;
       s_cmx = m2;
       s_cmn = m0;
-      s_M = zof(m1, Tf, unit_t);  // max z (division by T > 0 is monotone)
+      s_M = zof(m1);  // max z (division by T > 0 is monotone)
       s_csum = cs;
       s_csq = cq;
-      s_ncont = ncont;
-      s_n = 0;
       s_Z = 0.0;
       s_A = 0.0;
     }
   }
   __syncthreads();
+
+  // ---- 2. Z and A relative to the shard's max z ----
   if (soft && s_M > -INFINITY) {
     const float M = s_M;
     float z_t = 0.f, a_t = 0.f;
-    sweep([&](int, float v) {
-      const float d = zof(v, Tf, unit_t) - M;
-      const float e = expf(d);
-      z_t += e;
-      if (e > 0.f) a_t = fmaf(e, d, a_t);
-    });
+    for (int base = 0; base < n; base += kShardThreads * kSweepU) {
+      float v[kSweepU];
+#pragma unroll
+      for (int u = 0; u < kSweepU; ++u) {
+        const int li = base + u * kShardThreads + tid;
+        v[u] = li < n ? val(li) : -INFINITY;
+      }
+#pragma unroll
+      for (int u = 0; u < kSweepU; ++u) {
+        const float d = zof(v[u]) - M;
+        const float e = expf(d);
+        z_t += e;
+        a_t = e > 0.f ? fmaf(e, d, a_t) : a_t;
+      }
+    }
     const double zw = warp_sum((double)z_t), aw = warp_sum((double)a_t);
     if (lane == 0) {
       wd[warp][0] = zw;
@@ -236,7 +214,6 @@ __global__ void __launch_bounds__(kShardThreads, 1) shard_prep_kernel(ShardSelPa
     }
     __syncthreads();
   }
-  const int ncont = s_ncont;
   const int kc = imin(p.cap, ncont);
   double* st = reinterpret_cast<double*>(p.xmine) + (size_t)h * kShardStatD;
   unsigned long long* out = reinterpret_cast<unsigned long long*>(
@@ -254,18 +231,59 @@ __global__ void __launch_bounds__(kShardThreads, 1) shard_prep_kernel(ShardSelPa
   }
   if (kc == 0) return;  // uniform over the CTA
 
+  // content keys >= T (> T when strict) into the list in any order, at most
+  // kShardListCap of them; returns how many there are
+  auto gather = [&](uint32_t T, bool strict) -> int {
+    __syncthreads();  // the list and s_n may still be in use
+    if (tid == 0) s_n = 0;
+    __syncthreads();
+    for (int base = c0; base < c1; base += kShardThreads * kSweepU) {
+      float v[kSweepU];
+#pragma unroll
+      for (int u = 0; u < kSweepU; ++u) {
+        const int li = base + u * kShardThreads + tid;
+        v[u] = li < c1 ? val(li) : -INFINITY;
+      }
+#pragma unroll
+      for (int u = 0; u < kSweepU; ++u) {
+        const int li = base + u * kShardThreads + tid;
+        const uint32_t k = order_key(v[u]);
+        const bool take = li < c1 && (strict ? k > T : k >= T);
+        const unsigned b = __ballot_sync(0xffffffffu, take);
+        if (b) {
+          int at = 0;
+          if (lane == 0) at = atomicAdd(&s_n, __popc(b));
+          at = __shfl_sync(0xffffffffu, at, 0) + __popc(b & ((1u << lane) - 1u));
+          if (take && at < kShardListCap) list[at] = cand_key(v[u], lo + li);
+        }
+      }
+    }
+    __syncthreads();
+    return s_n;
+  };
   auto count_ge = [&](uint32_t T) -> int {
     int c = 0;
-    sweep([&](int li, float v) { c += (content(lo + li) && order_key(v) >= T) ? 1 : 0; });
+    for (int base = c0; base < c1; base += kShardThreads * kSweepU) {
+#pragma unroll
+      for (int u = 0; u < kSweepU; ++u) {
+        const int li = base + u * kShardThreads + tid;
+        c += (li < c1 && order_key(val(li)) >= T) ? 1 : 0;
+      }
+    }
     return block_sum_int(c, red);
   };
 
-  // ---- 2. threshold key T: a normal-fit guess, then bisection over the keys
-  //      until between kc and kShardListCap content keys are >= T, or T is
-  //      the largest key with at least kc keys >= it (exact) ----
-  uint32_t T = order_key(s_cmn);  // every content key (kc == ncont)
+  // ---- 3. threshold key T and the gathered keys: every content key when
+  //      the shard has at most kc; else the keys >= a normal-fit guess, when
+  //      there are between kc and kShardListCap of them; else bisection over
+  //      the keys until such a T is found, or T is the largest key with at
+  //      least kc keys >= it (exact: the keys above it, then its ties) ----
+  uint32_t T = order_key(s_cmn);
   bool exact = false;
-  if (kc < ncont) {
+  int m;
+  if (kc == ncont) {
+    m = gather(T, false);
+  } else {
     const double mean = s_csum / ncont, var = s_csq / ncont - mean * mean;
     const double sd = var > 0.0 ? sqrt(var) : 0.0;
     const double want = fmin((double)ncont, 1.25 * kc + 64.0);
@@ -275,66 +293,47 @@ __global__ void __launch_bounds__(kShardThreads, 1) shard_prep_kernel(ShardSelPa
       cur = order_key((float)(mean + (double)normcdfinvf((float)(1.0 - want / ncont)) * sd));
       cur = cur > hi_k ? hi_k : cur;
     }
-    bool done = false;
+    int c = gather(cur, false);
+    bool done = c >= kc && c <= kShardListCap;
+    T = cur;
     for (int it = 0; it < 40 && !done; ++it) {
-      const int c = count_ge(cur);
+      if (c < kc) hi_k = cur - 1u;  // cur > lo_k here: count(>= lo_k) >= kc
+      else lo_k = cur;
+      if (lo_k >= hi_k) {
+        T = lo_k;
+        exact = true;
+        break;
+      }
+      cur = lo_k + (uint32_t)(((uint64_t)hi_k - lo_k + 1u) >> 1);
+      c = count_ge(cur);
       if (c >= kc && c <= kShardListCap) {
         T = cur;
         done = true;
-      } else {
-        if (c < kc) hi_k = cur - 1u;  // cur > lo_k here: count(>= lo_k) >= kc
-        else lo_k = cur;
-        if (lo_k >= hi_k) {
-          T = lo_k;
-          exact = true;
-          done = true;
-        } else {
-          cur = lo_k + (uint32_t)(((uint64_t)hi_k - lo_k + 1u) >> 1);
-        }
+        c = gather(T, false);
       }
     }
-    if (!done) {
+    if (!done && !exact) {
       T = lo_k;
       exact = true;
     }
-  }
-
-  // ---- 3. gather the keys (above T when exact, else >= T) in any order ----
-  for (int base = 0; base < n; base += kShardThreads) {
-    const int li = base + tid;
-    bool take = false;
-    unsigned long long key = 0ull;
-    if (li < n) {
-      const float v = val(li);
-      const uint32_t k = order_key(v);
-      if (content(lo + li) && (exact ? k > T : k >= T)) {
-        take = true;
-        key = cand_key(v, lo + li);
+    m = c;
+    if (exact) {
+      m = gather(T, true);  // fewer than kc keys above T
+      // then keys equal to T in ascending block order (each thread owns a
+      // contiguous range), up to kc in all: the reference's lowest-index ties
+      const int R = ceil_div(ncont, kShardThreads);
+      const int a0 = imin(c1, c0 + tid * R), a1 = imin(c1, a0 + R);
+      int cnt = 0;
+      for (int li = a0; li < a1; ++li) cnt += order_key(val(li)) == T ? 1 : 0;
+      int off = block_exclusive_scan(cnt, red);
+      const int need = kc - m;
+      for (int li = a0; li < a1 && off < need; ++li) {
+        const float v = val(li);
+        if (order_key(v) == T) list[m + off++] = cand_key(v, lo + li);
       }
+      m = kc;
+      __syncthreads();
     }
-    const unsigned b = __ballot_sync(0xffffffffu, take);
-    int at = 0;
-    if (lane == 0 && b) at = atomicAdd(&s_n, __popc(b));
-    at = __shfl_sync(0xffffffffu, at, 0);
-    if (take) list[at + __popc(b & ((1u << lane) - 1u))] = key;
-  }
-  __syncthreads();
-  int m = s_n;
-  if (exact) {
-    // then keys equal to T in ascending block order (each thread owns a
-    // contiguous range), up to kc in all: the reference's lowest-index ties
-    const int R = ceil_div(n, kShardThreads);
-    const int a0 = imin(n, tid * R), a1 = imin(n, a0 + R);
-    int cnt = 0;
-    for (int li = a0; li < a1; ++li) cnt += (content(lo + li) && order_key(val(li)) == T) ? 1 : 0;
-    int off = block_exclusive_scan(cnt, red);
-    const int need = kc - m;
-    for (int li = a0; li < a1 && off < need; ++li) {
-      const float v = val(li);
-      if (content(lo + li) && order_key(v) == T) list[m + off++] = cand_key(v, lo + li);
-    }
-    m = kc;
-    __syncthreads();
   }
 
   // ---- 4. counting sort of the m keys, descending: buckets of the score key
@@ -399,14 +398,12 @@ __global__ void __launch_bounds__(kShardThreads, 1) shard_clamp_kernel(ShardSelP
   const float Tf = (float)(p.cfg.temperature > 1e-6 ? p.cfg.temperature : 1e-6);
   const bool unit_t = (Tf == 1.0f);
   pdl_wait();  // every rank's records have been gathered
-  if (warp == 0) {
+  if (tid == 0) {
     float mxg, M;
     double Z, A;
-    merge_head_warp(p, h, mxg, M, Z, A);
-    if (lane == 0) {
-      s_mx = mxg;
-      s_Z = Z;
-    }
+    merge_head(p, h, mxg, M, Z, A);
+    s_mx = mxg;
+    s_Z = Z;
   }
   __syncthreads();
   const double Z = s_Z;
@@ -457,7 +454,6 @@ __global__ void __launch_bounds__(kShardFinishThreads, 1) shard_finish_kernel(Sh
   __shared__ int red[33];
   __shared__ int s_nc[kShardMaxWorld];
   __shared__ double s_sumw;
-  constexpr int kW = kShardFinishThreads / 32;
   const int h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nb = p.nb;
   const bool adaptive = nb >= 2 && p.cfg.policy == ADAKV_POLICY_ADAPTIVE;
@@ -465,23 +461,19 @@ __global__ void __launch_bounds__(kShardFinishThreads, 1) shard_finish_kernel(Sh
   pdl_wait();
 
   // ---- 1. every head's weight (adakv/budget.py:36-37, float64 after the
-  //      division), one warp per head; summed in a fixed order: every rank
-  //      gets the same weights and sum ----
+  //      division), one thread per head; summed in a fixed order: every
+  //      rank gets the same weights and sum ----
   if (adaptive) {
-    for (int hh = warp; hh < p.Hq; hh += kW) {
+    for (int hh = tid; hh < p.Hq; hh += kShardFinishThreads) {
       float mxg, M;
-      double Z, A;
-      merge_head_warp(p, hh, mxg, M, Z, A);
-      double cc = 0.0;
+      double Z, A, cc = 0.0;
+      merge_head(p, hh, mxg, M, Z, A);
       if (p.cc_all) {
-        if (lane < p.world) cc = p.cc_all[(size_t)lane * p.Hq + hh];
-        if (lane + 32 < p.world) cc += p.cc_all[(size_t)(lane + 32) * p.Hq + hh];
-        cc = warp_sum(cc);
+#pragma unroll 8
+        for (int r = 0; r < p.world; ++r) cc += p.cc_all[(size_t)r * p.Hq + hh];
       }
-      if (lane == 0) {
-        const double e = Z > 0.0 ? log(Z) - A / Z - cc / Z : 0.0;
-        s_w[hh] = (double)(float)e / lognb + 1e-6;
-      }
+      const double e = Z > 0.0 ? log(Z) - A / Z - cc / Z : 0.0;
+      s_w[hh] = (double)(float)e / lognb + 1e-6;
     }
   }
   if (tid < p.world) s_nc[tid] = (int)stats_of(p, tid, h)[7];
@@ -578,18 +570,22 @@ size_t shard_finish_smem(int Hq, int world, int cap_pad) {
 }
 
 cudaError_t shard_kernels_init() {
-  cudaError_t e = cudaFuncSetAttribute(shard_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)prep_smem(kShardStageCap));
-  if (e != cudaSuccess) return e;
+  for (auto k : {shard_prep_kernel<true>, shard_prep_kernel<false>}) {
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)prep_smem(kShardStageCap));
+    if (e != cudaSuccess) return e;
+  }
   return cudaFuncSetAttribute(shard_finish_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                               (int)kShardFinishSmemMax);
 }
 
 cudaError_t launch_shard_select(int stage, const ShardSelParams& p, cudaStream_t st,
                                 const LaunchOpts& o) {
-  if (stage == 0)
-    return launch_ex(shard_prep_kernel, dim3(p.Hq), dim3(kShardThreads), prep_smem(p.n_local), st, o,
-                     p);
+  if (stage == 0) {
+    const bool unit_t = (float)(p.cfg.temperature > 1e-6 ? p.cfg.temperature : 1e-6) == 1.0f;
+    return launch_ex(unit_t ? shard_prep_kernel<true> : shard_prep_kernel<false>, dim3(p.Hq),
+                     dim3(kShardThreads), prep_smem(p.n_local), st, o, p);
+  }
   if (stage == 1)
     return launch_ex(shard_clamp_kernel, dim3(p.Hq), dim3(kShardThreads), 0, st, o, p);
   return launch_ex(shard_finish_kernel, dim3(p.Hq), dim3(kShardFinishThreads),
