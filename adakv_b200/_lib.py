@@ -80,6 +80,16 @@ _SIGNATURES = {
                                             ctypes.c_float, _vp, _vp, _vp, ctypes.c_size_t, _vp]),
     "adakv_combine": (ctypes.c_int, [ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                      ctypes.c_int32, _vp, _vp, _P(View), _vp]),
+    "adakv_combine_packed": (ctypes.c_int, [ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                            ctypes.c_int32, ctypes.c_int32, _vp, ctypes.c_int64,
+                                            _P(View), _vp]),
+    "adakv_peer_buffer_bytes": (ctypes.c_size_t, [ctypes.c_int32, ctypes.c_size_t]),
+    "adakv_peer_alloc": (ctypes.c_int, [ctypes.c_size_t, _P(ctypes.c_void_p), _vp]),
+    "adakv_peer_free": (ctypes.c_int, [_vp]),
+    "adakv_peer_open": (ctypes.c_int, [_vp, _P(ctypes.c_void_p)]),
+    "adakv_peer_close": (ctypes.c_int, [_vp]),
+    "adakv_peer_exchange": (ctypes.c_int, [_vp, ctypes.c_size_t, _vp, ctypes.c_int32,
+                                           ctypes.c_int32, ctypes.c_size_t, _vp, _vp, _vp]),
     "adakv_shard_record_bytes": (ctypes.c_size_t, [_P(Geometry), _P(SelectParams)]),
     "adakv_shard_prep": (ctypes.c_int, [_P(Geometry), _P(SelectParams), _vp, ctypes.c_int32,
                                         ctypes.c_int32, ctypes.c_int32, _vp, _vp]),

@@ -554,10 +554,10 @@ __global__ void __launch_bounds__(128) combine_kernel(CombineParams p) {
   const int row = blockIdx.x;
   pdl_wait();
   float M = -INFINITY;
-  for (int n = 0; n < p.n_parts; ++n) M = fmaxf(M, p.lse[(int64_t)n * p.rows + row]);
+  for (int n = 0; n < p.n_parts; ++n) M = fmaxf(M, p.lse[n * p.lse_stride + row]);
   float den = 0.f;
   for (int n = 0; n < p.n_parts; ++n) {
-    const float l = p.lse[(int64_t)n * p.rows + row];
+    const float l = p.lse[n * p.lse_stride + row];
     den += (M == -INFINITY || l == -INFINITY) ? 0.f : expf(l - M);
   }
   const int b = row / p.Hq, h = row - b * p.Hq;
@@ -565,9 +565,9 @@ __global__ void __launch_bounds__(128) combine_kernel(CombineParams p) {
   for (int d = threadIdx.x; d < p.D; d += blockDim.x) {
     float acc = 0.f;
     for (int n = 0; n < p.n_parts; ++n) {
-      const float l = p.lse[(int64_t)n * p.rows + row];
+      const float l = p.lse[n * p.lse_stride + row];
       if (M == -INFINITY || l == -INFINITY) continue;
-      acc += expf(l - M) * p.parts[((int64_t)n * p.rows + row) * p.D + d];
+      acc += expf(l - M) * p.parts[n * p.part_stride + (int64_t)row * p.D + d];
     }
     orow[d] = from_f32<T>(den > 0.f ? acc / den : 0.f);
   }

@@ -1174,6 +1174,37 @@ int adakv_combine(int32_t n_parts, int32_t batch, int32_t n_q_heads, int32_t hea
   cp.n_parts = n_parts;
   cp.rows = batch * n_q_heads;
   cp.D = head_dim;
+  cp.part_stride = (int64_t)cp.rows * head_dim;
+  cp.lse_stride = cp.rows;
+  cp.out = to_view(out);
+  cp.Hq = n_q_heads;
+  LaunchOpts oc;
+  oc.pdl = pdl_enabled();
+  CUDA_TRY(launch_combine(cp, dtype, static_cast<cudaStream_t>(stream), oc));
+  return ADAKV_OK;
+}
+
+int adakv_combine_packed(int32_t n_parts, int32_t batch, int32_t n_q_heads, int32_t head_dim,
+                         int32_t dtype, const float* packed, int64_t part_stride,
+                         const adakv_view* out, void* stream) {
+  int rc;
+  if (n_parts < 1 || batch < 1 || n_q_heads < 1 || head_dim < 1)
+    return fail(ADAKV_ERR_INVALID, "n_parts, batch, n_q_heads and head_dim must be >= 1");
+  if (dtype < ADAKV_DTYPE_F32 || dtype > ADAKV_DTYPE_BF16)
+    return fail(ADAKV_ERR_INVALID, "unknown dtype %d", dtype);
+  const int64_t rows = (int64_t)batch * n_q_heads;
+  if (!packed || part_stride < rows * (head_dim + 1))
+    return fail(ADAKV_ERR_INVALID, "packed is NULL or part_stride %lld < rows * (head_dim + 1)",
+                (long long)part_stride);
+  if ((rc = check_view(out, "out", dtype, false))) return rc;
+  CombineParams cp{};
+  cp.parts = packed;
+  cp.lse = packed + rows * head_dim;
+  cp.part_stride = part_stride;
+  cp.lse_stride = part_stride;
+  cp.n_parts = n_parts;
+  cp.rows = (int)rows;
+  cp.D = head_dim;
   cp.out = to_view(out);
   cp.Hq = n_q_heads;
   LaunchOpts oc;
@@ -1347,6 +1378,75 @@ int adakv_shard_finish(const adakv_geometry* geo, const adakv_select_params* sp,
   LaunchOpts o;
   o.pdl = pdl_enabled();
   CUDA_TRY(launch_shard_select(2, p, static_cast<cudaStream_t>(stream), o));
+  return ADAKV_OK;
+}
+
+size_t adakv_peer_buffer_bytes(int32_t world, size_t slot_bytes) {
+  if (world < 1 || world > kPeerMaxWorld || slot_bytes % 16) return 0;
+  return peer_buffer_bytes(world, slot_bytes);
+}
+
+int adakv_peer_alloc(size_t bytes, void** ptr, void* handle) {
+  if (!ptr || !handle || bytes == 0) return fail(ADAKV_ERR_INVALID, "ptr / handle NULL or bytes 0");
+  *ptr = nullptr;
+  void* p = nullptr;
+  CUDA_TRY(cudaMalloc(&p, bytes));
+  cudaError_t e = cudaMemset(p, 0, bytes);
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(handle), p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return fail(ADAKV_ERR_CUDA, "peer buffer set-up failed: %s", cudaGetErrorString(e));
+  }
+  *ptr = p;
+  return ADAKV_OK;
+}
+
+int adakv_peer_free(void* ptr) {
+  if (ptr) CUDA_TRY(cudaFree(ptr));
+  return ADAKV_OK;
+}
+
+int adakv_peer_open(const void* handle, void** ptr) {
+  if (!ptr || !handle) return fail(ADAKV_ERR_INVALID, "ptr / handle NULL");
+  *ptr = nullptr;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  CUDA_TRY(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess));
+  return ADAKV_OK;
+}
+
+int adakv_peer_close(void* ptr) {
+  if (ptr) CUDA_TRY(cudaIpcCloseMemHandle(ptr));
+  return ADAKV_OK;
+}
+
+int adakv_peer_exchange(const void* src, size_t bytes, void* const* dsts, int32_t world,
+                        int32_t rank, size_t slot_bytes, void* local, uint32_t* status,
+                        void* stream) {
+  if (world < 1 || world > kPeerMaxWorld || rank < 0 || rank >= world)
+    return fail(ADAKV_ERR_INVALID, "world %d / rank %d outside [1, %d] / [0, world)", world, rank,
+                kPeerMaxWorld);
+  if (!src || !dsts || !local || reinterpret_cast<uintptr_t>(src) % 16 ||
+      reinterpret_cast<uintptr_t>(local) % 16)
+    return fail(ADAKV_ERR_INVALID, "src, dsts and local are required; src and local 16-byte aligned");
+  if (bytes % 16 || slot_bytes % 16 || bytes > slot_bytes)
+    return fail(ADAKV_ERR_INVALID, "bytes (%zu) and slot_bytes (%zu) must be multiples of 16, "
+                "bytes <= slot_bytes", bytes, slot_bytes);
+  PeerParams p{};
+  p.src = src;
+  p.bytes = bytes;
+  p.world = world;
+  p.rank = rank;
+  p.dsts = reinterpret_cast<unsigned char* const*>(dsts);
+  p.slot_bytes = slot_bytes;
+  p.local = static_cast<unsigned char*>(local);
+  p.status = status;
+  p.wait_ns = wait_limit_ns();
+  LaunchOpts o;
+  o.pdl = pdl_enabled();
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  CUDA_TRY(launch_peer_put(p, st, o));
+  CUDA_TRY(launch_peer_wait(p, st, o));
   return ADAKV_OK;
 }
 

@@ -136,8 +136,9 @@ struct AttendParams {
 };
 
 struct CombineParams {      // log-sum-exp merge of per-shard attention outputs
-  const float* parts;       // [n_parts, rows, D]
-  const float* lse;         // [n_parts, rows]
+  const float* parts;       // part n: parts + n * part_stride, [rows, D]
+  const float* lse;         // part n: lse + n * lse_stride, [rows]
+  int64_t part_stride, lse_stride;
   int n_parts, rows, D;
   View out;                 // rows = b * Hq + h -> out[b, h, :]
   int Hq;
@@ -276,6 +277,24 @@ struct ShardSelParams {
 };
 
 // ---------------------------------------------------------------------------
+// all-gather of small payloads through peer-mapped memory (peer.cu)
+// ---------------------------------------------------------------------------
+constexpr int kPeerChunks = 16;    // CTAs (and flag words) per (source, destination)
+constexpr int kPeerThreads = 256;
+constexpr int kPeerMaxWorld = 16;
+
+struct PeerParams {
+  const void* src;                 // this rank's payload (16-byte aligned)
+  size_t bytes;                    // payload bytes, a multiple of 16, <= slot_bytes
+  int world, rank;
+  unsigned char* const* dsts;      // device array [world]: every rank's buffer, mapped here
+  size_t slot_bytes;               // a multiple of 16
+  unsigned char* local;            // this rank's buffer
+  uint32_t* status;                // optional ADAKV_ST_* word
+  uint64_t wait_ns;                // bound of the wait
+};
+
+// ---------------------------------------------------------------------------
 // launch helper: cudaLaunchKernelEx with optional PDL / cooperative / cluster
 // ---------------------------------------------------------------------------
 struct LaunchOpts {
@@ -340,6 +359,9 @@ cudaError_t launch_shard_select(int stage, const ShardSelParams& p, cudaStream_t
                                 const LaunchOpts& o);
 size_t shard_finish_smem(int Hq, int world, int cap_pad);
 cudaError_t shard_kernels_init();
+size_t peer_buffer_bytes(int world, size_t slot_bytes);
+cudaError_t launch_peer_put(const PeerParams& p, cudaStream_t stream, const LaunchOpts& o);
+cudaError_t launch_peer_wait(const PeerParams& p, cudaStream_t stream, const LaunchOpts& o);
 cudaError_t launch_step(const StepParams& p, int dtype, int D, int g, int grid, size_t smem,
                         cudaStream_t stream, const LaunchOpts& o);
 cudaError_t launch_step_scores(bool fused, const float* fscores,

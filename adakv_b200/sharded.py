@@ -111,9 +111,9 @@ class ShardCache:
             packed = torch.empty(n + self.Hq, dtype=torch.float32, device=q.device)
         o = packed[:n].view(self.Hq, self.D)
         lse = packed[n:n + self.Hq]
-        o.zero_()
-        lse.fill_(-math.inf)
-        if self.S == 0:
+        if self.S == 0:  # (otherwise the kernel writes every row, empty ones as 0 and -inf)
+            o.zero_()
+            lse.fill_(-math.inf)
             return o, lse
         L = _lib.lib()
         geo = self._geo()
@@ -247,6 +247,21 @@ def combine(parts, lse, dtype, out=None):
     return out
 
 
+def combine_packed(g, Hq, D, dtype, out=None):
+    """Log-sum-exp merge of gathered packed partials ``g [N, Hq * (D + 1)]``
+    (each row: o ``[Hq, D]`` then lse ``[Hq]``), read in place."""
+    if out is None:
+        out = torch.empty((Hq, D), dtype=dtype, device=g.device)
+    if g.stride(1) != 1:
+        g = g.contiguous()
+    with torch.cuda.device(g.device):
+        _lib.check(_lib.lib().adakv_combine_packed(g.shape[0], 1, Hq, D, _lib.TORCH_DTYPES[dtype],
+                                                   g.data_ptr(), g.stride(0),
+                                                   _lib.view4(out.unsqueeze(0)),
+                                                   _lib.stream_ptr(g.device)))
+    return out
+
+
 def _concat_scores(gathered, nb, L):
     """``gathered [world, Hq, L]`` (rank r holds blocks [r L, (r + 1) L)) -> ``[Hq, nb]``."""
     world, Hq, _ = gathered.shape
@@ -303,10 +318,112 @@ class TorchGroup:
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
 
-    def all_gather(self, t):
+    def all_gather(self, t, name=None):
         out = torch.empty((self.world,) + tuple(t.shape), dtype=t.dtype, device=t.device)
         self.dist.all_gather_into_tensor(out, t.contiguous(), group=self.group)
         return out
+
+
+class _DeviceBytes:
+    """A device allocation of the library seen by torch (no copy, not owned)."""
+
+    def __init__(self, ptr, nbytes):
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1",
+                                         "data": (ptr, False), "version": 3}
+
+
+class PeerGroup:
+    """All-gather through peer-mapped memory (``adakv_peer_*``): NVLink stores
+    into every rank's buffer and a bounded wait on per-chunk flags, two small
+    kernels per call instead of an NCCL collective.
+
+    One buffer per call site (``name``), set up on its first call: a
+    ``cudaMalloc``, its IPC handle shared over ``group`` (a collective, so
+    every rank makes that first call together, eagerly, before any stream
+    capture) and the other ranks' buffers mapped here.  The gathered result
+    is a view of this rank's buffer, valid until the next call on the same
+    name; every rank must make the same calls in the same order."""
+
+    def __init__(self, group=None, device=None):
+        import torch.distributed as dist
+        self.dist, self.group = dist, group
+        init = dist.is_available() and dist.is_initialized()
+        self.world = dist.get_world_size(group) if init else 1
+        self.rank = dist.get_rank(group) if init else 0
+        self.device = (torch.device(device) if device is not None
+                       else torch.device("cuda", torch.cuda.current_device()))
+        self.status = torch.zeros((4,), dtype=torch.int32, device=self.device)
+        self._bufs = {}
+
+    def _buffer(self, name, nbytes):
+        b = self._bufs.get(name)
+        if b is not None:
+            if b["slot"] != nbytes:
+                raise ValueError(f"peer buffer {name!r} carries {b['slot']} bytes, not {nbytes}")
+            return b
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError("peer buffers are set up by an eager call before stream capture")
+        import ctypes
+        L = _lib.lib()
+        total = L.adakv_peer_buffer_bytes(self.world, nbytes)
+        if total == 0:
+            raise ValueError(f"no peer buffer for world {self.world} and {nbytes} bytes per rank")
+        ptr = ctypes.c_void_p()
+        handle = (ctypes.c_ubyte * 64)()
+        with torch.cuda.device(self.device):
+            _lib.check(L.adakv_peer_alloc(total, ctypes.byref(ptr), handle))
+            handles = [bytes(handle)]
+            if self.world > 1:
+                handles = [None] * self.world
+                self.dist.all_gather_object(handles, bytes(handle), group=self.group)
+            ptrs, opened = [], []
+            for r in range(self.world):
+                if r == self.rank:
+                    ptrs.append(ptr.value)
+                    continue
+                q = ctypes.c_void_p()
+                hb = (ctypes.c_ubyte * 64).from_buffer_copy(handles[r])
+                _lib.check(L.adakv_peer_open(hb, ctypes.byref(q)))
+                ptrs.append(q.value)
+                opened.append(q.value)
+        dsts = torch.tensor(ptrs, dtype=torch.int64, device=self.device)
+        view = torch.as_tensor(_DeviceBytes(ptr.value, self.world * nbytes), device=self.device)
+        b = {"slot": nbytes, "local": ptr.value, "dsts": dsts, "opened": opened,
+             "view": view.view(self.world, nbytes)}
+        self._bufs[name] = b
+        return b
+
+    def all_gather(self, t, name=None):
+        t = t.contiguous()
+        nbytes = t.numel() * t.element_size()
+        if nbytes % 16 or t.data_ptr() % 16:
+            raise ValueError("peer all-gather payloads are 16-byte multiples, 16-byte aligned")
+        b = self._buffer(name or f"bytes{nbytes}", nbytes)
+        with torch.cuda.device(self.device):
+            _lib.check(_lib.lib().adakv_peer_exchange(
+                t.data_ptr(), nbytes, b["dsts"].data_ptr(), self.world, self.rank, nbytes,
+                b["local"], self.status.data_ptr(), _lib.stream_ptr(self.device)))
+        return b["view"].view(t.dtype).view((self.world,) + tuple(t.shape))
+
+    def timed_out(self):
+        """True when a wait gave up (ADAKV_ST_WAIT_TIMEOUT); synchronises."""
+        return bool(int(self.status[0].item()) & _lib.ST_WAIT_TIMEOUT)
+
+    def close(self):
+        """Unmap the other ranks' buffers, then free this rank's (a barrier
+        between, so no rank frees memory another still maps)."""
+        L = _lib.lib()
+        torch.cuda.synchronize(self.device)
+        with torch.cuda.device(self.device):
+            for b in self._bufs.values():
+                for q in b["opened"]:
+                    _lib.check(L.adakv_peer_close(q))
+            if self.world > 1:
+                self.dist.barrier(group=self.group)
+            for b in self._bufs.values():
+                b["view"] = None
+                _lib.check(L.adakv_peer_free(b["local"]))
+        self._bufs = {}
 
 
 class ShardedDecoder:
@@ -345,8 +462,9 @@ class ShardedDecoder:
         """This rank's ``(block table, sel_lens)`` from the current scores."""
         if self.stats_sel is not None:
             s = self.stats_sel
-            recs = self.comm.all_gather(s.prep(self.scores))          # [world, record_bytes]
-            ccs = self.comm.all_gather(s.clamp(self.scores, recs)) if s.adaptive else None
+            recs = self.comm.all_gather(s.prep(self.scores), name="records")  # [world, bytes]
+            ccs = (self.comm.all_gather(s.clamp(self.scores, recs), name="clamp")
+                   if s.adaptive else None)
             return s.finish(recs, ccs, self.comm.rank)
         gathered = self.comm.all_gather(self.scores)                  # [world, Hq, L]
         return self.selector.select(_concat_scores(gathered, self.nb, self.L))
@@ -359,7 +477,5 @@ class ShardedDecoder:
         scale = 1.0 / math.sqrt(D) if sm_scale is None else float(sm_scale)
         packed = torch.empty(Hq * D + Hq, dtype=torch.float32, device=q.device)
         self.shard.attend_partial(q, table, sel_lens, scale, packed=packed)
-        g = self.comm.all_gather(packed)                             # [world, Hq * (D + 1)]
-        parts = g[:, :Hq * D].reshape(g.shape[0], Hq, D)             # one collective for (o, lse)
-        lses = g[:, Hq * D:]
-        return combine(parts, lses, q.dtype)
+        g = self.comm.all_gather(packed, name="parts")   # [world, Hq * (D + 1)]: (o, lse) per rank
+        return combine_packed(g, Hq, D, q.dtype)

@@ -407,11 +407,13 @@ def run_cfg4(steps, warmup, world, rank, device):
     """Decode steps of the sharded path (single-GPU step at N=1), each captured
     in a CUDA graph and replayed.  Returns {exchange: (us per step on this
     rank, algorithmic bytes per step of the whole job)}: at N=1 {"single": ...};
-    at N>1 the selection from exchanged statistics ("stats", the default) and
-    the all-gather of the score rows ("rows") on the same shards."""
+    at N>1, on the same shards, the selection from exchanged statistics with
+    the exchanges through peer-mapped memory ("peer", the default), the same
+    over NCCL all-gathers ("stats"), and the NCCL all-gather of the score rows
+    ("rows")."""
     import torch
     from adakv_b200.batch import BatchedDecoder
-    from adakv_b200.sharded import ShardedDecoder, TorchGroup, shard_range
+    from adakv_b200.sharded import PeerGroup, ShardedDecoder, TorchGroup, shard_range
     c = CFG4
     Hq, Hkv, D, bs, S = c["Hq"], c["Hkv"], c["D"], c["bs"], c["S"]
     kw = dict(avg_budget=c["avg"], k_min=c["k_min"], k_max=c["k_max"])
@@ -432,9 +434,12 @@ def run_cfg4(steps, warmup, world, rank, device):
         dec.load(Kl[None], Vl[None], [S])
         variants = {"single": (lambda: dec.step(q[None]), lambda: dec.selected_sets())}
     else:
-        variants = {}
-        for ex in ("stats", "rows"):
-            d = ShardedDecoder(Kl, Vl, S, Hq, bs, TorchGroup(), selection=ex, **kw)
+        variants, comms = {}, []
+        for ex in ("peer", "stats", "rows"):
+            comm = PeerGroup() if ex == "peer" else TorchGroup()
+            comms.append(comm)
+            d = ShardedDecoder(Kl, Vl, S, Hq, bs, comm, selection="rows" if ex == "rows" else "stats",
+                               **kw)
 
             def sets(d=d):
                 sel = d.stats_sel if d.stats_sel is not None else d.selector
@@ -450,7 +455,7 @@ def run_cfg4(steps, warmup, world, rank, device):
         g_ = Hq // Hkv
         for kv in range(Hkv):
             union += len(set().union(*[set(x.tolist()) for x in ss[kv * g_:(kv + 1) * g_]]))
-        if ex == "stats":  # each rank holds its own picks: the job's union is their sum
+        if ex != "rows":  # each rank holds its own picks: the job's union is their sum
             import torch.distributed as dist
             t = torch.tensor([union], device=device, dtype=torch.int64)
             dist.all_reduce(t)
@@ -476,6 +481,10 @@ def run_cfg4(steps, warmup, world, rank, device):
         out[ex] = (a.elapsed_time(b) * 1000.0 / steps, nbytes)
         del graph  # a graph holding NCCL calls must go before the process group
         torch.cuda.synchronize(device)
+    if world > 1:
+        for comm in comms:
+            if isinstance(comm, PeerGroup):
+                comm.close()
     return out
 
 
@@ -661,11 +670,12 @@ def run_partitioned(steps, warmup, world, rank, device, seed):
             us, nbytes = run_cfg2(n, warmup, world, rank, device, seed)
         else:
             r4 = run_cfg4(n, warmup, world, rank, device)
-            us, nbytes = r4["single"] if world == 1 else r4["stats"]
+            us, nbytes = r4["single"] if world == 1 else r4["peer"]
             if world > 1:
-                t = torch.tensor([r4["rows"][0]], device=device, dtype=torch.float64)
+                t = torch.tensor([r4["stats"][0], r4["rows"][0]], device=device,
+                                 dtype=torch.float64)
                 dist.all_reduce(t, op=dist.ReduceOp.MAX)
-                rows_us = float(t[0])
+                rows_us = (float(t[0]), float(t[1]))
         if world > 1:
             t = torch.tensor([us, float(nbytes)], device=device, dtype=torch.float64)
             dist.all_reduce(t[:1], op=dist.ReduceOp.MAX)
@@ -677,13 +687,16 @@ def run_partitioned(steps, warmup, world, rank, device, seed):
                      "frac": achieved / (peak * world), "bytes_per_step": nbytes, "steps": n,
                      "scaling": "strong"}
         if rows_us is not None:
-            out[name]["us_row_exchange"] = rows_us
+            out[name]["us_stats_over_nccl"] = rows_us[0]
+            out[name]["us_row_exchange"] = rows_us[1]
         torch.cuda.empty_cache()
     out["cfg2"]["workload"] = (f"ragged batch {CFG2['B']}, contexts U[{CFG2['lo']}, {CFG2['hi']}], "
                                f"avg_budget {CFG2['avg']}, split by sequence, no collective")
     out["cfg4"]["workload"] = (f"one {CFG4['S']}-token sequence, {CFG4['Hq']} q / {CFG4['Hkv']} KV "
                                f"heads, avg_budget {CFG4['avg']}, sequence-sharded (selection from "
-                               f"exchanged statistics; us_row_exchange: score rows all-gathered)")
+                               f"exchanged statistics, exchanges through peer-mapped memory; "
+                               f"us_stats_over_nccl: the same over NCCL all-gathers; "
+                               f"us_row_exchange: score rows all-gathered over NCCL)")
     return out
 
 
@@ -793,11 +806,12 @@ def main():
         rows_us = None
         if args.workload == "cfg4":
             r4 = run_cfg4(steps, args.warmup, world, rank, device)
-            us, nbytes = r4["single"] if world == 1 else r4["stats"]
+            us, nbytes = r4["single"] if world == 1 else r4["peer"]
             if world > 1:
-                t = torch.tensor([r4["rows"][0]], device=device, dtype=torch.float64)
+                t = torch.tensor([r4["stats"][0], r4["rows"][0]], device=device,
+                                 dtype=torch.float64)
                 dist.all_reduce(t, op=dist.ReduceOp.MAX)
-                rows_us = float(t[0])
+                rows_us = (float(t[0]), float(t[1]))
         else:
             us, nbytes = run_cfg2(steps, args.warmup, world, rank, device, args.seed)
         if world > 1:
@@ -846,15 +860,17 @@ def main():
                 "config": {"workload": f"cfg4 one {c['S']}-token sequence, {c['Hq']} q / {c['Hkv']} KV "
                                        f"heads, head_dim {c['D']}, block {c['bs']}, avg_budget "
                                        f"{c['avg']}, k_max {c['k_max']}, bf16",
-                           "parallelism": f"sequence-sharded x{world} (NCCL all-gathers of per-head "
+                           "parallelism": f"sequence-sharded x{world} (all-gathers of per-head "
                                           "statistics + shard candidates, of clamp terms and of "
-                                          "(o, lse) partials)" if world > 1 else "single GPU",
+                                          "(o, lse) partials through peer-mapped memory)"
+                                          if world > 1 else "single GPU",
                            "timing": "CUDA events around CUDA-graph replays of one step "
                                      "(collectives included), max over ranks"},
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                              "frac": achieved / peak, "traffic": None,
                              "scope": "fp32 centroid table + union of selected K/V blocks, all ranks"},
-                "us_row_exchange": rows_us,
+                "us_stats_over_nccl": rows_us[0] if rows_us else None,
+                "us_row_exchange": rows_us[1] if rows_us else None,
             }), flush=True)
         if world > 1:
             dist.barrier()

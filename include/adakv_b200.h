@@ -374,6 +374,14 @@ int adakv_combine(int32_t n_parts, int32_t batch, int32_t n_q_heads, int32_t hea
                   int32_t dtype, const float* parts, const float* lse, const adakv_view* out,
                   void* stream);
 
+/* adakv_combine over parts packed the way adakv_attend_partial's outputs
+ * travel in one collective: part n at packed + n * part_stride holds
+ * out_f32 [batch * Hq][D] followed by lse [batch * Hq] (part_stride >=
+ * batch * Hq * (D + 1) floats). */
+int adakv_combine_packed(int32_t n_parts, int32_t batch, int32_t n_q_heads, int32_t head_dim,
+                         int32_t dtype, const float* packed, int64_t part_stride,
+                         const adakv_view* out, void* stream);
+
 /* ---- sequence-sharded selection from exchanged statistics ----
  * Replaces the score-row all-gather + adakv_select above for the fixed and
  * adaptive policies (adakv/budget.py:45-86, adakv/selector.py:18-60 over the
@@ -412,6 +420,35 @@ int adakv_shard_finish(const adakv_geometry* geo, const adakv_select_params* sp,
                        int32_t world, int32_t rank, int32_t block_lo, int32_t n_local,
                        int32_t* block_table, int32_t table_width, int32_t* sel_lens,
                        uint32_t* status, void* stream);
+
+/* ---- all-gather of small payloads through peer-mapped memory ----
+ * The sharded step's exchanges (records, clamp terms, partial outputs) are
+ * 0.5 KB - 0.5 MB; an NCCL all-gather of that size costs about 11 us inside
+ * a CUDA graph on two B200s.  These calls move them with NVLink stores into
+ * every rank's buffer instead (no counterpart in the reference, which runs
+ * on one device).  Set-up, once per buffer and process (these synchronise
+ * and allocate; do it before any stream capture):
+ *   adakv_peer_alloc   cudaMalloc of adakv_peer_buffer_bytes(world,
+ *                      slot_bytes), zeroed, and its 64-byte IPC handle;
+ *   share the handles between the ranks (the caller's collective);
+ *   adakv_peer_open    map another rank's buffer here (its own: use ptr);
+ *   adakv_peer_close / adakv_peer_free at the end.
+ * adakv_peer_exchange then copies `bytes` of `src` into slot `rank` of every
+ * rank's buffer (dsts: device array [world] of the mapped pointers, own
+ * included) and waits, bounded, until every rank's payload has arrived in
+ * `local`; slot r of `local` then holds rank r's payload.  Every rank calls
+ * it the same number of times on the same buffer; a payload must have been
+ * consumed everywhere before the next exchange on that buffer starts (the
+ * sharded step's order guarantees this).  On an expired wait the status word
+ * gets ADAKV_ST_WAIT_TIMEOUT and the call returns. */
+size_t adakv_peer_buffer_bytes(int32_t world, size_t slot_bytes);
+int adakv_peer_alloc(size_t bytes, void** ptr, void* handle);
+int adakv_peer_free(void* ptr);
+int adakv_peer_open(const void* handle, void** ptr);
+int adakv_peer_close(void* ptr);
+int adakv_peer_exchange(const void* src, size_t bytes, void* const* dsts, int32_t world,
+                        int32_t rank, size_t slot_bytes, void* local, uint32_t* status,
+                        void* stream);
 
 #ifdef __cplusplus
 }

@@ -1,7 +1,8 @@
 """Sequence-sharded decode over NCCL: one process per GPU (2-4 GPUs when the
 box has them, skipped otherwise), with the selection from exchanged
-statistics and with the score-row all-gather.  Every rank must return the
-output the single-GPU step computes on rank 0's device."""
+statistics and with the score-row all-gather, over NCCL and (statistics
+exchange) over peer-mapped memory.  Every rank must return the output the
+single-GPU step computes on rank 0's device."""
 import os
 import socket
 
@@ -30,11 +31,11 @@ def _inputs(dev):
     return q, K, V
 
 
-def _rank(rank, world, port, results, selection):
+def _rank(rank, world, port, results, selection, comm_kind):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     from datetime import timedelta
     import torch.distributed as dist
-    from adakv_b200.sharded import ShardedDecoder, TorchGroup, shard_range
+    from adakv_b200.sharded import PeerGroup, ShardedDecoder, TorchGroup, shard_range
     dev = torch.device("cuda", rank)
     torch.cuda.set_device(dev)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
@@ -44,13 +45,16 @@ def _rank(rank, world, port, results, selection):
         nb = -(-S // BS)
         lo, n = shard_range(nb, world, rank)
         t0, t1 = lo * BS, min(S, (lo + n) * BS)
+        comm = PeerGroup() if comm_kind == "peer" else TorchGroup()
         dec = ShardedDecoder(K[:, t0:t1].contiguous(), V[:, t0:t1].contiguous(), S, Hq, BS,
-                             TorchGroup(), selection=selection, **KW)
+                             comm, selection=selection, **KW)
         del K, V
         out = dec.step(q)
         out2 = dec.step(q)  # a second step reuses every buffer
         torch.cuda.synchronize(dev)
         same = bool(torch.equal(out, out2))
+        if comm_kind == "peer":
+            same = same and not comm.timed_out()
         outs = [torch.empty_like(out) for _ in range(world)]
         dist.all_gather(outs, out)
         if rank == 0:
@@ -62,19 +66,22 @@ def _rank(rank, world, port, results, selection):
             errs = [float((o.float() - r).abs().max()) for o in outs]
             results.put((errs, same))
         dist.barrier()
+        if comm_kind == "peer":
+            comm.close()
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("selection", ["stats", "rows"])
-def test_sharded_decode_over_nccl(selection):
+@pytest.mark.parametrize("selection,comm_kind", [("stats", "nccl"), ("rows", "nccl"),
+                                                 ("stats", "peer")])
+def test_sharded_decode_over_nccl(selection, comm_kind):
     if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
         pytest.skip("needs 2 or more GPUs")
     world = min(4, torch.cuda.device_count())
     ctx = mp.get_context("spawn")
     results = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank, args=(r, world, port, results, selection))
+    procs = [ctx.Process(target=_rank, args=(r, world, port, results, selection, comm_kind))
              for r in range(world)]
     for p in procs:
         p.start()

@@ -212,7 +212,7 @@ class _OneRank:
     """A communicator of one rank (all-gathers are a leading axis of 1)."""
     world, rank = 1, 0
 
-    def all_gather(self, t):
+    def all_gather(self, t, name=None):
         return t.unsqueeze(0)
 
 
@@ -405,3 +405,32 @@ def test_sharded_decoder_one_rank_stats_exchange():
     assert sum(same) >= Hq - 1
     err = (out.float() - out1.float()).abs().max(dim=-1).values.cpu().numpy()
     assert err[np.array(same)].max() < BF16_TOL
+
+
+def test_peer_group_one_rank_gathers_and_matches_the_decoder():
+    """PeerGroup with one rank (no process group): the exchange kernels copy
+    the payload into the rank's own slot, twice in a row with different
+    payloads, and ShardedDecoder over it equals the plain one-rank path."""
+    _need_cuda()
+    from adakv_b200.sharded import PeerGroup, ShardedDecoder
+    pg = PeerGroup()
+    try:
+        for k in range(2):
+            x = torch.arange(1024, dtype=torch.float32, device="cuda") * (k + 1)
+            y = pg.all_gather(x, name="t")
+            torch.cuda.synchronize()
+            assert y.shape == (1, 1024) and torch.equal(y[0], x)
+        assert not pg.timed_out()
+        Hq, Hkv, D, bs, S = 32, 8, 128, 16, 20000 + 5
+        kw = dict(avg_budget=64, k_min=2, k_max=512)
+        g = torch.Generator(device="cuda").manual_seed(11)
+        q = torch.randn((Hq, D), device="cuda", generator=g).to(torch.bfloat16)
+        K = torch.randn((Hkv, S, D), device="cuda", generator=g).to(torch.bfloat16)
+        V = torch.randn((Hkv, S, D), device="cuda", generator=g).to(torch.bfloat16)
+        a = ShardedDecoder(K, V, S, Hq, bs, pg, **kw).step(q)
+        b = ShardedDecoder(K, V, S, Hq, bs, _OneRank(), **kw).step(q)
+        torch.cuda.synchronize()
+        assert torch.equal(a, b)
+        assert not pg.timed_out()
+    finally:
+        pg.close()
