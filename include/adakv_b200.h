@@ -14,6 +14,9 @@
  *                          the minmax (Quest) estimator                 (b')
  *   adakv_estimate / adakv_select / adakv_attend_partial / adakv_combine
  *                          the same step split for a sequence sharded over GPUs (e)
+ *   adakv_shard_prep / adakv_shard_clamp / adakv_shard_finish
+ *                          its selection from exchanged statistics (e)
+ *   adakv_peer_*           all-gather through peer-mapped memory (e)
  *
  * Conventions
  *   - Every function returns ADAKV_OK (0) or an error code; the message of

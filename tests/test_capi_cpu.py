@@ -248,3 +248,20 @@ def test_shard_selection_sizes_and_validation(lib):
                                   None, None) == _lib.ERR_INVALID
     assert lib.adakv_shard_finish(geo, sp, rec, 1 << 20, rec, 2, 0, 0, 32768, rec, 1000, rec,
                                   None, None) == _lib.ERR_INVALID
+
+
+def test_peer_exchange_and_packed_combine_validate_on_the_host(lib):
+    """Sizes of the peer-memory exchange buffer, and argument checks of the
+    exchange and of the packed log-sum-exp merge that fail before any CUDA call."""
+    assert lib.adakv_peer_buffer_bytes(2, 512) == 2 * 512 + (2 * 16 + 2) * 8
+    assert lib.adakv_peer_buffer_bytes(0, 512) == 0
+    assert lib.adakv_peer_buffer_bytes(2, 100) == 0
+    buf = ctypes.c_void_p(1 << 20)  # never dereferenced
+    assert lib.adakv_peer_exchange(buf, 512, buf, 0, 0, 512, buf, None, None) == _lib.ERR_INVALID
+    assert lib.adakv_peer_exchange(buf, 512, buf, 2, 2, 512, buf, None, None) == _lib.ERR_INVALID
+    assert lib.adakv_peer_exchange(buf, 100, buf, 2, 0, 512, buf, None, None) == _lib.ERR_INVALID
+    assert lib.adakv_peer_exchange(buf, 1024, buf, 2, 0, 512, buf, None, None) == _lib.ERR_INVALID
+    out = _lib.View(1 << 20, 64 * 128, 128, 0)
+    assert lib.adakv_combine_packed(2, 1, 64, 128, _lib.DTYPE_BF16, buf, 64 * 128,
+                                    out, None) == _lib.ERR_INVALID
+    assert b"part_stride" in lib.adakv_last_error()
