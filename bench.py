@@ -455,7 +455,7 @@ def run_cfg4(steps, warmup, world, rank, device):
         g_ = Hq // Hkv
         for kv in range(Hkv):
             union += len(set().union(*[set(x.tolist()) for x in ss[kv * g_:(kv + 1) * g_]]))
-        if ex != "rows":  # each rank holds its own picks: the job's union is their sum
+        if ex in ("peer", "stats"):  # each rank holds its own picks: the job's union is their sum
             import torch.distributed as dist
             t = torch.tensor([union], device=device, dtype=torch.int64)
             dist.all_reduce(t)
