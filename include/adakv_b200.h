@@ -26,11 +26,12 @@
  *     allocates device memory: scratch lives in a caller-provided workspace
  *     (size from adakv_*_workspace_bytes, zero-filled once before first use;
  *     it keeps no state a later call depends on beyond call counters).
- *     Calls that share a workspace must be ordered on one stream.  The one
- *     exception is adakv_attend_noalloc's scratch: a fixed 4 MiB __device__
+ *     Calls that share a workspace must be ordered on one stream.  The
+ *     exceptions: adakv_attend_noalloc's scratch, a fixed 4 MiB __device__
  *     array of the library, present on every device the library's device
  *     code is loaded on (4 MiB of device memory each), whether or not that
- *     entry point is ever called.
+ *     entry point is ever called; and adakv_peer_alloc, the one-time
+ *     set-up of a multi-GPU exchange buffer, which calls cudaMalloc.
  *   - Inputs (q, K/V, centroids, seq_lens, tables) must be complete when the
  *     call is enqueued: the decode kernels use programmatic dependent launch
  *     and some of them read their inputs before waiting for the previous
