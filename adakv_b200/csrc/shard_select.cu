@@ -485,23 +485,35 @@ __global__ void __launch_bounds__(kShardFinishThreads, 1) shard_finish_kernel(Sh
     s = warp_sum(s);
     if (lane == 0) s_sumw = s;
   }
-  // the head's candidate lists, staged when they fit (loads in flight together)
+  __syncthreads();  // s_sumw
+
+  const SeqBudget sb = seq_budget(nb, p.cfg);
+  const double w = adaptive ? s_w[h] : 0.0;
+  const int K = imin(head_count(sb, p.cfg, w, s_sumw, p.Hq), p.table_width);
+  const int n_forced = (sb.sink + sb.local >= nb) ? nb : sb.sink + sb.local;
+  const int Kc = imax(K - n_forced, 0);
+
+  // The head's candidate lists, staged when they fit (loads in flight
+  // together).  Only each list's first Kc keys matter: a candidate with Kc
+  // larger keys in one list is out whatever the rest holds.
+  const int kl = imin(Kc, p.cap_pad);
   const bool staged = (size_t)p.world * p.cap_pad * sizeof(unsigned long long) <=
                       (size_t)kShardFinishStage;
-  if (staged) {
-    const int tot = p.world * p.cap_pad;
+  if (staged && kl > 0) {
+    const int tot = p.world * kl;
     for (int base = 0; base < tot; base += kShardFinishThreads * kSweepU) {
       unsigned long long v[kSweepU];
 #pragma unroll
       for (int u = 0; u < kSweepU; ++u) {
         const int i = base + u * kShardFinishThreads + tid;
-        const int r = i / imax(p.cap_pad, 1), j = i - r * p.cap_pad;
+        const int r = i / kl, j = i - r * kl;
         v[u] = (i < tot && j < s_nc[r]) ? cands_of(p, r, h)[j] : 0ull;
       }
 #pragma unroll
       for (int u = 0; u < kSweepU; ++u) {
         const int i = base + u * kShardFinishThreads + tid;
-        if (i < tot) lists[i] = v[u];
+        const int r = i / kl, j = i - r * kl;
+        if (i < tot) lists[(size_t)r * p.cap_pad + j] = v[u];
       }
     }
   }
@@ -509,12 +521,6 @@ __global__ void __launch_bounds__(kShardFinishThreads, 1) shard_finish_kernel(Sh
   auto list_of = [&](int r) -> const unsigned long long* {
     return staged ? lists + (size_t)r * p.cap_pad : cands_of(p, r, h);
   };
-
-  const SeqBudget sb = seq_budget(nb, p.cfg);
-  const double w = adaptive ? s_w[h] : 0.0;
-  const int K = imin(head_count(sb, p.cfg, w, s_sumw, p.Hq), p.table_width);
-  const int n_forced = (sb.sink + sb.local >= nb) ? nb : sb.sink + sb.local;
-  const int Kc = imax(K - n_forced, 0);
 
   // ---- 2. own candidates whose merged position is below Kc (a prefix; an
   //      own candidate at index j >= Kc is never in) ----
@@ -526,7 +532,7 @@ __global__ void __launch_bounds__(kShardFinishThreads, 1) shard_finish_kernel(Sh
     for (int r = 0; r < p.world && rk < Kc; ++r) {
       if (r == me) continue;
       const unsigned long long* L = list_of(r);
-      int a = 0, b = s_nc[r];  // entries of list r larger than key
+      int a = 0, b = imin(s_nc[r], Kc);  // entries of list r larger than key (up to Kc)
       while (a < b) {
         const int mid = (a + b) >> 1;
         if (L[mid] > key) a = mid + 1;
