@@ -9,7 +9,7 @@ selection) and to float32 dot-product rounding (output).
 The selection from exchanged statistics (``StatsSelector``: per-head
 softmax statistics and sorted shard candidates, then clamp terms) is
 modelled here in NumPy, float64, step for step as the three shard kernels
-compute it, and run as 2 and 3 gloo ranks: the union of the ranks' picks
+compute it, and run as 2, 3 and 4 gloo ranks: the union of the ranks' picks
 must equal the oracle's selection on the whole rows (up to classified
 near-ties)."""
 import os
@@ -207,7 +207,7 @@ def _stats_rank(rank, world, port, q_out, kw):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,T", [(2, 1.0), (3, 0.7)])
+@pytest.mark.parametrize("world,T", [(2, 1.0), (3, 0.7), (4, 1.0)])
 def test_stats_exchange_decomposition_gloo_ranks(world, T):
     kw = dict(avg=12, k_min=2, k_max=64, T=T)
     port = _free_port()
